@@ -1,0 +1,268 @@
+// Shared device helpers for the sm_100a kernels of this engine.
+//
+// * PTX wrappers: mbarrier, TMA (cp.async.bulk.tensor, no multicast anywhere),
+//   1-D bulk copies, tcgen05 (alloc / mma / commit / cp / ld / fences).
+// * Bounded waits: every spin in this code base is limited by wall time read
+//   from %globaltimer.  On expiry the waiting thread records an error code in a
+//   device error word (host reads it and raises) and the kernel unwinds: no
+//   wait may hang a GPU.
+// * Descriptor builders for the 5th-generation tensor core (UMMA shared-memory
+//   matrix descriptors and instruction descriptors).  Field positions follow the
+//   public sm_100 descriptor definitions (CUTLASS cute/arch/mma_sm100_desc.hpp).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define DSV4_DEV __device__ __forceinline__
+
+namespace dsv4 {
+
+// ------------------------------------------------------------------ errors
+// Error word layout: bits [0,8) code, [8,16) kernel id, [16,32) detail.
+enum ErrCode : uint32_t {
+  ERR_NONE = 0,
+  ERR_WAIT_TIMEOUT = 1,
+  ERR_PEER_TIMEOUT = 2,
+  ERR_BAD_ARG = 3,
+  ERR_CAPACITY = 4,
+};
+
+enum KernelId : uint32_t {
+  KID_GEMM = 1,
+  KID_ATTN = 2,
+  KID_MOE = 3,
+  KID_COMM = 4,
+  KID_MEGA = 5,
+};
+
+DSV4_DEV void report_error(uint32_t* err, uint32_t code, uint32_t kid, uint32_t detail) {
+  if (err) atomicCAS(err, 0u, code | (kid << 8) | (detail << 16));
+}
+
+DSV4_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Default limit for any device-side wait (2 s).  A healthy pipeline waits
+// microseconds; only a bug or a dead peer reaches this.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+DSV4_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+DSV4_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+DSV4_DEV void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+DSV4_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+DSV4_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+DSV4_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  ``abort`` is a CTA-shared flag: once any
+// role gives up, every other waiter in the CTA gives up too.
+DSV4_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* err,
+                        uint32_t kid, uint32_t detail) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (abort) *abort = 1;
+      report_error(err, ERR_WAIT_TIMEOUT, kid, detail);
+      return false;
+    }
+  }
+}
+
+// --------------------------------------------------------------------- TMA
+DSV4_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+DSV4_DEV void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// 1-D bulk global->shared copy; both addresses 16-byte aligned, bytes % 16 == 0.
+DSV4_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+DSV4_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ----------------------------------------------------------------- tcgen05
+DSV4_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+DSV4_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;"); }
+DSV4_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+DSV4_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+DSV4_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+DSV4_DEV void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+DSV4_DEV void umma_mx(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+DSV4_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Copy a 32-row x 16-byte shared-memory block to TMEM lanes 0..31 of the given
+// columns, replicated into all four lane quadrants.
+DSV4_DEV void utccp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+DSV4_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+DSV4_DEV void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+DSV4_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------- descriptors
+// UMMA shared-memory matrix descriptor (sm_100 "version 1").
+DSV4_DEV uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutNone = 0;
+
+// K-major operand tile, 128-byte rows, 128B swizzle, 8-row groups 1024 B apart.
+DSV4_DEV uint64_t sdesc_kmajor_sw128(uint32_t saddr) { return umma_sdesc(saddr, 16, 1024, kLayoutSw128); }
+
+// Instruction descriptor, kind::f16 with bf16 inputs and fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n) {
+  return (1u << 4)            // D format f32
+         | (1u << 7)          // A bf16
+         | (1u << 10)         // B bf16
+         | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Instruction descriptor, kind::mxf8f6f4 with ue8m0 block scales.
+// fmt: 0 = e4m3, 5 = e2m1.  sf_id selects the scale byte (k-block) in the TMEM word.
+__host__ __device__ constexpr uint32_t idesc_mx(uint32_t m, uint32_t n, uint32_t afmt, uint32_t bfmt) {
+  return (afmt << 7) | (bfmt << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
+}
+DSV4_DEV uint32_t idesc_mx_sf(uint32_t base, uint32_t sf_id) { return base | (sf_id << 29) | (sf_id << 4); }
+
+// ------------------------------------------------------------------ numerics
+// 2^ceil(log2(amax * inv_max)) as a biased exponent byte, from IEEE bits.
+DSV4_DEV uint32_t pow2_ceil_exp(float amax, float inv_max) {
+  float prod = amax * inv_max;
+  uint32_t bits = __float_as_uint(prod);
+  int e = (int)((bits >> 23) & 0xFF) + ((bits & 0x7FFFFF) != 0 ? 1 : 0);
+  e = e < 0 ? 0 : (e > 254 ? 254 : e);
+  return (uint32_t)e;
+}
+DSV4_DEV float exp_to_f32(uint32_t e) { return __uint_as_float(e << 23); }
+
+DSV4_DEV uint8_t f32_to_e4m3(float v) {
+  __nv_fp8_e4m3 q(v);  // round-to-nearest-even, saturating to +-448
+  return *reinterpret_cast<uint8_t*>(&q);
+}
+DSV4_DEV float e4m3_to_f32(uint8_t b) {
+  __nv_fp8_e4m3 q;
+  *reinterpret_cast<uint8_t*>(&q) = b;
+  return float(q);
+}
+
+DSV4_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+DSV4_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Byte offset of (row, k) inside the block-scale "chunk" layout: one 512-byte
+// chunk per (128-row tile, 128-column k tile); inside, row m of the tile and
+// k-block j (32 columns) live at 16*(m%32) + 4*(m/32) + j, which is the layout
+// the tensor core reads after a 32x128b.warpx4 copy into TMEM.
+__host__ __device__ inline size_t sf_chunk_offset(int row, int kblk, int k_tiles) {
+  const int rt = row >> 7, m = row & 127;
+  const int kt = kblk >> 2, j = kblk & 3;
+  return ((size_t)rt * k_tiles + kt) * 512 + (size_t)((m & 31) * 16 + (m >> 5) * 4 + j);
+}
+
+}  // namespace dsv4

@@ -1,0 +1,428 @@
+// tcgen05 GEMM for sm_100a: D[m, n] = sum_k A[m, k] * B[n, k].
+//
+// Orientation ("swap-AB"): A is the weight ([out_features, K], K-major), B is
+// the activation ([tokens, K], K-major).  The 128-row MMA M side covers output
+// features and tokens ride on the N side (16..256), which is what decode-sized
+// token counts need.  The result tile D[128 x BN] lives in TMEM and is written
+// transposed, out[token][feature].
+//
+// Kinds:
+//   KIND_BF16   tcgen05.mma kind::f16, bf16 x bf16 -> fp32.
+//   KIND_MX8    kind::mxf8f6f4.block_scale, e4m3 x e4m3 with ue8m0 scales per
+//               32 K-elements on both operands (MXFP8), fp32 accumulate.
+//   KIND_MX4A   same with the A operand e2m1 (MXFP4 weights, unpacked in smem by
+//               TMA's 16U4_ALIGN8B type).
+// Block scales arrive in the 512-byte "chunk" layout (common.cuh), one chunk per
+// (128-row tile, 128-column k tile), moved by a 1-D bulk copy into shared
+// memory and by tcgen05.cp into TMEM next to the accumulator.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer (one elected lane), warps 2..5 = epilogue (each reads the TMEM lane
+// quadrant it is allowed to access).  The kernel is persistent over a tile list
+// (dense: computed; grouped/MoE: device tile records), with optional split-K
+// whose partial sums are reduced deterministically by the last-arriving CTA.
+//
+// Epilogues: bf16 store, fp32 store, and SwiGLU-requant for expert W13 tiles
+// whose rows are [64 gate rows; 64 up rows]: h = silu(min(g, L)) * clip(u, L) *
+// row_weight, rounded to bf16 and re-quantized to MXFP8 (e4m3 + ue8m0 per 32)
+// for the W2 GEMM, so the intermediate never leaves the chip in high precision.
+#include "common.cuh"
+#include "gemm.h"
+
+namespace dsv4 {
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kA = 128 * 128;                // 16 KB
+  static constexpr int kB = BN * 128;
+  static constexpr int kSfbChunks = (BN + 127) / 128;
+  static constexpr int kSf = 512 * (1 + kSfbChunks);
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : 7);
+  static constexpr int kStage = kA + kB + kSf;
+  static constexpr int kXbuf = 2 * 32 * 32 * 4;        // SwiGLU exchange
+  static constexpr int kBarriers = 256;
+  static constexpr int kTotal = 1024 + kStages * kStage + kXbuf + kBarriers;
+  // TMEM: accumulator columns, then per-stage scale-factor columns.
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kSfCols = 4 * (1 + kSfbChunks);
+  static constexpr int kColsNeeded = kAccCols + kStages * kSfCols;
+  static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
+                                 : kColsNeeded <= 256 ? 256 : 512;
+};
+
+DSV4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+struct TileCoord {
+  int a_row0, b_row0, b_valid, out_col0, k_begin, k_end, split, tile, n_eff;
+};
+
+// Per-tile MMA width: the smallest of 32/64/128/256 covering the valid rows.
+// Tiles start on 128-row boundaries of the activation buffer (256 for n_eff
+// 256), so scale-factor chunks are always used unshifted: the tensor core wants
+// scale-factor TMEM addresses on a 4-column boundary.
+DSV4_DEV int n_eff_for(int valid) { return valid <= 32 ? 32 : valid <= 64 ? 64 : valid <= 128 ? 128 : 256; }
+DSV4_DEV int bmap_index(int n_eff) { return n_eff == 32 ? 0 : n_eff == 64 ? 1 : n_eff == 128 ? 2 : 3; }
+
+template <bool GROUPED, int BN>
+DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
+  const int n_units = (GROUPED ? __ldg(p.n_tiles_ptr) : p.n_tiles) * p.splits;
+  if (w >= n_units) return false;
+  const int tile = w / p.splits;
+  const int split = w % p.splits;
+  if (GROUPED) {
+    const int4 r = p.tiles[tile];
+    t.a_row0 = r.x;
+    t.b_row0 = r.y;
+    t.b_valid = r.z;
+    t.out_col0 = r.w;
+    t.n_eff = min(BN, n_eff_for(r.z));
+  } else {
+    const int m_tiles = p.M / 128;
+    const int mt = tile % m_tiles, nt = tile / m_tiles;
+    t.a_row0 = mt * 128;
+    t.b_row0 = nt * BN;
+    t.b_valid = min(BN, p.N - t.b_row0);
+    t.out_col0 = mt * 128;
+    t.n_eff = BN;
+  }
+  const int per = (p.k_tiles + p.splits - 1) / p.splits;
+  t.k_begin = split * per;
+  t.k_end = min(p.k_tiles, t.k_begin + per);
+  t.split = split;
+  t.tile = tile;
+  return true;
+}
+
+template <int KIND, int BN, int EPI, bool GROUPED>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ BMaps tma_b, GemmParams p) {
+  using L = GemmSmem<BN>;
+  constexpr bool MX = KIND != KIND_BF16;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + S * L::kA;
+  uint8_t* sSF = sB + S * L::kB;
+  float* xbuf = reinterpret_cast<float*>(sSF + S * L::kSf);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + L::kXbuf);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* acc_full = bars + 2 * S;
+  uint64_t* acc_empty = bars + 2 * S + 1;
+  uint64_t* drain = bars + 2 * S + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b.m[0]);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  constexpr int kBkElems = KIND == KIND_BF16 ? 64 : 128;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    TileCoord t;
+    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+      const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
+      const uint32_t tx = L::kA + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
+      const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
+      const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
+      for (int kt = t.k_begin; kt < t.k_end; ++kt) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, KID_GEMM, 1)) goto done;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], tx);
+          tma_load_2d(sA + stage * L::kA, &tma_a, &full[stage], kt * kBkElems, t.a_row0);
+          tma_load_2d(sB + stage * L::kB, bmap, &full[stage], b_kofs + kt * kBkElems, t.b_row0);
+          if constexpr (MX) {
+            uint8_t* sf = sSF + stage * L::kSf;
+            bulk_load(sf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512, &full[stage]);
+            for (int c = 0; c < sfb_chunks; ++c)
+              bulk_load(sf + 512 * (1 + c),
+                        p.sfb + ((size_t)((t.b_row0 >> 7) + c) * p.sfb_ktiles + kt + b_kofs / 128) * 512, 512,
+                        &full[stage]);
+          }
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t acc_phase = 0;
+    TileCoord t;
+    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+      const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, KIND == KIND_MX4A ? 5 : 0, 0) : idesc_bf16(128, t.n_eff);
+      const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
+      if (!mbar_wait(acc_empty, acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
+      tc_fence_after();
+      for (int kt = t.k_begin; kt < t.k_end; ++kt) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.err, KID_GEMM, 3)) goto done;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = smem_u32(sA + stage * L::kA);
+          const uint32_t b0 = smem_u32(sB + stage * L::kB);
+          uint32_t sfa_t = 0, sfb_t = 0;
+          if constexpr (MX) {
+            const uint32_t sf0 = smem_u32(sSF + stage * L::kSf);
+            const uint32_t col = tmem + L::kAccCols + stage * L::kSfCols;
+            utccp_32x128b_x4(col, umma_sdesc(sf0, 16, 128, kLayoutNone));
+            for (int c = 0; c < sfb_chunks; ++c)
+              utccp_32x128b_x4(col + 4 + 4 * c, umma_sdesc(sf0 + 512 * (1 + c), 16, 128, kLayoutNone));
+            sfa_t = col;
+            sfb_t = col + 4;
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_kmajor_sw128(a0 + kk * 32);
+            const uint64_t bd = sdesc_kmajor_sw128(b0 + kk * 32);
+            const uint32_t acc = (kt > t.k_begin || kk > 0) ? 1u : 0u;
+            if constexpr (MX)
+              umma_mx(tmem, ad, bd, idesc_mx_sf(idesc, kk), sfa_t, sfb_t, acc);
+            else
+              umma_bf16(tmem, ad, bd, idesc, acc);
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (lane == 0) umma_commit(acc_full);
+      __syncwarp();
+      acc_phase ^= 1;
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = 32 * q + lane;
+    uint32_t acc_phase = 0;
+    TileCoord t;
+    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+      if (!mbar_wait(acc_full, acc_phase, abort_flag, p.err, KID_GEMM, 4)) goto done;
+      tc_fence_after();
+      const bool split = p.splits > 1;
+      constexpr int kCols = BN < 32 ? BN : 32;
+      float* ws_tile = split ? p.workspace + (size_t)t.tile * p.splits * 128 * BN : nullptr;
+      if (split) {
+        // Publish this split's partial tile, then let the last arrival reduce.
+        for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+          uint32_t r[32];
+          if constexpr (kCols == 32) tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+          else tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld_wait();
+          float* dst = ws_tile + (size_t)t.split * 128 * BN;
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) dst[(c0 + j) * 128 + row] = __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int prev = atomicAdd(&p.tile_counters[t.tile], 1);
+          *last_flag = (prev == p.splits - 1);
+          if (prev == p.splits - 1) p.tile_counters[t.tile] = 0;  // re-arm for the next launch
+          __threadfence();
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!*last_flag) {
+          acc_phase ^= 1;
+          continue;
+        }
+        __threadfence();
+      }
+      for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+        float v[32];
+        if (split) {
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) v[j] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float* src = ws_tile + (size_t)s * 128 * BN;
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) v[j] += __ldcg(src + (c0 + j) * 128 + row);
+          }
+        } else {
+          uint32_t r[32];
+          if constexpr (kCols == 32) tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+          else tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) v[j] = __uint_as_float(r[j]);
+        }
+        if constexpr (EPI == EPI_SWIGLU) {
+          // rows 0..63 gate, 64..127 up (same 64 intermediate indices)
+          if (q >= 2) {
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) xbuf[((q - 2) * 32 + j) * 32 + lane] = v[j];
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q < 2) {
+            const int i_local = 32 * q + lane;
+            const int i_global = (t.out_col0 >> 1) + i_local;  // out_col0 = 128 * m-tile
+            const int kblk = i_global >> 5;
+            const float lim = p.swiglu_limit;
+#pragma unroll 4
+            for (int j = 0; j < kCols; ++j) {
+              const int n = c0 + j;
+              float g = bf16_round(v[j]);
+              float u = bf16_round(xbuf[(q * 32 + j) * 32 + lane]);
+              if (lim > 0.f) {
+                u = fminf(fmaxf(u, -lim), lim);
+                g = fminf(g, lim);
+              }
+              float h = g / (1.f + expf(-g)) * u;
+              const int brow = t.b_row0 + n;
+              if (p.row_scale && n < t.b_valid) h *= __ldg(p.row_scale + brow);
+              h = bf16_round(h);
+              const float amax = fmaxf(warp_max(fabsf(h)), 1e-4f);
+              const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
+              const float qv = fminf(fmaxf(h / exp_to_f32(e), -448.f), 448.f);
+              if (n < t.b_valid) {
+                p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
+                if (lane == 0) p.hsf[sf_chunk_offset(brow, kblk, p.h_ktiles)] = (uint8_t)e;
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        } else {
+          const int m = t.out_col0 + row;
+          if (m < p.m_valid) {
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) {
+              if (c0 + j < t.b_valid) {
+                const size_t o = (size_t)(t.b_row0 + c0 + j) * p.ldo + m;
+                float x = v[j];
+                if (p.row_scale) x *= __ldg(p.row_scale + t.b_row0 + c0 + j);
+                if constexpr (EPI == EPI_F32)
+                  reinterpret_cast<float*>(p.out)[o] = x;
+                else
+                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
+              }
+            }
+          }
+        }
+      }
+      if (!split) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+      }
+      acc_phase ^= 1;
+    }
+  }
+done:
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort_flag) {
+      // Make sure no tensor-core op still reads TMEM before releasing it.
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
+      mbar_wait(drain, 0, nullptr, p.err, KID_GEMM, 5);
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------- host
+template <int KIND, int BN, int EPI, bool GROUPED>
+static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
+                              cudaStream_t st) {
+  using L = GemmSmem<BN>;
+  auto k = gemm_kernel<KIND, BN, EPI, GROUPED>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  k<<<grid, 192, L::kTotal, st>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+template <int KIND, int EPI, bool GROUPED>
+static cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
+                               cudaStream_t st) {
+  switch (bn) {
+    case 32: return launch_one<KIND, 32, EPI, GROUPED>(ta, tb, p, grid, st);
+    case 64: return launch_one<KIND, 64, EPI, GROUPED>(ta, tb, p, grid, st);
+    case 128: return launch_one<KIND, 128, EPI, GROUPED>(ta, tb, p, grid, st);
+    case 256: return launch_one<KIND, 256, EPI, GROUPED>(ta, tb, p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int gemm_smem_bytes(int bn) {
+  switch (bn) {
+    case 32: return GemmSmem<32>::kTotal;
+    case 64: return GemmSmem<64>::kTotal;
+    case 128: return GemmSmem<128>::kTotal;
+    case 256: return GemmSmem<256>::kTotal;
+    default: return -1;
+  }
+}
+
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorMap& ta, const BMaps& tb,
+                        const GemmParams& p, int grid, cudaStream_t st) {
+  if (kind == KIND_BF16) {
+    if (grouped) return cudaErrorInvalidValue;
+    if (epi == EPI_BF16) return dispatch_bn<KIND_BF16, EPI_BF16, false>(bn, ta, tb, p, grid, st);
+    if (epi == EPI_F32) return dispatch_bn<KIND_BF16, EPI_F32, false>(bn, ta, tb, p, grid, st);
+    return cudaErrorInvalidValue;
+  }
+#define DSV4_MX(KD)                                                                                  \
+  if (kind == KD) {                                                                                  \
+    if (!grouped) {                                                                                  \
+      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, false>(bn, ta, tb, p, grid, st);         \
+      if (epi == EPI_F32) return dispatch_bn<KD, EPI_F32, false>(bn, ta, tb, p, grid, st);           \
+      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, false>(bn, ta, tb, p, grid, st);     \
+    } else {                                                                                         \
+      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, true>(bn, ta, tb, p, grid, st);          \
+      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, true>(bn, ta, tb, p, grid, st);      \
+    }                                                                                                \
+    return cudaErrorInvalidValue;                                                                    \
+  }
+  DSV4_MX(KIND_MX8)
+  DSV4_MX(KIND_MX4A)
+#undef DSV4_MX
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dsv4

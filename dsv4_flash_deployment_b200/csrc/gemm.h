@@ -1,0 +1,59 @@
+// Host-visible interface of the tcgen05 GEMM (gemm.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsv4 {
+
+enum GemmKind { KIND_BF16 = 0, KIND_MX8 = 1, KIND_MX4A = 2 };
+enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2 };
+
+struct GemmParams {
+  int M;         // dense: A rows (multiple of 128)
+  int N;         // dense: B rows (tokens)
+  int k_tiles;   // K / 128 bytes
+  int n_tiles;   // dense tile count
+  int splits;    // split-K factor (1 = none)
+  const uint8_t* sfa;  // A scale chunks [M/128][sfa_ktiles][512]
+  int sfa_ktiles;
+  const uint8_t* sfb;  // B scale chunks [rows/128][sfb_ktiles][512]
+  int sfb_ktiles;
+  const int4* tiles;   // grouped: {a_row0, b_row0, b_valid, out_col0}
+  const int* n_tiles_ptr;
+  // batched dense mode: A rows group_rows apart read B columns group_k apart
+  int group_rows;
+  int group_k;
+  void* out;           // out[b_row][out_col0 + m]
+  int ldo;
+  int m_valid;
+  const float* row_scale;  // optional per-B-row multiplier
+  // SwiGLU epilogue output (MXFP8 for the next GEMM)
+  uint8_t* hq;
+  int ldh;
+  uint8_t* hsf;
+  int h_ktiles;
+  float swiglu_limit;
+  // split-K
+  float* workspace;
+  int* tile_counters;
+  uint32_t* err;
+};
+
+// Activation tensor maps with box heights 32/64/128/256 rows (grouped GEMMs
+// pick one per tile); dense GEMMs use m[0] with box height BN.
+struct BMaps {
+  CUtensorMap m[4];
+};
+
+int gemm_smem_bytes(int bn);
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorMap& ta, const BMaps& tb,
+                        const GemmParams& p, int grid, cudaStream_t st);
+
+// 2-D tensor map over a row-major [rows, cols] matrix of 1-byte (e4m3), 2-byte
+// (bf16) or packed 4-bit (e2m1, unpacked to 1 byte per element in smem)
+// elements; box = {128 bytes of K, box_rows}, 128B swizzle.
+enum TmaElem { TMA_U8 = 0, TMA_BF16 = 1, TMA_E2M1 = 2 };
+bool make_tma_2d(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+}  // namespace dsv4
