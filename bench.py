@@ -1,0 +1,291 @@
+"""Headline benchmark: output tok/s on the 1k/1k workload at concurrency 512.
+
+Workload (BASELINE.json metric and config 3, the reference's V4-Flash sweep row
+``V4/results/raw/1k1k.json:236``): 512 concurrent requests, 1024 uniform-random
+prompt tokens, 1024 forced output tokens (ignore EOS), DeepSeek-V4-Flash-shaped
+model with random-init weights (FP8 block-scaled dense layers, MXFP8 experts,
+FP8-roundtrip KV).  A *step* is one continuous-batching iteration in the
+steady state of that sweep: with every request taking 1024 prefill tokens and
+1024 decode steps, each step decodes one token for each of the ~511 requests
+past their prompt and prefills a 512-token chunk of the one request in
+prefill (512 prompt tokens per 512 output tokens, the sweep's equilibrium).
+
+Two numbers:
+  value  device-timed: K back-to-back steps of the captured step graph (CUDA
+         events, barrier + synchronize on both sides, max over ranks); each
+         step uploads its own metadata (advancing positions) and reads back the
+         sampled ids.
+  e2e    the same workload through the public API ``Engine.step()`` (real
+         scheduler, pinned host->device copy of each step's token/position
+         inputs, device->host read of the sampled tokens), wall-clock.
+
+Multi-GPU: one rank per GPU; attention is data-parallel over the requests
+(512/N per rank) and experts are split over ranks (EP=N).  The expert exchange
+runs in the fused NVLink dispatch/combine kernels of ``parallel/ep.py``.
+
+    python bench.py [--gpus N --steps K --warmup W]
+    python bench.py --impl reference     # the reference arm
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+BASELINE_TOKS = 8463.7   # V4-Flash 1k/1k C=512, TPU v6e-16 (V4/results/raw/1k1k.json:236)
+METRIC = "output tok/s @1k/1k C=512 (8×B200, max over ranks); C=1 TPOT ms; vs BASELINE"
+
+
+def _reference_arm(args) -> None:
+    why = ("the reference is a JAX/Pallas TPU deployment (vLLM + tpu-inference, not vendored) with no GPU "
+           "build; it cannot run on a B200")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "samples": len(rows)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--concurrency", type=int, default=512)
+    ap.add_argument("--isl", type=int, default=1024)
+    ap.add_argument("--osl", type=int, default=1024)
+    ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-graphs", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        _reference_arm(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from dsv4_flash_deployment_b200.config import v4_flash_config
+    from dsv4_flash_deployment_b200.engine.engine import Engine
+    from dsv4_flash_deployment_b200.engine.memory import plan_expert_storage
+    from dsv4_flash_deployment_b200.models.model import SeqChunk, StepMeta
+    from dsv4_flash_deployment_b200.ops import _ext
+    from dsv4_flash_deployment_b200.parallel import ep as ep_mod
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        group = dist.group.WORLD
+    cfg = v4_flash_config()
+    C, isl, osl, chunk = args.concurrency, args.isl, args.osl, args.chunk
+    c_rank = C // world
+    chunk_rank = max(1, chunk // world)
+    n_dec = c_rank - 1
+    max_tokens = n_dec + chunk_rank
+    max_seq = isl + osl
+    ep = ep_mod.EPGroup(rank, world, group, dev) if world > 1 else None
+    n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world)
+    eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
+                       expert_storage_layers=n_phys, ep=ep, use_graphs=not args.no_graphs, chunk_size=chunk_rank)
+    model = eng.model
+    rng = np.random.default_rng(1234 + rank)
+
+    # ---------------------------------------------------------- device-timed
+    # staggered decode positions over the sweep's context range; the prefill
+    # request walks its prompt chunk by chunk and restarts in the same slot.
+    dec_pos = (isl + (np.arange(n_dec) * (osl // max(1, n_dec)) + 1) % osl).astype(np.int64)
+    pre_slot = n_dec
+    state = {"pre": 0, "dec": dec_pos.copy()}
+
+    def make_meta():
+        chunks = [SeqChunk(s, int(state["dec"][s]), [int(rng.integers(0, cfg.vocab_size))], True)
+                  for s in range(n_dec)]
+        p0 = state["pre"]
+        chunks.append(SeqChunk(pre_slot, p0, rng.integers(0, cfg.vocab_size, chunk_rank).tolist(),
+                               p0 + chunk_rank >= isl))
+        state["dec"] = np.where(state["dec"] + 1 >= max_seq, isl, state["dec"] + 1)
+        state["pre"] = (p0 + chunk_rank) % isl
+        return StepMeta(cfg, chunks)
+
+    # one eager step counts this library's kernel launches per step (the graph
+    # replays exactly these launches), then W warm-up steps
+    counter = _ext.LaunchCounter()
+    use_graphs = eng.use_graphs
+    eng.use_graphs = False
+    with counter.counting(True):
+        eng.run_meta(make_meta())
+    eng.use_graphs = use_graphs
+    launches_per_step = counter.count
+    for i in range(args.warmup):
+        eng.run_meta(make_meta())
+    eng.check_errors()
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    metas = [make_meta() for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if group is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(eng.stream)
+        for m in metas:
+            eng.run_meta(m)
+        t1.record(eng.stream)
+        torch.cuda.synchronize()
+        if group is not None:
+            dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    eng.check_errors()
+    ms_t = torch.tensor([ms], device=dev)
+    if group is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    out_tok_step = n_dec * world
+    value = out_tok_step / (ms_max / 1e3)
+
+    # ----------------------------------------------------------------- e2e
+    sched = eng.sched
+    e2e_steps = args.e2e_steps or args.steps
+    # inject the steady state: n_dec requests past their prompt, one in prefill
+    for s in range(n_dec):
+        r = sched.add(rng.integers(0, cfg.vocab_size, isl).tolist(), osl, ignore_eos=True)
+        sched.waiting.remove(r)
+        r.slot = sched.slots.alloc()
+        r.n_prefilled = isl
+        k = int(dec_pos[s] - isl) + 1
+        r.output = rng.integers(0, cfg.vocab_size, k).tolist()
+        sched.running.append(r)
+
+    def top_up():
+        while len(sched.running) + len(sched.waiting) < c_rank:
+            eng.add_request(rng.integers(0, cfg.vocab_size, isl).tolist(), osl, ignore_eos=True)
+
+    top_up()
+    for _ in range(2):
+        eng.step()
+        top_up()
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    out_tokens = 0
+    w0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        ev = eng.step()
+        out_tokens += sum(1 for _, tok in ev if tok is not None)
+        top_up()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    tok_t = torch.tensor([out_tokens / wall], device=dev)
+    wall_t = torch.tensor([wall], device=dev)
+    if group is not None:
+        dist.all_reduce(tok_t)
+        dist.all_reduce(wall_t, op=dist.ReduceOp.MAX)
+    e2e = float(tok_t.item())
+    h2d = int(model.last_upload_bytes)
+    d2h = 4 * (n_dec + 1)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": round(value / BASELINE_TOKS, 3),
+            "dtype": "bf16",
+            "data": "synthetic: uniform-random token ids, random-init weights",
+            "config": {
+                "model": "deepseek-v4-flash (assumed dims: 43L, d4096, 64x512 heads, 256 experts top-8 inter2048)",
+                "global_batch": C,
+                "seq_len": max_seq,
+                "workload": f"1k/1k C={C} steady-state step: {n_dec * world} decode + {chunk_rank * world} prefill tokens",
+                "parallelism": f"dp-attention{world} x ep{world}" if world > 1 else "single GPU",
+                "weights": "fp8 e4m3 block-scaled dense (checkpoint-native), mxfp8 experts, bf16 activations",
+                "expert_storage_layers": n_phys,
+                "l2": "inputs larger than L2 (expert weights 6.6 GB/layer/all ranks, caches)",
+                "cuda_graphs": not args.no_graphs,
+            },
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        eng.graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,413 @@
+// Sparse multi-query attention over gathered latent rows (decode + prefill).
+//
+// Per query token t at position p (reference.py:172-235, _attention_step
+// :704-838): q [H, Dh] gets (optional per-head RMSNorm, V4-Flash) + RoPE on the
+// last 64 dims; the attended row set is the sliding window (positions
+// max(0, p-W+1)..p) plus the selected compressed rows (indexer top-k list, or
+// every compressed entry for dense layers).  K and V are the same latent row.
+// Scores in fp32, online softmax over blocks of 64 rows with P rounded to bf16
+// before PV, and exp(sink - max) added to the denominator.  The output gets the
+// inverse RoPE on the last 64 dims and is written bf16.
+//
+// Window rows of positions at or after the token's chunk start come from this
+// step's kv buffer (prefill chunks), earlier ones from the per-sequence ring.
+//
+// One CTA (8 warps) per (token, split).  Rows are gathered with cp.async into
+// double-buffered shared memory; QK^T and PV use mma.sync m16n8k16 bf16 with
+// fp32 accumulators (PV accumulators stay in registers, 64 dims per warp).
+// With splits > 1 the partial (acc, max, sum) go to a workspace and
+// attn_combine merges them (C = 1 decode spreads a token over many SMs).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+namespace {
+constexpr int kH = 64;
+constexpr int kDh = 512;
+constexpr int kBlk = 64;
+constexpr int kPadE = 8;                 // row padding (bf16 elements) to spread banks
+constexpr int kRowE = kDh + kPadE;       // 520
+constexpr int kPPad = kBlk + 8;          // P row stride (bf16)
+
+constexpr size_t kSmemQ = (size_t)kH * kRowE * 2;
+constexpr size_t kSmemKV = (size_t)kBlk * kRowE * 2;
+constexpr size_t kSmemP = (size_t)kH * kPPad * 2;
+constexpr size_t kSmemRows = (size_t)kAttnMaxRows * 8;
+constexpr size_t kSmemStats = (size_t)kH * 4 * 7;  // max, sum, corr, 2x partial max, 2x partial sum
+constexpr size_t kSmemTotal = kSmemQ + 2 * kSmemKV + kSmemP + kSmemRows + kSmemStats;
+}  // namespace
+
+DSV4_DEV void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = smem_u32(dst);
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(sz) : "memory");
+}
+DSV4_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+DSV4_DEV void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+DSV4_DEV void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+DSV4_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+DSV4_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+DSV4_DEV uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* sKV = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ);
+  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ + 2 * kSmemKV);
+  const __nv_bfloat16** sRows = reinterpret_cast<const __nv_bfloat16**>(smem + kSmemQ + 2 * kSmemKV + kSmemP);
+  float* sMax = reinterpret_cast<float*>(smem + kSmemQ + 2 * kSmemKV + kSmemP + kSmemRows);
+  float* sSum = sMax + kH;
+  float* sCorr = sSum + kH;
+  float* sPMax = sCorr + kH;   // [kH][2]
+  float* sPSum = sPMax + 2 * kH;
+
+  const int t = blockIdx.x;
+  const int split = blockIdx.y;
+  const int nsplit = gridDim.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pos = p.pos[t];
+  const int slot = p.slot[t];
+  const int rope_pos = p.rope_pos ? p.rope_pos[t] : pos;
+
+  // ---------------- row list: window, then compressed entries (valid ones first)
+  const int n_win = min(pos + 1, p.W);
+  const int n_comp = p.comp != nullptr ? min(p.comp_cnt[t], kAttnMaxRows - n_win) : 0;
+  {
+    const int cs = p.chunk_start[t];
+    for (int j = tid; j < n_win + n_comp; j += blockDim.x) {
+      const __nv_bfloat16* r;
+      if (j < n_win) {
+        const int pp = pos - n_win + 1 + j;
+        if (pp >= cs)
+          r = p.kv_step + (size_t)(p.step_row0[t] + (pp - cs)) * kDh;
+        else
+          r = p.ring + ((size_t)slot * p.W + (pp % p.W)) * kDh;
+      } else {
+        const int jj = j - n_win;
+        const int ci = p.comp_idx != nullptr ? p.comp_idx[(size_t)t * p.comp_k + jj] : jj;
+        r = p.comp + ((size_t)slot * p.max_c + ci) * kDh;
+      }
+      sRows[j] = r;
+    }
+  }
+  // ---------------- Q: optional head norm, RoPE, into smem
+  for (int h = warp; h < kH; h += 8) {
+    const __nv_bfloat16* qg = p.q + (size_t)t * p.q_stride + (size_t)h * kDh;
+    float v[16];
+    {
+      uint4 raw[2];
+      raw[0] = *reinterpret_cast<const uint4*>(qg + lane * 16);
+      raw[1] = *reinterpret_cast<const uint4*>(qg + lane * 16 + 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+    if (p.q_head_norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ss += v[i] * v[i];
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / (float)kDh + p.norm_eps);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i] * r));
+    }
+    if (lane * 16 >= kDh - 64) {  // rope dims 448..511, pairs (2i, 2i+1)
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const int pi = (lane * 16 + i - (kDh - 64)) >> 1;
+        const float c = p.rope_cos[(size_t)rope_pos * 32 + pi], s = p.rope_sin[(size_t)rope_pos * 32 + pi];
+        const float e = v[i], o = v[i + 1];
+        v[i] = e * c - o * s;
+        v[i + 1] = e * s + o * c;
+      }
+    }
+    __nv_bfloat16* qs = sQ + (size_t)h * kRowE + lane * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qs[i] = __float2bfloat16(v[i]);
+  }
+  if (tid < kH) {
+    sMax[tid] = -1e30f;
+    sSum[tid] = 0.f;
+  }
+  __syncthreads();
+  const int n_rows = n_win + n_comp;
+  const int n_blocks = (n_rows + kBlk - 1) / kBlk;
+  const int bps = (n_blocks + nsplit - 1) / nsplit;
+  const int b_begin = split * bps;
+  const int b_end = min(n_blocks, b_begin + bps);
+
+  auto load_block = [&](int b, int buf) {
+    __nv_bfloat16* dst = sKV + (size_t)buf * kBlk * kRowE;
+    for (int c = tid; c < kBlk * (kDh / 8); c += 256) {
+      const int r = c / (kDh / 8), ch = c % (kDh / 8);
+      const int gr = b * kBlk + r;
+      const bool ok = gr < n_rows;
+      const __nv_bfloat16* src = ok ? sRows[gr] + ch * 8 : p.q;  // any valid address when masked
+      cp_async16(dst + (size_t)r * kRowE + ch * 8, src, ok);
+    }
+    cp_async_commit();
+  };
+
+  float acc[4][8][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[i][j][k] = 0.f;
+
+  const int g = lane >> 2, cq = lane & 3;
+  if (b_begin < b_end) load_block(b_begin, 0);
+  for (int b = b_begin; b < b_end; ++b) {
+    const int buf = (b - b_begin) & 1;
+    if (b + 1 < b_end) {
+      load_block(b + 1, buf ^ 1);
+      cp_async_wait1();
+    } else {
+      cp_async_wait0();
+    }
+    __syncthreads();
+    const __nv_bfloat16* kv = sKV + (size_t)buf * kBlk * kRowE;
+    // ---- S = Q K^T : warp -> heads (warp%4)*16, rows (warp/4)*32
+    {
+      const int h0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+      float s[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) s[i][k] = 0.f;
+      const uint32_t qa = smem_u32(sQ + (size_t)(h0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kRowE + 8 * (lane >> 4));
+#pragma unroll 4
+      for (int k0 = 0; k0 < kDh; k0 += 16) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(qa + k0 * 2, a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < 4; nt += 2) {
+          uint32_t b0, b1, b2, b3;
+          const uint32_t ba =
+              smem_u32(kv + (size_t)(n0 + nt * 8 + (lane & 7) + 8 * (lane >> 4)) * kRowE + k0 + 8 * ((lane >> 3) & 1));
+          ldsm_x4(ba, b0, b1, b2, b3);
+          mma16816(s[nt], a0, a1, a2, a3, b0, b1);
+          mma16816(s[nt + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+      // ---- online softmax from registers (each head's 64 columns span 2 warps)
+      const int valid = min(kBlk, n_rows - b * kBlk);
+      float pm[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int col = n0 + nt * 8 + 2 * cq;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int cc = col + (e & 1);
+          s[nt][e] = cc < valid ? s[nt][e] * p.scale : -INFINITY;
+          pm[e >> 1] = fmaxf(pm[e >> 1], s[nt][e]);
+        }
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        pm[hf] = fmaxf(pm[hf], __shfl_xor_sync(0xffffffffu, pm[hf], 1));
+        pm[hf] = fmaxf(pm[hf], __shfl_xor_sync(0xffffffffu, pm[hf], 2));
+      }
+      if (cq == 0) {
+        sPMax[(h0 + g) * 2 + (warp >> 2)] = pm[0];
+        sPMax[(h0 + g + 8) * 2 + (warp >> 2)] = pm[1];
+      }
+      __syncthreads();
+      float nm[2], ps[2] = {0.f, 0.f};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int h = h0 + g + 8 * hf;
+        nm[hf] = fmaxf(sMax[h], fmaxf(sPMax[h * 2], sPMax[h * 2 + 1]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int col = n0 + nt * 8 + 2 * cq;
+        const float p0 = expf(s[nt][0] - nm[0]), p1 = expf(s[nt][1] - nm[0]);
+        const float p2 = expf(s[nt][2] - nm[1]), p3 = expf(s[nt][3] - nm[1]);
+        ps[0] += p0 + p1;
+        ps[1] += p2 + p3;
+        *reinterpret_cast<uint32_t*>(sP + (h0 + g) * kPPad + col) = pack_bf16(p0, p1);
+        *reinterpret_cast<uint32_t*>(sP + (h0 + g + 8) * kPPad + col) = pack_bf16(p2, p3);
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        ps[hf] += __shfl_xor_sync(0xffffffffu, ps[hf], 1);
+        ps[hf] += __shfl_xor_sync(0xffffffffu, ps[hf], 2);
+      }
+      if (cq == 0) {
+        sPSum[(h0 + g) * 2 + (warp >> 2)] = ps[0];
+        sPSum[(h0 + g + 8) * 2 + (warp >> 2)] = ps[1];
+      }
+    }
+    __syncthreads();
+    if (tid < kH) {
+      const float om = sMax[tid];
+      const float nmx = fmaxf(om, fmaxf(sPMax[tid * 2], sPMax[tid * 2 + 1]));
+      const float corr = expf(om - nmx);
+      sCorr[tid] = corr;
+      sSum[tid] = sSum[tid] * corr + sPSum[tid * 2] + sPSum[tid * 2 + 1];
+      sMax[tid] = nmx;
+    }
+    __syncthreads();
+    // ---- O += P V : warp -> dims 64*warp.., all heads
+    {
+      const int d0 = warp * 64;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const float c0 = sCorr[mt * 16 + g], c1 = sCorr[mt * 16 + g + 8];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          acc[mt][nt][0] *= c0;
+          acc[mt][nt][1] *= c0;
+          acc[mt][nt][2] *= c1;
+          acc[mt][nt][3] *= c1;
+        }
+      }
+#pragma unroll
+      for (int k0 = 0; k0 < kBlk; k0 += 16) {
+        uint32_t bfr[8][2];
+#pragma unroll
+        for (int nt = 0; nt < 8; nt += 2) {
+          const uint32_t va =
+              smem_u32(kv + (size_t)(k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kRowE + d0 + nt * 8 + 8 * (lane >> 4));
+          ldsm_x4_t(va, bfr[nt][0], bfr[nt][1], bfr[nt + 1][0], bfr[nt + 1][1]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          const uint32_t pa =
+              smem_u32(sP + (size_t)(mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kPPad + k0 + 8 * (lane >> 4));
+          ldsm_x4(pa, a0, a1, a2, a3);
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt) mma16816(acc[mt][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---------------- epilogue
+  const int d0 = warp * 64;
+  if (nsplit == 1) {
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int h = mt * 16 + g + 8 * half;
+        const float den = sSum[h] + expf(p.sink[h] - sMax[h]);
+        const float inv = 1.f / den;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int d = d0 + nt * 8 + 2 * cq;
+          float e = acc[mt][nt][2 * half] * inv, o = acc[mt][nt][2 * half + 1] * inv;
+          // output rounds to bf16 before the inverse rotation, as the reference does
+          e = __bfloat162float(__float2bfloat16(e));
+          o = __bfloat162float(__float2bfloat16(o));
+          if (d >= kDh - 64) {
+            const int pi = (d - (kDh - 64)) >> 1;
+            const float c = p.rope_cos[(size_t)rope_pos * 32 + pi], s = -p.rope_sin[(size_t)rope_pos * 32 + pi];
+            const float ne = e * c - o * s, no = e * s + o * c;
+            e = ne;
+            o = no;
+          }
+          *reinterpret_cast<uint32_t*>(p.out + (size_t)t * kH * kDh + (size_t)h * kDh + d) = pack_bf16(e, o);
+        }
+      }
+    }
+  } else {
+    float* ws = p.workspace + ((size_t)t * nsplit + split) * kH * (kDh + 2);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int h = mt * 16 + g + 8 * half;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int d = d0 + nt * 8 + 2 * cq;
+          ws[(size_t)h * (kDh + 2) + d] = acc[mt][nt][2 * half];
+          ws[(size_t)h * (kDh + 2) + d + 1] = acc[mt][nt][2 * half + 1];
+        }
+      }
+    }
+    if (tid < kH) {
+      ws[(size_t)tid * (kDh + 2) + kDh] = sMax[tid];
+      ws[(size_t)tid * (kDh + 2) + kDh + 1] = sSum[tid];
+    }
+  }
+}
+
+// Merge split partials: one CTA per token, thread -> (head, dim pair).
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p, int nsplit) {
+  const int t = blockIdx.x;
+  const int rope_pos = p.rope_pos ? p.rope_pos[t] : p.pos[t];
+  const float* base = p.workspace + (size_t)t * nsplit * kH * (kDh + 2);
+  for (int e = threadIdx.x; e < kH * kDh / 2; e += blockDim.x) {
+    const int h = e / (kDh / 2), d = 2 * (e % (kDh / 2));
+    float m = -1e30f;
+    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, base[((size_t)s * kH + h) * (kDh + 2) + kDh]);
+    float num0 = 0.f, num1 = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float* w = base + ((size_t)s * kH + h) * (kDh + 2);
+      const float f = expf(w[kDh] - m);
+      num0 += w[d] * f;
+      num1 += w[d + 1] * f;
+      den += w[kDh + 1] * f;
+    }
+    den += expf(p.sink[h] - m);
+    float e0 = __bfloat162float(__float2bfloat16(num0 / den));
+    float o0 = __bfloat162float(__float2bfloat16(num1 / den));
+    if (d >= kDh - 64) {
+      const int pi = (d - (kDh - 64)) >> 1;
+      const float c = p.rope_cos[(size_t)rope_pos * 32 + pi], s = -p.rope_sin[(size_t)rope_pos * 32 + pi];
+      const float ne = e0 * c - o0 * s, no = e0 * s + o0 * c;
+      e0 = ne;
+      o0 = no;
+    }
+    *reinterpret_cast<uint32_t*>(p.out + (size_t)t * kH * kDh + (size_t)h * kDh + d) = pack_bf16(e0, o0);
+  }
+}
+
+size_t attn_smem_bytes() { return kSmemTotal; }
+
+cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid(p.T, nsplit);
+  attn_kernel<<<grid, 256, kSmemTotal, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || nsplit == 1) return e;
+  attn_combine_kernel<<<p.T, 256, 0, st>>>(p, nsplit);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

@@ -154,6 +154,280 @@ void fp4_roundtrip(const Tensor& x, Tensor& y, int64_t block, bool e4m3_scale) {
 
 int64_t gemm_smem(int64_t bn) { return dsv4::gemm_smem_bytes((int)bn); }
 
+template <typename T>
+T* ptr(const optional<Tensor>& t) {
+  return t ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+template <typename T>
+T* ptr(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+using bf16 = __nv_bfloat16;
+
+void hc_step(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
+             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn, const optional<Tensor>& scale,
+             const optional<Tensor>& base, const optional<Tensor>& cw, int64_t cw_stride,
+             const optional<Tensor>& norm_w, const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials,
+             const optional<Tensor>& u, const optional<Tensor>& uq, const optional<Tensor>& usf,
+             const optional<Tensor>& tap, int64_t T, int64_t iters, double hc_eps, double norm_eps) {
+  CHECK_CUDA(X);
+  TORCH_CHECK(X.size(1) == 4, "hc_mult must be 4");
+  dsv4::HcParams p{};
+  p.T = (int)T;
+  p.D = (int)X.size(2);
+  TORCH_CHECK(p.D % 128 == 0, "D % 128");
+  TORCH_CHECK(partials.numel() >= T * dsv4::hc_num_slices(p.D) * 26, "partials too small");
+  p.X = ptr<bf16>(X);
+  p.Y = ptr<const bf16>(Y);
+  p.yperm = ptr<const bf16>(yperm);
+  p.pos = ptr<const int>(pos);
+  p.topk = (int)topk;
+  p.prev_mix = ptr<const float>(prev_mix);
+  p.fn = ptr<const float>(fn);
+  p.scale = ptr<const float>(scale);
+  p.base = ptr<const float>(base);
+  p.cw = ptr<const float>(cw);
+  p.cw_stride = (int)cw_stride;
+  p.norm_w = ptr<const bf16>(norm_w);
+  p.mix_out = ptr<float>(mix_out);
+  p.c = ptr<bf16>(c);
+  p.partials = ptr<float>(partials);
+  p.u = ptr<bf16>(u);
+  p.uq = ptr<uint8_t>(uq);
+  p.usf = ptr<uint8_t>(usf);
+  p.tap = ptr<bf16>(tap);
+  p.iters = (int)iters;
+  p.hc_eps = (float)hc_eps;
+  p.norm_eps = (float)norm_eps;
+  const c10::cuda::CUDAGuard guard(X.device());
+  CUDA_OK(dsv4::hc_step(p, cur_stream()));
+}
+
+void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const optional<Tensor>& rope_pos,
+               bool q_head_norm, double norm_eps, const Tensor& kv_step, const Tensor& ring,
+               const optional<Tensor>& comp, const Tensor& slot, const Tensor& pos, const Tensor& chunk_start,
+               const Tensor& step_row0, const optional<Tensor>& comp_idx, const optional<Tensor>& comp_cnt,
+               const Tensor& sink, double scale, const Tensor& out, const optional<Tensor>& workspace, int64_t T,
+               int64_t nsplit) {
+  CHECK_CUDA(q);
+  TORCH_CHECK(q.size(-1) == 512 && q.size(-2) == 64, "q must be [T, 64, 512]");
+  dsv4::AttnParams p{};
+  p.T = (int)T;
+  p.q = ptr<const bf16>(q);
+  p.q_stride = 64 * 512;
+  p.rope_cos = ptr<const float>(cos);
+  p.rope_sin = ptr<const float>(sin);
+  p.rope_pos = ptr<const int>(rope_pos);
+  p.q_head_norm = q_head_norm;
+  p.norm_eps = (float)norm_eps;
+  p.kv_step = ptr<const bf16>(kv_step);
+  p.ring = ptr<const bf16>(ring);
+  p.W = (int)ring.size(1);
+  p.comp = ptr<const bf16>(comp);
+  p.max_c = comp ? (int)comp->size(1) : 0;
+  p.slot = ptr<const int>(slot);
+  p.pos = ptr<const int>(pos);
+  p.chunk_start = ptr<const int>(chunk_start);
+  p.step_row0 = ptr<const int>(step_row0);
+  p.comp_idx = ptr<const int>(comp_idx);
+  p.comp_k = comp_idx ? (int)comp_idx->size(1) : 0;
+  p.comp_cnt = ptr<const int>(comp_cnt);
+  if (comp) TORCH_CHECK(comp_cnt.has_value(), "comp_cnt required with comp");
+  p.sink = ptr<const float>(sink);
+  p.scale = (float)scale;
+  p.out = ptr<bf16>(out);
+  p.workspace = ptr<float>(workspace);
+  if (nsplit > 1) TORCH_CHECK(workspace && workspace->numel() >= T * nsplit * 64 * 514, "attention workspace");
+  const c10::cuda::CUDAGuard guard(q.device());
+  CUDA_OK(dsv4::attention(p, (int)nsplit, cur_stream()));
+}
+
+void qkv_post(const Tensor& in, int64_t q_dim, int64_t kv_dim, const Tensor& q_norm_w, const Tensor& kv_norm_w,
+              double eps, const Tensor& qr_q, const Tensor& qr_sf, const Tensor& cos, const Tensor& sin,
+              const Tensor& pos, const Tensor& kv_out, int64_t T) {
+  dsv4::QkvParams p{};
+  p.T = (int)T;
+  p.q_dim = (int)q_dim;
+  p.kv_dim = (int)kv_dim;
+  TORCH_CHECK(q_dim % 128 == 0 && kv_dim % 32 == 0, "dims");
+  p.in = ptr<const bf16>(in);
+  p.q_norm_w = ptr<const bf16>(q_norm_w);
+  p.kv_norm_w = ptr<const bf16>(kv_norm_w);
+  p.eps = (float)eps;
+  p.qr_q = ptr<uint8_t>(qr_q);
+  p.qr_sf = ptr<uint8_t>(qr_sf);
+  p.rope_cos = ptr<const float>(cos);
+  p.rope_sin = ptr<const float>(sin);
+  p.pos = ptr<const int>(pos);
+  p.kv_out = ptr<bf16>(kv_out);
+  const c10::cuda::CUDAGuard guard(in.device());
+  CUDA_OK(dsv4::qkv_post(p, cur_stream()));
+}
+
+void idx_q_prep(const Tensor& q, int64_t T, int64_t n_heads, int64_t head_dim, const Tensor& cos, const Tensor& sin,
+                const Tensor& pos, const optional<Tensor>& w_in, double w_scale, const optional<Tensor>& w_out) {
+  CUDA_OK(dsv4::idx_q_prep(ptr<bf16>(q), (int)T, (int)n_heads, (int)head_dim, ptr<const float>(cos),
+                           ptr<const float>(sin), ptr<const int>(pos), ptr<const float>(w_in), (float)w_scale,
+                           ptr<float>(w_out), cur_stream()));
+}
+
+void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g_slot, const Tensor& g_index, const Tensor& g_chunk_start,
+                   const Tensor& g_row0, int64_t r, int64_t co, const Tensor& proj, const optional<Tensor>& ape,
+                   const Tensor& ring, const Tensor& norm_w, double eps, const Tensor& cos, const Tensor& sin,
+                   const Tensor& comp_out, const optional<Tensor>& wk, const optional<Tensor>& k_norm_w,
+                   const optional<Tensor>& idx_out) {
+  dsv4::CompParams p{};
+  p.n_groups = (int)n_groups;
+  p.n_groups_dev = ptr<const int>(n_groups_dev);
+  p.g_slot = ptr<const int>(g_slot);
+  p.g_index = ptr<const int>(g_index);
+  p.g_chunk_start = ptr<const int>(g_chunk_start);
+  p.g_row0 = ptr<const int>(g_row0);
+  p.r = (int)r;
+  p.co = (int)co;
+  p.dh = (int)comp_out.size(2);
+  p.proj = ptr<const float>(proj);
+  p.ape = ptr<const float>(ape);
+  p.ring = ptr<const float>(ring);
+  p.norm_w = ptr<const bf16>(norm_w);
+  p.eps = (float)eps;
+  p.rope_cos = ptr<const float>(cos);
+  p.rope_sin = ptr<const float>(sin);
+  p.comp_out = ptr<bf16>(comp_out);
+  p.max_c = (int)comp_out.size(1);
+  p.wk = ptr<const bf16>(wk);
+  p.k_norm_w = ptr<const bf16>(k_norm_w);
+  p.idx_out = ptr<bf16>(idx_out);
+  p.idx_dim = idx_out ? (int)idx_out->size(2) : 0;
+  CUDA_OK(dsv4::compress_pool(p, cur_stream()));
+}
+
+void ring_update(const Tensor& ring, const Tensor& src, int64_t T, const Tensor& slot, const Tensor& pos,
+                 const Tensor& last_pos) {
+  const int depth = (int)ring.size(1);
+  const int width = (int)ring.size(2);
+  if (ring.scalar_type() == at::kFloat)
+    CUDA_OK(dsv4::ring_update_f32(ptr<float>(ring), depth, width, ptr<const float>(src), (int)T, ptr<const int>(slot),
+                                  ptr<const int>(pos), ptr<const int>(last_pos), cur_stream()));
+  else
+    CUDA_OK(dsv4::ring_update_bf16(ptr<bf16>(ring), depth, width, ptr<const bf16>(src), (int)T, ptr<const int>(slot),
+                                   ptr<const int>(pos), ptr<const int>(last_pos), cur_stream()));
+}
+
+void router_topk(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
+                 double route_scale, const Tensor& ids, const Tensor& wts) {
+  CUDA_OK(dsv4::router_topk(ptr<const float>(logits), (int)T, (int)logits.size(1), ptr<const float>(bias), (int)topk,
+                            (int)score_func, (float)route_scale, ptr<int>(ids), ptr<float>(wts), cur_stream()));
+}
+
+void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const Tensor& ids, const Tensor& wts,
+              const Tensor& counts, const Tensor& seg_start, const Tensor& rank, int64_t tile_rows, int64_t m13,
+              int64_t m2, const Tensor& tiles13, const Tensor& n_tiles13, const Tensor& tiles2,
+              const Tensor& n_tiles2, int64_t cap_rows, const Tensor& pos, const Tensor& row_scale,
+              const Tensor& err) {
+  dsv4::MoePlanParams p{};
+  p.T = (int)T;
+  p.topk = (int)topk;
+  p.E_local = (int)e_local;
+  p.e_begin = (int)e_begin;
+  p.ids = ptr<const int>(ids);
+  p.wts = ptr<const float>(wts);
+  p.counts = ptr<int>(counts);
+  p.seg_start = ptr<int>(seg_start);
+  p.rank = ptr<int>(rank);
+  p.tile_rows = (int)tile_rows;
+  p.m13 = (int)m13;
+  p.m2 = (int)m2;
+  p.tiles13 = ptr<int4>(tiles13);
+  p.n_tiles13 = ptr<int>(n_tiles13);
+  p.tiles2 = ptr<int4>(tiles2);
+  p.n_tiles2 = ptr<int>(n_tiles2);
+  p.max_tiles13 = (int)tiles13.size(0);
+  p.max_tiles2 = (int)tiles2.size(0);
+  p.cap_rows = (int)cap_rows;
+  p.pos = ptr<int>(pos);
+  p.row_scale = ptr<float>(row_scale);
+  p.err = ptr<uint32_t>(err);
+  CUDA_OK(dsv4::moe_plan(p, cur_stream()));
+}
+
+void moe_scatter(const Tensor& xq, const Tensor& xsf, int64_t T, int64_t topk, const Tensor& pos, const Tensor& pq,
+                 const Tensor& psf) {
+  CUDA_OK(dsv4::moe_scatter(ptr<const uint8_t>(xq), ptr<const uint8_t>(xsf), (int)T, (int)xq.size(1), (int)topk,
+                            ptr<const int>(pos), ptr<uint8_t>(pq), ptr<uint8_t>(psf), cur_stream()));
+}
+
+void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const Tensor& slot, const Tensor& clen,
+                  int64_t topk, const Tensor& out_idx, const Tensor& out_cnt, const optional<Tensor>& cand,
+                  int64_t cand_mode, int64_t cand_block, int64_t cand_topk, int64_t T, const Tensor& err,
+                  const optional<Tensor>& kcache_alt, const optional<Tensor>& pos,
+                  const optional<Tensor>& chunk_start, const optional<Tensor>& last_pos, int64_t own_r) {
+  dsv4::IdxParams p{};
+  p.T = (int)T;
+  p.n_heads = (int)q.size(1);
+  p.head_dim = (int)q.size(2);
+  p.q = ptr<const bf16>(q);
+  p.w = ptr<const float>(w);
+  p.kcache = ptr<const bf16>(kcache);
+  p.max_c = (int)kcache.size(1);
+  p.slot = ptr<const int>(slot);
+  p.clen = ptr<const int>(clen);
+  p.topk = (int)topk;
+  p.out_idx = ptr<int>(out_idx);
+  p.out_cnt = ptr<int>(out_cnt);
+  p.cand = ptr<uint8_t>(cand);
+  p.cand_mode = (int)cand_mode;
+  p.cand_block = (int)std::max<int64_t>(1, cand_block);
+  p.cand_topk = (int)cand_topk;
+  p.err = ptr<uint32_t>(err);
+  p.kcache_alt = ptr<const bf16>(kcache_alt);
+  p.alt_max_c = kcache_alt ? (int)kcache_alt->size(1) : 0;
+  p.pos = ptr<const int>(pos);
+  p.chunk_start = ptr<const int>(chunk_start);
+  p.last_pos = ptr<const int>(last_pos);
+  p.own_r = (int)std::max<int64_t>(1, own_r);
+  if (kcache_alt) TORCH_CHECK(pos && chunk_start && last_pos, "pos/chunk_start/last_pos required with kcache_alt");
+  CUDA_OK(dsv4::indexer_topk(p, cur_stream()));
+}
+
+void ep_pack(const Tensor& ids, const Tensor& wts, int64_t T, const Tensor& xq, const Tensor& xsf, int64_t e_local,
+             int64_t world, int64_t cap, int64_t rec, const Tensor& send, const Tensor& cnt, const Tensor& pos_back,
+             const optional<Tensor>& peer_recv, int64_t my_rank, const Tensor& err) {
+  CUDA_OK(dsv4::ep_pack(ptr<const int>(ids), ptr<const float>(wts), (int)T, (int)ids.size(1), ptr<const uint8_t>(xq),
+                        ptr<const uint8_t>(xsf), (int)xq.size(1), (int)e_local, (int)world, (int)cap, (int)rec,
+                        ptr<uint8_t>(send), ptr<int>(cnt), ptr<int>(pos_back), ptr<uint8_t* const>(peer_recv),
+                        (int)my_rank, ptr<uint32_t>(err), cur_stream()));
+}
+
+void ep_unpack_meta(const Tensor& recv, const Tensor& cnt, int64_t world, int64_t cap, int64_t rec, int64_t D,
+                    const Tensor& ids, const Tensor& wts) {
+  CUDA_OK(dsv4::ep_unpack_meta(ptr<const uint8_t>(recv), ptr<const int>(cnt), (int)world, (int)cap, (int)rec, (int)D,
+                               ptr<int>(ids), ptr<float>(wts), cur_stream()));
+}
+
+void ep_unpack_rows(const Tensor& recv, int64_t n, int64_t rec, int64_t D, const Tensor& pos, const Tensor& pq,
+                    const Tensor& psf) {
+  CUDA_OK(dsv4::ep_unpack_rows(ptr<const uint8_t>(recv), (int)n, (int)rec, (int)D, ptr<const int>(pos),
+                               ptr<uint8_t>(pq), ptr<uint8_t>(psf), cur_stream()));
+}
+
+void ep_combine_pack(const Tensor& yperm, const Tensor& pos, int64_t n, int64_t cap, const Tensor& back,
+                     const optional<Tensor>& peer_back, int64_t my_rank) {
+  CUDA_OK(dsv4::ep_combine_pack(ptr<const bf16>(yperm), ptr<const int>(pos), (int)n, (int)yperm.size(1), (int)cap,
+                                ptr<bf16>(back), ptr<bf16* const>(peer_back), (int)my_rank, cur_stream()));
+}
+
+void embed_streams(const Tensor& table, const Tensor& ids, int64_t T, const Tensor& X) {
+  CUDA_OK(dsv4::embed_streams(ptr<const bf16>(table), ptr<const int>(ids), (int)T, (int)table.size(1),
+                              (int)X.size(1), ptr<bf16>(X), cur_stream()));
+}
+
+void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out) {
+  CUDA_OK(dsv4::argmax_rows(ptr<const float>(logits), (int)T, (int)V, (int)logits.stride(0), ptr<int>(out),
+                            cur_stream()));
+}
+
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -163,4 +437,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_quant_mx", &act_quant_mx);
   m.def("act_roundtrip", &act_roundtrip);
   m.def("fp4_roundtrip", &fp4_roundtrip);
+  m.def("hc_step", &hc_step);
+  m.def("hc_num_slices", [](int64_t d) { return (int64_t)dsv4::hc_num_slices((int)d); });
+  m.def("attention", &attention);
+  m.def("attn_smem", []() { return (int64_t)dsv4::attn_smem_bytes(); });
+  m.def("qkv_post", &qkv_post);
+  m.def("idx_q_prep", &idx_q_prep);
+  m.def("compress_pool", &compress_pool);
+  m.def("ring_update", &ring_update);
+  m.def("router_topk", &router_topk);
+  m.def("moe_plan", &moe_plan);
+  m.def("moe_scatter", &moe_scatter);
+  m.def("indexer_topk", &indexer_topk);
+  m.def("embed_streams", &embed_streams);
+  m.def("ep_pack", &ep_pack);
+  m.def("ep_unpack_meta", &ep_unpack_meta);
+  m.def("ep_unpack_rows", &ep_unpack_rows);
+  m.def("ep_combine_pack", &ep_combine_pack);
+  m.def("argmax_rows", &argmax_rows);
 }

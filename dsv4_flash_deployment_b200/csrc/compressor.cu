@@ -1,0 +1,159 @@
+// KV compressor: softmax-gated pooling of r (or 2r, overlapped) token
+// projections into one compressed latent row, then RMSNorm, RoPE at the group
+// start, e2m1/e4m3-per-16 round trip and a store into the sequence's
+// compressed cache; optionally the indexer key of the same entry (latent @ wk
+// -> RMSNorm -> RoPE -> e2m1/ue8m0-per-32 round trip).  Reference:
+// _compressor_step (reference.py:547-603), _indexer_step k path (:621-640),
+// latent store (:792-807).
+//
+// One CTA per compressed entry closed in this step.  Source positions come from
+// this step's projection rows when they belong to the step, otherwise from the
+// per-sequence ring of the most recent (overlap * r) projections.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+DSV4_DEV float e2m1_qdq_c(float x, float s) {
+  const float ax = fabsf(x);
+  const int c = (ax > 0.25f * s) + (ax >= 0.75f * s) + (ax > 1.25f * s) + (ax >= 1.75f * s) + (ax > 2.5f * s) +
+                (ax >= 3.5f * s) + (ax > 5.0f * s);
+  const float mag = c <= 4 ? 0.5f * c : (c == 5 ? 3.f : (c == 6 ? 4.f : 6.f));
+  return (signbit(x) ? -mag : mag) * s;
+}
+
+template <int NT>
+DSV4_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) red[NT / 32] = s;
+  }
+  __syncthreads();
+  return red[NT / 32];
+}
+
+// 512 threads: thread d owns latent dim d (dh == 512).
+__global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
+  __shared__ float red[32];
+  __shared__ __nv_bfloat16 lat[512];
+  __shared__ float kbuf[256];
+  const int gi = blockIdx.x;
+  if (gi >= *p.n_groups_dev) return;
+  const int slot = p.g_slot[gi], g = p.g_index[gi], cs = p.g_chunk_start[gi], row0 = p.g_row0[gi];
+  const int d = threadIdx.x;
+  const int r = p.r, co = p.co, dh = p.dh;
+  const int width = 2 * co * dh;
+  const int depth = co * r;
+  // softmax over the (co * r) slots, per dim, online in fp32
+  float m = -INFINITY, ssum = 0.f, acc = 0.f;
+  const int first = g * r - (co - 1) * r;
+  for (int pp = first; pp < (g + 1) * r; ++pp) {
+    if (pp < 0) continue;
+    const int half = (pp < g * r) ? 0 : (co - 1);
+    const float* src = (pp >= cs) ? p.proj + (size_t)(row0 + pp - cs) * width
+                                  : p.ring + ((size_t)slot * depth + (pp % depth)) * width;
+    const float kv = src[half * dh + d];
+    float sc = src[co * dh + half * dh + d];
+    if (p.ape) sc += p.ape[(size_t)(pp % r) * co * dh + half * dh + d];
+    const float nm = fmaxf(m, sc);
+    const float corr = expf(m - nm);
+    const float e = expf(sc - nm);
+    ssum = ssum * corr + e;
+    acc = acc * corr + e * kv;
+    m = nm;
+  }
+  const float pooled = __bfloat162float(__float2bfloat16(acc / ssum));
+  const float ss = block_sum<512>(pooled * pooled, red);
+  const float rr = rsqrtf(ss / (float)dh + p.eps);
+  const float y = __bfloat162float(__float2bfloat16(pooled * rr * __bfloat162float(p.norm_w[d])));
+  lat[d] = __float2bfloat16(y);
+  // RoPE at the group start position, pairs (2i, 2i+1) in the last 64 dims
+  const int gp = g * r;
+  __syncthreads();
+  float z = y;
+  if (d >= dh - 64) {
+    const int pi = (d - (dh - 64)) >> 1;
+    const float c = p.rope_cos[(size_t)gp * 32 + pi], s = p.rope_sin[(size_t)gp * 32 + pi];
+    const float e = __bfloat162float(lat[d & ~1]), o = __bfloat162float(lat[d | 1]);
+    z = (d & 1) ? (e * s + o * c) : (e * c - o * s);
+    z = __bfloat162float(__float2bfloat16(z));
+  }
+  // e2m1 round trip, e4m3 scale per 16 (16 consecutive dims = half a warp)
+  {
+    float amax = fabsf(z);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    amax = fmaxf(amax, 6.f * 0.001953125f);
+    const float s = e4m3_to_f32(f32_to_e4m3(amax / 6.f));
+    p.comp_out[((size_t)slot * p.max_c + g) * dh + d] = __float2bfloat16(e2m1_qdq_c(z, s));
+  }
+  if (p.wk == nullptr) return;
+  // ---- indexer key: k = bf16(latent @ wk^T) -> RMSNorm -> RoPE -> e2m1 (ue8m0 / 32)
+  const int kd = p.idx_dim;
+  if (d < kd) {
+    float a = 0.f;
+    const __nv_bfloat16* wr = p.wk + (size_t)d * dh;
+    for (int j = 0; j < dh; ++j) a += __bfloat162float(lat[j]) * __bfloat162float(wr[j]);
+    kbuf[d] = __bfloat162float(__float2bfloat16(a));
+  }
+  __syncthreads();
+  const float kv = d < kd ? kbuf[d] : 0.f;
+  const float kss = block_sum<512>(kv * kv, red);
+  if (d >= kd) return;  // whole warps exit (kd is a multiple of 32)
+  const float kr = rsqrtf(kss / (float)kd + p.eps);
+  float kn = __bfloat162float(__float2bfloat16(kv * kr * __bfloat162float(p.k_norm_w[d])));
+  {
+    const float other = __shfl_xor_sync(0xffffffffu, kn, 1);
+    if (d >= kd - 64) {
+      const int pi = (d - (kd - 64)) >> 1;
+      const float c = p.rope_cos[(size_t)gp * 32 + pi], s = p.rope_sin[(size_t)gp * 32 + pi];
+      kn = (d & 1) ? (other * s + kn * c) : (kn * c - other * s);
+      kn = __bfloat162float(__float2bfloat16(kn));
+    }
+  }
+  const float amax = fmaxf(warp_max(fabsf(kn)), 6.f * 1.1754943508222875e-38f);
+  const float s = exp_to_f32(pow2_ceil_exp(amax, 1.f / 6.f));
+  p.idx_out[((size_t)slot * p.max_c + g) * kd + d] = __float2bfloat16(e2m1_qdq_c(kn, s));
+}
+
+cudaError_t compress_pool(const CompParams& p, cudaStream_t st) {
+  if (p.n_groups == 0) return cudaSuccess;
+  if (p.dh != 512 || (p.wk && (p.idx_dim % 32 || p.idx_dim > 256))) return cudaErrorInvalidValue;
+  compress_pool_kernel<<<p.n_groups, 512, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+__global__ void ring_update_kernel(T* ring, int depth, int width, const T* src, int T_, const int* slot,
+                                   const int* pos, const int* last_pos) {
+  const int t = blockIdx.x;
+  if (t >= T_) return;
+  const int ps = pos[t];
+  if (ps <= last_pos[t] - depth) return;  // overwritten later in the same step
+  T* dst = ring + ((size_t)slot[t] * depth + (ps % depth)) * width;
+  const T* s = src + (size_t)t * width;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) dst[i] = s[i];
+}
+
+cudaError_t ring_update_f32(float* ring, int depth, int width, const float* src, int T, const int* slot,
+                            const int* pos, const int* last_pos, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  ring_update_kernel<float><<<T, 256, 0, st>>>(ring, depth, width, src, T, slot, pos, last_pos);
+  return cudaGetLastError();
+}
+
+cudaError_t ring_update_bf16(__nv_bfloat16* ring, int depth, int width, const __nv_bfloat16* src, int T,
+                             const int* slot, const int* pos, const int* last_pos, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  ring_update_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(ring, depth, width, src, T, slot, pos, last_pos);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

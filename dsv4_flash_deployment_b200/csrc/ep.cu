@@ -1,0 +1,134 @@
+// Expert-parallel dispatch / combine packing.
+//
+// Transport record of one (token, expert) pair: [e4m3 row D bytes | ue8m0
+// scales D/32 bytes | local expert id int32 | routing weight f32], padded to
+// 16 bytes.  The source rank packs every pair into the per-destination region
+// of its send buffer (fixed capacity per peer, so the exchange needs no host
+// synchronization and replays inside a CUDA graph); the destination unpacks
+// records into the permuted expert buffer; expert outputs travel back in
+// bf16 rows, and the source combines them through the (peer * cap + slot)
+// position of each pair (the mHC boundary kernel reads them directly).
+//
+// The same packers feed the NCCL all-to-all baseline and the NVLink
+// peer-store exchange (records written straight into the owner's receive
+// buffer).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+__global__ void ep_pack_kernel(const int* __restrict__ ids, const float* __restrict__ wts, int T, int topk,
+                               const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int D, int e_local,
+                               int world, int cap, int rec, uint8_t* __restrict__ send, int* cnt, int* pos_back,
+                               uint8_t* const* peer_recv, int my_rank, uint32_t* err) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= T * topk) return;
+  const int t = w / topk;
+  const int e = ids[w];
+  const int dest = e / e_local;
+  int slot = 0;
+  if (lane == 0) slot = atomicAdd(&cnt[dest], 1);
+  slot = __shfl_sync(0xffffffffu, slot, 0);
+  if (slot >= cap) {
+    if (lane == 0) {
+      pos_back[w] = -1;
+      report_error(err, ERR_CAPACITY, KID_MOE, 2);
+    }
+    return;
+  }
+  // direct peer store (NVLink) when the peer's receive buffer is mapped, else the local send buffer
+  uint8_t* dst = peer_recv ? peer_recv[dest] + ((size_t)my_rank * cap + slot) * rec
+                           : send + ((size_t)dest * cap + slot) * rec;
+  const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)t * D);
+  for (int i = lane; i < D / 16; i += 32) reinterpret_cast<uint4*>(dst)[i] = src[i];
+  const int kt = D / 128;
+  for (int b = lane; b < D / 32; b += 32) dst[D + b] = xsf[sf_chunk_offset(t, b, kt)];
+  if (lane == 0) {
+    *reinterpret_cast<int*>(dst + D + D / 32) = e - dest * e_local;
+    *reinterpret_cast<float*>(dst + D + D / 32 + 4) = wts[w];
+    pos_back[w] = dest * cap + slot;
+  }
+}
+
+cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uint8_t* xq, const uint8_t* xsf, int D,
+                    int e_local, int world, int cap, int rec, uint8_t* send, int* cnt, int* pos_back,
+                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, cudaStream_t st) {
+  const long long warps = (long long)T * topk;
+  if (warps == 0) return cudaSuccess;
+  ep_pack_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(ids, wts, T, topk, xq, xsf, D, e_local, world,
+                                                                      cap, rec, send, cnt, pos_back, peer_recv,
+                                                                      my_rank, err);
+  return cudaGetLastError();
+}
+
+// recv [world * cap] records with per-peer counts -> ids/wts (-1 beyond count).
+__global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, const int* __restrict__ cnt, int world,
+                                      int cap, int rec, int D, int* ids, float* wts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= world * cap) return;
+  const int p = i / cap, j = i % cap;
+  if (j < cnt[p]) {
+    const uint8_t* r = recv + (size_t)i * rec;
+    ids[i] = *reinterpret_cast<const int*>(r + D + D / 32);
+    wts[i] = *reinterpret_cast<const float*>(r + D + D / 32 + 4);
+  } else {
+    ids[i] = -1;
+    wts[i] = 0.f;
+  }
+}
+
+cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
+                           float* wts, cudaStream_t st) {
+  const int n = world * cap;
+  ep_unpack_meta_kernel<<<(n + 255) / 256, 256, 0, st>>>(recv, cnt, world, cap, rec, D, ids, wts);
+  return cudaGetLastError();
+}
+
+// Received records -> permuted expert rows (e4m3 + scale chunks), one warp per record.
+__global__ void ep_unpack_rows_kernel(const uint8_t* __restrict__ recv, int n, int rec, int D,
+                                      const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const int row = pos[w];
+  if (row < 0) return;
+  const uint8_t* r = recv + (size_t)w * rec;
+  uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
+  for (int i = lane; i < D / 16; i += 32) dst[i] = reinterpret_cast<const uint4*>(r)[i];
+  const int kt = D / 128;
+  for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = r[D + b];
+}
+
+cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
+                           cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  ep_unpack_rows_kernel<<<(unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st>>>(recv, n, rec, D, pos, pq, psf);
+  return cudaGetLastError();
+}
+
+// Expert outputs back to record order: back[i] = yperm[pos[i]] (bf16 rows), or
+// written straight into the source rank's return buffer over NVLink.
+__global__ void ep_combine_pack_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ pos, int n,
+                                       int D, int cap, __nv_bfloat16* back, __nv_bfloat16* const* peer_back,
+                                       int my_rank) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const int row = pos[w];
+  if (row < 0) return;
+  const int src_rank = w / cap, j = w % cap;
+  __nv_bfloat16* dst = peer_back ? peer_back[src_rank] + ((size_t)my_rank * cap + j) * D : back + (size_t)w * D;
+  const uint4* s = reinterpret_cast<const uint4*>(yperm + (size_t)row * D);
+  for (int i = lane; i < D / 8; i += 32) reinterpret_cast<uint4*>(dst)[i] = s[i];
+}
+
+cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
+                            __nv_bfloat16* const* peer_back, int my_rank, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  ep_combine_pack_kernel<<<(unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st>>>(yperm, pos, n, D, cap, back,
+                                                                                      peer_back, my_rank);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

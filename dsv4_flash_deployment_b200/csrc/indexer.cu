@@ -1,0 +1,225 @@
+// Lightning-indexer scoring and top-k selection (reference.py:605-702).
+//
+// For query token t with causal compressed length clen:
+//   raw[h, j]  = bf16(q[h] . k[j])                  (fp32 dot of bf16 values)
+//   score[j]   = bf16( sum_h bf16(relu(raw[h, j]) * w[h]) )
+// optional level-1 candidate mask (V4.1): layer 20 keeps the top cand_topk
+// blocks of cand_block entries by block max (the block holding the newest
+// entry is always kept); later indexers mask scores outside those blocks.
+// Output: the top-k entries sorted by index ascending (ties broken toward the
+// lower index); when clen <= topk every entry is selected, as top_k of a
+// shorter list returns all of it.
+//
+// One CTA (256 threads) per token; lane-per-row scoring with the query in
+// shared memory; 4-pass radix select on order-preserving keys in shared memory.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+DSV4_DEV uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Returns the k-th largest key (1-based k) among keys[0..n) and the number of
+// keys strictly greater than it.
+DSV4_DEV void radix_select(const uint32_t* keys, int n, int k, uint32_t* hist, uint32_t& kth, int& n_greater) {
+  __shared__ uint32_t s_prefix, s_mask, s_k;
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_k = k;
+  }
+  __syncthreads();
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t pre = s_prefix, msk = s_mask;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t key = keys[i];
+      if ((key & msk) == pre) atomicAdd(&hist[(key >> shift) & 0xFF], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t need = s_k;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (hist[b] >= need) break;
+        need -= hist[b];
+      }
+      s_prefix = pre | ((uint32_t)b << shift);
+      s_mask = msk | (0xFFu << shift);
+      s_k = need;
+    }
+    __syncthreads();
+  }
+  kth = s_prefix;
+  // count strictly greater
+  __shared__ int s_gt;
+  if (threadIdx.x == 0) s_gt = 0;
+  __syncthreads();
+  int local = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) local += keys[i] > kth;
+  atomicAdd(&s_gt, local);
+  __syncthreads();
+  n_greater = s_gt;
+}
+
+// Writes, in index order, every j with keys[j] > kth, plus the first (k - n_gt)
+// indices with keys[j] == kth.  Block-wide ordered compaction, chunk by chunk.
+DSV4_DEV int ordered_select(const uint32_t* keys, int n, uint32_t kth, int n_eq_take, int* out) {
+  __shared__ int s_base, s_eq_base;
+  __shared__ int s_warp[8], s_warp_eq[8];
+  if (threadIdx.x == 0) {
+    s_base = 0;
+    s_eq_base = 0;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + threadIdx.x;
+    const uint32_t key = i < n ? keys[i] : 0u;
+    const bool gt = i < n && key > kth;
+    const bool eq = i < n && key == kth;
+    const unsigned mg = __ballot_sync(0xffffffffu, gt), me = __ballot_sync(0xffffffffu, eq);
+    if (lane == 0) {
+      s_warp[warp] = __popc(mg);
+      s_warp_eq[warp] = __popc(me);
+    }
+    __syncthreads();
+    int wo = 0, weo = 0;
+    for (int w = 0; w < warp; ++w) {
+      wo += s_warp[w];
+      weo += s_warp_eq[w];
+    }
+    const int below = __popc(mg & ((1u << lane) - 1)), below_eq = __popc(me & ((1u << lane) - 1));
+    const int eq_rank = s_eq_base + weo + below_eq;
+    // selected entries before this one = gt so far + min(eq so far, n_eq_take)
+    int tot_gt = 0, tot_eq = 0;
+    for (int w = 0; w < 8; ++w) {
+      tot_gt += s_warp[w];
+      tot_eq += s_warp_eq[w];
+    }
+    if (gt || (eq && eq_rank < n_eq_take)) {
+      const int gt_before = s_base + wo + below;  // gt entries strictly before i (global)
+      const int eq_before = min(eq_rank, n_eq_take);
+      out[gt_before + eq_before] = i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_base += tot_gt;
+      s_eq_base += tot_eq;
+    }
+    __syncthreads();
+  }
+  return s_base + min(s_eq_base, n_eq_take);
+}
+
+__global__ void __launch_bounds__(256) indexer_topk_kernel(IdxParams p) {
+  extern __shared__ uint8_t smem[];
+  const int t = blockIdx.x;
+  const int H = p.n_heads, hd = p.head_dim;
+  __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem);
+  float* sw = reinterpret_cast<float*>(smem + (size_t)H * hd * 2);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sw + H);
+  uint32_t* keys = hist + 256;
+  const int clen = p.clen[t];
+  const int slot = p.slot[t];
+  for (int i = threadIdx.x; i < H * hd; i += blockDim.x) sq[i] = p.q[(size_t)t * H * hd + i];
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sw[i] = p.w[(size_t)t * H + i];
+  __syncthreads();
+  const int k = p.topk;
+  if (clen <= k) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) p.out_idx[(size_t)t * k + j] = j < clen ? j : -1;
+    if (threadIdx.x == 0) p.out_cnt[t] = clen;
+    if (p.cand_mode != 1) return;
+  }
+  // ---- scores (lane per row)
+  const bool use_alt = p.kcache_alt != nullptr && ((p.pos[t] + 1) % p.own_r) != 0 &&
+                       p.chunk_start[t] == p.last_pos[t];
+  const __nv_bfloat16* kbase = use_alt ? p.kcache_alt + (size_t)slot * p.alt_max_c * hd
+                                       : p.kcache + (size_t)slot * p.max_c * hd;
+  for (int j = threadIdx.x; j < clen; j += blockDim.x) {
+    const __nv_bfloat16* kr = kbase + (size_t)j * hd;
+    float sum = 0.f;
+    for (int h = 0; h < H; ++h) {
+      float dot = 0.f;
+      const __nv_bfloat16* qh = sq + h * hd;
+      for (int d = 0; d < hd; d += 8) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(kr + d);
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(qh + d);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a = __bfloat1622float2(k2[e]), b = __bfloat1622float2(q2[e]);
+          dot += a.x * b.x + a.y * b.y;
+        }
+      }
+      const float raw = __bfloat162float(__float2bfloat16(dot));
+      sum += __bfloat162float(__float2bfloat16(fmaxf(raw, 0.f) * sw[h]));
+    }
+    float sc = __bfloat162float(__float2bfloat16(sum));
+    if (p.cand_mode == 2 && !p.cand[(size_t)t * (p.max_c / p.cand_block) + j / p.cand_block]) sc = -INFINITY;
+    keys[j] = order_key(sc);
+  }
+  __syncthreads();
+  if (p.cand_mode == 1) {
+    // block maxima (newest block forced in), top cand_topk blocks -> mask
+    const int nb = (clen + p.cand_block - 1) / p.cand_block;
+    uint32_t* bkeys = keys + clen;
+    const int last = (clen - 1) / p.cand_block;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+      uint32_t m = 0;
+      for (int j = b * p.cand_block; j < min(clen, (b + 1) * p.cand_block); ++j) m = max(m, keys[j]);
+      bkeys[b] = (b == last) ? order_key(INFINITY) : m;
+    }
+    __syncthreads();
+    uint8_t* cand = p.cand + (size_t)t * (p.max_c / p.cand_block);
+    if (nb <= p.cand_topk) {
+      for (int b = threadIdx.x; b < p.max_c / p.cand_block; b += blockDim.x)
+        cand[b] = (b < nb) && bkeys[b] > order_key(-INFINITY);
+    } else {
+      uint32_t kth;
+      int ngt;
+      radix_select(bkeys, nb, p.cand_topk, hist, kth, ngt);
+      // ties at the threshold: keep lower block ids
+      __shared__ int s_eq;
+      if (threadIdx.x == 0) {
+        s_eq = 0;
+        for (int b = 0; b < nb; ++b) {
+          const bool keep = bkeys[b] > kth || (bkeys[b] == kth && s_eq < p.cand_topk - ngt && (++s_eq, true));
+          cand[b] = keep && bkeys[b] > order_key(-INFINITY);
+        }
+      }
+      __syncthreads();
+      for (int b = nb + threadIdx.x; b < p.max_c / p.cand_block; b += blockDim.x) cand[b] = 0;
+    }
+    __syncthreads();
+    if (clen <= k) return;
+  }
+  uint32_t kth;
+  int ngt;
+  radix_select(keys, clen, k, hist, kth, ngt);
+  const int cnt = ordered_select(keys, clen, kth, k - ngt, p.out_idx + (size_t)t * k);
+  for (int j = cnt + threadIdx.x; j < k; j += blockDim.x) p.out_idx[(size_t)t * k + j] = -1;
+  if (threadIdx.x == 0) p.out_cnt[t] = cnt;
+}
+
+cudaError_t indexer_topk(const IdxParams& p, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  const size_t smem = (size_t)p.n_heads * p.head_dim * 2 + p.n_heads * 4 + 256 * 4 +
+                      (size_t)(p.max_c + p.max_c / max(1, p.cand_block) + 1) * 4;
+  // dynamic + the kernel's static shared memory must stay under the 227 KB opt-in limit
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;
+  static size_t configured = 48 * 1024;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  indexer_topk_kernel<<<p.T, 256, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

@@ -1,4 +1,4 @@
-// Host launchers of the element-wise / fused kernels (one .cu file each).
+// Host launchers and parameter blocks of the fused kernels (one .cu file each).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -6,11 +6,191 @@
 
 namespace dsv4 {
 
-// quant.cu
+// ------------------------------------------------------------ quant.cu
 cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t* q, int ldq, uint8_t* sf,
                          int k_tiles, cudaStream_t st);
 cudaError_t act_roundtrip(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, cudaStream_t st);
 cudaError_t fp4_roundtrip(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, int block, int e4m3_scale,
                           cudaStream_t st);
+
+// -------------------------------------------------------------- mhc.cu
+struct HcParams {
+  int T, D;
+  __nv_bfloat16* X;                 // [T, 4, D] residual streams (updated in place)
+  const __nv_bfloat16* Y;           // sublayer output [T, D] (or the shared-expert term with yperm)
+  const __nv_bfloat16* yperm;       // MoE: expert outputs in permuted-row order [R, D]
+  const int* pos;                   // MoE: [T, topk] permuted row per slot (-1 = none)
+  int topk;
+  const float* prev_mix;            // [T, 24] (pre | post | comb) of the previous boundary
+  const float* fn;                  // [24, 4*D] mixing projection (null = no mixes)
+  const float* scale;               // [3]
+  const float* base;                // [24]
+  const float* cw;                  // collapse weights: cw[t * cw_stride + i]
+  int cw_stride;
+  const __nv_bfloat16* norm_w;      // [D]
+  float* mix_out;                   // [T, 24]
+  __nv_bfloat16* c;                 // scratch [T, D]
+  float* partials;                  // scratch [T, n_slices, 26]
+  __nv_bfloat16* u;                 // [T, D] normalized collapse
+  uint8_t* uq;                      // [T_pad, D] e4m3 (optional)
+  uint8_t* usf;                     // scale chunks of uq
+  __nv_bfloat16* tap;               // optional [T, D] mean of the updated streams
+  int iters;
+  float hc_eps, norm_eps;
+};
+int hc_num_slices(int D);
+cudaError_t hc_step(const HcParams& p, cudaStream_t st);
+
+// -------------------------------------------------------- attention.cu
+constexpr int kAttnMaxRows = 768;   // window (<= 256) + selected compressed rows
+struct AttnParams {
+  int T;
+  const __nv_bfloat16* q;           // [T, 64, 512]
+  int q_stride;
+  const float* rope_cos;            // [positions, 32]
+  const float* rope_sin;
+  const int* rope_pos;              // optional rope position (default pos)
+  int q_head_norm;
+  float norm_eps;
+  const __nv_bfloat16* kv_step;     // this step's window rows [R, 512]
+  const __nv_bfloat16* ring;        // [slots, W, 512]
+  int W;
+  const __nv_bfloat16* comp;        // [slots, max_c, 512] or null
+  int max_c;
+  const int* slot;
+  const int* pos;
+  const int* chunk_start;           // first position of this step for the token's sequence
+  const int* step_row0;             // kv_step row holding chunk_start
+  const int* comp_idx;              // [T, comp_k] selected compressed rows (null = dense 0..cnt)
+  int comp_k;
+  const int* comp_cnt;              // [T] number of valid compressed rows
+  const float* sink;                // [64]
+  float scale;
+  __nv_bfloat16* out;               // [T, 64, 512]
+  float* workspace;                 // split partials
+};
+size_t attn_smem_bytes();
+cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st);
+
+// -------------------------------------------------------- norm_rope.cu
+struct QkvParams {
+  int T, q_dim, kv_dim;
+  const __nv_bfloat16* in;          // [T, q_dim + kv_dim] fused wq_a|wkv output
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* kv_norm_w;
+  float eps;
+  uint8_t* qr_q;                    // [T_pad, q_dim] e4m3
+  uint8_t* qr_sf;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int* pos;
+  __nv_bfloat16* kv_out;            // [T, kv_dim]
+};
+cudaError_t qkv_post(const QkvParams& p, cudaStream_t st);
+
+// Indexer query: per head RoPE on the last 64 dims + e2m1 round trip (block 32,
+// ue8m0); weights: bf16(w * scale).
+cudaError_t idx_q_prep(__nv_bfloat16* q, int T, int n_heads, int head_dim, const float* cos, const float* sin,
+                       const int* pos, const float* w_in, float w_scale, float* w_out, cudaStream_t st);
+
+// -------------------------------------------------------- compressor.cu
+struct CompParams {
+  int n_groups;                     // grid size (upper bound)
+  const int* n_groups_dev;          // actual number of closed groups (device)
+  const int* g_slot;
+  const int* g_index;               // compressed entry index g (closes at position g*r + r - 1)
+  const int* g_chunk_start;         // first position of this step for the group's sequence
+  const int* g_row0;                // proj_step row of g_chunk_start
+  int r, co, dh;
+  const float* proj;                // [T, 2*co*dh] (kv | score) this step
+  const float* ape;                 // [r, co*dh] or null
+  const float* ring;                // [slots, co*r, 2*co*dh]
+  const __nv_bfloat16* norm_w;
+  float eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  __nv_bfloat16* comp_out;          // [slots, max_c, dh]
+  int max_c;
+  const __nv_bfloat16* wk;          // indexer K projection [idx_dim, dh] (null = none)
+  const __nv_bfloat16* k_norm_w;
+  __nv_bfloat16* idx_out;           // [slots, max_c, idx_dim]
+  int idx_dim;
+};
+cudaError_t compress_pool(const CompParams& p, cudaStream_t st);
+// ring[slot][pos % depth] = proj[row] for tokens whose position is among the
+// last ``depth`` positions of their sequence in this step.
+cudaError_t ring_update_f32(float* ring, int depth, int width, const float* src, int T, const int* slot,
+                            const int* pos, const int* last_pos, cudaStream_t st);
+cudaError_t ring_update_bf16(__nv_bfloat16* ring, int depth, int width, const __nv_bfloat16* src, int T,
+                             const int* slot, const int* pos, const int* last_pos, cudaStream_t st);
+
+// ------------------------------------------------------------ moe.cu
+cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,
+                        float route_scale, int* ids, float* wts, cudaStream_t st);
+struct MoePlanParams {
+  int T, topk, E_local, e_begin;    // experts [e_begin, e_begin + E_local) live here
+  const int* ids;                   // [T, topk] global expert ids
+  const float* wts;
+  int* counts;                      // [E_local] scratch (zeroed by the plan)
+  int* seg_start;                   // [E_local]
+  int* rank;                        // [T, topk] scratch
+  int tile_rows;                    // 128 or 256
+  int m13, m2;                      // W13 / W2 output rows per expert
+  int4* tiles13;
+  int* n_tiles13;
+  int4* tiles2;
+  int* n_tiles2;
+  int max_tiles13, max_tiles2;
+  int cap_rows;                     // capacity of the permuted buffers
+  int* pos;                         // [T, topk] permuted row (-1 if the expert is not local)
+  float* row_scale;                 // [cap_rows]
+  uint32_t* err;
+};
+cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st);
+// Copies quantized token rows (e4m3 + scale chunks) into permuted-row order.
+cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
+                        uint8_t* psf, cudaStream_t st);
+
+// ----------------------------------------------------------- indexer.cu
+struct IdxParams {
+  int T, n_heads, head_dim;
+  const __nv_bfloat16* q;           // [T, n_heads, head_dim]
+  const float* w;                   // [T, n_heads] (already bf16-rounded)
+  const __nv_bfloat16* kcache;      // [slots, max_c, head_dim]
+  int max_c;
+  const int* slot;
+  const int* clen;                  // [T] causal number of compressed entries
+  int topk;
+  int* out_idx;                     // [T, topk]
+  int* out_cnt;                     // [T]
+  uint8_t* cand;                    // [T, max_c/cand_block] candidate block mask (optional)
+  int cand_mode;                    // 0 none, 1 build, 2 apply
+  int cand_block, cand_topk;
+  uint32_t* err;
+  // tokens whose position does not close a group of ratio own_r read kcache_alt
+  const __nv_bfloat16* kcache_alt;
+  int alt_max_c;
+  const int* pos;
+  const int* chunk_start;           // alt only applies to single-token (decode) chunks
+  const int* last_pos;
+  int own_r;
+};
+cudaError_t indexer_topk(const IdxParams& p, cudaStream_t st);
+
+// ---------------------------------------------------------------- ep.cu
+cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uint8_t* xq, const uint8_t* xsf, int D,
+                    int e_local, int world, int cap, int rec, uint8_t* send, int* cnt, int* pos_back,
+                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, cudaStream_t st);
+cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
+                           float* wts, cudaStream_t st);
+cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
+                           cudaStream_t st);
+cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
+                            __nv_bfloat16* const* peer_back, int my_rank, cudaStream_t st);
+
+// -------------------------------------------------------------- misc.cu
+cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
+                          cudaStream_t st);
+cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st);
 
 }  // namespace dsv4

@@ -1,0 +1,71 @@
+// Small fused kernels: embedding lookup into the residual streams, row argmax.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+// X[t, i, :] = table[ids[t], :] for every stream i (reference.py:909-911).
+__global__ void embed_streams_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids, int D,
+                                     int hc, __nv_bfloat16* X) {
+  const int t = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)ids[t] * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) {
+    const uint4 v = src[i];
+    for (int s = 0; s < hc; ++s) reinterpret_cast<uint4*>(X + ((size_t)t * hc + s) * D)[i] = v;
+  }
+}
+
+cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
+                          cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  embed_streams_kernel<<<T, 256, 0, st>>>(table, ids, D, hc, X);
+  return cudaGetLastError();
+}
+
+// out[t] = argmax_v logits[t, v] (first index on ties).
+__global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int V, int ld, int* out) {
+  const int t = blockIdx.x;
+  const float* row = logits + (size_t)t * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = row[v];
+    if (x > bv) {
+      bv = x;
+      bi = v;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[16];
+  __shared__ int si[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    out[t] = bi;
+  }
+}
+
+cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  argmax_kernel<<<T, 512, 0, st>>>(logits, V, ld, out);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

@@ -1,0 +1,184 @@
+// MoE routing, dispatch planning and token permutation.
+//
+// router_topk: scores = sqrt(softplus(logit)) (V4 family) or sigmoid(logit);
+//   experts = top-k of (score + bias) (ties -> lower expert id); weights =
+//   score / sum(score) * route_scale (reference.py:355-382).  One warp per token.
+// moe_plan: per-expert counts -> 128-row-aligned segments of the permuted
+//   activation buffer -> GEMM tile lists for W13 and W2 (device-built, so the
+//   whole MoE block replays inside a CUDA graph) -> permuted row of every
+//   (token, slot) and its routing weight.
+// moe_scatter: copies MXFP8 token rows and their scale bytes into permuted order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsv4 {
+
+__global__ void router_topk_kernel(const float* __restrict__ logits, int T, int E, const float* __restrict__ bias,
+                                   int topk, int score_func, float route_scale, int* ids, float* wts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  constexpr int kMaxPer = 16;  // E <= 512
+  float sc[kMaxPer], key[kMaxPer];
+  const int per = (E + 31) / 32;
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    if (i < per && e < E) {
+      const float x = logits[(size_t)warp * E + e];
+      float s;
+      if (score_func == 1) {
+        s = 1.f / (1.f + expf(-x));
+      } else {
+        const float sp = x > 20.f ? x : log1pf(expf(x));
+        s = sqrtf(sp);
+      }
+      sc[i] = s;
+      key[i] = s + (bias ? bias[e] : 0.f);
+    } else {
+      sc[i] = 0.f;
+      key[i] = -INFINITY;
+    }
+  }
+  float chosen[16];
+  int chosen_id[16];
+  float total = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    // local best (lowest index on ties)
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (key[i] > bv) {
+        bv = key[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    float s = 0.f;
+    if ((bi & 31) == lane) {
+      const int i = bi >> 5;
+      s = sc[i];
+      key[i] = -INFINITY;
+    }
+    s = __shfl_sync(0xffffffffu, s, bi & 31);
+    chosen[k] = s;
+    chosen_id[k] = bi;
+    total += s;
+  }
+  if (lane == 0) {
+    const float inv = topk > 1 ? 1.f / (total + 1e-20f) : 1.f;
+    for (int k = 0; k < topk; ++k) {
+      ids[(size_t)warp * topk + k] = chosen_id[k];
+      wts[(size_t)warp * topk + k] = chosen[k] * inv * route_scale;
+    }
+  }
+}
+
+cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,
+                        float route_scale, int* ids, float* wts, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (E > 512 || topk > 16) return cudaErrorInvalidValue;
+  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits, T, E, bias, topk, score_func, route_scale, ids,
+                                                           wts);
+  return cudaGetLastError();
+}
+
+// Single CTA of 1024 threads: counts, scan, tiles, positions.
+__global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
+  extern __shared__ int sh[];
+  int* cnt = sh;                        // [E_local]
+  int* start = sh + p.E_local;          // [E_local + 1]
+  int* toff = sh + 2 * p.E_local + 1;   // [E_local + 1] row-tile offsets
+  __shared__ int s_ok;
+  const int n = p.T * p.topk;
+  const int mt13 = p.m13 / 128, mt2 = p.m2 / 128;
+  for (int e = threadIdx.x; e < p.E_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = p.ids[i] - p.e_begin;
+    if (e >= 0 && e < p.E_local) p.rank[i] = atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, tacc = 0;
+    for (int e = 0; e < p.E_local; ++e) {
+      start[e] = acc;
+      toff[e] = tacc;
+      acc += (cnt[e] + 127) / 128 * 128;
+      tacc += (cnt[e] + p.tile_rows - 1) / p.tile_rows;
+    }
+    start[p.E_local] = acc;
+    toff[p.E_local] = tacc;
+    const bool ok = acc <= p.cap_rows && tacc * mt13 <= p.max_tiles13 && tacc * mt2 <= p.max_tiles2;
+    if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 1);
+    s_ok = ok;
+    *p.n_tiles13 = ok ? tacc * mt13 : 0;  // run nothing rather than overrun the buffers
+    *p.n_tiles2 = ok ? tacc * mt2 : 0;
+  }
+  __syncthreads();
+  const bool ok = s_ok;
+  for (int e = threadIdx.x; e < p.E_local; e += blockDim.x) {
+    p.counts[e] = cnt[e];
+    p.seg_start[e] = start[e];
+    if (!ok) continue;
+    const int c = cnt[e];
+    int rt = toff[e];
+    for (int r0 = 0; r0 < c; r0 += p.tile_rows, ++rt) {
+      const int valid = min(p.tile_rows, c - r0);
+      for (int mt = 0; mt < mt13; ++mt)
+        p.tiles13[(size_t)rt * mt13 + mt] = make_int4(e * p.m13 + mt * 128, start[e] + r0, valid, mt * 128);
+      for (int mt = 0; mt < mt2; ++mt)
+        p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, start[e] + r0, valid, mt * 128);
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = p.ids[i] - p.e_begin;
+    if (ok && e >= 0 && e < p.E_local) {
+      const int row = start[e] + p.rank[i];
+      p.pos[i] = row;
+      p.row_scale[row] = p.wts[i];
+    } else {
+      p.pos[i] = -1;
+    }
+  }
+}
+
+cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
+  const int smem = (3 * p.E_local + 2) * 4;
+  moe_plan_kernel<<<1, 1024, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+// One warp per (token, slot): 16-byte copies of the e4m3 row, then scale bytes.
+__global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int T, int D,
+                                   int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= T * topk) return;
+  const int row = pos[w];
+  if (row < 0) return;
+  const int t = w / topk;
+  const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)t * D);
+  uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
+  for (int i = lane; i < D / 16; i += 32) dst[i] = src[i];
+  const int kt = D / 128;
+  for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = xsf[sf_chunk_offset(t, b, kt)];
+}
+
+cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
+                        uint8_t* psf, cudaStream_t st) {
+  const long long warps = (long long)T * topk;
+  if (warps == 0) return cudaSuccess;
+  moe_scatter_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(xq, xsf, T, D, topk, pos, pq, psf);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4

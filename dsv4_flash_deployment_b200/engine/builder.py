@@ -1,0 +1,55 @@
+"""Model construction: checkpoint tensors or device-side random init."""
+
+from __future__ import annotations
+
+import torch
+
+from ..models.model import DSV4Model
+from ..models.weights import load_layer, random_experts, random_layer
+from ..ops.layout import ceil_to
+
+
+def _pad_rows(w: torch.Tensor) -> torch.Tensor:
+    n = w.shape[0]
+    npad = ceil_to(n, 128)
+    if npad == n:
+        return w.contiguous()
+    out = torch.zeros(npad, *w.shape[1:], dtype=w.dtype, device=w.device)
+    out[:n] = w
+    return out
+
+
+def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
+                weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
+                ep=None) -> DSV4Model:
+    """Builds the backbone.
+
+    ``weights``: checkpoint dict (names of the reference checkpoint); None draws
+    random weights on the device.  ``expert_storage_layers``: with random init,
+    the number of distinct physical expert blocks (layers share them round-robin
+    when the model does not fit one GPU).  ``ep``: expert-parallel group.
+    """
+    dev = torch.device(device)
+    e_begin, e_local = 0, cfg.n_routed_experts
+    if ep is not None:
+        e_begin, e_local = ep.expert_range(cfg.n_routed_experts)
+    layers = []
+    if weights is not None:
+        for lid in range(cfg.n_layers):
+            layers.append(load_layer(cfg, weights, lid, dev))
+        embed = weights["embed.weight"].to(dev)
+        head = _pad_rows(weights["head.weight"]).to(dev)
+        norm = weights["norm.weight"].to(dev)
+    else:
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        n_phys = expert_storage_layers or cfg.n_layers
+        stores = [random_experts(cfg, e_local, dev, g) for _ in range(min(n_phys, cfg.n_layers))]
+        for lid in range(cfg.n_layers):
+            layers.append(random_layer(cfg, lid, dev, g, stores[lid % len(stores)]))
+        embed = (torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        head = _pad_rows((torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) / cfg.dim ** 0.5)
+                         .to(torch.bfloat16))
+        norm = (1.0 + 0.05 * torch.randn(cfg.dim, device=dev, generator=g)).to(torch.bfloat16)
+    return DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
+                     head_vocab=cfg.vocab_size)

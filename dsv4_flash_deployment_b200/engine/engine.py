@@ -1,0 +1,114 @@
+"""Serving engine: scheduler + model step + CUDA-graph replay.
+
+Public API (what the server, the benchmark and users call):
+
+    eng = Engine.build(cfg, ...)                  # random-init or checkpoint weights
+    req = eng.add_request(prompt_ids, max_new_tokens, ignore_eos=True)
+    events = eng.step()                           # one continuous-batching step
+    outs = eng.generate([prompt, ...], max_new_tokens)
+
+Each step: the scheduler picks decode tokens and prompt chunks, the host
+builds :class:`StepMeta`, copies it from pinned memory to the device, the
+model step runs (replayed from a CUDA graph captured per batch shape), and the
+sampled token ids come back to the host.  The step is the reference engine's
+``generate_greedy`` inner loop (deepseek_v41/engine.py:384-475) generalized to
+many sequences, and the vLLM scheduler loop for the vLLM-served recipes.
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Iterable
+
+import numpy as np
+import torch
+
+from ..models.model import DSV4Model, SeqChunk, StepMeta
+from ..ops.gemm import ErrorWord
+from .scheduler import Request, Scheduler
+
+
+class Engine:
+    def __init__(self, model: DSV4Model, max_seqs: int, max_batched_tokens: int, max_seq_len: int,
+                 chunk_size: int | None = None, use_graphs: bool = True, eos_id: int | None = None):
+        self.model = model
+        self.cfg = model.cfg
+        self.sched = Scheduler(max_seqs, max_batched_tokens, max_seq_len, chunk_size)
+        self.use_graphs = use_graphs and model.dev.type == "cuda"
+        self.graphs: dict = {}
+        self.pinned: dict = {}
+        self.eos_id = self.cfg.eos_token_id if eos_id is None else eos_id
+        self.stream = torch.cuda.Stream(model.dev) if model.dev.type == "cuda" else None
+        self.stats = {"steps": 0, "tokens": 0, "graph_captures": 0}
+
+    # ----------------------------------------------------------------- build
+    @classmethod
+    def build(cls, cfg, device="cuda", max_seqs: int = 16, max_batched_tokens: int = 512, max_seq_len: int = 2048,
+              weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None, ep=None,
+              use_graphs: bool = True, chunk_size: int | None = None) -> "Engine":
+        from .builder import build_model
+        model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs, max_seq_len=max_seq_len,
+                            weights=weights, seed=seed, expert_storage_layers=expert_storage_layers, ep=ep)
+        return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs)
+
+    # ------------------------------------------------------------------- API
+    def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
+                    stop_ids: Iterable[int] = ()) -> Request:
+        return self.sched.add(prompt, max_new_tokens, ignore_eos=ignore_eos, eos_id=self.eos_id,
+                              stop_ids=tuple(stop_ids))
+
+    def step(self) -> list[tuple[Request, int | None]]:
+        chunks = self.sched.schedule()
+        if not chunks:
+            return []
+        meta = StepMeta(self.cfg, [SeqChunk(c.req.slot, c.start_pos, c.tokens, c.sample) for c in chunks])
+        ids = self.run_meta(meta)
+        return self.sched.commit(chunks, ids)
+
+    def run_meta(self, meta: StepMeta) -> list[int]:
+        """Uploads ``meta``, runs the model step, returns the sampled ids on the host."""
+        m = self.model
+        if self.stream is not None:
+            with torch.cuda.stream(self.stream):
+                out = self._run_device(meta)
+                host = out.to("cpu", non_blocking=True) if len(out) else out.cpu()
+            self.stream.synchronize()
+        else:
+            out = self._run_device(meta)
+            host = out
+        self.stats["steps"] += 1
+        self.stats["tokens"] += meta.T
+        return [int(x) for x in host.tolist()]
+
+    def _run_device(self, meta: StepMeta) -> torch.Tensor:
+        m = self.model
+        m.upload(meta, self.pinned)
+        if not self.use_graphs:
+            return m.forward(meta)
+        key = meta.key()
+        g = self.graphs.get(key)
+        if g is None:
+            # The first step of a shape runs eagerly (it is the real step: it advances
+            # the caches once and its output is returned).  Capture then records the
+            # same launches without executing them; later steps of this shape replay.
+            out = m.forward(meta)
+            torch.cuda.current_stream().synchronize()
+            ErrorWord.check(m.dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=torch.cuda.current_stream()):
+                gout = m.forward(meta)
+            self.graphs[key] = (graph, gout)
+            self.stats["graph_captures"] += 1
+            return out
+        graph, out = g
+        graph.replay()
+        return out
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False) -> list[list[int]]:
+        reqs = [self.add_request(p, max_new_tokens, ignore_eos) for p in prompts]
+        while not all(r.finished for r in reqs):
+            self.step()
+        return [r.output for r in reqs]
+
+    def check_errors(self) -> None:
+        ErrorWord.check(self.model.dev)

@@ -1,0 +1,54 @@
+"""HBM budgeting for a model instance on one GPU (180 GB B200).
+
+Estimates everything that is not routed-expert weight (dense weights, the
+caches, step buffers, runtime reserve) and returns how many distinct physical
+expert blocks fit.  When fewer blocks than layers fit, layers share blocks
+round-robin (random-init benchmark runs only); each layer still streams a full
+block from HBM, so the work per step is unchanged.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def expert_block_bytes(cfg, ep_world: int = 1) -> int:
+    e_local = cfg.n_routed_experts // ep_world
+    per = 3 * cfg.dim * cfg.moe_inter_dim
+    if cfg.expert_format == "mxfp4":
+        return int(e_local * per * (0.5 + 1 / 32))
+    return int(e_local * per * (1 + 1 / 32))
+
+
+def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int) -> int:
+    d = cfg.dim
+    per_layer = ((cfg.q_lora_rank + cfg.head_dim) * d + cfg.q_dim * cfg.q_lora_rank + 2 * cfg.o_inter * cfg.o_group_in
+                 + d * cfg.o_inter + 3 * d * cfg.n_shared_experts * cfg.moe_inter_dim
+                 + 2 * cfg.n_routed_experts * d + 2 * 2 * cfg.hc_rows * cfg.hc_mult * d * 2)
+    dense = cfg.n_layers * per_layer
+    for l in cfg.kv_source_layer_ids:
+        dense += 2 * 2 * cfg.overlap(l) * cfg.head_dim * d
+    for l in cfg.index_source_layer_ids:
+        dense += cfg.index_n_heads * cfg.index_head_dim * cfg.q_lora_rank + 2 * 128 * d
+    emb = 2 * 2 * cfg.vocab_size * d
+    s = n_slots + 1
+    kv = cfg.n_layers * s * cfg.sliding_window * cfg.head_dim * 2
+    for l in cfg.kv_source_layer_ids:
+        r, co = cfg.ratio(l), cfg.overlap(l)
+        kv += s * (max_seq // r) * cfg.head_dim * 2 + s * co * r * 2 * co * cfg.head_dim * 4
+        if l in cfg.index_source_layer_ids:
+            kv += s * (max_seq // r) * cfg.index_head_dim * 2
+    t = max_tokens
+    k = cfg.n_activated_experts
+    cap = t * k * 2 + cfg.n_routed_experts * 128
+    step = (t * (cfg.hc_mult * d * 2 + 6 * d + 2 * 2 * cfg.q_dim + 6 * cfg.o_inter + 16 * cfg.head_dim)
+            + cap * (d * 3 + cfg.moe_inter_dim * 2) + t * cfg.vocab_size * 4 + 64 * 2 ** 20)
+    return dense + emb + kv + step
+
+
+def plan_expert_storage(cfg, device, max_tokens: int, n_slots: int, max_seq: int, ep_world: int = 1,
+                        reserve_gb: float = 10.0) -> int:
+    free, _ = torch.cuda.mem_get_info(device)
+    avail = free - non_expert_bytes(cfg, max_tokens, n_slots, max_seq) - int(reserve_gb * 2 ** 30)
+    n = int(avail // expert_block_bytes(cfg, ep_world))
+    return max(1, min(cfg.n_layers, n))

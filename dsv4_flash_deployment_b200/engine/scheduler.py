@@ -1,0 +1,156 @@
+"""Continuous batching with chunked prefill (host side, no torch).
+
+Plays the role of the vLLM V1 scheduler the reference serves behind
+(``--max-num-seqs``, ``--max-num-batched-tokens``, chunked prefill at 256/2048
+tokens per step; ``KO/dsv41-flash-v6e16-serving.yaml:360-373``).  Policy per
+step: every running sequence that has finished its prompt decodes one token;
+the remaining token budget goes to prompt chunks, oldest request first.  A
+request enters only when a cache slot is free (``max_seqs``) and its total
+length fits ``max_seq_len``.  Finished requests release their slot at once.
+"""
+
+from __future__ import annotations
+
+import itertools
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+
+@dataclass
+class Request:
+    req_id: int
+    prompt: list[int]
+    max_new_tokens: int
+    ignore_eos: bool = False
+    eos_id: int | None = None
+    stop_ids: tuple[int, ...] = ()
+    slot: int = -1
+    n_prefilled: int = 0
+    output: list[int] = field(default_factory=list)
+    finished: bool = False
+    finish_reason: str | None = None
+    t_arrival: float = field(default_factory=time.perf_counter)
+    t_first_token: float | None = None
+    t_done: float | None = None
+    cancelled: bool = False
+
+    @property
+    def prompt_done(self) -> bool:
+        return self.n_prefilled >= len(self.prompt)
+
+    @property
+    def position(self) -> int:
+        """Next position to be written."""
+        return self.n_prefilled + len(self.output) - (1 if self.output else 0)
+
+
+@dataclass
+class ScheduledChunk:
+    req: Request
+    start_pos: int
+    tokens: list[int]
+    sample: bool
+
+
+class SlotAllocator:
+    def __init__(self, n: int):
+        self.free = deque(range(n))
+
+    def alloc(self) -> int | None:
+        return self.free.popleft() if self.free else None
+
+    def release(self, s: int) -> None:
+        self.free.append(s)
+
+    @property
+    def n_free(self) -> int:
+        return len(self.free)
+
+
+class Scheduler:
+    def __init__(self, max_seqs: int, max_batched_tokens: int, max_seq_len: int, chunk_size: int | None = None):
+        self.max_seqs = max_seqs
+        self.budget = max_batched_tokens
+        self.max_seq_len = max_seq_len
+        self.chunk = chunk_size or max_batched_tokens
+        self.slots = SlotAllocator(max_seqs)
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self._ids = itertools.count()
+
+    def add(self, prompt: list[int], max_new_tokens: int, **kw) -> Request:
+        if not prompt:
+            raise ValueError("empty prompt")
+        if len(prompt) + max_new_tokens > self.max_seq_len:
+            raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len {self.max_seq_len}")
+        r = Request(next(self._ids), list(prompt), max_new_tokens, **kw)
+        self.waiting.append(r)
+        return r
+
+    def cancel(self, req: Request) -> None:
+        req.cancelled = True
+
+    def schedule(self) -> list[ScheduledChunk]:
+        # drop cancelled requests
+        for r in [r for r in self.running if r.cancelled]:
+            self._finish(r, "cancelled")
+        self.waiting = deque(r for r in self.waiting if not r.cancelled)
+        out: list[ScheduledChunk] = []
+        budget = self.budget
+        for r in self.running:
+            if r.prompt_done and budget > 0:
+                out.append(ScheduledChunk(r, r.position, [r.output[-1]], True))
+                budget -= 1
+        # continue partially prefilled requests first, then admit new ones
+        for r in self.running:
+            if budget <= 0:
+                break
+            if not r.prompt_done:
+                n = min(self.chunk, budget, len(r.prompt) - r.n_prefilled)
+                out.append(ScheduledChunk(r, r.n_prefilled, r.prompt[r.n_prefilled:r.n_prefilled + n],
+                                          r.n_prefilled + n == len(r.prompt)))
+                budget -= n
+        while budget > 0 and self.waiting and self.slots.n_free > 0:
+            r = self.waiting.popleft()
+            r.slot = self.slots.alloc()
+            self.running.append(r)
+            n = min(self.chunk, budget, len(r.prompt))
+            out.append(ScheduledChunk(r, 0, r.prompt[:n], n == len(r.prompt)))
+            budget -= n
+        return out
+
+    def commit(self, chunks: list[ScheduledChunk], next_ids: list[int]) -> list[tuple[Request, int | None]]:
+        """Applies a step's results; returns (request, new token or None) per chunk."""
+        events = []
+        it = iter(next_ids)
+        now = time.perf_counter()
+        for c in chunks:
+            r = c.req
+            if not r.prompt_done:
+                r.n_prefilled += len(c.tokens)
+            tok = next(it) if c.sample else None
+            if tok is not None:
+                r.output.append(int(tok))
+                if r.t_first_token is None:
+                    r.t_first_token = now
+                if len(r.output) >= r.max_new_tokens:
+                    self._finish(r, "length")
+                elif not r.ignore_eos and (tok == r.eos_id or tok in r.stop_ids):
+                    self._finish(r, "stop")
+            events.append((r, tok))
+        return events
+
+    def _finish(self, r: Request, reason: str) -> None:
+        r.finished = True
+        r.finish_reason = reason
+        r.t_done = time.perf_counter()
+        if r in self.running:
+            self.running.remove(r)
+        if r.slot >= 0:
+            self.slots.release(r.slot)
+            r.slot = -1
+
+    @property
+    def idle(self) -> bool:
+        return not self.running and not self.waiting

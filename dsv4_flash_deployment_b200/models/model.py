@@ -1,0 +1,506 @@
+"""DeepSeek-V4-family model step on the sm_100a kernels.
+
+One call of :meth:`DSV4Model.forward` runs a *mixed batch*: any number of
+sequences, each contributing a contiguous run of tokens (one for a decoding
+sequence, a chunk for a prefilling one).  Per layer (reference
+``_block_step`` reference.py:840-891):
+
+  hc_step (post of previous MoE + mixes + collapse + RMSNorm + MXFP8)
+  -> [wq_a|wkv] GEMM -> qkv_post (q norm+quant, kv norm+RoPE+FP8 round trip)
+  -> wq_b GEMM -> compressor (kv sources) -> indexer (index sources)
+  -> sparse attention over window ring + this step's rows + compressed rows
+  -> window ring update -> grouped wo_a (bf16) -> MXFP8 wo_b
+  -> hc_step -> router GEMM + top-k -> dispatch plan -> grouped W13 (SwiGLU
+     epilogue requantizes to MXFP8) -> grouped W2 -> shared expert
+and the next layer's hc_step consumes the expert outputs (combine fused).
+
+All buffers are allocated once for a maximum token count, so a step replays
+inside a CUDA graph.  Expert parallelism is a parameter of the MoE block
+(``ep_rank, ep_size``): tokens routed to experts of another rank travel in the
+dispatch/combine exchange of :mod:`..parallel.ep`.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..ops import _ext
+from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
+                        pick_bn)
+from ..ops.layout import ceil_to
+from ..ref import numerics as N
+from .weights import LayerW
+
+
+# --------------------------------------------------------------------------
+# step metadata
+# --------------------------------------------------------------------------
+@dataclass
+class SeqChunk:
+    slot: int
+    start_pos: int
+    tokens: list[int]
+    sample: bool = True   # produce logits for the last token of the chunk
+
+
+class StepMeta:
+    """Host description of one mixed step, and its pinned/device mirrors."""
+
+    def __init__(self, cfg, chunks: list[SeqChunk], ring_pad_slot: int | None = None):
+        self.cfg = cfg
+        self.chunks = chunks
+        ids, pos, slot, cstart, row0, last, sample = [], [], [], [], [], [], []
+        for c in chunks:
+            r0 = len(ids)
+            n = len(c.tokens)
+            for j, tok in enumerate(c.tokens):
+                ids.append(tok)
+                pos.append(c.start_pos + j)
+                slot.append(c.slot)
+                cstart.append(c.start_pos)
+                row0.append(r0)
+                last.append(c.start_pos + n - 1)
+            if c.sample:
+                sample.append(r0 + n - 1)
+        self.T = len(ids)
+        self.ids = np.asarray(ids, np.int32)
+        self.pos = np.asarray(pos, np.int32)
+        self.slot = np.asarray(slot, np.int32)
+        self.chunk_start = np.asarray(cstart, np.int32)
+        self.step_row0 = np.asarray(row0, np.int32)
+        self.last_pos = np.asarray(last, np.int32)
+        self.sample_rows = np.asarray(sample, np.int32)
+        self.max_pos = int(self.pos.max()) if self.T else 0
+        # compressor groups closed in this step, per ratio
+        self.groups = {}
+        for r in sorted({cfg.ratio(l) for l in cfg.kv_source_layer_ids}):
+            gs, gi, gc, gr = [], [], [], []
+            for c, r0 in zip(chunks, self._row0s()):
+                for p in range(c.start_pos, c.start_pos + len(c.tokens)):
+                    if (p + 1) % r == 0:
+                        gs.append(c.slot)
+                        gi.append(p // r)
+                        gc.append(c.start_pos)
+                        gr.append(r0)
+            self.groups[r] = tuple(np.asarray(a, np.int32) for a in (gs, gi, gc, gr))
+        self.clen = {r: ((self.pos + 1) // r).astype(np.int32) for r in self.groups}
+
+    def _row0s(self):
+        out, acc = [], 0
+        for c in self.chunks:
+            out.append(acc)
+            acc += len(c.tokens)
+        return out
+
+    def index_bypass(self, r: int) -> bool:
+        """True when every token's compressed length <= index_topk: top-k selects all."""
+        return int(self.clen[r].max(initial=0)) <= self.cfg.index_topk
+
+    def key(self):
+        """Graph key: shapes and control flow of the step."""
+        return (self.T, len(self.sample_rows), tuple(len(c.tokens) for c in self.chunks),
+                tuple(self.index_bypass(r) for r in self.groups))
+
+
+# --------------------------------------------------------------------------
+# model
+# --------------------------------------------------------------------------
+class DSV4Model:
+    def __init__(self, cfg, layers: list[LayerW], embed: torch.Tensor, head: torch.Tensor, norm_w: torch.Tensor,
+                 max_tokens: int, n_slots: int, max_seq_len: int, device, ep=None, max_sample: int | None = None,
+                 head_vocab: int | None = None):
+        self.cfg = cfg
+        self.layers = layers
+        self.dev = torch.device(device)
+        self.embed = embed
+        self.head = head                      # bf16 [pad128(V), D]
+        self.vocab = head_vocab or cfg.vocab_size
+        self.norm_w = norm_w
+        self.max_tokens = max_tokens
+        self.n_slots = n_slots
+        self.max_seq_len = max_seq_len
+        self.ep = ep
+        self.max_sample = max_sample or max_tokens
+        self.err = ErrorWord.get(self.dev)
+        self.ext = _ext.load()
+        self._alloc()
+
+    # ------------------------------------------------------------- buffers
+    def _alloc(self):
+        cfg, dev, T = self.cfg, self.dev, self.max_tokens
+        D = cfg.dim
+        Tp = ceil_to(T, 128)
+        bf, f32, u8, i32 = torch.bfloat16, torch.float32, torch.uint8, torch.int32
+        e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=dev)
+        z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=dev)
+        self.X = e(T, cfg.hc_mult, D)
+        self.hc_c = e(T, D)
+        self.hc_part = e(T * self.ext.hc_num_slices(D) * 26, dt=f32)
+        self.mixA, self.mixF = z(T, 24, dt=f32), z(T, 24, dt=f32)
+        init = torch.zeros(T, 24, dtype=f32, device=dev)
+        init[:, 0] = 1.0
+        self.mix0 = init
+        self.u = e(T, D)
+        self.uq = e(Tp, D, dt=u8)
+        self.usf = z(Tp // 128, D // 128, 512, dt=u8)
+        qa = cfg.q_lora_rank
+        self.qkv = e(T, qa + cfg.head_dim)
+        self.qr_q = e(Tp, qa, dt=u8)
+        self.qr_sf = z(Tp // 128, qa // 128, 512, dt=u8)
+        self.kv_step = e(T, cfg.head_dim)
+        self.q = e(T, cfg.n_heads, cfg.head_dim)
+        self.o = e(T, cfg.n_heads, cfg.head_dim)
+        self.oa = e(T, cfg.o_inter)
+        self.oa_q = e(Tp, cfg.o_inter, dt=u8)
+        self.oa_sf = z(Tp // 128, cfg.o_inter // 128, 512, dt=u8)
+        self.attn_out = e(T, D)
+        self.proj = {co: e(T, 2 * co * cfg.head_dim, dt=f32)
+                     for co in sorted({cfg.overlap(l) for l in cfg.kv_source_layer_ids})}
+        nih = cfg.index_n_heads
+        self.qidx = e(T, nih, cfg.index_head_dim)
+        self.widx_raw = e(T, nih, dt=f32)
+        self.widx = e(T, nih, dt=f32)
+        self.comp_idx = e(T, cfg.index_topk, dt=i32)
+        self.comp_cnt = e(T, dt=i32)
+        self.dense_cnt = e(T, dt=i32)
+        max_c = max([self.max_seq_len // cfg.ratio(l) for l in cfg.kv_source_layer_ids] or [1])
+        self.cand = z(T, max(1, max_c // max(1, cfg.candidate_block_size)), dt=u8)
+        # MoE
+        E = max(cfg.n_routed_experts, cfg.dspark_n_routed_experts if cfg.n_mtp_layers else 0)
+        k = max(cfg.n_activated_experts, cfg.dspark_n_activated_experts if cfg.n_mtp_layers else 0)
+        self.router_logits = {}
+        self.route = {}   # top-k -> (ids, wts, pos, rank)
+        for lid in range(cfg.n_total_layers):
+            ee, kk = cfg.n_experts_for(lid), cfg.topk_for(lid)
+            if ee not in self.router_logits:
+                self.router_logits[ee] = e(T, ee, dt=f32)
+            if kk not in self.route:
+                self.route[kk] = (e(T, kk, dt=i32), e(T, kk, dt=f32), e(T, kk, dt=i32), e(T, kk, dt=i32))
+        self.counts = e(E, dt=i32)
+        self.seg = e(E, dt=i32)
+        e_local = E if self.ep is None else self.ep.experts_per_rank(E)
+        recv_rows = T * k if self.ep is None else self.ep.recv_rows(T, k)
+        self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
+        self.tile_rows = 128 if recv_rows <= 4096 else 256
+        tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
+        I = cfg.moe_inter_dim
+        self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)
+        self.tiles2 = e(tiles_rows_max * (D // 128), 4, dt=i32)
+        self.nt13, self.nt2 = z(1, dt=i32), z(1, dt=i32)
+        self.xperm = e(self.cap, D, dt=u8)
+        self.xperm_sf = z(self.cap // 128, D // 128, 512, dt=u8)
+        self.hperm = e(self.cap, I, dt=u8)
+        self.hperm_sf = z(self.cap // 128, I // 128, 512, dt=u8)
+        self.yperm = e(self.cap, D)
+        self.row_scale = z(self.cap, dt=f32)
+        si = cfg.n_shared_experts * I
+        self.hs = e(Tp, si, dt=u8)
+        self.hs_sf = z(Tp // 128, si // 128, 512, dt=u8)
+        self.shared_out = e(T, D)
+        # head
+        self.u_sample = e(self.max_sample, D)
+        self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
+        self.next_ids = e(self.max_sample, dt=i32)
+        # split-K scratch (reused sequentially on the stream)
+        self.ws = e(8 * 1024 * 1024, dt=f32)
+        self.counters = z(65536, dt=i32)
+        self.attn_ws = e(max(1, min(T, 8)) * 16 * 64 * 514, dt=f32)
+        # step metadata (device)
+        self.m_ids, self.m_pos, self.m_slot = e(T, dt=i32), e(T, dt=i32), e(T, dt=i32)
+        self.m_cstart, self.m_row0, self.m_last = e(T, dt=i32), e(T, dt=i32), e(T, dt=i32)
+        self.m_sample = e(self.max_sample, dt=torch.int64)
+        self.m_groups = {}
+        self.m_clen = {}
+        self.m_ngroups = {}
+        for r in sorted({cfg.ratio(l) for l in cfg.kv_source_layer_ids}):
+            self.m_groups[r] = tuple(e(T, dt=i32) for _ in range(4))
+            self.m_clen[r] = e(T, dt=i32)
+            self.m_ngroups[r] = z(1, dt=i32)
+        self._alloc_cache()
+        # rope tables on device
+        tabs = N.layer_rope_tables(cfg, self.max_seq_len + 8)
+        self.rope = {k_: (c.to(dev).contiguous(), s.to(dev).contiguous()) for k_, (c, s) in tabs.items()}
+
+    def _alloc_cache(self):
+        cfg, dev = self.cfg, self.dev
+        S = self.n_slots + 1  # last slot absorbs padding tokens
+        self.ring = {}
+        self.comp = {}
+        self.idx_cache = {}
+        self.comp_ring = {}
+        for l in range(cfg.n_layers):
+            self.ring[l] = torch.zeros(S, cfg.sliding_window, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+        for l in cfg.kv_source_layer_ids:
+            r, co = cfg.ratio(l), cfg.overlap(l)
+            max_c = max(1, self.max_seq_len // r)
+            self.comp[l] = torch.zeros(S, max_c, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            if l in cfg.index_source_layer_ids:
+                self.idx_cache[l] = torch.zeros(S, max_c, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
+            self.comp_ring[l] = torch.zeros(S, co * r, 2 * co * cfg.head_dim, dtype=torch.float32, device=dev)
+
+    def cache_bytes(self) -> int:
+        tot = 0
+        for d in (self.ring, self.comp, self.idx_cache, self.comp_ring):
+            tot += sum(t.numel() * t.element_size() for t in d.values())
+        return tot
+
+    # ------------------------------------------------------------- metadata
+    def upload(self, m: StepMeta, pinned: dict | None = None) -> None:
+        """Host -> device copy of the step metadata (async on the current stream)."""
+        T = m.T
+        self.last_upload_bytes = 0
+
+        def put(dst, arr):
+            self.last_upload_bytes += arr.nbytes
+            src = torch.from_numpy(arr)
+            if pinned is not None:
+                key = id(dst)
+                buf = pinned.get(key)
+                if buf is None or buf.numel() < dst.numel():
+                    buf = torch.empty(dst.numel(), dtype=dst.dtype).pin_memory()
+                    pinned[key] = buf
+                buf[: len(arr)].copy_(src)
+                src = buf[: len(arr)]
+            dst[: len(arr)].copy_(src, non_blocking=True)
+
+        put(self.m_ids, m.ids)
+        put(self.m_pos, m.pos)
+        put(self.m_slot, m.slot)
+        put(self.m_cstart, m.chunk_start)
+        put(self.m_row0, m.step_row0)
+        put(self.m_last, m.last_pos)
+        put(self.m_sample, m.sample_rows.astype(np.int64))
+        for r, g in m.groups.items():
+            for dst, arr in zip(self.m_groups[r], g):
+                if len(arr):
+                    put(dst, arr)
+            put(self.m_clen[r], m.clen[r])
+            put(self.m_ngroups[r], np.asarray([len(g[0])], np.int32))
+
+    last_upload_bytes = 0
+
+    # --------------------------------------------------------------- helpers
+    def _gemm(self, xq, xsf, n_tok, w: MxWeight, out, epi=EPI_BF16, **kw):
+        bn = pick_bn(n_tok)
+        tiles = (w.q.shape[0] // 128) * ((n_tok + bn - 1) // bn)
+        splits = 1
+        if tiles < 100 and w.k >= 1024:
+            splits = max(1, min(w.k // 512, 148 // max(tiles, 1)))
+            while tiles * splits * 128 * bn > self.ws.numel() and splits > 1:
+                splits -= 1
+        return gemm_mx(xq, xsf, n_tok, w, out, epi, splits=splits, workspace=self.ws if splits > 1 else None,
+                       counters=self.counters if splits > 1 else None, **kw)
+
+    def _gemm_bf16(self, x, w, out, n_tok, f32_out=False, groups=1, m_valid=None):
+        return gemm_bf16(x, w, out, f32_out=f32_out, groups=groups, n_tokens=n_tok, m_valid=m_valid)
+
+    def _hc(self, T, Y=None, yperm=None, pos=None, topk=0, prev=None, mixes=None, cw=None, norm=None,
+            mix_out=None, u=None, uq=None, usf=None, tap=None):
+        cfg = self.cfg
+        fn = scale = base = None
+        if mixes is not None:
+            fn, scale, base = mixes
+        self.ext.hc_step(self.X, Y, yperm, pos, topk, prev, fn, scale, base, cw, 24, norm, mix_out, self.hc_c,
+                         self.hc_part, u, uq, usf, tap, T, self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
+
+    sinkhorn_iters = None
+
+    # --------------------------------------------------------------- forward
+    def forward(self, m: StepMeta, taps: dict | None = None, trace: dict | None = None) -> torch.Tensor:
+        """Runs one step whose metadata is already uploaded; returns next ids [n_sample] (device)."""
+        cfg = self.cfg
+        if self.sinkhorn_iters is None:
+            self.sinkhorn_iters = cfg.hc_sinkhorn_iters
+        T = m.T
+        ext = self.ext
+        self.ext.embed_streams(self.embed, self.m_ids, T, self.X)
+        prev, cw = None, self.mix0
+        moe_state = None
+        for li, L in enumerate(self.layers):
+            lid = L.layer_id
+            tap = None
+            if taps is not None and lid in cfg.dspark_target_layer_ids:
+                tap = taps[lid]
+            if moe_state is None:
+                self._hc(T, prev=None, mixes=L.hc_attn, cw=cw, norm=L.attn_norm, mix_out=self.mixA, u=self.u,
+                         uq=self.uq, usf=self.usf, tap=tap)
+            else:
+                yp, ps, kk = moe_state
+                self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
+                         cw=self.mixF, norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf,
+                         tap=tap)
+            if trace is not None:
+                trace[lid] = self.X[:T].clone()
+            self._attention(L, m)
+            if trace is not None:
+                trace[f"attn{lid}"] = self.attn_out[:T].clone()
+            self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
+                     mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
+            moe_state = self._moe(L, T)
+        # final collapse + norm on all tokens, then head on the sampled rows
+        yp, ps, kk = moe_state
+        self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=None, cw=self.mixF,
+                 norm=self.norm_w, u=self.u)
+        S = len(m.sample_rows)
+        if S == 0:
+            return self.next_ids[:0]
+        torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
+        self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
+        ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S])
+        return self.next_ids[:S]
+
+    # ------------------------------------------------------------- attention
+    def _attention(self, L: LayerW, m: StepMeta):
+        cfg, ext = self.cfg, self.ext
+        T = m.T
+        lid = L.layer_id
+        r = cfg.ratio(lid)
+        cos, sin = self.rope["yarn" if r > 0 else "swa"]
+        qa = cfg.q_lora_rank
+        self._gemm(self.uq, self.usf, T, L.wqkv_a, self.qkv)
+        ext.qkv_post(self.qkv, qa, cfg.head_dim, L.q_norm, L.kv_norm, cfg.rms_norm_eps, self.qr_q, self.qr_sf, cos,
+                     sin, self.m_pos, self.kv_step, T)
+        self._gemm(self.qr_q, self.qr_sf, T, L.wq_b, self.q.view(self.q.shape[0], -1))
+        comp = None
+        comp_idx = None
+        comp_cnt = None
+        if r > 0:
+            src = cfg.kv_source_for(lid)
+            if lid in cfg.kv_source_layer_ids:
+                self._compress(L, m, r)
+            clen = self.m_clen[r]
+            if lid in cfg.index_source_layer_ids:
+                if m.index_bypass(r):
+                    self._idx_sel = None
+                else:
+                    self._indexer(L, m, r)
+                    self._idx_sel = (self.comp_idx, self.comp_cnt)
+            if lid in cfg.index_source_layer_ids or lid not in cfg.kv_source_layer_ids:
+                sel = getattr(self, "_idx_sel", None)
+                if sel is None:
+                    comp_cnt = clen
+                else:
+                    comp_idx, comp_cnt = sel
+            else:
+                comp_cnt = clen   # owns a compressor but no indexer: dense over its entries
+            comp = self.comp[src]
+        splits = 1
+        if T <= 8:
+            splits = 8
+        ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, self.ring[lid], comp,
+                      self.m_slot, self.m_pos, self.m_cstart, self.m_row0, comp_idx, comp_cnt, L.sink,
+                      cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits)
+        ext.ring_update(self.ring[lid], self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
+        self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=cfg.o_groups)
+        ext.act_quant_mx(self.oa[:T], self.oa_q, self.oa_sf)
+        self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.attn_out)
+
+    def _compress(self, L: LayerW, m: StepMeta, r: int):
+        cfg, ext = self.cfg, self.ext
+        T = m.T
+        lid = L.layer_id
+        co = cfg.overlap(lid)
+        width = 2 * co * cfg.head_dim
+        proj = self.proj[co]
+        self._gemm_bf16(self.u, L.comp_wkvg, proj, T, f32_out=True, m_valid=width)
+        g = self.m_groups[r]
+        cos, sin = self.rope["yarn"]
+        # grid covers every token that could close a group; the kernel reads the real count
+        max_groups = min(T, sum(len(c.tokens) // r + 1 for c in m.chunks))
+        if max_groups:
+            ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
+                              self.comp_ring[lid],
+                              L.comp_norm, cfg.rms_norm_eps, cos, sin, self.comp[lid], L.idx_wk, L.idx_knorm,
+                              self.idx_cache.get(lid) if L.idx_wk is not None else None)
+        ext.ring_update(self.comp_ring[lid], proj, T, self.m_slot, self.m_pos, self.m_last)
+
+    def _indexer(self, L: LayerW, m: StepMeta, r: int):
+        cfg, ext = self.cfg, self.ext
+        T = m.T
+        lid = L.layer_id
+        nih, hd = cfg.index_n_heads, cfg.index_head_dim
+        self._gemm(self.qr_q, self.qr_sf, T, L.idx_wq_b, self.qidx.view(self.qidx.shape[0], -1))
+        self._gemm_bf16(self.u, L.idx_wproj, self.widx_raw, T, f32_out=True)
+        cos, sin = self.rope["yarn"]
+        ext.idx_q_prep(self.qidx, T, nih, hd, cos, sin, self.m_pos, self.widx_raw, (hd ** -0.5) * (nih ** -0.5),
+                       self.widx)
+        # widx_raw rows are 128 wide; idx_q_prep reads [T, nih] with row stride nih
+        src = self._k_source(lid)
+        cand_mode = 0
+        if lid == cfg.candidate_source_layer_id:
+            cand_mode = 1
+        elif 0 <= cfg.candidate_source_layer_id < lid:
+            cand_mode = 2
+        alt = self._k_alt(lid)
+        ext.indexer_topk(self.qidx, self.widx, self.idx_cache[src], self.m_slot, self.m_clen[r], cfg.index_topk,
+                         self.comp_idx, self.comp_cnt, self.cand if cand_mode else None, cand_mode,
+                         cfg.candidate_block_size, cfg.candidate_topk_blocks, T, self.err,
+                         self.idx_cache[alt] if alt is not None else None, self.m_pos, self.m_cstart, self.m_last, r)
+
+    def _k_alt(self, lid: int) -> int | None:
+        """K cache read by tokens that do not close a group at ``lid`` this step.
+
+        With ``index_k_mode == "reference"`` the indexer reads the K cache of the
+        most recent K producer (reference.py:645-654).  A layer that owns K only
+        produces it on positions closing a group; for the other positions the
+        most recent producer is the last ratio-1 K owner (it produces every
+        position).  Returns None when every token reads the layer's own cache.
+        """
+        cfg = self.cfg
+        if cfg.index_k_mode != "reference" or lid not in cfg.kv_source_layer_ids or cfg.ratio(lid) == 1:
+            return None
+        r1 = [s for s in self.idx_cache if cfg.ratio(s) == 1]
+        if not r1:
+            raise NotImplementedError("reference index_k_mode needs a ratio-1 K owner; use index_k_mode='intended'")
+        return max(r1)
+
+    def _k_source(self, lid: int) -> int:
+        cfg = self.cfg
+        src = cfg.kv_source_for(lid)
+        # layers that own an indexer but no K projection read the newest K producer
+        while src not in self.idx_cache:
+            cands = [s for s in self.idx_cache if s <= lid]
+            src = max(cands)
+        return src
+
+    # ------------------------------------------------------------------- MoE
+    def _moe(self, L: LayerW, T: int):
+        cfg, ext = self.cfg, self.ext
+        lid = L.layer_id
+        E = cfg.n_experts_for(lid)
+        k = cfg.topk_for(lid)
+        D = cfg.dim
+        I = cfg.moe_inter_dim
+        logits = self.router_logits[E]
+        self._gemm_bf16(self.u, L.gate_w, logits, T, f32_out=True)
+        ids, wts, pos, rank = self.route[k]
+        ext.router_topk(logits, T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale, ids, wts)
+        if self.ep is not None and self.ep.world > 1:
+            return self.ep.moe(self, L, T, k)
+        ext.moe_plan(T, k, E, 0, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
+                     self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err)
+        ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf)
+        self._grouped(L, k)
+        self._shared_expert(L, T)
+        return self.yperm, pos, k
+
+    def _shared_expert(self, L: LayerW, T: int):
+        cfg = self.cfg
+        self._gemm(self.uq, self.usf, T, L.shared_w13, None, EPI_SWIGLU, hq=self.hs, hsf=self.hs_sf,
+                   swiglu_limit=cfg.swiglu_limit)
+        self._gemm(self.hs, self.hs_sf, T, L.shared_w2, self.shared_out)
+
+    def _grouped(self, L: LayerW, k: int):
+        cfg, ext = self.cfg, self.ext
+        I, D = cfg.moe_inter_dim, cfg.dim
+        ex = L.experts
+        bn = self.tile_rows
+        ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
+                 self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
+                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1)
+        ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm, ex.w2.q.shape[0],
+                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1)

@@ -31,6 +31,64 @@ CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG"]
 
 _mod = None
 
+# kernels launched per binding call (used to report how many of this
+# library's kernels a step issues)
+_KERNELS_PER_CALL = {"hc_step": 2, "attention": 1, "gemm": 1, "act_quant_mx": 1, "qkv_post": 1, "idx_q_prep": 1,
+                     "compress_pool": 1, "ring_update": 1, "router_topk": 1, "moe_plan": 1, "moe_scatter": 1,
+                     "indexer_topk": 1, "embed_streams": 1, "argmax_rows": 1, "act_roundtrip": 1,
+                     "fp4_roundtrip": 1, "ep_pack": 1, "ep_unpack_meta": 1, "ep_unpack_rows": 1,
+                     "ep_combine_pack": 1}
+
+
+class _Counting:
+    """Proxy of the extension module that counts kernel launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.active = False
+        self.count = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        k = _KERNELS_PER_CALL.get(name)
+        if k is None or not callable(fn):
+            return fn
+
+        def wrapped(*a, **kw):
+            if self.active:
+                n = k
+                if name == "attention" and len(a) > 20 and a[20] > 1:
+                    n = 2
+                self.count += n
+            return fn(*a, **kw)
+
+        return wrapped
+
+
+class LaunchCounter:
+    """Counts this library's kernel launches issued inside ``counting(True)``."""
+
+    def __init__(self):
+        self.count = 0
+
+    def counting(self, on: bool):
+        import contextlib
+
+        @contextlib.contextmanager
+        def cm():
+            px = load()
+            if not on or not isinstance(px, _Counting):
+                yield
+                return
+            px.active, px.count = True, 0
+            try:
+                yield
+            finally:
+                px.active = False
+                self.count = px.count
+
+        return cm()
+
 
 def sources() -> list[str]:
     return sorted(glob.glob(str(CSRC / "*.cu")) + glob.glob(str(CSRC / "*.cpp")))
@@ -77,5 +135,5 @@ def load(required: bool | None = None):
     mod = importlib.util.module_from_spec(spec)
     sys.modules[NAME] = mod
     spec.loader.exec_module(mod)
-    _mod = mod
-    return mod
+    _mod = _Counting(mod)
+    return _mod

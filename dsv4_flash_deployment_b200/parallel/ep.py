@@ -1,0 +1,94 @@
+"""Expert parallelism across the GPUs of one node.
+
+Ranks own contiguous expert ranges (EP = world size; 256/8 = 32 experts per
+rank for V4-Flash, 384/8 = 48 for V4.1).  Attention is data-parallel, so
+every rank routes its own tokens and exchanges (token, expert) pairs:
+
+  pack     routed pairs -> per-destination transport records (ep.cu)
+  exchange records to their expert's rank          (dispatch)
+  experts  plan + unpack + grouped W13/SwiGLU/W2 on the received rows
+  return   expert output rows back to the source   (combine)
+  combine  the mHC boundary kernel sums a token's rows by position
+
+Transports: ``nccl`` = ``all_to_all_single`` over fixed-capacity per-peer
+regions (the baseline; no host synchronization, graph-capturable); ``p2p`` =
+the pack/combine kernels store records straight into the peer's receive
+buffer through NVLink (symmetric memory) and a device barrier orders the two
+sides.  Capacity per peer is ``2 * T * k / world`` pairs (+64); overflow is
+reported through the device error word, never dropped silently.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+from ..ops.layout import ceil_to
+
+
+class EPGroup:
+    def __init__(self, rank: int, world: int, group=None, device=None, transport: str = "nccl"):
+        self.rank = rank
+        self.world = world
+        self.group = group
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", rank)
+        self.transport = transport
+        self._bufs = None
+
+    def expert_range(self, n_experts: int) -> tuple[int, int]:
+        per = n_experts // self.world
+        return self.rank * per, per
+
+    def experts_per_rank(self, n_experts: int) -> int:
+        return n_experts // self.world
+
+    def cap_per_peer(self, T: int, k: int) -> int:
+        return ceil_to(2 * T * k // self.world + 64, 16)
+
+    def recv_rows(self, T: int, k: int) -> int:
+        return self.world * self.cap_per_peer(T, k)
+
+    def _alloc(self, T: int, k: int, D: int):
+        cap = self.cap_per_peer(T, k)
+        rec = ceil_to(D + D // 32 + 8, 16)
+        n = self.world * cap
+        e = lambda *s, dt: torch.empty(*s, dtype=dt, device=self.dev)
+        self._bufs = dict(
+            cap=cap, rec=rec, k=k,
+            send=e(n * rec, dt=torch.uint8), recv=e(n * rec, dt=torch.uint8),
+            cnt=torch.zeros(self.world, dtype=torch.int32, device=self.dev),
+            rcnt=torch.zeros(self.world, dtype=torch.int32, device=self.dev),
+            pos_back=e(T, k, dt=torch.int32),
+            ids=e(n, 1, dt=torch.int32), wts=e(n, 1, dt=torch.float32), pos=e(n, 1, dt=torch.int32),
+            rank=e(n, 1, dt=torch.int32),
+            back_send=e(n, D, dt=torch.bfloat16), back_recv=e(n, D, dt=torch.bfloat16),
+        )
+
+    def moe(self, model, L, T: int, k: int):
+        """Runs the expert-parallel MoE block; returns (rows, positions, topk) for the combine."""
+        cfg, ext = model.cfg, model.ext
+        D, I = cfg.dim, cfg.moe_inter_dim
+        E = cfg.n_experts_for(L.layer_id)
+        e_begin, e_local = self.expert_range(E)
+        if self._bufs is None:
+            self._alloc(model.max_tokens, k, D)
+        b = self._bufs
+        cap, rec = b["cap"], b["rec"]
+        ids, wts, _, _ = model.route[k]
+        b["cnt"].zero_()
+        ext.ep_pack(ids, wts, T, model.uq, model.usf, e_local, self.world, cap, rec, b["send"], b["cnt"],
+                    b["pos_back"], None, self.rank, model.err)
+        dist.all_to_all_single(b["rcnt"], b["cnt"], group=self.group)
+        dist.all_to_all_single(b["recv"], b["send"], group=self.group)
+        n = self.world * cap
+        ext.ep_unpack_meta(b["recv"], b["rcnt"], self.world, cap, rec, D, b["ids"], b["wts"])
+        ext.moe_plan(n, 1, e_local, 0, b["ids"], b["wts"], model.counts, model.seg, b["rank"], model.tile_rows,
+                     2 * I, D, model.tiles13, model.nt13, model.tiles2, model.nt2, model.cap, b["pos"],
+                     model.row_scale, model.err)
+        ext.ep_unpack_rows(b["recv"], n, rec, D, b["pos"], model.xperm, model.xperm_sf)
+        model._grouped(L, 1)
+        ext.ep_combine_pack(model.yperm, b["pos"], n, cap, b["back_send"], None, self.rank)
+        dist.all_to_all_single(b["back_recv"], b["back_send"], group=self.group)
+        model._shared_expert(L, T)
+        return b["back_recv"], b["pos_back"], k

@@ -288,7 +288,7 @@ class RefModel:
         h = N.hc_post(self._moe(lid, v, p), h, f_post, f_comb)
         return h, f_pre
 
-    def step(self, ids: torch.Tensor, st: RefState):
+    def step(self, ids: torch.Tensor, st: RefState, trace: dict | None = None):
         """One decode step for tokens ``ids`` [B] at ``st.pos``.
 
         Returns (logits [B, V] fp32, main_hidden [B, n_taps*D] bf16 or None).
@@ -307,6 +307,8 @@ class RefModel:
                 h = self._engram(lid, h, hashes[:, cfg.engram_layer_ids.index(lid)])
             if lid in cfg.dspark_target_layer_ids:
                 taps.append(h.float().mean(-2).to(torch.bfloat16))
+            if trace is not None:
+                trace.setdefault(lid, []).append(h.clone())
             h, pre_mix = self._block(lid, h, pre_mix, pos, st, rt)
         y = N.rms_norm(N.hc_pre(h, pre_mix), self.w["norm.weight"], cfg.rms_norm_eps)
         logits = y.float() @ self.w["head.weight"].float().t()
