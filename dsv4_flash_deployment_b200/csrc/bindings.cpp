@@ -164,26 +164,27 @@ T* ptr(const Tensor& t) {
 }
 using bf16 = __nv_bfloat16;
 
-void hc_step(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
-             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn, const optional<Tensor>& scale,
-             const optional<Tensor>& base, const optional<Tensor>& cw, int64_t cw_stride,
-             const optional<Tensor>& norm_w, const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials,
-             const optional<Tensor>& u, const optional<Tensor>& uq, const optional<Tensor>& usf,
-             const optional<Tensor>& tap, int64_t T, int64_t iters, double hc_eps, double norm_eps) {
+dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm,
+                         const optional<Tensor>& pos, int64_t topk, const optional<Tensor>& prev_mix,
+                         const optional<Tensor>& mix_raw, const optional<Tensor>& scale, const optional<Tensor>& base,
+                         const optional<Tensor>& cw, int64_t cw_stride, const optional<Tensor>& norm_w,
+                         const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials,
+                         const optional<Tensor>& u, const optional<Tensor>& uq, const optional<Tensor>& usf,
+                         const optional<Tensor>& tap, int64_t T, int64_t iters, double hc_eps, double norm_eps) {
   CHECK_CUDA(X);
   TORCH_CHECK(X.size(1) == 4, "hc_mult must be 4");
   dsv4::HcParams p{};
   p.T = (int)T;
   p.D = (int)X.size(2);
-  TORCH_CHECK(p.D % 128 == 0, "D % 128");
-  TORCH_CHECK(partials.numel() >= T * dsv4::hc_num_slices(p.D) * 26, "partials too small");
+  TORCH_CHECK(p.D % 256 == 0, "D % 256");
+  TORCH_CHECK(partials.numel() >= T * dsv4::hc_num_slices(p.D) * 2, "partials too small");
   p.X = ptr<bf16>(X);
   p.Y = ptr<const bf16>(Y);
   p.yperm = ptr<const bf16>(yperm);
   p.pos = ptr<const int>(pos);
   p.topk = (int)topk;
   p.prev_mix = ptr<const float>(prev_mix);
-  p.fn = ptr<const float>(fn);
+  p.mix_raw = ptr<const float>(mix_raw);
   p.scale = ptr<const float>(scale);
   p.base = ptr<const float>(base);
   p.cw = ptr<const float>(cw);
@@ -199,8 +200,28 @@ void hc_step(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>&
   p.iters = (int)iters;
   p.hc_eps = (float)hc_eps;
   p.norm_eps = (float)norm_eps;
+  return p;
+}
+
+void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
+             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& cw, int64_t cw_stride,
+             const Tensor& c, const Tensor& partials, const optional<Tensor>& tap, int64_t T) {
+  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, c10::nullopt, c10::nullopt, c10::nullopt, cw, cw_stride,
+                     c10::nullopt, c10::nullopt, c, partials, c10::nullopt, c10::nullopt, c10::nullopt, tap, T, 0, 0,
+                     0);
   const c10::cuda::CUDAGuard guard(X.device());
-  CUDA_OK(dsv4::hc_step(p, cur_stream()));
+  CUDA_OK(dsv4::hc_post(p, cur_stream()));
+}
+
+void hc_finish(const Tensor& X, const optional<Tensor>& mix_raw, const optional<Tensor>& scale,
+               const optional<Tensor>& base, const optional<Tensor>& cw, const optional<Tensor>& norm_w,
+               const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials, const optional<Tensor>& u,
+               const optional<Tensor>& uq, const optional<Tensor>& usf, int64_t T, int64_t iters, double hc_eps,
+               double norm_eps) {
+  auto p = hc_params(X, c10::nullopt, c10::nullopt, c10::nullopt, 0, c10::nullopt, mix_raw, scale, base, cw, 24,
+                     norm_w, mix_out, c, partials, u, uq, usf, c10::nullopt, T, iters, hc_eps, norm_eps);
+  const c10::cuda::CUDAGuard guard(X.device());
+  CUDA_OK(dsv4::hc_finish(p, cur_stream()));
 }
 
 void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const optional<Tensor>& rope_pos,
@@ -437,7 +458,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_quant_mx", &act_quant_mx);
   m.def("act_roundtrip", &act_roundtrip);
   m.def("fp4_roundtrip", &fp4_roundtrip);
-  m.def("hc_step", &hc_step);
+  m.def("hc_post", &hc_post);
+  m.def("hc_finish", &hc_finish);
   m.def("hc_num_slices", [](int64_t d) { return (int64_t)dsv4::hc_num_slices((int)d); });
   m.def("attention", &attention);
   m.def("attn_smem", []() { return (int64_t)dsv4::attn_smem_bytes(); });

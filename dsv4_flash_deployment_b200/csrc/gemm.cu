@@ -10,8 +10,9 @@
 //   KIND_BF16   tcgen05.mma kind::f16, bf16 x bf16 -> fp32.
 //   KIND_MX8    kind::mxf8f6f4.block_scale, e4m3 x e4m3 with ue8m0 scales per
 //               32 K-elements on both operands (MXFP8), fp32 accumulate.
-//   KIND_MX4A   same with the A operand e2m1 (MXFP4 weights, unpacked in smem by
-//               TMA's 16U4_ALIGN8B type).
+//   KIND_MX4A   same with the A operand e2m1 (MXFP4 weights, unpacked to one byte
+//               per element in smem by TMA's 16U4_ALIGN16B type; the TMA
+//               transaction count is the packed size, half the smem footprint).
 // Block scales arrive in the 512-byte "chunk" layout (common.cuh), one chunk per
 // (128-row tile, 128-column k tile), moved by a 1-D bulk copy into shared
 // memory and by tcgen05.cp into TMEM next to the accumulator.
@@ -37,15 +38,18 @@ struct GemmSmem {
   static constexpr int kB = BN * 128;
   static constexpr int kSfbChunks = (BN + 127) / 128;
   static constexpr int kSf = 512 * (1 + kSfbChunks);
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : 7);
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 7);
   static constexpr int kStage = kA + kB + kSf;
-  static constexpr int kXbuf = 2 * 32 * 32 * 4;        // SwiGLU exchange
+  static constexpr int kXbuf = 4 * 32 * 32 * 4;        // SwiGLU exchange (4 warps x 32 cols x 32 lanes)
   static constexpr int kBarriers = 256;
   static constexpr int kTotal = 1024 + kStages * kStage + kXbuf + kBarriers;
-  // TMEM: accumulator columns, then per-stage scale-factor columns.
+  // TMEM: NUM_ACC accumulator buffers (double-buffered when they fit, so the
+  // epilogue of one tile overlaps the mainloop of the next), then per-stage
+  // scale-factor columns.
+  static constexpr int kNumAcc = BN <= 128 ? 2 : 1;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
   static constexpr int kSfCols = 4 * (1 + kSfbChunks);
-  static constexpr int kColsNeeded = kAccCols + kStages * kSfCols;
+  static constexpr int kColsNeeded = kNumAcc * kAccCols + kStages * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                  : kColsNeeded <= 256 ? 256 : 512;
 };
@@ -106,12 +110,13 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sSF = sB + S * L::kB;
   float* xbuf = reinterpret_cast<float*>(sSF + S * L::kSf);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + L::kXbuf);
+  constexpr int NA = L::kNumAcc;
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* acc_full = bars + 2 * S;
-  uint64_t* acc_empty = bars + 2 * S + 1;
-  uint64_t* drain = bars + 2 * S + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
+  uint64_t* acc_empty = bars + 2 * S + NA;
+  uint64_t* drain = bars + 2 * S + 2 * NA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 2 * NA + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = const_cast<int*>(abort_flag) + 1;
 
@@ -123,8 +128,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    for (int a = 0; a < NA; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -151,7 +158,8 @@ __global__ void __launch_bounds__(192, 1)
     TileCoord t;
     for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-      const uint32_t tx = L::kA + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
+      constexpr uint32_t kATx = KIND == KIND_MX4A ? L::kA / 2 : L::kA;
+      const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
       for (int kt = t.k_begin; kt < t.k_end; ++kt) {
@@ -180,12 +188,14 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------------------------------------------------------- MMA
     int stage = 0;
     uint32_t phase = 0;
+    int acc = 0;
     uint32_t acc_phase = 0;
     TileCoord t;
     for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
       const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, KIND == KIND_MX4A ? 5 : 0, 0) : idesc_bf16(128, t.n_eff);
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-      if (!mbar_wait(acc_empty, acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
+      const uint32_t d_tmem = tmem + acc * L::kAccCols;
+      if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
       tc_fence_after();
       for (int kt = t.k_begin; kt < t.k_end; ++kt) {
         if (!mbar_wait(&full[stage], phase, abort_flag, p.err, KID_GEMM, 3)) goto done;
@@ -196,7 +206,7 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t sfa_t = 0, sfb_t = 0;
           if constexpr (MX) {
             const uint32_t sf0 = smem_u32(sSF + stage * L::kSf);
-            const uint32_t col = tmem + L::kAccCols + stage * L::kSfCols;
+            const uint32_t col = tmem + NA * L::kAccCols + stage * L::kSfCols;
             utccp_32x128b_x4(col, umma_sdesc(sf0, 16, 128, kLayoutNone));
             for (int c = 0; c < sfb_chunks; ++c)
               utccp_32x128b_x4(col + 4 + 4 * c, umma_sdesc(sf0 + 512 * (1 + c), 16, 128, kLayoutNone));
@@ -207,11 +217,11 @@ __global__ void __launch_bounds__(192, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = sdesc_kmajor_sw128(a0 + kk * 32);
             const uint64_t bd = sdesc_kmajor_sw128(b0 + kk * 32);
-            const uint32_t acc = (kt > t.k_begin || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (kt > t.k_begin || kk > 0) ? 1u : 0u;
             if constexpr (MX)
-              umma_mx(tmem, ad, bd, idesc_mx_sf(idesc, kk), sfa_t, sfb_t, acc);
+              umma_mx(d_tmem, ad, bd, idesc_mx_sf(idesc, kk), sfa_t, sfb_t, accum);
             else
-              umma_bf16(tmem, ad, bd, idesc, acc);
+              umma_bf16(d_tmem, ad, bd, idesc, accum);
           }
           umma_commit(&empty[stage]);
         }
@@ -221,19 +231,24 @@ __global__ void __launch_bounds__(192, 1)
           phase ^= 1;
         }
       }
-      if (lane == 0) umma_commit(acc_full);
+      if (lane == 0) umma_commit(&acc_full[acc]);
       __syncwarp();
-      acc_phase ^= 1;
+      if (++acc == NA) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
     }
   } else {
     // ----------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = 32 * q + lane;
+    int acc = 0;
     uint32_t acc_phase = 0;
     TileCoord t;
     for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
-      if (!mbar_wait(acc_full, acc_phase, abort_flag, p.err, KID_GEMM, 4)) goto done;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, KID_GEMM, 4)) goto done;
       tc_fence_after();
+      const uint32_t d_tmem = tmem + acc * L::kAccCols;
       const bool split = p.splits > 1;
       constexpr int kCols = BN < 32 ? BN : 32;
       float* ws_tile = split ? p.workspace + (size_t)t.tile * p.splits * 128 * BN : nullptr;
@@ -241,8 +256,8 @@ __global__ void __launch_bounds__(192, 1)
         // Publish this split's partial tile, then let the last arrival reduce.
         for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
           uint32_t r[32];
-          if constexpr (kCols == 32) tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, r);
-          else tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_ld_wait();
           float* dst = ws_tile + (size_t)t.split * 128 * BN;
 #pragma unroll
@@ -250,7 +265,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
@@ -261,7 +276,10 @@ __global__ void __launch_bounds__(192, 1)
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!*last_flag) {
-          acc_phase ^= 1;
+          if (++acc == NA) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
           continue;
         }
         __threadfence();
@@ -278,34 +296,37 @@ __global__ void __launch_bounds__(192, 1)
           }
         } else {
           uint32_t r[32];
-          if constexpr (kCols == 32) tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, r);
-          else tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < kCols; ++j) v[j] = __uint_as_float(r[j]);
         }
         if constexpr (EPI == EPI_SWIGLU) {
-          // rows 0..63 gate, 64..127 up (same 64 intermediate indices)
-          if (q >= 2) {
+          // rows 0..63 gate, 64..127 up (same 64 intermediate indices).  Every warp
+          // stages its 32 columns, then warp w finishes row group (w & 1) for the
+          // column half (w >> 1): all four warps share the SwiGLU/requant work.
 #pragma unroll
-            for (int j = 0; j < kCols; ++j) xbuf[((q - 2) * 32 + j) * 32 + lane] = v[j];
-          }
+          for (int j = 0; j < kCols; ++j) xbuf[(q * 32 + j) * 32 + lane] = v[j];
           asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (q < 2) {
-            const int i_local = 32 * q + lane;
+          {
+            const int g = q & 1, half = q >> 1;
+            const int i_local = 32 * g + lane;
             const int i_global = (t.out_col0 >> 1) + i_local;  // out_col0 = 128 * m-tile
             const int kblk = i_global >> 5;
             const float lim = p.swiglu_limit;
+            const int j0 = half * (kCols / 2);
 #pragma unroll 4
-            for (int j = 0; j < kCols; ++j) {
+            for (int jj = 0; jj < kCols / 2; ++jj) {
+              const int j = j0 + jj;
               const int n = c0 + j;
-              float g = bf16_round(v[j]);
-              float u = bf16_round(xbuf[(q * 32 + j) * 32 + lane]);
+              float gv = bf16_round(xbuf[(g * 32 + j) * 32 + lane]);
+              float u = bf16_round(xbuf[((2 + g) * 32 + j) * 32 + lane]);
               if (lim > 0.f) {
                 u = fminf(fmaxf(u, -lim), lim);
-                g = fminf(g, lim);
+                gv = fminf(gv, lim);
               }
-              float h = g / (1.f + expf(-g)) * u;
+              float h = gv / (1.f + expf(-gv)) * u;
               const int brow = t.b_row0 + n;
               if (p.row_scale && n < t.b_valid) h *= __ldg(p.row_scale + brow);
               h = bf16_round(h);
@@ -340,9 +361,12 @@ __global__ void __launch_bounds__(192, 1)
       if (!split) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
       }
-      acc_phase ^= 1;
+      if (++acc == NA) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
     }
   }
 done:

@@ -51,7 +51,7 @@ cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorM
                         const GemmParams& p, int grid, cudaStream_t st);
 
 // 2-D tensor map over a row-major [rows, cols] matrix of 1-byte (e4m3), 2-byte
-// (bf16) or packed 4-bit (e2m1, unpacked to 1 byte per element in smem)
+// (bf16) or packed 4-bit (e2m1, TMA type 16U4_ALIGN16B: unpacked to one byte per element in smem, the operand form of kind::mxf8f6f4)
 // elements; box = {128 bytes of K, box_rows}, 128B swizzle.
 enum TmaElem { TMA_U8 = 0, TMA_BF16 = 1, TMA_E2M1 = 2 };
 bool make_tma_2d(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols, uint32_t box_rows);

@@ -22,7 +22,7 @@ struct HcParams {
   const int* pos;                   // MoE: [T, topk] permuted row per slot (-1 = none)
   int topk;
   const float* prev_mix;            // [T, 24] (pre | post | comb) of the previous boundary
-  const float* fn;                  // [24, 4*D] mixing projection (null = no mixes)
+  const float* mix_raw;             // [T, 48] projection of X' on (hi | lo) rows of hc_fn (null = no mixes)
   const float* scale;               // [3]
   const float* base;                // [24]
   const float* cw;                  // collapse weights: cw[t * cw_stride + i]
@@ -30,7 +30,7 @@ struct HcParams {
   const __nv_bfloat16* norm_w;      // [D]
   float* mix_out;                   // [T, 24]
   __nv_bfloat16* c;                 // scratch [T, D]
-  float* partials;                  // scratch [T, n_slices, 26]
+  float* partials;                  // scratch [T, n_slices, 2]
   __nv_bfloat16* u;                 // [T, D] normalized collapse
   uint8_t* uq;                      // [T_pad, D] e4m3 (optional)
   uint8_t* usf;                     // scale chunks of uq
@@ -39,7 +39,8 @@ struct HcParams {
   float hc_eps, norm_eps;
 };
 int hc_num_slices(int D);
-cudaError_t hc_step(const HcParams& p, cudaStream_t st);
+cudaError_t hc_post(const HcParams& p, cudaStream_t st);
+cudaError_t hc_finish(const HcParams& p, cudaStream_t st);
 
 // -------------------------------------------------------- attention.cu
 constexpr int kAttnMaxRows = 768;   // window (<= 256) + selected compressed rows

@@ -45,7 +45,7 @@ bool make_tma_2d(CUtensorMap* map, const void* base, int elem, uint64_t rows, ui
       box_k = 64;
       break;
     case TMA_E2M1:
-      dt = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN8B;
+      dt = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;  // each 16 e2m1 values land in 16 smem bytes (unpacked)
       row_bytes = cols / 2;
       box_k = 128;
       break;

@@ -139,7 +139,7 @@ def _seed_for(seed: int, name: str) -> int:
 
 
 def random_tensor(name: str, tag: str, shape: tuple[int, ...], seed: int = 0,
-                  device: str | torch.device = "cpu") -> torch.Tensor:
+                  device: str | torch.device = "cpu", mxfp4_experts: bool = False) -> torch.Tensor:
     """One deterministic random tensor for checkpoint entry ``name``.
 
     Scales are powers of two near 2^-7 so block-scaled weights have unit-ish
@@ -149,7 +149,10 @@ def random_tensor(name: str, tag: str, shape: tuple[int, ...], seed: int = 0,
     g.manual_seed(_seed_for(seed, name))
     dev = torch.device(device)
     if tag == E8:
-        return torch.randint(118, 123, shape, generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+        # MXFP4 expert codes span +-6 (vs ~N(0, 0.5) for e4m3 values): their scales sit
+        # 3 binades lower so both expert formats have the same weight magnitude.
+        lo = 115 if (".experts." in name and name.endswith(".scale") and mxfp4_experts) else 118
+        return torch.randint(lo, lo + 5, shape, generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
     if tag == I8:
         return torch.randint(-128, 128, shape, generator=g, device=dev, dtype=torch.int32).to(torch.int8)
     if tag == F8:
@@ -182,4 +185,5 @@ def make_random_weights(cfg, seed: int = 0, device: str | torch.device = "cpu",
                         names: Iterable[str] | None = None, include_mtp: bool = True) -> dict[str, torch.Tensor]:
     specs = checkpoint_specs(cfg, include_mtp=include_mtp)
     keys = list(specs) if names is None else list(names)
-    return {k: random_tensor(k, specs[k][0], specs[k][1], seed, device) for k in keys}
+    mx4 = cfg.expert_format == "mxfp4"
+    return {k: random_tensor(k, specs[k][0], specs[k][1], seed, device, mx4) for k in keys}

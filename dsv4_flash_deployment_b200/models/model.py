@@ -22,6 +22,7 @@ dispatch/combine exchange of :mod:`..parallel.ep`.
 
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 
@@ -139,7 +140,8 @@ class DSV4Model:
         z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=dev)
         self.X = e(T, cfg.hc_mult, D)
         self.hc_c = e(T, D)
-        self.hc_part = e(T * self.ext.hc_num_slices(D) * 26, dt=f32)
+        self.hc_part = e(T * self.ext.hc_num_slices(D) * 2, dt=f32)
+        self.mix_raw = e(T, 48, dt=f32)
         self.mixA, self.mixF = z(T, 24, dt=f32), z(T, 24, dt=f32)
         init = torch.zeros(T, 24, dtype=f32, device=dev)
         init[:, 0] = 1.0
@@ -185,7 +187,9 @@ class DSV4Model:
         e_local = E if self.ep is None else self.ep.experts_per_rank(E)
         recv_rows = T * k if self.ep is None else self.ep.recv_rows(T, k)
         self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
-        self.tile_rows = 128 if recv_rows <= 4096 else 256
+        # 128-row expert tiles keep two accumulators in TMEM (epilogue overlaps the
+        # next tile); 256-row tiles halve weight re-reads when experts get many rows
+        self.tile_rows = 128 if recv_rows <= 192 * e_local else 256
         tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
         I = cfg.moe_inter_dim
         self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)
@@ -282,6 +286,20 @@ class DSV4Model:
             put(self.m_ngroups[r], np.asarray([len(g[0])], np.int32))
 
     last_upload_bytes = 0
+    op_timer: dict | None = None
+
+    @contextlib.contextmanager
+    def _t(self, name: str):
+        """CUDA-event timing of one op group (eager runs only; off by default)."""
+        if self.op_timer is None:
+            yield
+            return
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        self.op_timer.setdefault(name, []).append((s, e))
 
     # --------------------------------------------------------------- helpers
     def _gemm(self, xq, xsf, n_tok, w: MxWeight, out, epi=EPI_BF16, **kw):
@@ -296,16 +314,31 @@ class DSV4Model:
                        counters=self.counters if splits > 1 else None, **kw)
 
     def _gemm_bf16(self, x, w, out, n_tok, f32_out=False, groups=1, m_valid=None):
-        return gemm_bf16(x, w, out, f32_out=f32_out, groups=groups, n_tokens=n_tok, m_valid=m_valid)
+        bn = pick_bn(n_tok)
+        tiles = (w.shape[0] // 128) * ((n_tok + bn - 1) // bn)
+        k_tiles = x.shape[1] // groups // 64
+        splits = 1
+        if tiles < 100 and k_tiles >= 16:
+            splits = max(1, min(k_tiles // 8, 148 // max(tiles, 1)))
+            while tiles * splits * 128 * bn > self.ws.numel() and splits > 1:
+                splits -= 1
+        return gemm_bf16(x, w, out, f32_out=f32_out, groups=groups, n_tokens=n_tok, m_valid=m_valid, splits=splits,
+                         workspace=self.ws if splits > 1 else None, counters=self.counters if splits > 1 else None,
+                         bn=bn)
 
     def _hc(self, T, Y=None, yperm=None, pos=None, topk=0, prev=None, mixes=None, cw=None, norm=None,
             mix_out=None, u=None, uq=None, usf=None, tap=None):
-        cfg = self.cfg
-        fn = scale = base = None
+        """One mHC boundary: post/combine/collapse, tensor-core mixes, Sinkhorn + norm + quant."""
+        cfg, ext = self.cfg, self.ext
+        ext.hc_post(self.X, Y, yperm, pos, topk, prev, cw, 24, self.hc_c, self.hc_part, tap, T)
+        mix_raw = scale = base = None
         if mixes is not None:
-            fn, scale, base = mixes
-        self.ext.hc_step(self.X, Y, yperm, pos, topk, prev, fn, scale, base, cw, 24, norm, mix_out, self.hc_c,
-                         self.hc_part, u, uq, usf, tap, T, self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
+            fnhl, scale, base = mixes
+            self._gemm_bf16(self.X.view(self.X.shape[0], -1), fnhl, self.mix_raw, T, f32_out=True, m_valid=48)
+            mix_raw = self.mix_raw
+        if mixes is not None or (cw is not None and u is not None):
+            ext.hc_finish(self.X, mix_raw, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
+                          self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
 
     sinkhorn_iters = None
 
@@ -317,7 +350,8 @@ class DSV4Model:
             self.sinkhorn_iters = cfg.hc_sinkhorn_iters
         T = m.T
         ext = self.ext
-        self.ext.embed_streams(self.embed, self.m_ids, T, self.X)
+        with self._t("embed"):
+            self.ext.embed_streams(self.embed, self.m_ids, T, self.X)
         prev, cw = None, self.mix0
         moe_state = None
         for li, L in enumerate(self.layers):
@@ -325,6 +359,8 @@ class DSV4Model:
             tap = None
             if taps is not None and lid in cfg.dspark_target_layer_ids:
                 tap = taps[lid]
+            hc_ctx = self._t("mhc")
+            hc_ctx.__enter__()
             if moe_state is None:
                 self._hc(T, prev=None, mixes=L.hc_attn, cw=cw, norm=L.attn_norm, mix_out=self.mixA, u=self.u,
                          uq=self.uq, usf=self.usf, tap=tap)
@@ -333,13 +369,15 @@ class DSV4Model:
                 self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
                          cw=self.mixF, norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf,
                          tap=tap)
+            hc_ctx.__exit__(None, None, None)
             if trace is not None:
                 trace[lid] = self.X[:T].clone()
             self._attention(L, m)
             if trace is not None:
                 trace[f"attn{lid}"] = self.attn_out[:T].clone()
-            self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
-                     mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
+            with self._t("mhc"):
+                self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
+                         mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
             moe_state = self._moe(L, T)
         # final collapse + norm on all tokens, then head on the sampled rows
         yp, ps, kk = moe_state
@@ -348,9 +386,10 @@ class DSV4Model:
         S = len(m.sample_rows)
         if S == 0:
             return self.next_ids[:0]
-        torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
-        self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
-        ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S])
+        with self._t("head"):
+            torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
+            self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
+            ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S])
         return self.next_ids[:S]
 
     # ------------------------------------------------------------- attention
@@ -361,23 +400,28 @@ class DSV4Model:
         r = cfg.ratio(lid)
         cos, sin = self.rope["yarn" if r > 0 else "swa"]
         qa = cfg.q_lora_rank
-        self._gemm(self.uq, self.usf, T, L.wqkv_a, self.qkv)
-        ext.qkv_post(self.qkv, qa, cfg.head_dim, L.q_norm, L.kv_norm, cfg.rms_norm_eps, self.qr_q, self.qr_sf, cos,
+        with self._t("gemm_wqkv_a"):
+            self._gemm(self.uq, self.usf, T, L.wqkv_a, self.qkv)
+        with self._t("qkv_post"):
+            ext.qkv_post(self.qkv, qa, cfg.head_dim, L.q_norm, L.kv_norm, cfg.rms_norm_eps, self.qr_q, self.qr_sf, cos,
                      sin, self.m_pos, self.kv_step, T)
-        self._gemm(self.qr_q, self.qr_sf, T, L.wq_b, self.q.view(self.q.shape[0], -1))
+        with self._t("gemm_wq_b"):
+            self._gemm(self.qr_q, self.qr_sf, T, L.wq_b, self.q.view(self.q.shape[0], -1))
         comp = None
         comp_idx = None
         comp_cnt = None
         if r > 0:
             src = cfg.kv_source_for(lid)
             if lid in cfg.kv_source_layer_ids:
-                self._compress(L, m, r)
+                with self._t("compressor"):
+                    self._compress(L, m, r)
             clen = self.m_clen[r]
             if lid in cfg.index_source_layer_ids:
                 if m.index_bypass(r):
                     self._idx_sel = None
                 else:
-                    self._indexer(L, m, r)
+                    with self._t("indexer"):
+                        self._indexer(L, m, r)
                     self._idx_sel = (self.comp_idx, self.comp_cnt)
             if lid in cfg.index_source_layer_ids or lid not in cfg.kv_source_layer_ids:
                 sel = getattr(self, "_idx_sel", None)
@@ -391,13 +435,20 @@ class DSV4Model:
         splits = 1
         if T <= 8:
             splits = 8
+        tctx = self._t("attention")
+        tctx.__enter__()
         ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, self.ring[lid], comp,
                       self.m_slot, self.m_pos, self.m_cstart, self.m_row0, comp_idx, comp_cnt, L.sink,
                       cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits)
-        ext.ring_update(self.ring[lid], self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
-        self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=cfg.o_groups)
-        ext.act_quant_mx(self.oa[:T], self.oa_q, self.oa_sf)
-        self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.attn_out)
+        tctx.__exit__(None, None, None)
+        with self._t("ring_update"):
+            ext.ring_update(self.ring[lid], self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
+        with self._t("gemm_wo_a"):
+            self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=cfg.o_groups)
+        with self._t("quant_oa"):
+            ext.act_quant_mx(self.oa[:T], self.oa_q, self.oa_sf)
+        with self._t("gemm_wo_b"):
+            self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.attn_out)
 
     def _compress(self, L: LayerW, m: StepMeta, r: int):
         cfg, ext = self.cfg, self.ext
@@ -476,16 +527,23 @@ class DSV4Model:
         D = cfg.dim
         I = cfg.moe_inter_dim
         logits = self.router_logits[E]
+        rctx = self._t("router")
+        rctx.__enter__()
         self._gemm_bf16(self.u, L.gate_w, logits, T, f32_out=True)
         ids, wts, pos, rank = self.route[k]
         ext.router_topk(logits, T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale, ids, wts)
+        rctx.__exit__(None, None, None)
         if self.ep is not None and self.ep.world > 1:
             return self.ep.moe(self, L, T, k)
+        pctx = self._t("moe_plan_scatter")
+        pctx.__enter__()
         ext.moe_plan(T, k, E, 0, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
                      self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err)
         ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf)
+        pctx.__exit__(None, None, None)
         self._grouped(L, k)
-        self._shared_expert(L, T)
+        with self._t("shared_expert"):
+            self._shared_expert(L, T)
         return self.yperm, pos, k
 
     def _shared_expert(self, L: LayerW, T: int):
@@ -499,8 +557,14 @@ class DSV4Model:
         I, D = cfg.moe_inter_dim, cfg.dim
         ex = L.experts
         bn = self.tile_rows
+        c13 = self._t("grouped_w13")
+        c13.__enter__()
         ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                  self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
                  cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1)
+        c13.__exit__(None, None, None)
+        c2 = self._t("grouped_w2")
+        c2.__enter__()
         ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm, ex.w2.q.shape[0],
                  self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1)
+        c2.__exit__(None, None, None)

@@ -42,7 +42,7 @@ class ExpertBlock:
 class LayerW:
     layer_id: int
     prefix: str
-    hc_attn: tuple = ()    # (fn, scale, base)
+    hc_attn: tuple = ()    # (fn as bf16 hi|lo rows [128, 4D], scale [3], base [24])
     hc_ffn: tuple = ()
     attn_norm: torch.Tensor | None = None
     ffn_norm: torch.Tensor | None = None
@@ -66,6 +66,23 @@ class LayerW:
     shared_w13: MxWeight | None = None
     shared_w2: MxWeight | None = None
     extra: dict = field(default_factory=dict)
+
+
+def hc_fn_hilo(fn: torch.Tensor) -> torch.Tensor:
+    """fp32 mixing projection [24, 4D] -> bf16 [128, 4D]: rows 0-23 = bf16(fn), rows
+    24-47 = bf16(fn - bf16(fn)), rest zero.  hi + lo reproduces fn to ~2^-16 relative,
+    so the tensor-core GEMM with fp32 accumulation matches the fp32 projection."""
+    fn = fn.float()
+    hi = fn.to(torch.bfloat16)
+    lo = (fn - hi.float()).to(torch.bfloat16)
+    out = torch.zeros(128, fn.shape[1], dtype=torch.bfloat16, device=fn.device)
+    out[: fn.shape[0]] = hi
+    out[fn.shape[0]: 2 * fn.shape[0]] = lo
+    return out
+
+
+def _hc_params(fn, scale, base, dev):
+    return (hc_fn_hilo(fn.to(dev)), scale.float().to(dev).contiguous(), base.float().to(dev).contiguous())
 
 
 def _pad_rows(w: torch.Tensor, mult: int = 128) -> torch.Tensor:
@@ -94,8 +111,8 @@ def load_layer(cfg, W: dict, lid: int, dev, prefix: str | None = None, experts: 
     p = prefix or f"layers.{lid}"
     g = lambda k: W[f"{p}.{k}"]
     L = LayerW(layer_id=lid, prefix=p)
-    L.hc_attn = tuple(g(f"hc_attn_{x}").float().to(dev).contiguous() for x in ("fn", "scale", "base"))
-    L.hc_ffn = tuple(g(f"hc_ffn_{x}").float().to(dev).contiguous() for x in ("fn", "scale", "base"))
+    L.hc_attn = _hc_params(g("hc_attn_fn"), g("hc_attn_scale"), g("hc_attn_base"), dev)
+    L.hc_ffn = _hc_params(g("hc_ffn_fn"), g("hc_ffn_scale"), g("hc_ffn_base"), dev)
     L.attn_norm = g("attn_norm.weight").to(dev)
     L.ffn_norm = g("ffn_norm.weight").to(dev)
     L.wqkv_a = _cat_mx([(g("attn.wq_a.weight"), g("attn.wq_a.scale")), (g("attn.wkv.weight"), g("attn.wkv.scale"))], dev)
@@ -155,7 +172,8 @@ def _rand_mx(n: int, k: int, dev, gen: torch.Generator, kind_e2m1: bool = False)
             r1 = min(npad, r0 + step)
             q[r0:r1] = (torch.randn(r1 - r0, k, device=dev, generator=gen) * 0.5).to(torch.float8_e4m3fn).view(
                 torch.uint8)
-    sf = torch.randint(118, 123, (npad // 128, k // 128, 512), device=dev, dtype=torch.uint8, generator=gen)
+    lo = 115 if kind_e2m1 else 118   # e2m1 codes span +-6: scales 3 binades lower match e4m3 magnitudes
+    sf = torch.randint(lo, lo + 5, (npad // 128, k // 128, 512), device=dev, dtype=torch.uint8, generator=gen)
     return MxWeight(q, sf, n, k, 2 if kind_e2m1 else 1)
 
 
@@ -179,7 +197,8 @@ def random_layer(cfg, lid: int, dev, gen: torch.Generator, experts: ExpertBlock)
 
     def hc():
         fn = torch.randn(cfg.hc_rows, cfg.hc_mult * d, device=dev, generator=gen) * 0.02
-        return fn, torch.full((3,), 0.25, device=dev), torch.randn(cfg.hc_rows, device=dev, generator=gen) * 0.05
+        return _hc_params(fn, torch.full((3,), 0.25, device=dev),
+                          torch.randn(cfg.hc_rows, device=dev, generator=gen) * 0.05, dev)
 
     L.hc_attn, L.hc_ffn = hc(), hc()
     L.attn_norm, L.ffn_norm = norm(d), norm(d)

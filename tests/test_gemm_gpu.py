@@ -153,3 +153,86 @@ def test_grouped_mx8():
         if c:
             ref = N.fp8_linear(x[st:st + c], *ws[ei], torch.float32)
             _close(out[st:st + c], ref)
+
+
+def test_mx4_weights_dense_and_grouped():
+    """MXFP4 (e2m1 + ue8m0/32) weights x MXFP8 activations (the V4.1 expert format)."""
+    from dsv4_flash_deployment_b200.ref.numerics import pack_e2m1
+
+    n, k, t = 256, 512, 40
+    g = torch.Generator().manual_seed(7)
+    codes = torch.randint(0, 16, (n, k), generator=g, dtype=torch.int32).to(torch.uint8)
+    w = pack_e2m1(codes).view(torch.int8)
+    s = torch.randint(118, 123, (n, k // 32), generator=g, dtype=torch.int32).to(torch.uint8)
+    x = torch.randn(t, k, generator=g).to(torch.bfloat16)
+    ref = N.fp8_linear(x, w, s, torch.float32)
+    mw = G.MxWeight.from_checkpoint(w, s, "cuda")
+    assert mw.kind == G.KIND_MX4A
+    xq, xsf = G.quantize(x.cuda())
+    out = torch.empty(t, n, dtype=torch.float32, device="cuda")
+    G.gemm_mx(xq, xsf, t, mw, out, G.EPI_F32)
+    torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
+    _close(out, ref, 1e-3)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "mxfp8"])
+def test_grouped_expert_ffn_matches_oracle(fmt):
+    """Grouped W13 (SwiGLU + requant epilogue) then grouped W2, vs the oracle expert FFN."""
+    from dsv4_flash_deployment_b200.ops.gemm import prepare_w13
+    from dsv4_flash_deployment_b200.ref.numerics import pack_e2m1
+
+    E, I, D = 4, 256, 512
+    counts = [3, 0, 37, 130]
+    g = torch.Generator().manual_seed(11)
+
+    def wt(n, k):
+        if fmt == "mxfp4":
+            w = pack_e2m1(torch.randint(0, 16, (n, k), generator=g, dtype=torch.int32).to(torch.uint8)).view(torch.int8)
+            s = torch.randint(115, 120, (n, k // 32), generator=g, dtype=torch.int32).to(torch.uint8)
+        else:
+            w = (torch.randn(n, k, generator=g) * 0.5).to(torch.float8_e4m3fn)
+            s = torch.randint(118, 123, (n, k // 32), generator=g, dtype=torch.int32).to(torch.uint8)
+        return w, s
+
+    experts = [(wt(I, D), wt(I, D), wt(D, I)) for _ in range(E)]
+    w13s = [prepare_w13(a[0], a[1], b[0], b[1], "cpu") for a, b, _ in experts]
+    w13 = G.MxWeight(torch.cat([m.q for m in w13s]).cuda(), torch.cat([m.sf for m in w13s]).cuda(),
+                     E * 2 * I, D, w13s[0].kind)
+    w2s = [G.MxWeight.from_checkpoint(c[0], c[1], "cpu") for _, _, c in experts]
+    w2 = G.MxWeight(torch.cat([m.q for m in w2s]).cuda(), torch.cat([m.sf for m in w2s]).cuda(), E * D, I,
+                    w2s[0].kind)
+    starts, rows = [], 0
+    for c in counts:
+        starts.append(rows)
+        rows += ceil_to(c, 128)
+    x = torch.randn(rows, D, generator=g).to(torch.bfloat16)
+    rw = torch.rand(rows, generator=g)
+    xq, xsf = G.quantize(x.cuda())
+    t13, t2 = [], []
+    for e, (st, c) in enumerate(zip(starts, counts)):
+        for r0 in range(0, c, 128):
+            v = min(128, c - r0)
+            t13 += [[e * 2 * I + mt * 128, st + r0, v, mt * 128] for mt in range(2 * I // 128)]
+            t2 += [[e * D + mt * 128, st + r0, v, mt * 128] for mt in range(D // 128)]
+    t13 = torch.tensor(t13, dtype=torch.int32, device="cuda")
+    t2 = torch.tensor(t2, dtype=torch.int32, device="cuda")
+    hq = torch.zeros(rows, I, dtype=torch.uint8, device="cuda")
+    hsf = torch.zeros(rows // 128, I // 128, 512, dtype=torch.uint8, device="cuda")
+    y = torch.zeros(rows, D, dtype=torch.bfloat16, device="cuda")
+    ext = G._ext.load()
+    err = G.ErrorWord.get("cuda")
+    ext.gemm(w13.kind, G.EPI_SWIGLU, w13.q, w13.sf, xq, xsf, None, w13.q.shape[0], rows, D, 128, 1, t13,
+             torch.tensor([len(t13)], dtype=torch.int32, device="cuda"), rw.cuda(), hq, hsf, 10.0, 2 * I, 0, None,
+             None, err, 0, 1)
+    ext.gemm(w2.kind, G.EPI_BF16, w2.q, w2.sf, hq, hsf, y, w2.q.shape[0], rows, I, 128, 1, t2,
+             torch.tensor([len(t2)], dtype=torch.int32, device="cuda"), None, None, None, 0.0, D, D, None, None,
+             err, 0, 1)
+    torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
+    for e, (st, c) in enumerate(zip(starts, counts)):
+        if not c:
+            continue
+        (w1, s1), (w3, s3), (w2_, s2) = experts[e]
+        ref = N.expert_ffn(x[st:st + c], w1, s1, w3, s3, w2_, s2, 10.0, rw[st:st + c, None])
+        _close(y[st:st + c], ref, 0.05)
