@@ -138,7 +138,7 @@ def main() -> None:
     group = None
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
     cfg = v4_flash_config()
     C, isl, osl, chunk = args.concurrency, args.isl, args.osl, args.chunk
@@ -165,8 +165,9 @@ def main() -> None:
         chunks = [SeqChunk(s, int(state["dec"][s]), [int(rng.integers(0, cfg.vocab_size))], True)
                   for s in range(n_dec)]
         p0 = state["pre"]
-        chunks.append(SeqChunk(pre_slot, p0, rng.integers(0, cfg.vocab_size, chunk_rank).tolist(),
-                               p0 + chunk_rank >= isl))
+        # the prefill chunk always samples (one extra logits row on non-final
+        # chunks) so every step has the same shape and replays one graph
+        chunks.append(SeqChunk(pre_slot, p0, rng.integers(0, cfg.vocab_size, chunk_rank).tolist(), True))
         state["dec"] = np.where(state["dec"] + 1 >= max_seq, isl, state["dec"] + 1)
         state["pre"] = (p0 + chunk_rank) % isl
         return StepMeta(cfg, chunks)

@@ -30,25 +30,40 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=None, help="override routed experts (small profiling cases)")
     ap.add_argument("--topk", type=int, default=None)
     a = ap.parse_args()
+    import os
+
+    import torch.distributed as dist
+
+    from ..parallel.ep import EPGroup
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    ep = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local))
     kw = {"n_layers": a.layers} if a.layers else {}
     if a.experts:
         kw["n_routed_experts"] = a.experts
     if a.topk:
         kw["n_activated_experts"] = a.topk
     cfg = v4_flash_config(**kw)
-    dev = torch.device("cuda")
-    n_dec = a.concurrency - 1
-    T = n_dec + a.chunk
-    n_phys = plan_expert_storage(cfg, dev, T, a.concurrency + 1, 2048)
-    eng = Engine.build(cfg, dev, max_seqs=a.concurrency + 1, max_batched_tokens=T, max_seq_len=2048,
-                       expert_storage_layers=n_phys, use_graphs=False)
+    dev = torch.device("cuda", local)
+    n_dec = a.concurrency // world - 1
+    chunk = a.chunk // world
+    T = n_dec + chunk
+    n_phys = plan_expert_storage(cfg, dev, T, n_dec + 2, 2048, world)
+    eng = Engine.build(cfg, dev, max_seqs=n_dec + 2, max_batched_tokens=T, max_seq_len=2048,
+                       expert_storage_layers=n_phys, use_graphs=False, ep=ep)
     m = eng.model
     rng = np.random.default_rng(0)
     dec = 1024 + (np.arange(n_dec) * (1024 // n_dec) + 1) % 1024
 
     def meta(i):
         ch = [SeqChunk(s, int(dec[s]) + i, [int(rng.integers(0, cfg.vocab_size))], True) for s in range(n_dec)]
-        ch.append(SeqChunk(n_dec, (i % 2) * a.chunk, rng.integers(0, cfg.vocab_size, a.chunk).tolist(), i % 2 == 1))
+        ch.append(SeqChunk(n_dec, (i % 2) * chunk, rng.integers(0, cfg.vocab_size, chunk).tolist(), i % 2 == 1))
         return StepMeta(cfg, ch)
 
     eng.run_meta(meta(0))
@@ -65,10 +80,14 @@ def main() -> None:
     total = tot_s.elapsed_time(tot_e) / a.steps
     rows = {k: sum(s.elapsed_time(e) for s, e in v) / a.steps for k, v in m.op_timer.items()}
     acc = sum(rows.values())
-    for k, v in sorted(rows.items(), key=lambda x: -x[1]):
-        print(f"{k:20s} {v:9.3f} ms  {100 * v / total:5.1f}%  ({len(m.op_timer[k]) // a.steps} launches/step)")
-    print(json.dumps({"step_ms": round(total, 3), "sum_ops_ms": round(acc, 3), "T": T, "n_layers": cfg.n_layers,
-                      "expert_storage_layers": n_phys}))
+    if rank == 0:
+        for k, v in sorted(rows.items(), key=lambda x: -x[1]):
+            print(f"{k:20s} {v:9.3f} ms  {100 * v / total:5.1f}%  ({len(m.op_timer[k]) // a.steps} launches/step)")
+        print(json.dumps({"step_ms": round(total, 3), "sum_ops_ms": round(acc, 3), "T": T, "n_layers": cfg.n_layers,
+                          "expert_storage_layers": n_phys, "world": world}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -166,7 +166,7 @@ using bf16 = __nv_bfloat16;
 
 dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm,
                          const optional<Tensor>& pos, int64_t topk, const optional<Tensor>& prev_mix,
-                         const optional<Tensor>& mix_raw, const optional<Tensor>& scale, const optional<Tensor>& base,
+                         const optional<Tensor>& fn_hilo, const optional<Tensor>& scale, const optional<Tensor>& base,
                          const optional<Tensor>& cw, int64_t cw_stride, const optional<Tensor>& norm_w,
                          const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials,
                          const optional<Tensor>& u, const optional<Tensor>& uq, const optional<Tensor>& usf,
@@ -176,15 +176,15 @@ dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optio
   dsv4::HcParams p{};
   p.T = (int)T;
   p.D = (int)X.size(2);
-  TORCH_CHECK(p.D % 256 == 0, "D % 256");
-  TORCH_CHECK(partials.numel() >= T * dsv4::hc_num_slices(p.D) * 2, "partials too small");
+  TORCH_CHECK(p.D % 128 == 0, "D % 128");
+  TORCH_CHECK(partials.numel() >= T * dsv4::hc_num_slices(p.D) * 50, "partials too small");
   p.X = ptr<bf16>(X);
   p.Y = ptr<const bf16>(Y);
   p.yperm = ptr<const bf16>(yperm);
   p.pos = ptr<const int>(pos);
   p.topk = (int)topk;
   p.prev_mix = ptr<const float>(prev_mix);
-  p.mix_raw = ptr<const float>(mix_raw);
+  p.fn_hilo = ptr<const bf16>(fn_hilo);
   p.scale = ptr<const float>(scale);
   p.base = ptr<const float>(base);
   p.cw = ptr<const float>(cw);
@@ -204,21 +204,22 @@ dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optio
 }
 
 void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
-             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& cw, int64_t cw_stride,
-             const Tensor& c, const Tensor& partials, const optional<Tensor>& tap, int64_t T) {
-  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, c10::nullopt, c10::nullopt, c10::nullopt, cw, cw_stride,
+             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn_hilo,
+             const optional<Tensor>& cw, int64_t cw_stride, const Tensor& c, const Tensor& partials,
+             const optional<Tensor>& tap, int64_t T) {
+  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, fn_hilo, c10::nullopt, c10::nullopt, cw, cw_stride,
                      c10::nullopt, c10::nullopt, c, partials, c10::nullopt, c10::nullopt, c10::nullopt, tap, T, 0, 0,
                      0);
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));
 }
 
-void hc_finish(const Tensor& X, const optional<Tensor>& mix_raw, const optional<Tensor>& scale,
+void hc_finish(const Tensor& X, const optional<Tensor>& fn_hilo, const optional<Tensor>& scale,
                const optional<Tensor>& base, const optional<Tensor>& cw, const optional<Tensor>& norm_w,
                const optional<Tensor>& mix_out, const Tensor& c, const Tensor& partials, const optional<Tensor>& u,
                const optional<Tensor>& uq, const optional<Tensor>& usf, int64_t T, int64_t iters, double hc_eps,
                double norm_eps) {
-  auto p = hc_params(X, c10::nullopt, c10::nullopt, c10::nullopt, 0, c10::nullopt, mix_raw, scale, base, cw, 24,
+  auto p = hc_params(X, c10::nullopt, c10::nullopt, c10::nullopt, 0, c10::nullopt, fn_hilo, scale, base, cw, 24,
                      norm_w, mix_out, c, partials, u, uq, usf, c10::nullopt, T, iters, hc_eps, norm_eps);
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_finish(p, cur_stream()));

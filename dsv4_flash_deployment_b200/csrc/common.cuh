@@ -1,6 +1,6 @@
 // Shared device helpers for the sm_100a kernels of this engine.
 //
-// * PTX wrappers: mbarrier, TMA (cp.async.bulk.tensor, no multicast anywhere),
+// * PTX wrappers: mbarrier, TMA tile loads (plain, each CTA loads its own tiles),
 //   1-D bulk copies, tcgen05 (alloc / mma / commit / cp / ld / fences).
 // * Bounded waits: every spin in this code base is limited by wall time read
 //   from %globaltimer.  On expiry the waiting thread records an error code in a

@@ -341,21 +341,39 @@ __global__ void __launch_bounds__(192, 1)
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");
         } else {
-          const int m = t.out_col0 + row;
-          if (m < p.m_valid) {
+          // Stage the 32 x 128 chunk in shared memory as [token][feature] and store
+          // whole 256-byte (bf16) / 512-byte (fp32) token rows with 16-byte writes.
+          constexpr int kEl = EPI == EPI_F32 ? 4 : 2;
+          uint8_t* stage = reinterpret_cast<uint8_t*>(xbuf);   // 32 x 128 x 4 B = 16 KB
 #pragma unroll
-            for (int j = 0; j < kCols; ++j) {
-              if (c0 + j < t.b_valid) {
-                const size_t o = (size_t)(t.b_row0 + c0 + j) * p.ldo + m;
-                float x = v[j];
-                if (p.row_scale) x *= __ldg(p.row_scale + t.b_row0 + c0 + j);
-                if constexpr (EPI == EPI_F32)
-                  reinterpret_cast<float*>(p.out)[o] = x;
-                else
-                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
-              }
+          for (int j = 0; j < kCols; ++j) {
+            float x = v[j];
+            if (p.row_scale && c0 + j < t.b_valid) x *= __ldg(p.row_scale + t.b_row0 + c0 + j);
+            if constexpr (EPI == EPI_F32)
+              reinterpret_cast<float*>(stage)[j * 128 + row] = x;
+            else
+              reinterpret_cast<__nv_bfloat16*>(stage)[j * 128 + row] = __float2bfloat16(x);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          constexpr int kVecPerRow = 128 * kEl / 16;   // 16 (bf16) or 32 (fp32) vectors per token row
+          const int tid = threadIdx.x - 64;
+          const bool full_m = t.out_col0 + 128 <= p.m_valid && (p.ldo * kEl) % 16 == 0;
+          for (int e = tid; e < kCols * kVecPerRow; e += 128) {
+            const int j = e / kVecPerRow, vi = e % kVecPerRow;
+            if (c0 + j >= t.b_valid) continue;
+            const size_t orow = (size_t)(t.b_row0 + c0 + j) * p.ldo;
+            const uint4 val = reinterpret_cast<const uint4*>(stage + (size_t)j * 128 * kEl)[vi];
+            if (full_m) {
+              reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (orow + t.out_col0) * kEl)[vi] = val;
+            } else {
+              const int m0 = t.out_col0 + vi * (16 / kEl);
+              const uint8_t* src = reinterpret_cast<const uint8_t*>(&val);
+              for (int b = 0; b < 16 / kEl; ++b)
+                if (m0 + b < p.m_valid)
+                  memcpy(reinterpret_cast<uint8_t*>(p.out) + (orow + m0 + b) * kEl, src + b * kEl, kEl);
             }
           }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
         }
       }
       if (!split) {

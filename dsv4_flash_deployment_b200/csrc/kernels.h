@@ -22,7 +22,7 @@ struct HcParams {
   const int* pos;                   // MoE: [T, topk] permuted row per slot (-1 = none)
   int topk;
   const float* prev_mix;            // [T, 24] (pre | post | comb) of the previous boundary
-  const float* mix_raw;             // [T, 48] projection of X' on (hi | lo) rows of hc_fn (null = no mixes)
+  const __nv_bfloat16* fn_hilo;     // [128, 4D] bf16 hi rows 0..23, lo rows 24..47 of hc_fn (null = no mixes)
   const float* scale;               // [3]
   const float* base;                // [24]
   const float* cw;                  // collapse weights: cw[t * cw_stride + i]
@@ -30,7 +30,7 @@ struct HcParams {
   const __nv_bfloat16* norm_w;      // [D]
   float* mix_out;                   // [T, 24]
   __nv_bfloat16* c;                 // scratch [T, D]
-  float* partials;                  // scratch [T, n_slices, 2]
+  float* partials;                  // scratch [T, n_slices, 50]
   __nv_bfloat16* u;                 // [T, D] normalized collapse
   uint8_t* uq;                      // [T_pad, D] e4m3 (optional)
   uint8_t* usf;                     // scale chunks of uq

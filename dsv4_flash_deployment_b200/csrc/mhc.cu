@@ -13,148 +13,265 @@
 //            from the previous boundary
 //   u      = bf16( rmsnorm(c) * norm_w ), then MXFP8-quantized for the next GEMM.
 //
-// Three launches per boundary:
-//   hc_post    (memory bound) X' and c for a (token tile, D slice), with per-slice
-//              partial sums of squares of X' and c;
-//   mixes GEMM (tensor cores, issued by the host) flat(X') [T, 4D] x fn^T where
-//              fn is stored as bf16 hi + lo rows (fn = hi + lo to 2^-16), so the
-//              fp32 projection runs on tcgen05 with split-K;
-//   hc_finish  per token: fixed-order reduction of the partials, Sinkhorn with one
-//              lane per comb entry, RMSNorm and MXFP8 quantization.
+// Two launches per boundary:
+//   hc_post    one pass over X per (16-token, 128-column) tile: X', the collapse c,
+//              sums of squares, and the tile's share of the 24-mix projection on
+//              tensor cores (mma.sync, bf16 operands, fp32 accumulate): hc_fn is
+//              stored as bf16 hi + lo rows (fn = hi + lo to 2^-16), 48 outputs;
+//   hc_finish  per token: fixed-order reduction of the per-slice partials,
+//              Sinkhorn with one lane per comb entry, RMSNorm, MXFP8 quantization.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace dsv4 {
 
 constexpr int HC = 4;
-constexpr int kSlice = 512;       // D-columns per CTA
-constexpr int kTokTile = 16;      // tokens per CTA
+constexpr int kSlice = 128;       // D-columns per CTA
+constexpr int kTokTile = 16;      // tokens per CTA (one m16 MMA tile)
+constexpr int kK = HC * kSlice;   // 512 = projection depth per CTA
+constexpr int kRowE = kK + 8;     // padded smem row (bf16 elements)
+constexpr int kNMix = 48;         // hi | lo rows of hc_fn
+constexpr int kNPart = kNMix + 2; // + sumsq(X'), sumsq(c)
 
-// 256 threads: each thread owns 2 consecutive columns of the slice.
+DSV4_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+DSV4_DEV void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 256 threads.  Thread -> (token tid/16, 8 columns (tid%16)*8 of the slice).
 __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* sFn = reinterpret_cast<__nv_bfloat16*>(smem);                 // [48][kRowE]
+  __nv_bfloat16* sX = sFn + kNMix * kRowE;                                      // [16][kRowE]
+  float* sRed = reinterpret_cast<float*>(sX + kTokTile * kRowE);                // [8 warps][16][48]
   const int slice = blockIdx.x;
   const int t0 = blockIdx.y * kTokTile;
   const int D = p.D;
-  const int d = slice * kSlice + 2 * threadIdx.x;
+  const int d0 = slice * kSlice;
+  const bool mixes = p.fn_hilo != nullptr;
   const bool has_y = p.Y != nullptr || p.yperm != nullptr;
   const bool collapse = p.cw != nullptr;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float red[8][2];
-  for (int tt = 0; tt < kTokTile; ++tt) {
-    const int t = t0 + tt;
-    if (t >= p.T) break;
-    float ssx = 0.f, ssc = 0.f;
-    if (d < D) {
-      __nv_bfloat16* xt = p.X + (size_t)t * HC * D;
-      float2 xv[HC];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (mixes) {
+    // fn slice: rows 0..47, k = i*128 + c  <-  fn_hilo[row][i*D + d0 + c]
+    for (int e = tid; e < kNMix * HC * (kSlice / 8); e += 256) {
+      const int row = e / (HC * 16), r = e % (HC * 16), i = r / 16, ch = r % 16;
+      const uint4 v = *reinterpret_cast<const uint4*>(p.fn_hilo + (size_t)row * HC * D + (size_t)i * D + d0 + ch * 8);
+      *reinterpret_cast<uint4*>(sFn + row * kRowE + i * kSlice + ch * 8) = v;
+    }
+  }
+  const int tt = tid >> 4;            // token within the tile
+  const int cc = (tid & 15) * 8;      // column offset within the slice
+  const int t = t0 + tt;
+  const int d = d0 + cc;
+  float ssx = 0.f, ssc = 0.f;
+  float xn[HC][8];
+  if (t < p.T) {
+    __nv_bfloat16* xt = p.X + (size_t)t * HC * D;
 #pragma unroll
-      for (int i = 0; i < HC; ++i) xv[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xt + (size_t)i * D + d));
-      if (has_y) {
-        float2 y;
-        if (p.yperm != nullptr) {
-          float2 acc = make_float2(0.f, 0.f);
-          for (int s = 0; s < p.topk; ++s) {
-            const int r = p.pos[(size_t)t * p.topk + s];
-            if (r >= 0) {
-              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.yperm + (size_t)r * D + d));
-              acc.x += v.x;
-              acc.y += v.y;
+    for (int i = 0; i < HC; ++i) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xt + (size_t)i * D + d);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h2[k]);
+        xn[i][2 * k] = f.x;
+        xn[i][2 * k + 1] = f.y;
+      }
+    }
+    if (has_y) {
+      float y[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] = 0.f;
+      if (p.yperm != nullptr) {
+        for (int s = 0; s < p.topk; ++s) {
+          const int r = p.pos[(size_t)t * p.topk + s];
+          if (r >= 0) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(p.yperm + (size_t)r * D + d);
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(h2[k]);
+              y[2 * k] += f.x;
+              y[2 * k + 1] += f.y;
             }
           }
-          if (p.Y) {
-            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.Y + (size_t)t * D + d));
-            acc.x += v.x;
-            acc.y += v.y;
-          }
-          y = __bfloat1622float2(__floats2bfloat162_rn(acc.x, acc.y));
-        } else {
-          y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.Y + (size_t)t * D + d));
         }
-        const float* pm = p.prev_mix + (size_t)t * 24;
-        float2 nx[HC];
+      }
+      if (p.Y != nullptr) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p.Y + (size_t)t * D + d);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-        for (int j = 0; j < HC; ++j) {
-          const float po = pm[HC + j];
-          float ax = po * y.x, ay = po * y.y;
-#pragma unroll
-          for (int i = 0; i < HC; ++i) {
-            const float cb = pm[2 * HC + i * HC + j];
-            ax += cb * xv[i].x;
-            ay += cb * xv[i].y;
-          }
-          const __nv_bfloat162 b = __floats2bfloat162_rn(ax, ay);
-          *reinterpret_cast<__nv_bfloat162*>(xt + (size_t)j * D + d) = b;
-          nx[j] = __bfloat1622float2(b);
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h2[k]);
+          y[2 * k] += f.x;
+          y[2 * k + 1] += f.y;
         }
+      }
+      if (p.yperm != nullptr) {
 #pragma unroll
-        for (int j = 0; j < HC; ++j) xv[j] = nx[j];
+        for (int k = 0; k < 8; ++k) y[k] = __bfloat162float(__float2bfloat16(y[k]));
+      }
+      const float* pm = p.prev_mix + (size_t)t * 24;
+      float nx[HC][8];
+#pragma unroll
+      for (int j = 0; j < HC; ++j) {
+        const float po = pm[HC + j];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float a = po * y[k];
+#pragma unroll
+          for (int i = 0; i < HC; ++i) a += pm[2 * HC + i * HC + j] * xn[i][k];
+          nx[j][k] = __bfloat162float(__float2bfloat16(a));
+        }
       }
 #pragma unroll
-      for (int i = 0; i < HC; ++i) ssx += xv[i].x * xv[i].x + xv[i].y * xv[i].y;
-      if (p.tap) {
-        const float mx = (xv[0].x + xv[1].x + xv[2].x + xv[3].x) * 0.25f;
-        const float my = (xv[0].y + xv[1].y + xv[2].y + xv[3].y) * 0.25f;
-        *reinterpret_cast<__nv_bfloat162*>(p.tap + (size_t)t * D + d) = __floats2bfloat162_rn(mx, my);
+      for (int j = 0; j < HC; ++j) {
+        uint4 o;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(nx[j][2 * k], nx[j][2 * k + 1]);
+        *reinterpret_cast<uint4*>(xt + (size_t)j * D + d) = o;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) xn[j][k] = nx[j][k];
       }
-      if (collapse) {
-        const float* w = p.cw + (size_t)t * p.cw_stride;
-        float cx = 0.f, cy = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < HC; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ssx += xn[i][k] * xn[i][k];
+    if (p.tap) {
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = (xn[0][2 * k] + xn[1][2 * k] + xn[2][2 * k] + xn[3][2 * k]) * 0.25f;
+        const float b = (xn[0][2 * k + 1] + xn[1][2 * k + 1] + xn[2][2 * k + 1] + xn[3][2 * k + 1]) * 0.25f;
+        o2[k] = __floats2bfloat162_rn(a, b);
+      }
+      *reinterpret_cast<uint4*>(p.tap + (size_t)t * D + d) = o;
+    }
+    if (collapse) {
+      const float* w = p.cw + (size_t)t * p.cw_stride;
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float a = 0.f, b = 0.f;
 #pragma unroll
         for (int i = 0; i < HC; ++i) {
-          cx += w[i] * xv[i].x;
-          cy += w[i] * xv[i].y;
+          a += w[i] * xn[i][2 * k];
+          b += w[i] * xn[i][2 * k + 1];
         }
-        const __nv_bfloat162 cb = __floats2bfloat162_rn(cx, cy);
-        *reinterpret_cast<__nv_bfloat162*>(p.c + (size_t)t * D + d) = cb;
-        const float2 cf = __bfloat1622float2(cb);
-        ssc = cf.x * cf.x + cf.y * cf.y;
+        o2[k] = __floats2bfloat162_rn(a, b);
+        const float2 f = __bfloat1622float2(o2[k]);
+        ssc += f.x * f.x + f.y * f.y;
       }
+      *reinterpret_cast<uint4*>(p.c + (size_t)t * D + d) = o;
     }
-    if (p.partials != nullptr) {
-      ssx = warp_sum(ssx);
-      ssc = warp_sum(ssc);
-      if (lane == 0) {
-        red[warp][0] = ssx;
-        red[warp][1] = ssc;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float a = 0.f, b = 0.f;
-        for (int w = 0; w < 8; ++w) {
-          a += red[w][0];
-          b += red[w][1];
-        }
-        float* dst = p.partials + ((size_t)t * n_slices + slice) * 2;
-        dst[0] = a;
-        dst[1] = b;
-      }
-      __syncthreads();
+  } else {
+#pragma unroll
+    for (int i = 0; i < HC; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) xn[i][k] = 0.f;
+  }
+  // per-token sums of squares: the 16 threads of a token are 16 consecutive lanes
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    ssx += __shfl_xor_sync(0xffffffffu, ssx, o);
+    ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
+  }
+  float* part = p.partials;
+  if (t < p.T && (tid & 15) == 0) {
+    part[((size_t)t * n_slices + slice) * kNPart + kNMix] = ssx;
+    part[((size_t)t * n_slices + slice) * kNPart + kNMix + 1] = ssc;
+  }
+  if (!mixes) return;
+  // X' tile into shared memory as the A operand [16 tokens][k = i*128 + c]
+#pragma unroll
+  for (int i = 0; i < HC; ++i) {
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(xn[i][2 * k], xn[i][2 * k + 1]);
+    *reinterpret_cast<uint4*>(sX + tt * kRowE + i * kSlice + cc) = o;
+  }
+  __syncthreads();
+  // [16 x 512] x [512 x 48]: warp w takes k in [64w, 64w+64), all six n8 tiles
+  float acc[6][4];
+#pragma unroll
+  for (int n = 0; n < 6; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const int k0 = warp * 64 + ks * 16;
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4(smem_u32(sX + ((lane & 7) + 8 * ((lane >> 3) & 1)) * kRowE + k0 + 8 * (lane >> 4)), a0, a1, a2, a3);
+#pragma unroll
+    for (int n = 0; n < 6; ++n) {
+      uint32_t b0, b1;
+      ldsm_x2(smem_u32(sFn + (n * 8 + (lane & 7)) * kRowE + k0 + 8 * ((lane >> 3) & 1)), b0, b1);
+      mma16816(acc[n], a0, a1, a2, a3, b0, b1);
     }
+  }
+  const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+  for (int n = 0; n < 6; ++n) {
+    sRed[(warp * 16 + g) * kNMix + n * 8 + 2 * cq] = acc[n][0];
+    sRed[(warp * 16 + g) * kNMix + n * 8 + 2 * cq + 1] = acc[n][1];
+    sRed[(warp * 16 + g + 8) * kNMix + n * 8 + 2 * cq] = acc[n][2];
+    sRed[(warp * 16 + g + 8) * kNMix + n * 8 + 2 * cq + 1] = acc[n][3];
+  }
+  __syncthreads();
+  for (int e = tid; e < kTokTile * kNMix; e += 256) {
+    const int r = e / kNMix, c = e % kNMix;
+    if (t0 + r >= p.T) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += sRed[(w * 16 + r) * kNMix + c];
+    part[((size_t)(t0 + r) * n_slices + slice) * kNPart + c] = v;
   }
 }
 
-// One warp per token.  mix_raw: [T, 48] = (hi | lo) halves of the projection.
+// One warp per token.  Partials per slice: 48 projections (hi | lo rows of
+// hc_fn), sumsq(X'), sumsq(c); reduced here in slice order.
 __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + warp;
   if (t >= p.T) return;
   const int D = p.D;
-  float ssx = 0.f, ssc = 0.f;
-  for (int s = lane; s < n_slices; s += 32) {
-    ssx += p.partials[((size_t)t * n_slices + s) * 2];
-    ssc += p.partials[((size_t)t * n_slices + s) * 2 + 1];
+  const float* part = p.partials + (size_t)t * n_slices * kNPart;
+  float r0 = 0.f, r1 = 0.f;   // lane: columns lane and 32 + lane (< 50)
+  for (int s = 0; s < n_slices; ++s) {
+    r0 += part[s * kNPart + lane];
+    if (lane + 32 < kNPart) r1 += part[s * kNPart + 32 + lane];
   }
-  ssx = warp_sum(ssx);
-  ssc = warp_sum(ssc);
-  if (p.mix_raw != nullptr) {
+  const float ssx = __shfl_sync(0xffffffffu, r1, kNMix - 32);
+  const float ssc = __shfl_sync(0xffffffffu, r1, kNMix + 1 - 32);
+  if (p.fn_hilo != nullptr) {
     // lanes 0-3 pre, 4-7 post, 16-31 comb[i][j] with i = (lane-16)/4, j = lane%4
     const int idx = lane < 8 ? lane : (lane >= 16 ? 8 + lane - 16 : -1);
     const float r = rsqrtf(ssx / (float)(HC * D) + p.norm_eps);
+    // projection m = hi[m] + lo[m] = column m + column 24 + m
+    const float hi_lo0 = __shfl_sync(0xffffffffu, r0, idx < 0 ? 0 : idx);          // hi rows 0..23 live in r0
+    const int lo_col = 24 + (idx < 0 ? 0 : idx);                                    // 24..47
+    const float lo_a = __shfl_sync(0xffffffffu, r0, lo_col & 31);
+    const float lo_b = __shfl_sync(0xffffffffu, r1, lo_col & 31);
+    const float lo = lo_col < 32 ? lo_a : lo_b;
     float v = 0.f;
-    if (idx >= 0) {
-      const float* raw = p.mix_raw + (size_t)t * 48;
-      v = (raw[idx] + raw[24 + idx]) * r * p.scale[idx < HC ? 0 : (idx < 2 * HC ? 1 : 2)] + p.base[idx];
-    }
+    if (idx >= 0) v = (hi_lo0 + lo) * r * p.scale[idx < HC ? 0 : (idx < 2 * HC ? 1 : 2)] + p.base[idx];
     float outv = 0.f;
     if (lane < HC) outv = 1.f / (1.f + expf(-v)) + p.hc_eps;
     else if (lane < 2 * HC) outv = 2.f / (1.f + expf(-v));
@@ -226,9 +343,17 @@ int hc_num_slices(int D) { return (D + kSlice - 1) / kSlice; }
 
 cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
+  if (p.D % kSlice) return cudaErrorInvalidValue;
   const int ns = hc_num_slices(p.D);
+  const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2 + (size_t)8 * kTokTile * kNMix * 4;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(hc_post_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
   dim3 g(ns, (p.T + kTokTile - 1) / kTokTile);
-  hc_post_kernel<<<g, 256, 0, st>>>(p, ns);
+  hc_post_kernel<<<g, 256, smem, st>>>(p, ns);
   return cudaGetLastError();
 }
 

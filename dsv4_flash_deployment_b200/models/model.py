@@ -140,7 +140,7 @@ class DSV4Model:
         z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=dev)
         self.X = e(T, cfg.hc_mult, D)
         self.hc_c = e(T, D)
-        self.hc_part = e(T * self.ext.hc_num_slices(D) * 2, dt=f32)
+        self.hc_part = e(T * self.ext.hc_num_slices(D) * 50, dt=f32)
         self.mix_raw = e(T, 48, dt=f32)
         self.mixA, self.mixF = z(T, 24, dt=f32), z(T, 24, dt=f32)
         init = torch.zeros(T, 24, dtype=f32, device=dev)
@@ -328,16 +328,14 @@ class DSV4Model:
 
     def _hc(self, T, Y=None, yperm=None, pos=None, topk=0, prev=None, mixes=None, cw=None, norm=None,
             mix_out=None, u=None, uq=None, usf=None, tap=None):
-        """One mHC boundary: post/combine/collapse, tensor-core mixes, Sinkhorn + norm + quant."""
+        """One mHC boundary: post/combine/collapse + tensor-core mixes, then Sinkhorn + norm + quant."""
         cfg, ext = self.cfg, self.ext
-        ext.hc_post(self.X, Y, yperm, pos, topk, prev, cw, 24, self.hc_c, self.hc_part, tap, T)
-        mix_raw = scale = base = None
+        fnhl = scale = base = None
         if mixes is not None:
             fnhl, scale, base = mixes
-            self._gemm_bf16(self.X.view(self.X.shape[0], -1), fnhl, self.mix_raw, T, f32_out=True, m_valid=48)
-            mix_raw = self.mix_raw
+        ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T)
         if mixes is not None or (cw is not None and u is not None):
-            ext.hc_finish(self.X, mix_raw, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
+            ext.hc_finish(self.X, fnhl, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
                           self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
 
     sinkhorn_iters = None

@@ -95,11 +95,13 @@ def quantize(x: torch.Tensor, q_out: torch.Tensor | None = None, sf_out: torch.T
 
 
 def pick_bn(n_tokens: int) -> int:
+    """Token-tile width: the smallest covering tile for small batches, 128 (two TMEM
+    accumulators, epilogue overlapped) up to 2048 tokens, 256 beyond."""
     if n_tokens <= 32:
         return 32
     if n_tokens <= 64:
         return 64
-    if n_tokens <= 128:
+    if n_tokens <= 2048:
         return 128
     return 256
 

@@ -76,19 +76,25 @@ class EPGroup:
         b = self._bufs
         cap, rec = b["cap"], b["rec"]
         ids, wts, _, _ = model.route[k]
-        b["cnt"].zero_()
-        ext.ep_pack(ids, wts, T, model.uq, model.usf, e_local, self.world, cap, rec, b["send"], b["cnt"],
-                    b["pos_back"], None, self.rank, model.err)
-        dist.all_to_all_single(b["rcnt"], b["cnt"], group=self.group)
-        dist.all_to_all_single(b["recv"], b["send"], group=self.group)
+        with model._t("ep_pack"):
+            b["cnt"].zero_()
+            ext.ep_pack(ids, wts, T, model.uq, model.usf, e_local, self.world, cap, rec, b["send"], b["cnt"],
+                        b["pos_back"], None, self.rank, model.err)
+        with model._t("ep_exchange"):
+            dist.all_to_all_single(b["rcnt"], b["cnt"], group=self.group)
+            dist.all_to_all_single(b["recv"], b["send"], group=self.group)
         n = self.world * cap
-        ext.ep_unpack_meta(b["recv"], b["rcnt"], self.world, cap, rec, D, b["ids"], b["wts"])
-        ext.moe_plan(n, 1, e_local, 0, b["ids"], b["wts"], model.counts, model.seg, b["rank"], model.tile_rows,
-                     2 * I, D, model.tiles13, model.nt13, model.tiles2, model.nt2, model.cap, b["pos"],
-                     model.row_scale, model.err)
-        ext.ep_unpack_rows(b["recv"], n, rec, D, b["pos"], model.xperm, model.xperm_sf)
+        with model._t("ep_plan_unpack"):
+            ext.ep_unpack_meta(b["recv"], b["rcnt"], self.world, cap, rec, D, b["ids"], b["wts"])
+            ext.moe_plan(n, 1, e_local, 0, b["ids"], b["wts"], model.counts, model.seg, b["rank"], model.tile_rows,
+                         2 * I, D, model.tiles13, model.nt13, model.tiles2, model.nt2, model.cap, b["pos"],
+                         model.row_scale, model.err)
+            ext.ep_unpack_rows(b["recv"], n, rec, D, b["pos"], model.xperm, model.xperm_sf)
         model._grouped(L, 1)
-        ext.ep_combine_pack(model.yperm, b["pos"], n, cap, b["back_send"], None, self.rank)
-        dist.all_to_all_single(b["back_recv"], b["back_send"], group=self.group)
-        model._shared_expert(L, T)
+        with model._t("ep_combine"):
+            ext.ep_combine_pack(model.yperm, b["pos"], n, cap, b["back_send"], None, self.rank)
+        with model._t("ep_exchange"):
+            dist.all_to_all_single(b["back_recv"], b["back_send"], group=self.group)
+        with model._t("shared_expert"):
+            model._shared_expert(L, T)
         return b["back_recv"], b["pos_back"], k
