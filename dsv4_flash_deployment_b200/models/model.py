@@ -23,6 +23,7 @@ dispatch/combine exchange of :mod:`..parallel.ep`.
 from __future__ import annotations
 
 import contextlib
+import itertools
 import math
 from dataclasses import dataclass
 
@@ -54,48 +55,33 @@ class StepMeta:
     def __init__(self, cfg, chunks: list[SeqChunk], ring_pad_slot: int | None = None):
         self.cfg = cfg
         self.chunks = chunks
-        ids, pos, slot, cstart, row0, last, sample = [], [], [], [], [], [], []
-        for c in chunks:
-            r0 = len(ids)
-            n = len(c.tokens)
-            for j, tok in enumerate(c.tokens):
-                ids.append(tok)
-                pos.append(c.start_pos + j)
-                slot.append(c.slot)
-                cstart.append(c.start_pos)
-                row0.append(r0)
-                last.append(c.start_pos + n - 1)
-            if c.sample:
-                sample.append(r0 + n - 1)
-        self.T = len(ids)
-        self.ids = np.asarray(ids, np.int32)
-        self.pos = np.asarray(pos, np.int32)
-        self.slot = np.asarray(slot, np.int32)
-        self.chunk_start = np.asarray(cstart, np.int32)
-        self.step_row0 = np.asarray(row0, np.int32)
-        self.last_pos = np.asarray(last, np.int32)
-        self.sample_rows = np.asarray(sample, np.int32)
-        self.max_pos = int(self.pos.max()) if self.T else 0
-        # compressor groups closed in this step, per ratio
+        n = len(chunks)
+        lens = np.fromiter((len(c.tokens) for c in chunks), np.int64, n)
+        starts = np.fromiter((c.start_pos for c in chunks), np.int64, n)
+        slots = np.fromiter((c.slot for c in chunks), np.int64, n)
+        samp = np.fromiter((c.sample for c in chunks), bool, n)
+        row0 = np.zeros(n, np.int64)
+        if n:
+            row0[1:] = np.cumsum(lens)[:-1]
+        T = int(lens.sum())
+        self.T = T
+        self.ids = np.fromiter(itertools.chain.from_iterable(c.tokens for c in chunks), np.int32, T)
+        offs = np.arange(T, dtype=np.int64) - np.repeat(row0, lens)
+        self.pos = (np.repeat(starts, lens) + offs).astype(np.int32)
+        self.slot = np.repeat(slots, lens).astype(np.int32)
+        self.chunk_start = np.repeat(starts, lens).astype(np.int32)
+        self.step_row0 = np.repeat(row0, lens).astype(np.int32)
+        self.last_pos = np.repeat(starts + lens - 1, lens).astype(np.int32)
+        self.sample_rows = (row0 + lens - 1)[samp].astype(np.int32)
+        self.max_pos = int(self.pos.max()) if T else 0
+        # compressor groups closed in this step, per ratio (token order)
         self.groups = {}
         for r in sorted({cfg.ratio(l) for l in cfg.kv_source_layer_ids}):
-            gs, gi, gc, gr = [], [], [], []
-            for c, r0 in zip(chunks, self._row0s()):
-                for p in range(c.start_pos, c.start_pos + len(c.tokens)):
-                    if (p + 1) % r == 0:
-                        gs.append(c.slot)
-                        gi.append(p // r)
-                        gc.append(c.start_pos)
-                        gr.append(r0)
-            self.groups[r] = tuple(np.asarray(a, np.int32) for a in (gs, gi, gc, gr))
+            mask = (self.pos + 1) % r == 0
+            self.groups[r] = (self.slot[mask], (self.pos[mask] // r).astype(np.int32), self.chunk_start[mask],
+                              self.step_row0[mask])
         self.clen = {r: ((self.pos + 1) // r).astype(np.int32) for r in self.groups}
-
-    def _row0s(self):
-        out, acc = [], 0
-        for c in self.chunks:
-            out.append(acc)
-            acc += len(c.tokens)
-        return out
+        self._lens = lens
 
     def index_bypass(self, r: int) -> bool:
         """True when every token's compressed length <= index_topk: top-k selects all."""
@@ -103,7 +89,7 @@ class StepMeta:
 
     def key(self):
         """Graph key: shapes and control flow of the step."""
-        return (self.T, len(self.sample_rows), tuple(len(c.tokens) for c in self.chunks),
+        return (self.T, len(self.sample_rows), self._lens.tobytes(),
                 tuple(self.index_bypass(r) for r in self.groups))
 
 
@@ -459,7 +445,7 @@ class DSV4Model:
         g = self.m_groups[r]
         cos, sin = self.rope["yarn"]
         # grid covers every token that could close a group; the kernel reads the real count
-        max_groups = min(T, sum(len(c.tokens) // r + 1 for c in m.chunks))
+        max_groups = min(T, int((m._lens // r + 1).sum()))
         if max_groups:
             ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
                               self.comp_ring[lid],
