@@ -306,6 +306,8 @@ def v4_flash_config(**overrides: Any) -> ModelConfig:
         n_routed_experts=256, n_activated_experts=8, n_shared_experts=1, moe_inter_dim=2048,
         route_scale=1.5, score_func="sqrtsoftplus", expert_format="mxfp8",
         engram_layer_ids=(), engram_num_embeddings=(), dspark_target_layer_ids=(),
+        # the "reference" K-read quirk belongs to the V4.1 oracle; V4 indexers read their own K
+        index_k_mode="intended",
     )
     d.update(overrides)
     cfg = ModelConfig(**d)
@@ -328,7 +330,7 @@ def toy_v4_config(**overrides: Any) -> ModelConfig:
         index_n_heads=4, index_head_dim=32, index_topk=64,
         n_routed_experts=8, n_activated_experts=2, n_shared_experts=1, moe_inter_dim=128,
         route_scale=1.0, score_func="sigmoid", expert_format="mxfp8",
-        engram_layer_ids=(), engram_num_embeddings=(), dspark_target_layer_ids=(),
+        engram_layer_ids=(), engram_num_embeddings=(), dspark_target_layer_ids=(), index_k_mode="intended",
     )
     d.update(overrides)
     return ModelConfig(**d)

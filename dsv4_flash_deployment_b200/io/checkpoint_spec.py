@@ -139,15 +139,29 @@ def _seed_for(seed: int, name: str) -> int:
 
 
 def random_tensor(name: str, tag: str, shape: tuple[int, ...], seed: int = 0,
-                  device: str | torch.device = "cpu", mxfp4_experts: bool = False) -> torch.Tensor:
+                  device: str | torch.device = "cpu", mxfp4_experts: bool = False,
+                  init_std: float | None = None) -> torch.Tensor:
     """One deterministic random tensor for checkpoint entry ``name``.
 
-    Scales are powers of two near 2^-7 so block-scaled weights have unit-ish
-    gain per sqrt(fan-in); BF16 matrices are N(0, 1/fan_in); norm weights ~1.
+    Default: scales are powers of two near 2^-7 so block-scaled weights have
+    unit-ish gain per sqrt(fan-in); BF16 matrices are N(0, 1/fan_in); norm
+    weights ~1.  With ``init_std`` every weight matrix dequantizes to
+    ~N(0, init_std) (FP8 codes ~N(0, init_std * 32) under a 2^-5 scale), norm
+    weights are 1 and mHC parameters keep their defaults.
     """
     g = torch.Generator(device=device)
     g.manual_seed(_seed_for(seed, name))
     dev = torch.device(device)
+    if init_std is not None and tag in (E8, F8, BF16):
+        if tag == E8:
+            return torch.full(shape, 122, dtype=torch.uint8, device=dev)
+        if tag == F8:
+            v = (torch.randn(shape, generator=g, device=dev) * (init_std * 32.0)).to(torch.float8_e4m3fn)
+            v.view(torch.uint8)[v.view(torch.uint8) == 0x80] = 0
+            return v
+        if name.endswith("norm.weight"):
+            return torch.ones(shape, dtype=torch.bfloat16, device=dev)
+        return (torch.randn(shape, generator=g, device=dev) * init_std).to(torch.bfloat16)
     if tag == E8:
         # MXFP4 expert codes span +-6 (vs ~N(0, 0.5) for e4m3 values): their scales sit
         # 3 binades lower so both expert formats have the same weight magnitude.
@@ -182,8 +196,9 @@ def random_tensor(name: str, tag: str, shape: tuple[int, ...], seed: int = 0,
 
 
 def make_random_weights(cfg, seed: int = 0, device: str | torch.device = "cpu",
-                        names: Iterable[str] | None = None, include_mtp: bool = True) -> dict[str, torch.Tensor]:
+                        names: Iterable[str] | None = None, include_mtp: bool = True,
+                        init_std: float | None = None) -> dict[str, torch.Tensor]:
     specs = checkpoint_specs(cfg, include_mtp=include_mtp)
     keys = list(specs) if names is None else list(names)
     mx4 = cfg.expert_format == "mxfp4"
-    return {k: random_tensor(k, specs[k][0], specs[k][1], seed, device, mx4) for k in keys}
+    return {k: random_tensor(k, specs[k][0], specs[k][1], seed, device, mx4, init_std) for k in keys}
