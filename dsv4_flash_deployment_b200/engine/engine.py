@@ -45,10 +45,13 @@ class Engine:
     @classmethod
     def build(cls, cfg, device="cuda", max_seqs: int = 16, max_batched_tokens: int = 512, max_seq_len: int = 2048,
               weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None, ep=None,
-              use_graphs: bool = True, chunk_size: int | None = None) -> "Engine":
+              use_graphs: bool = True, chunk_size: int | None = None, extra_slots: int = 0) -> "Engine":
+        """``extra_slots`` cache slots beyond ``max_seqs`` are kept out of the scheduler
+        (the multi-rank control plane runs its 1-token join steps on one)."""
         from .builder import build_model
-        model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs, max_seq_len=max_seq_len,
-                            weights=weights, seed=seed, expert_storage_layers=expert_storage_layers, ep=ep)
+        model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs + extra_slots,
+                            max_seq_len=max_seq_len, weights=weights, seed=seed,
+                            expert_storage_layers=expert_storage_layers, ep=ep)
         return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs)
 
     # ------------------------------------------------------------------- API
@@ -78,6 +81,7 @@ class Engine:
             host = out
         self.stats["steps"] += 1
         self.stats["tokens"] += meta.T
+        self.stats["last_T"] = meta.T
         return [int(x) for x in host.tolist()]
 
     def _run_device(self, meta: StepMeta) -> torch.Tensor:

@@ -95,6 +95,8 @@ class Scheduler:
         # drop cancelled requests
         for r in [r for r in self.running if r.cancelled]:
             self._finish(r, "cancelled")
+        for r in [r for r in self.waiting if r.cancelled]:
+            self._finish(r, "cancelled")
         self.waiting = deque(r for r in self.waiting if not r.cancelled)
         out: list[ScheduledChunk] = []
         budget = self.budget

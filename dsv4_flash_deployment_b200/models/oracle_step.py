@@ -1,0 +1,48 @@
+"""CPU step model on the oracle, with the step interface of :class:`.model.DSV4Model`.
+
+The serving engine drives a model through three members: ``cfg``, ``dev`` and
+``forward(meta) -> sampled ids`` (plus ``upload``).  This class gives the
+engine, the scheduler, the HTTP server and the multi-rank control plane a
+model that runs anywhere (tests, a laptop, gloo ranks) with the oracle's
+exact numerics: every slot owns a :class:`..ref.model.RefState`; a chunk is
+stepped token by token; a sampled chunk returns the greedy argmax of its last
+token.  It is a test and plumbing backend, not a serving path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..ref.model import RefModel, RefState
+from .model import StepMeta
+
+
+class OracleStepModel:
+    def __init__(self, cfg, weights: dict[str, torch.Tensor], n_slots: int, max_seq_len: int,
+                 ref: RefModel | None = None):
+        self.cfg = cfg
+        self.dev = torch.device("cpu")
+        self.ref = ref or RefModel(cfg, weights, max_seq_len=max_seq_len)
+        self.states: list[RefState | None] = [None] * n_slots
+        self.last_upload_bytes = 0
+
+    def upload(self, meta: StepMeta, pinned: dict | None = None) -> None:
+        self.last_upload_bytes = 0
+
+    def forward(self, meta: StepMeta) -> torch.Tensor:
+        out = []
+        for c in meta.chunks:
+            st = self.states[c.slot]
+            if c.start_pos == 0 or st is None:
+                if c.start_pos != 0:
+                    raise RuntimeError(f"slot {c.slot}: chunk at {c.start_pos} without a prefix")
+                st = self.ref.new_state(1)
+                self.states[c.slot] = st
+            if st.pos != c.start_pos:
+                raise RuntimeError(f"slot {c.slot}: state at {st.pos}, chunk starts at {c.start_pos}")
+            logits = None
+            for tok in c.tokens:
+                logits, _ = self.ref.step(torch.tensor([tok]), st)
+            if c.sample:
+                out.append(int(logits[0].argmax()))
+        return torch.tensor(out, dtype=torch.int32)

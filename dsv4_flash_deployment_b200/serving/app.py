@@ -1,0 +1,219 @@
+"""OpenAI-compatible HTTP server.
+
+Endpoints (the union of the reference's ``tpu-v7x/deepseek_v41/server.py``
+and what its sweep client asks of vLLM, ``kernel-optimizations-recipe/
+scripts/benchmark_sweep.py:70-125``):
+
+  GET  /health                 status, model, device, totals (503 when the engine is unhealthy)
+  GET  /v1/models              the served model id
+  GET  /metrics                Prometheus text: requests, tokens, step time, batch, TTFT, slots
+  POST /tokenize               {"prompt"} or {"messages"} -> {"count", "tokens", "max_model_len"}
+  POST /detokenize             {"tokens"} -> {"prompt"}
+  POST /v1/completions         prompt (text | ids | [text]), max_tokens, stream, ignore_eos, stop
+  POST /v1/chat/completions    messages, max_tokens / max_completion_tokens, stream, stop
+
+Decoding is greedy (``temperature`` is accepted and reported; the engine
+samples argmax, as every reference benchmark does at temperature 0).
+Streaming sends one SSE event per generated token and ends with
+``data: [DONE]``; a client that disconnects cancels its request.
+
+Run: ``python -m dsv4_flash_deployment_b200.serving --config v4-flash --port 8000``.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import json
+import time
+import uuid
+
+from aiohttp import web
+
+from .engine_loop import EngineLoop, GenParams
+
+
+class ServerState:
+    def __init__(self, loop: EngineLoop, tokenizer, model_name: str, max_model_len: int, info: dict | None = None):
+        self.loop = loop
+        self.tok = tokenizer
+        self.model_name = model_name
+        self.max_model_len = max_model_len
+        self.info = info or {}
+        self.t_start = time.time()
+
+
+def _prompt_ids(st: ServerState, body: dict, chat: bool) -> list[int]:
+    if chat:
+        text = st.tok.apply_chat_template(body.get("messages") or [])
+        return st.tok.encode(text, add_bos=True)
+    p = body.get("prompt", "")
+    if isinstance(p, list):
+        if p and all(isinstance(t, int) for t in p):
+            return [int(t) for t in p]
+        if len(p) != 1:
+            raise web.HTTPBadRequest(text=json.dumps({"error": "batched prompts: send one prompt per request"}),
+                                     content_type="application/json")
+        p = p[0]
+    return st.tok.encode(str(p), add_bos=True)
+
+
+def _params(st: ServerState, body: dict, n_prompt: int) -> tuple[GenParams, list[str]]:
+    mt = body.get("max_completion_tokens") or body.get("max_tokens") or body.get("max_new_tokens") or 256
+    mt = int(mt)
+    if mt < 1:
+        raise web.HTTPBadRequest(text=json.dumps({"error": "max_tokens must be >= 1"}), content_type="application/json")
+    if n_prompt + mt > st.max_model_len:
+        raise web.HTTPBadRequest(
+            text=json.dumps({"error": f"prompt ({n_prompt}) + max_tokens ({mt}) exceeds max_model_len "
+                                      f"({st.max_model_len})"}), content_type="application/json")
+    stop = body.get("stop") or []
+    if isinstance(stop, str):
+        stop = [stop]
+    stop_ids = tuple(int(t) for t in (body.get("stop_token_ids") or []))
+    return GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids), [s for s in stop if s]
+
+
+def _err(code: int, msg: str) -> web.Response:
+    return web.json_response({"error": {"message": msg, "code": code}}, status=code)
+
+
+async def _generate(st: ServerState, request: web.Request, chat: bool):
+    try:
+        body = await request.json()
+    except Exception as e:  # noqa: BLE001
+        return _err(400, f"invalid JSON: {e}")
+    try:
+        ids = _prompt_ids(st, body, chat)
+        params, stops = _params(st, body, len(ids))
+    except web.HTTPBadRequest as e:
+        return web.Response(status=400, text=e.text, content_type="application/json")
+    if not st.loop.healthy:
+        return _err(503, f"engine unhealthy: {st.loop.error}")
+    stream = bool(body.get("stream", False))
+    rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:16]
+    created = int(time.time())
+    ts = st.loop.submit(ids, params)
+    out_ids: list[int] = []
+    text = ""
+    finish = None
+
+    def chunk_obj(piece: str | None, fin: str | None) -> dict:
+        if chat:
+            delta = {} if piece is None else {"content": piece}
+            if piece is not None and not out_ids[:-1]:
+                delta["role"] = "assistant"
+            return {"id": rid, "object": "chat.completion.chunk", "created": created, "model": st.model_name,
+                    "choices": [{"index": 0, "delta": delta, "finish_reason": fin}]}
+        return {"id": rid, "object": "text_completion", "created": created, "model": st.model_name,
+                "choices": [{"index": 0, "text": piece or "", "finish_reason": fin, "logprobs": None}]}
+
+    resp = None
+    if stream:
+        resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
+        await resp.prepare(request)
+    try:
+        while True:
+            kind, val = await ts.q.get()
+            if kind == "error":
+                if resp is None:
+                    return _err(500 if ts.req is not None else 400, val)
+                await resp.write(f"data: {json.dumps({'error': {'message': val}})}\n\n".encode())
+                finish = "error"
+                break
+            if kind == "done":
+                finish = "stop" if val == "stop" else ("length" if val == "length" else val)
+                break
+            tok = int(val)
+            out_ids.append(tok)
+            if tok == st.tok.eos_token_id and not params.ignore_eos:
+                continue
+            piece = st.tok.decode_token(tok)
+            if stops:
+                cand = text + piece
+                hit = min((cand.find(s) for s in stops if s in cand), default=-1)
+                if hit >= 0:
+                    piece = cand[:hit][len(text):]
+                    text = cand[:hit]
+                    st.loop.cancel(ts)
+                    if resp is not None and piece:
+                        await resp.write(f"data: {json.dumps(chunk_obj(piece, None))}\n\n".encode())
+                    finish = "stop"
+                    # drain until the engine confirms the cancel
+                    while True:
+                        k2, _ = await ts.q.get()
+                        if k2 in ("done", "error"):
+                            break
+                    break
+            text += piece
+            if resp is not None:
+                await resp.write(f"data: {json.dumps(chunk_obj(piece, None))}\n\n".encode())
+    except (asyncio.CancelledError, ConnectionResetError):
+        st.loop.cancel(ts)
+        raise
+    usage = {"prompt_tokens": len(ids), "completion_tokens": len(out_ids), "total_tokens": len(ids) + len(out_ids)}
+    if resp is not None:
+        last = chunk_obj(None, finish)
+        last["usage"] = usage
+        await resp.write(f"data: {json.dumps(last)}\n\n".encode())
+        await resp.write(b"data: [DONE]\n\n")
+        await resp.write_eof()
+        return resp
+    if chat:
+        choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish}
+        obj = "chat.completion"
+    else:
+        choice = {"index": 0, "text": text, "finish_reason": finish, "logprobs": None}
+        obj = "text_completion"
+    req = ts.req
+    metrics = {"ttft_s": (req.t_first_token - req.t_arrival) if req and req.t_first_token else None,
+               "e2e_s": (req.t_done - req.t_arrival) if req and req.t_done else None}
+    return web.json_response({"id": rid, "object": obj, "created": created, "model": st.model_name,
+                              "choices": [choice], "usage": usage, "x_metrics": metrics})
+
+
+def build_app(st: ServerState) -> web.Application:
+    app = web.Application(client_max_size=64 * 1024 * 1024)
+
+    async def health(_):
+        lp = st.loop
+        body = {"status": "ok" if lp.healthy else "unhealthy", "error": lp.error, "model": st.model_name,
+                "uptime_s": time.time() - st.t_start, "live_requests": lp.n_live,
+                "total_requests": lp.stats["requests"], "total_generated_tokens": lp.stats["generated_tokens"],
+                **st.info}
+        return web.json_response(body, status=200 if lp.healthy else 503)
+
+    async def models(_):
+        return web.json_response({"object": "list", "data": [
+            {"id": st.model_name, "object": "model", "created": int(st.t_start), "owned_by": "dsv4-b200",
+             "max_model_len": st.max_model_len}]})
+
+    async def tokenize(request):
+        body = await request.json()
+        if "messages" in body:
+            ids = st.tok.encode(st.tok.apply_chat_template(body["messages"]), add_bos=True)
+        else:
+            ids = st.tok.encode(str(body.get("prompt", "")), add_bos=bool(body.get("add_special_tokens", True)))
+        return web.json_response({"count": len(ids), "tokens": ids, "max_model_len": st.max_model_len})
+
+    async def detokenize(request):
+        body = await request.json()
+        return web.json_response({"prompt": st.tok.decode([int(t) for t in body.get("tokens", [])])})
+
+    async def metrics(_):
+        from .metrics import render_prometheus
+        return web.Response(text=render_prometheus(st), content_type="text/plain", charset="utf-8")
+
+    async def completions(request):
+        return await _generate(st, request, chat=False)
+
+    async def chat(request):
+        return await _generate(st, request, chat=True)
+
+    app.router.add_get("/health", health)
+    app.router.add_get("/v1/models", models)
+    app.router.add_get("/metrics", metrics)
+    app.router.add_post("/tokenize", tokenize)
+    app.router.add_post("/detokenize", detokenize)
+    app.router.add_post("/v1/completions", completions)
+    app.router.add_post("/v1/chat/completions", chat)
+    return app

@@ -1,0 +1,91 @@
+"""Builds the engine from an :class:`..engine.config.EngineConfig` and serves it.
+
+Rank 0 runs the HTTP server and the engine thread; other ranks follow the
+control plane (:func:`..engine.dist_engine.worker_loop`).
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..engine.config import EngineConfig
+
+
+def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0):
+    from ..engine.engine import Engine
+
+    cfg = ec.model_config()
+    if ec.device == "cpu":
+        from ..io.checkpoint_spec import make_random_weights
+        from ..models.oracle_step import OracleStepModel
+
+        w = _load_weights(ec, cfg) or make_random_weights(cfg, seed=ec.seed, include_mtp=False)
+        model = OracleStepModel(cfg, w, n_slots=ec.max_seqs + extra_slots, max_seq_len=ec.max_model_len)
+        return Engine(model, ec.max_seqs, ec.max_batched_tokens, ec.max_model_len, ec.chunk_size, use_graphs=False)
+    return Engine.build(cfg, device=ec.device, max_seqs=ec.max_seqs, max_batched_tokens=ec.max_batched_tokens,
+                        max_seq_len=ec.max_model_len, weights=_load_weights(ec, cfg), seed=ec.seed,
+                        expert_storage_layers=ec.expert_storage_layers, ep=ep, use_graphs=ec.use_cuda_graphs,
+                        chunk_size=ec.chunk_size, extra_slots=extra_slots)
+
+
+def _load_weights(ec: EngineConfig, cfg):
+    if ec.checkpoint is None:
+        return None
+    from ..io.safetensors import load_checkpoint
+    return load_checkpoint(ec.checkpoint, cfg)
+
+
+def init_distributed(ec: EngineConfig):
+    """(rank, world, ep, cpu_group) from torchrun's environment; world 1 without it."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1:
+        return 0, 1, None, None
+    rank = int(os.environ["RANK"])
+    if ec.device == "cpu":
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        return rank, world, None, dist.group.WORLD
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                            timeout=datetime.timedelta(seconds=300))
+    cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
+    from ..parallel.ep import EPGroup
+    ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), transport=ec.ep_transport)
+    return rank, world, ep, cpu_group
+
+
+def main(argv: list[str] | None = None) -> None:
+    from aiohttp import web
+
+    from ..engine.dist_engine import DistributedEngine, worker_loop
+    from .app import ServerState, build_app
+    from .engine_loop import EngineLoop
+    from .tokenizer import load_tokenizer
+
+    ec = EngineConfig.from_args(argv)
+    rank, world, ep, cpu_group = init_distributed(ec)
+    if ec.device == "cuda" and world == 1:
+        torch.cuda.set_device(0)
+    local = build_local_engine(ec, ep, extra_slots=1 if world > 1 else 0)
+    if rank != 0:
+        worker_loop(local, cpu_group)
+        dist.destroy_process_group()
+        return
+    eng = DistributedEngine(local, cpu_group) if world > 1 else local
+    loop = EngineLoop(eng, step_deadline_s=ec.step_deadline_s).start()
+    tok = load_tokenizer(ec.tokenizer, local.cfg)
+    info = {"device": ec.device, "world_size": world, "engine_config": ec.to_dict()}
+    if ec.device == "cuda":
+        info["device_name"] = torch.cuda.get_device_name()
+    st = ServerState(loop, tok, ec.served_model_name, ec.max_model_len, info)
+    try:
+        web.run_app(build_app(st), host=ec.host, port=ec.port, print=None)
+    finally:
+        loop.stop()
+        if world > 1:
+            eng.shutdown()
+            dist.destroy_process_group()

@@ -1,0 +1,175 @@
+"""OpenAI-compatible server on the CPU oracle engine (toy V4 model).
+
+Checks the API surface the reference's server and sweep client use: health,
+models, tokenize, completions (plain / streamed / token-id prompts / stop
+strings / length errors), chat completions, metrics, and that concurrent
+requests share engine steps and get the oracle's greedy tokens.
+"""
+
+import asyncio
+import json
+
+import pytest
+import torch
+from aiohttp.test_utils import TestClient, TestServer
+
+from dsv4_flash_deployment_b200.engine.config import EngineConfig
+from dsv4_flash_deployment_b200.ref.model import RefModel
+from dsv4_flash_deployment_b200.serving.app import ServerState, build_app
+from dsv4_flash_deployment_b200.serving.engine_loop import EngineLoop
+from dsv4_flash_deployment_b200.serving.launch import build_local_engine
+from dsv4_flash_deployment_b200.serving.tokenizer import ByteTokenizer
+
+
+@pytest.fixture(scope="module")
+def served():
+    ec = EngineConfig(device="cpu", model="toy-v4", max_seqs=4, max_batched_tokens=48, chunk_size=16,
+                      max_model_len=160, served_model_name="toy")
+    eng = build_local_engine(ec)
+    loop = EngineLoop(eng).start()
+    tok = ByteTokenizer(eng.cfg.vocab_size, eng.cfg.bos_token_id, eng.cfg.eos_token_id)
+    st = ServerState(loop, tok, "toy", ec.max_model_len, {"device": "cpu"})
+    yield st, eng
+    loop.stop()
+
+
+def _run(st, coro_fn):
+    async def main():
+        async with TestClient(TestServer(build_app(st))) as c:
+            return await coro_fn(c)
+    return asyncio.run(main())
+
+
+def _greedy(eng, ids, n):
+    ref = RefModel(eng.cfg, eng.model.ref.w, max_seq_len=256)
+    out, _ = ref.generate(torch.tensor([ids]), n)
+    return out[0].tolist()
+
+
+def test_health_models_tokenize(served):
+    st, _ = served
+
+    async def go(c):
+        h = await (await c.get("/health")).json()
+        m = await (await c.get("/v1/models")).json()
+        t = await (await c.post("/tokenize", json={"model": "toy", "prompt": "hello"})).json()
+        d = await (await c.post("/detokenize", json={"tokens": t["tokens"]})).json()
+        return h, m, t, d
+    h, m, t, d = _run(st, go)
+    assert h["status"] == "ok" and h["model"] == "toy"
+    assert m["data"][0]["id"] == "toy"
+    assert t["count"] == 6 and t["max_model_len"] == 160   # bos + 5 bytes
+    assert d["prompt"] == "hello"
+
+
+def test_completion_matches_oracle_and_streams(served):
+    st, eng = served
+    ids = [0] + [20 + (7 * i) % 200 for i in range(40)]
+
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 6, "ignore_eos": True})
+        body = await r.json()
+        r2 = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 6, "ignore_eos": True,
+                                                   "stream": True})
+        chunks, done = [], False
+        async for raw in r2.content:
+            line = raw.decode().strip()
+            if not line.startswith("data: "):
+                continue
+            if line[6:] == "[DONE]":
+                done = True
+                break
+            chunks.append(json.loads(line[6:]))
+        return body, chunks, done
+    body, chunks, done = _run(st, go)
+    want = _greedy(eng, ids, 6)
+    tok = st.tok
+    assert body["usage"]["completion_tokens"] == 6
+    assert body["choices"][0]["text"] == "".join(tok.decode_token(t) for t in want)
+    assert body["choices"][0]["finish_reason"] == "length"
+    texts = [c["choices"][0]["text"] for c in chunks if c["choices"][0]["text"]]
+    assert done and len(texts) == 6 and "".join(texts) == body["choices"][0]["text"]
+    assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+
+
+def test_concurrent_requests_share_steps(served):
+    st, eng = served
+    prompts = [[0] + [30 + (i * 13 + j) % 150 for j in range(20 + 9 * i)] for i in range(3)]
+    steps0 = eng.stats["steps"]
+
+    async def go(c):
+        rs = await asyncio.gather(*(c.post("/v1/completions", json={"prompt": p, "max_tokens": 5,
+                                                                    "ignore_eos": True}) for p in prompts))
+        return [await r.json() for r in rs]
+    outs = _run(st, go)
+    for p, o in zip(prompts, outs):
+        want = _greedy(eng, p, 5)
+        assert o["choices"][0]["text"] == "".join(st.tok.decode_token(t) for t in want)
+    # 3 requests x (prefill + 5 tokens) in far fewer steps than serially
+    assert eng.stats["steps"] - steps0 < 3 * 9
+
+
+def test_chat_stop_and_errors(served):
+    st, eng = served
+
+    async def go(c):
+        chat = await (await c.post("/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "ignore_eos": True})).json()
+        too_long = await c.post("/v1/completions", json={"prompt": "x" * 150, "max_tokens": 20})
+        bad = await c.post("/v1/completions", data=b"{not json")
+        full = await (await c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8,
+                                                            "ignore_eos": True})).json()
+        text = full["choices"][0]["text"]
+        stop = text[len(text) // 2: len(text) // 2 + 2] if len(text) > 3 else None
+        stopped = None
+        if stop:
+            stopped = await (await c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8,
+                                                                   "ignore_eos": True, "stop": [stop]})).json()
+        metrics = await (await c.get("/metrics")).text()
+        return chat, too_long.status, bad.status, text, stop, stopped, metrics
+    chat, too_long, bad, text, stop, stopped, metrics = _run(st, go)
+    assert chat["object"] == "chat.completion" and chat["usage"]["completion_tokens"] == 3
+    assert chat["choices"][0]["message"]["role"] == "assistant"
+    assert too_long == 400 and bad == 400
+    if stop:
+        assert stopped["choices"][0]["finish_reason"] == "stop"
+        assert stopped["choices"][0]["text"] == text[:text.find(stop)]
+    assert "dsv4_generation_tokens_total" in metrics and "dsv4_healthy 1" in metrics
+
+
+def test_sweep_client_rows(served, tmp_path):
+    from dsv4_flash_deployment_b200.bench.sweep import sweep
+
+    st, _ = served
+    out = tmp_path / "rows.json"
+
+    async def go(c):
+        base = str(c.make_url("")).rstrip("/")
+        shape = {"isl": 24, "osl": 4, "min_reqs": 2, "label": "tiny"}
+        rows = await sweep(base, "toy", shape, "tiny", [1, 3], str(out), n_gpus=1, vocab=1024, max_model_len=160)
+        words = await sweep(base, "toy", shape, "tiny", [2], None, n_gpus=1, prompt_mode="words")
+        return rows, words
+    rows, words = _run(st, go)
+    saved = json.loads(out.read_text())
+    assert [r["concurrency"] for r in saved] == [1, 3]
+    for r in rows + words:
+        assert r["failed"] == 0 and r["success_rate_pct"] == 100.0
+        assert r["output_tokens"] == 4 * r["requests_issued"]
+        assert r["ttft_mean_ms"] > 0 and r["tpot_mean_ms"] > 0
+        for k in ("output_throughput_tok_s", "output_tok_s_per_chip", "requests_per_s", "ttft_p50_ms",
+                  "ttft_p90_ms", "wall_time_s", "isl_min", "isl_max", "osl", "started_at", "first_error"):
+            assert k in r
+    assert words[0]["isl_max"] <= 24 and words[0]["n_words"] > 0
+
+
+def test_client_smoke_and_determinism(served):
+    from dsv4_flash_deployment_b200.bench.client_checks import determinism, smoke
+
+    st, _ = served
+
+    async def go(c):
+        base = str(c.make_url("")).rstrip("/")
+        return await smoke(base, "toy"), await determinism(base, "toy", n=6, max_tokens=3, concurrency=4, max_words=12)
+    s, d = _run(st, go)
+    assert s["ok"], s
+    assert d["ok"] and d["n"] == 6, d
