@@ -36,7 +36,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     layers = []
     if weights is not None:
         for lid in range(cfg.n_layers):
-            layers.append(load_layer(cfg, weights, lid, dev))
+            rng = ep.expert_range(cfg.n_experts_for(lid)) if ep is not None else None
+            layers.append(load_layer(cfg, weights, lid, dev, expert_range=rng))
         embed = weights["embed.weight"].to(dev)
         head = _pad_rows(weights["head.weight"]).to(dev)
         norm = weights["norm.weight"].to(dev)

@@ -106,8 +106,12 @@ def _cat_mx(parts, dev) -> MxWeight:
     return MxWeight.from_checkpoint(ws.to(dev), ss.to(dev), dev)
 
 
-def load_layer(cfg, W: dict, lid: int, dev, prefix: str | None = None, experts: ExpertBlock | None = None) -> LayerW:
-    """Checkpoint tensors -> LayerW for backbone layer ``lid`` (or an MTP stage)."""
+def load_layer(cfg, W: dict, lid: int, dev, prefix: str | None = None, experts: ExpertBlock | None = None,
+               expert_range: tuple[int, int] | None = None) -> LayerW:
+    """Checkpoint tensors -> LayerW for backbone layer ``lid`` (or an MTP stage).
+
+    ``expert_range`` = (first, count) loads only an expert-parallel rank's experts.
+    """
     p = prefix or f"layers.{lid}"
     g = lambda k: W[f"{p}.{k}"]
     L = LayerW(layer_id=lid, prefix=p)
@@ -141,8 +145,8 @@ def load_layer(cfg, W: dict, lid: int, dev, prefix: str | None = None, experts: 
     L.gate_w = _pad_rows(g("ffn.gate.weight")).to(dev)
     L.gate_b = g("ffn.gate.bias").float().to(dev)
     if experts is None:
-        n_exp = cfg.n_experts_for(lid)
-        e = lambda i, k: W[f"{p}.ffn.experts.{i}.{k}"]
+        e0, n_exp = expert_range or (0, cfg.n_experts_for(lid))
+        e = lambda i, k: W[f"{p}.ffn.experts.{e0 + i}.{k}"]
         w13s = [prepare_w13(e(i, "w1.weight"), e(i, "w1.scale"), e(i, "w3.weight"), e(i, "w3.scale"), "cpu")
                 for i in range(n_exp)]
         w13 = MxWeight(torch.cat([m.q for m in w13s]).to(dev), torch.cat([m.sf for m in w13s]).to(dev),
