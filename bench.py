@@ -114,6 +114,8 @@ def main() -> None:
     ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert exchange: NVLink peer stores (p2p) or the NCCL all-to-all baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
@@ -147,7 +149,7 @@ def main() -> None:
     n_dec = c_rank - 1
     max_tokens = n_dec + chunk_rank
     max_seq = isl + osl
-    ep = ep_mod.EPGroup(rank, world, group, dev) if world > 1 else None
+    ep = ep_mod.EPGroup(rank, world, group, dev, transport=args.ep_transport) if world > 1 else None
     n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world)
     eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
                        expert_storage_layers=n_phys, ep=ep, use_graphs=not args.no_graphs, chunk_size=chunk_rank)
@@ -275,6 +277,7 @@ def main() -> None:
                 "expert_storage_layers": n_phys,
                 "l2": "inputs larger than L2 (expert weights 6.6 GB/layer/all ranks, caches)",
                 "cuda_graphs": not args.no_graphs,
+                "ep_transport": args.ep_transport if world > 1 else None,
             },
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},

@@ -412,13 +412,32 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
   CUDA_OK(dsv4::indexer_topk(p, cur_stream()));
 }
 
+// sync = optional int64 tensor [peer_sig_table, peer_cnt_table, done, epoch] of device addresses
+static dsv4::EpSync ep_sync(const optional<Tensor>& sync, int phase) {
+  dsv4::EpSync s{nullptr, nullptr, nullptr, nullptr, phase};
+  if (!sync) return s;
+  TORCH_CHECK(sync->device().is_cpu() && sync->dtype() == torch::kInt64 && sync->numel() == 4,
+              "sync must be a CPU int64 tensor of 4 device addresses");
+  const int64_t* a = sync->data_ptr<int64_t>();
+  s.peer_sig = reinterpret_cast<uint32_t* const*>(a[0]);
+  s.peer_cnt = reinterpret_cast<int* const*>(a[1]);
+  s.done = reinterpret_cast<int*>(a[2]);
+  s.epoch = reinterpret_cast<uint32_t*>(a[3]);
+  return s;
+}
+
 void ep_pack(const Tensor& ids, const Tensor& wts, int64_t T, const Tensor& xq, const Tensor& xsf, int64_t e_local,
              int64_t world, int64_t cap, int64_t rec, const Tensor& send, const Tensor& cnt, const Tensor& pos_back,
-             const optional<Tensor>& peer_recv, int64_t my_rank, const Tensor& err) {
+             const optional<Tensor>& peer_recv, int64_t my_rank, const Tensor& err, const optional<Tensor>& sync) {
   CUDA_OK(dsv4::ep_pack(ptr<const int>(ids), ptr<const float>(wts), (int)T, (int)ids.size(1), ptr<const uint8_t>(xq),
                         ptr<const uint8_t>(xsf), (int)xq.size(1), (int)e_local, (int)world, (int)cap, (int)rec,
                         ptr<uint8_t>(send), ptr<int>(cnt), ptr<int>(pos_back), ptr<uint8_t* const>(peer_recv),
-                        (int)my_rank, ptr<uint32_t>(err), cur_stream()));
+                        (int)my_rank, ptr<uint32_t>(err), ep_sync(sync, 0), cur_stream()));
+}
+
+void ep_wait(const Tensor& sig, int64_t world, int64_t phase, const Tensor& epoch, const Tensor& err) {
+  CUDA_OK(dsv4::ep_wait(ptr<const uint32_t>(sig), (int)world, (int)phase, ptr<const uint32_t>(epoch),
+                        ptr<uint32_t>(err), cur_stream()));
 }
 
 void ep_unpack_meta(const Tensor& recv, const Tensor& cnt, int64_t world, int64_t cap, int64_t rec, int64_t D,
@@ -434,9 +453,10 @@ void ep_unpack_rows(const Tensor& recv, int64_t n, int64_t rec, int64_t D, const
 }
 
 void ep_combine_pack(const Tensor& yperm, const Tensor& pos, int64_t n, int64_t cap, const Tensor& back,
-                     const optional<Tensor>& peer_back, int64_t my_rank) {
+                     const optional<Tensor>& peer_back, int64_t my_rank, int64_t world, const optional<Tensor>& sync) {
   CUDA_OK(dsv4::ep_combine_pack(ptr<const bf16>(yperm), ptr<const int>(pos), (int)n, (int)yperm.size(1), (int)cap,
-                                ptr<bf16>(back), ptr<bf16* const>(peer_back), (int)my_rank, cur_stream()));
+                                ptr<bf16>(back), ptr<bf16* const>(peer_back), (int)my_rank, (int)world,
+                                ep_sync(sync, 1), cur_stream()));
 }
 
 void embed_streams(const Tensor& table, const Tensor& ids, int64_t T, const Tensor& X) {
@@ -474,6 +494,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_topk", &indexer_topk);
   m.def("embed_streams", &embed_streams);
   m.def("ep_pack", &ep_pack);
+  m.def("ep_wait", &ep_wait);
   m.def("ep_unpack_meta", &ep_unpack_meta);
   m.def("ep_unpack_rows", &ep_unpack_rows);
   m.def("ep_combine_pack", &ep_combine_pack);

@@ -15,50 +15,114 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace dsv4 {
+
+// ------------------------------------------------------------ peer signals
+// NVLink transport: after the last CTA of a packing kernel has finished its
+// peer stores, it publishes (for the dispatch) this rank's record counts into
+// every peer's count array, then release-stores the step's epoch into slot
+// [phase * world + my_rank] of every peer's signal array.  The consumer side
+// (ep_wait_kernel) acquire-loads its own signal slots until every peer has
+// reached the epoch, bounded by kWaitLimitNs.  Epochs advance once per call
+// on every rank (all ranks run the same sequence of MoE layers), so no reset
+// is needed between CUDA-graph replays.
+DSV4_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+DSV4_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every CTA at its end (all threads).  The last CTA publishes.
+DSV4_DEV void grid_publish(const EpSync& s, const int* cnt, int world, int my_rank, int cap) {
+  __syncthreads();
+  if (threadIdx.x != 0 || s.done == nullptr) return;
+  __threadfence_system();
+  const int prev = atomicAdd(s.done, 1);
+  if (prev != (int)gridDim.x - 1) return;
+  *s.done = 0;
+  const uint32_t ep = *s.epoch + 1u;
+  *s.epoch = ep;
+  if (s.peer_cnt) {
+    for (int p = 0; p < world; ++p) {
+      const int c = atomicAdd(const_cast<int*>(cnt) + p, 0);
+      s.peer_cnt[p][my_rank] = c < cap ? c : cap;
+    }
+  }
+  __threadfence_system();
+  for (int p = 0; p < world; ++p) st_release_sys(s.peer_sig[p] + s.phase * world + my_rank, ep);
+}
+
+__global__ void ep_wait_kernel(const uint32_t* sig, int world, int phase, const uint32_t* epoch, uint32_t* err) {
+  const int p = threadIdx.x;
+  if (p >= world) return;
+  const uint32_t want = *epoch;
+  const uint32_t* slot = sig + phase * world + p;
+  if ((int)(ld_acquire_sys(slot) - want) >= 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  while ((int)(ld_acquire_sys(slot) - want) < 0) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_error(err, ERR_PEER_TIMEOUT, KID_COMM, (uint32_t)(phase * 16 + p));
+      return;
+    }
+  }
+}
+
+cudaError_t ep_wait(const uint32_t* sig, int world, int phase, const uint32_t* epoch, uint32_t* err,
+                    cudaStream_t st) {
+  ep_wait_kernel<<<1, 32, 0, st>>>(sig, world, phase, epoch, err);
+  return cudaGetLastError();
+}
 
 __global__ void ep_pack_kernel(const int* __restrict__ ids, const float* __restrict__ wts, int T, int topk,
                                const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int D, int e_local,
                                int world, int cap, int rec, uint8_t* __restrict__ send, int* cnt, int* pos_back,
-                               uint8_t* const* peer_recv, int my_rank, uint32_t* err) {
+                               uint8_t* const* peer_recv, int my_rank, uint32_t* err, EpSync sync) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= T * topk) return;
-  const int t = w / topk;
-  const int e = ids[w];
-  const int dest = e / e_local;
-  int slot = 0;
-  if (lane == 0) slot = atomicAdd(&cnt[dest], 1);
-  slot = __shfl_sync(0xffffffffu, slot, 0);
-  if (slot >= cap) {
-    if (lane == 0) {
-      pos_back[w] = -1;
-      report_error(err, ERR_CAPACITY, KID_MOE, 2);
+  if (w < T * topk) {
+    const int t = w / topk;
+    const int e = ids[w];
+    const int dest = e / e_local;
+    int slot = 0;
+    if (lane == 0) slot = atomicAdd(&cnt[dest], 1);
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    if (slot >= cap) {
+      if (lane == 0) {
+        pos_back[w] = -1;
+        report_error(err, ERR_CAPACITY, KID_MOE, 2);
+      }
+    } else {
+      // direct peer store (NVLink) when the peer's receive buffer is mapped, else the local send buffer
+      uint8_t* dst = peer_recv ? peer_recv[dest] + ((size_t)my_rank * cap + slot) * rec
+                               : send + ((size_t)dest * cap + slot) * rec;
+      const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)t * D);
+      for (int i = lane; i < D / 16; i += 32) reinterpret_cast<uint4*>(dst)[i] = src[i];
+      const int kt = D / 128;
+      for (int b = lane; b < D / 32; b += 32) dst[D + b] = xsf[sf_chunk_offset(t, b, kt)];
+      if (lane == 0) {
+        *reinterpret_cast<int*>(dst + D + D / 32) = e - dest * e_local;
+        *reinterpret_cast<float*>(dst + D + D / 32 + 4) = wts[w];
+        pos_back[w] = dest * cap + slot;
+      }
     }
-    return;
   }
-  // direct peer store (NVLink) when the peer's receive buffer is mapped, else the local send buffer
-  uint8_t* dst = peer_recv ? peer_recv[dest] + ((size_t)my_rank * cap + slot) * rec
-                           : send + ((size_t)dest * cap + slot) * rec;
-  const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)t * D);
-  for (int i = lane; i < D / 16; i += 32) reinterpret_cast<uint4*>(dst)[i] = src[i];
-  const int kt = D / 128;
-  for (int b = lane; b < D / 32; b += 32) dst[D + b] = xsf[sf_chunk_offset(t, b, kt)];
-  if (lane == 0) {
-    *reinterpret_cast<int*>(dst + D + D / 32) = e - dest * e_local;
-    *reinterpret_cast<float*>(dst + D + D / 32 + 4) = wts[w];
-    pos_back[w] = dest * cap + slot;
-  }
+  grid_publish(sync, cnt, world, my_rank, cap);
 }
 
 cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uint8_t* xq, const uint8_t* xsf, int D,
                     int e_local, int world, int cap, int rec, uint8_t* send, int* cnt, int* pos_back,
-                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, cudaStream_t st) {
+                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, const EpSync& sync, cudaStream_t st) {
   const long long warps = (long long)T * topk;
-  if (warps == 0) return cudaSuccess;
-  ep_pack_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(ids, wts, T, topk, xq, xsf, D, e_local, world,
-                                                                      cap, rec, send, cnt, pos_back, peer_recv,
-                                                                      my_rank, err);
+  if (warps == 0 && sync.done == nullptr) return cudaSuccess;
+  const unsigned grid = (unsigned)std::max(1LL, (warps * 32 + 255) / 256);
+  ep_pack_kernel<<<grid, 256, 0, st>>>(ids, wts, T, topk, xq, xsf, D, e_local, world, cap, rec, send, cnt, pos_back,
+                                       peer_recv, my_rank, err, sync);
   return cudaGetLastError();
 }
 
@@ -111,23 +175,25 @@ cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int
 // written straight into the source rank's return buffer over NVLink.
 __global__ void ep_combine_pack_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ pos, int n,
                                        int D, int cap, __nv_bfloat16* back, __nv_bfloat16* const* peer_back,
-                                       int my_rank) {
+                                       int my_rank, int world, EpSync sync) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= n) return;
-  const int row = pos[w];
-  if (row < 0) return;
-  const int src_rank = w / cap, j = w % cap;
-  __nv_bfloat16* dst = peer_back ? peer_back[src_rank] + ((size_t)my_rank * cap + j) * D : back + (size_t)w * D;
-  const uint4* s = reinterpret_cast<const uint4*>(yperm + (size_t)row * D);
-  for (int i = lane; i < D / 8; i += 32) reinterpret_cast<uint4*>(dst)[i] = s[i];
+  const int row = w < n ? pos[w] : -1;
+  if (row >= 0) {
+    const int src_rank = w / cap, j = w % cap;
+    __nv_bfloat16* dst = peer_back ? peer_back[src_rank] + ((size_t)my_rank * cap + j) * D : back + (size_t)w * D;
+    const uint4* s = reinterpret_cast<const uint4*>(yperm + (size_t)row * D);
+    for (int i = lane; i < D / 8; i += 32) reinterpret_cast<uint4*>(dst)[i] = s[i];
+  }
+  grid_publish(sync, nullptr, world, my_rank, cap);
 }
 
 cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
-                            __nv_bfloat16* const* peer_back, int my_rank, cudaStream_t st) {
-  if (n == 0) return cudaSuccess;
-  ep_combine_pack_kernel<<<(unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st>>>(yperm, pos, n, D, cap, back,
-                                                                                      peer_back, my_rank);
+                            __nv_bfloat16* const* peer_back, int my_rank, int world, const EpSync& sync,
+                            cudaStream_t st) {
+  if (n == 0 && sync.done == nullptr) return cudaSuccess;
+  const unsigned grid = (unsigned)std::max(1LL, ((long long)n * 32 + 255) / 256);
+  ep_combine_pack_kernel<<<grid, 256, 0, st>>>(yperm, pos, n, D, cap, back, peer_back, my_rank, world, sync);
   return cudaGetLastError();
 }
 

@@ -179,15 +179,27 @@ struct IdxParams {
 cudaError_t indexer_topk(const IdxParams& p, cudaStream_t st);
 
 // ---------------------------------------------------------------- ep.cu
+// Completion signalling of the NVLink (peer-store) transport; all null for the
+// NCCL transport.
+struct EpSync {
+  uint32_t* const* peer_sig;   // [world] each rank's signal array (uint32 [2 * world])
+  int* const* peer_cnt;        // [world] each rank's receive-count array (dispatch only)
+  int* done;                   // this rank's CTA completion counter for the phase
+  uint32_t* epoch;             // this rank's epoch counter for the phase
+  int phase;                   // 0 dispatch, 1 combine
+};
+cudaError_t ep_wait(const uint32_t* sig, int world, int phase, const uint32_t* epoch, uint32_t* err,
+                    cudaStream_t st);
 cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uint8_t* xq, const uint8_t* xsf, int D,
                     int e_local, int world, int cap, int rec, uint8_t* send, int* cnt, int* pos_back,
-                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, cudaStream_t st);
+                    uint8_t* const* peer_recv, int my_rank, uint32_t* err, const EpSync& sync, cudaStream_t st);
 cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
                            float* wts, cudaStream_t st);
 cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
                            cudaStream_t st);
 cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
-                            __nv_bfloat16* const* peer_back, int my_rank, cudaStream_t st);
+                            __nv_bfloat16* const* peer_back, int my_rank, int world, const EpSync& sync,
+                            cudaStream_t st);
 
 // -------------------------------------------------------------- misc.cu
 cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
