@@ -29,6 +29,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=None, help="override n_layers (smaller smoke runs)")
     ap.add_argument("--experts", type=int, default=None, help="override routed experts (small profiling cases)")
     ap.add_argument("--topk", type=int, default=None)
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"])
     a = ap.parse_args()
     import os
 
@@ -43,7 +44,7 @@ def main() -> None:
     ep = None
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local))
+        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), transport=a.ep_transport)
     kw = {"n_layers": a.layers} if a.layers else {}
     if a.experts:
         kw["n_routed_experts"] = a.experts

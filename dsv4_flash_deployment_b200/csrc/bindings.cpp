@@ -459,6 +459,72 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, int64_t n, int64_t 
                                 ep_sync(sync, 1), cur_stream()));
 }
 
+// tables: int64 CPU tensor [nl, 3] = (device-mapped table address, scale table address, n_emb)
+void engram_prepare(const Tensor& ids, const Tensor& pos, const Tensor& slot, const Tensor& chunk_start,
+                    const Tensor& step_row0, const Tensor& last_pos, int64_t T, const Tensor& token_map,
+                    const Tensor& ring, const Tensor& mult, const Tensor& primes, const Tensor& offsets, int64_t pad,
+                    const Tensor& rows, const optional<Tensor>& tables, const optional<Tensor>& a_q,
+                    const optional<Tensor>& a_sf, int64_t hd) {
+  dsv4::EngramParams p{};
+  p.T = (int)T;
+  p.nl = (int)mult.size(0);
+  p.N = (int)mult.size(1);
+  p.H = (int)primes.size(2);
+  p.hd = (int)hd;
+  p.ids = ptr<const int>(ids);
+  p.pos = ptr<const int>(pos);
+  p.slot = ptr<const int>(slot);
+  p.chunk_start = ptr<const int>(chunk_start);
+  p.step_row0 = ptr<const int>(step_row0);
+  p.last_pos = ptr<const int>(last_pos);
+  p.token_map = ptr<const int64_t>(token_map);
+  p.ring = ptr<int64_t>(ring);
+  p.mult = ptr<const int64_t>(mult);
+  p.primes = ptr<const int64_t>(primes);
+  p.offsets = ptr<const int64_t>(offsets);
+  p.pad = pad;
+  p.rows = ptr<int64_t>(rows);
+  TORCH_CHECK(p.nl <= dsv4::kEngramMaxLayers, "too many Engram layers");
+  const bool gather = tables.has_value();
+  if (gather) {
+    TORCH_CHECK(a_q && a_sf && tables->device().is_cpu() && tables->size(0) == p.nl, "bad Engram tables");
+    const int64_t* t = tables->data_ptr<int64_t>();
+    for (int l = 0; l < p.nl; ++l) {
+      p.table[l] = reinterpret_cast<const uint8_t*>(t[3 * l]);
+      p.table_sf[l] = reinterpret_cast<const uint8_t*>(t[3 * l + 1]);
+      p.n_emb[l] = t[3 * l + 2];
+    }
+    p.a_q = ptr<uint8_t>(a_q);
+    p.a_sf = ptr<uint8_t>(a_sf);
+    p.a_stride_q = (size_t)a_q->stride(0);
+    p.a_stride_sf = (size_t)a_sf->stride(0);
+  }
+  CUDA_OK(dsv4::engram_prepare(p, gather, cur_stream()));
+}
+
+void engram_gate(const Tensor& X, const Tensor& kv, const Tensor& wgt, int64_t T, double eps) {
+  CUDA_OK(dsv4::engram_gate(ptr<bf16>(X), ptr<const bf16>(kv), ptr<const float>(wgt), (int)T, (int)X.size(2),
+                            (int)X.size(1), (float)eps, cur_stream()));
+}
+
+// Pins an existing host allocation and returns the device address that kernels read it through.
+int64_t host_register(int64_t addr, int64_t bytes) {
+  void* p = reinterpret_cast<void*>(addr);
+  CUDA_OK(cudaHostRegister(p, (size_t)bytes, cudaHostRegisterMapped | cudaHostRegisterPortable));
+  void* d = nullptr;
+  CUDA_OK(cudaHostGetDevicePointer(&d, p, 0));
+  return reinterpret_cast<int64_t>(d);
+}
+
+void host_unregister(int64_t addr) { CUDA_OK(cudaHostUnregister(reinterpret_cast<void*>(addr))); }
+
+// Device address of page-locked host memory (e.g. a pinned torch tensor).
+int64_t host_device_ptr(int64_t addr) {
+  void* d = nullptr;
+  CUDA_OK(cudaHostGetDevicePointer(&d, reinterpret_cast<void*>(addr), 0));
+  return reinterpret_cast<int64_t>(d);
+}
+
 void embed_streams(const Tensor& table, const Tensor& ids, int64_t T, const Tensor& X) {
   CUDA_OK(dsv4::embed_streams(ptr<const bf16>(table), ptr<const int>(ids), (int)T, (int)table.size(1),
                               (int)X.size(1), ptr<bf16>(X), cur_stream()));
@@ -493,6 +559,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter", &moe_scatter);
   m.def("indexer_topk", &indexer_topk);
   m.def("embed_streams", &embed_streams);
+  m.def("engram_prepare", &engram_prepare);
+  m.def("engram_gate", &engram_gate);
+  m.def("host_register", &host_register);
+  m.def("host_unregister", &host_unregister);
+  m.def("host_device_ptr", &host_device_ptr);
   m.def("ep_pack", &ep_pack);
   m.def("ep_wait", &ep_wait);
   m.def("ep_unpack_meta", &ep_unpack_meta);

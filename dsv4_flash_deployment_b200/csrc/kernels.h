@@ -201,6 +201,34 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, i
                             __nv_bfloat16* const* peer_back, int my_rank, int world, const EpSync& sync,
                             cudaStream_t st);
 
+// ------------------------------------------------------------ engram.cu
+constexpr int kEngramMaxLayers = 4;
+struct EngramParams {
+  int T, nl, N, H, hd;              // tokens, Engram layers, max n-gram, heads per order, row bytes
+  const int* ids;                   // [T] this step's token ids
+  const int* pos;
+  const int* slot;
+  const int* chunk_start;
+  const int* step_row0;
+  const int* last_pos;
+  const int64_t* token_map;         // [vocab] compressed id (-1 = dead token)
+  int64_t* ring;                    // [slots, N-1] compressed ids by position % (N-1)
+  const int64_t* mult;              // [nl, N]
+  const int64_t* primes;            // [nl, N-1, H]
+  const int64_t* offsets;           // [nl, (N-1)*H]
+  int64_t pad;                      // compressed pad id
+  int64_t* rows;                    // [T, nl, (N-1)*H] row ids (out)
+  const uint8_t* table[kEngramMaxLayers];     // device-mapped host tables [n_emb, hd] e4m3
+  const uint8_t* table_sf[kEngramMaxLayers];  // [n_emb, hd/32] ue8m0
+  int64_t n_emb[kEngramMaxLayers];
+  uint8_t* a_q;                     // [nl] x [T_pad, K] e4m3 (K = (N-1)*H*hd)
+  uint8_t* a_sf;                    // [nl] x scale chunks
+  size_t a_stride_q, a_stride_sf;   // per-layer strides (bytes)
+};
+cudaError_t engram_prepare(const EngramParams& p, bool gather, cudaStream_t st);
+cudaError_t engram_gate(__nv_bfloat16* X, const __nv_bfloat16* kv, const float* wgt, int T, int D, int hc, float eps,
+                        cudaStream_t st);
+
 // -------------------------------------------------------------- misc.cu
 cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
                           cudaStream_t st);

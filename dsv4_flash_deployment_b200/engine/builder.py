@@ -52,5 +52,9 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
         head = _pad_rows((torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) / cfg.dim ** 0.5)
                          .to(torch.bfloat16))
         norm = (1.0 + 0.05 * torch.randn(cfg.dim, device=dev, generator=g)).to(torch.bfloat16)
-    return DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
-                     head_vocab=cfg.vocab_size)
+    model = DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
+                      head_vocab=cfg.vocab_size)
+    if cfg.engram_layer_ids:
+        from ..models.engram import EngramRuntime
+        model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed)
+    return model

@@ -1,0 +1,137 @@
+"""Engram on the device, with the embedding tables in pinned host memory.
+
+V4.1 adds, before the blocks of layers 1 and 14, a lookup of 24 hashed
+n-gram rows (orders 2..4 x 8 heads) per token in two ~100 GB FP8 tables, an
+FP8 ``wkv`` projection to 4 keys + 1 value, and a per-stream sigmoid gate
+(``reference.py:272-319``; host-resident tables in the vLLM recipe,
+P/0005:1183-1370).  Here:
+
+* the tables stay in page-locked host memory (``cudaHostRegister`` of the
+  loaded arrays, or pinned allocations for random init) and the GPU reads the
+  rows it needs straight over the host link: 24 x (256 + 8) bytes per token
+  and layer, with no host thread on the step's critical path;
+* hashing runs on the GPU from this step's tokens and a per-slot ring of the
+  previous 3 compressed ids (the int64 contract of ``ref/engram.py``);
+* the gathered rows are already MXFP8 (e4m3 + ue8m0 per 32), so they feed the
+  block-scaled tcgen05 GEMM directly as its A operand; a small kernel applies
+  the gate to the four residual streams.
+
+Hash + gather for every Engram layer run once per step at the first Engram
+layer; each Engram layer then runs its GEMM and gate.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ..ops.gemm import MxWeight
+from ..ops.layout import ceil_to, expand_block_scales
+from ..ref.engram import EngramHasher
+
+
+class HostTable:
+    """One layer's table: e4m3 rows [n_emb, hd] + ue8m0 scales [n_emb, hd/32], page-locked.
+
+    Pageable tensors are page-locked in place by registering their whole
+    storage once (tensors loaded from one checkpoint file share a storage, and
+    two registrations may not overlap); pinned tensors are used as they are.
+    """
+
+    _registered: dict[int, tuple[int, int]] = {}   # storage address -> (device address, users)
+
+    def __init__(self, q: torch.Tensor, sf: torch.Tensor, ext):
+        self.q, self.sf = q.contiguous().view(torch.uint8), sf.contiguous().view(torch.uint8)
+        self.n = self.q.shape[0]
+        self.storages = []
+        self.dq = self._device_addr(self.q, ext)
+        self.dsf = self._device_addr(self.sf, ext)
+
+    def _device_addr(self, t: torch.Tensor, ext) -> int:
+        st = t.untyped_storage()
+        base = st.data_ptr()
+        if t.is_pinned():
+            return int(ext.host_device_ptr(base)) + (t.data_ptr() - base)
+        reg = HostTable._registered.get(base)
+        if reg is None:
+            reg = (int(ext.host_register(base, st.nbytes())), 0)
+        HostTable._registered[base] = (reg[0], reg[1] + 1)
+        self.storages.append(base)
+        return reg[0] + (t.data_ptr() - base)
+
+    def release(self, ext) -> None:
+        for base in self.storages:
+            dev, users = HostTable._registered[base]
+            if users <= 1:
+                ext.host_unregister(base)
+                del HostTable._registered[base]
+            else:
+                HostTable._registered[base] = (dev, users - 1)
+        self.storages = []
+
+
+class EngramRuntime:
+    def __init__(self, cfg, dev, n_slots: int, max_tokens: int, ext, weights: dict | None = None, seed: int = 0):
+        self.cfg, self.dev, self.ext = cfg, dev, ext
+        h = EngramHasher(cfg)
+        lay = h.layout
+        self.nl, self.N, self.H, self.hd = len(lay.layer_ids), lay.max_ngram, lay.n_heads, lay.head_dim
+        self.cols = (self.N - 1) * self.H
+        self.K = self.cols * self.hd
+        i64 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.int64, device=dev)
+        self.token_map = i64(h.token_map)
+        self.mult, self.primes, self.offsets = i64(h.mult), i64(lay.primes), i64(lay.offsets)
+        self.pad = int(h.pad)
+        self.ring = torch.zeros(n_slots, self.N - 1, dtype=torch.int64, device=dev)
+        self.rows = torch.zeros(max_tokens, self.nl, self.cols, dtype=torch.int64, device=dev)
+        tp = ceil_to(max_tokens, 128)
+        self.a_q = torch.zeros(self.nl, tp, self.K, dtype=torch.uint8, device=dev)
+        self.a_sf = torch.full((self.nl, (tp // 128) * (self.K // 128) * 512), 127, dtype=torch.uint8, device=dev)
+        D, hc = cfg.dim, cfg.hc_mult
+        self.kv = torch.empty(max_tokens, (hc + 1) * D, dtype=torch.bfloat16, device=dev)
+        self.layer_index = {lid: i for i, lid in enumerate(lay.layer_ids)}
+        self.tables, self.wkv, self.wgt = [], [], []
+        g = torch.Generator().manual_seed(seed + 4242)
+        for i, lid in enumerate(lay.layer_ids):
+            p = f"layers.{lid}.engram"
+            if weights is not None:
+                q, sf = weights[f"{p}.embed.weight"], weights[f"{p}.embed.scale"]
+                wkv = MxWeight.from_checkpoint(weights[f"{p}.wkv.weight"],
+                                               expand_block_scales(weights[f"{p}.wkv.scale"],
+                                                                   weights[f"{p}.wkv.weight"].shape[0]), dev)
+                qw, kw = weights[f"{p}.q_weight"], weights[f"{p}.k_weight"]
+            else:
+                # tables of the full model are ~100 GB each: fill them with the native
+                # multithreaded generator, then page-lock them in place (HostTable)
+                from ..ops import host
+                n_emb = lay.num_embeddings[i]
+                q = torch.empty(n_emb, self.hd, dtype=torch.uint8)
+                sf = torch.empty(n_emb, self.hd // 32, dtype=torch.uint8)
+                host.fill_random(q, seed * 1000 + 2 * i + 1, 0)
+                host.fill_random(sf, seed * 1000 + 2 * i + 2, 1, 118)
+                wq = (torch.randn((hc + 1) * D, self.K, generator=g) * 0.5).to(torch.float8_e4m3fn)
+                ws = torch.randint(118, 123, ((hc + 1) * D // 32, self.K // 32), generator=g,
+                                   dtype=torch.int32).to(torch.uint8)
+                wkv = MxWeight.from_checkpoint(wq, expand_block_scales(ws, (hc + 1) * D), dev)
+                qw = (1 + 0.05 * torch.randn(hc, D, generator=g)).to(torch.bfloat16)
+                kw = (1 + 0.05 * torch.randn(hc, D, generator=g)).to(torch.bfloat16)
+            self.tables.append(HostTable(q, sf, ext))
+            self.wkv.append(wkv)
+            self.wgt.append((qw.float() * kw.float()).to(dev).contiguous())
+        self.table_addrs = torch.tensor([[t.dq, t.dsf, t.n] for t in self.tables], dtype=torch.int64)
+
+    def prepare(self, model, T: int) -> None:
+        """Hashes this step's tokens and gathers every Engram layer's rows from host memory."""
+        self.ext.engram_prepare(model.m_ids, model.m_pos, model.m_slot, model.m_cstart, model.m_row0, model.m_last,
+                                T, self.token_map, self.ring, self.mult, self.primes, self.offsets, self.pad,
+                                self.rows, self.table_addrs, self.a_q, self.a_sf, self.hd)
+
+    def apply(self, model, lid: int, T: int) -> None:
+        """X += gate * value for Engram layer ``lid`` (rows gathered by :meth:`prepare`)."""
+        i = self.layer_index[lid]
+        model._gemm(self.a_q[i], self.a_sf[i], T, self.wkv[i], self.kv)
+        self.ext.engram_gate(model.X, self.kv, self.wgt[i], T, self.cfg.rms_norm_eps)
+
+    def release(self) -> None:
+        for t in self.tables:
+            t.release(self.ext)

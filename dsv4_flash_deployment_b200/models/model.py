@@ -273,6 +273,7 @@ class DSV4Model:
 
     last_upload_bytes = 0
     op_timer: dict | None = None
+    engram = None            # EngramRuntime for configs with Engram layers
 
     @contextlib.contextmanager
     def _t(self, name: str):
@@ -319,10 +320,12 @@ class DSV4Model:
         fnhl = scale = base = None
         if mixes is not None:
             fnhl, scale, base = mixes
-        ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T)
+        with self._t("hc_post"):
+            ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T)
         if mixes is not None or (cw is not None and u is not None):
-            ext.hc_finish(self.X, fnhl, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
-                          self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
+            with self._t("hc_finish"):
+                ext.hc_finish(self.X, fnhl, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
+                              self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)
 
     sinkhorn_iters = None
 
@@ -336,6 +339,10 @@ class DSV4Model:
         ext = self.ext
         with self._t("embed"):
             self.ext.embed_streams(self.embed, self.m_ids, T, self.X)
+        eng = self.engram
+        if eng is not None:
+            with self._t("engram_gather"):
+                eng.prepare(self, T)
         prev, cw = None, self.mix0
         moe_state = None
         for li, L in enumerate(self.layers):
@@ -343,9 +350,17 @@ class DSV4Model:
             tap = None
             if taps is not None and lid in cfg.dspark_target_layer_ids:
                 tap = taps[lid]
-            hc_ctx = self._t("mhc")
-            hc_ctx.__enter__()
-            if moe_state is None:
+            if eng is not None and lid in eng.layer_index:
+                # the streams take the previous MoE output, then the Engram update, and
+                # only then this block's mixes and collapse (reference.py:925-931)
+                if moe_state is not None:
+                    yp, ps, kk = moe_state
+                    self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF)
+                with self._t("engram"):
+                    eng.apply(self, lid, T)
+                self._hc(T, prev=None, mixes=L.hc_attn, cw=cw if moe_state is None else self.mixF,
+                         norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf, tap=tap)
+            elif moe_state is None:
                 self._hc(T, prev=None, mixes=L.hc_attn, cw=cw, norm=L.attn_norm, mix_out=self.mixA, u=self.u,
                          uq=self.uq, usf=self.usf, tap=tap)
             else:
@@ -353,15 +368,13 @@ class DSV4Model:
                 self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
                          cw=self.mixF, norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf,
                          tap=tap)
-            hc_ctx.__exit__(None, None, None)
             if trace is not None:
                 trace[lid] = self.X[:T].clone()
             self._attention(L, m)
             if trace is not None:
                 trace[f"attn{lid}"] = self.attn_out[:T].clone()
-            with self._t("mhc"):
-                self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
-                         mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
+            self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
+                     mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
             moe_state = self._moe(L, T)
         # final collapse + norm on all tokens, then head on the sampled rows
         yp, ps, kk = moe_state
@@ -397,8 +410,7 @@ class DSV4Model:
         if r > 0:
             src = cfg.kv_source_for(lid)
             if lid in cfg.kv_source_layer_ids:
-                with self._t("compressor"):
-                    self._compress(L, m, r)
+                self._compress(L, m, r)
             clen = self.m_clen[r]
             if lid in cfg.index_source_layer_ids:
                 if m.index_bypass(r):
@@ -441,17 +453,19 @@ class DSV4Model:
         co = cfg.overlap(lid)
         width = 2 * co * cfg.head_dim
         proj = self.proj[co]
-        self._gemm_bf16(self.u, L.comp_wkvg, proj, T, f32_out=True, m_valid=width)
+        with self._t("comp_gemm"):
+            self._gemm_bf16(self.u, L.comp_wkvg, proj, T, f32_out=True, m_valid=width)
         g = self.m_groups[r]
         cos, sin = self.rope["yarn"]
         # grid covers every token that could close a group; the kernel reads the real count
         max_groups = min(T, int((m._lens // r + 1).sum()))
         if max_groups:
-            ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
-                              self.comp_ring[lid],
-                              L.comp_norm, cfg.rms_norm_eps, cos, sin, self.comp[lid], L.idx_wk, L.idx_knorm,
-                              self.idx_cache.get(lid) if L.idx_wk is not None else None)
-        ext.ring_update(self.comp_ring[lid], proj, T, self.m_slot, self.m_pos, self.m_last)
+            with self._t("comp_pool"):
+                ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
+                                  self.comp_ring[lid], L.comp_norm, cfg.rms_norm_eps, cos, sin, self.comp[lid],
+                                  L.idx_wk, L.idx_knorm, self.idx_cache.get(lid) if L.idx_wk is not None else None)
+        with self._t("comp_ring"):
+            ext.ring_update(self.comp_ring[lid], proj, T, self.m_slot, self.m_pos, self.m_last)
 
     def _indexer(self, L: LayerW, m: StepMeta, r: int):
         cfg, ext = self.cfg, self.ext

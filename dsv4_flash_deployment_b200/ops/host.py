@@ -54,16 +54,51 @@ def lib() -> ctypes.CDLL:
 
 
 def _declare_engram(L) -> None:
-    if not hasattr(L, "dsv4_engram_hash"):
-        return
-    i64p = ctypes.POINTER(ctypes.c_int64)
-    L.dsv4_engram_hash.argtypes = [i64p, ctypes.c_int64, i64p, ctypes.c_int64, i64p, ctypes.c_int, ctypes.c_int,
-                                   i64p, i64p, ctypes.c_int64, i64p]
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    L.dsv4_engram_hash.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp, vp]
     L.dsv4_engram_hash.restype = ctypes.c_int
-    if hasattr(L, "dsv4_gather_rows"):
-        L.dsv4_gather_rows.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, i64p, ctypes.c_int64,
-                                       ctypes.c_void_p, ctypes.c_int]
-        L.dsv4_gather_rows.restype = ctypes.c_int
+    L.dsv4_gather_rows.argtypes = [vp, i64, i64, vp, i64, vp, ctypes.c_int]
+    L.dsv4_gather_rows.restype = ctypes.c_int
+    L.dsv4_fill_random.argtypes = [vp, i64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.dsv4_fill_random.restype = ctypes.c_int
+
+
+def fill_random(t, seed: int, mode: int, lo: int = 118, threads: int = 32) -> None:
+    """Fills a contiguous uint8 host tensor: mode 0 = e4m3 codes (no NaN), 1 = ue8m0 bytes in [lo, lo+4]."""
+    lib().dsv4_fill_random(t.data_ptr(), t.numel() * t.element_size(), seed, mode, lo, threads)
+
+
+def engram_hash(hist, positions, mult, primes, offsets, pad: int, threads: int = 8):
+    """Native twin of :meth:`..ref.engram.EngramHasher.hash` (numpy int64 arrays in and out)."""
+    import numpy as np
+
+    hist = np.ascontiguousarray(hist, dtype=np.int64)
+    pos = np.ascontiguousarray(positions, dtype=np.int64)
+    mult = np.ascontiguousarray(mult, dtype=np.int64)
+    primes = np.ascontiguousarray(primes, dtype=np.int64)
+    offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+    nl, N = mult.shape
+    H = primes.shape[-1]
+    meta = np.array([nl, N, H, pad, threads], dtype=np.int64)
+    out = np.empty((len(pos), nl, (N - 1) * H), dtype=np.int64)
+    r = lib().dsv4_engram_hash(hist.ctypes.data, len(hist), pos.ctypes.data, len(pos), mult.ctypes.data,
+                               primes.ctypes.data, offsets.ctypes.data, meta.ctypes.data, out.ctypes.data)
+    if r != 0:
+        raise ValueError(f"dsv4_engram_hash failed ({r})")
+    return out
+
+
+def gather_rows(table, ids, out=None, threads: int = 8):
+    """out[i] = table[ids[i]] (rows of a 2-D host tensor), zero rows for out-of-range ids."""
+    import numpy as np
+    import torch
+
+    ids = np.ascontiguousarray(ids, dtype=np.int64).reshape(-1)
+    rb = table.shape[1] * table.element_size()
+    if out is None:
+        out = torch.empty((len(ids), table.shape[1]), dtype=table.dtype)
+    lib().dsv4_gather_rows(table.data_ptr(), table.shape[0], rb, ids.ctypes.data, len(ids), out.data_ptr(), threads)
+    return out
 
 
 def pread_many(path: str, offsets: list[int], sizes: list[int], dst_ptrs: list[int], threads: int = 16) -> None:
