@@ -212,6 +212,35 @@ def main() -> None:
     out_tok_step = n_dec * world
     value = out_tok_step / (ms_max / 1e3)
 
+    # ------------------------------------------------------------ C=1 TPOT
+    # one sequence decoding at mid-sweep context (every rank runs its own
+    # 1-token step so the EP exchange is part of the latency); graph replay
+    c1_pos = isl + osl // 2
+    c1_steps = max(8, args.steps)
+
+    def c1_meta(i):
+        return StepMeta(cfg, [SeqChunk(0, c1_pos + i, [int(rng.integers(0, cfg.vocab_size))], True)])
+
+    for i in range(3):
+        eng.run_meta(c1_meta(i))
+    c1m = [c1_meta(3 + i) for i in range(c1_steps)]
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    c0, c1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    c0.record(eng.stream)
+    for mm in c1m:
+        eng.run_meta(mm)
+    c1e.record(eng.stream)
+    torch.cuda.synchronize()
+    c1_wall = (time.perf_counter() - w0) / c1_steps * 1e3
+    c1_dev = c0.elapsed_time(c1e) / c1_steps
+    c1_t = torch.tensor([c1_dev, c1_wall], device=dev)
+    if group is not None:
+        dist.all_reduce(c1_t, op=dist.ReduceOp.MAX)
+    c1_dev, c1_wall = (float(x) for x in c1_t.tolist())
+
     # ----------------------------------------------------------------- e2e
     sched = eng.sched
     e2e_steps = args.e2e_steps or args.steps
@@ -282,6 +311,9 @@ def main() -> None:
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches_per_step * args.steps,
+            "c1_tpot_ms": {"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,
+                           "baseline_ms": 27.69, "note": "one sequence per rank, 1-token steps through "
+                           "Engine.run_meta (pinned H2D + D2H + sync each token), graph replay"},
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

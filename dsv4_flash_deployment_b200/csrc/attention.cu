@@ -90,14 +90,15 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   const int rope_pos = p.rope_pos ? p.rope_pos[t] : pos;
 
   // ---------------- row list: window, then compressed entries (valid ones first)
-  const int n_win = min(pos + 1, p.W);
+  const int we = p.win_end ? p.win_end[t] : pos;
+  const int n_win = min(we + 1, p.win_len > 0 ? p.win_len : p.W);
   const int n_comp = p.comp != nullptr ? min(p.comp_cnt[t], kAttnMaxRows - n_win) : 0;
   {
     const int cs = p.chunk_start[t];
     for (int j = tid; j < n_win + n_comp; j += blockDim.x) {
       const __nv_bfloat16* r;
       if (j < n_win) {
-        const int pp = pos - n_win + 1 + j;
+        const int pp = we - n_win + 1 + j;
         if (pp >= cs)
           r = p.kv_step + (size_t)(p.step_row0[t] + (pp - cs)) * kDh;
         else

@@ -230,7 +230,7 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
                const optional<Tensor>& comp, const Tensor& slot, const Tensor& pos, const Tensor& chunk_start,
                const Tensor& step_row0, const optional<Tensor>& comp_idx, const optional<Tensor>& comp_cnt,
                const Tensor& sink, double scale, const Tensor& out, const optional<Tensor>& workspace, int64_t T,
-               int64_t nsplit) {
+               int64_t nsplit, const optional<Tensor>& win_end, int64_t win_len) {
   CHECK_CUDA(q);
   TORCH_CHECK(q.size(-1) == 512 && q.size(-2) == 64, "q must be [T, 64, 512]");
   dsv4::AttnParams p{};
@@ -255,6 +255,9 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
   p.comp_k = comp_idx ? (int)comp_idx->size(1) : 0;
   p.comp_cnt = ptr<const int>(comp_cnt);
   if (comp) TORCH_CHECK(comp_cnt.has_value(), "comp_cnt required with comp");
+  p.win_end = ptr<const int>(win_end);
+  p.win_len = (int)win_len;
+  TORCH_CHECK(win_len <= dsv4::kAttnMaxRows, "window longer than the attention row limit");
   p.sink = ptr<const float>(sink);
   p.scale = (float)scale;
   p.out = ptr<bf16>(out);
@@ -464,7 +467,7 @@ void engram_prepare(const Tensor& ids, const Tensor& pos, const Tensor& slot, co
                     const Tensor& step_row0, const Tensor& last_pos, int64_t T, const Tensor& token_map,
                     const Tensor& ring, const Tensor& mult, const Tensor& primes, const Tensor& offsets, int64_t pad,
                     const Tensor& rows, const optional<Tensor>& tables, const optional<Tensor>& a_q,
-                    const optional<Tensor>& a_sf, int64_t hd) {
+                    const optional<Tensor>& a_sf, int64_t hd, int64_t mode) {
   dsv4::EngramParams p{};
   p.T = (int)T;
   p.nl = (int)mult.size(0);
@@ -485,7 +488,7 @@ void engram_prepare(const Tensor& ids, const Tensor& pos, const Tensor& slot, co
   p.pad = pad;
   p.rows = ptr<int64_t>(rows);
   TORCH_CHECK(p.nl <= dsv4::kEngramMaxLayers, "too many Engram layers");
-  const bool gather = tables.has_value();
+  const bool gather = (mode & 4) != 0;
   if (gather) {
     TORCH_CHECK(a_q && a_sf && tables->device().is_cpu() && tables->size(0) == p.nl, "bad Engram tables");
     const int64_t* t = tables->data_ptr<int64_t>();
@@ -499,7 +502,7 @@ void engram_prepare(const Tensor& ids, const Tensor& pos, const Tensor& slot, co
     p.a_stride_q = (size_t)a_q->stride(0);
     p.a_stride_sf = (size_t)a_sf->stride(0);
   }
-  CUDA_OK(dsv4::engram_prepare(p, gather, cur_stream()));
+  CUDA_OK(dsv4::engram_prepare(p, (int)mode, cur_stream()));
 }
 
 void engram_gate(const Tensor& X, const Tensor& kv, const Tensor& wgt, int64_t T, double eps) {
@@ -528,6 +531,13 @@ int64_t host_device_ptr(int64_t addr) {
 void embed_streams(const Tensor& table, const Tensor& ids, int64_t T, const Tensor& X) {
   CUDA_OK(dsv4::embed_streams(ptr<const bf16>(table), ptr<const int>(ids), (int)T, (int)table.size(1),
                               (int)X.size(1), ptr<bf16>(X), cur_stream()));
+}
+
+void markov_step(const Tensor& logits, int64_t blk, int64_t i, const Tensor& mlog, int64_t V, int64_t n,
+                 const Tensor& toks, const Tensor& memb, const Tensor& emb) {
+  CUDA_OK(dsv4::markov_step(ptr<const float>(logits), (int)logits.stride(0), (int)blk, (int)i,
+                            ptr<const float>(mlog), (int)mlog.stride(0), (int)V, (int)n, ptr<int>(toks),
+                            ptr<const bf16>(memb), (int)memb.size(1), ptr<bf16>(emb), cur_stream()));
 }
 
 void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out) {
@@ -570,4 +580,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_unpack_rows", &ep_unpack_rows);
   m.def("ep_combine_pack", &ep_combine_pack);
   m.def("argmax_rows", &argmax_rows);
+  m.def("markov_step", &markov_step);
 }

@@ -39,11 +39,14 @@ DSV4_DEV float block_sum(float v, float* red) {
   return red[NT / 32];
 }
 
-// 512 threads: thread d owns latent dim d (dh == 512).
+// 512 threads.  Pooling: 128 dim-quads (float4 loads) x 4 slot lanes, each lane an
+// independent online softmax over every 4th slot, merged through shared
+// memory.  Then thread d owns latent dim d (dh == 512).
 __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
   __shared__ float red[32];
   __shared__ __nv_bfloat16 lat[512];
   __shared__ float kbuf[256];
+  __shared__ float4 sm_m[4][128], sm_s[4][128], sm_a[4][128];
   const int gi = blockIdx.x;
   if (gi >= *p.n_groups_dev) return;
   const int slot = p.g_slot[gi], g = p.g_index[gi], cs = p.g_chunk_start[gi], row0 = p.g_row0[gi];
@@ -51,23 +54,56 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
   const int r = p.r, co = p.co, dh = p.dh;
   const int width = 2 * co * dh;
   const int depth = co * r;
-  // softmax over the (co * r) slots, per dim, online in fp32
-  float m = -INFINITY, ssum = 0.f, acc = 0.f;
-  const int first = g * r - (co - 1) * r;
-  for (int pp = first; pp < (g + 1) * r; ++pp) {
-    if (pp < 0) continue;
-    const int half = (pp < g * r) ? 0 : (co - 1);
-    const float* src = (pp >= cs) ? p.proj + (size_t)(row0 + pp - cs) * width
-                                  : p.ring + ((size_t)slot * depth + (pp % depth)) * width;
-    const float kv = src[half * dh + d];
-    float sc = src[co * dh + half * dh + d];
-    if (p.ape) sc += p.ape[(size_t)(pp % r) * co * dh + half * dh + d];
-    const float nm = fmaxf(m, sc);
-    const float corr = expf(m - nm);
-    const float e = expf(sc - nm);
-    ssum = ssum * corr + e;
-    acc = acc * corr + e * kv;
-    m = nm;
+  {
+    const int q4 = (threadIdx.x & 127) * 4, lane4 = threadIdx.x >> 7;
+    float m[4], ss[4], ac[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m[k] = -INFINITY, ss[k] = 0.f, ac[k] = 0.f;
+    const int first = g * r - (co - 1) * r;
+#pragma unroll 4
+    for (int pp = first + lane4; pp < (g + 1) * r; pp += 4) {
+      if (pp < 0) continue;
+      const int half = (pp < g * r) ? 0 : (co - 1);
+      const float* src = (pp >= cs) ? p.proj + (size_t)(row0 + pp - cs) * width
+                                    : p.ring + ((size_t)slot * depth + (pp % depth)) * width;
+      const float4 kv = *reinterpret_cast<const float4*>(src + half * dh + q4);
+      float4 sc = *reinterpret_cast<const float4*>(src + co * dh + half * dh + q4);
+      if (p.ape) {
+        const float4 a = *reinterpret_cast<const float4*>(p.ape + (size_t)(pp % r) * co * dh + half * dh + q4);
+        sc.x += a.x, sc.y += a.y, sc.z += a.z, sc.w += a.w;
+      }
+      const float scv[4] = {sc.x, sc.y, sc.z, sc.w}, kvv[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float nm = fmaxf(m[k], scv[k]);
+        const float corr = expf(m[k] - nm);
+        const float e = expf(scv[k] - nm);
+        ss[k] = ss[k] * corr + e;
+        ac[k] = ac[k] * corr + e * kvv[k];
+        m[k] = nm;
+      }
+    }
+    sm_m[lane4][threadIdx.x & 127] = make_float4(m[0], m[1], m[2], m[3]);
+    sm_s[lane4][threadIdx.x & 127] = make_float4(ss[0], ss[1], ss[2], ss[3]);
+    sm_a[lane4][threadIdx.x & 127] = make_float4(ac[0], ac[1], ac[2], ac[3]);
+  }
+  __syncthreads();
+  float acc = 0.f, ssum = 0.f;
+  {
+    const int q = d >> 2, k = d & 3;
+    float mj[4], M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mj[j] = reinterpret_cast<const float*>(&sm_m[j][q])[k];
+      M = fmaxf(M, mj[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (mj[j] == -INFINITY) continue;   // lane saw no slot
+      const float w = expf(mj[j] - M);
+      ssum += reinterpret_cast<const float*>(&sm_s[j][q])[k] * w;
+      acc += reinterpret_cast<const float*>(&sm_a[j][q])[k] * w;
+    }
   }
   const float pooled = __bfloat162float(__float2bfloat16(acc / ssum));
   const float ss = block_sum<512>(pooled * pooled, red);
@@ -97,11 +133,30 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
   if (p.wk == nullptr) return;
   // ---- indexer key: k = bf16(latent @ wk^T) -> RMSNorm -> RoPE -> e2m1 (ue8m0 / 32)
   const int kd = p.idx_dim;
-  if (d < kd) {
-    float a = 0.f;
-    const __nv_bfloat16* wr = p.wk + (size_t)d * dh;
-    for (int j = 0; j < dh; ++j) a += __bfloat162float(lat[j]) * __bfloat162float(wr[j]);
-    kbuf[d] = __bfloat162float(__float2bfloat16(a));
+  {
+    // warp-cooperative GEMV: warp w computes outputs w, w+16, ...; lanes split the 512 inputs
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float lv[16];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(lat + c * 256 + lane * 8);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) lv[c * 8 + e] = __bfloat162float(b[e]);
+    }
+    for (int o = warp; o < kd; o += 16) {
+      const __nv_bfloat16* wr = p.wk + (size_t)o * dh;
+      float a = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(wr + c * 256 + lane * 8);
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a += lv[c * 8 + e] * __bfloat162float(b[e]);
+      }
+      a = warp_sum(a);
+      if (lane == 0) kbuf[o] = __bfloat162float(__float2bfloat16(a));
+    }
   }
   __syncthreads();
   const float kv = d < kd ? kbuf[d] : 0.f;
@@ -136,7 +191,9 @@ __global__ void ring_update_kernel(T* ring, int depth, int width, const T* src, 
   const int t = blockIdx.x;
   if (t >= T_) return;
   const int ps = pos[t];
-  if (ps <= last_pos[t] - depth) return;  // overwritten later in the same step
+  // rows past last_pos are not committed (rejected draft tokens of a verify step);
+  // rows more than depth before it are overwritten later in the same step
+  if (ps > last_pos[t] || ps <= last_pos[t] - depth) return;
   T* dst = ring + ((size_t)slot[t] * depth + (ps % depth)) * width;
   const T* s = src + (size_t)t * width;
   for (int i = threadIdx.x; i < width; i += blockDim.x) dst[i] = s[i];

@@ -58,7 +58,7 @@ __global__ void engram_ring_kernel(EngramParams p) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= p.T) return;
   const int pos = p.pos[t];
-  if (pos <= p.last_pos[t] - (p.N - 1)) return;
+  if (pos > p.last_pos[t] || pos <= p.last_pos[t] - (p.N - 1)) return;
   p.ring[(size_t)p.slot[t] * (p.N - 1) + pos % (p.N - 1)] = p.token_map[p.ids[t]];
 }
 
@@ -87,13 +87,14 @@ __global__ void engram_gather_kernel(EngramParams p) {
   }
 }
 
-cudaError_t engram_prepare(const EngramParams& p, bool gather, cudaStream_t st) {
+cudaError_t engram_prepare(const EngramParams& p, int mode, cudaStream_t st) {
+  // mode: bit 0 hash, bit 1 ring update, bit 2 gather
   if (p.T == 0) return cudaSuccess;
   if (p.N < 2 || p.N > 8 || p.nl > kEngramMaxLayers || p.hd % 32 || ((p.N - 1) * p.H * p.hd) % 128)
     return cudaErrorInvalidValue;
-  engram_hash_kernel<<<(p.T * p.nl + 127) / 128, 128, 0, st>>>(p);
-  engram_ring_kernel<<<(p.T + 127) / 128, 128, 0, st>>>(p);
-  if (gather) {
+  if (mode & 1) engram_hash_kernel<<<(p.T * p.nl + 127) / 128, 128, 0, st>>>(p);
+  if (mode & 2) engram_ring_kernel<<<(p.T + 127) / 128, 128, 0, st>>>(p);
+  if (mode & 4) {
     const long long total = (long long)p.T * p.nl * (p.N - 1) * p.H * (p.hd / 16);
     engram_gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
   }

@@ -65,6 +65,9 @@ struct AttnParams {
   const int* comp_idx;              // [T, comp_k] selected compressed rows (null = dense 0..cnt)
   int comp_k;
   const int* comp_cnt;              // [T] number of valid compressed rows
+  const int* win_end;               // optional last window position per token (default pos): a
+                                    // draft block attends to all of its rows (bidirectional)
+  int win_len;                      // window rows (default W)
   const float* sink;                // [64]
   float scale;
   __nv_bfloat16* out;               // [T, 64, 512]
@@ -225,7 +228,7 @@ struct EngramParams {
   uint8_t* a_sf;                    // [nl] x scale chunks
   size_t a_stride_q, a_stride_sf;   // per-layer strides (bytes)
 };
-cudaError_t engram_prepare(const EngramParams& p, bool gather, cudaStream_t st);
+cudaError_t engram_prepare(const EngramParams& p, int mode, cudaStream_t st);   // bits: 1 hash, 2 ring, 4 gather
 cudaError_t engram_gate(__nv_bfloat16* X, const __nv_bfloat16* kv, const float* wgt, int T, int D, int hc, float eps,
                         cudaStream_t st);
 
@@ -233,5 +236,7 @@ cudaError_t engram_gate(__nv_bfloat16* X, const __nv_bfloat16* kv, const float* 
 cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
                           cudaStream_t st);
 cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st);
+cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
+                        int* toks, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st);
 
 }  // namespace dsv4

@@ -120,11 +120,21 @@ class EngramRuntime:
             self.wgt.append((qw.float() * kw.float()).to(dev).contiguous())
         self.table_addrs = torch.tensor([[t.dq, t.dsf, t.n] for t in self.tables], dtype=torch.int64)
 
-    def prepare(self, model, T: int) -> None:
-        """Hashes this step's tokens and gathers every Engram layer's rows from host memory."""
+    def prepare(self, model, T: int, update_ring: bool = True) -> None:
+        """Hashes this step's tokens and gathers every Engram layer's rows from host memory.
+
+        ``update_ring=False`` (speculative verify) leaves the token ring untouched;
+        :meth:`commit_ring` then stores only the accepted tokens.
+        """
         self.ext.engram_prepare(model.m_ids, model.m_pos, model.m_slot, model.m_cstart, model.m_row0, model.m_last,
                                 T, self.token_map, self.ring, self.mult, self.primes, self.offsets, self.pad,
-                                self.rows, self.table_addrs, self.a_q, self.a_sf, self.hd)
+                                self.rows, self.table_addrs, self.a_q, self.a_sf, self.hd, 7 if update_ring else 5)
+
+    def commit_ring(self, model, T: int, last_pos: torch.Tensor) -> None:
+        """Stores the ring tokens of positions <= last_pos (per token) from the last step's ids."""
+        self.ext.engram_prepare(model.m_ids, model.m_pos, model.m_slot, model.m_cstart, model.m_row0, last_pos,
+                                T, self.token_map, self.ring, self.mult, self.primes, self.offsets, self.pad,
+                                self.rows, None, None, None, self.hd, 2)
 
     def apply(self, model, lid: int, T: int) -> None:
         """X += gate * value for Engram layer ``lid`` (rows gathered by :meth:`prepare`)."""

@@ -46,7 +46,8 @@ class SeqChunk:
     slot: int
     start_pos: int
     tokens: list[int]
-    sample: bool = True   # produce logits for the last token of the chunk
+    sample: bool = True        # produce logits for the last token of the chunk
+    sample_all: bool = False   # produce logits for every token (speculative verify, draft blocks)
 
 
 class StepMeta:
@@ -72,7 +73,13 @@ class StepMeta:
         self.chunk_start = np.repeat(starts, lens).astype(np.int32)
         self.step_row0 = np.repeat(row0, lens).astype(np.int32)
         self.last_pos = np.repeat(starts + lens - 1, lens).astype(np.int32)
-        self.sample_rows = (row0 + lens - 1)[samp].astype(np.int32)
+        sall = np.fromiter((c.sample_all for c in chunks), bool, n)
+        if sall.any():
+            rows = [np.arange(row0[i], row0[i] + lens[i]) if sall[i] else
+                    (np.array([row0[i] + lens[i] - 1]) if samp[i] else np.zeros(0, np.int64)) for i in range(n)]
+            self.sample_rows = np.concatenate(rows).astype(np.int32)
+        else:
+            self.sample_rows = (row0 + lens - 1)[samp].astype(np.int32)
         self.max_pos = int(self.pos.max()) if T else 0
         # compressor groups closed in this step, per ratio (token order)
         self.groups = {}
@@ -330,9 +337,21 @@ class DSV4Model:
     sinkhorn_iters = None
 
     # --------------------------------------------------------------- forward
-    def forward(self, m: StepMeta, taps: dict | None = None, trace: dict | None = None) -> torch.Tensor:
-        """Runs one step whose metadata is already uploaded; returns next ids [n_sample] (device)."""
+    def forward(self, m: StepMeta, taps: dict | None = None, trace: dict | None = None,
+                defer_rings: bool = False) -> torch.Tensor:
+        """Runs one step whose metadata is already uploaded; returns next ids [n_sample] (device).
+
+        ``taps``: {layer id: [T, D] bf16 buffer} receives the mean of the four
+        streams entering that layer (the DSpark drafter's main hidden).
+        ``defer_rings``: a speculative verify step; the per-sequence rings
+        (attention window, compressor projections, Engram tokens) are left as
+        they are and this step's rows are parked, so that :meth:`commit_rings`
+        stores only the accepted prefix.  Position-indexed caches (compressed
+        KV, indexer keys) are written as usual: an entry of a rejected token
+        is rewritten before any later token can read it.
+        """
         cfg = self.cfg
+        self._defer = defer_rings
         if self.sinkhorn_iters is None:
             self.sinkhorn_iters = cfg.hc_sinkhorn_iters
         T = m.T
@@ -342,7 +361,7 @@ class DSV4Model:
         eng = self.engram
         if eng is not None:
             with self._t("engram_gather"):
-                eng.prepare(self, T)
+                eng.prepare(self, T, update_ring=not defer_rings)
         prev, cw = None, self.mix0
         moe_state = None
         for li, L in enumerate(self.layers):
@@ -389,11 +408,41 @@ class DSV4Model:
             ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S])
         return self.next_ids[:S]
 
+    # ------------------------------------------------- deferred ring commits
+    _defer = False
+    pending_rows = 256
+
+    def _pending(self, kind: str, lid: int, src: torch.Tensor, T: int) -> None:
+        if T > self.pending_rows:
+            raise ValueError(f"deferred-ring step of {T} tokens exceeds {self.pending_rows}")
+        store = self.__dict__.setdefault("_pend", {})
+        buf = store.get((kind, lid))
+        if buf is None:
+            buf = torch.empty(self.pending_rows, src.shape[1], dtype=src.dtype, device=self.dev)
+            store[(kind, lid)] = buf
+        buf[:T].copy_(src[:T])
+
+    def commit_rings(self, T: int, last_commit: torch.Tensor) -> None:
+        """After a deferred (verify) step: store the rows of positions <= last_commit[t]
+        into every ring.  The step's metadata must still be the uploaded one."""
+        ext = self.ext
+        for (kind, lid), buf in self.__dict__.get("_pend", {}).items():
+            ring = self.ring[lid] if kind == "kv" else self.comp_ring[lid]
+            ext.ring_update(ring, buf, T, self.m_slot, self.m_pos, last_commit)
+        if self.engram is not None:
+            self.engram.commit_ring(self, T, last_commit)
+
     # ------------------------------------------------------------- attention
-    def _attention(self, L: LayerW, m: StepMeta):
+    def _attention(self, L: LayerW, m: StepMeta, ring: torch.Tensor | None = None, win_len: int = 0):
+        """Attention sublayer.  ``ring``/``win_len``: a DSpark draft stage attends to its
+        own ring plus every row of the draft block (window ending at the block's
+        last position) and stores nothing."""
         cfg, ext = self.cfg, self.ext
         T = m.T
         lid = L.layer_id
+        draft = ring is not None
+        if ring is None:
+            ring = self.ring[lid]
         r = cfg.ratio(lid)
         cos, sin = self.rope["yarn" if r > 0 else "swa"]
         qa = cfg.q_lora_rank
@@ -433,12 +482,18 @@ class DSV4Model:
             splits = 8
         tctx = self._t("attention")
         tctx.__enter__()
-        ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, self.ring[lid], comp,
+        ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, ring, comp,
                       self.m_slot, self.m_pos, self.m_cstart, self.m_row0, comp_idx, comp_cnt, L.sink,
-                      cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits)
+                      cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits,
+                      self.m_last if draft else None, win_len)
         tctx.__exit__(None, None, None)
-        with self._t("ring_update"):
-            ext.ring_update(self.ring[lid], self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
+        if draft:
+            pass
+        elif self._defer:
+            self._pending("kv", lid, self.kv_step, T)
+        else:
+            with self._t("ring_update"):
+                ext.ring_update(ring, self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
         with self._t("gemm_wo_a"):
             self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=cfg.o_groups)
         with self._t("quant_oa"):
@@ -464,8 +519,11 @@ class DSV4Model:
                 ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
                                   self.comp_ring[lid], L.comp_norm, cfg.rms_norm_eps, cos, sin, self.comp[lid],
                                   L.idx_wk, L.idx_knorm, self.idx_cache.get(lid) if L.idx_wk is not None else None)
-        with self._t("comp_ring"):
-            ext.ring_update(self.comp_ring[lid], proj, T, self.m_slot, self.m_pos, self.m_last)
+        if self._defer:
+            self._pending("proj", lid, proj, T)
+        else:
+            with self._t("comp_ring"):
+                ext.ring_update(self.comp_ring[lid], proj, T, self.m_slot, self.m_pos, self.m_last)
 
     def _indexer(self, L: LayerW, m: StepMeta, r: int):
         cfg, ext = self.cfg, self.ext

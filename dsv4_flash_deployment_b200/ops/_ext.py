@@ -37,7 +37,8 @@ _KERNELS_PER_CALL = {"hc_post": 1, "hc_finish": 1, "attention": 1, "gemm": 1, "a
                      "compress_pool": 1, "ring_update": 1, "router_topk": 1, "moe_plan": 1, "moe_scatter": 1,
                      "indexer_topk": 1, "embed_streams": 1, "argmax_rows": 1, "act_roundtrip": 1,
                      "fp4_roundtrip": 1, "ep_pack": 1, "ep_unpack_meta": 1, "ep_unpack_rows": 1,
-                     "ep_combine_pack": 1, "ep_wait": 1, "engram_gate": 1, "engram_prepare": 2}
+                     "ep_combine_pack": 1, "ep_wait": 1, "engram_gate": 1, "engram_prepare": 2,
+                     "markov_step": 1}
 
 
 class _Counting:
@@ -59,8 +60,8 @@ class _Counting:
                 n = k
                 if name == "attention" and len(a) > 20 and a[20] > 1:
                     n = 2
-                if name == "engram_prepare" and len(a) > 14 and a[14] is not None:
-                    n = 3   # hash + ring + gather
+                if name == "engram_prepare":
+                    n = bin(int(a[18])).count("1")   # one kernel per mode bit (hash, ring, gather)
                 self.count += n
             return fn(*a, **kw)
 
