@@ -30,6 +30,7 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=None, help="override routed experts (small profiling cases)")
     ap.add_argument("--topk", type=int, default=None)
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"])
+    ap.add_argument("--decode-only", action="store_true", help="C decoding sequences per rank, no prefill chunk")
     a = ap.parse_args()
     import os
 
@@ -52,19 +53,20 @@ def main() -> None:
         kw["n_activated_experts"] = a.topk
     cfg = v4_flash_config(**kw)
     dev = torch.device("cuda", local)
-    n_dec = a.concurrency // world - 1
-    chunk = a.chunk // world
+    n_dec = a.concurrency // world - (0 if a.decode_only else 1)
+    chunk = 0 if a.decode_only else a.chunk // world
     T = n_dec + chunk
     n_phys = plan_expert_storage(cfg, dev, T, n_dec + 2, 2048, world)
     eng = Engine.build(cfg, dev, max_seqs=n_dec + 2, max_batched_tokens=T, max_seq_len=2048,
                        expert_storage_layers=n_phys, use_graphs=False, ep=ep)
     m = eng.model
     rng = np.random.default_rng(0)
-    dec = 1024 + (np.arange(n_dec) * (1024 // n_dec) + 1) % 1024
+    dec = 1024 + (np.arange(n_dec) * (1024 // max(1, n_dec)) + 1) % 1024
 
     def meta(i):
         ch = [SeqChunk(s, int(dec[s]) + i, [int(rng.integers(0, cfg.vocab_size))], True) for s in range(n_dec)]
-        ch.append(SeqChunk(n_dec, (i % 2) * chunk, rng.integers(0, cfg.vocab_size, chunk).tolist(), i % 2 == 1))
+        if chunk:
+            ch.append(SeqChunk(n_dec, (i % 2) * chunk, rng.integers(0, cfg.vocab_size, chunk).tolist(), i % 2 == 1))
         return StepMeta(cfg, ch)
 
     eng.run_meta(meta(0))

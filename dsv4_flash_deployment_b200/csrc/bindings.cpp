@@ -537,7 +537,8 @@ void markov_step(const Tensor& logits, int64_t blk, int64_t i, const Tensor& mlo
                  const Tensor& toks, const Tensor& memb, const Tensor& emb) {
   CUDA_OK(dsv4::markov_step(ptr<const float>(logits), (int)logits.stride(0), (int)blk, (int)i,
                             ptr<const float>(mlog), (int)mlog.stride(0), (int)V, (int)n, ptr<int>(toks),
-                            ptr<const bf16>(memb), (int)memb.size(1), ptr<bf16>(emb), cur_stream()));
+                            (int)toks.stride(0), ptr<const bf16>(memb), (int)memb.size(1), ptr<bf16>(emb),
+                            cur_stream()));
 }
 
 void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out) {

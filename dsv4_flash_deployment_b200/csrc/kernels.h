@@ -237,6 +237,6 @@ cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int
                           cudaStream_t st);
 cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st);
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
-                        int* toks, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st);
+                        int* toks, int ts, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st);
 
 }  // namespace dsv4

@@ -73,13 +73,13 @@ cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cud
 namespace dsv4 {
 
 // One DSpark Markov-head step per sequence j (reference.py:1216-1247):
-//   i >= 0: tok = argmax_v(logits[(j*blk + i), v] + mlog[j, v]), toks[(i+1)*n + j] = tok
-//   i <  0: tok = toks[j] (the root)
+//   i >= 0: tok = argmax_v(logits[(j*blk + i), v] + mlog[j, v]), toks[i+1][j] = tok
+//   i <  0: tok = toks[0][j] (the root)      (toks rows are ts apart)
 // then emb[j, :] = memb[tok, :] (the next step's rank-R input).
 __global__ void __launch_bounds__(512) markov_step_kernel(const float* __restrict__ logits, int ld, int blk, int i,
                                                           const float* __restrict__ mlog, int mld, int V, int n,
-                                                          int* toks, const __nv_bfloat16* __restrict__ memb, int R,
-                                                          __nv_bfloat16* emb) {
+                                                          int* toks, int ts, const __nv_bfloat16* __restrict__ memb,
+                                                          int R, __nv_bfloat16* emb) {
   const int j = blockIdx.x;
   __shared__ int s_tok;
   if (i >= 0) {
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(512) markov_step_kernel(const float* __restric
           bv = sv[w];
           bi = si[w];
         }
-      toks[(size_t)(i + 1) * n + j] = bi;
+      toks[(size_t)(i + 1) * ts + j] = bi;
       s_tok = bi;
     }
   } else if (threadIdx.x == 0) {
@@ -129,9 +129,9 @@ __global__ void __launch_bounds__(512) markov_step_kernel(const float* __restric
 }
 
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
-                        int* toks, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st) {
+                        int* toks, int ts, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  markov_step_kernel<<<n, 512, 0, st>>>(logits, ld, blk, i, mlog, mld, V, n, toks, memb, R, emb);
+  markov_step_kernel<<<n, 512, 0, st>>>(logits, ld, blk, i, mlog, mld, V, n, toks, ts, memb, R, emb);
   return cudaGetLastError();
 }
 

