@@ -56,24 +56,40 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
+    def __init__(self, gpus: str):
+        self.gpus = gpus
         self.proc = None
         self.path = None
+
+    def _lines(self) -> int:
+        try:
+            with open(self.path) as f:
+                return sum(1 for _ in f)
+        except OSError:
+            return 0
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # the sampler needs a moment to start: wait for its first sample
+        t0 = time.time()
+        while self.proc is not None and self._lines() == 0 and time.time() - t0 < 5:
+            time.sleep(0.02)
+        self.n0 = self._lines()
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # make sure at least one sample was taken after the timed work started
+            t0 = time.time()
+            while self._lines() <= self.n0 and time.time() - t0 < 1.0:
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -92,6 +108,8 @@ class ClockSampler:
         finally:
             if self.path:
                 os.unlink(self.path)
+        if len(rows) > getattr(self, "n0", 0):
+            rows = rows[self.n0:]          # samples taken after the timed work started
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in rows]
@@ -192,7 +210,10 @@ def main() -> None:
     metas = [make_meta() for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    # rank 0 samples every GPU of the job (the timed region of a short run can
+    # be a fraction of a second; samples from the whole timed loop are kept)
+    smi_ids = ",".join(str(i) for i in range(world)) if world > 1 else str(local)
+    with ClockSampler(smi_ids if rank == 0 else str(local)) as clk:
         if group is not None:
             dist.barrier()
         torch.cuda.synchronize()

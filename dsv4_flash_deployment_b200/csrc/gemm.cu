@@ -259,9 +259,12 @@ __global__ void __launch_bounds__(192, 1)
           if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
           else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_ld_wait();
-          float* dst = ws_tile + (size_t)t.split * 128 * BN;
+          // row-major partial tile: each thread stores whole 16-byte column groups of its row
+          float4* dst = reinterpret_cast<float4*>(ws_tile + (size_t)t.split * 128 * BN + (size_t)row * BN + c0);
 #pragma unroll
-          for (int j = 0; j < kCols; ++j) dst[(c0 + j) * 128 + row] = __uint_as_float(r[j]);
+          for (int j = 0; j < kCols / 4; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
         }
         tc_fence_before();
         __syncwarp();
@@ -287,12 +290,32 @@ __global__ void __launch_bounds__(192, 1)
       for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
         float v[32];
         if (split) {
+          // fixed summation order s = 0..splits-1 (deterministic); two splits' loads in flight
 #pragma unroll
           for (int j = 0; j < kCols; ++j) v[j] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float* src = ws_tile + (size_t)s * 128 * BN;
+          int s = 0;
+          for (; s + 1 < p.splits; s += 2) {
+            const float4* a = reinterpret_cast<const float4*>(ws_tile + (size_t)s * 128 * BN + (size_t)row * BN + c0);
+            const float4* b = reinterpret_cast<const float4*>(ws_tile + (size_t)(s + 1) * 128 * BN +
+                                                              (size_t)row * BN + c0);
+            float4 x[kCols / 4], y[kCols / 4];
 #pragma unroll
-            for (int j = 0; j < kCols; ++j) v[j] += __ldcg(src + (c0 + j) * 128 + row);
+            for (int j = 0; j < kCols / 4; ++j) x[j] = __ldcg(a + j);
+#pragma unroll
+            for (int j = 0; j < kCols / 4; ++j) y[j] = __ldcg(b + j);
+#pragma unroll
+            for (int j = 0; j < kCols / 4; ++j) {
+              v[4 * j] += x[j].x, v[4 * j + 1] += x[j].y, v[4 * j + 2] += x[j].z, v[4 * j + 3] += x[j].w;
+              v[4 * j] += y[j].x, v[4 * j + 1] += y[j].y, v[4 * j + 2] += y[j].z, v[4 * j + 3] += y[j].w;
+            }
+          }
+          if (s < p.splits) {
+            const float4* a = reinterpret_cast<const float4*>(ws_tile + (size_t)s * 128 * BN + (size_t)row * BN + c0);
+#pragma unroll
+            for (int j = 0; j < kCols / 4; ++j) {
+              const float4 x = __ldcg(a + j);
+              v[4 * j] += x.x, v[4 * j + 1] += x.y, v[4 * j + 2] += x.z, v[4 * j + 3] += x.w;
+            }
           }
         } else {
           uint32_t r[32];

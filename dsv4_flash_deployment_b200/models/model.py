@@ -182,7 +182,8 @@ class DSV4Model:
         self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
         # 128-row expert tiles keep two accumulators in TMEM (epilogue overlaps the
         # next tile); 256-row tiles halve weight re-reads when experts get many rows
-        self.tile_rows = 128 if recv_rows <= 192 * e_local else 256
+        # (decided on the expected rows per rank, T*k, not on the worst-case capacity)
+        self.tile_rows = 128 if T * k <= 192 * e_local else 256
         tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
         I = cfg.moe_inter_dim
         self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)

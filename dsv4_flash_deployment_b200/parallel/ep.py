@@ -14,8 +14,9 @@ Transports: ``nccl`` = ``all_to_all_single`` over fixed-capacity per-peer
 regions (the baseline; no host synchronization, graph-capturable); ``p2p`` =
 the pack/combine kernels store records straight into the peer's receive
 buffer through NVLink (symmetric memory) and a device barrier orders the two
-sides.  Capacity per peer is ``2 * T * k / world`` pairs (+64); overflow is
-reported through the device error word, never dropped silently.
+sides.  Capacity per peer is the worst case ``T * k`` pairs (every pair of a rank
+to one peer), so no routing can overflow; an overflow would be reported
+through the device error word, never dropped silently.
 """
 
 from __future__ import annotations
@@ -44,7 +45,10 @@ class EPGroup:
         return n_experts // self.world
 
     def cap_per_peer(self, T: int, k: int) -> int:
-        return ceil_to(2 * T * k // self.world + 64, 16)
+        # worst case: every routed pair of this rank goes to one peer (a token's k
+        # experts are distinct, so T*k bounds it).  Random-init routers are skewed
+        # enough to exceed 2x the average; the bound costs ~35 MB per rank.
+        return ceil_to(T * k, 16)
 
     def recv_rows(self, T: int, k: int) -> int:
         return self.world * self.cap_per_peer(T, k)
