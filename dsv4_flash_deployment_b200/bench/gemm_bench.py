@@ -25,6 +25,10 @@ SHAPES = [
     ("wq_b/dec1", 32768, 1024, 1),
     ("wo_b/dec1", 4096, 8192, 1),
     ("wq_b/dec64", 32768, 1024, 64),
+    ("wqkv_a/127", 1536, 4096, 127),
+    ("wq_b/127", 32768, 1024, 127),
+    ("wo_b/127", 4096, 8192, 127),
+    ("shared_w2/127", 4096, 2048, 127),
     ("expert_w13/16", 4096, 4096, 16),
     ("wo_b/512", 4096, 8192, 512),
     ("wq_b/1024", 32768, 1024, 1024),
@@ -62,12 +66,11 @@ def run(shapes=SHAPES, iters: int = 20) -> list[dict]:
         out = torch.empty(t, n, dtype=torch.bfloat16, device=dev)
         bn = G.pick_bn(t)
         tiles = ceil_to(n, 128) // 128 * ((t + bn - 1) // bn)
-        splits = max(1, min(k // 128 // 4, 148 // max(1, tiles))) if tiles < 148 else 1
-        wsp = torch.empty(tiles * splits * 128 * bn, dtype=torch.float32, device=dev)
-        cnt = torch.zeros(tiles, dtype=torch.int32, device=dev)
+        # the engine's policy: split-K inside a thread-block cluster for few output tiles
+        splits = max(1, min(8, (k // 128) // 2, 148 // max(1, tiles))) if tiles < 100 else 1
 
         def ours(i):
-            G.gemm_mx(xq, xsf, t, ws[i % copies], out, G.EPI_BF16, splits=splits, workspace=wsp, counters=cnt)
+            G.gemm_mx(xq, xsf, t, ws[i % copies], out, G.EPI_BF16, splits=splits)
 
         for i in range(3):
             ours(i)
@@ -97,5 +100,7 @@ def run(shapes=SHAPES, iters: int = 20) -> list[dict]:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", default=None, help="comma-separated shape names")
     a = ap.parse_args()
-    run(iters=a.iters)
+    sel = SHAPES if not a.only else [x for x in SHAPES if x[0] in a.only.split(",")]
+    run(sel, iters=a.iters)

@@ -105,7 +105,18 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.workspace = workspace ? workspace->data_ptr<float>() : nullptr;
   p.tile_counters = counters ? counters->data_ptr<int>() : nullptr;
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
-  if (p.splits > 1) TORCH_CHECK(workspace && counters, "split-K needs workspace and counters");
+  if (p.splits > 1 && !(workspace && counters)) {
+    // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
+    // Halve the split count until every tile's cluster is resident at once.
+    TORCH_CHECK(!grouped, "cluster split-K: dense GEMMs only");
+    TORCH_CHECK(M % 128 == 0, "M must be a multiple of 128");
+    const int tiles = (int)(M / 128) * (int)((N + bn - 1) / bn);
+    int s = 1;
+    while (s * 2 <= std::min(p.splits, 8)) s *= 2;
+    while (s >= 2 && dsv4::gemm_max_clusters((int)kind, (int)epi, (int)bn, s) < tiles) s /= 2;
+    p.splits = s >= 2 ? s : 1;
+    p.cluster_split = p.splits > 1;
+  }
   int units;
   if (grouped) {
     p.tiles = reinterpret_cast<const int4*>(tiles->data_ptr<int>());
@@ -117,7 +128,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
     units = p.n_tiles * p.splits;
   }
   if (units == 0) return;
-  int grid = std::min(units, max_grid > 0 ? (int)max_grid : num_sms());
+  int grid = p.cluster_split ? units : std::min(units, max_grid > 0 ? (int)max_grid : num_sms());
   CUDA_OK(dsv4::gemm_launch((int)kind, (int)epi, grouped, (int)bn, ta, tb, p, grid, cur_stream()));
 }
 

@@ -20,8 +20,13 @@
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
 // issuer (one elected lane), warps 2..5 = epilogue (each reads the TMEM lane
 // quadrant it is allowed to access).  The kernel is persistent over a tile list
-// (dense: computed; grouped/MoE: device tile records), with optional split-K
-// whose partial sums are reduced deterministically by the last-arriving CTA.
+// (dense: computed; grouped/MoE: device tile records), with optional split-K.
+// Split-K reduces deterministically (fixed summation order over splits), either
+// through a global workspace by the last-arriving CTA, or -- the default for
+// dense GEMMs -- inside a thread-block cluster: the S splits of a tile are one
+// cluster, each parks its fp32 partial tile in its own (now idle) pipeline
+// shared memory, and after a cluster barrier CTA r reduces column chunks
+// r, r+S, ... by reading all S partials over distributed shared memory.
 //
 // Epilogues: bf16 store, fp32 store, and SwiGLU-requant for expert W13 tiles
 // whose rows are [64 gate rows; 64 up rows]: h = silu(min(g, L)) * clip(u, L) *
@@ -122,6 +127,8 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const bool csplit = p.cluster_split != 0 && p.splits > 1;
+  int csyncs = 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -251,8 +258,31 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t d_tmem = tmem + acc * L::kAccCols;
       const bool split = p.splits > 1;
       constexpr int kCols = BN < 32 ? BN : 32;
-      float* ws_tile = split ? p.workspace + (size_t)t.tile * p.splits * 128 * BN : nullptr;
-      if (split) {
+      constexpr int kPS = BN + 4;   // padded row stride of a parked partial tile (floats)
+      float* ws_tile = split && !csplit ? p.workspace + (size_t)t.tile * p.splits * 128 * BN : nullptr;
+      int c_begin = 0, c_step = kCols;
+      if (csplit) {
+        // park this split's partial (row-major, 16-byte stores) in the idle stage buffers
+        float* part = reinterpret_cast<float*>(smem);
+        for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+          uint32_t r[32];
+          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(part + (size_t)row * kPS + c0);
+#pragma unroll
+          for (int j = 0; j < kCols / 4; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        cluster_sync_all();   // every split's partial is parked
+        ++csyncs;
+        c_begin = kCols * (int)cluster_ctarank();
+        c_step = kCols * p.splits;
+      } else if (split) {
         // Publish this split's partial tile, then let the last arrival reduce.
         for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
           uint32_t r[32];
@@ -287,9 +317,23 @@ __global__ void __launch_bounds__(192, 1)
         }
         __threadfence();
       }
-      for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+      for (int c0 = c_begin; c0 < t.n_eff; c0 += c_step) {
         float v[32];
-        if (split) {
+        if (csplit) {
+          // fixed summation order s = 0..splits-1 over the cluster's parked partials
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) v[j] = 0.f;
+          const uint32_t local = smem_u32(reinterpret_cast<float*>(smem) + (size_t)row * kPS + c0);
+          for (int s = 0; s < p.splits; ++s) {
+            const uint32_t ra = dsmem_map(local, (uint32_t)s);
+            float4 x[kCols / 4];
+#pragma unroll
+            for (int j = 0; j < kCols / 4; ++j) x[j] = dsmem_ld_f4(ra + 16 * j);
+#pragma unroll
+            for (int j = 0; j < kCols / 4; ++j)
+              v[4 * j] += x[j].x, v[4 * j + 1] += x[j].y, v[4 * j + 2] += x[j].z, v[4 * j + 3] += x[j].w;
+          }
+        } else if (split) {
           // fixed summation order s = 0..splits-1 (deterministic); two splits' loads in flight
 #pragma unroll
           for (int j = 0; j < kCols; ++j) v[j] = 0.f;
@@ -399,6 +443,10 @@ __global__ void __launch_bounds__(192, 1)
           asm volatile("bar.sync 1, 128;" ::: "memory");
         }
       }
+      if (csplit) {
+        cluster_sync_all();   // the cluster has finished reading this CTA's partial
+        ++csyncs;
+      }
       if (!split) {
         tc_fence_before();
         __syncwarp();
@@ -412,6 +460,14 @@ __global__ void __launch_bounds__(192, 1)
   }
 done:
   __syncwarp();
+  // cluster split: every thread takes part in exactly two cluster barriers (the
+  // epilogue's, or here for the producer/MMA warps and after an abort), so no
+  // CTA of the cluster can be left waiting
+  if (csplit)
+    while (csyncs < 2) {
+      cluster_sync_all();
+      ++csyncs;
+    }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -438,6 +494,22 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  if (p.cluster_split && p.splits > 1) {
+    // one CTA per (tile, split); the splits of a tile are one cluster
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, ta, tb, p);
+  }
   k<<<grid, 192, L::kTotal, st>>>(ta, tb, p);
   return cudaGetLastError();
 }
@@ -452,6 +524,69 @@ static cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const BMaps& tb, c
     case 256: return launch_one<KIND, 256, EPI, GROUPED>(ta, tb, p, grid, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// How many clusters of `splits` CTAs of this kernel can be resident at once
+// (clusters live inside one GPC, so this is below SMs / splits).  Cached.
+template <int KIND, int BN, int EPI>
+static int cluster_cap(int splits) {
+  static int cache[9] = {0};
+  if (splits < 2 || splits > 8) return 0;
+  if (cache[splits]) return cache[splits];
+  using L = GemmSmem<BN>;
+  auto k = gemm_kernel<KIND, BN, EPI, false>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)splits);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cache[splits] = n;
+  return n;
+}
+
+template <int KIND, int EPI>
+static int cap_bn(int bn, int splits) {
+  switch (bn) {
+    case 32: return cluster_cap<KIND, 32, EPI>(splits);
+    case 64: return cluster_cap<KIND, 64, EPI>(splits);
+    case 128: return cluster_cap<KIND, 128, EPI>(splits);
+    case 256: return cluster_cap<KIND, 256, EPI>(splits);
+    default: return 0;
+  }
+}
+
+int gemm_max_clusters(int kind, int epi, int bn, int splits) {
+  if (kind == KIND_BF16) {
+    if (epi == EPI_BF16) return cap_bn<KIND_BF16, EPI_BF16>(bn, splits);
+    if (epi == EPI_F32) return cap_bn<KIND_BF16, EPI_F32>(bn, splits);
+    return 0;
+  }
+  if (kind == KIND_MX8) {
+    if (epi == EPI_BF16) return cap_bn<KIND_MX8, EPI_BF16>(bn, splits);
+    if (epi == EPI_F32) return cap_bn<KIND_MX8, EPI_F32>(bn, splits);
+    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX8, EPI_SWIGLU>(bn, splits);
+  }
+  if (kind == KIND_MX4A) {
+    if (epi == EPI_BF16) return cap_bn<KIND_MX4A, EPI_BF16>(bn, splits);
+    if (epi == EPI_F32) return cap_bn<KIND_MX4A, EPI_F32>(bn, splits);
+    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX4A, EPI_SWIGLU>(bn, splits);
+  }
+  return 0;
 }
 
 int gemm_smem_bytes(int bn) {

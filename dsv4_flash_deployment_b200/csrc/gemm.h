@@ -34,9 +34,12 @@ struct GemmParams {
   uint8_t* hsf;
   int h_ktiles;
   float swiglu_limit;
-  // split-K
+  // split-K: either partial tiles in a global workspace reduced by the last
+  // arriving CTA (workspace + tile_counters), or cluster_split: the splits of a
+  // tile form one thread-block cluster and reduce through distributed shared memory
   float* workspace;
   int* tile_counters;
+  int cluster_split;
   uint32_t* err;
 };
 
@@ -47,6 +50,7 @@ struct BMaps {
 };
 
 int gemm_smem_bytes(int bn);
+int gemm_max_clusters(int kind, int epi, int bn, int splits);   // resident clusters of `splits` CTAs
 cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorMap& ta, const BMaps& tb,
                         const GemmParams& p, int grid, cudaStream_t st);
 

@@ -245,22 +245,26 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
   }
 }
 
-// One warp per token.  Partials per slice: 48 projections (hi | lo rows of
-// hc_fn), sumsq(X'), sumsq(c); reduced here in slice order.
+// One CTA (4 warps) per token.  Partials per slice: 48 projections (hi | lo
+// rows of hc_fn), sumsq(X'), sumsq(c); every warp reduces them in slice order
+// (8 slices' loads in flight), warp 0 forms the mixes and runs Sinkhorn, and the
+// four warps share the RMSNorm + MXFP8 pass over the D columns.
 __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
+  const int t = blockIdx.x;
   if (t >= p.T) return;
   const int D = p.D;
   const float* part = p.partials + (size_t)t * n_slices * kNPart;
   float r0 = 0.f, r1 = 0.f;   // lane: columns lane and 32 + lane (< 50)
+  const bool hi_lane = lane + 32 < kNPart;
+#pragma unroll 8
   for (int s = 0; s < n_slices; ++s) {
     r0 += part[s * kNPart + lane];
-    if (lane + 32 < kNPart) r1 += part[s * kNPart + 32 + lane];
+    if (hi_lane) r1 += part[s * kNPart + 32 + lane];
   }
   const float ssx = __shfl_sync(0xffffffffu, r1, kNMix - 32);
   const float ssc = __shfl_sync(0xffffffffu, r1, kNMix + 1 - 32);
-  if (p.fn_hilo != nullptr) {
+  if (p.fn_hilo != nullptr && warp == 0) {
     // lanes 0-3 pre, 4-7 post, 16-31 comb[i][j] with i = (lane-16)/4, j = lane%4
     const int idx = lane < 8 ? lane : (lane >= 16 ? 8 + lane - 16 : -1);
     const float r = rsqrtf(ssx / (float)(HC * D) + p.norm_eps);
@@ -304,7 +308,8 @@ __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices
   // 256-column chunk; 4 lanes cover one 32-column scale block.
   const float rr = rsqrtf(ssc / (float)D + p.norm_eps);
   const __nv_bfloat16* c = p.c + (size_t)t * D;
-  for (int base = 0; base < D; base += 256) {
+#pragma unroll 2
+  for (int base = warp * 256; base < D; base += 1024) {
     const int d0 = base + lane * 8;
     const uint4 raw = *reinterpret_cast<const uint4*>(c + d0);
     const uint4 wr = *reinterpret_cast<const uint4*>(p.norm_w + d0);
@@ -359,7 +364,8 @@ cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
 
 cudaError_t hc_finish(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  hc_finish_kernel<<<(p.T + 3) / 4, 128, 0, st>>>(p, hc_num_slices(p.D));
+  if (p.D % 256) return cudaErrorInvalidValue;
+  hc_finish_kernel<<<p.T, 128, 0, st>>>(p, hc_num_slices(p.D));
   return cudaGetLastError();
 }
 

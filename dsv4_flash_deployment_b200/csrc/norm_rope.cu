@@ -11,21 +11,33 @@
 
 namespace dsv4 {
 
+// One CTA (4 warps) per token: every warp reduces the row's sums of squares
+// (16-byte loads), then warp w handles the 32-column blocks w, w+4, ... of both
+// parts.
 __global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
+  const int t = blockIdx.x;
   if (t >= p.T) return;
   const __nv_bfloat16* in = p.in + (size_t)t * (p.q_dim + p.kv_dim);
-  // ---- q part
-  {
+  auto sumsq = [&](const __nv_bfloat16* x, int n) {
     float ss = 0.f;
-    for (int d = lane; d < p.q_dim; d += 32) {
-      const float v = __bfloat162float(in[d]);
-      ss += v * v;
+#pragma unroll 4
+    for (int d = lane * 8; d < n; d += 256) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(x + d);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        ss += f.x * f.x + f.y * f.y;
+      }
     }
-    ss = warp_sum(ss);
+    return warp_sum(ss);
+  };
+  // ---- q part
+  if (p.q_dim > 0) {
+    const float ss = sumsq(in, p.q_dim);
     const float r = rsqrtf(ss / (float)p.q_dim + p.eps);
-    for (int b = 0; b < p.q_dim / 32; ++b) {
+    for (int b = warp; b < p.q_dim / 32; b += 4) {
       const int d = 32 * b + lane;
       const float y = __bfloat162float(__float2bfloat16(__bfloat162float(in[d]) * r *
                                                         __bfloat162float(p.q_norm_w[d])));
@@ -38,15 +50,10 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
   // ---- kv part
   {
     const __nv_bfloat16* kin = in + p.q_dim;
-    float ss = 0.f;
-    for (int d = lane; d < p.kv_dim; d += 32) {
-      const float v = __bfloat162float(kin[d]);
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
+    const float ss = sumsq(kin, p.kv_dim);
     const float r = rsqrtf(ss / (float)p.kv_dim + p.eps);
     const int pos = p.pos[t];
-    for (int b = 0; b < p.kv_dim / 32; ++b) {
+    for (int b = warp; b < p.kv_dim / 32; b += 4) {
       const int d = 32 * b + lane;
       float y = __bfloat162float(__float2bfloat16(__bfloat162float(kin[d]) * r * __bfloat162float(p.kv_norm_w[d])));
       if (d >= p.kv_dim - 64) {
@@ -68,7 +75,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
 
 cudaError_t qkv_post(const QkvParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  qkv_post_kernel<<<(p.T + 3) / 4, 128, 0, st>>>(p);
+  if (p.q_dim % 256 || p.kv_dim % 256) return cudaErrorInvalidValue;
+  qkv_post_kernel<<<p.T, 128, 0, st>>>(p);
   return cudaGetLastError();
 }
 

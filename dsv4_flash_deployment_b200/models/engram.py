@@ -43,6 +43,7 @@ class HostTable:
     def __init__(self, q: torch.Tensor, sf: torch.Tensor, ext):
         self.q, self.sf = q.contiguous().view(torch.uint8), sf.contiguous().view(torch.uint8)
         self.n = self.q.shape[0]
+        self._ext = ext
         self.storages = []
         self.dq = self._device_addr(self.q, ext)
         self.dsf = self._device_addr(self.sf, ext)
@@ -58,6 +59,15 @@ class HostTable:
         HostTable._registered[base] = (reg[0], reg[1] + 1)
         self.storages.append(base)
         return reg[0] + (t.data_ptr() - base)
+
+    def __del__(self):
+        # a registration must not outlive its storage (a freed, still-registered
+        # range makes later copies through reused memory fail)
+        try:
+            if self.storages:
+                self.release(self._ext)
+        except Exception:
+            pass
 
     def release(self, ext) -> None:
         for base in self.storages:

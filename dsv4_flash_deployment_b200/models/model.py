@@ -298,27 +298,24 @@ class DSV4Model:
 
     # --------------------------------------------------------------- helpers
     def _gemm(self, xq, xsf, n_tok, w: MxWeight, out, epi=EPI_BF16, **kw):
+        """Block-scaled GEMM; few output tiles -> split-K inside a thread-block cluster
+        (each split keeps >= 2 k-tiles; the kernel binding trims the split count to
+        what the GPU can keep resident)."""
         bn = pick_bn(n_tok)
         tiles = (w.q.shape[0] // 128) * ((n_tok + bn - 1) // bn)
         splits = 1
-        if tiles < 100 and w.k >= 1024:
-            splits = max(1, min(w.k // 512, 148 // max(tiles, 1)))
-            while tiles * splits * 128 * bn > self.ws.numel() and splits > 1:
-                splits -= 1
-        return gemm_mx(xq, xsf, n_tok, w, out, epi, splits=splits, workspace=self.ws if splits > 1 else None,
-                       counters=self.counters if splits > 1 else None, **kw)
+        if tiles < 100:
+            splits = max(1, min(8, (w.k // 128) // 2, 148 // max(tiles, 1)))
+        return gemm_mx(xq, xsf, n_tok, w, out, epi, splits=splits, **kw)
 
     def _gemm_bf16(self, x, w, out, n_tok, f32_out=False, groups=1, m_valid=None):
         bn = pick_bn(n_tok)
         tiles = (w.shape[0] // 128) * ((n_tok + bn - 1) // bn)
         k_tiles = x.shape[1] // groups // 64
         splits = 1
-        if tiles < 100 and k_tiles >= 16:
-            splits = max(1, min(k_tiles // 8, 148 // max(tiles, 1)))
-            while tiles * splits * 128 * bn > self.ws.numel() and splits > 1:
-                splits -= 1
+        if tiles < 100:
+            splits = max(1, min(8, k_tiles // 2, 148 // max(tiles, 1)))
         return gemm_bf16(x, w, out, f32_out=f32_out, groups=groups, n_tokens=n_tok, m_valid=m_valid, splits=splits,
-                         workspace=self.ws if splits > 1 else None, counters=self.counters if splits > 1 else None,
                          bn=bn)
 
     def _hc(self, T, Y=None, yperm=None, pos=None, topk=0, prev=None, mixes=None, cw=None, norm=None,

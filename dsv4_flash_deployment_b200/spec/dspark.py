@@ -192,69 +192,82 @@ class SpecEngine:
     def _ingest_meta(self, seqs, rows_per_seq, starts) -> StepMeta:
         return StepMeta(self.cfg, [SeqChunk(s, st, [0] * r, False) for s, r, st in zip(seqs, rows_per_seq, starts)])
 
-    def generate(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
+    # ------------------------------------------------------------ phases
+    def prefill(self, prompts: list[list[int]]) -> None:
+        """Prefills each prompt (chunked), fills the MTP rings; sets the first token."""
         m, cfg, dr = self.m, self.cfg, self.drafter
-        n = len(prompts)
-        if n > self.max_seqs:
+        if len(prompts) > self.max_seqs:
             raise ValueError("too many sequences for the drafter's buffers")
-        slots = list(range(n))
-        outs: list[list[int]] = [[] for _ in range(n)]
-        # ---- prefill each prompt (chunks up to the token budget), taps -> rings
+        self.slots = list(range(len(prompts)))
+        self.outs = [[] for _ in prompts]
         for j, p in enumerate(prompts):
             for c0 in range(0, len(p), m.max_tokens):
                 piece = p[c0:c0 + m.max_tokens]
                 last = c0 + len(piece) == len(p)
-                meta = StepMeta(cfg, [SeqChunk(slots[j], c0, piece, last)])
+                meta = StepMeta(cfg, [SeqChunk(self.slots[j], c0, piece, last)])
                 ids = self._run(meta, taps=dr.taps)
                 dr.ingest(None, meta.T)
                 if last:
-                    outs[j].append(int(ids[0]))
-        pos = [len(p) for p in prompts]       # position of each root
-        # ---- speculative rounds
+                    self.outs[j].append(int(ids[0]))
+        self.pos = [len(p) for p in prompts]       # position of each root
+
+    def draft(self, act: list[int]) -> np.ndarray:
+        """Drafts for sequences ``act``; returns toks [blk+1, len(act)] (row 0 = roots)."""
+        m, cfg, dr = self.m, self.cfg, self.drafter
+        na = len(act)
+        dmeta = StepMeta(cfg, [SeqChunk(self.slots[j], self.pos[j], [self.outs[j][-1]] +
+                                        [cfg.dspark_noise_token_id] * (self.blk - 1), True, True) for j in act])
+        m.upload(dmeta, self.pinned)
+        m._last_meta = dmeta
+        dr.toks[0, :na].copy_(torch.tensor([self.outs[j][-1] for j in act], dtype=torch.int32))
+        return dr.draft(na).cpu().numpy()
+
+    def verify(self, act: list[int], blocks: list[list[int]], max_new_tokens: int | None = None) -> list[int]:
+        """Verifies blocks [root, d1..d_{B-1}] per sequence; commits, ingests, emits.
+
+        Returns the accepted draft count per sequence."""
+        m, cfg, dr = self.m, self.cfg, self.drafter
+        na = len(act)
+        vmeta = StepMeta(cfg, [SeqChunk(self.slots[j], self.pos[j], blocks[a], True, True) for a, j in enumerate(act)])
+        preds = self._run(vmeta, taps=dr.taps, defer_rings=True).cpu().numpy().reshape(na, self.blk)
+        n_acc = []
+        for a in range(na):
+            if self.force_accept is not None:
+                k = min(int(self.force_accept), self.blk - 1)
+            else:
+                k = 0
+                while k < self.blk - 1 and preds[a, k] == blocks[a][k + 1]:
+                    k += 1
+            n_acc.append(k)
+        # rings keep positions <= pos + n_acc only
+        last = np.repeat([self.pos[j] + n_acc[a] for a, j in enumerate(act)], self.blk).astype(np.int32)
+        m.commit_rings(vmeta.T, torch.from_numpy(last).to(m.dev))
+        # the accepted rows' main hidden enters every stage ring
+        rows = np.concatenate([a * self.blk + np.arange(n_acc[a] + 1) for a in range(na)]).astype(np.int64)
+        imeta = self._ingest_meta([self.slots[j] for j in act], [k + 1 for k in n_acc], [self.pos[j] for j in act])
+        m.upload(imeta, self.pinned)
+        dr.ingest(torch.from_numpy(rows).to(m.dev), imeta.T)
+        for a, j in enumerate(act):
+            k = n_acc[a]
+            emitted = blocks[a][1:k + 1] + [int(preds[a, k])]
+            room = len(emitted) if max_new_tokens is None else max_new_tokens - len(self.outs[j])
+            self.outs[j].extend(emitted[:room])
+            self.pos[j] += k + 1
+            self.stats.rounds += 1
+            self.stats.drafted += self.blk - 1
+            self.stats.accepted += k
+            self.stats.emitted += min(len(emitted), room)
+            self.stats.histogram[k] += 1
+        return n_acc
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
+        self.prefill(prompts)
         while True:
-            act = [j for j in range(n) if len(outs[j]) < max_new_tokens]
+            act = [j for j in range(len(prompts)) if len(self.outs[j]) < max_new_tokens]
             if not act:
                 break
-            na = len(act)
-            # draft
-            dmeta = StepMeta(cfg, [SeqChunk(slots[j], pos[j], [outs[j][-1]] + [cfg.dspark_noise_token_id] *
-                                            (self.blk - 1), True, True) for j in act])
-            m.upload(dmeta, self.pinned)
-            m._last_meta = dmeta
-            dr.toks[0, :na].copy_(torch.tensor([outs[j][-1] for j in act], dtype=torch.int32), non_blocking=False)
-            toks = dr.draft(na).cpu().numpy()          # [blk+1, na]
-            # verify: [root, d1..d_{B-1}] with logits at every position, rings deferred
-            blocks = [[outs[j][-1]] + [int(toks[i + 1, a]) for i in range(self.blk - 1)] for a, j in enumerate(act)]
-            vmeta = StepMeta(cfg, [SeqChunk(slots[j], pos[j], blocks[a], True, True) for a, j in enumerate(act)])
-            preds = self._run(vmeta, taps=dr.taps, defer_rings=True).cpu().numpy().reshape(na, self.blk)
-            n_acc = []
-            for a in range(na):
-                if self.force_accept is not None:
-                    k = min(int(self.force_accept), self.blk - 1)
-                else:
-                    k = 0
-                    while k < self.blk - 1 and preds[a, k] == blocks[a][k + 1]:
-                        k += 1
-                n_acc.append(k)
-            # commit rings for positions <= pos + n_acc
-            last = np.repeat([pos[j] + n_acc[a] for a, j in enumerate(act)], self.blk).astype(np.int32)
-            lc = torch.from_numpy(last).to(m.dev)
-            m.commit_rings(vmeta.T, lc)
-            # ingest accepted rows' main hidden
-            rows = np.concatenate([a * self.blk + np.arange(n_acc[a] + 1) for a in range(na)]).astype(np.int64)
-            imeta = self._ingest_meta([slots[j] for j in act], [k + 1 for k in n_acc], [pos[j] for j in act])
-            m.upload(imeta, self.pinned)
-            dr.ingest(torch.from_numpy(rows).to(m.dev), imeta.T)
-            # emit
-            for a, j in enumerate(act):
-                k = n_acc[a]
-                emitted = blocks[a][1:k + 1] + [int(preds[a, k])]
-                room = max_new_tokens - len(outs[j])
-                outs[j].extend(emitted[:room])
-                pos[j] += k + 1
-                self.stats.rounds += 1
-                self.stats.drafted += self.blk - 1
-                self.stats.accepted += k
-                self.stats.emitted += min(len(emitted), room)
-                self.stats.histogram[k] += 1
-        return outs
+            toks = self.draft(act)
+            blocks = [[self.outs[j][-1]] + [int(toks[i + 1, a]) for i in range(self.blk - 1)]
+                      for a, j in enumerate(act)]
+            self.verify(act, blocks, max_new_tokens)
+        return self.outs

@@ -98,7 +98,8 @@ def test_bf16_dense(n_tok):
     _close(out, ref, 1e-3)
 
 
-def test_swiglu_epilogue_dense():
+@pytest.mark.parametrize("splits", [1, 2])
+def test_swiglu_epilogue_dense(splits):
     inter, d = 256, 512
     w1, s1 = _rand_fp8_weight(inter, d, 3)
     w3, s3 = _rand_fp8_weight(inter, d, 4)
@@ -112,8 +113,10 @@ def test_swiglu_epilogue_dense():
     xq, xsf = G.quantize(x.cuda())
     hq = torch.zeros(128, inter, dtype=torch.uint8, device="cuda")
     hsf = torch.zeros(1, inter // 128, 512, dtype=torch.uint8, device="cuda")
-    G.gemm_mx(xq, xsf, 40, mw, None, G.EPI_SWIGLU, row_scale=wts.cuda(), hq=hq, hsf=hsf, swiglu_limit=10.0)
+    G.gemm_mx(xq, xsf, 40, mw, None, G.EPI_SWIGLU, row_scale=wts.cuda(), hq=hq, hsf=hsf, swiglu_limit=10.0,
+              splits=splits)
     torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
     got = N.act_dequant(hq[:40].cpu().view(torch.float8_e4m3fn), chunks_to_sf(hsf.cpu(), 40, inter // 32))
     want = N.act_dequant(rq, rs)
     # identical up to rare one-ulp e4m3 flips from fp32 summation order
@@ -236,3 +239,43 @@ def test_grouped_expert_ffn_matches_oracle(fmt):
         (w1, s1), (w3, s3), (w2_, s2) = experts[e]
         ref = N.expert_ffn(x[st:st + c], w1, s1, w3, s3, w2_, s2, 10.0, rw[st:st + c, None])
         _close(y[st:st + c], ref, 0.05)
+
+
+@pytest.mark.parametrize("n_tok", [1, 20, 64, 127, 200])
+@pytest.mark.parametrize("splits", [2, 4, 8])
+def test_cluster_split_k_dense(n_tok, splits):
+    """Split-K reduced inside a thread-block cluster over distributed shared memory:
+    bf16/f32 outputs match the oracle and the workspace path bit for bit."""
+    n, k = 512, 2048
+    w, s = _rand_fp8_weight(n, k, 7)
+    torch.manual_seed(n_tok + splits)
+    x = torch.randn(n_tok, k).to(torch.bfloat16)
+    ref = N.fp8_linear(x, w, s, torch.float32)
+    mw = G.MxWeight.from_checkpoint(w, s, "cuda")
+    xq, xsf = G.quantize(x.cuda())
+    out_c = torch.empty(n_tok, n, dtype=torch.float32, device="cuda")
+    G.gemm_mx(xq, xsf, n_tok, mw, out_c, G.EPI_F32, splits=splits)
+    out_1 = torch.empty(n_tok, n, dtype=torch.float32, device="cuda")
+    G.gemm_mx(xq, xsf, n_tok, mw, out_1, G.EPI_F32, splits=1)
+    ob = torch.empty(n_tok, n, dtype=torch.bfloat16, device="cuda")
+    G.gemm_mx(xq, xsf, n_tok, mw, ob, G.EPI_BF16, splits=splits)
+    torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
+    _close(out_c, ref, 1e-3)
+    _close(ob, ref)
+    assert torch.allclose(out_c, out_1, rtol=1e-4, atol=1e-4)
+
+
+def test_cluster_split_k_bf16_and_swiglu():
+    n, k = 256, 4096
+    torch.manual_seed(3)
+    x = torch.randn(60, k).to(torch.bfloat16)
+    wb = (torch.randn(n, k) / k ** 0.5).to(torch.bfloat16)
+    wp = torch.zeros(n, k, dtype=torch.bfloat16)
+    wp[:n] = wb
+    ref = x.float() @ wb.float().t()
+    out = torch.empty(60, n, dtype=torch.float32, device="cuda")
+    G.gemm_bf16(x.cuda(), wp.cuda(), out, f32_out=True, splits=8)
+    torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
+    _close(out, ref, 1e-3)
