@@ -41,6 +41,17 @@ import time
 BASELINE_TOKS = 8463.7   # V4-Flash 1k/1k C=512, TPU v6e-16 (V4/results/raw/1k1k.json:236)
 METRIC = "output tok/s @1k/1k C=512 (8×B200, max over ranks); C=1 TPOT ms; vs BASELINE"
 
+# Sweep shapes (BASELINE.json configs 3 and 4).  In the steady state of a
+# C-request sweep the prompt tokens prefilled per step are isl/osl times the
+# decode tokens: 1k/1k and 1k/8k keep every request but one decoding; 8k/1k is
+# prefill-bound, so a step is a token budget split 1 : 8 between decode and
+# prefill (2048-token chunks, the V4 recipe's chunk size).
+WORKLOADS = {
+    "1k1k": {"isl": 1024, "osl": 1024, "baseline": 8463.7, "src": "V4/results/raw/1k1k.json:236"},
+    "8k1k": {"isl": 8192, "osl": 1024, "baseline": 1758.53, "src": "V4/results/raw/8k1k.json:236"},
+    "1k8k": {"isl": 1024, "osl": 8192, "baseline": 8067.9, "src": "V4/results/raw/1k8k.json:236"},
+}
+
 
 def _reference_arm(args) -> None:
     why = ("the reference is a JAX/Pallas TPU deployment (vLLM + tpu-inference, not vendored) with no GPU "
@@ -127,9 +138,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--concurrency", type=int, default=512)
-    ap.add_argument("--isl", type=int, default=1024)
-    ap.add_argument("--osl", type=int, default=1024)
-    ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--workload", default="1k1k", choices=sorted(WORKLOADS),
+                    help="sweep shape whose steady-state step is timed (1k1k is the headline)")
+    ap.add_argument("--isl", type=int, default=None)
+    ap.add_argument("--osl", type=int, default=None)
+    ap.add_argument("--chunk", type=int, default=None, help="prefill tokens per step (all ranks)")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
@@ -161,10 +174,19 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
     cfg = v4_flash_config()
-    C, isl, osl, chunk = args.concurrency, args.isl, args.osl, args.chunk
+    wl = WORKLOADS[args.workload]
+    isl = args.isl or wl["isl"]
+    osl = args.osl or wl["osl"]
+    C = args.concurrency
     c_rank = C // world
-    chunk_rank = max(1, chunk // world)
-    n_dec = c_rank - 1
+    if args.workload == "1k1k":
+        n_dec = c_rank - 1
+        chunk_rank = max(1, (args.chunk or 512) // world)
+    else:
+        # decode tokens capped so one step stays within a 2304-token budget per
+        # rank; prefill tokens = isl/osl x decode tokens (the sweep's equilibrium)
+        n_dec = max(1, min(c_rank - 1, 2304 * osl // (isl + osl)))
+        chunk_rank = (args.chunk // world) if args.chunk else max(1, -(-n_dec * isl // osl))
     max_tokens = n_dec + chunk_rank
     max_seq = isl + osl
     ep = ep_mod.EPGroup(rank, world, group, dev, transport=args.ep_transport) if world > 1 else None
@@ -305,7 +327,8 @@ def main() -> None:
 
     if rank == 0:
         line = {
-            "metric": METRIC,
+            "metric": METRIC if args.workload == "1k1k" else
+            f"output tok/s @{isl // 1024}k/{osl // 1024}k C={C} (max over ranks); vs {wl['src']}",
             "value": round(value, 1),
             "unit": "tok/s",
             "n_gpus": world,
@@ -314,14 +337,15 @@ def main() -> None:
             "ms_per_step": round(ms_max, 3),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(value / BASELINE_TOKS, 3),
+            "vs_baseline": round(value / wl["baseline"], 3),
             "dtype": "bf16",
             "data": "synthetic: uniform-random token ids, random-init weights",
             "config": {
                 "model": "deepseek-v4-flash (assumed dims: 43L, d4096, 64x512 heads, 256 experts top-8 inter2048)",
                 "global_batch": C,
                 "seq_len": max_seq,
-                "workload": f"1k/1k C={C} steady-state step: {n_dec * world} decode + {chunk_rank * world} prefill tokens",
+                "workload": f"{args.workload} C={C} steady-state step: {n_dec * world} decode + "
+                            f"{chunk_rank * world} prefill tokens",
                 "parallelism": f"dp-attention{world} x ep{world}" if world > 1 else "single GPU",
                 "weights": "fp8 e4m3 block-scaled dense (checkpoint-native), mxfp8 experts, bf16 activations",
                 "expert_storage_layers": n_phys,

@@ -50,7 +50,8 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
           int64_t splits, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
           const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
           double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
-          const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups) {
+          const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
+          int64_t probe) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -105,6 +106,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.workspace = workspace ? workspace->data_ptr<float>() : nullptr;
   p.tile_counters = counters ? counters->data_ptr<int>() : nullptr;
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
+  p.probe = (int)probe;
   if (p.splits > 1 && !(workspace && counters)) {
     // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
     // Halve the split count until every tile's cluster is resident at once.

@@ -63,7 +63,18 @@ DSV4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)
 
 struct TileCoord {
   int a_row0, b_row0, b_valid, out_col0, k_begin, k_end, split, tile, n_eff;
+  int k_rot;   // the k loop starts at k_begin + k_rot and wraps (dense GEMMs)
 };
+
+// k tile of step i of a tile's mainloop.  Dense GEMMs share one activation
+// matrix across all CTAs: started in lockstep at the same k they would all read
+// the same L2 lines at once, so each tile starts at a different k and wraps.
+DSV4_DEV int k_of(const TileCoord& t, int i) {
+  const int nk = t.k_end - t.k_begin;
+  int k = i + t.k_rot;
+  if (k >= nk) k -= nk;
+  return t.k_begin + k;
+}
 
 // Per-tile MMA width: the smallest of 32/64/128/256 covering the valid rows.
 // Tiles start on 128-row boundaries of the activation buffer (256 for n_eff
@@ -99,6 +110,7 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
   t.k_end = min(p.k_tiles, t.k_begin + per);
   t.split = split;
   t.tile = tile;
+  t.k_rot = (!GROUPED && t.k_end - t.k_begin > 1) ? tile % (t.k_end - t.k_begin) : 0;
   return true;
 }
 
@@ -169,7 +181,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
-      for (int kt = t.k_begin; kt < t.k_end; ++kt) {
+      for (int i = 0; i < t.k_end - t.k_begin; ++i) {
+        const int kt = k_of(t, i);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, KID_GEMM, 1)) goto done;
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[stage], tx);
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t d_tmem = tmem + acc * L::kAccCols;
       if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
       tc_fence_after();
-      for (int kt = t.k_begin; kt < t.k_end; ++kt) {
+      for (int i = 0; i < t.k_end - t.k_begin; ++i) {
         if (!mbar_wait(&full[stage], phase, abort_flag, p.err, KID_GEMM, 3)) goto done;
         tc_fence_after();
         if (lane == 0) {
@@ -221,10 +234,10 @@ __global__ void __launch_bounds__(192, 1)
             sfb_t = col + 4;
           }
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < ((p.probe & 1) ? 0 : 4); ++kk) {
             const uint64_t ad = sdesc_kmajor_sw128(a0 + kk * 32);
             const uint64_t bd = sdesc_kmajor_sw128(b0 + kk * 32);
-            const uint32_t accum = (kt > t.k_begin || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
             if constexpr (MX)
               umma_mx(d_tmem, ad, bd, idesc_mx_sf(idesc, kk), sfa_t, sfb_t, accum);
             else
@@ -425,7 +438,7 @@ __global__ void __launch_bounds__(192, 1)
           constexpr int kVecPerRow = 128 * kEl / 16;   // 16 (bf16) or 32 (fp32) vectors per token row
           const int tid = threadIdx.x - 64;
           const bool full_m = t.out_col0 + 128 <= p.m_valid && (p.ldo * kEl) % 16 == 0;
-          for (int e = tid; e < kCols * kVecPerRow; e += 128) {
+          for (int e = tid; e < ((p.probe & 2) ? 0 : kCols * kVecPerRow); e += 128) {
             const int j = e / kVecPerRow, vi = e % kVecPerRow;
             if (c0 + j >= t.b_valid) continue;
             const size_t orow = (size_t)(t.b_row0 + c0 + j) * p.ldo;

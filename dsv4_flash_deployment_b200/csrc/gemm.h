@@ -40,6 +40,7 @@ struct GemmParams {
   float* workspace;
   int* tile_counters;
   int cluster_split;
+  int probe;           // measurement only: bit 0 = no MMA (stages released as they land), bit 1 = no output stores
   uint32_t* err;
 };
 

@@ -615,10 +615,10 @@ class DSV4Model:
         c13.__enter__()
         ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                  self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1)
+                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, 0)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
         ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm, ex.w2.q.shape[0],
-                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1)
+                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1, 0)
         c2.__exit__(None, None, None)
