@@ -63,12 +63,11 @@ DSV4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)
 
 struct TileCoord {
   int a_row0, b_row0, b_valid, out_col0, k_begin, k_end, split, tile, n_eff;
-  int k_rot;   // the k loop starts at k_begin + k_rot and wraps (dense GEMMs)
+  int k_rot;   // the k loop starts at k_begin + k_rot and wraps (0: plain order; a
+               // rotated start per tile was measured and gave no gain)
 };
 
-// k tile of step i of a tile's mainloop.  Dense GEMMs share one activation
-// matrix across all CTAs: started in lockstep at the same k they would all read
-// the same L2 lines at once, so each tile starts at a different k and wraps.
+// k tile of step i of a tile's mainloop.
 DSV4_DEV int k_of(const TileCoord& t, int i) {
   const int nk = t.k_end - t.k_begin;
   int k = i + t.k_rot;
@@ -110,7 +109,7 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
   t.k_end = min(p.k_tiles, t.k_begin + per);
   t.split = split;
   t.tile = tile;
-  t.k_rot = (!GROUPED && t.k_end - t.k_begin > 1) ? tile % (t.k_end - t.k_begin) : 0;
+  t.k_rot = 0;
   return true;
 }
 
