@@ -31,6 +31,7 @@ def main() -> None:
     ap.add_argument("--topk", type=int, default=None)
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"])
     ap.add_argument("--decode-only", action="store_true", help="C decoding sequences per rank, no prefill chunk")
+    ap.add_argument("--context", type=int, default=1024, help="decode positions start here (span of 1024)")
     a = ap.parse_args()
     import os
 
@@ -56,12 +57,13 @@ def main() -> None:
     n_dec = a.concurrency // world - (0 if a.decode_only else 1)
     chunk = 0 if a.decode_only else a.chunk // world
     T = n_dec + chunk
-    n_phys = plan_expert_storage(cfg, dev, T, n_dec + 2, 2048, world)
-    eng = Engine.build(cfg, dev, max_seqs=n_dec + 2, max_batched_tokens=T, max_seq_len=2048,
+    max_seq = a.context + 1024 + 16
+    n_phys = plan_expert_storage(cfg, dev, T, n_dec + 2, max_seq, world)
+    eng = Engine.build(cfg, dev, max_seqs=n_dec + 2, max_batched_tokens=T, max_seq_len=max_seq,
                        expert_storage_layers=n_phys, use_graphs=False, ep=ep)
     m = eng.model
     rng = np.random.default_rng(0)
-    dec = 1024 + (np.arange(n_dec) * (1024 // max(1, n_dec)) + 1) % 1024
+    dec = a.context + (np.arange(n_dec) * (1024 // max(1, n_dec)) + 1) % 1024
 
     def meta(i):
         ch = [SeqChunk(s, int(dec[s]) + i, [int(rng.integers(0, cfg.vocab_size))], True) for s in range(n_dec)]

@@ -399,7 +399,8 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
                   int64_t topk, const Tensor& out_idx, const Tensor& out_cnt, const optional<Tensor>& cand,
                   int64_t cand_mode, int64_t cand_block, int64_t cand_topk, int64_t T, const Tensor& err,
                   const optional<Tensor>& kcache_alt, const optional<Tensor>& pos,
-                  const optional<Tensor>& chunk_start, const optional<Tensor>& last_pos, int64_t own_r) {
+                  const optional<Tensor>& chunk_start, const optional<Tensor>& last_pos, int64_t own_r,
+                  const Tensor& keys) {
   dsv4::IdxParams p{};
   p.T = (int)T;
   p.n_heads = (int)q.size(1);
@@ -425,7 +426,9 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
   p.last_pos = ptr<const int>(last_pos);
   p.own_r = (int)std::max<int64_t>(1, own_r);
   if (kcache_alt) TORCH_CHECK(pos && chunk_start && last_pos, "pos/chunk_start/last_pos required with kcache_alt");
-  CUDA_OK(dsv4::indexer_topk(p, cur_stream()));
+  TORCH_CHECK(keys.dim() == 2 && keys.size(0) >= T && keys.size(1) >= p.max_c && keys.element_size() == 4,
+              "keys scratch must be [>=T, >=max_c] 32-bit");
+  CUDA_OK(dsv4::indexer_topk(p, ptr<uint32_t>(keys), (int)keys.stride(0), cur_stream()));
 }
 
 // sync = optional int64 tensor [peer_sig_table, peer_cnt_table, done, epoch] of device addresses

@@ -10,10 +10,18 @@
 // lower index); when clen <= topk every entry is selected, as top_k of a
 // shorter list returns all of it.
 //
-// One CTA (256 threads) per token; lane-per-row scoring with the query in
-// shared memory; 4-pass radix select on order-preserving keys in shared memory.
+// Two kernels:
+//   idx_score   one CTA per (token, 64 compressed rows): the head x row dot
+//               products on tensor cores (mma.sync m16n8k16, bf16 in, fp32
+//               accumulate), then per row the head sum in fixed order h = 0..H-1
+//               with the bf16 rounding points above; writes order-preserving keys
+//   idx_select  one CTA per token: candidate-block mask (level 1), 4-pass radix
+//               select and ordered compaction on the keys in shared memory
+// Spreading the scoring over the compressed rows keeps long contexts (9K
+// tokens = 2304 entries at ratio 4) from serializing on one CTA per token.
 #include "common.cuh"
 #include "kernels.h"
+#include "mma_sync.cuh"
 
 namespace dsv4 {
 
@@ -116,53 +124,94 @@ DSV4_DEV int ordered_select(const uint32_t* keys, int n, uint32_t kth, int n_eq_
   return s_base + min(s_eq_base, n_eq_take);
 }
 
-__global__ void __launch_bounds__(256) indexer_topk_kernel(IdxParams p) {
+constexpr int kIdxRows = 64;            // compressed rows per scoring CTA
+constexpr int kIdxDh = 128;             // indexer head dim (both model families)
+constexpr int kIdxPad = kIdxDh + 8;     // smem row stride (bf16) against bank conflicts
+constexpr int kIdxMaxHeads = 64;
+
+DSV4_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+__global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* keys, int keys_ld) {
+  __shared__ __align__(16) __nv_bfloat16 sQ[kIdxMaxHeads * kIdxPad];
+  __shared__ __align__(16) __nv_bfloat16 sK[kIdxRows * kIdxPad];
+  __shared__ __nv_bfloat16 sS[kIdxMaxHeads * (kIdxRows + 2)];   // terms are bf16 values: exact
+  __shared__ float sw[kIdxMaxHeads];
+  const int t = blockIdx.x, r0 = blockIdx.y * kIdxRows;
+  const int clen = p.clen[t];
+  if (r0 >= clen) return;
+  if (clen <= p.topk && p.cand_mode != 1) return;   // every entry is selected: no scores needed
+  const int H = p.n_heads, Hp = (H + 15) & ~15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int c = tid; c < Hp * (kIdxDh / 8); c += 128) {
+    const int h = c / (kIdxDh / 8), ch = c % (kIdxDh / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < H) v = *reinterpret_cast<const uint4*>(p.q + ((size_t)t * H + h) * kIdxDh + ch * 8);
+    *reinterpret_cast<uint4*>(sQ + h * kIdxPad + ch * 8) = v;
+  }
+  if (tid < kIdxMaxHeads) sw[tid] = tid < H ? p.w[(size_t)t * H + tid] : 0.f;
+  const int slot = p.slot[t];
+  const bool use_alt = p.kcache_alt != nullptr && ((p.pos[t] + 1) % p.own_r) != 0 &&
+                       p.chunk_start[t] == p.last_pos[t];
+  const __nv_bfloat16* kbase = use_alt ? p.kcache_alt + (size_t)slot * p.alt_max_c * kIdxDh
+                                       : p.kcache + (size_t)slot * p.max_c * kIdxDh;
+  for (int c = tid; c < kIdxRows * (kIdxDh / 8); c += 128) {
+    const int r = c / (kIdxDh / 8), ch = c % (kIdxDh / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r0 + r < clen) v = *reinterpret_cast<const uint4*>(kbase + (size_t)(r0 + r) * kIdxDh + ch * 8);
+    *reinterpret_cast<uint4*>(sK + r * kIdxPad + ch * 8) = v;
+  }
+  __syncthreads();
+  // raw[h, j] = q_h . k_j : warp w takes rows 16w..16w+15, all head tiles
+  const int n0 = warp * 16, g = lane >> 2, cq = lane & 3;
+  const uint32_t ba = smem_u32(sK + (n0 + (lane & 7) + 8 * (lane >> 4)) * kIdxPad + 8 * ((lane >> 3) & 1));
+  for (int mt = 0; mt < Hp / 16; ++mt) {
+    float acc[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
+    const uint32_t qa = smem_u32(sQ + (mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kIdxPad + 8 * (lane >> 4));
+#pragma unroll
+    for (int k0 = 0; k0 < kIdxDh; k0 += 16) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(qa + k0 * 2, a0, a1, a2, a3);
+      ldsm_x4(ba + k0 * 2, b0, b1, b2, b3);
+      mma16816(acc[0], a0, a1, a2, a3, b0, b1);
+      mma16816(acc[1], a0, a1, a2, a3, b2, b3);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = mt * 16 + g + 8 * (e >> 1);
+        const int col = n0 + nt * 8 + 2 * cq + (e & 1);
+        sS[h * (kIdxRows + 2) + col] = __float2bfloat16(fmaxf(bf16r(acc[nt][e]), 0.f) * sw[h]);
+      }
+  }
+  __syncthreads();
+  if (tid < kIdxRows && r0 + tid < clen) {
+    float sum = 0.f;
+    for (int h = 0; h < H; ++h) sum += __bfloat162float(sS[h * (kIdxRows + 2) + tid]);
+    float sc = bf16r(sum);
+    const int j = r0 + tid;
+    if (p.cand_mode == 2 && !p.cand[(size_t)t * (p.max_c / p.cand_block) + j / p.cand_block]) sc = -INFINITY;
+    keys[(size_t)t * keys_ld + j] = order_key(sc);
+  }
+}
+
+__global__ void __launch_bounds__(256) idx_select_kernel(IdxParams p, const uint32_t* keys_in, int keys_ld) {
   extern __shared__ uint8_t smem[];
   const int t = blockIdx.x;
-  const int H = p.n_heads, hd = p.head_dim;
-  __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem);
-  float* sw = reinterpret_cast<float*>(smem + (size_t)H * hd * 2);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(sw + H);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem);
   uint32_t* keys = hist + 256;
   const int clen = p.clen[t];
-  const int slot = p.slot[t];
-  for (int i = threadIdx.x; i < H * hd; i += blockDim.x) sq[i] = p.q[(size_t)t * H * hd + i];
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sw[i] = p.w[(size_t)t * H + i];
-  __syncthreads();
   const int k = p.topk;
   if (clen <= k) {
     for (int j = threadIdx.x; j < k; j += blockDim.x) p.out_idx[(size_t)t * k + j] = j < clen ? j : -1;
     if (threadIdx.x == 0) p.out_cnt[t] = clen;
     if (p.cand_mode != 1) return;
   }
-  // ---- scores (lane per row)
-  const bool use_alt = p.kcache_alt != nullptr && ((p.pos[t] + 1) % p.own_r) != 0 &&
-                       p.chunk_start[t] == p.last_pos[t];
-  const __nv_bfloat16* kbase = use_alt ? p.kcache_alt + (size_t)slot * p.alt_max_c * hd
-                                       : p.kcache + (size_t)slot * p.max_c * hd;
-  for (int j = threadIdx.x; j < clen; j += blockDim.x) {
-    const __nv_bfloat16* kr = kbase + (size_t)j * hd;
-    float sum = 0.f;
-    for (int h = 0; h < H; ++h) {
-      float dot = 0.f;
-      const __nv_bfloat16* qh = sq + h * hd;
-      for (int d = 0; d < hd; d += 8) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(kr + d);
-        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
-        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(qh + d);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 a = __bfloat1622float2(k2[e]), b = __bfloat1622float2(q2[e]);
-          dot += a.x * b.x + a.y * b.y;
-        }
-      }
-      const float raw = __bfloat162float(__float2bfloat16(dot));
-      sum += __bfloat162float(__float2bfloat16(fmaxf(raw, 0.f) * sw[h]));
-    }
-    float sc = __bfloat162float(__float2bfloat16(sum));
-    if (p.cand_mode == 2 && !p.cand[(size_t)t * (p.max_c / p.cand_block) + j / p.cand_block]) sc = -INFINITY;
-    keys[j] = order_key(sc);
-  }
+  for (int j = threadIdx.x; j < clen; j += blockDim.x) keys[j] = keys_in[(size_t)t * keys_ld + j];
   __syncthreads();
   if (p.cand_mode == 1) {
     // block maxima (newest block forced in), top cand_topk blocks -> mask
@@ -206,19 +255,21 @@ __global__ void __launch_bounds__(256) indexer_topk_kernel(IdxParams p) {
   if (threadIdx.x == 0) p.out_cnt[t] = cnt;
 }
 
-cudaError_t indexer_topk(const IdxParams& p, cudaStream_t st) {
+cudaError_t indexer_topk(const IdxParams& p, uint32_t* keys, int keys_ld, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  const size_t smem = (size_t)p.n_heads * p.head_dim * 2 + p.n_heads * 4 + 256 * 4 +
-                      (size_t)(p.max_c + p.max_c / max(1, p.cand_block) + 1) * 4;
+  if (p.head_dim != kIdxDh || p.n_heads > kIdxMaxHeads || keys_ld < p.max_c) return cudaErrorInvalidValue;
+  dim3 g(p.T, (p.max_c + kIdxRows - 1) / kIdxRows);
+  idx_score_kernel<<<g, 128, 0, st>>>(p, keys, keys_ld);
+  const size_t smem = 256 * 4 + (size_t)(p.max_c + p.max_c / max(1, p.cand_block) + 1) * 4;
   // dynamic + the kernel's static shared memory must stay under the 227 KB opt-in limit
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   static size_t configured = 48 * 1024;
   if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(idx_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  indexer_topk_kernel<<<p.T, 256, smem, st>>>(p);
+  idx_select_kernel<<<p.T, 256, smem, st>>>(p, keys, keys_ld);
   return cudaGetLastError();
 }
 

@@ -179,7 +179,8 @@ struct IdxParams {
   const int* last_pos;
   int own_r;
 };
-cudaError_t indexer_topk(const IdxParams& p, cudaStream_t st);
+// keys: [T, keys_ld] uint32 scratch (keys_ld >= max_c) for the order keys of the scores
+cudaError_t indexer_topk(const IdxParams& p, uint32_t* keys, int keys_ld, cudaStream_t st);
 
 // ---------------------------------------------------------------- ep.cu
 // Completion signalling of the NVLink (peer-store) transport; all null for the

@@ -239,6 +239,9 @@ class DSV4Model:
             if l in cfg.index_source_layer_ids:
                 self.idx_cache[l] = torch.zeros(S, max_c, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
             self.comp_ring[l] = torch.zeros(S, co * r, 2 * co * cfg.head_dim, dtype=torch.float32, device=dev)
+        # order keys of the indexer scores, [T, widest index cache] (scoring CTAs -> select CTA)
+        kc = max([t.shape[1] for t in self.idx_cache.values()] or [1])
+        self.idx_keys = torch.empty(self.max_tokens, kc, dtype=torch.int32, device=dev)
 
     def cache_bytes(self) -> int:
         tot = 0
@@ -463,8 +466,7 @@ class DSV4Model:
                 if m.index_bypass(r):
                     self._idx_sel = None
                 else:
-                    with self._t("indexer"):
-                        self._indexer(L, m, r)
+                    self._indexer(L, m, r)
                     self._idx_sel = (self.comp_idx, self.comp_cnt)
             if lid in cfg.index_source_layer_ids or lid not in cfg.kv_source_layer_ids:
                 sel = getattr(self, "_idx_sel", None)
@@ -528,11 +530,13 @@ class DSV4Model:
         T = m.T
         lid = L.layer_id
         nih, hd = cfg.index_n_heads, cfg.index_head_dim
-        self._gemm(self.qr_q, self.qr_sf, T, L.idx_wq_b, self.qidx.view(self.qidx.shape[0], -1))
-        self._gemm_bf16(self.u, L.idx_wproj, self.widx_raw, T, f32_out=True)
+        with self._t("idx_gemm"):
+            self._gemm(self.qr_q, self.qr_sf, T, L.idx_wq_b, self.qidx.view(self.qidx.shape[0], -1))
+            self._gemm_bf16(self.u, L.idx_wproj, self.widx_raw, T, f32_out=True)
         cos, sin = self.rope["yarn"]
-        ext.idx_q_prep(self.qidx, T, nih, hd, cos, sin, self.m_pos, self.widx_raw, (hd ** -0.5) * (nih ** -0.5),
-                       self.widx)
+        with self._t("idx_q_prep"):
+            ext.idx_q_prep(self.qidx, T, nih, hd, cos, sin, self.m_pos, self.widx_raw,
+                           (hd ** -0.5) * (nih ** -0.5), self.widx)
         # widx_raw rows are 128 wide; idx_q_prep reads [T, nih] with row stride nih
         src = self._k_source(lid)
         cand_mode = 0
@@ -541,10 +545,14 @@ class DSV4Model:
         elif 0 <= cfg.candidate_source_layer_id < lid:
             cand_mode = 2
         alt = self._k_alt(lid)
+        tk = self._t("idx_topk")
+        tk.__enter__()
         ext.indexer_topk(self.qidx, self.widx, self.idx_cache[src], self.m_slot, self.m_clen[r], cfg.index_topk,
                          self.comp_idx, self.comp_cnt, self.cand if cand_mode else None, cand_mode,
                          cfg.candidate_block_size, cfg.candidate_topk_blocks, T, self.err,
-                         self.idx_cache[alt] if alt is not None else None, self.m_pos, self.m_cstart, self.m_last, r)
+                         self.idx_cache[alt] if alt is not None else None, self.m_pos, self.m_cstart, self.m_last, r,
+                         self.idx_keys)
+        tk.__exit__(None, None, None)
 
     def _k_alt(self, lid: int) -> int | None:
         """K cache read by tokens that do not close a group at ``lid`` this step.
