@@ -332,30 +332,45 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   }
 }
 
-// Merge split partials: one CTA per token, thread -> (head, dim pair).
+// Merge split partials: one CTA per (token, head), thread -> dim pair.  The
+// per-split rescale factors exp(m_s - m) and the denominator are formed once
+// in shared memory; each thread then issues nsplit independent float2 loads.
+constexpr int kMaxSplits = 32;
 __global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p, int nsplit) {
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, h = blockIdx.y;
+  __shared__ float sF[kMaxSplits];
+  __shared__ float sInv;
+  const float* base = p.workspace + (size_t)t * nsplit * kH * (kDh + 2) + (size_t)h * (kDh + 2);
+  const size_t sstride = (size_t)kH * (kDh + 2);
+  if (threadIdx.x < 32) {
+    const int s = threadIdx.x;
+    const float ms = s < nsplit ? base[s * sstride + kDh] : -1e30f;
+    float m = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float f = s < nsplit ? expf(ms - m) : 0.f;
+    float den = s < nsplit ? base[s * sstride + kDh + 1] * f : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (s < nsplit) sF[s] = f;
+    if (s == 0) sInv = 1.f / (den + expf(p.sink[h] - m));
+  }
+  __syncthreads();
   const int rope_pos = p.rope_pos ? p.rope_pos[t] : p.pos[t];
-  const float* base = p.workspace + (size_t)t * nsplit * kH * (kDh + 2);
-  for (int e = threadIdx.x; e < kH * kDh / 2; e += blockDim.x) {
-    const int h = e / (kDh / 2), d = 2 * (e % (kDh / 2));
-    float m = -1e30f;
-    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, base[((size_t)s * kH + h) * (kDh + 2) + kDh]);
-    float num0 = 0.f, num1 = 0.f, den = 0.f;
+  const float inv = sInv;
+  for (int d = 2 * threadIdx.x; d < kDh; d += 2 * blockDim.x) {
+    float num0 = 0.f, num1 = 0.f;
     for (int s = 0; s < nsplit; ++s) {
-      const float* w = base + ((size_t)s * kH + h) * (kDh + 2);
-      const float f = expf(w[kDh] - m);
-      num0 += w[d] * f;
-      num1 += w[d + 1] * f;
-      den += w[kDh + 1] * f;
+      const float2 w = *reinterpret_cast<const float2*>(base + s * sstride + d);
+      num0 += w.x * sF[s];
+      num1 += w.y * sF[s];
     }
-    den += expf(p.sink[h] - m);
-    float e0 = __bfloat162float(__float2bfloat16(num0 / den));
-    float o0 = __bfloat162float(__float2bfloat16(num1 / den));
+    float e0 = __bfloat162float(__float2bfloat16(num0 * inv));
+    float o0 = __bfloat162float(__float2bfloat16(num1 * inv));
     if (d >= kDh - 64) {
       const int pi = (d - (kDh - 64)) >> 1;
-      const float c = p.rope_cos[(size_t)rope_pos * 32 + pi], s = -p.rope_sin[(size_t)rope_pos * 32 + pi];
-      const float ne = e0 * c - o0 * s, no = e0 * s + o0 * c;
+      const float c = p.rope_cos[(size_t)rope_pos * 32 + pi], sn = -p.rope_sin[(size_t)rope_pos * 32 + pi];
+      const float ne = e0 * c - o0 * sn, no = e0 * sn + o0 * c;
       e0 = ne;
       o0 = no;
     }
@@ -377,7 +392,8 @@ cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
   attn_kernel<<<grid, 256, kSmemTotal, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nsplit == 1) return e;
-  attn_combine_kernel<<<p.T, 256, 0, st>>>(p, nsplit);
+  if (nsplit > kMaxSplits) return cudaErrorInvalidValue;
+  attn_combine_kernel<<<dim3(p.T, kH), 256, 0, st>>>(p, nsplit);
   return cudaGetLastError();
 }
 

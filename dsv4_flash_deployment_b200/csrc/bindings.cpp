@@ -557,9 +557,24 @@ void markov_step(const Tensor& logits, int64_t blk, int64_t i, const Tensor& mlo
                             cur_stream()));
 }
 
-void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out) {
-  CUDA_OK(dsv4::argmax_rows(ptr<const float>(logits), (int)T, (int)V, (int)logits.stride(0), ptr<int>(out),
-                            cur_stream()));
+// scratch: optional int32 [2 * max(T, 296) + T]; its tail (T entries) must start zeroed and is left zeroed
+void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out, const optional<Tensor>& scratch) {
+  float* wv = nullptr;
+  int* wi = nullptr;
+  int* cnt = nullptr;
+  if (scratch) {
+    const int64_t cap = std::max<int64_t>(T, 296);
+    TORCH_CHECK(scratch->scalar_type() == at::kInt && scratch->numel() >= 2 * cap + T, "argmax scratch too small");
+    const int64_t n = scratch->numel();
+    int* base = ptr<int>(*scratch);
+    const int64_t tail = n - T;   // counters live at the fixed end of the buffer
+    wv = reinterpret_cast<float*>(base);
+    wi = base + cap;
+    cnt = base + tail;
+    TORCH_CHECK(cap * 2 <= tail, "argmax scratch too small");
+  }
+  CUDA_OK(dsv4::argmax_rows(ptr<const float>(logits), (int)T, (int)V, (int)logits.stride(0), ptr<int>(out), wv, wi,
+                            cnt, cur_stream()));
 }
 
 

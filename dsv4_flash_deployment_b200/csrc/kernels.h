@@ -236,7 +236,10 @@ cudaError_t engram_gate(__nv_bfloat16* X, const __nv_bfloat16* kv, const float* 
 // -------------------------------------------------------------- misc.cu
 cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
                           cudaStream_t st);
-cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st);
+// ws_v/ws_i: >= max(T, 296) entries; counters: >= T ints, zero (left zero); all null = one CTA per row
+int argmax_splits(int T);
+cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, float* ws_v, int* ws_i, int* counters,
+                        cudaStream_t st);
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
                         int* toks, int ts, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st);
 

@@ -2,6 +2,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace dsv4 {
 
 // X[t, i, :] = table[ids[t], :] for every stream i (reference.py:909-911).
@@ -23,29 +25,52 @@ cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int
 }
 
 // out[t] = argmax_v logits[t, v] (first index on ties).
-__global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int V, int ld, int* out) {
-  const int t = blockIdx.x;
+//
+// Grid (S, T): CTA s of row t scans columns [s*chunk, (s+1)*chunk) with
+// float4 loads (4 in flight per thread), writes its (value, index) to ws, and
+// the last CTA of the row to arrive (counter per row, reset by that CTA)
+// merges the S partials in order.  S spreads a few rows over many SMs: a
+// 129K-entry row read by one CTA is latency-bound.
+DSV4_DEV void better(float& bv, int& bi, float ov, int oi) {
+  if (ov > bv || (ov == bv && oi < bi)) {
+    bv = ov;
+    bi = oi;
+  }
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int* out,
+                                                     float* ws_v, int* ws_i, int* counters) {
+  const int t = blockIdx.y, s = blockIdx.x, S = gridDim.x;
   const float* row = logits + (size_t)t * ld;
+  const int chunk = ((V + S - 1) / S + 3) & ~3;
+  const int v0 = s * chunk, v1 = min(V, v0 + chunk);
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = row[v];
-    if (x > bv) {
-      bv = x;
-      bi = v;
+  const bool vec = (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (vec) {
+    const int n4 = (v1 - v0) >> 2;
+    const float4* r4 = reinterpret_cast<const float4*>(row + v0);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 x = r4[i];
+      const int v = v0 + 4 * i;
+      better(bv, bi, x.x, v);
+      better(bv, bi, x.y, v + 1);
+      better(bv, bi, x.z, v + 2);
+      better(bv, bi, x.w, v + 3);
     }
+    for (int v = v0 + 4 * n4 + threadIdx.x; v < v1; v += blockDim.x) better(bv, bi, row[v], v);
+  } else {
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) better(bv, bi, row[v], v);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
-    }
+    better(bv, bi, ov, oi);
   }
-  __shared__ float sv[16];
-  __shared__ int si[16];
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  __shared__ bool s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     sv[warp] = bv;
@@ -53,18 +78,34 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
-        bv = sv[w];
-        bi = si[w];
-      }
-    out[t] = bi;
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    if (S == 1) {
+      out[t] = bi;
+    } else {
+      ws_v[(size_t)t * S + s] = bv;
+      ws_i[(size_t)t * S + s] = bi;
+      __threadfence();
+      s_last = atomicAdd(&counters[t], 1) == S - 1;
+    }
   }
+  if (S == 1) return;
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  float fv = -INFINITY;
+  int fi = 0x7fffffff;
+  for (int k = 0; k < S; ++k) better(fv, fi, __ldcg(ws_v + (size_t)t * S + k), __ldcg(ws_i + (size_t)t * S + k));
+  out[t] = fi;
+  counters[t] = 0;
 }
 
-cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, cudaStream_t st) {
+int argmax_splits(int T) { return T >= 148 ? 1 : std::min(32, 296 / std::max(T, 1)); }
+
+cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, float* ws_v, int* ws_i, int* counters,
+                        cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  argmax_kernel<<<T, 512, 0, st>>>(logits, V, ld, out);
+  const int S = (ws_v && ws_i && counters) ? argmax_splits(T) : 1;
+  argmax_kernel<<<dim3(S, T), 256, 0, st>>>(logits, V, ld, out, ws_v, ws_i, counters);
   return cudaGetLastError();
 }
 

@@ -203,6 +203,8 @@ class DSV4Model:
         self.u_sample = e(self.max_sample, D)
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
         self.next_ids = e(self.max_sample, dt=i32)
+        # multi-CTA argmax: partials [2 * max(S, 296)] + zeroed per-row counters at the end
+        self.argmax_scratch = z(2 * max(self.max_sample, 296) + self.max_sample, dt=i32)
         # split-K scratch (reused sequentially on the stream)
         self.ws = e(8 * 1024 * 1024, dt=f32)
         self.counters = z(65536, dt=i32)
@@ -406,7 +408,7 @@ class DSV4Model:
         with self._t("head"):
             torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
             self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
-            ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S])
+            ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch)
         return self.next_ids[:S]
 
     # ------------------------------------------------- deferred ring commits
