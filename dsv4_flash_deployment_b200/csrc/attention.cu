@@ -83,6 +83,11 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   }
   // ---------------- Q: optional head norm, RoPE, into smem
   for (int h = warp; h < kH; h += 8) {
+    if (h >= p.n_heads) {   // padding rows of the head tile
+      *reinterpret_cast<uint4*>(sQ + (size_t)h * kRowE + lane * 16) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sQ + (size_t)h * kRowE + lane * 16 + 8) = make_uint4(0, 0, 0, 0);
+      continue;
+    }
     const __nv_bfloat16* qg = p.q + (size_t)t * p.q_stride + (size_t)h * kDh;
     float v[16];
     {
@@ -290,6 +295,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int h = mt * 16 + g + 8 * half;
+        if (h >= p.n_heads) continue;
         const float den = sSum[h] + expf(p.sink[h] - sMax[h]);
         const float inv = 1.f / den;
 #pragma unroll
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
             e = ne;
             o = no;
           }
-          *reinterpret_cast<uint32_t*>(p.out + (size_t)t * kH * kDh + (size_t)h * kDh + d) = pack_bf16(e, o);
+          *reinterpret_cast<uint32_t*>(p.out + (size_t)t * p.out_stride + (size_t)h * kDh + d) = pack_bf16(e, o);
         }
       }
     }
@@ -374,7 +380,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p, int nsp
       e0 = ne;
       o0 = no;
     }
-    *reinterpret_cast<uint32_t*>(p.out + (size_t)t * kH * kDh + (size_t)h * kDh + d) = pack_bf16(e0, o0);
+    *reinterpret_cast<uint32_t*>(p.out + (size_t)t * p.out_stride + (size_t)h * kDh + d) = pack_bf16(e0, o0);
   }
 }
 
@@ -382,6 +388,7 @@ size_t attn_smem_bytes() { return kSmemTotal; }
 
 cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
+  if (p.n_heads < 1 || p.n_heads > kH) return cudaErrorInvalidValue;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
@@ -393,7 +400,7 @@ cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nsplit == 1) return e;
   if (nsplit > kMaxSplits) return cudaErrorInvalidValue;
-  attn_combine_kernel<<<dim3(p.T, kH), 256, 0, st>>>(p, nsplit);
+  attn_combine_kernel<<<dim3(p.T, p.n_heads), 256, 0, st>>>(p, nsplit);
   return cudaGetLastError();
 }
 

@@ -45,13 +45,30 @@ int tma_elem_of(const Tensor& t, bool e2m1) {
 //   kind 0: bf16 x bf16; 1: e4m3 x e4m3 (MXFP8); 2: e2m1 (A) x e4m3 (B).
 //   A [a_rows, K] (packed e2m1: [a_rows, K/2]); B [b_rows, K].
 //   grouped: tiles int32 [n, 4] + n_tiles int32 [1] device tensors.
+// Optional int64 CPU tensor [peer_sig table, sig, done, epoch, phase, world, rank] of device
+// addresses / values -> PeerSync (all zero = none)
+static dsv4::PeerSync peer_sync_of(const optional<Tensor>& t) {
+  dsv4::PeerSync s{};
+  if (!t) return s;
+  TORCH_CHECK(!t->is_cuda() && t->scalar_type() == at::kLong && t->numel() >= 7, "peer sync: int64 CPU [7]");
+  const int64_t* v = t->data_ptr<int64_t>();
+  s.peer_sig = reinterpret_cast<uint32_t* const*>(v[0]);
+  s.sig = reinterpret_cast<const uint32_t*>(v[1]);
+  s.done = reinterpret_cast<int*>(v[2]);
+  s.epoch = reinterpret_cast<uint32_t*>(v[3]);
+  s.phase = (int)v[4];
+  s.world = (int)v[5];
+  s.rank = (int)v[6];
+  return s;
+}
+
 void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_sf, const Tensor& B,
           const optional<Tensor>& B_sf, const optional<Tensor>& out, int64_t M, int64_t N, int64_t K, int64_t bn,
           int64_t splits, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
           const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
           double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
           const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
-          int64_t probe) {
+          int64_t probe, const optional<Tensor>& publish) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -107,6 +124,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.tile_counters = counters ? counters->data_ptr<int>() : nullptr;
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
   p.probe = (int)probe;
+  p.pub = peer_sync_of(publish);
   if (p.splits > 1 && !(workspace && counters)) {
     // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
     // Halve the split count until every tile's cluster is resident at once.
@@ -129,7 +147,10 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
     p.n_tiles = (int)(M / 128) * (int)((N + bn - 1) / bn);
     units = p.n_tiles * p.splits;
   }
-  if (units == 0) return;
+  if (units == 0) {
+    TORCH_CHECK(!publish, "a publishing GEMM must launch");
+    return;
+  }
   int grid = p.cluster_split ? units : std::min(units, max_grid > 0 ? (int)max_grid : num_sms());
   CUDA_OK(dsv4::gemm_launch((int)kind, (int)epi, grouped, (int)bn, ta, tb, p, grid, cur_stream()));
 }
@@ -219,10 +240,27 @@ dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optio
 void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
              int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn_hilo,
              const optional<Tensor>& cw, int64_t cw_stride, const Tensor& c, const Tensor& partials,
-             const optional<Tensor>& tap, int64_t T) {
+             const optional<Tensor>& tap, int64_t T, const optional<Tensor>& tp, const optional<Tensor>& err) {
   auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, fn_hilo, c10::nullopt, c10::nullopt, cw, cw_stride,
                      c10::nullopt, c10::nullopt, c, partials, c10::nullopt, c10::nullopt, c10::nullopt, tap, T, 0, 0,
                      0);
+  if (tp) {
+    // int64 CPU [mode, peer_sig, sig, done, epoch, phase, world, rank, peer_y, peer_yperm, peer_pos, ids, e_local]
+    TORCH_CHECK(!tp->is_cuda() && tp->scalar_type() == at::kLong && tp->numel() >= 13, "tp: int64 CPU [13]");
+    TORCH_CHECK(err.has_value(), "tp mode needs the error word");
+    const int64_t* v = tp->data_ptr<int64_t>();
+    p.tp_mode = (int)v[0];
+    p.wait = peer_sync_of(tp->narrow(0, 1, 7));
+    p.peer_y = reinterpret_cast<const float* const*>(v[8]);
+    p.peer_yperm = reinterpret_cast<const bf16* const*>(v[9]);
+    p.peer_pos = reinterpret_cast<const int* const*>(v[10]);
+    p.ids = reinterpret_cast<const int*>(v[11]);
+    p.e_local = (int)v[12];
+    p.err = reinterpret_cast<uint32_t*>(err->data_ptr<int>());
+    TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
+                "tp mode tables missing");
+    TORCH_CHECK(p.tp_mode == 1 || p.tp_mode == 2, "tp mode must be 1 or 2");
+  }
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));
 }
@@ -245,11 +283,17 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
                const Tensor& sink, double scale, const Tensor& out, const optional<Tensor>& workspace, int64_t T,
                int64_t nsplit, const optional<Tensor>& win_end, int64_t win_len) {
   CHECK_CUDA(q);
-  TORCH_CHECK(q.size(-1) == 512 && q.size(-2) == 64, "q must be [T, 64, 512]");
+  TORCH_CHECK(q.dim() == 3 && q.size(-1) == 512 && q.size(-2) <= 64 && q.stride(1) == 512 && q.stride(2) == 1,
+              "q must be [T, H <= 64, 512]");
+  TORCH_CHECK(out.dim() == 3 && out.size(1) == q.size(1) && out.stride(1) == 512 && out.stride(2) == 1,
+              "out must be [T, H, 512]");
+  TORCH_CHECK(sink.numel() >= q.size(1), "sink must hold every head");
   dsv4::AttnParams p{};
   p.T = (int)T;
   p.q = ptr<const bf16>(q);
-  p.q_stride = 64 * 512;
+  p.q_stride = (int)q.stride(0);
+  p.n_heads = (int)q.size(1);
+  p.out_stride = (int)out.stride(0);
   p.rope_cos = ptr<const float>(cos);
   p.rope_sin = ptr<const float>(sin);
   p.rope_pos = ptr<const int>(rope_pos);
@@ -558,7 +602,8 @@ void markov_step(const Tensor& logits, int64_t blk, int64_t i, const Tensor& mlo
 }
 
 // scratch: optional int32 [2 * max(T, 296) + T]; its tail (T entries) must start zeroed and is left zeroed
-void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out, const optional<Tensor>& scratch) {
+void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out, const optional<Tensor>& scratch,
+                 const optional<Tensor>& out_val, int64_t idx_base) {
   float* wv = nullptr;
   int* wi = nullptr;
   int* cnt = nullptr;
@@ -574,7 +619,15 @@ void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out, 
     TORCH_CHECK(cap * 2 <= tail, "argmax scratch too small");
   }
   CUDA_OK(dsv4::argmax_rows(ptr<const float>(logits), (int)T, (int)V, (int)logits.stride(0), ptr<int>(out), wv, wi,
-                            cnt, cur_stream()));
+                            cnt, ptr<float>(out_val), (int)idx_base, cur_stream()));
+}
+
+// sync: int64 CPU [7] (PeerSync); peer_val / peer_idx: int64 device tables of each rank's pairs
+void tp_argmax_merge(const Tensor& sync, const Tensor& peer_val, const Tensor& peer_idx, int64_t T, const Tensor& out,
+                     const Tensor& err) {
+  CUDA_OK(dsv4::tp_argmax_merge(peer_sync_of(sync), reinterpret_cast<const float* const*>(peer_val.data_ptr()),
+                                reinterpret_cast<const int* const*>(peer_idx.data_ptr()), (int)T, ptr<int>(out),
+                                reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream()));
 }
 
 
@@ -612,5 +665,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_unpack_rows", &ep_unpack_rows);
   m.def("ep_combine_pack", &ep_combine_pack);
   m.def("argmax_rows", &argmax_rows);
+  m.def("tp_argmax_merge", &tp_argmax_merge);
   m.def("markov_step", &markov_step);
 }

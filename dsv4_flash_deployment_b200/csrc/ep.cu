@@ -14,6 +14,7 @@
 // buffer).
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 #include <algorithm>
 
@@ -28,16 +29,6 @@ namespace dsv4 {
 // reached the epoch, bounded by kWaitLimitNs.  Epochs advance once per call
 // on every rank (all ranks run the same sequence of MoE layers), so no reset
 // is needed between CUDA-graph replays.
-DSV4_DEV void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-DSV4_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Called by every CTA at its end (all threads).  The last CTA publishes.
 DSV4_DEV void grid_publish(const EpSync& s, const int* cnt, int world, int my_rank, int cap) {
   __syncthreads();

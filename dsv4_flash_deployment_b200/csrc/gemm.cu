@@ -34,6 +34,7 @@
 // for the W2 GEMM, so the intermediate never leaves the chip in high precision.
 #include "common.cuh"
 #include "gemm.h"
+#include "peer.cuh"
 
 namespace dsv4 {
 
@@ -492,6 +493,7 @@ done:
     tc_fence_after();
     tmem_dealloc(tmem, L::kTmemCols);
   }
+  peer_publish_grid(p.pub);
 }
 
 // ------------------------------------------------------------------- host

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "peer.h"
+
 namespace dsv4 {
 
 enum GemmKind { KIND_BF16 = 0, KIND_MX8 = 1, KIND_MX4A = 2 };
@@ -41,6 +43,9 @@ struct GemmParams {
   int* tile_counters;
   int cluster_split;
   int probe;           // measurement only: bit 0 = no MMA (stages released as they land), bit 1 = no output stores
+  // optional: after the last CTA has stored its tiles, publish the phase to every
+  // peer (tensor-parallel partial sums read by the next kernel over NVLink)
+  PeerSync pub;
   uint32_t* err;
 };
 

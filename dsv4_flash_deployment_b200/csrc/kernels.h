@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "peer.h"
+
 namespace dsv4 {
 
 // ------------------------------------------------------------ quant.cu
@@ -37,6 +39,19 @@ struct HcParams {
   __nv_bfloat16* tap;               // optional [T, D] mean of the updated streams
   int iters;
   float hc_eps, norm_eps;
+  // tensor parallel (hc_post): tp_mode 1 = the sublayer output is the rank-order
+  // sum of every rank's f32 partial (peer_y, rows D apart); tp_mode 2 = each
+  // (token, slot) pair's expert row is read from the rank owning its expert
+  // (peer_yperm / peer_pos; ids are identical on every rank).  Both wait first
+  // (bounded) until every rank has published the phase.
+  int tp_mode;
+  const float* const* peer_y;
+  const __nv_bfloat16* const* peer_yperm;
+  const int* const* peer_pos;
+  const int* ids;
+  int e_local;
+  PeerSync wait;
+  uint32_t* err;
 };
 int hc_num_slices(int D);
 cudaError_t hc_post(const HcParams& p, cudaStream_t st);
@@ -46,8 +61,11 @@ cudaError_t hc_finish(const HcParams& p, cudaStream_t st);
 constexpr int kAttnMaxRows = 768;   // window (<= 256) + selected compressed rows
 struct AttnParams {
   int T;
-  const __nv_bfloat16* q;           // [T, 64, 512]
+  const __nv_bfloat16* q;           // [T, n_heads, 512] rows q_stride apart
   int q_stride;
+  int n_heads;                      // <= 64 (tensor parallel: this rank's heads; the rest of the
+                                    // 64-head tile computes on zero queries and is not stored)
+  int out_stride;
   const float* rope_cos;            // [positions, 32]
   const float* rope_sin;
   const int* rope_pos;              // optional rope position (default pos)
@@ -68,9 +86,9 @@ struct AttnParams {
   const int* win_end;               // optional last window position per token (default pos): a
                                     // draft block attends to all of its rows (bidirectional)
   int win_len;                      // window rows (default W)
-  const float* sink;                // [64]
+  const float* sink;                // [n_heads]
   float scale;
-  __nv_bfloat16* out;               // [T, 64, 512]
+  __nv_bfloat16* out;               // [T, n_heads, 512] rows out_stride apart
   float* workspace;                 // split partials
 };
 size_t attn_smem_bytes();
@@ -238,8 +256,11 @@ cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int
                           cudaStream_t st);
 // ws_v/ws_i: >= max(T, 296) entries; counters: >= T ints, zero (left zero); all null = one CTA per row
 int argmax_splits(int T);
+// out_val (optional) receives the best value; idx_base is added to every index
 cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, float* ws_v, int* ws_i, int* counters,
-                        cudaStream_t st);
+                        float* out_val, int idx_base, cudaStream_t st);
+cudaError_t tp_argmax_merge(const PeerSync& s, const float* const* peer_val, const int* const* peer_idx, int T,
+                            int* out, uint32_t* err, cudaStream_t st);
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
                         int* toks, int ts, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st);
 

@@ -22,6 +22,7 @@
 //              Sinkhorn with one lane per comb entry, RMSNorm, MXFP8 quantization.
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 namespace dsv4 {
 
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
   const int D = p.D;
   const int d0 = slice * kSlice;
   const bool mixes = p.fn_hilo != nullptr;
-  const bool has_y = p.Y != nullptr || p.yperm != nullptr;
+  const bool has_y = p.Y != nullptr || p.yperm != nullptr || p.tp_mode != 0;
   const bool collapse = p.cw != nullptr;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (mixes) {
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
       *reinterpret_cast<uint4*>(sFn + row * kRowE + i * kSlice + ch * 8) = v;
     }
   }
+  if (p.tp_mode) peer_wait(p.wait, p.err, KID_COMM);   // the fn slice load above overlaps the wait
   const int tt = tid >> 4;            // token within the tile
   const int cc = (tid & 15) * 8;      // column offset within the slice
   const int t = t0 + tt;
@@ -94,7 +96,24 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
       float y[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) y[k] = 0.f;
-      if (p.yperm != nullptr) {
+      if (p.tp_mode == 2) {
+        // each pair's row lives on the rank that owns its expert
+        for (int s = 0; s < p.topk; ++s) {
+          const size_t pi = (size_t)t * p.topk + s;
+          const int owner = p.ids[pi] / p.e_local;
+          const int r = p.peer_pos[owner][pi];
+          if (r >= 0) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(p.peer_yperm[owner] + (size_t)r * D + d);
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(h2[k]);
+              y[2 * k] += f.x;
+              y[2 * k + 1] += f.y;
+            }
+          }
+        }
+      } else if (p.yperm != nullptr) {
         for (int s = 0; s < p.topk; ++s) {
           const int r = p.pos[(size_t)t * p.topk + s];
           if (r >= 0) {
@@ -109,7 +128,15 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
           }
         }
       }
-      if (p.Y != nullptr) {
+      if (p.tp_mode == 1) {
+        // rank-order sum of the f32 partials: the same bits on every rank
+        for (int rr = 0; rr < p.wait.world; ++rr) {
+          const float4* src = reinterpret_cast<const float4*>(p.peer_y[rr] + (size_t)t * D + d);
+          const float4 a = src[0], b = src[1];
+          y[0] += a.x; y[1] += a.y; y[2] += a.z; y[3] += a.w;
+          y[4] += b.x; y[5] += b.y; y[6] += b.z; y[7] += b.w;
+        }
+      } else if (p.Y != nullptr) {
         const uint4 raw = *reinterpret_cast<const uint4*>(p.Y + (size_t)t * D + d);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -119,7 +146,7 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
           y[2 * k + 1] += f.y;
         }
       }
-      if (p.yperm != nullptr) {
+      if (p.yperm != nullptr || p.tp_mode != 0) {   // the sublayer output is a bf16 tensor
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = __bfloat162float(__float2bfloat16(y[k]));
       }

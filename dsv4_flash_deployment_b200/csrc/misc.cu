@@ -1,6 +1,7 @@
 // Small fused kernels: embedding lookup into the residual streams, row argmax.
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 #include <algorithm>
 
@@ -39,7 +40,8 @@ DSV4_DEV void better(float& bv, int& bi, float ov, int oi) {
 }
 
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int* out,
-                                                     float* ws_v, int* ws_i, int* counters) {
+                                                     float* ws_v, int* ws_i, int* counters, float* out_val,
+                                                     int idx_base) {
   const int t = blockIdx.y, s = blockIdx.x, S = gridDim.x;
   const float* row = logits + (size_t)t * ld;
   const int chunk = ((V + S - 1) / S + 3) & ~3;
@@ -80,7 +82,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
   if (threadIdx.x == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
     if (S == 1) {
-      out[t] = bi;
+      out[t] = bi + idx_base;
+      if (out_val) out_val[t] = bv;
     } else {
       ws_v[(size_t)t * S + s] = bv;
       ws_i[(size_t)t * S + s] = bi;
@@ -95,17 +98,43 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
   float fv = -INFINITY;
   int fi = 0x7fffffff;
   for (int k = 0; k < S; ++k) better(fv, fi, __ldcg(ws_v + (size_t)t * S + k), __ldcg(ws_i + (size_t)t * S + k));
-  out[t] = fi;
+  out[t] = fi + idx_base;
+  if (out_val) out_val[t] = fv;
   counters[t] = 0;
 }
 
 int argmax_splits(int T) { return T >= 148 ? 1 : std::min(32, 296 / std::max(T, 1)); }
 
 cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, float* ws_v, int* ws_i, int* counters,
-                        cudaStream_t st) {
+                        float* out_val, int idx_base, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int S = (ws_v && ws_i && counters) ? argmax_splits(T) : 1;
-  argmax_kernel<<<dim3(S, T), 256, 0, st>>>(logits, V, ld, out, ws_v, ws_i, counters);
+  argmax_kernel<<<dim3(S, T), 256, 0, st>>>(logits, V, ld, out, ws_v, ws_i, counters, out_val, idx_base);
+  return cudaGetLastError();
+}
+
+// Vocab-parallel head: every rank holds (value, global index) of its shard's
+// best entry per row in symmetric memory.  One CTA publishes this rank's pairs,
+// waits (bounded) for every rank's, and keeps the best (the lower index on
+// ties, as a single argmax over the whole vocabulary would).  Every rank gets
+// the same ids.
+__global__ void __launch_bounds__(256) tp_argmax_merge_kernel(PeerSync s, const float* const* peer_val,
+                                                              const int* const* peer_idx, int T, int* out,
+                                                              uint32_t* err) {
+  peer_publish_cta(s);
+  peer_wait(s, err, KID_COMM);
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < s.world; ++r) better(bv, bi, peer_val[r][t], peer_idx[r][t]);
+    out[t] = bi;
+  }
+}
+
+cudaError_t tp_argmax_merge(const PeerSync& s, const float* const* peer_val, const int* const* peer_idx, int T,
+                            int* out, uint32_t* err, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  tp_argmax_merge_kernel<<<1, 256, 0, st>>>(s, peer_val, peer_idx, T, out, err);
   return cudaGetLastError();
 }
 

@@ -21,22 +21,30 @@ def _pad_rows(w: torch.Tensor) -> torch.Tensor:
 
 def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
-                ep=None) -> DSV4Model:
+                ep=None, tp=None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
     random weights on the device.  ``expert_storage_layers``: with random init,
     the number of distinct physical expert blocks (layers share them round-robin
     when the model does not fit one GPU).  ``ep``: expert-parallel group.
+    ``tp``: tensor-parallel group (parallel/tp.py): every rank draws or loads the
+    full weights with the same seed and keeps its shard of heads, output groups,
+    wo_b columns, experts and head rows.
     """
     dev = torch.device(device)
+    if tp is not None and ep is not None:
+        raise ValueError("tensor parallelism owns the experts itself; pass tp or ep, not both")
+    if tp is not None and (cfg.engram_layer_ids or cfg.n_mtp_layers):
+        raise NotImplementedError("tensor-parallel layout: V4 backbone without Engram / MTP stages")
+    par = ep if ep is not None else tp
     e_begin, e_local = 0, cfg.n_routed_experts
-    if ep is not None:
-        e_begin, e_local = ep.expert_range(cfg.n_routed_experts)
+    if par is not None:
+        e_begin, e_local = par.expert_range(cfg.n_routed_experts)
     layers = []
     if weights is not None:
         for lid in range(cfg.n_layers):
-            rng = ep.expert_range(cfg.n_experts_for(lid)) if ep is not None else None
+            rng = par.expert_range(cfg.n_experts_for(lid)) if par is not None else None
             layers.append(load_layer(cfg, weights, lid, dev, expert_range=rng))
         embed = weights["embed.weight"].to(dev)
         head = _pad_rows(weights["head.weight"]).to(dev)
@@ -52,8 +60,12 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
         head = _pad_rows((torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) / cfg.dim ** 0.5)
                          .to(torch.bfloat16))
         norm = (1.0 + 0.05 * torch.randn(cfg.dim, device=dev, generator=g)).to(torch.bfloat16)
+    if tp is not None:
+        for L in layers:
+            tp.shard_layer(cfg, L)
+        head = tp.shard_head(head, cfg.vocab_size)
     model = DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
-                      head_vocab=cfg.vocab_size)
+                      head_vocab=cfg.vocab_size, tp=tp)
     if cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
         model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed)

@@ -106,7 +106,7 @@ class StepMeta:
 class DSV4Model:
     def __init__(self, cfg, layers: list[LayerW], embed: torch.Tensor, head: torch.Tensor, norm_w: torch.Tensor,
                  max_tokens: int, n_slots: int, max_seq_len: int, device, ep=None, max_sample: int | None = None,
-                 head_vocab: int | None = None):
+                 head_vocab: int | None = None, tp=None):
         self.cfg = cfg
         self.layers = layers
         self.dev = torch.device(device)
@@ -118,6 +118,7 @@ class DSV4Model:
         self.n_slots = n_slots
         self.max_seq_len = max_seq_len
         self.ep = ep
+        self.tp = tp                          # tensor-parallel group (parallel/tp.py) or None
         self.max_sample = max_sample or max_tokens
         self.err = ErrorWord.get(self.dev)
         self.ext = _ext.load()
@@ -147,11 +148,14 @@ class DSV4Model:
         self.qr_q = e(Tp, qa, dt=u8)
         self.qr_sf = z(Tp // 128, qa // 128, 512, dt=u8)
         self.kv_step = e(T, cfg.head_dim)
-        self.q = e(T, cfg.n_heads, cfg.head_dim)
-        self.o = e(T, cfg.n_heads, cfg.head_dim)
-        self.oa = e(T, cfg.o_inter)
-        self.oa_q = e(Tp, cfg.o_inter, dt=u8)
-        self.oa_sf = z(Tp // 128, cfg.o_inter // 128, 512, dt=u8)
+        tpw = self.tp.world if self.tp is not None else 1
+        self.n_heads_local = cfg.n_heads // tpw
+        o_inter = cfg.o_inter // tpw
+        self.q = e(T, self.n_heads_local, cfg.head_dim)
+        self.o = e(T, self.n_heads_local, cfg.head_dim)
+        self.oa = e(T, o_inter)
+        self.oa_q = e(Tp, o_inter, dt=u8)
+        self.oa_sf = z(Tp // 128, o_inter // 128, 512, dt=u8)
         self.attn_out = e(T, D)
         self.proj = {co: e(T, 2 * co * cfg.head_dim, dt=f32)
                      for co in sorted({cfg.overlap(l) for l in cfg.kv_source_layer_ids})}
@@ -177,7 +181,11 @@ class DSV4Model:
                 self.route[kk] = (e(T, kk, dt=i32), e(T, kk, dt=f32), e(T, kk, dt=i32), e(T, kk, dt=i32))
         self.counts = e(E, dt=i32)
         self.seg = e(E, dt=i32)
-        e_local = E if self.ep is None else self.ep.experts_per_rank(E)
+        e_local = E
+        if self.ep is not None:
+            e_local = self.ep.experts_per_rank(E)
+        elif self.tp is not None:
+            e_local = self.tp.experts_per_rank(E)
         recv_rows = T * k if self.ep is None else self.ep.recv_rows(T, k)
         self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
         # 128-row expert tiles keep two accumulators in TMEM (epilogue overlaps the
@@ -205,6 +213,14 @@ class DSV4Model:
         self.next_ids = e(self.max_sample, dt=i32)
         # multi-CTA argmax: partials [2 * max(S, 296)] + zeroed per-row counters at the end
         self.argmax_scratch = z(2 * max(self.max_sample, 296) + self.max_sample, dt=i32)
+        if self.tp is not None:
+            # buffers peers read (expert rows, pair rows) live in symmetric memory
+            if len(self.route) != 1:
+                raise NotImplementedError("tensor parallelism with several routing widths (MTP stages)")
+            self.tp.alloc(T, D, self.cap, k, self.max_sample)
+            self.yperm = self.tp.buf("yperm")
+            ids_, wts_, _, rank_ = self.route[k]
+            self.route[k] = (ids_, wts_, self.tp.buf("pos"), rank_)
         # split-K scratch (reused sequentially on the stream)
         self.ws = e(8 * 1024 * 1024, dt=f32)
         self.counters = z(65536, dt=i32)
@@ -324,14 +340,16 @@ class DSV4Model:
                          bn=bn)
 
     def _hc(self, T, Y=None, yperm=None, pos=None, topk=0, prev=None, mixes=None, cw=None, norm=None,
-            mix_out=None, u=None, uq=None, usf=None, tap=None):
-        """One mHC boundary: post/combine/collapse + tensor-core mixes, then Sinkhorn + norm + quant."""
+            mix_out=None, u=None, uq=None, usf=None, tap=None, tp=None):
+        """One mHC boundary: post/combine/collapse + tensor-core mixes, then Sinkhorn + norm + quant.
+        ``tp``: tensor-parallel descriptor; the sublayer output is reduced from the peers."""
         cfg, ext = self.cfg, self.ext
         fnhl = scale = base = None
         if mixes is not None:
             fnhl, scale, base = mixes
         with self._t("hc_post"):
-            ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T)
+            ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T, tp,
+                        self.err)
         if mixes is not None or (cw is not None and u is not None):
             with self._t("hc_finish"):
                 ext.hc_finish(self.X, fnhl, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
@@ -376,8 +394,8 @@ class DSV4Model:
                 # the streams take the previous MoE output, then the Engram update, and
                 # only then this block's mixes and collapse (reference.py:925-931)
                 if moe_state is not None:
-                    yp, ps, kk = moe_state
-                    self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF)
+                    yp, ps, kk, td = moe_state
+                    self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, tp=td)
                 with self._t("engram"):
                     eng.apply(self, lid, T)
                 self._hc(T, prev=None, mixes=L.hc_attn, cw=cw if moe_state is None else self.mixF,
@@ -386,29 +404,40 @@ class DSV4Model:
                 self._hc(T, prev=None, mixes=L.hc_attn, cw=cw, norm=L.attn_norm, mix_out=self.mixA, u=self.u,
                          uq=self.uq, usf=self.usf, tap=tap)
             else:
-                yp, ps, kk = moe_state
+                yp, ps, kk, td = moe_state
                 self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
                          cw=self.mixF, norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf,
-                         tap=tap)
+                         tap=tap, tp=td)
             if trace is not None:
                 trace[lid] = self.X[:T].clone()
             self._attention(L, m)
             if trace is not None:
                 trace[f"attn{lid}"] = self.attn_out[:T].clone()
-            self._hc(T, Y=self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA, norm=L.ffn_norm,
-                     mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf)
+            tpa = self.tp.attn_desc() if self.tp is not None else None
+            self._hc(T, Y=None if tpa is not None else self.attn_out, prev=self.mixA, mixes=L.hc_ffn, cw=self.mixA,
+                     norm=L.ffn_norm, mix_out=self.mixF, u=self.u, uq=self.uq, usf=self.usf, tp=tpa)
             moe_state = self._moe(L, T)
         # final collapse + norm on all tokens, then head on the sampled rows
-        yp, ps, kk = moe_state
+        yp, ps, kk, td = moe_state
         self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=None, cw=self.mixF,
-                 norm=self.norm_w, u=self.u)
+                 norm=self.norm_w, u=self.u, tp=td)
         S = len(m.sample_rows)
         if S == 0:
             return self.next_ids[:0]
         with self._t("head"):
             torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
             self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
-            ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch)
+            if self.tp is None:
+                ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch, None, 0)
+            else:
+                # vocab-parallel head: best (value, index) of this shard, then the merge over ranks
+                tp = self.tp
+                r0, rows = tp.vocab_rows(self.vocab)
+                valid = max(0, min(rows, self.vocab - r0))
+                ext.argmax_rows(self.logits[:S], S, valid, tp.buf("aidx")[:S], self.argmax_scratch,
+                                tp.buf("aval")[:S], r0)
+                ext.tp_argmax_merge(tp.sync(2), tp.buf("peer_aval"), tp.buf("peer_aidx"), S, self.next_ids[:S],
+                                    self.err)
         return self.next_ids[:S]
 
     # ------------------------------------------------- deferred ring commits
@@ -496,12 +525,19 @@ class DSV4Model:
         else:
             with self._t("ring_update"):
                 ext.ring_update(ring, self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
+        groups = cfg.o_groups if self.tp is None else self.tp.groups(cfg.o_groups)
         with self._t("gemm_wo_a"):
-            self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=cfg.o_groups)
+            self._gemm_bf16(self.o.view(self.o.shape[0], -1), L.wo_a, self.oa, T, groups=groups)
         with self._t("quant_oa"):
             ext.act_quant_mx(self.oa[:T], self.oa_q, self.oa_sf)
         with self._t("gemm_wo_b"):
-            self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.attn_out)
+            if self.tp is None:
+                self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.attn_out)
+            else:
+                # this rank's wo_b input columns -> f32 partial in symmetric memory, published
+                # to the peers when the last tile is stored (reduced in the next mHC boundary)
+                self._gemm(self.oa_q, self.oa_sf, T, L.wo_b, self.tp.buf("part"), EPI_F32,
+                           publish=self.tp.sync(0))
 
     def _compress(self, L: LayerW, m: StepMeta, r: int):
         cfg, ext = self.cfg, self.ext
@@ -598,17 +634,21 @@ class DSV4Model:
         ext.router_topk(logits, T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale, ids, wts)
         rctx.__exit__(None, None, None)
         if self.ep is not None and self.ep.world > 1:
-            return self.ep.moe(self, L, T, k)
+            return self.ep.moe(self, L, T, k) + (None,)
+        e_begin, e_local = (0, E) if self.tp is None else self.tp.expert_range(E)
         pctx = self._t("moe_plan_scatter")
         pctx.__enter__()
-        ext.moe_plan(T, k, E, 0, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
+        ext.moe_plan(T, k, e_local, e_begin, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
                      self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err)
         ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf)
         pctx.__exit__(None, None, None)
         self._grouped(L, k)
         with self._t("shared_expert"):
             self._shared_expert(L, T)
-        return self.yperm, pos, k
+        if self.tp is not None:
+            # the next mHC boundary reads every pair's row from the rank owning its expert
+            return None, None, k, self.tp.moe_desc(ids, e_local)
+        return self.yperm, pos, k, None
 
     def _shared_expert(self, L: LayerW, T: int):
         cfg = self.cfg
@@ -625,10 +665,11 @@ class DSV4Model:
         c13.__enter__()
         ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                  self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, 0)
+                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, 0, None)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
         ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm, ex.w2.q.shape[0],
-                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1, 0)
+                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1, 0,
+                 self.tp.sync(1) if self.tp is not None else None)
         c2.__exit__(None, None, None)

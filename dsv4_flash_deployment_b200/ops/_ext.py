@@ -38,7 +38,7 @@ _KERNELS_PER_CALL = {"hc_post": 1, "hc_finish": 1, "attention": 1, "gemm": 1, "a
                      "indexer_topk": 2, "embed_streams": 1, "argmax_rows": 1, "act_roundtrip": 1,
                      "fp4_roundtrip": 1, "ep_pack": 1, "ep_unpack_meta": 1, "ep_unpack_rows": 1,
                      "ep_combine_pack": 1, "ep_wait": 1, "engram_gate": 1, "engram_prepare": 2,
-                     "markov_step": 1}
+                     "markov_step": 1, "tp_argmax_merge": 1}
 
 
 class _Counting:

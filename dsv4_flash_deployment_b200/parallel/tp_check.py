@@ -1,0 +1,142 @@
+"""Tensor-parallel self-check and decode timing (run under torchrun, one rank per GPU).
+
+Every rank builds the same small V4-shaped model (same checkpoint tensors)
+twice: whole on its GPU (the reference) and tensor-parallel over all ranks.
+All ranks step the same sequences; the tensor-parallel next tokens must match
+the local model's and each rank's logits shard must match the same rows of the
+local model's logits.  Then a one-token decode step is timed on the device
+(CUDA-graph replay and eager, max over ranks):
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m dsv4_flash_deployment_b200.parallel.tp_check
+
+Prints one JSON line on rank 0 and exits non-zero on a mismatch.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def small_cfg(n_layers: int = 3):
+    from .ep_check import small_cfg as cfg_of
+
+    return cfg_of(n_layers)
+
+
+def _meta(cfg, step: int, n_seq: int, plen: int):
+    from ..models.model import SeqChunk, StepMeta
+
+    g = torch.Generator().manual_seed(7)
+    prompts = torch.randint(16, cfg.vocab_size, (n_seq, plen), generator=g).tolist()
+    if step == 0:
+        return StepMeta(cfg, [SeqChunk(i, 0, prompts[i], True) for i in range(n_seq)])
+    return StepMeta(cfg, [SeqChunk(i, plen + step - 1, [(37 * i + 11 * step) % 1000 + 16], True)
+                          for i in range(n_seq)])
+
+
+def _time(model, meta, iters: int, graph: bool, dev) -> float:
+    for _ in range(3):
+        model.forward(meta)
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                model.forward(meta)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        if g is not None:
+            g.replay()
+        else:
+            model.forward(meta)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / iters], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    del g
+    return ms.item()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--seqs", type=int, default=3)
+    ap.add_argument("--plen", type=int, default=40)
+    ap.add_argument("--iters", type=int, default=30)
+    a = ap.parse_args(argv)
+
+    from ..engine.builder import build_model
+    from ..io.checkpoint_spec import make_random_weights
+    from ..models.model import SeqChunk, StepMeta
+    from ..ops.gemm import ErrorWord
+    from .tp import TPGroup
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    cfg = small_cfg()
+    w = make_random_weights(cfg, seed=11, include_mtp=False)
+    ref = build_model(cfg, dev, max_tokens=256, n_slots=a.seqs + 1, max_seq_len=256, weights=w)
+    tp = TPGroup(rank, world, dist.group.WORLD, dev)
+    m = build_model(cfg, dev, max_tokens=256, n_slots=a.seqs + 1, max_seq_len=256, weights=w, tp=tp)
+    r0, rows = tp.vocab_rows(cfg.vocab_size)
+    valid = max(0, min(rows, cfg.vocab_size - r0))
+    worst, agree, total = 1.0, 0, 0
+    for s in range(a.steps):
+        meta = _meta(cfg, s, a.seqs, a.plen)
+        for mod in (ref, m):
+            mod.upload(meta, {})
+        ids_ref = ref.forward(meta).clone()
+        lg_ref = ref.logits[:a.seqs, r0:r0 + valid].clone()
+        ids = m.forward(meta).clone()
+        lg = m.logits[:a.seqs, :valid].clone()
+        torch.cuda.synchronize()
+        ErrorWord.check(dev)
+        if valid:
+            cos = torch.nn.functional.cosine_similarity(lg.float(), lg_ref.float(), dim=-1).min().item()
+            worst = min(worst, cos)
+        agree += int((ids == ids_ref).sum())
+        total += ids.numel()
+    good = worst > 0.999 and agree >= total - 1
+    flag = torch.tensor([0 if good else 1], device=dev)
+    dist.all_reduce(flag)
+    # decode timing: one token of one sequence (C=1), graph replay and eager
+    tm = StepMeta(cfg, [SeqChunk(0, a.plen + a.steps, [123], True)])
+    m.upload(tm, {})
+    ms_graph = _time(m, tm, a.iters, True, dev)
+    ms_eager = _time(m, tm, a.iters, False, dev)
+    ErrorWord.check(dev)
+    ref.upload(tm, {})
+    ms_one = _time(ref, tm, a.iters, True, dev)
+    res = {"world": world, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
+           "decode_ms_graph": round(ms_graph, 4), "decode_ms_eager": round(ms_eager, 4),
+           "decode_ms_one_gpu_graph": round(ms_one, 4), "layers": cfg.n_layers}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    del m
+    tp.release()
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    raise SystemExit(0 if flag.item() == 0 else 1)
+
+
+if __name__ == "__main__":
+    main()

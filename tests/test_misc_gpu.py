@@ -24,7 +24,7 @@ def test_argmax_rows_matches_torch(T, V):
     for use_scratch in (False, True):
         out = torch.full((T,), -1, dtype=torch.int32, device="cuda")
         for _ in range(3):   # counters must come back to zero between calls
-            ext.argmax_rows(logits, T, V, out, scratch if use_scratch else None)
+            ext.argmax_rows(logits, T, V, out, scratch if use_scratch else None, None, 0)
         want = torch.argmax(logits[:, :V], dim=1).int()
         torch.cuda.synchronize()
         assert torch.equal(out, want)
