@@ -4,10 +4,9 @@
 // code); it is an addition of this library.
 //
 // Who it is for: callers that cannot allocate device memory while they run.
-// Examples are code executing inside a CUDA stream capture that must not
-// change the allocator's state, real-time serving loops that forbid
-// cudaMalloc/cudaFree (both synchronize the device and can stall every stream),
-// and embedders with a fixed, pre-sized memory budget that owns every byte.
+// Examples are real-time serving loops that forbid cudaMalloc/cudaFree (both
+// synchronize the device and can stall every stream), and embedders with a
+// fixed, pre-sized memory budget that owns every byte.
 // The regular `gemm` binding expects the caller to pass a split-K workspace and
 // tile counters; this variant instead uses one scratch array that lives in the
 // library itself.

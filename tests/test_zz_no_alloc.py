@@ -1,9 +1,8 @@
 """The allocation-free GEMM entry point, called through its exported C symbol.
 
 ``dsv4_gemm_mx8_noalloc`` serves callers that may not allocate device memory
-while they run (inside a stream capture that must leave the allocator alone,
-real-time loops that forbid cudaMalloc/cudaFree, embedders with a fixed memory
-budget).  Its split-K scratch is a fixed array inside the library.  This test
+while they run (real-time loops that forbid cudaMalloc/cudaFree, which
+synchronize the device; embedders with a fixed memory budget).  Its split-K scratch is a fixed array inside the library.  This test
 checks it against the regular ``gemm`` binding (which takes a caller-allocated
 workspace) on two calls in a row, since calls share and reuse the array, and
 that oversized problems are refused without a launch.  The file sorts last so a
