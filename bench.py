@@ -145,6 +145,8 @@ def main() -> None:
     ap.add_argument("--chunk", type=int, default=None, help="prefill tokens per step (all ranks)")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--c1-layout", default="auto", choices=["auto", "tp", "dp"],
+                    help="C=1 TPOT on N>1 GPUs: tensor-parallel decode model (auto/tp) or the batch layout (dp)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert exchange: NVLink peer stores (p2p) or the NCCL all-to-all baseline")
     args = ap.parse_args()
@@ -325,6 +327,46 @@ def main() -> None:
     h2d = int(model.last_upload_bytes)
     d2h = 4 * (n_dec + 1)
 
+    # ------------------------------------------------ C=1 TPOT, tensor parallel
+    # N>1: the latency layout of the same model on the same GPUs: attention heads,
+    # wo_a groups, wo_b columns and head rows split over the ranks, the expert
+    # blocks shared with the batch model (same ownership); every rank runs the
+    # same 1-token step
+    c1_tp = None
+    if world > 1 and args.c1_layout in ("auto", "tp"):
+        from dsv4_flash_deployment_b200.parallel.tp import TPGroup
+        tpg = TPGroup(rank, world, group, dev)
+        eng_tp = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=16, max_seq_len=max_seq, tp=tpg,
+                              experts_from=model, use_graphs=not args.no_graphs, chunk_size=16)
+        rng_tp = np.random.default_rng(4321)   # the same tokens on every rank
+
+        def tp_meta(i):
+            return StepMeta(cfg, [SeqChunk(0, c1_pos + i, [int(rng_tp.integers(0, cfg.vocab_size))], True)])
+
+        for i in range(3):
+            eng_tp.run_meta(tp_meta(i))
+        tpm = [tp_meta(3 + i) for i in range(c1_steps)]
+        eng_tp.check_errors()
+        dist.barrier()
+        torch.cuda.synchronize()
+        c0, c1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        c0.record(eng_tp.stream)
+        for mm in tpm:
+            eng_tp.run_meta(mm)
+        c1e.record(eng_tp.stream)
+        torch.cuda.synchronize()
+        tp_wall = (time.perf_counter() - w0) / c1_steps * 1e3
+        tp_dev = c0.elapsed_time(c1e) / c1_steps
+        eng_tp.check_errors()
+        tp_t = torch.tensor([tp_dev, tp_wall], device=dev)
+        dist.all_reduce(tp_t, op=dist.ReduceOp.MAX)
+        c1_tp = tuple(float(x) for x in tp_t.tolist())
+        eng_tp.graphs.clear()
+        del eng_tp
+        tpg.release()
+        dist.barrier()
+
     if rank == 0:
         line = {
             "metric": METRIC if args.workload == "1k1k" else
@@ -356,9 +398,19 @@ def main() -> None:
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches_per_step * args.steps,
-            "c1_tpot_ms": {"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,
-                           "baseline_ms": 27.69, "note": "one sequence per rank, 1-token steps through "
-                           "Engine.run_meta (pinned H2D + D2H + sync each token), graph replay"},
+            "c1_tpot_ms": ({"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,
+                            "baseline_ms": 27.69, "layout": "batch layout (dp-attention x ep)" if world > 1
+                            else "single GPU",
+                            "note": "one sequence per rank, 1-token steps through Engine.run_meta (pinned H2D + "
+                                    "D2H + sync each token), graph replay"}
+                           if c1_tp is None else
+                           {"value": round(c1_tp[1], 3), "device_ms": round(c1_tp[0], 3), "context": c1_pos,
+                            "baseline_ms": 27.69,
+                            "layout": f"tp{world} attention/wo_b/head + ep{world} experts (no dispatch), "
+                                      "NVLink reductions inside the producing/consuming kernels",
+                            "batch_layout_ms": round(c1_wall, 3),
+                            "note": "one sequence, the same 1-token step on every rank through Engine.run_meta "
+                                    "(pinned H2D + D2H + sync each token), graph replay, max over ranks"}),
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -21,7 +21,7 @@ def _pad_rows(w: torch.Tensor) -> torch.Tensor:
 
 def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
-                ep=None, tp=None) -> DSV4Model:
+                ep=None, tp=None, experts_from: DSV4Model | None = None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -30,7 +30,9 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     when the model does not fit one GPU).  ``ep``: expert-parallel group.
     ``tp``: tensor-parallel group (parallel/tp.py): every rank draws or loads the
     full weights with the same seed and keeps its shard of heads, output groups,
-    wo_b columns, experts and head rows.
+    wo_b columns, experts and head rows.  ``experts_from``: random init only; the
+    layers reuse that model's expert blocks (a second layout of the same model on
+    the same GPUs, e.g. tensor-parallel decode next to the expert-parallel batch).
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -52,8 +54,13 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     else:
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
-        n_phys = expert_storage_layers or cfg.n_layers
-        stores = [random_experts(cfg, e_local, dev, g) for _ in range(min(n_phys, cfg.n_layers))]
+        if experts_from is not None:
+            stores = [L.experts for L in experts_from.layers]
+            if stores[0].n_experts != e_local:
+                raise ValueError("shared expert blocks belong to a different expert split")
+        else:
+            n_phys = expert_storage_layers or cfg.n_layers
+            stores = [random_experts(cfg, e_local, dev, g) for _ in range(min(n_phys, cfg.n_layers))]
         for lid in range(cfg.n_layers):
             layers.append(random_layer(cfg, lid, dev, g, stores[lid % len(stores)]))
         embed = (torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) * 0.02).to(torch.bfloat16)
