@@ -63,7 +63,9 @@ class SpecStats:
 class DSparkDrafter:
     """MTP stages, Markov head and the per-stage main-hidden rings on the device."""
 
-    def __init__(self, model, weights: dict, max_seqs: int):
+    def __init__(self, model, weights: dict | None, max_seqs: int, seed: int = 0):
+        """``weights``: checkpoint dict (``mtp.*`` names); None draws random stage
+        weights on the device (full-size benchmark runs without a checkpoint)."""
         cfg = model.cfg
         if cfg.n_mtp_layers < 1 or not cfg.dspark_target_layer_ids:
             raise ValueError("config has no DSpark stages")
@@ -71,15 +73,19 @@ class DSparkDrafter:
         self.ext = model.ext
         self.blk = cfg.dspark_block_size
         self.K = cfg.n_mtp_layers
-        self.stages = [load_layer(cfg, weights, cfg.n_layers + k, dev, prefix=f"mtp.{k}") for k in range(self.K)]
-        self.main_proj = MxWeight.from_checkpoint(weights["mtp.0.main_proj.weight"].to(dev),
-                                                  weights["mtp.0.main_proj.scale"].to(dev), dev)
-        self.main_norm = weights["mtp.0.main_norm.weight"].to(dev)
-        last = f"mtp.{self.K - 1}"
-        self.final_norm = weights[f"{last}.norm.weight"].to(dev)
-        self.memb = weights[f"{last}.markov_head.embed.weight"].to(dev, torch.bfloat16).contiguous()
-        self.mhead = _pad_rows(weights[f"{last}.markov_head.head.weight"].to(dev, torch.bfloat16))
-        self.conf_w = weights[f"{last}.confidence_head.proj.weight"].float().to(dev)
+        if weights is None:
+            self._random_init(seed)
+        else:
+            self.stages = [load_layer(cfg, weights, cfg.n_layers + k, dev, prefix=f"mtp.{k}")
+                           for k in range(self.K)]
+            self.main_proj = MxWeight.from_checkpoint(weights["mtp.0.main_proj.weight"].to(dev),
+                                                      weights["mtp.0.main_proj.scale"].to(dev), dev)
+            self.main_norm = weights["mtp.0.main_norm.weight"].to(dev)
+            last = f"mtp.{self.K - 1}"
+            self.final_norm = weights[f"{last}.norm.weight"].to(dev)
+            self.memb = weights[f"{last}.markov_head.embed.weight"].to(dev, torch.bfloat16).contiguous()
+            self.mhead = _pad_rows(weights[f"{last}.markov_head.head.weight"].to(dev, torch.bfloat16))
+            self.conf_w = weights[f"{last}.confidence_head.proj.weight"].float().to(dev)
         self.R = self.memb.shape[1]
         S = model.n_slots + 1
         W = cfg.sliding_window
@@ -98,6 +104,28 @@ class DSparkDrafter:
         self.mlog = torch.zeros(n, self.mhead.shape[0], dtype=torch.float32, device=dev)
         self.dummy_q = torch.zeros(ceil_to(T, 128), 128, dtype=torch.uint8, device=dev)
         self.dummy_sf = torch.zeros(ceil_to(T, 128) // 128, 1, 512, dtype=torch.uint8, device=dev)
+
+    def _random_init(self, seed: int) -> None:
+        """Stage layers (each with its own expert block), main_proj, norms and the
+        Markov / confidence heads drawn on the device, in the checkpoint layouts."""
+        from ..models.weights import _rand_mx, random_experts, random_layer
+
+        cfg, dev = self.cfg, self.m.dev
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 777)
+        D, V, R = cfg.dim, cfg.vocab_size, cfg.markov_rank
+        self.stages = []
+        for k in range(self.K):
+            lid = cfg.n_layers + k
+            ex = random_experts(cfg, cfg.n_experts_for(lid), dev, g)
+            self.stages.append(random_layer(cfg, lid, dev, g, ex))
+        nt = len(cfg.dspark_target_layer_ids)
+        self.main_proj = _rand_mx(D, nt * D, dev, g)
+        norm = lambda n: (1.0 + 0.05 * torch.randn(n, device=dev, generator=g)).to(torch.bfloat16)
+        self.main_norm, self.final_norm = norm(D), norm(D)
+        self.memb = (torch.randn(V, R, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.mhead = _pad_rows((torch.randn(V, R, device=dev, generator=g) / R ** 0.5).to(torch.bfloat16))
+        self.conf_w = torch.randn(1, D + R, device=dev, generator=g) * 0.02
 
     # ----------------------------------------------------------------- ingest
     def ingest(self, rows: torch.Tensor | None, T: int) -> None:
@@ -172,7 +200,7 @@ class SpecEngine:
     outputs then differ from greedy, the acceptance path is exercised.
     """
 
-    def __init__(self, model, weights: dict, max_seqs: int = 16, force_accept: int | None = None):
+    def __init__(self, model, weights: dict | None, max_seqs: int = 16, force_accept: int | None = None):
         self.m = model
         self.cfg = model.cfg
         self.drafter = DSparkDrafter(model, weights, max_seqs)

@@ -112,3 +112,25 @@ def test_lossless_vs_greedy():
     same = sum(int(a == b) for a, b in zip(got[0], want[0]))
     assert same >= 18, (got[0], want[0])
     assert eng.stats.rounds > 0 and len(got[1]) == 20
+
+
+def test_random_init_drafter_forced_acceptance():
+    """Device-drawn MTP stages (no checkpoint, as the full-size benchmark runs):
+    with the forced-acceptance knob every round emits force+1 tokens and the
+    error word stays clear; the first token equals plain greedy decoding."""
+    from dsv4_flash_deployment_b200.ops.gemm import ErrorWord
+    from dsv4_flash_deployment_b200.spec.dspark import SpecEngine
+
+    cfg = spec_cfg()
+    model = build_model(cfg, "cuda", max_tokens=64, n_slots=3, max_seq_len=256, seed=5)
+    prompt = list(range(20, 53))
+    want = _greedy(model, cfg, prompt, 1)
+    model2 = build_model(cfg, "cuda", max_tokens=64, n_slots=3, max_seq_len=256, seed=5)
+    eng = SpecEngine(model2, None, max_seqs=2, force_accept=3)
+    out = eng.generate([prompt], 13)
+    torch.cuda.synchronize()
+    ErrorWord.check("cuda")
+    assert out[0][0] == want[0]
+    assert len(out[0]) == 13
+    st = eng.stats.as_dict()
+    assert st["rounds"] == 3 and st["accepted"] == 9 and st["histogram"][3] == 3
