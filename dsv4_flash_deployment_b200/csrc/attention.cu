@@ -40,6 +40,7 @@ constexpr size_t kSmemTotal = kSmemQ + 2 * kSmemKV + kSmemP + kSmemRows + kSmemS
 }  // namespace
 
 __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
+  pdl_entry();
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* sKV = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ);
@@ -343,6 +344,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
 // in shared memory; each thread then issues nsplit independent float2 loads.
 constexpr int kMaxSplits = 32;
 __global__ void __launch_bounds__(256) attn_combine_kernel(AttnParams p, int nsplit) {
+  pdl_entry();
   const int t = blockIdx.x, h = blockIdx.y;
   __shared__ float sF[kMaxSplits];
   __shared__ float sInv;
@@ -396,11 +398,11 @@ cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(p.T, nsplit);
-  attn_kernel<<<grid, 256, kSmemTotal, st>>>(p);
+  launch_pdl(attn_kernel, grid, 256, kSmemTotal, st, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nsplit == 1) return e;
   if (nsplit > kMaxSplits) return cudaErrorInvalidValue;
-  attn_combine_kernel<<<dim3(p.T, p.n_heads), 256, 0, st>>>(p, nsplit);
+  launch_pdl(attn_combine_kernel, dim3(p.T, p.n_heads), 256, 0, st, p, nsplit);
   return cudaGetLastError();
 }
 

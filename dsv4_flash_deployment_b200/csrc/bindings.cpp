@@ -622,6 +622,13 @@ void argmax_rows(const Tensor& logits, int64_t T, int64_t V, const Tensor& out, 
                             cnt, ptr<float>(out_val), (int)idx_base, cur_stream()));
 }
 
+// measurement: stamps int64 [1 + 2 * ctas]
+void pdl_probe(const Tensor& stamps, int64_t ctas, int64_t ns) {
+  TORCH_CHECK(stamps.numel() >= 1 + 2 * ctas && stamps.scalar_type() == at::kLong, "stamps: int64 [1 + 2 ctas]");
+  CUDA_OK(dsv4::pdl_probe(reinterpret_cast<unsigned long long*>(stamps.data_ptr()), (int)ctas,
+                          (unsigned long long)ns, cur_stream()));
+}
+
 // sync: int64 CPU [7] (PeerSync); peer_val / peer_idx: int64 device tables of each rank's pairs
 void tp_argmax_merge(const Tensor& sync, const Tensor& peer_val, const Tensor& peer_idx, int64_t T, const Tensor& out,
                      const Tensor& err) {
@@ -666,5 +673,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_pack", &ep_combine_pack);
   m.def("argmax_rows", &argmax_rows);
   m.def("tp_argmax_merge", &tp_argmax_merge);
+  m.def("pdl_probe", &pdl_probe);
   m.def("markov_step", &markov_step);
 }

@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define DSV4_DEV __device__ __forceinline__
 
 namespace dsv4 {
@@ -52,6 +54,40 @@ DSV4_DEV uint64_t globaltimer_ns() {
 // Default limit for any device-side wait (2 s).  A healthy pipeline waits
 // microseconds; only a bug or a dead peer reaches this.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ------------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream
+// serialization (launch_pdl) and begins with pdl_entry(): it lets the next
+// kernel of the stream be scheduled right away (its CTAs take free SM slots
+// and run their own preamble, e.g. a GEMM's weight prefetch) and then waits
+// until the previous kernel has completed and its writes are visible.  Nothing
+// that depends on, or overwrites, another kernel's data may run before
+// pdl_wait().  Without the launch attribute both are no-ops.
+DSV4_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+DSV4_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DSV4_DEV void pdl_entry() {
+  pdl_trigger();
+  pdl_wait();
+}
+
+// DSV4_PDL=0 in the environment turns the launch attribute off (A/B timing).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 DSV4_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

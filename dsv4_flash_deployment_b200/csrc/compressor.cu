@@ -43,6 +43,7 @@ DSV4_DEV float block_sum(float v, float* red) {
 // independent online softmax over every 4th slot, merged through shared
 // memory.  Then thread d owns latent dim d (dh == 512).
 __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
+  pdl_entry();
   __shared__ float red[32];
   __shared__ __nv_bfloat16 lat[512];
   __shared__ float kbuf[256];
@@ -181,13 +182,14 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
 cudaError_t compress_pool(const CompParams& p, cudaStream_t st) {
   if (p.n_groups == 0) return cudaSuccess;
   if (p.dh != 512 || (p.wk && (p.idx_dim % 32 || p.idx_dim > 256))) return cudaErrorInvalidValue;
-  compress_pool_kernel<<<p.n_groups, 512, 0, st>>>(p);
+  launch_pdl(compress_pool_kernel, p.n_groups, 512, 0, st, p);
   return cudaGetLastError();
 }
 
 template <typename T>
 __global__ void ring_update_kernel(T* ring, int depth, int width, const T* src, int T_, const int* slot,
                                    const int* pos, const int* last_pos) {
+  pdl_entry();
   const int t = blockIdx.x;
   if (t >= T_) return;
   const int ps = pos[t];
@@ -202,14 +204,14 @@ __global__ void ring_update_kernel(T* ring, int depth, int width, const T* src, 
 cudaError_t ring_update_f32(float* ring, int depth, int width, const float* src, int T, const int* slot,
                             const int* pos, const int* last_pos, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ring_update_kernel<float><<<T, 256, 0, st>>>(ring, depth, width, src, T, slot, pos, last_pos);
+  launch_pdl(ring_update_kernel<float>, T, 256, 0, st, ring, depth, width, src, T, slot, pos, last_pos);
   return cudaGetLastError();
 }
 
 cudaError_t ring_update_bf16(__nv_bfloat16* ring, int depth, int width, const __nv_bfloat16* src, int T,
                              const int* slot, const int* pos, const int* last_pos, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ring_update_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(ring, depth, width, src, T, slot, pos, last_pos);
+  launch_pdl(ring_update_kernel<__nv_bfloat16>, T, 256, 0, st, ring, depth, width, src, T, slot, pos, last_pos);
   return cudaGetLastError();
 }
 

@@ -25,6 +25,7 @@ DSV4_DEV int64_t floor_mod64(int64_t a, int64_t m) {
 }
 
 __global__ void engram_hash_kernel(EngramParams p) {
+  pdl_entry();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= p.T * p.nl) return;
   const int t = i / p.nl, l = i % p.nl;
@@ -55,6 +56,7 @@ __global__ void engram_hash_kernel(EngramParams p) {
 }
 
 __global__ void engram_ring_kernel(EngramParams p) {
+  pdl_entry();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= p.T) return;
   const int pos = p.pos[t];
@@ -64,6 +66,7 @@ __global__ void engram_ring_kernel(EngramParams p) {
 
 // one thread per 16 bytes of a gathered row; threads with c < hd/32 also move one scale byte
 __global__ void engram_gather_kernel(EngramParams p) {
+  pdl_entry();
   const int per_row = p.hd / 16;
   const int cols = (p.N - 1) * p.H;
   const long long total = (long long)p.T * p.nl * cols * per_row;
@@ -92,17 +95,18 @@ cudaError_t engram_prepare(const EngramParams& p, int mode, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
   if (p.N < 2 || p.N > 8 || p.nl > kEngramMaxLayers || p.hd % 32 || ((p.N - 1) * p.H * p.hd) % 128)
     return cudaErrorInvalidValue;
-  if (mode & 1) engram_hash_kernel<<<(p.T * p.nl + 127) / 128, 128, 0, st>>>(p);
-  if (mode & 2) engram_ring_kernel<<<(p.T + 127) / 128, 128, 0, st>>>(p);
+  if (mode & 1) launch_pdl(engram_hash_kernel, (p.T * p.nl + 127) / 128, 128, 0, st, p);
+  if (mode & 2) launch_pdl(engram_ring_kernel, (p.T + 127) / 128, 128, 0, st, p);
   if (mode & 4) {
     const long long total = (long long)p.T * p.nl * (p.N - 1) * p.H * (p.hd / 16);
-    engram_gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
+    launch_pdl(engram_gather_kernel, (unsigned)((total + 255) / 256), 256, 0, st, p);
   }
   return cudaGetLastError();
 }
 
 __global__ void __launch_bounds__(128) engram_gate_kernel(__nv_bfloat16* X, const __nv_bfloat16* __restrict__ kv,
                                                           const float* __restrict__ wgt, int D, int hc, float eps) {
+  pdl_entry();
   const int t = blockIdx.x;
   const int s = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (s >= hc) return;
@@ -146,7 +150,7 @@ cudaError_t engram_gate(__nv_bfloat16* X, const __nv_bfloat16* kv, const float* 
                         cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (D % 256 || hc > 4) return cudaErrorInvalidValue;
-  engram_gate_kernel<<<T, 128, 0, st>>>(X, kv, wgt, D, hc, eps);
+  launch_pdl(engram_gate_kernel, T, 128, 0, st, X, kv, wgt, D, hc, eps);
   return cudaGetLastError();
 }
 

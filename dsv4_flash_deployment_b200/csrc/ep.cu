@@ -50,6 +50,7 @@ DSV4_DEV void grid_publish(const EpSync& s, const int* cnt, int world, int my_ra
 }
 
 __global__ void ep_wait_kernel(const uint32_t* sig, int world, int phase, const uint32_t* epoch, uint32_t* err) {
+  pdl_entry();
   const int p = threadIdx.x;
   if (p >= world) return;
   const uint32_t want = *epoch;
@@ -66,7 +67,7 @@ __global__ void ep_wait_kernel(const uint32_t* sig, int world, int phase, const 
 
 cudaError_t ep_wait(const uint32_t* sig, int world, int phase, const uint32_t* epoch, uint32_t* err,
                     cudaStream_t st) {
-  ep_wait_kernel<<<1, 32, 0, st>>>(sig, world, phase, epoch, err);
+  launch_pdl(ep_wait_kernel, 1, 32, 0, st, sig, world, phase, epoch, err);
   return cudaGetLastError();
 }
 
@@ -74,6 +75,7 @@ __global__ void ep_pack_kernel(const int* __restrict__ ids, const float* __restr
                                const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int D, int e_local,
                                int world, int cap, int rec, uint8_t* __restrict__ send, int* cnt, int* pos_back,
                                uint8_t* const* peer_recv, int my_rank, uint32_t* err, EpSync sync) {
+  pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w < T * topk) {
@@ -112,7 +114,7 @@ cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uin
   const long long warps = (long long)T * topk;
   if (warps == 0 && sync.done == nullptr) return cudaSuccess;
   const unsigned grid = (unsigned)std::max(1LL, (warps * 32 + 255) / 256);
-  ep_pack_kernel<<<grid, 256, 0, st>>>(ids, wts, T, topk, xq, xsf, D, e_local, world, cap, rec, send, cnt, pos_back,
+  launch_pdl(ep_pack_kernel, grid, 256, 0, st, ids, wts, T, topk, xq, xsf, D, e_local, world, cap, rec, send, cnt, pos_back,
                                        peer_recv, my_rank, err, sync);
   return cudaGetLastError();
 }
@@ -120,6 +122,7 @@ cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uin
 // recv [world * cap] records with per-peer counts -> ids/wts (-1 beyond count).
 __global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, const int* __restrict__ cnt, int world,
                                       int cap, int rec, int D, int* ids, float* wts) {
+  pdl_entry();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= world * cap) return;
   const int p = i / cap, j = i % cap;
@@ -136,13 +139,14 @@ __global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, const in
 cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
                            float* wts, cudaStream_t st) {
   const int n = world * cap;
-  ep_unpack_meta_kernel<<<(n + 255) / 256, 256, 0, st>>>(recv, cnt, world, cap, rec, D, ids, wts);
+  launch_pdl(ep_unpack_meta_kernel, (n + 255) / 256, 256, 0, st, recv, cnt, world, cap, rec, D, ids, wts);
   return cudaGetLastError();
 }
 
 // Received records -> permuted expert rows (e4m3 + scale chunks), one warp per record.
 __global__ void ep_unpack_rows_kernel(const uint8_t* __restrict__ recv, int n, int rec, int D,
                                       const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+  pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= n) return;
@@ -158,7 +162,7 @@ __global__ void ep_unpack_rows_kernel(const uint8_t* __restrict__ recv, int n, i
 cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
                            cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  ep_unpack_rows_kernel<<<(unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st>>>(recv, n, rec, D, pos, pq, psf);
+  launch_pdl(ep_unpack_rows_kernel, (unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st, recv, n, rec, D, pos, pq, psf);
   return cudaGetLastError();
 }
 
@@ -167,6 +171,7 @@ cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int
 __global__ void ep_combine_pack_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ pos, int n,
                                        int D, int cap, __nv_bfloat16* back, __nv_bfloat16* const* peer_back,
                                        int my_rank, int world, EpSync sync) {
+  pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int row = w < n ? pos[w] : -1;
@@ -184,7 +189,7 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, i
                             cudaStream_t st) {
   if (n == 0 && sync.done == nullptr) return cudaSuccess;
   const unsigned grid = (unsigned)std::max(1LL, ((long long)n * 32 + 255) / 256);
-  ep_combine_pack_kernel<<<grid, 256, 0, st>>>(yperm, pos, n, D, cap, back, peer_back, my_rank, world, sync);
+  launch_pdl(ep_combine_pack_kernel, grid, 256, 0, st, yperm, pos, n, D, cap, back, peer_back, my_rank, world, sync);
   return cudaGetLastError();
 }
 

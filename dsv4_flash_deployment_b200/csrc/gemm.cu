@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   const bool csplit = p.cluster_split != 0 && p.splits > 1;
   int csyncs = 0;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -167,6 +168,9 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // grouped GEMMs read their tile list from the previous kernel (moe_plan); in
+  // dense GEMMs only the producer runs ahead (weight prefetch below)
+  if (GROUPED || warp != 0) pdl_wait();
 
   constexpr int kBkElems = KIND == KIND_BF16 ? 64 : 128;
 
@@ -175,22 +179,49 @@ __global__ void __launch_bounds__(192, 1)
     int stage = 0;
     uint32_t phase = 0;
     TileCoord t;
-    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+    constexpr uint32_t kATx = KIND == KIND_MX4A ? L::kA / 2 : L::kA;
+    // dense GEMMs: the weight tiles (A + their scales) of the first stages do not
+    // depend on the previous kernel, so they stream in while it finishes
+    int pre = 0;
+    if constexpr (!GROUPED) {
+      if (get_work<GROUPED, BN>(p, blockIdx.x, t)) {
+        pre = min(S, t.k_end - t.k_begin);
+        if (lane == 0) {
+          const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
+          const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
+          for (int i = 0; i < pre; ++i) {
+            const int kt = k_of(t, i);
+            mbar_arrive_expect_tx(&full[i], tx);
+            tma_load_2d(sA + i * L::kA, &tma_a, &full[i], kt * kBkElems, t.a_row0);
+            if constexpr (MX)
+              bulk_load(sSF + i * L::kSf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512,
+                        &full[i]);
+          }
+        }
+        __syncwarp();
+      }
+      pdl_wait();
+    }
+    bool first = true;
+    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x, first = false) {
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-      constexpr uint32_t kATx = KIND == KIND_MX4A ? L::kA / 2 : L::kA;
       const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
       for (int i = 0; i < t.k_end - t.k_begin; ++i) {
         const int kt = k_of(t, i);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, KID_GEMM, 1)) goto done;
+        const bool prefetched = first && i < pre;   // fresh stage: its A half is already in flight
+        if (!prefetched && !mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, KID_GEMM, 1)) goto done;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[stage], tx);
-          tma_load_2d(sA + stage * L::kA, &tma_a, &full[stage], kt * kBkElems, t.a_row0);
+          if (!prefetched) {
+            mbar_arrive_expect_tx(&full[stage], tx);
+            tma_load_2d(sA + stage * L::kA, &tma_a, &full[stage], kt * kBkElems, t.a_row0);
+          }
           tma_load_2d(sB + stage * L::kB, bmap, &full[stage], b_kofs + kt * kBkElems, t.b_row0);
           if constexpr (MX) {
             uint8_t* sf = sSF + stage * L::kSf;
-            bulk_load(sf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512, &full[stage]);
+            if (!prefetched)
+              bulk_load(sf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512, &full[stage]);
             for (int c = 0; c < sfb_chunks; ++c)
               bulk_load(sf + 512 * (1 + c),
                         p.sfb + ((size_t)((t.b_row0 >> 7) + c) * p.sfb_ktiles + kt + b_kofs / 128) * 512, 512,
@@ -295,6 +326,42 @@ __global__ void __launch_bounds__(192, 1)
         ++csyncs;
         c_begin = kCols * (int)cluster_ctarank();
         c_step = kCols * p.splits;
+        if constexpr (EPI != EPI_SWIGLU) {
+          // Spread (row, 4-token group) items of the valid token columns over every
+          // CTA of the cluster: each item sums its S partials (independent DSMEM
+          // loads, fixed order s = 0..S-1) and stores 4 outputs.  Decode tiles hold
+          // one or a few valid tokens, so this reads a small part of each partial.
+          const int nv = min(t.n_eff, t.b_valid);
+          const int items = 128 * ((nv + 3) >> 2);
+          const int etid = threadIdx.x - 64;
+          constexpr int kEl = EPI == EPI_F32 ? 4 : 2;
+          for (int it = (int)cluster_ctarank() * 128 + etid; it < items; it += p.splits * 128) {
+            const int r = it & 127, c4 = it >> 7;
+            const uint32_t local = smem_u32(part + (size_t)r * kPS + 4 * c4);
+            float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float4 x = dsmem_ld_f4(dsmem_map(local, (uint32_t)sp));
+              acc4.x += x.x, acc4.y += x.y, acc4.z += x.z, acc4.w += x.w;
+            }
+            const int m = t.out_col0 + r;
+            if ((p.probe & 2) || m >= p.m_valid) continue;
+            const float vals[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int n = 4 * c4 + j;
+              if (n >= nv) break;
+              float x = vals[j];
+              if (p.row_scale) x *= __ldg(p.row_scale + t.b_row0 + n);
+              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(t.b_row0 + n) * p.ldo + m) * kEl;
+              if constexpr (EPI == EPI_F32)
+                *reinterpret_cast<float*>(dst) = x;
+              else
+                *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16(x);
+            }
+          }
+          c_begin = t.n_eff;   // nothing left for the column-chunk loop below
+        }
       } else if (split) {
         // Publish this split's partial tile, then let the last arrival reduce.
         for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
@@ -515,17 +582,18 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
     cfg.blockDim = dim3(192);
     cfg.dynamicSmemBytes = L::kTotal;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)p.splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, k, ta, tb, p);
   }
-  k<<<grid, 192, L::kTotal, st>>>(ta, tb, p);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, 192, L::kTotal, st, ta, tb, p);
 }
 
 template <int KIND, int EPI, bool GROUPED>

@@ -132,6 +132,7 @@ constexpr int kIdxMaxHeads = 64;
 DSV4_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
 __global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* keys, int keys_ld) {
+  pdl_entry();
   __shared__ __align__(16) __nv_bfloat16 sQ[kIdxMaxHeads * kIdxPad];
   __shared__ __align__(16) __nv_bfloat16 sK[kIdxRows * kIdxPad];
   __shared__ __nv_bfloat16 sS[kIdxMaxHeads * (kIdxRows + 2)];   // terms are bf16 values: exact
@@ -200,6 +201,7 @@ __global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* k
 }
 
 __global__ void __launch_bounds__(256) idx_select_kernel(IdxParams p, const uint32_t* keys_in, int keys_ld) {
+  pdl_entry();
   extern __shared__ uint8_t smem[];
   const int t = blockIdx.x;
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem);
@@ -259,7 +261,7 @@ cudaError_t indexer_topk(const IdxParams& p, uint32_t* keys, int keys_ld, cudaSt
   if (p.T == 0) return cudaSuccess;
   if (p.head_dim != kIdxDh || p.n_heads > kIdxMaxHeads || keys_ld < p.max_c) return cudaErrorInvalidValue;
   dim3 g(p.T, (p.max_c + kIdxRows - 1) / kIdxRows);
-  idx_score_kernel<<<g, 128, 0, st>>>(p, keys, keys_ld);
+  launch_pdl(idx_score_kernel, g, 128, 0, st, p, keys, keys_ld);
   const size_t smem = 256 * 4 + (size_t)(p.max_c + p.max_c / max(1, p.cand_block) + 1) * 4;
   // dynamic + the kernel's static shared memory must stay under the 227 KB opt-in limit
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
@@ -269,7 +271,7 @@ cudaError_t indexer_topk(const IdxParams& p, uint32_t* keys, int keys_ld, cudaSt
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  idx_select_kernel<<<p.T, 256, smem, st>>>(p, keys, keys_ld);
+  launch_pdl(idx_select_kernel, p.T, 256, smem, st, p, keys, keys_ld);
   return cudaGetLastError();
 }
 

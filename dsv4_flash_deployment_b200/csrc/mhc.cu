@@ -52,6 +52,7 @@ DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 
 // 256 threads.  Thread -> (token tid/16, 8 columns (tid%16)*8 of the slice).
 __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) {
+  pdl_entry();
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sFn = reinterpret_cast<__nv_bfloat16*>(smem);                 // [48][kRowE]
   __nv_bfloat16* sX = sFn + kNMix * kRowE;                                      // [16][kRowE]
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
 // (8 slices' loads in flight), warp 0 forms the mixes and runs Sinkhorn, and the
 // four warps share the RMSNorm + MXFP8 pass over the D columns.
 __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
+  pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (t >= p.T) return;
@@ -385,14 +387,14 @@ cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
     configured = true;
   }
   dim3 g(ns, (p.T + kTokTile - 1) / kTokTile);
-  hc_post_kernel<<<g, 256, smem, st>>>(p, ns);
+  launch_pdl(hc_post_kernel, g, 256, smem, st, p, ns);
   return cudaGetLastError();
 }
 
 cudaError_t hc_finish(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
   if (p.D % 256) return cudaErrorInvalidValue;
-  hc_finish_kernel<<<p.T, 128, 0, st>>>(p, hc_num_slices(p.D));
+  launch_pdl(hc_finish_kernel, p.T, 128, 0, st, p, hc_num_slices(p.D));
   return cudaGetLastError();
 }
 

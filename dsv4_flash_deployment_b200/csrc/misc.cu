@@ -4,12 +4,54 @@
 #include "peer.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace dsv4 {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DSV4_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
+// PDL probe: a one-CTA kernel that runs for `ns` nanoseconds (bounded by the
+// clock, nothing else), then a dependent grid whose CTAs stamp %globaltimer on
+// entry (before griddepcontrol.wait) and after it.  With programmatic launch the
+// dependent's entry stamps precede the first kernel's end stamp.
+__global__ void pdl_probe_first(unsigned long long* stamps, unsigned long long ns) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
+  stamps[0] = globaltimer_ns();
+}
+
+__global__ void pdl_probe_second(unsigned long long* stamps) {
+  pdl_trigger();
+  const uint64_t t_in = globaltimer_ns();
+  pdl_wait();
+  const uint64_t t_out = globaltimer_ns();
+  if (threadIdx.x == 0) {
+    stamps[1 + 2 * blockIdx.x] = t_in;
+    stamps[2 + 2 * blockIdx.x] = t_out;
+  }
+}
+
+cudaError_t pdl_probe(unsigned long long* stamps, int ctas, unsigned long long ns, cudaStream_t st) {
+  if (ns > 1000000ull) return cudaErrorInvalidValue;   // at most 1 ms of spinning
+  cudaError_t e = launch_pdl(pdl_probe_first, 1, 32, 0, st, stamps, ns);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(pdl_probe_second, ctas, 32, 0, st, stamps);
+}
 
 // X[t, i, :] = table[ids[t], :] for every stream i (reference.py:909-911).
 __global__ void embed_streams_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids, int D,
                                      int hc, __nv_bfloat16* X) {
+  pdl_entry();
   const int t = blockIdx.x;
   const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)ids[t] * D);
   for (int i = threadIdx.x; i < D / 8; i += blockDim.x) {
@@ -21,7 +63,7 @@ __global__ void embed_streams_kernel(const __nv_bfloat16* __restrict__ table, co
 cudaError_t embed_streams(const __nv_bfloat16* table, const int* ids, int T, int D, int hc, __nv_bfloat16* X,
                           cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  embed_streams_kernel<<<T, 256, 0, st>>>(table, ids, D, hc, X);
+  launch_pdl(embed_streams_kernel, T, 256, 0, st, table, ids, D, hc, X);
   return cudaGetLastError();
 }
 
@@ -42,6 +84,7 @@ DSV4_DEV void better(float& bv, int& bi, float ov, int oi) {
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int* out,
                                                      float* ws_v, int* ws_i, int* counters, float* out_val,
                                                      int idx_base) {
+  pdl_entry();
   const int t = blockIdx.y, s = blockIdx.x, S = gridDim.x;
   const float* row = logits + (size_t)t * ld;
   const int chunk = ((V + S - 1) / S + 3) & ~3;
@@ -109,7 +152,7 @@ cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, flo
                         float* out_val, int idx_base, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int S = (ws_v && ws_i && counters) ? argmax_splits(T) : 1;
-  argmax_kernel<<<dim3(S, T), 256, 0, st>>>(logits, V, ld, out, ws_v, ws_i, counters, out_val, idx_base);
+  launch_pdl(argmax_kernel, dim3(S, T), 256, 0, st, logits, V, ld, out, ws_v, ws_i, counters, out_val, idx_base);
   return cudaGetLastError();
 }
 
@@ -121,6 +164,7 @@ cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, flo
 __global__ void __launch_bounds__(256) tp_argmax_merge_kernel(PeerSync s, const float* const* peer_val,
                                                               const int* const* peer_idx, int T, int* out,
                                                               uint32_t* err) {
+  pdl_entry();
   peer_publish_cta(s);
   peer_wait(s, err, KID_COMM);
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
@@ -134,7 +178,7 @@ __global__ void __launch_bounds__(256) tp_argmax_merge_kernel(PeerSync s, const 
 cudaError_t tp_argmax_merge(const PeerSync& s, const float* const* peer_val, const int* const* peer_idx, int T,
                             int* out, uint32_t* err, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  tp_argmax_merge_kernel<<<1, 256, 0, st>>>(s, peer_val, peer_idx, T, out, err);
+  launch_pdl(tp_argmax_merge_kernel, 1, 256, 0, st, s, peer_val, peer_idx, T, out, err);
   return cudaGetLastError();
 }
 
@@ -150,6 +194,7 @@ __global__ void __launch_bounds__(512) markov_step_kernel(const float* __restric
                                                           const float* __restrict__ mlog, int mld, int V, int n,
                                                           int* toks, int ts, const __nv_bfloat16* __restrict__ memb,
                                                           int R, __nv_bfloat16* emb) {
+  pdl_entry();
   const int j = blockIdx.x;
   __shared__ int s_tok;
   if (i >= 0) {
@@ -201,7 +246,7 @@ __global__ void __launch_bounds__(512) markov_step_kernel(const float* __restric
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,
                         int* toks, int ts, const __nv_bfloat16* memb, int R, __nv_bfloat16* emb, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  markov_step_kernel<<<n, 512, 0, st>>>(logits, ld, blk, i, mlog, mld, V, n, toks, ts, memb, R, emb);
+  launch_pdl(markov_step_kernel, n, 512, 0, st, logits, ld, blk, i, mlog, mld, V, n, toks, ts, memb, R, emb);
   return cudaGetLastError();
 }
 

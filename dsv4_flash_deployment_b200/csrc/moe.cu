@@ -15,6 +15,7 @@ namespace dsv4 {
 
 __global__ void router_topk_kernel(const float* __restrict__ logits, int T, int E, const float* __restrict__ bias,
                                    int topk, int score_func, float route_scale, int* ids, float* wts) {
+  pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -86,13 +87,14 @@ cudaError_t router_topk(const float* logits, int T, int E, const float* bias, in
                         float route_scale, int* ids, float* wts, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (E > 512 || topk > 16) return cudaErrorInvalidValue;
-  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits, T, E, bias, topk, score_func, route_scale, ids,
+  launch_pdl(router_topk_kernel, (T * 32 + 255) / 256, 256, 0, st, logits, T, E, bias, topk, score_func, route_scale, ids,
                                                            wts);
   return cudaGetLastError();
 }
 
 // Single CTA of 1024 threads: counts, scan, tiles, positions.
 __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
+  pdl_entry();
   extern __shared__ int sh[];
   int* cnt = sh;                        // [E_local]
   int* start = sh + p.E_local;          // [E_local + 1]
@@ -153,13 +155,14 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
 
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
   const int smem = (3 * p.E_local + 2) * 4;
-  moe_plan_kernel<<<1, 1024, smem, st>>>(p);
+  launch_pdl(moe_plan_kernel, 1, 1024, smem, st, p);
   return cudaGetLastError();
 }
 
 // One warp per (token, slot): 16-byte copies of the e4m3 row, then scale bytes.
 __global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int T, int D,
                                    int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+  pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= T * topk) return;
@@ -177,7 +180,7 @@ cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int
                         uint8_t* psf, cudaStream_t st) {
   const long long warps = (long long)T * topk;
   if (warps == 0) return cudaSuccess;
-  moe_scatter_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(xq, xsf, T, D, topk, pos, pq, psf);
+  launch_pdl(moe_scatter_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, xq, xsf, T, D, topk, pos, pq, psf);
   return cudaGetLastError();
 }
 

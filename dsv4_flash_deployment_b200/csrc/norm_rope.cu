@@ -15,6 +15,7 @@ namespace dsv4 {
 // (16-byte loads), then warp w handles the 32-column blocks w, w+4, ... of both
 // parts.
 __global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
+  pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (t >= p.T) return;
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
 cudaError_t qkv_post(const QkvParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
   if (p.q_dim % 256 || p.kv_dim % 256) return cudaErrorInvalidValue;
-  qkv_post_kernel<<<p.T, 128, 0, st>>>(p);
+  launch_pdl(qkv_post_kernel, p.T, 128, 0, st, p);
   return cudaGetLastError();
 }
 
@@ -91,6 +92,7 @@ DSV4_DEV float e2m1_qdq(float x, float s) {
 // One warp per (token, head); head_dim = 32 * k.
 __global__ void idx_q_prep_kernel(__nv_bfloat16* q, int T, int H, int hd, const float* cos, const float* sin,
                                   const int* pos, const float* w_in, float w_scale, float* w_out) {
+  pdl_entry();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= T * H) return;
@@ -123,7 +125,7 @@ cudaError_t idx_q_prep(__nv_bfloat16* q, int T, int n_heads, int head_dim, const
                        const int* pos, const float* w_in, float w_scale, float* w_out, cudaStream_t st) {
   const long long warps = (long long)T * n_heads;
   if (warps == 0) return cudaSuccess;
-  idx_q_prep_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(q, T, n_heads, head_dim, cos, sin, pos,
+  launch_pdl(idx_q_prep_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, q, T, n_heads, head_dim, cos, sin, pos,
                                                                         w_in, w_scale, w_out);
   return cudaGetLastError();
 }

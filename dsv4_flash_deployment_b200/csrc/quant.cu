@@ -17,6 +17,7 @@ namespace dsv4 {
 // 4 threads per 32-element block, 8 elements per thread.
 __global__ void act_quant_mx_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int T, int K,
                                     uint8_t* __restrict__ q, int ldq, uint8_t* __restrict__ sf, int k_tiles) {
+  pdl_entry();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = K / 8;
   const long long total = (long long)T * per_row;
@@ -53,6 +54,7 @@ __global__ void act_quant_mx_kernel(const __nv_bfloat16* __restrict__ x, int ldx
 
 __global__ void act_roundtrip_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                      long long total8) {
+  pdl_entry();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool active = gid < total8;
   float v[8];
@@ -95,6 +97,7 @@ DSV4_DEV float e2m1_quant_dequant(float x, float s) {
 // One thread per block of 16 (e4m3 scale) or 32 (ue8m0 scale) elements.
 __global__ void fp4_roundtrip_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                      long long n_blocks, int block, int e4m3_scale) {
+  pdl_entry();
   const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= n_blocks) return;
   const __nv_bfloat16* src = x + b * block;
@@ -121,7 +124,7 @@ cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t*
   const long long total = (long long)T * (K / 8);
   if (total == 0) return cudaSuccess;
   const int threads = 256;
-  act_quant_mx_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(x, ldx, T, K, q, ldq, sf,
+  launch_pdl(act_quant_mx_kernel, (unsigned)((total + threads - 1) / threads), threads, 0, st, x, ldx, T, K, q, ldq, sf,
                                                                                         k_tiles);
   return cudaGetLastError();
 }
@@ -129,7 +132,7 @@ cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t*
 cudaError_t act_roundtrip(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, cudaStream_t st) {
   const long long total8 = n / 8;
   if (total8 == 0) return cudaSuccess;
-  act_roundtrip_kernel<<<(unsigned)((total8 + 255) / 256), 256, 0, st>>>(x, y, total8);
+  launch_pdl(act_roundtrip_kernel, (unsigned)((total8 + 255) / 256), 256, 0, st, x, y, total8);
   return cudaGetLastError();
 }
 
@@ -137,7 +140,7 @@ cudaError_t fp4_roundtrip(const __nv_bfloat16* x, __nv_bfloat16* y, long long n,
                           cudaStream_t st) {
   const long long nb = n / block;
   if (nb == 0) return cudaSuccess;
-  fp4_roundtrip_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, st>>>(x, y, nb, block, e4m3_scale);
+  launch_pdl(fp4_roundtrip_kernel, (unsigned)((nb + 255) / 256), 256, 0, st, x, y, nb, block, e4m3_scale);
   return cudaGetLastError();
 }
 
