@@ -44,11 +44,13 @@ struct GemmSmem {
   static constexpr int kB = BN * 128;
   static constexpr int kSfbChunks = (BN + 127) / 128;
   static constexpr int kSf = 512 * (1 + kSfbChunks);
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 7);
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 9));
   static constexpr int kStage = kA + kB + kSf;
   static constexpr int kXbuf = 4 * 32 * 32 * 4;        // SwiGLU exchange (4 warps x 32 cols x 32 lanes)
   static constexpr int kBarriers = 256;
   static constexpr int kTotal = 1024 + kStages * kStage + kXbuf + kBarriers;
+  static_assert(kTotal <= 227 * 1024, "GEMM shared memory exceeds the per-CTA limit");
+  static_assert(8 * (2 * kStages + 2 * 2 + 1) + 16 <= kBarriers, "barrier region too small");
   // TMEM: NUM_ACC accumulator buffers (double-buffered when they fit, so the
   // epilogue of one tile overlaps the mainloop of the next), then per-stage
   // scale-factor columns.
