@@ -169,6 +169,12 @@ DSV4_DEV float4 dsmem_ld_f4(uint32_t addr) {
   return v;
 }
 
+DSV4_DEV float dsmem_ld_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // --------------------------------------------------------------------- TMA
 DSV4_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(

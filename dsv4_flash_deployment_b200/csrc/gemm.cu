@@ -363,6 +363,45 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
           c_begin = t.n_eff;   // nothing left for the column-chunk loop below
+        } else {
+          // SwiGLU: a warp item is (token n, 32-block ib of the tile's 64 intermediate
+          // indices); lane l sums gate row 32*ib + l and up row 64 + 32*ib + l over
+          // the splits (fixed order), then the same SwiGLU / clamp / row scale /
+          // MXFP8 requant as the column-chunk epilogue below (one scale per 32 indices).
+          const int nv = min(t.n_eff, t.b_valid);
+          const int n_items = 2 * nv;
+          const int gw = (int)cluster_ctarank() * 4 + (warp - 2);
+          const float lim = p.swiglu_limit;
+          for (int it = gw; it < n_items; it += 4 * p.splits) {
+            const int n = it >> 1, ib = it & 1;
+            const int i_local = 32 * ib + lane;
+            const uint32_t lg = smem_u32(part + (size_t)i_local * kPS + n);
+            const uint32_t lu = smem_u32(part + (size_t)(64 + i_local) * kPS + n);
+            float gsum = 0.f, usum = 0.f;
+#pragma unroll 8
+            for (int sp = 0; sp < p.splits; ++sp) {
+              gsum += dsmem_ld_f32(dsmem_map(lg, (uint32_t)sp));
+              usum += dsmem_ld_f32(dsmem_map(lu, (uint32_t)sp));
+            }
+            float gv = bf16_round(gsum), u = bf16_round(usum);
+            if (lim > 0.f) {
+              u = fminf(fmaxf(u, -lim), lim);
+              gv = fminf(gv, lim);
+            }
+            float h = gv / (1.f + expf(-gv)) * u;
+            const int brow = t.b_row0 + n;
+            if (p.row_scale) h *= __ldg(p.row_scale + brow);
+            h = bf16_round(h);
+            const float amax = fmaxf(warp_max(fabsf(h)), 1e-4f);
+            const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
+            const float qv = fminf(fmaxf(h / exp_to_f32(e), -448.f), 448.f);
+            const int i_global = (t.out_col0 >> 1) + i_local;
+            if (!(p.probe & 2)) {
+              p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
+              if (lane == 0) p.hsf[sf_chunk_offset(brow, i_global >> 5, p.h_ktiles)] = (uint8_t)e;
+            }
+          }
+          c_begin = t.n_eff;
         }
       } else if (split) {
         // Publish this split's partial tile, then let the last arrival reduce.
