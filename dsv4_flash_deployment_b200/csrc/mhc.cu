@@ -51,6 +51,8 @@ DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 }
 
 // 256 threads.  Thread -> (token tid/16, 8 columns (tid%16)*8 of the slice).
+constexpr int kMaxCombine = 8;   // routed experts per token summed by the MoE combine
+
 __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) {
   pdl_entry();
   extern __shared__ __align__(16) uint8_t smem[];
@@ -97,40 +99,47 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
       float y[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) y[k] = 0.f;
-      if (p.tp_mode == 2) {
-        // each pair's row lives on the rank that owns its expert
-        for (int s = 0; s < p.topk; ++s) {
-          const size_t pi = (size_t)t * p.topk + s;
-          const int owner = p.ids[pi] / p.e_local;
-          const int r = p.peer_pos[owner][pi];
-          if (r >= 0) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(p.peer_yperm[owner] + (size_t)r * D + d);
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      // MoE combine: every pair's row index first, then all rows in flight, summed
+      // in slot order (a per-slot index -> row load chain is 2 x topk round trips)
+      if (p.tp_mode == 2 || p.yperm != nullptr) {
+        const int k = min(p.topk, kMaxCombine);
+        int rr[kMaxCombine];
+        const __nv_bfloat16* src[kMaxCombine];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(h2[k]);
-              y[2 * k] += f.x;
-              y[2 * k + 1] += f.y;
+        for (int s = 0; s < kMaxCombine; ++s) {
+          rr[s] = -1;
+          src[s] = nullptr;
+          if (s < k) {
+            const size_t pi = (size_t)t * p.topk + s;
+            if (p.tp_mode == 2) {   // each pair's row lives on the rank that owns its expert
+              const int owner = p.ids[pi] / p.e_local;
+              rr[s] = p.peer_pos[owner][pi];
+              src[s] = p.peer_yperm[owner];
+            } else {
+              rr[s] = p.pos[pi];
+              src[s] = p.yperm;
             }
           }
         }
-      } else if (p.yperm != nullptr) {
-        for (int s = 0; s < p.topk; ++s) {
-          const int r = p.pos[(size_t)t * p.topk + s];
-          if (r >= 0) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(p.yperm + (size_t)r * D + d);
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint4 raw[kMaxCombine];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(h2[k]);
-              y[2 * k] += f.x;
-              y[2 * k + 1] += f.y;
-            }
+        for (int s = 0; s < kMaxCombine; ++s)
+          if (rr[s] >= 0) raw[s] = *reinterpret_cast<const uint4*>(src[s] + (size_t)rr[s] * D + d);
+#pragma unroll
+        for (int s = 0; s < kMaxCombine; ++s) {
+          if (rr[s] < 0) continue;
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[s]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h2[q]);
+            y[2 * q] += f.x;
+            y[2 * q + 1] += f.y;
           }
         }
       }
       if (p.tp_mode == 1) {
         // rank-order sum of the f32 partials: the same bits on every rank
+#pragma unroll 8
         for (int rr = 0; rr < p.wait.world; ++rr) {
           const float4* src = reinterpret_cast<const float4*>(p.peer_y[rr] + (size_t)t * D + d);
           const float4 a = src[0], b = src[1];
@@ -277,20 +286,43 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
 // rows of hc_fn), sumsq(X'), sumsq(c); every warp reduces them in slice order
 // (8 slices' loads in flight), warp 0 forms the mixes and runs Sinkhorn, and the
 // four warps share the RMSNorm + MXFP8 pass over the D columns.
+constexpr int kFinMaxIt = 5;   // norm pass: 1024 columns per iteration, D <= 5120
+
 __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
   pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (t >= p.T) return;
   const int D = p.D;
+  const bool do_norm = p.cw != nullptr && p.u != nullptr;
+  // the collapse row and the norm weights do not depend on the partials: load them first
+  uint4 craw[kFinMaxIt], wraw[kFinMaxIt];
+  if (do_norm) {
+#pragma unroll
+    for (int i = 0; i < kFinMaxIt; ++i) {
+      const int d0 = warp * 256 + i * 1024 + lane * 8;
+      if (d0 < D) {
+        craw[i] = *reinterpret_cast<const uint4*>(p.c + (size_t)t * D + d0);
+        wraw[i] = *reinterpret_cast<const uint4*>(p.norm_w + d0);
+      }
+    }
+  }
+  // partial sums: warp w adds slices w, w+4, ... (loads in flight), then the four
+  // warp sums combine in warp order; lane holds columns lane and 32 + lane (< 50)
   const float* part = p.partials + (size_t)t * n_slices * kNPart;
-  float r0 = 0.f, r1 = 0.f;   // lane: columns lane and 32 + lane (< 50)
   const bool hi_lane = lane + 32 < kNPart;
-#pragma unroll 8
-  for (int s = 0; s < n_slices; ++s) {
+  float r0 = 0.f, r1 = 0.f;
+#pragma unroll 4
+  for (int s = warp; s < n_slices; s += 4) {
     r0 += part[s * kNPart + lane];
     if (hi_lane) r1 += part[s * kNPart + 32 + lane];
   }
+  __shared__ float s_part[4][64];
+  s_part[warp][lane] = r0;
+  s_part[warp][32 + lane] = r1;
+  __syncthreads();
+  r0 = ((s_part[0][lane] + s_part[1][lane]) + s_part[2][lane]) + s_part[3][lane];
+  r1 = ((s_part[0][32 + lane] + s_part[1][32 + lane]) + s_part[2][32 + lane]) + s_part[3][32 + lane];
   const float ssx = __shfl_sync(0xffffffffu, r1, kNMix - 32);
   const float ssc = __shfl_sync(0xffffffffu, r1, kNMix + 1 - 32);
   if (p.fn_hilo != nullptr && warp == 0) {
@@ -332,16 +364,16 @@ __global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices
     if (lane >= 16) outv = c;
     if (idx >= 0) p.mix_out[(size_t)t * 24 + idx] = outv;
   }
-  if (p.cw == nullptr || p.u == nullptr) return;
+  if (!do_norm) return;
   // RMSNorm of the collapse + MXFP8: lane owns 8 consecutive columns of each
   // 256-column chunk; 4 lanes cover one 32-column scale block.
   const float rr = rsqrtf(ssc / (float)D + p.norm_eps);
-  const __nv_bfloat16* c = p.c + (size_t)t * D;
-#pragma unroll 2
-  for (int base = warp * 256; base < D; base += 1024) {
-    const int d0 = base + lane * 8;
-    const uint4 raw = *reinterpret_cast<const uint4*>(c + d0);
-    const uint4 wr = *reinterpret_cast<const uint4*>(p.norm_w + d0);
+#pragma unroll
+  for (int i = 0; i < kFinMaxIt; ++i) {
+    const int d0 = warp * 256 + i * 1024 + lane * 8;
+    if (d0 >= D) break;
+    const uint4 raw = craw[i];
+    const uint4 wr = wraw[i];
     const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
     const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wr);
     float uf[8];
@@ -377,6 +409,7 @@ int hc_num_slices(int D) { return (D + kSlice - 1) / kSlice; }
 
 cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
+  if ((p.yperm != nullptr || p.tp_mode == 2) && p.topk > kMaxCombine) return cudaErrorInvalidValue;
   if (p.D % kSlice) return cudaErrorInvalidValue;
   const int ns = hc_num_slices(p.D);
   const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2 + (size_t)8 * kTokTile * kNMix * 4;
@@ -393,7 +426,7 @@ cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
 
 cudaError_t hc_finish(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  if (p.D % 256) return cudaErrorInvalidValue;
+  if (p.D % 256 || p.D > 1024 * kFinMaxIt) return cudaErrorInvalidValue;
   launch_pdl(hc_finish_kernel, p.T, 128, 0, st, p, hc_num_slices(p.D));
   return cudaGetLastError();
 }

@@ -13,7 +13,11 @@
 
 namespace dsv4 {
 
-__global__ void router_topk_kernel(const float* __restrict__ logits, int T, int E, const float* __restrict__ bias,
+// One warp per token: sqrt-softplus or sigmoid scores (+ bias for the choice),
+// top-k by repeated warp argmax (lowest expert id on ties), weights renormalized
+// over the chosen scores and scaled.  Register arrays are only indexed by
+// unrolled loop counters (no local memory); lane k keeps the k-th pick.
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, const float* __restrict__ bias,
                                    int topk, int score_func, float route_scale, int* ids, float* wts) {
   pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -21,37 +25,35 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int T, int 
   if (warp >= T) return;
   constexpr int kMaxPer = 16;  // E <= 512
   float sc[kMaxPer], key[kMaxPer];
-  const int per = (E + 31) / 32;
+#pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     const int e = lane + 32 * i;
-    if (i < per && e < E) {
+    sc[i] = 0.f;
+    key[i] = -INFINITY;
+    if (e < E) {
       const float x = logits[(size_t)warp * E + e];
-      float s;
+      float sv;
       if (score_func == 1) {
-        s = 1.f / (1.f + expf(-x));
+        sv = 1.f / (1.f + expf(-x));
       } else {
         const float sp = x > 20.f ? x : log1pf(expf(x));
-        s = sqrtf(sp);
+        sv = sqrtf(sp);
       }
-      sc[i] = s;
-      key[i] = s + (bias ? bias[e] : 0.f);
-    } else {
-      sc[i] = 0.f;
-      key[i] = -INFINITY;
+      sc[i] = sv;
+      key[i] = sv + (bias ? bias[e] : 0.f);
     }
   }
-  float chosen[16];
-  int chosen_id[16];
-  float total = 0.f;
+  float my_s = 0.f, total = 0.f;
+  int my_id = 0;
+  uint32_t taken = 0;   // bit i: this lane's element i is already chosen
   for (int k = 0; k < topk; ++k) {
-    // local best (lowest index on ties)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = 0; i < per; ++i) {
-      const int e = lane + 32 * i;
-      if (key[i] > bv) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      if (!((taken >> i) & 1u) && key[i] > bv) {
         bv = key[i];
-        bi = e;
+        bi = lane + 32 * i;
       }
     }
 #pragma unroll
@@ -63,23 +65,22 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int T, int 
         bi = oi;
       }
     }
-    float s = 0.f;
-    if ((bi & 31) == lane) {
-      const int i = bi >> 5;
-      s = sc[i];
-      key[i] = -INFINITY;
+    float sv = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
+      if (i == (bi >> 5)) sv = sc[i];
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    sv = __shfl_sync(0xffffffffu, sv, bi & 31);
+    if (lane == k) {
+      my_s = sv;
+      my_id = bi;
     }
-    s = __shfl_sync(0xffffffffu, s, bi & 31);
-    chosen[k] = s;
-    chosen_id[k] = bi;
-    total += s;
+    total += sv;
   }
-  if (lane == 0) {
+  if (lane < topk) {
     const float inv = topk > 1 ? 1.f / (total + 1e-20f) : 1.f;
-    for (int k = 0; k < topk; ++k) {
-      ids[(size_t)warp * topk + k] = chosen_id[k];
-      wts[(size_t)warp * topk + k] = chosen[k] * inv * route_scale;
-    }
+    ids[(size_t)warp * topk + lane] = my_id;
+    wts[(size_t)warp * topk + lane] = my_s * inv * route_scale;
   }
 }
 
@@ -109,21 +110,59 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
     if (e >= 0 && e < p.E_local) p.rank[i] = atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, tacc = 0;
-    for (int e = 0; e < p.E_local; ++e) {
-      start[e] = acc;
-      toff[e] = tacc;
-      acc += (cnt[e] + 127) / 128 * 128;
-      tacc += (cnt[e] + p.tile_rows - 1) / p.tile_rows;
+  {
+    // exclusive scans of the 128-aligned row counts and the row-tile counts,
+    // one expert per thread (E_local <= 1024): warp scans, then warp totals
+    __shared__ int s_wrows[32], s_wtiles[32];
+    const int e = threadIdx.x;
+    const int lane = e & 31, w = e >> 5;
+    const int c = e < p.E_local ? cnt[e] : 0;
+    const int rows = (c + 127) & ~127;
+    const int tl = (c + p.tile_rows - 1) / p.tile_rows;
+    int ir = rows, it = tl;   // inclusive within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, ir, o), b = __shfl_up_sync(0xffffffffu, it, o);
+      if (lane >= o) {
+        ir += a;
+        it += b;
+      }
     }
-    start[p.E_local] = acc;
-    toff[p.E_local] = tacc;
-    const bool ok = acc <= p.cap_rows && tacc * mt13 <= p.max_tiles13 && tacc * mt2 <= p.max_tiles2;
-    if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 1);
-    s_ok = ok;
-    *p.n_tiles13 = ok ? tacc * mt13 : 0;  // run nothing rather than overrun the buffers
-    *p.n_tiles2 = ok ? tacc * mt2 : 0;
+    if (lane == 31) {
+      s_wrows[w] = ir;
+      s_wtiles[w] = it;
+    }
+    __syncthreads();
+    if (w == 0) {
+      const int nw = (int)(blockDim.x >> 5);
+      int vr = lane < nw ? s_wrows[lane] : 0, vt = lane < nw ? s_wtiles[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, vr, o), b = __shfl_up_sync(0xffffffffu, vt, o);
+        if (lane >= o) {
+          vr += a;
+          vt += b;
+        }
+      }
+      s_wrows[lane] = vr;   // inclusive totals through warp `lane`
+      s_wtiles[lane] = vt;
+    }
+    __syncthreads();
+    const int base_r = w > 0 ? s_wrows[w - 1] : 0, base_t = w > 0 ? s_wtiles[w - 1] : 0;
+    if (e < p.E_local) {
+      start[e] = base_r + ir - rows;
+      toff[e] = base_t + it - tl;
+    }
+    if (e == p.E_local - 1) {
+      const int acc = base_r + ir, tacc = base_t + it;
+      start[p.E_local] = acc;
+      toff[p.E_local] = tacc;
+      const bool ok = acc <= p.cap_rows && tacc * mt13 <= p.max_tiles13 && tacc * mt2 <= p.max_tiles2;
+      if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 1);
+      s_ok = ok;
+      *p.n_tiles13 = ok ? tacc * mt13 : 0;  // run nothing rather than overrun the buffers
+      *p.n_tiles2 = ok ? tacc * mt2 : 0;
+    }
   }
   __syncthreads();
   const bool ok = s_ok;
@@ -154,6 +193,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
 }
 
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
+  if (p.E_local < 1 || p.E_local > 1024) return cudaErrorInvalidValue;
   const int smem = (3 * p.E_local + 2) * 4;
   launch_pdl(moe_plan_kernel, 1, 1024, smem, st, p);
   return cudaGetLastError();

@@ -4,80 +4,143 @@
 //   qr = bf16(rmsnorm(q part) * q_norm)   -> MXFP8 for the wq_b / indexer GEMMs
 //   kv = bf16(rmsnorm(kv part) * kv_norm) -> RoPE at pos (fp32, rounded to bf16)
 //        -> FP8 e4m3 / ue8m0-per-32 round trip (the window KV contract)
-// (reference.py:704-731).  One warp per token; lane l owns column 32*b + l of
-// every 32-column block b, so a block's amax is one warp reduction.
+// (reference.py:704-731).
 #include "common.cuh"
 #include "kernels.h"
 
 namespace dsv4 {
 
-// One CTA (4 warps) per token: every warp reduces the row's sums of squares
-// (16-byte loads), then warp w handles the 32-column blocks w, w+4, ... of both
-// parts.
-__global__ void __launch_bounds__(128) qkv_post_kernel(QkvParams p) {
+// One CTA (256 threads) per token.  Thread i owns the 8-column chunks i, i+256, ...
+// of each part: every global load (row, norm weights, RoPE table) is issued up
+// front as a 16-byte vector, one block reduction gives both sums of squares,
+// and a 32-column scale block is 4 adjacent lanes (two shuffles).  At decode
+// sizes the kernel is one memory round trip plus the reduction.
+constexpr int kQkvThreads = 256;
+constexpr int kQkvMaxJ = 1;   // chunks per thread: q_dim and kv_dim up to 2048
+
+DSV4_DEV void ld8(const __nv_bfloat16* src, float* v) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h2[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__global__ void __launch_bounds__(kQkvThreads) qkv_post_kernel(QkvParams p) {
   pdl_entry();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (t >= p.T) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = p.q_dim / 8, nk = p.kv_dim / 8;
   const __nv_bfloat16* in = p.in + (size_t)t * (p.q_dim + p.kv_dim);
-  auto sumsq = [&](const __nv_bfloat16* x, int n) {
-    float ss = 0.f;
-#pragma unroll 4
-    for (int d = lane * 8; d < n; d += 256) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(x + d);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const __nv_bfloat16* kin = in + p.q_dim;
+  const int pos = p.pos[t];
+  float xq[kQkvMaxJ][8], wq[kQkvMaxJ][8], xk[kQkvMaxJ][8], wk[kQkvMaxJ][8], cs[kQkvMaxJ][8];
+  float ssq = 0.f, ssk = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h2[i]);
-        ss += f.x * f.x + f.y * f.y;
-      }
+  for (int j = 0; j < kQkvMaxJ; ++j) {
+    const int c = tid + kQkvThreads * j;
+    if (c < nq) {
+      ld8(in + 8 * c, xq[j]);
+      ld8(p.q_norm_w + 8 * c, wq[j]);
     }
-    return warp_sum(ss);
-  };
-  // ---- q part
-  if (p.q_dim > 0) {
-    const float ss = sumsq(in, p.q_dim);
-    const float r = rsqrtf(ss / (float)p.q_dim + p.eps);
-    for (int b = warp; b < p.q_dim / 32; b += 4) {
-      const int d = 32 * b + lane;
-      const float y = __bfloat162float(__float2bfloat16(__bfloat162float(in[d]) * r *
-                                                        __bfloat162float(p.q_norm_w[d])));
-      const float amax = fmaxf(warp_max(fabsf(y)), 1e-4f);
-      const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
-      p.qr_q[(size_t)t * p.q_dim + d] = f32_to_e4m3(fminf(fmaxf(y / exp_to_f32(e), -448.f), 448.f));
-      if (lane == 0) p.qr_sf[sf_chunk_offset(t, b, p.q_dim / 128)] = (uint8_t)e;
+    if (c < nk) {
+      ld8(kin + 8 * c, xk[j]);
+      ld8(p.kv_norm_w + 8 * c, wk[j]);
+      if (8 * c >= p.kv_dim - 64) {   // RoPE on the last 64 dims: pairs (2i, 2i+1) -> table index i
+        const int pi = (8 * c - (p.kv_dim - 64)) >> 1;
+        const float4 co = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 32 + pi);
+        const float4 si = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 32 + pi);
+        cs[j][0] = co.x, cs[j][1] = co.y, cs[j][2] = co.z, cs[j][3] = co.w;
+        cs[j][4] = si.x, cs[j][5] = si.y, cs[j][6] = si.z, cs[j][7] = si.w;
+      }
     }
   }
-  // ---- kv part
-  {
-    const __nv_bfloat16* kin = in + p.q_dim;
-    const float ss = sumsq(kin, p.kv_dim);
-    const float r = rsqrtf(ss / (float)p.kv_dim + p.eps);
-    const int pos = p.pos[t];
-    for (int b = warp; b < p.kv_dim / 32; b += 4) {
-      const int d = 32 * b + lane;
-      float y = __bfloat162float(__float2bfloat16(__bfloat162float(kin[d]) * r * __bfloat162float(p.kv_norm_w[d])));
-      if (d >= p.kv_dim - 64) {
-        const int pi = (d - (p.kv_dim - 64)) >> 1;
-        const float c = p.rope_cos[(size_t)pos * 32 + pi], s = p.rope_sin[(size_t)pos * 32 + pi];
-        const float other = __shfl_xor_sync(0xffffffffu, y, 1);
-        y = (lane & 1) ? (other * s + y * c) : (y * c - other * s);
-        y = __bfloat162float(__float2bfloat16(y));
-      } else {
-        (void)__shfl_xor_sync(0xffffffffu, y, 1);
+#pragma unroll
+  for (int j = 0; j < kQkvMaxJ; ++j) {
+    const int c = tid + kQkvThreads * j;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (c < nq) ssq += xq[j][i] * xq[j][i];
+      if (c < nk) ssk += xk[j][i] * xk[j][i];
+    }
+  }
+  __shared__ float s_red[2][kQkvThreads / 32];
+  ssq = warp_sum(ssq);
+  ssk = warp_sum(ssk);
+  if (lane == 0) {
+    s_red[0][warp] = ssq;
+    s_red[1][warp] = ssk;
+  }
+  __syncthreads();
+  ssq = 0.f;
+  ssk = 0.f;
+#pragma unroll
+  for (int w = 0; w < kQkvThreads / 32; ++w) {
+    ssq += s_red[0][w];
+    ssk += s_red[1][w];
+  }
+  const float rq = rsqrtf(ssq / (float)max(p.q_dim, 1) + p.eps);
+  const float rk = rsqrtf(ssk / (float)p.kv_dim + p.eps);
+#pragma unroll
+  for (int j = 0; j < kQkvMaxJ; ++j) {
+    const int c = tid + kQkvThreads * j;
+    if (c < nq) {   // warp-uniform: nq is a multiple of 32
+      float y[8], amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[i] = __bfloat162float(__float2bfloat16(xq[j][i] * rq * wq[j][i]));
+        amax = fmaxf(amax, fabsf(y[i]));
       }
-      const float amax = fmaxf(warp_max(fabsf(y)), 1e-4f);
-      const float sc = exp_to_f32(pow2_ceil_exp(amax, 1.f / 448.f));
-      const float qv = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(y / sc, -448.f), 448.f))) * sc;
-      p.kv_out[(size_t)t * p.kv_dim + d] = __float2bfloat16(qv);
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const uint32_t e = pow2_ceil_exp(fmaxf(amax, 1e-4f), 1.f / 448.f);
+      const float sc = exp_to_f32(e);
+      uint32_t qb[2] = {0, 0};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        qb[i >> 2] |= (uint32_t)f32_to_e4m3(fminf(fmaxf(y[i] / sc, -448.f), 448.f)) << (8 * (i & 3));
+      *reinterpret_cast<uint2*>(p.qr_q + (size_t)t * p.q_dim + 8 * c) = make_uint2(qb[0], qb[1]);
+      if ((lane & 3) == 0) p.qr_sf[sf_chunk_offset(t, c >> 2, p.q_dim / 128)] = (uint8_t)e;
+    }
+    if (c < nk) {   // warp-uniform: nk is a multiple of 32
+      float y[8], amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = __bfloat162float(__float2bfloat16(xk[j][i] * rk * wk[j][i]));
+      if (8 * c >= p.kv_dim - 64) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float ev = y[2 * i], od = y[2 * i + 1], co = cs[j][i], si = cs[j][4 + i];
+          y[2 * i] = __bfloat162float(__float2bfloat16(ev * co - od * si));
+          y[2 * i + 1] = __bfloat162float(__float2bfloat16(od * co + ev * si));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const float sc = exp_to_f32(pow2_ceil_exp(fmaxf(amax, 1e-4f), 1.f / 448.f));
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(y[2 * i] / sc, -448.f), 448.f))) * sc;
+        const float b = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(y[2 * i + 1] / sc, -448.f), 448.f))) * sc;
+        o2[i] = __floats2bfloat162_rn(a, b);
+      }
+      *reinterpret_cast<uint4*>(p.kv_out + (size_t)t * p.kv_dim + 8 * c) = o;
     }
   }
 }
 
 cudaError_t qkv_post(const QkvParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  if (p.q_dim % 256 || p.kv_dim % 256) return cudaErrorInvalidValue;
-  launch_pdl(qkv_post_kernel, p.T, 128, 0, st, p);
+  if (p.q_dim % 256 || p.kv_dim % 256 || p.q_dim > 8 * kQkvThreads * kQkvMaxJ || p.kv_dim > 8 * kQkvThreads * kQkvMaxJ)
+    return cudaErrorInvalidValue;
+  launch_pdl(qkv_post_kernel, p.T, kQkvThreads, 0, st, p);
   return cudaGetLastError();
 }
 
