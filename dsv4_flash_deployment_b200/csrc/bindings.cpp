@@ -406,7 +406,7 @@ void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const T
               const Tensor& counts, const Tensor& seg_start, const Tensor& rank, int64_t tile_rows, int64_t m13,
               int64_t m2, const Tensor& tiles13, const Tensor& n_tiles13, const Tensor& tiles2,
               const Tensor& n_tiles2, int64_t cap_rows, const Tensor& pos, const Tensor& row_scale,
-              const Tensor& err) {
+              const Tensor& err, const optional<Tensor>& seg_cnt, int64_t seg_cap) {
   dsv4::MoePlanParams p{};
   p.T = (int)T;
   p.topk = (int)topk;
@@ -430,6 +430,8 @@ void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const T
   p.pos = ptr<int>(pos);
   p.row_scale = ptr<float>(row_scale);
   p.err = ptr<uint32_t>(err);
+  p.seg_cnt = ptr<const int>(seg_cnt);
+  p.seg_cap = (int)seg_cap;
   CUDA_OK(dsv4::moe_plan(p, cur_stream()));
 }
 
@@ -509,17 +511,18 @@ void ep_unpack_meta(const Tensor& recv, const Tensor& cnt, int64_t world, int64_
                                ptr<int>(ids), ptr<float>(wts), cur_stream()));
 }
 
-void ep_unpack_rows(const Tensor& recv, int64_t n, int64_t rec, int64_t D, const Tensor& pos, const Tensor& pq,
-                    const Tensor& psf) {
-  CUDA_OK(dsv4::ep_unpack_rows(ptr<const uint8_t>(recv), (int)n, (int)rec, (int)D, ptr<const int>(pos),
-                               ptr<uint8_t>(pq), ptr<uint8_t>(psf), cur_stream()));
+// cnt: int32 [world] records received from each peer
+void ep_unpack_rows(const Tensor& recv, const Tensor& cnt, int64_t world, int64_t cap, int64_t rec, int64_t D,
+                    const Tensor& pos, const Tensor& pq, const Tensor& psf) {
+  CUDA_OK(dsv4::ep_unpack_rows(ptr<const uint8_t>(recv), ptr<const int>(cnt), (int)world, (int)cap, (int)rec, (int)D,
+                               ptr<const int>(pos), ptr<uint8_t>(pq), ptr<uint8_t>(psf), cur_stream()));
 }
 
-void ep_combine_pack(const Tensor& yperm, const Tensor& pos, int64_t n, int64_t cap, const Tensor& back,
+void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, int64_t cap, const Tensor& back,
                      const optional<Tensor>& peer_back, int64_t my_rank, int64_t world, const optional<Tensor>& sync) {
-  CUDA_OK(dsv4::ep_combine_pack(ptr<const bf16>(yperm), ptr<const int>(pos), (int)n, (int)yperm.size(1), (int)cap,
-                                ptr<bf16>(back), ptr<bf16* const>(peer_back), (int)my_rank, (int)world,
-                                ep_sync(sync, 1), cur_stream()));
+  CUDA_OK(dsv4::ep_combine_pack(ptr<const bf16>(yperm), ptr<const int>(pos), ptr<const int>(cnt),
+                                (int)yperm.size(1), (int)cap, ptr<bf16>(back), ptr<bf16* const>(peer_back),
+                                (int)my_rank, (int)world, ep_sync(sync, 1), cur_stream()));
 }
 
 // tables: int64 CPU tensor [nl, 3] = (device-mapped table address, scale table address, n_emb)

@@ -20,6 +20,12 @@
 
 namespace dsv4 {
 
+// Grid of the packing / unpacking kernels: two CTAs of 256 threads per SM, each
+// striding over the valid records (the buffers are sized for the worst case,
+// so one thread per capacity slot would launch mostly idle CTAs and make the
+// completion counter of the publishing kernels a long chain of atomics).
+constexpr long long kEpGrid = 296;
+
 // ------------------------------------------------------------ peer signals
 // NVLink transport: after the last CTA of a packing kernel has finished its
 // peer stores, it publishes (for the dispatch) this rank's record counts into
@@ -76,9 +82,9 @@ __global__ void ep_pack_kernel(const int* __restrict__ ids, const float* __restr
                                int world, int cap, int rec, uint8_t* __restrict__ send, int* cnt, int* pos_back,
                                uint8_t* const* peer_recv, int my_rank, uint32_t* err, EpSync sync) {
   pdl_entry();
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w < T * topk) {
+  const int n_warps = (int)(gridDim.x * blockDim.x) >> 5;
+  for (int w = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < T * topk; w += n_warps) {
     const int t = w / topk;
     const int e = ids[w];
     const int dest = e / e_local;
@@ -113,83 +119,97 @@ cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uin
                     uint8_t* const* peer_recv, int my_rank, uint32_t* err, const EpSync& sync, cudaStream_t st) {
   const long long warps = (long long)T * topk;
   if (warps == 0 && sync.done == nullptr) return cudaSuccess;
-  const unsigned grid = (unsigned)std::max(1LL, (warps * 32 + 255) / 256);
+  const unsigned grid = (unsigned)std::min<long long>(kEpGrid, std::max(1LL, (warps * 32 + 255) / 256));
   launch_pdl(ep_pack_kernel, grid, 256, 0, st, ids, wts, T, topk, xq, xsf, D, e_local, world, cap, rec, send, cnt, pos_back,
                                        peer_recv, my_rank, err, sync);
   return cudaGetLastError();
 }
 
-// recv [world * cap] records with per-peer counts -> ids/wts (-1 beyond count).
+// recv [world * cap] records with per-peer counts -> ids/wts of the valid slots
+// (slot p * cap + j, j < cnt[p]); the other slots are never read (moe_plan and
+// the unpack/combine kernels below visit valid slots only).
 __global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv, const int* __restrict__ cnt, int world,
                                       int cap, int rec, int D, int* ids, float* wts) {
   pdl_entry();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= world * cap) return;
-  const int p = i / cap, j = i % cap;
-  if (j < cnt[p]) {
-    const uint8_t* r = recv + (size_t)i * rec;
-    ids[i] = *reinterpret_cast<const int*>(r + D + D / 32);
-    wts[i] = *reinterpret_cast<const float*>(r + D + D / 32 + 4);
-  } else {
-    ids[i] = -1;
-    wts[i] = 0.f;
+  const int n_thr = (int)(gridDim.x * blockDim.x);
+  for (int p = 0; p < world; ++p) {
+    const int c = min(cnt[p], cap);
+    for (int j = (int)(blockIdx.x * blockDim.x + threadIdx.x); j < c; j += n_thr) {
+      const size_t i = (size_t)p * cap + j;
+      const uint8_t* r = recv + i * rec;
+      ids[i] = *reinterpret_cast<const int*>(r + D + D / 32);
+      wts[i] = *reinterpret_cast<const float*>(r + D + D / 32 + 4);
+    }
   }
 }
 
 cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
                            float* wts, cudaStream_t st) {
-  const int n = world * cap;
-  launch_pdl(ep_unpack_meta_kernel, (n + 255) / 256, 256, 0, st, recv, cnt, world, cap, rec, D, ids, wts);
+  const long long n = (long long)world * cap;
+  const unsigned grid = (unsigned)std::min<long long>(kEpGrid, std::max(1LL, (n + 255) / 256));
+  launch_pdl(ep_unpack_meta_kernel, grid, 256, 0, st, recv, cnt, world, cap, rec, D, ids, wts);
   return cudaGetLastError();
 }
 
 // Received records -> permuted expert rows (e4m3 + scale chunks), one warp per record.
-__global__ void ep_unpack_rows_kernel(const uint8_t* __restrict__ recv, int n, int rec, int D,
-                                      const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+__global__ void ep_unpack_rows_kernel(const uint8_t* __restrict__ recv, const int* __restrict__ cnt, int world,
+                                      int cap, int rec, int D, const int* __restrict__ pos, uint8_t* pq,
+                                      uint8_t* psf) {
   pdl_entry();
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= n) return;
-  const int row = pos[w];
-  if (row < 0) return;
-  const uint8_t* r = recv + (size_t)w * rec;
-  uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
-  for (int i = lane; i < D / 16; i += 32) dst[i] = reinterpret_cast<const uint4*>(r)[i];
+  const int n_warps = (int)(gridDim.x * blockDim.x) >> 5;
   const int kt = D / 128;
-  for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = r[D + b];
+  for (int p = 0; p < world; ++p) {
+    const int c = min(cnt[p], cap);
+    for (int j = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < c; j += n_warps) {
+      const size_t w = (size_t)p * cap + j;
+      const int row = pos[w];
+      if (row < 0) continue;
+      const uint8_t* r = recv + w * rec;
+      uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
+      for (int i = lane; i < D / 16; i += 32) dst[i] = reinterpret_cast<const uint4*>(r)[i];
+      for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = r[D + b];
+    }
+  }
 }
 
-cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
-                           cudaStream_t st) {
-  if (n == 0) return cudaSuccess;
-  launch_pdl(ep_unpack_rows_kernel, (unsigned)(((long long)n * 32 + 255) / 256), 256, 0, st, recv, n, rec, D, pos, pq, psf);
+cudaError_t ep_unpack_rows(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, const int* pos,
+                           uint8_t* pq, uint8_t* psf, cudaStream_t st) {
+  if (world * cap == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)std::min<long long>(kEpGrid, std::max(1LL, ((long long)world * cap * 32 + 255) / 256));
+  launch_pdl(ep_unpack_rows_kernel, grid, 256, 0, st, recv, cnt, world, cap, rec, D, pos, pq, psf);
   return cudaGetLastError();
 }
 
 // Expert outputs back to record order: back[i] = yperm[pos[i]] (bf16 rows), or
 // written straight into the source rank's return buffer over NVLink.
-__global__ void ep_combine_pack_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ pos, int n,
-                                       int D, int cap, __nv_bfloat16* back, __nv_bfloat16* const* peer_back,
-                                       int my_rank, int world, EpSync sync) {
+__global__ void ep_combine_pack_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ pos,
+                                       const int* __restrict__ cnt, int D, int cap, __nv_bfloat16* back,
+                                       __nv_bfloat16* const* peer_back, int my_rank, int world, EpSync sync) {
   pdl_entry();
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int row = w < n ? pos[w] : -1;
-  if (row >= 0) {
-    const int src_rank = w / cap, j = w % cap;
-    __nv_bfloat16* dst = peer_back ? peer_back[src_rank] + ((size_t)my_rank * cap + j) * D : back + (size_t)w * D;
-    const uint4* s = reinterpret_cast<const uint4*>(yperm + (size_t)row * D);
-    for (int i = lane; i < D / 8; i += 32) reinterpret_cast<uint4*>(dst)[i] = s[i];
+  const int n_warps = (int)(gridDim.x * blockDim.x) >> 5;
+  for (int src_rank = 0; src_rank < world; ++src_rank) {
+    const int c = min(cnt[src_rank], cap);
+    for (int j = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < c; j += n_warps) {
+      const size_t w = (size_t)src_rank * cap + j;
+      const int row = pos[w];
+      if (row < 0) continue;
+      __nv_bfloat16* dst = peer_back ? peer_back[src_rank] + ((size_t)my_rank * cap + j) * D : back + w * D;
+      const uint4* s = reinterpret_cast<const uint4*>(yperm + (size_t)row * D);
+      for (int i = lane; i < D / 8; i += 32) reinterpret_cast<uint4*>(dst)[i] = s[i];
+    }
   }
   grid_publish(sync, nullptr, world, my_rank, cap);
 }
 
-cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
-                            __nv_bfloat16* const* peer_back, int my_rank, int world, const EpSync& sync,
-                            cudaStream_t st) {
+cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const int* cnt, int D, int cap,
+                            __nv_bfloat16* back, __nv_bfloat16* const* peer_back, int my_rank, int world,
+                            const EpSync& sync, cudaStream_t st) {
+  const long long n = (long long)world * cap;
   if (n == 0 && sync.done == nullptr) return cudaSuccess;
-  const unsigned grid = (unsigned)std::max(1LL, ((long long)n * 32 + 255) / 256);
-  launch_pdl(ep_combine_pack_kernel, grid, 256, 0, st, yperm, pos, n, D, cap, back, peer_back, my_rank, world, sync);
+  const unsigned grid = (unsigned)std::min<long long>(kEpGrid, std::max(1LL, (n * 32 + 255) / 256));
+  launch_pdl(ep_combine_pack_kernel, grid, 256, 0, st, yperm, pos, cnt, D, cap, back, peer_back, my_rank, world, sync);
   return cudaGetLastError();
 }
 

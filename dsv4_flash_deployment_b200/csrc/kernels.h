@@ -167,6 +167,10 @@ struct MoePlanParams {
   int* pos;                         // [T, topk] permuted row (-1 if the expert is not local)
   float* row_scale;                 // [cap_rows]
   uint32_t* err;
+  // optional: the T*topk entries are segments of seg_cap slots of which the
+  // first seg_cnt[s] are valid (expert-parallel receive buffers); others are skipped
+  const int* seg_cnt;
+  int seg_cap;
 };
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st);
 // Copies quantized token rows (e4m3 + scale chunks) into permuted-row order.
@@ -217,11 +221,12 @@ cudaError_t ep_pack(const int* ids, const float* wts, int T, int topk, const uin
                     uint8_t* const* peer_recv, int my_rank, uint32_t* err, const EpSync& sync, cudaStream_t st);
 cudaError_t ep_unpack_meta(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, int* ids,
                            float* wts, cudaStream_t st);
-cudaError_t ep_unpack_rows(const uint8_t* recv, int n, int rec, int D, const int* pos, uint8_t* pq, uint8_t* psf,
-                           cudaStream_t st);
-cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, int n, int D, int cap, __nv_bfloat16* back,
-                            __nv_bfloat16* const* peer_back, int my_rank, int world, const EpSync& sync,
-                            cudaStream_t st);
+// cnt: received records per peer (slot p * cap + j is valid for j < cnt[p])
+cudaError_t ep_unpack_rows(const uint8_t* recv, const int* cnt, int world, int cap, int rec, int D, const int* pos,
+                           uint8_t* pq, uint8_t* psf, cudaStream_t st);
+cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const int* cnt, int D, int cap,
+                            __nv_bfloat16* back, __nv_bfloat16* const* peer_back, int my_rank, int world,
+                            const EpSync& sync, cudaStream_t st);
 
 // ------------------------------------------------------------ engram.cu
 constexpr int kEngramMaxLayers = 4;

@@ -105,9 +105,16 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
   const int mt13 = p.m13 / 128, mt2 = p.m2 / 128;
   for (int e = threadIdx.x; e < p.E_local; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = p.ids[i] - p.e_begin;
-    if (e >= 0 && e < p.E_local) p.rank[i] = atomicAdd(&cnt[e], 1);
+  // entries to visit: all n, or the valid prefix of each receive segment
+  const int n_seg = p.seg_cnt ? n / p.seg_cap : 1;
+  const int seg_len = p.seg_cnt ? p.seg_cap : n;
+  for (int sg = 0; sg < n_seg; ++sg) {
+    const int c = p.seg_cnt ? min(p.seg_cnt[sg], p.seg_cap) : n;
+    for (int j = threadIdx.x; j < c; j += blockDim.x) {
+      const int i = sg * seg_len + j;
+      const int e = p.ids[i] - p.e_begin;
+      if (e >= 0 && e < p.E_local) p.rank[i] = atomicAdd(&cnt[e], 1);
+    }
   }
   __syncthreads();
   {
@@ -180,20 +187,25 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
         p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, start[e] + r0, valid, mt * 128);
     }
   }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = p.ids[i] - p.e_begin;
-    if (ok && e >= 0 && e < p.E_local) {
-      const int row = start[e] + p.rank[i];
-      p.pos[i] = row;
-      p.row_scale[row] = p.wts[i];
-    } else {
-      p.pos[i] = -1;
+  for (int sg = 0; sg < n_seg; ++sg) {
+    const int c = p.seg_cnt ? min(p.seg_cnt[sg], p.seg_cap) : n;
+    for (int j = threadIdx.x; j < c; j += blockDim.x) {
+      const int i = sg * seg_len + j;
+      const int e = p.ids[i] - p.e_begin;
+      if (ok && e >= 0 && e < p.E_local) {
+        const int row = start[e] + p.rank[i];
+        p.pos[i] = row;
+        p.row_scale[row] = p.wts[i];
+      } else {
+        p.pos[i] = -1;
+      }
     }
   }
 }
 
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
   if (p.E_local < 1 || p.E_local > 1024) return cudaErrorInvalidValue;
+  if (p.seg_cnt && (p.seg_cap < 1 || (p.T * p.topk) % p.seg_cap)) return cudaErrorInvalidValue;
   const int smem = (3 * p.E_local + 2) * 4;
   launch_pdl(moe_plan_kernel, 1, 1024, smem, st, p);
   return cudaGetLastError();

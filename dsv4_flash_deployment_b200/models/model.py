@@ -639,7 +639,8 @@ class DSV4Model:
         pctx = self._t("moe_plan_scatter")
         pctx.__enter__()
         ext.moe_plan(T, k, e_local, e_begin, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
-                     self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err)
+                     self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err,
+                     None, 0)
         ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf)
         pctx.__exit__(None, None, None)
         self._grouped(L, k)

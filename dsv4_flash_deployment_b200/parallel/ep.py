@@ -139,14 +139,15 @@ class EPGroup:
         n = self.world * cap
         with model._t("ep_plan_unpack"):
             ext.ep_unpack_meta(b["recv"], b["rcnt"], self.world, cap, rec, D, b["ids"], b["wts"])
+            # only the valid prefix of each peer's segment (rcnt) is visited
             ext.moe_plan(n, 1, e_local, 0, b["ids"], b["wts"], model.counts, model.seg, b["rank"], model.tile_rows,
                          2 * I, D, model.tiles13, model.nt13, model.tiles2, model.nt2, model.cap, b["pos"],
-                         model.row_scale, model.err)
-            ext.ep_unpack_rows(b["recv"], n, rec, D, b["pos"], model.xperm, model.xperm_sf)
+                         model.row_scale, model.err, b["rcnt"], cap)
+            ext.ep_unpack_rows(b["recv"], b["rcnt"], self.world, cap, rec, D, b["pos"], model.xperm, model.xperm_sf)
         model._grouped(L, 1)
         with model._t("ep_combine"):
-            ext.ep_combine_pack(model.yperm, b["pos"], n, cap, b["back_send"], b["peer_back"] if p2p else None,
-                                self.rank, self.world, b["sync1"] if p2p else None)
+            ext.ep_combine_pack(model.yperm, b["pos"], b["rcnt"], cap, b["back_send"],
+                                b["peer_back"] if p2p else None, self.rank, self.world, b["sync1"] if p2p else None)
         if not p2p:
             with model._t("ep_exchange"):
                 dist.all_to_all_single(b["back_recv"], b["back_send"], group=self.group)
