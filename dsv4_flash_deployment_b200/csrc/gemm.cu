@@ -328,7 +328,11 @@ __global__ void __launch_bounds__(192, 1)
         ++csyncs;
         c_begin = kCols * (int)cluster_ctarank();
         c_step = kCols * p.splits;
-        if constexpr (EPI != EPI_SWIGLU) {
+        const int nv_tile = min(t.n_eff, t.b_valid);
+        // the column-chunk reduction below gives each CTA of the cluster one 32-column
+        // chunk; with fewer valid chunks than splits (decode) spread the work instead
+        const bool spread = (nv_tile + kCols - 1) / kCols < p.splits && (EPI != EPI_SWIGLU || nv_tile <= 8);
+        if (EPI != EPI_SWIGLU && spread) {
           // Spread (row, 4-token group) items of the valid token columns over every
           // CTA of the cluster: each item sums its S partials (independent DSMEM
           // loads, fixed order s = 0..S-1) and stores 4 outputs.  Decode tiles hold
@@ -363,7 +367,7 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
           c_begin = t.n_eff;   // nothing left for the column-chunk loop below
-        } else {
+        } else if (EPI == EPI_SWIGLU && spread) {
           // SwiGLU: a warp item is (token n, 32-block ib of the tile's 64 intermediate
           // indices); lane l sums gate row 32*ib + l and up row 64 + 32*ib + l over
           // the splits (fixed order), then the same SwiGLU / clamp / row scale /
