@@ -17,13 +17,16 @@ namespace dsv4 {
 // top-k by repeated warp argmax (lowest expert id on ties), weights renormalized
 // over the chosen scores and scaled.  Register arrays are only indexed by
 // unrolled loop counters (no local memory); lane k keeps the k-th pick.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E, const float* __restrict__ bias,
-                                   int topk, int score_func, float route_scale, int* ids, float* wts) {
+// kMaxPer = experts per lane (ceil(E / 32)); one instantiation per width keeps the
+// unrolled code of a one-token launch small (instruction fetch dominates it).
+template <int kMaxPer>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E,
+                                                          const float* __restrict__ bias, int topk, int score_func,
+                                                          float route_scale, int* ids, float* wts) {
   pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
-  constexpr int kMaxPer = 16;  // E <= 512
   float sc[kMaxPer], key[kMaxPer];
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
@@ -87,9 +90,17 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,
                         float route_scale, int* ids, float* wts, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  if (E > 512 || topk > 16) return cudaErrorInvalidValue;
-  launch_pdl(router_topk_kernel, (T * 32 + 255) / 256, 256, 0, st, logits, T, E, bias, topk, score_func, route_scale, ids,
-                                                           wts);
+  if (E > 512 || topk > 16 || topk > E) return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)((T * 32 + 255) / 256);
+  const int per = (E + 31) / 32;
+#define DSV4_ROUTER(P) \
+  launch_pdl(router_topk_kernel<P>, grid, 256, 0, st, logits, T, E, bias, topk, score_func, route_scale, ids, wts)
+  if (per <= 2) DSV4_ROUTER(2);
+  else if (per <= 4) DSV4_ROUTER(4);
+  else if (per <= 8) DSV4_ROUTER(8);
+  else if (per <= 12) DSV4_ROUTER(12);
+  else DSV4_ROUTER(16);
+#undef DSV4_ROUTER
   return cudaGetLastError();
 }
 
