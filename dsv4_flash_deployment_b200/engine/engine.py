@@ -71,6 +71,8 @@ class Engine:
         ids = self.run_meta(meta)
         return self.sched.commit(chunks, ids)
 
+    _trace_left: int | None = None
+
     def run_meta(self, meta: StepMeta) -> list[int]:
         """Uploads ``meta``, runs the model step, returns the sampled ids on the host."""
         m = self.model
@@ -90,6 +92,18 @@ class Engine:
     def _run_device(self, meta: StepMeta) -> torch.Tensor:
         m = self.model
         m.upload(meta, self.pinned)
+        if self._trace_left is None:
+            from ..utils.trace import trace_steps_from_env
+            self._trace_left = trace_steps_from_env()
+        if self._trace_left > 0:
+            # numeric trace of the first steps (eager): per-layer stream statistics
+            from ..utils.trace import format_stats, layer_stats, log
+            self._trace_left -= 1
+            trace: dict = {}
+            out = m.forward(meta, trace=trace)
+            for line in format_stats(layer_stats(trace)):
+                log.info("step %d T=%d %s", self.stats["steps"], meta.T, line)
+            return out
         if not self.use_graphs:
             return m.forward(meta)
         key = meta.key()

@@ -312,9 +312,11 @@ class DSV4Model:
             return
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(name)     # named ranges for timeline profilers
         s.record()
         yield
         e.record()
+        torch.cuda.nvtx.range_pop()
         self.op_timer.setdefault(name, []).append((s, e))
 
     # --------------------------------------------------------------- helpers
