@@ -35,11 +35,13 @@ def test_engine_traces_first_steps(monkeypatch, caplog):
     trace and log one line per layer; later steps go back to graph replay."""
     import logging
 
-    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.config import v4_flash_config
     from dsv4_flash_deployment_b200.engine.engine import Engine
 
     monkeypatch.setenv("DSV4_TRACE_LAYER_STATS", "2")
-    cfg = toy_v4_config()
+    # kernel dimensions of V4 (64 x 512 heads, 128-wide indexer heads), small elsewhere
+    cfg = v4_flash_config(n_layers=3, dim=512, vocab_size=1024, padded_vocab_size=1024, q_lora_rank=256,
+                          o_lora_rank=128, n_routed_experts=16, moe_inter_dim=256, index_n_heads=8, index_topk=8)
     eng = Engine.build(cfg, "cuda", max_seqs=2, max_batched_tokens=32, max_seq_len=128)
     with caplog.at_level(logging.INFO, logger="dsv4.trace"):
         out = eng.generate([list(range(10, 30))], 4, ignore_eos=True)
