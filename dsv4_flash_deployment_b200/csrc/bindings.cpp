@@ -8,6 +8,9 @@
 #include "gemm.h"
 #include "kernels.h"
 
+#include <algorithm>
+#include <cstdlib>
+
 namespace {
 
 using at::Tensor;
@@ -45,6 +48,15 @@ int tma_elem_of(const Tensor& t, bool e2m1) {
 //   kind 0: bf16 x bf16; 1: e4m3 x e4m3 (MXFP8); 2: e2m1 (A) x e4m3 (B).
 //   A [a_rows, K] (packed e2m1: [a_rows, K/2]); B [b_rows, K].
 //   grouped: tiles int32 [n, 4] + n_tiles int32 [1] device tensors.
+// DSV4_GEMM_BM256=0 keeps every GEMM on 128-row weight tiles (A/B timing).
+static bool bm256_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DSV4_GEMM_BM256");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 // Optional int64 CPU tensor [peer_sig table, sig, done, epoch, phase, world, rank] of device
 // addresses / values -> PeerSync (all zero = none)
 static dsv4::PeerSync peer_sync_of(const optional<Tensor>& t) {
@@ -79,9 +91,21 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   const c10::cuda::CUDAGuard guard(A.device());
   const int64_t b_cols = B.size(1);  // full activation width (groups * K in batched mode)
   TORCH_CHECK(b_cols == K * std::max<int64_t>(1, groups), "B width must be groups * K");
+  // 256-row weight tiles: two M=128 MMAs per stage share the token tile.  Measured
+  // faster only without split-K on long K with enough tiles to fill the GPU (e.g.
+  // wo_b at 1023 tokens: 53 vs 61 us); with split-K the cluster reduction doubles
+  // and the single accumulator serializes the epilogue, so those stay at 128 rows.
+  const bool caller_ws = workspace.has_value() && counters.has_value();
+  const int k_tiles_mx = (int)(K / 128);
+  const int tiles256 = (int)(M / 256) * (int)((N + bn - 1) / bn);
+  const int bm = (kind != dsv4::KIND_BF16 && !grouped && groups <= 1 && epi != dsv4::EPI_SWIGLU && M % 256 == 0 &&
+                  (bn == 64 || bn == 128) && !caller_ws && splits <= 1 && k_tiles_mx >= 64 && tiles256 >= 96 &&
+                  bm256_enabled())
+                     ? 256 : 128;
   CUtensorMap ta;
   dsv4::BMaps tb;
-  TORCH_CHECK(dsv4::make_tma_2d(&ta, A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, 128), "TMA(A) encode failed");
+  TORCH_CHECK(dsv4::make_tma_2d(&ta, A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
+              "TMA(A) encode failed");
   if (grouped) {
     const uint32_t boxes[4] = {32, 64, 128, 256};
     for (int i = 0; i < 4; ++i)
@@ -97,6 +121,12 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.N = (int)N;
   const int elem_bytes = kind == dsv4::KIND_BF16 ? 2 : 1;
   p.k_tiles = (int)(K * elem_bytes / 128);
+  if (splits < 0 && !grouped) {
+    // automatic: split K when the output tiles cannot fill the SMs (each split keeps
+    // >= 2 k-tiles; at most 8 splits, one cluster per tile)
+    const int tiles_auto = (int)(M / bm) * (int)((N + bn - 1) / bn);
+    splits = tiles_auto < 100 ? std::max(1, std::min({8, p.k_tiles / 2, 148 / std::max(tiles_auto, 1)})) : 1;
+  }
   p.splits = (int)std::max<int64_t>(1, splits);
   p.sfa = u8ptr(A_sf);
   p.sfa_ktiles = (int)(K / 128);
@@ -130,10 +160,10 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
     // Halve the split count until every tile's cluster is resident at once.
     TORCH_CHECK(!grouped, "cluster split-K: dense GEMMs only");
     TORCH_CHECK(M % 128 == 0, "M must be a multiple of 128");
-    const int tiles = (int)(M / 128) * (int)((N + bn - 1) / bn);
+    const int tiles = (int)(M / bm) * (int)((N + bn - 1) / bn);
     int s = 1;
     while (s * 2 <= std::min(p.splits, 8)) s *= 2;
-    while (s >= 2 && dsv4::gemm_max_clusters((int)kind, (int)epi, (int)bn, s) < tiles) s /= 2;
+    while (s >= 2 && dsv4::gemm_max_clusters((int)kind, (int)epi, (int)bn, s, bm) < tiles) s /= 2;
     p.splits = s >= 2 ? s : 1;
     p.cluster_split = p.splits > 1;
   }
@@ -144,7 +174,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
     units = (int)tiles->size(0) * p.splits;
   } else {
     TORCH_CHECK(M % 128 == 0, "M must be a multiple of 128");
-    p.n_tiles = (int)(M / 128) * (int)((N + bn - 1) / bn);
+    p.n_tiles = (int)(M / bm) * (int)((N + bn - 1) / bn);
     units = p.n_tiles * p.splits;
   }
   if (units == 0) {
@@ -152,7 +182,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
     return;
   }
   int grid = p.cluster_split ? units : std::min(units, max_grid > 0 ? (int)max_grid : num_sms());
-  CUDA_OK(dsv4::gemm_launch((int)kind, (int)epi, grouped, (int)bn, ta, tb, p, grid, cur_stream()));
+  CUDA_OK(dsv4::gemm_launch((int)kind, (int)epi, grouped, (int)bn, bm, ta, tb, p, grid, cur_stream()));
 }
 
 void act_quant_mx(const Tensor& x, Tensor& q, Tensor& sf) {

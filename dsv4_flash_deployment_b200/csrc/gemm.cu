@@ -38,13 +38,15 @@
 
 namespace dsv4 {
 
-template <int BN>
+template <int BN, int BM = 128>
 struct GemmSmem {
-  static constexpr int kA = 128 * 128;                // 16 KB
+  static constexpr int kA = BM * 128;                 // 16 KB per 128 weight rows
   static constexpr int kB = BN * 128;
+  static constexpr int kSfaChunks = BM / 128;         // 128-row halves of the weight tile
   static constexpr int kSfbChunks = (BN + 127) / 128;
-  static constexpr int kSf = 512 * (1 + kSfbChunks);
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 9));
+  static constexpr int kSf = 512 * (kSfaChunks + kSfbChunks);
+  static constexpr int kStages = BM == 256 ? (BN >= 128 ? 4 : 5)
+                                           : (BN >= 256 ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 9)));
   static constexpr int kStage = kA + kB + kSf;
   static constexpr int kXbuf = 4 * 32 * 32 * 4;        // SwiGLU exchange (4 warps x 32 cols x 32 lanes)
   static constexpr int kBarriers = 256;
@@ -54,12 +56,15 @@ struct GemmSmem {
   // TMEM: NUM_ACC accumulator buffers (double-buffered when they fit, so the
   // epilogue of one tile overlaps the mainloop of the next), then per-stage
   // scale-factor columns.
-  static constexpr int kNumAcc = BN <= 128 ? 2 : 1;
-  static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kSfCols = 4 * (1 + kSfbChunks);
+  static constexpr int kNumAcc = (BM == 128 && BN <= 128) ? 2 : 1;
+  static constexpr int kAccColsHalf = BN < 32 ? 32 : BN;     // one 128-row half of the tile
+  static constexpr int kAccCols = kAccColsHalf * kSfaChunks;
+  static constexpr int kSfCols = 4 * (kSfaChunks + kSfbChunks);
   static constexpr int kColsNeeded = kNumAcc * kAccCols + kStages * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                  : kColsNeeded <= 256 ? 256 : 512;
+  static_assert(kColsNeeded <= 512, "TMEM columns exceed one SM's 512");
+  static_assert(BM == 128 || BM == 256, "weight tile rows");
 };
 
 DSV4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
@@ -85,7 +90,7 @@ DSV4_DEV int k_of(const TileCoord& t, int i) {
 DSV4_DEV int n_eff_for(int valid) { return valid <= 32 ? 32 : valid <= 64 ? 64 : valid <= 128 ? 128 : 256; }
 DSV4_DEV int bmap_index(int n_eff) { return n_eff == 32 ? 0 : n_eff == 64 ? 1 : n_eff == 128 ? 2 : 3; }
 
-template <bool GROUPED, int BN>
+template <bool GROUPED, int BN, int BM = 128>
 DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
   const int n_units = (GROUPED ? __ldg(p.n_tiles_ptr) : p.n_tiles) * p.splits;
   if (w >= n_units) return false;
@@ -99,12 +104,12 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
     t.out_col0 = r.w;
     t.n_eff = min(BN, n_eff_for(r.z));
   } else {
-    const int m_tiles = p.M / 128;
+    const int m_tiles = p.M / BM;
     const int mt = tile % m_tiles, nt = tile / m_tiles;
-    t.a_row0 = mt * 128;
+    t.a_row0 = mt * BM;
     t.b_row0 = nt * BN;
     t.b_valid = min(BN, p.N - t.b_row0);
-    t.out_col0 = mt * 128;
+    t.out_col0 = mt * BM;
     t.n_eff = BN;
   }
   const int per = (p.k_tiles + p.splits - 1) / p.splits;
@@ -116,10 +121,10 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
   return true;
 }
 
-template <int KIND, int BN, int EPI, bool GROUPED>
+template <int KIND, int BN, int EPI, bool GROUPED, int BM = 128>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ BMaps tma_b, GemmParams p) {
-  using L = GemmSmem<BN>;
+  using L = GemmSmem<BN, BM>;
   constexpr bool MX = KIND != KIND_BF16;
   constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -186,18 +191,19 @@ __global__ void __launch_bounds__(192, 1)
     // depend on the previous kernel, so they stream in while it finishes
     int pre = 0;
     if constexpr (!GROUPED) {
-      if (get_work<GROUPED, BN>(p, blockIdx.x, t)) {
+      if (get_work<GROUPED, BN, BM>(p, blockIdx.x, t)) {
         pre = min(S, t.k_end - t.k_begin);
         if (lane == 0) {
           const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-          const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
+          const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
           for (int i = 0; i < pre; ++i) {
             const int kt = k_of(t, i);
             mbar_arrive_expect_tx(&full[i], tx);
             tma_load_2d(sA + i * L::kA, &tma_a, &full[i], kt * kBkElems, t.a_row0);
             if constexpr (MX)
-              bulk_load(sSF + i * L::kSf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512,
-                        &full[i]);
+              for (int h = 0; h < L::kSfaChunks; ++h)
+                bulk_load(sSF + i * L::kSf + 512 * h, p.sfa + ((size_t)((t.a_row0 >> 7) + h) * p.sfa_ktiles + kt) * 512,
+                          512, &full[i]);
           }
         }
         __syncwarp();
@@ -205,9 +211,9 @@ __global__ void __launch_bounds__(192, 1)
       pdl_wait();
     }
     bool first = true;
-    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x, first = false) {
+    for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x, first = false) {
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-      const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (1 + sfb_chunks) : 0);
+      const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
       for (int i = 0; i < t.k_end - t.k_begin; ++i) {
@@ -223,9 +229,11 @@ __global__ void __launch_bounds__(192, 1)
           if constexpr (MX) {
             uint8_t* sf = sSF + stage * L::kSf;
             if (!prefetched)
-              bulk_load(sf, p.sfa + ((size_t)(t.a_row0 >> 7) * p.sfa_ktiles + kt) * 512, 512, &full[stage]);
+              for (int h = 0; h < L::kSfaChunks; ++h)
+                bulk_load(sf + 512 * h, p.sfa + ((size_t)((t.a_row0 >> 7) + h) * p.sfa_ktiles + kt) * 512, 512,
+                          &full[stage]);
             for (int c = 0; c < sfb_chunks; ++c)
-              bulk_load(sf + 512 * (1 + c),
+              bulk_load(sf + 512 * (L::kSfaChunks + c),
                         p.sfb + ((size_t)((t.b_row0 >> 7) + c) * p.sfb_ktiles + kt + b_kofs / 128) * 512, 512,
                         &full[stage]);
           }
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     TileCoord t;
-    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+    for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x) {
       const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, KIND == KIND_MX4A ? 5 : 0, 0) : idesc_bf16(128, t.n_eff);
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
       const uint32_t d_tmem = tmem + acc * L::kAccCols;
@@ -260,21 +268,27 @@ __global__ void __launch_bounds__(192, 1)
           if constexpr (MX) {
             const uint32_t sf0 = smem_u32(sSF + stage * L::kSf);
             const uint32_t col = tmem + NA * L::kAccCols + stage * L::kSfCols;
-            utccp_32x128b_x4(col, umma_sdesc(sf0, 16, 128, kLayoutNone));
+            for (int h = 0; h < L::kSfaChunks; ++h)
+              utccp_32x128b_x4(col + 4 * h, umma_sdesc(sf0 + 512 * h, 16, 128, kLayoutNone));
             for (int c = 0; c < sfb_chunks; ++c)
-              utccp_32x128b_x4(col + 4 + 4 * c, umma_sdesc(sf0 + 512 * (1 + c), 16, 128, kLayoutNone));
+              utccp_32x128b_x4(col + 4 * (L::kSfaChunks + c),
+                               umma_sdesc(sf0 + 512 * (L::kSfaChunks + c), 16, 128, kLayoutNone));
             sfa_t = col;
-            sfb_t = col + 4;
+            sfb_t = col + 4 * L::kSfaChunks;
           }
 #pragma unroll
           for (int kk = 0; kk < ((p.probe & 1) ? 0 : 4); ++kk) {
-            const uint64_t ad = sdesc_kmajor_sw128(a0 + kk * 32);
             const uint64_t bd = sdesc_kmajor_sw128(b0 + kk * 32);
             const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-            if constexpr (MX)
-              umma_mx(d_tmem, ad, bd, idesc_mx_sf(idesc, kk), sfa_t, sfb_t, accum);
-            else
-              umma_bf16(d_tmem, ad, bd, idesc, accum);
+            // 256-row weight tiles: two M=128 MMAs (rows 0-127, 128-255) share the token tile
+#pragma unroll
+            for (int h = 0; h < L::kSfaChunks; ++h) {
+              const uint64_t ad = sdesc_kmajor_sw128(a0 + h * 128 * 128 + kk * 32);
+              if constexpr (MX)
+                umma_mx(d_tmem + h * L::kAccColsHalf, ad, bd, idesc_mx_sf(idesc, kk), sfa_t + 4 * h, sfb_t, accum);
+              else
+                umma_bf16(d_tmem + h * L::kAccColsHalf, ad, bd, idesc, accum);
+            }
           }
           umma_commit(&empty[stage]);
         }
@@ -298,19 +312,26 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     TileCoord t;
-    for (int w = blockIdx.x; get_work<GROUPED, BN>(p, w, t); w += gridDim.x) {
+    for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x) {
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, KID_GEMM, 4)) goto done;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + acc * L::kAccCols;
+      // 256-row weight tiles: the two 128-row halves (TMEM columns BN apart) are
+      // finished one after the other; the accumulator is released after the last
+      bool tile_done = false;
+      for (int hh = 0; hh < L::kSfaChunks && !tile_done; ++hh) {
+      const bool last_h = hh == L::kSfaChunks - 1;
+      TileCoord th = t;
+      th.out_col0 += 128 * hh;
+      const uint32_t d_tmem = tmem + acc * L::kAccCols + hh * L::kAccColsHalf;
       const bool split = p.splits > 1;
       constexpr int kCols = BN < 32 ? BN : 32;
       constexpr int kPS = BN + 4;   // padded row stride of a parked partial tile (floats)
-      float* ws_tile = split && !csplit ? p.workspace + (size_t)t.tile * p.splits * 128 * BN : nullptr;
+      float* ws_tile = split && !csplit ? p.workspace + (size_t)th.tile * p.splits * 128 * BN : nullptr;
       int c_begin = 0, c_step = kCols;
       if (csplit) {
         // park this split's partial (row-major, 16-byte stores) in the idle stage buffers
         float* part = reinterpret_cast<float*>(smem);
-        for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+        for (int c0 = 0; c0 < th.n_eff; c0 += kCols) {
           uint32_t r[32];
           if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
           else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
@@ -323,12 +344,12 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0 && last_h) mbar_arrive(&acc_empty[acc]);
         cluster_sync_all();   // every split's partial is parked
         ++csyncs;
         c_begin = kCols * (int)cluster_ctarank();
         c_step = kCols * p.splits;
-        const int nv_tile = min(t.n_eff, t.b_valid);
+        const int nv_tile = min(th.n_eff, th.b_valid);
         // the column-chunk reduction below gives each CTA of the cluster one 32-column
         // chunk; with fewer valid chunks than splits (decode) spread the work instead
         const bool spread = (nv_tile + kCols - 1) / kCols < p.splits && (EPI != EPI_SWIGLU || nv_tile <= 8);
@@ -337,7 +358,7 @@ __global__ void __launch_bounds__(192, 1)
           // CTA of the cluster: each item sums its S partials (independent DSMEM
           // loads, fixed order s = 0..S-1) and stores 4 outputs.  Decode tiles hold
           // one or a few valid tokens, so this reads a small part of each partial.
-          const int nv = min(t.n_eff, t.b_valid);
+          const int nv = min(th.n_eff, th.b_valid);
           const int items = 128 * ((nv + 3) >> 2);
           const int etid = threadIdx.x - 64;
           constexpr int kEl = EPI == EPI_F32 ? 4 : 2;
@@ -350,7 +371,7 @@ __global__ void __launch_bounds__(192, 1)
               const float4 x = dsmem_ld_f4(dsmem_map(local, (uint32_t)sp));
               acc4.x += x.x, acc4.y += x.y, acc4.z += x.z, acc4.w += x.w;
             }
-            const int m = t.out_col0 + r;
+            const int m = th.out_col0 + r;
             if ((p.probe & 2) || m >= p.m_valid) continue;
             const float vals[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
 #pragma unroll
@@ -358,21 +379,21 @@ __global__ void __launch_bounds__(192, 1)
               const int n = 4 * c4 + j;
               if (n >= nv) break;
               float x = vals[j];
-              if (p.row_scale) x *= __ldg(p.row_scale + t.b_row0 + n);
-              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(t.b_row0 + n) * p.ldo + m) * kEl;
+              if (p.row_scale) x *= __ldg(p.row_scale + th.b_row0 + n);
+              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(th.b_row0 + n) * p.ldo + m) * kEl;
               if constexpr (EPI == EPI_F32)
                 *reinterpret_cast<float*>(dst) = x;
               else
                 *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16(x);
             }
           }
-          c_begin = t.n_eff;   // nothing left for the column-chunk loop below
+          c_begin = th.n_eff;   // nothing left for the column-chunk loop below
         } else if (EPI == EPI_SWIGLU && spread) {
           // SwiGLU: a warp item is (token n, 32-block ib of the tile's 64 intermediate
           // indices); lane l sums gate row 32*ib + l and up row 64 + 32*ib + l over
           // the splits (fixed order), then the same SwiGLU / clamp / row scale /
           // MXFP8 requant as the column-chunk epilogue below (one scale per 32 indices).
-          const int nv = min(t.n_eff, t.b_valid);
+          const int nv = min(th.n_eff, th.b_valid);
           const int n_items = 2 * nv;
           const int gw = (int)cluster_ctarank() * 4 + (warp - 2);
           const float lim = p.swiglu_limit;
@@ -393,29 +414,29 @@ __global__ void __launch_bounds__(192, 1)
               gv = fminf(gv, lim);
             }
             float h = gv / (1.f + expf(-gv)) * u;
-            const int brow = t.b_row0 + n;
+            const int brow = th.b_row0 + n;
             if (p.row_scale) h *= __ldg(p.row_scale + brow);
             h = bf16_round(h);
             const float amax = fmaxf(warp_max(fabsf(h)), 1e-4f);
             const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
             const float qv = fminf(fmaxf(h / exp_to_f32(e), -448.f), 448.f);
-            const int i_global = (t.out_col0 >> 1) + i_local;
+            const int i_global = (th.out_col0 >> 1) + i_local;
             if (!(p.probe & 2)) {
               p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
               if (lane == 0) p.hsf[sf_chunk_offset(brow, i_global >> 5, p.h_ktiles)] = (uint8_t)e;
             }
           }
-          c_begin = t.n_eff;
+          c_begin = th.n_eff;
         }
       } else if (split) {
         // Publish this split's partial tile, then let the last arrival reduce.
-        for (int c0 = 0; c0 < t.n_eff; c0 += kCols) {
+        for (int c0 = 0; c0 < th.n_eff; c0 += kCols) {
           uint32_t r[32];
           if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
           else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_ld_wait();
           // row-major partial tile: each thread stores whole 16-byte column groups of its row
-          float4* dst = reinterpret_cast<float4*>(ws_tile + (size_t)t.split * 128 * BN + (size_t)row * BN + c0);
+          float4* dst = reinterpret_cast<float4*>(ws_tile + (size_t)th.split * 128 * BN + (size_t)row * BN + c0);
 #pragma unroll
           for (int j = 0; j < kCols / 4; ++j)
             dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
@@ -423,26 +444,23 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0 && last_h) mbar_arrive(&acc_empty[acc]);
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
-          const int prev = atomicAdd(&p.tile_counters[t.tile], 1);
+          const int prev = atomicAdd(&p.tile_counters[th.tile], 1);
           *last_flag = (prev == p.splits - 1);
-          if (prev == p.splits - 1) p.tile_counters[t.tile] = 0;  // re-arm for the next launch
+          if (prev == p.splits - 1) p.tile_counters[th.tile] = 0;  // re-arm for the next launch
           __threadfence();
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!*last_flag) {
-          if (++acc == NA) {
-            acc = 0;
-            acc_phase ^= 1;
-          }
+          tile_done = true;   // another split reduces this tile
           continue;
         }
         __threadfence();
       }
-      for (int c0 = c_begin; c0 < t.n_eff; c0 += c_step) {
+      for (int c0 = c_begin; c0 < th.n_eff; c0 += c_step) {
         float v[32];
         if (csplit) {
           // fixed summation order s = 0..splits-1 over the cluster's parked partials
@@ -504,7 +522,7 @@ __global__ void __launch_bounds__(192, 1)
           {
             const int g = q & 1, half = q >> 1;
             const int i_local = 32 * g + lane;
-            const int i_global = (t.out_col0 >> 1) + i_local;  // out_col0 = 128 * m-tile
+            const int i_global = (th.out_col0 >> 1) + i_local;  // out_col0 = 128 * m-tile
             const int kblk = i_global >> 5;
             const float lim = p.swiglu_limit;
             const int j0 = half * (kCols / 2);
@@ -519,13 +537,13 @@ __global__ void __launch_bounds__(192, 1)
                 gv = fminf(gv, lim);
               }
               float h = gv / (1.f + expf(-gv)) * u;
-              const int brow = t.b_row0 + n;
-              if (p.row_scale && n < t.b_valid) h *= __ldg(p.row_scale + brow);
+              const int brow = th.b_row0 + n;
+              if (p.row_scale && n < th.b_valid) h *= __ldg(p.row_scale + brow);
               h = bf16_round(h);
               const float amax = fmaxf(warp_max(fabsf(h)), 1e-4f);
               const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
               const float qv = fminf(fmaxf(h / exp_to_f32(e), -448.f), 448.f);
-              if (n < t.b_valid) {
+              if (n < th.b_valid) {
                 p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
                 if (lane == 0) p.hsf[sf_chunk_offset(brow, kblk, p.h_ktiles)] = (uint8_t)e;
               }
@@ -540,7 +558,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < kCols; ++j) {
             float x = v[j];
-            if (p.row_scale && c0 + j < t.b_valid) x *= __ldg(p.row_scale + t.b_row0 + c0 + j);
+            if (p.row_scale && c0 + j < th.b_valid) x *= __ldg(p.row_scale + th.b_row0 + c0 + j);
             if constexpr (EPI == EPI_F32)
               reinterpret_cast<float*>(stage)[j * 128 + row] = x;
             else
@@ -549,16 +567,16 @@ __global__ void __launch_bounds__(192, 1)
           asm volatile("bar.sync 1, 128;" ::: "memory");
           constexpr int kVecPerRow = 128 * kEl / 16;   // 16 (bf16) or 32 (fp32) vectors per token row
           const int tid = threadIdx.x - 64;
-          const bool full_m = t.out_col0 + 128 <= p.m_valid && (p.ldo * kEl) % 16 == 0;
+          const bool full_m = th.out_col0 + 128 <= p.m_valid && (p.ldo * kEl) % 16 == 0;
           for (int e = tid; e < ((p.probe & 2) ? 0 : kCols * kVecPerRow); e += 128) {
             const int j = e / kVecPerRow, vi = e % kVecPerRow;
-            if (c0 + j >= t.b_valid) continue;
-            const size_t orow = (size_t)(t.b_row0 + c0 + j) * p.ldo;
+            if (c0 + j >= th.b_valid) continue;
+            const size_t orow = (size_t)(th.b_row0 + c0 + j) * p.ldo;
             const uint4 val = reinterpret_cast<const uint4*>(stage + (size_t)j * 128 * kEl)[vi];
             if (full_m) {
-              reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (orow + t.out_col0) * kEl)[vi] = val;
+              reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (orow + th.out_col0) * kEl)[vi] = val;
             } else {
-              const int m0 = t.out_col0 + vi * (16 / kEl);
+              const int m0 = th.out_col0 + vi * (16 / kEl);
               const uint8_t* src = reinterpret_cast<const uint8_t*>(&val);
               for (int b = 0; b < 16 / kEl; ++b)
                 if (m0 + b < p.m_valid)
@@ -575,8 +593,9 @@ __global__ void __launch_bounds__(192, 1)
       if (!split) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0 && last_h) mbar_arrive(&acc_empty[acc]);
       }
+      }   // halves
       if (++acc == NA) {
         acc = 0;
         acc_phase ^= 1;
@@ -589,7 +608,7 @@ done:
   // epilogue's, or here for the producer/MMA warps and after an abort), so no
   // CTA of the cluster can be left waiting
   if (csplit)
-    while (csyncs < 2) {
+    while (csyncs < 2 * L::kSfaChunks) {
       cluster_sync_all();
       ++csyncs;
     }
@@ -609,11 +628,11 @@ done:
 }
 
 // ------------------------------------------------------------------- host
-template <int KIND, int BN, int EPI, bool GROUPED>
+template <int KIND, int BN, int EPI, bool GROUPED, int BM = 128>
 static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
                               cudaStream_t st) {
-  using L = GemmSmem<BN>;
-  auto k = gemm_kernel<KIND, BN, EPI, GROUPED>;
+  using L = GemmSmem<BN, BM>;
+  auto k = gemm_kernel<KIND, BN, EPI, GROUPED, BM>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -642,8 +661,18 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
 }
 
 template <int KIND, int EPI, bool GROUPED>
-static cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
+static cudaError_t dispatch_bn(int bn, int bm, const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
                                cudaStream_t st) {
+  if constexpr (KIND != KIND_BF16 && !GROUPED && EPI != EPI_SWIGLU) {
+    if (bm == 256) {
+      switch (bn) {
+        case 64: return launch_one<KIND, 64, EPI, GROUPED, 256>(ta, tb, p, grid, st);
+        case 128: return launch_one<KIND, 128, EPI, GROUPED, 256>(ta, tb, p, grid, st);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+  }
+  if (bm != 128) return cudaErrorInvalidValue;
   switch (bn) {
     case 32: return launch_one<KIND, 32, EPI, GROUPED>(ta, tb, p, grid, st);
     case 64: return launch_one<KIND, 64, EPI, GROUPED>(ta, tb, p, grid, st);
@@ -655,13 +684,13 @@ static cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const BMaps& tb, c
 
 // How many clusters of `splits` CTAs of this kernel can be resident at once
 // (clusters live inside one GPC, so this is below SMs / splits).  Cached.
-template <int KIND, int BN, int EPI>
+template <int KIND, int BN, int EPI, int BM = 128>
 static int cluster_cap(int splits) {
   static int cache[9] = {0};
   if (splits < 2 || splits > 8) return 0;
   if (cache[splits]) return cache[splits];
-  using L = GemmSmem<BN>;
-  auto k = gemm_kernel<KIND, BN, EPI, false>;
+  using L = GemmSmem<BN, BM>;
+  auto k = gemm_kernel<KIND, BN, EPI, false, BM>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess) {
     (void)cudaGetLastError();
     return 0;
@@ -687,7 +716,17 @@ static int cluster_cap(int splits) {
 }
 
 template <int KIND, int EPI>
-static int cap_bn(int bn, int splits) {
+static int cap_bn(int bn, int splits, int bm) {
+  if constexpr (KIND != KIND_BF16 && EPI != EPI_SWIGLU) {
+    if (bm == 256) {
+      switch (bn) {
+        case 64: return cluster_cap<KIND, 64, EPI, 256>(splits);
+        case 128: return cluster_cap<KIND, 128, EPI, 256>(splits);
+        default: return 0;
+      }
+    }
+  }
+  if (bm != 128) return 0;
   switch (bn) {
     case 32: return cluster_cap<KIND, 32, EPI>(splits);
     case 64: return cluster_cap<KIND, 64, EPI>(splits);
@@ -697,21 +736,21 @@ static int cap_bn(int bn, int splits) {
   }
 }
 
-int gemm_max_clusters(int kind, int epi, int bn, int splits) {
+int gemm_max_clusters(int kind, int epi, int bn, int splits, int bm) {
   if (kind == KIND_BF16) {
-    if (epi == EPI_BF16) return cap_bn<KIND_BF16, EPI_BF16>(bn, splits);
-    if (epi == EPI_F32) return cap_bn<KIND_BF16, EPI_F32>(bn, splits);
+    if (epi == EPI_BF16) return cap_bn<KIND_BF16, EPI_BF16>(bn, splits, bm);
+    if (epi == EPI_F32) return cap_bn<KIND_BF16, EPI_F32>(bn, splits, bm);
     return 0;
   }
   if (kind == KIND_MX8) {
-    if (epi == EPI_BF16) return cap_bn<KIND_MX8, EPI_BF16>(bn, splits);
-    if (epi == EPI_F32) return cap_bn<KIND_MX8, EPI_F32>(bn, splits);
-    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX8, EPI_SWIGLU>(bn, splits);
+    if (epi == EPI_BF16) return cap_bn<KIND_MX8, EPI_BF16>(bn, splits, bm);
+    if (epi == EPI_F32) return cap_bn<KIND_MX8, EPI_F32>(bn, splits, bm);
+    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX8, EPI_SWIGLU>(bn, splits, bm);
   }
   if (kind == KIND_MX4A) {
-    if (epi == EPI_BF16) return cap_bn<KIND_MX4A, EPI_BF16>(bn, splits);
-    if (epi == EPI_F32) return cap_bn<KIND_MX4A, EPI_F32>(bn, splits);
-    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX4A, EPI_SWIGLU>(bn, splits);
+    if (epi == EPI_BF16) return cap_bn<KIND_MX4A, EPI_BF16>(bn, splits, bm);
+    if (epi == EPI_F32) return cap_bn<KIND_MX4A, EPI_F32>(bn, splits, bm);
+    if (epi == EPI_SWIGLU) return cap_bn<KIND_MX4A, EPI_SWIGLU>(bn, splits, bm);
   }
   return 0;
 }
@@ -726,23 +765,23 @@ int gemm_smem_bytes(int bn) {
   }
 }
 
-cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorMap& ta, const BMaps& tb,
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const CUtensorMap& ta, const BMaps& tb,
                         const GemmParams& p, int grid, cudaStream_t st) {
   if (kind == KIND_BF16) {
     if (grouped) return cudaErrorInvalidValue;
-    if (epi == EPI_BF16) return dispatch_bn<KIND_BF16, EPI_BF16, false>(bn, ta, tb, p, grid, st);
-    if (epi == EPI_F32) return dispatch_bn<KIND_BF16, EPI_F32, false>(bn, ta, tb, p, grid, st);
+    if (epi == EPI_BF16) return dispatch_bn<KIND_BF16, EPI_BF16, false>(bn, bm, ta, tb, p, grid, st);
+    if (epi == EPI_F32) return dispatch_bn<KIND_BF16, EPI_F32, false>(bn, bm, ta, tb, p, grid, st);
     return cudaErrorInvalidValue;
   }
 #define DSV4_MX(KD)                                                                                  \
   if (kind == KD) {                                                                                  \
     if (!grouped) {                                                                                  \
-      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, false>(bn, ta, tb, p, grid, st);         \
-      if (epi == EPI_F32) return dispatch_bn<KD, EPI_F32, false>(bn, ta, tb, p, grid, st);           \
-      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, false>(bn, ta, tb, p, grid, st);     \
+      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, false>(bn, bm, ta, tb, p, grid, st);         \
+      if (epi == EPI_F32) return dispatch_bn<KD, EPI_F32, false>(bn, bm, ta, tb, p, grid, st);           \
+      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, false>(bn, bm, ta, tb, p, grid, st);     \
     } else {                                                                                         \
-      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, true>(bn, ta, tb, p, grid, st);          \
-      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, true>(bn, ta, tb, p, grid, st);      \
+      if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, true>(bn, bm, ta, tb, p, grid, st);          \
+      if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, true>(bn, bm, ta, tb, p, grid, st);      \
     }                                                                                                \
     return cudaErrorInvalidValue;                                                                    \
   }

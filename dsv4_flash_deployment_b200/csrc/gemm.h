@@ -56,8 +56,10 @@ struct BMaps {
 };
 
 int gemm_smem_bytes(int bn);
-int gemm_max_clusters(int kind, int epi, int bn, int splits);   // resident clusters of `splits` CTAs
-cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, const CUtensorMap& ta, const BMaps& tb,
+// bm: weight rows per tile, 128, or 256 (two 128-row MMAs sharing the token tile;
+// dense MXFP8/MXFP4 GEMMs with bf16/fp32 outputs and 64/128-token tiles only)
+int gemm_max_clusters(int kind, int epi, int bn, int splits, int bm);   // resident clusters of `splits` CTAs
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const CUtensorMap& ta, const BMaps& tb,
                         const GemmParams& p, int grid, cudaStream_t st);
 
 // 2-D tensor map over a row-major [rows, cols] matrix of 1-byte (e4m3), 2-byte

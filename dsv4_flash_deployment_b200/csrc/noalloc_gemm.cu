@@ -139,5 +139,5 @@ extern "C" __attribute__((visibility("default"))) int dsv4_gemm_mx8_noalloc(
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int units = tiles * splits;
   const int grid = units < sms ? units : sms;
-  return (int)dsv4::gemm_launch(dsv4::KIND_MX8, dsv4::EPI_BF16, false, bn, ta, tb, p, grid, stream);
+  return (int)dsv4::gemm_launch(dsv4::KIND_MX8, dsv4::EPI_BF16, false, bn, 128, ta, tb, p, grid, stream);
 }

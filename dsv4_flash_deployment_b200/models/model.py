@@ -324,12 +324,9 @@ class DSV4Model:
         """Block-scaled GEMM; few output tiles -> split-K inside a thread-block cluster
         (each split keeps >= 2 k-tiles; the kernel binding trims the split count to
         what the GPU can keep resident)."""
-        bn = pick_bn(n_tok)
-        tiles = (w.q.shape[0] // 128) * ((n_tok + bn - 1) // bn)
-        splits = 1
-        if tiles < 100:
-            splits = max(1, min(8, (w.k // 128) // 2, 148 // max(tiles, 1)))
-        return gemm_mx(xq, xsf, n_tok, w, out, epi, splits=splits, **kw)
+        # splits=-1: the binding picks the split count from the tile count of the
+        # weight-tile height it chooses (128 or 256 rows)
+        return gemm_mx(xq, xsf, n_tok, w, out, epi, splits=-1, **kw)
 
     def _gemm_bf16(self, x, w, out, n_tok, f32_out=False, groups=1, m_valid=None):
         bn = pick_bn(n_tok)

@@ -279,3 +279,27 @@ def test_cluster_split_k_bf16_and_swiglu():
     torch.cuda.synchronize()
     G.ErrorWord.check("cuda")
     _close(out, ref, 1e-3)
+
+
+@pytest.mark.parametrize("n_tok", [40, 100, 127, 300])
+@pytest.mark.parametrize("n,k", [(512, 1024), (4096, 4096), (1536, 2048)])
+@pytest.mark.parametrize("epi", [G.EPI_F32, G.EPI_BF16])
+@pytest.mark.parametrize("splits", [-1, 1])
+def test_mx8_dense_256_row_tiles(n_tok, n, k, epi, splits):
+    """Dense GEMMs with M % 256 == 0 and 64/128-token tiles run two M=128 MMAs per
+    stage (one 256-row weight tile sharing the token tile), with split-K inside a
+    cluster (splits=-1: automatic) and without; the result must match the fp32
+    reference of the same op."""
+    w, s = _rand_fp8_weight(n, k, 5)
+    torch.manual_seed(n_tok + n)
+    x = torch.randn(n_tok, k).to(torch.bfloat16)
+    ref = N.fp8_linear(x, w, s, torch.float32)
+    mw = G.MxWeight.from_checkpoint(w, s, "cuda")
+    xq, xsf = G.quantize(x.cuda())
+    dt = torch.float32 if epi == G.EPI_F32 else torch.bfloat16
+    out = torch.empty(n_tok, n, dtype=dt, device="cuda")
+    for _ in range(2):   # the second call reuses the resident cluster / stage state
+        G.gemm_mx(xq, xsf, n_tok, mw, out, epi, splits=splits)
+    torch.cuda.synchronize()
+    G.ErrorWord.check("cuda")
+    _close(out, ref, 1e-3 if epi == G.EPI_F32 else 2e-2)
