@@ -33,6 +33,8 @@ class EngineConfig:
     use_cuda_graphs: bool = True
     expert_storage_layers: int | None = None
     ep_transport: str = "nccl"              # "nccl" (baseline) or "p2p" (NVLink peer stores)
+    parallel: str = "ep"                    # multi-GPU layout: "ep" (data-parallel attention + expert
+                                            # parallelism, throughput) or "tp" (tensor-parallel, latency)
     dspark: bool = False
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True

@@ -10,7 +10,11 @@ model step, so all ranks step in lockstep.  Per step:
            when this rank has none, to join the step's collectives)
   all      gather     [(request id, token, finished, reason)] -> rank 0
 
-Rank 0 assigns new requests to the rank with the fewest live requests.  The
+Rank 0 assigns new requests to the rank with the fewest live requests.  In the
+replicated mode (tensor-parallel layout) every request goes to every rank: the
+local schedulers see the same adds and cancels in the same order, so they
+build the same step, the tensor-parallel kernels exchange their partials, and
+only rank 0 reports tokens (all ranks hold the same ones).  The
 control messages travel on a gloo group so they never queue behind NCCL
 kernels.  A rank that dies or stalls makes the next control collective fail
 after the group's timeout; rank 0 raises, and the HTTP layer fails the live
@@ -70,21 +74,21 @@ class _SchedView:
 
     @property
     def max_seqs(self) -> int:
-        return self.de.world * self.de.local.sched.max_seqs
+        return (1 if self.de.replicated else self.de.world) * self.de.local.sched.max_seqs
 
     @property
     def slots(self):
         de = self.de
 
         class _S:
-            n_free = max(0, de.world * de.local.sched.max_seqs - len(de.live))
+            n_free = max(0, (1 if de.replicated else de.world) * de.local.sched.max_seqs - len(de.live))
         return _S()
 
 
-def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int) -> list[tuple]:
+def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int, replicated: bool = False) -> list[tuple]:
     """Applies a control message to this rank's engine and runs its part of the step."""
     for gid, r, prompt, mt, ignore_eos, stop_ids in msg["adds"]:
-        if r == rank:
+        if r == rank or r == -1:
             req = engine.add_request(prompt, mt, ignore_eos=ignore_eos, stop_ids=stop_ids)
             id_map[req.req_id] = gid
             id_map[("g", gid)] = req
@@ -96,7 +100,7 @@ def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int) -> li
         return []
     before = engine.stats["steps"]
     events = engine.step() if not engine.sched.idle else []
-    if engine.stats["steps"] == before:
+    if engine.stats["steps"] == before and not replicated:
         # no local forward ran: join the step's collectives with a 1-token step on the reserved slot
         engine.run_meta(StepMeta(engine.cfg, [SeqChunk(pad_slot, 0, [0], True)]))
         engine.stats["dummy_steps"] = engine.stats.get("dummy_steps", 0) + 1
@@ -112,14 +116,17 @@ def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int) -> li
                 out.append((key[1], None, True, req.finish_reason))
             del id_map[key]
             id_map.pop(req.req_id, None)
+    if replicated and rank != 0:
+        return []   # every rank produced the same tokens; rank 0 reports them
     return out
 
 
 class DistributedEngine:
     """Rank-0 front with the :class:`.engine.Engine` API over all ranks."""
 
-    def __init__(self, local_engine, cpu_group=None, pad_slot: int | None = None):
+    def __init__(self, local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False):
         self.local = local_engine
+        self.replicated = replicated
         self.cfg = local_engine.cfg
         self.group = cpu_group
         self.rank = dist.get_rank(cpu_group)
@@ -142,7 +149,7 @@ class DistributedEngine:
         if len(prompt) + max_new_tokens > self.local.sched.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.local.sched.max_seq_len}")
-        r = min(range(self.world), key=lambda i: self.load[i])
+        r = -1 if self.replicated else min(range(self.world), key=lambda i: self.load[i])
         g = GlobalRequest(self.next_id, r, list(prompt), max_new_tokens)
         g._opts = (bool(ignore_eos), tuple(stop_ids))
         self.next_id += 1
@@ -159,7 +166,7 @@ class DistributedEngine:
         self.pending_cancels = []
         box = [msg]
         dist.broadcast_object_list(box, src=0, group=self.group)
-        mine = _local_step(self.local, msg, 0, self.id_map, self.pad_slot)
+        mine = _local_step(self.local, msg, 0, self.id_map, self.pad_slot, self.replicated)
         gathered = [None] * self.world
         dist.gather_object(mine, gathered, dst=0, group=self.group)
         now = time.perf_counter()
@@ -175,7 +182,8 @@ class DistributedEngine:
                         g.t_first_token = now
                 if fin:
                     g.finished, g.finish_reason, g.t_done = True, reason, now
-                    self.load[g.rank] -= 1
+                    if g.rank >= 0:
+                        self.load[g.rank] -= 1
                     del self.live[gid]
                 events.append((g, tok))
         self.stats["steps"] += 1
@@ -198,7 +206,7 @@ class DistributedEngine:
         return [r.output for r in reqs]
 
 
-def worker_loop(local_engine, cpu_group=None, pad_slot: int | None = None) -> int:
+def worker_loop(local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False) -> int:
     """Ranks > 0: follow rank 0's control messages until it sends stop. Returns steps run."""
     rank = dist.get_rank(cpu_group)
     pad = local_engine.sched.max_seqs if pad_slot is None else pad_slot
@@ -210,6 +218,6 @@ def worker_loop(local_engine, cpu_group=None, pad_slot: int | None = None) -> in
         msg = box[0]
         if msg["stop"]:
             return n
-        mine = _local_step(local_engine, msg, rank, id_map, pad)
+        mine = _local_step(local_engine, msg, rank, id_map, pad, replicated)
         dist.gather_object(mine, None, dst=0, group=cpu_group)
         n += 1

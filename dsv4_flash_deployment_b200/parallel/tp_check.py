@@ -125,13 +125,37 @@ def main(argv=None):
     ErrorWord.check(dev)
     ref.upload(tm, {})
     ms_one = _time(ref, tm, a.iters, True, dev)
+    # serving path: the replicated control plane (gloo) over tensor-parallel engines
+    # must emit what a single-GPU engine emits for the same prompts
+    from ..engine.dist_engine import DistributedEngine, worker_loop
+    from ..engine.engine import Engine
+    cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+    prompts = [[16 + (7 * i + 3 * j) % 900 for j in range(20 + 9 * i)] for i in range(2)]
+    tp2 = TPGroup(rank, world, dist.group.WORLD, dev)
+    eng_tp = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=64, max_seq_len=256, weights=w, tp=tp2)
+    if rank == 0:
+        de = DistributedEngine(eng_tp, cpu_group, replicated=True)
+        served = de.generate(prompts, 6, ignore_eos=True)
+        de.shutdown()
+    else:
+        worker_loop(eng_tp, cpu_group, replicated=True)
+        served = None
+    eng_tp.graphs.clear()
+    eng_one = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=64, max_seq_len=256, weights=w)
+    local = eng_one.generate(prompts, 6, ignore_eos=True)
+    eng_one.graphs.clear()
+    serve_ok = torch.tensor([0 if rank != 0 or served == local else 1], device=dev)
+    dist.all_reduce(serve_ok)
+    flag += serve_ok
     res = {"world": world, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
+           "served_matches_one_gpu": bool(serve_ok.item() == 0),
            "decode_ms_graph": round(ms_graph, 4), "decode_ms_eager": round(ms_eager, 4),
            "decode_ms_one_gpu_graph": round(ms_one, 4), "layers": cfg.n_layers}
     if rank == 0:
         print(json.dumps(res), flush=True)
-    del m
+    del m, eng_tp
     tp.release()
+    tp2.release()
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()

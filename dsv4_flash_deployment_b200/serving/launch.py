@@ -15,7 +15,7 @@ import torch.distributed as dist
 from ..engine.config import EngineConfig
 
 
-def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0):
+def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None):
     from ..engine.engine import Engine
 
     cfg = ec.model_config()
@@ -29,7 +29,7 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0):
     return Engine.build(cfg, device=ec.device, max_seqs=ec.max_seqs, max_batched_tokens=ec.max_batched_tokens,
                         max_seq_len=ec.max_model_len, weights=_load_weights(ec, cfg), seed=ec.seed,
                         expert_storage_layers=ec.expert_storage_layers, ep=ep, use_graphs=ec.use_cuda_graphs,
-                        chunk_size=ec.chunk_size, extra_slots=extra_slots)
+                        chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp)
 
 
 def _load_weights(ec: EngineConfig, cfg):
@@ -40,7 +40,9 @@ def _load_weights(ec: EngineConfig, cfg):
 
 
 def init_distributed(ec: EngineConfig):
-    """(rank, world, ep, cpu_group) from torchrun's environment; world 1 without it."""
+    """(rank, world, par, cpu_group) from torchrun's environment; world 1 without it.
+    ``par`` is the expert-parallel group (``parallel="ep"``) or the tensor-parallel
+    group (``parallel="tp"``)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world == 1:
         return 0, 1, None, None
@@ -53,6 +55,9 @@ def init_distributed(ec: EngineConfig):
     dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                             timeout=datetime.timedelta(seconds=300))
     cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
+    if ec.parallel == "tp":
+        from ..parallel.tp import TPGroup
+        return rank, world, TPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local)), cpu_group
     from ..parallel.ep import EPGroup
     ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), transport=ec.ep_transport)
     return rank, world, ep, cpu_group
@@ -67,15 +72,18 @@ def main(argv: list[str] | None = None) -> None:
     from .tokenizer import load_tokenizer
 
     ec = EngineConfig.from_args(argv)
-    rank, world, ep, cpu_group = init_distributed(ec)
+    rank, world, par, cpu_group = init_distributed(ec)
     if ec.device == "cuda" and world == 1:
         torch.cuda.set_device(0)
-    local = build_local_engine(ec, ep, extra_slots=1 if world > 1 else 0)
+    replicated = world > 1 and ec.parallel == "tp"
+    local = build_local_engine(ec, None if replicated else par, extra_slots=1 if world > 1 else 0,
+                               tp=par if replicated else None)
     if rank != 0:
-        worker_loop(local, cpu_group)
+        worker_loop(local, cpu_group, replicated=replicated)
+        local.graphs.clear()
         dist.destroy_process_group()
         return
-    eng = DistributedEngine(local, cpu_group) if world > 1 else local
+    eng = DistributedEngine(local, cpu_group, replicated=replicated) if world > 1 else local
     loop = EngineLoop(eng, step_deadline_s=ec.step_deadline_s).start()
     tok = load_tokenizer(ec.tokenizer, local.cfg)
     info = {"device": ec.device, "world_size": world, "engine_config": ec.to_dict()}

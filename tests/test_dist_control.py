@@ -59,6 +59,43 @@ def test_two_ranks_serve_and_match_oracle():
     assert res[1]["steps"] > 0 and res[1]["served"] > 0
 
 
+def _rank_generate_replicated(rank, world):
+    import torch.distributed as dist
+
+    from dsv4_flash_deployment_b200.engine.dist_engine import DistributedEngine, worker_loop
+
+    eng = _engine()
+    if rank != 0:
+        n = worker_loop(eng, dist.group.WORLD, replicated=True)
+        return {"steps": n, "served": eng.stats["steps"], "dummy": eng.stats.get("dummy_steps", 0),
+                "tokens": eng.stats["tokens"]}
+    de = DistributedEngine(eng, dist.group.WORLD, replicated=True)
+    reqs = [de.add_request(p, N_NEW, ignore_eos=True) for p in PROMPTS]
+    while not all(r.finished for r in reqs):
+        de.step()
+    de.shutdown()
+    return {"outs": [r.output for r in reqs], "ranks": [r.rank for r in reqs], "tokens": eng.stats["tokens"],
+            "max_seqs": de.sched.max_seqs}
+
+
+def test_replicated_mode_runs_the_same_steps_on_every_rank():
+    """Tensor-parallel serving: every rank schedules every request and runs the
+    same steps (same token count, no dummy steps); rank 0 alone reports tokens."""
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
+    from dsv4_flash_deployment_b200.ref.model import RefModel
+
+    res = spawn(_rank_generate_replicated, 2, timeout_s=300)
+    cfg = toy_v4_config()
+    ref = RefModel(cfg, make_random_weights(cfg, seed=0, include_mtp=False), max_seq_len=96)
+    for p, got in zip(PROMPTS, res[0]["outs"]):
+        want, _ = ref.generate(torch.tensor([p]), N_NEW)
+        assert got == want[0].tolist()
+    assert set(res[0]["ranks"]) == {-1}
+    assert res[0]["max_seqs"] == 2
+    assert res[1]["dummy"] == 0 and res[1]["tokens"] == res[0]["tokens"]
+
+
 def _rank_dies(rank, world):
     import torch.distributed as dist
 
