@@ -53,12 +53,14 @@ DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 // 256 threads.  Thread -> (token tid/16, 8 columns (tid%16)*8 of the slice).
 constexpr int kMaxCombine = 8;   // routed experts per token summed by the MoE combine
 
-__global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) {
+__global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slices) {
   pdl_entry();
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sFn = reinterpret_cast<__nv_bfloat16*>(smem);                 // [48][kRowE]
   __nv_bfloat16* sX = sFn + kNMix * kRowE;                                      // [16][kRowE]
-  float* sRed = reinterpret_cast<float*>(sX + kTokTile * kRowE);                // [8 warps][16][48]
+  // [8 warps][16][48] cross-warp sums of the mixes; aliases sFn, which is dead
+  // once every warp's MMAs have read it (barrier below)
+  float* sRed = reinterpret_cast<float*>(sFn);
   const int slice = blockIdx.x;
   const int t0 = blockIdx.y * kTokTile;
   const int D = p.D;
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(256) hc_post_kernel(HcParams p, int n_slices) 
       mma16816(acc[n], a0, a1, a2, a3, b0, b1);
     }
   }
+  __syncthreads();   // every warp is done reading sFn before sRed overwrites it
   const int g = lane >> 2, cq = lane & 3;
 #pragma unroll
   for (int n = 0; n < 6; ++n) {
@@ -412,7 +415,8 @@ cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   if ((p.yperm != nullptr || p.tp_mode == 2) && p.topk > kMaxCombine) return cudaErrorInvalidValue;
   if (p.D % kSlice) return cudaErrorInvalidValue;
   const int ns = hc_num_slices(p.D);
-  const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2 + (size_t)8 * kTokTile * kNMix * 4;
+  const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2;
+  static_assert((size_t)8 * kTokTile * kNMix * 4 <= (size_t)kNMix * kRowE * 2, "sRed must fit in sFn");
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(hc_post_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
