@@ -147,6 +147,9 @@ def main() -> None:
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--c1-layout", default="auto", choices=["auto", "tp", "dp"],
                     help="C=1 TPOT on N>1 GPUs: tensor-parallel decode model (auto/tp) or the batch layout (dp)")
+    ap.add_argument("--c1-moe", default="ep", choices=["ep", "tp"],
+                    help="experts in the tensor-parallel C=1 model: owned whole (ep, shared with the batch model) "
+                         "or split by intermediate index over all GPUs (tp)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert exchange: NVLink peer stores (p2p) or the NCCL all-to-all baseline")
     args = ap.parse_args()
@@ -335,9 +338,11 @@ def main() -> None:
     c1_tp = None
     if world > 1 and args.c1_layout in ("auto", "tp"):
         from dsv4_flash_deployment_b200.parallel.tp import TPGroup
-        tpg = TPGroup(rank, world, group, dev)
+        tpg = TPGroup(rank, world, group, dev, moe=args.c1_moe)
         eng_tp = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=16, max_seq_len=max_seq, tp=tpg,
-                              experts_from=model, use_graphs=not args.no_graphs, chunk_size=16)
+                              experts_from=model if args.c1_moe == "ep" else None,
+                              expert_storage_layers=n_phys if args.c1_moe == "tp" else None,
+                              use_graphs=not args.no_graphs, chunk_size=16)
         rng_tp = np.random.default_rng(4321)   # the same tokens on every rank
 
         def tp_meta(i):
@@ -406,8 +411,10 @@ def main() -> None:
                            if c1_tp is None else
                            {"value": round(c1_tp[1], 3), "device_ms": round(c1_tp[0], 3), "context": c1_pos,
                             "baseline_ms": 27.69,
-                            "layout": f"tp{world} attention/wo_b/head + ep{world} experts (no dispatch), "
-                                      "NVLink reductions inside the producing/consuming kernels",
+                            "layout": f"tp{world} attention/wo_b/head + "
+                                      + (f"ep{world} experts (no dispatch)" if args.c1_moe == "ep"
+                                         else f"experts split by intermediate over {world} GPUs (ep x tp{world})")
+                                      + ", NVLink reductions inside the producing/consuming kernels",
                             "batch_layout_ms": round(c1_wall, 3),
                             "note": "one sequence, the same 1-token step on every rank through Engine.run_meta "
                                     "(pinned H2D + D2H + sync each token), graph replay, max over ranks"}),

@@ -287,9 +287,11 @@ void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>&
     p.ids = reinterpret_cast<const int*>(v[11]);
     p.e_local = (int)v[12];
     p.err = reinterpret_cast<uint32_t*>(err->data_ptr<int>());
-    TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
+    TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr
+                : p.tp_mode == 3 ? (p.peer_y != nullptr && p.pos != nullptr && topk > 0)
+                                 : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
                 "tp mode tables missing");
-    TORCH_CHECK(p.tp_mode == 1 || p.tp_mode == 2, "tp mode must be 1 or 2");
+    TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 3, "tp mode must be 1, 2 or 3");
   }
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));

@@ -781,6 +781,7 @@ cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const C
       if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, false>(bn, bm, ta, tb, p, grid, st);     \
     } else {                                                                                         \
       if (epi == EPI_BF16) return dispatch_bn<KD, EPI_BF16, true>(bn, bm, ta, tb, p, grid, st);          \
+      if (epi == EPI_F32) return dispatch_bn<KD, EPI_F32, true>(bn, bm, ta, tb, p, grid, st);            \
       if (epi == EPI_SWIGLU) return dispatch_bn<KD, EPI_SWIGLU, true>(bn, bm, ta, tb, p, grid, st);      \
     }                                                                                                \
     return cudaErrorInvalidValue;                                                                    \

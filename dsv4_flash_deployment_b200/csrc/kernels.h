@@ -42,7 +42,9 @@ struct HcParams {
   // tensor parallel (hc_post): tp_mode 1 = the sublayer output is the rank-order
   // sum of every rank's f32 partial (peer_y, rows D apart); tp_mode 2 = each
   // (token, slot) pair's expert row is read from the rank owning its expert
-  // (peer_yperm / peer_pos; ids are identical on every rank).  Both wait first
+  // (peer_yperm / peer_pos; ids are identical on every rank); tp_mode 3 = experts
+  // split by intermediate index: every rank's f32 partial row of each pair
+  // (peer_y tables, row pos[t, slot]) summed in rank order.  All wait first
   // (bounded) until every rank has published the phase.
   int tp_mode;
   const float* const* peer_y;

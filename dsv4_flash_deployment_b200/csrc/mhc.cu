@@ -139,6 +139,32 @@ __global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slice
           }
         }
       }
+      if (p.tp_mode == 3) {
+        // experts split over the ranks by intermediate index: every rank holds an
+        // f32 partial row for every routed pair (same row index on every rank);
+        // sum ranks in order, slots in order, so every rank gets the same bits
+        const int k = min(p.topk, kMaxCombine);
+        int rw[kMaxCombine];
+#pragma unroll
+        for (int s = 0; s < kMaxCombine; ++s) rw[s] = s < k ? p.pos[(size_t)t * p.topk + s] : -1;
+        for (int rk = 0; rk < p.wait.world; ++rk) {
+          const float* base = p.peer_y[rk];
+          float4 a[kMaxCombine], b[kMaxCombine];
+#pragma unroll
+          for (int s = 0; s < kMaxCombine; ++s)
+            if (rw[s] >= 0) {
+              const float4* src = reinterpret_cast<const float4*>(base + (size_t)rw[s] * D + d);
+              a[s] = src[0];
+              b[s] = src[1];
+            }
+#pragma unroll
+          for (int s = 0; s < kMaxCombine; ++s)
+            if (rw[s] >= 0) {
+              y[0] += a[s].x; y[1] += a[s].y; y[2] += a[s].z; y[3] += a[s].w;
+              y[4] += b[s].x; y[5] += b[s].y; y[6] += b[s].z; y[7] += b[s].w;
+            }
+        }
+      }
       if (p.tp_mode == 1) {
         // rank-order sum of the f32 partials: the same bits on every rank
 #pragma unroll 8
@@ -412,7 +438,7 @@ int hc_num_slices(int D) { return (D + kSlice - 1) / kSlice; }
 
 cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  if ((p.yperm != nullptr || p.tp_mode == 2) && p.topk > kMaxCombine) return cudaErrorInvalidValue;
+  if ((p.yperm != nullptr || p.tp_mode >= 2) && p.topk > kMaxCombine) return cudaErrorInvalidValue;
   if (p.D % kSlice) return cudaErrorInvalidValue;
   const int ns = hc_num_slices(p.D);
   const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2;

@@ -47,7 +47,10 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     if weights is not None:
         for lid in range(cfg.n_layers):
             rng = par.expert_range(cfg.n_experts_for(lid)) if par is not None else None
-            layers.append(load_layer(cfg, weights, lid, dev, expert_range=rng))
+            L = load_layer(cfg, weights, lid, dev, expert_range=rng)
+            if tp is not None and tp.moe == "tp":
+                L.experts = tp.shard_experts(L.experts)   # this rank's intermediate slice
+            layers.append(L)
         embed = weights["embed.weight"].to(dev)
         head = _pad_rows(weights["head.weight"]).to(dev)
         norm = weights["norm.weight"].to(dev)
@@ -60,7 +63,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
                 raise ValueError("shared expert blocks belong to a different expert split")
         else:
             n_phys = expert_storage_layers or cfg.n_layers
-            stores = [random_experts(cfg, e_local, dev, g) for _ in range(min(n_phys, cfg.n_layers))]
+            inter = tp.inter_local(cfg.moe_inter_dim) if tp is not None else None
+            stores = [random_experts(cfg, e_local, dev, g, inter=inter) for _ in range(min(n_phys, cfg.n_layers))]
         for lid in range(cfg.n_layers):
             layers.append(random_layer(cfg, lid, dev, g, stores[lid % len(stores)]))
         embed = (torch.randn(cfg.vocab_size, cfg.dim, device=dev, generator=g) * 0.02).to(torch.bfloat16)

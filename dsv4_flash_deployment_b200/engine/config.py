@@ -35,6 +35,8 @@ class EngineConfig:
     ep_transport: str = "nccl"              # "nccl" (baseline) or "p2p" (NVLink peer stores)
     parallel: str = "ep"                    # multi-GPU layout: "ep" (data-parallel attention + expert
                                             # parallelism, throughput) or "tp" (tensor-parallel, latency)
+    moe_split: str = "ep"                   # parallel="tp": experts owned whole ("ep") or split by
+                                            # intermediate index over every GPU ("tp")
     dspark: bool = False
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True

@@ -193,7 +193,9 @@ class DSV4Model:
         # (decided on the expected rows per rank, T*k, not on the worst-case capacity)
         self.tile_rows = 128 if T * k <= 192 * e_local else 256
         tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
-        I = cfg.moe_inter_dim
+        # expert intermediate width on this rank (a tensor-parallel expert split keeps 1/N)
+        I = self.tp.inter_local(cfg.moe_inter_dim) if self.tp is not None else cfg.moe_inter_dim
+        self.inter_local = I
         self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)
         self.tiles2 = e(tiles_rows_max * (D // 128), 4, dt=i32)
         self.nt13, self.nt2 = z(1, dt=i32), z(1, dt=i32)
@@ -624,7 +626,7 @@ class DSV4Model:
         E = cfg.n_experts_for(lid)
         k = cfg.topk_for(lid)
         D = cfg.dim
-        I = cfg.moe_inter_dim
+        I = L.experts.inter
         logits = self.router_logits[E]
         rctx = self._t("router")
         rctx.__enter__()
@@ -647,7 +649,8 @@ class DSV4Model:
             self._shared_expert(L, T)
         if self.tp is not None:
             # the next mHC boundary reads every pair's row from the rank owning its expert
-            return None, None, k, self.tp.moe_desc(ids, e_local)
+            # (expert ownership) or sums every rank's partial row of each pair (expert split)
+            return None, pos, k, self.tp.moe_desc(ids, e_local)
         return self.yperm, pos, k, None
 
     def _shared_expert(self, L: LayerW, T: int):
@@ -658,7 +661,7 @@ class DSV4Model:
 
     def _grouped(self, L: LayerW, k: int):
         cfg, ext = self.cfg, self.ext
-        I, D = cfg.moe_inter_dim, cfg.dim
+        I, D = L.experts.inter, cfg.dim
         ex = L.experts
         bn = self.tile_rows
         c13 = self._t("grouped_w13")
@@ -669,7 +672,9 @@ class DSV4Model:
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
-        ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm, ex.w2.q.shape[0],
+        split = self.tp is not None and self.tp.moe == "tp"   # f32 partial rows, summed over ranks
+        ext.gemm(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm,
+                 ex.w2.q.shape[0],
                  self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1, 0,
                  self.tp.sync(1) if self.tp is not None else None)
         c2.__exit__(None, None, None)

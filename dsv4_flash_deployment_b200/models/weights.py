@@ -181,9 +181,11 @@ def _rand_mx(n: int, k: int, dev, gen: torch.Generator, kind_e2m1: bool = False)
     return MxWeight(q, sf, n, k, 2 if kind_e2m1 else 1)
 
 
-def random_experts(cfg, n_experts: int, dev, gen: torch.Generator) -> ExpertBlock:
+def random_experts(cfg, n_experts: int, dev, gen: torch.Generator, inter: int | None = None) -> ExpertBlock:
+    """``inter``: intermediate width per expert (default the model's; a tensor-parallel
+    expert split draws each rank's 1/N slice directly)."""
     e2m1 = cfg.expert_format == "mxfp4"
-    i, d = cfg.moe_inter_dim, cfg.dim
+    i, d = inter or cfg.moe_inter_dim, cfg.dim
     w13 = _rand_mx(n_experts * 2 * i, d, dev, gen, e2m1)
     w2 = _rand_mx(n_experts * d, i, dev, gen, e2m1)
     return ExpertBlock(w13, w2, n_experts, i)

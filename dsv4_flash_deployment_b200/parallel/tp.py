@@ -61,8 +61,18 @@ def mx_cols(w: MxWeight, k0: int, k1: int) -> MxWeight:
 
 
 class TPGroup:
-    def __init__(self, rank: int, world: int, group=None, device=None):
+    """``moe``: how the experts are split.  "ep" (default): each rank owns E/N whole
+    experts and gathers a pair's row from its owner.  "tp": every rank holds the
+    1/N slice of every expert's intermediate dimension (W13 rows, W2 input
+    columns), runs every routed pair on its slice, and the mHC boundary sums the
+    N f32 partial rows of each pair (the hybrid EP x TP layout with TP = N);
+    balanced weight streaming for decode batches where few experts are active."""
+
+    def __init__(self, rank: int, world: int, group=None, device=None, moe: str = "ep"):
+        if moe not in ("ep", "tp"):
+            raise ValueError(f"moe split {moe!r}")
         self.rank, self.world, self.group = rank, world, group
+        self.moe = moe
         self.dev = torch.device(device) if device is not None else torch.device("cuda", rank)
         self._b = None
 
@@ -78,11 +88,38 @@ class TPGroup:
         return o_groups // self.world
 
     def expert_range(self, n_experts: int) -> tuple[int, int]:
+        if self.moe == "tp":
+            return 0, n_experts
         per = n_experts // self.world
         return self.rank * per, per
 
     def experts_per_rank(self, n_experts: int) -> int:
-        return n_experts // self.world
+        return n_experts if self.moe == "tp" else n_experts // self.world
+
+    def inter_local(self, inter: int) -> int:
+        """Expert intermediate width on this rank."""
+        if self.moe != "tp":
+            return inter
+        if inter % (128 * self.world):
+            raise ValueError(f"expert intermediate {inter} does not split into 128-wide slices over {self.world}")
+        return inter // self.world
+
+    def shard_experts(self, ex):
+        """This rank's intermediate slice of an expert block holding every expert whole
+        (checkpoint path): W13 rows [e*2I + r*2I/N, ...) (gate/up interleaved in
+        64-row blocks, so a 128-row aligned slice keeps pairs together), W2 input
+        columns [r*I/N, ...)."""
+        from ..models.weights import ExpertBlock
+        il = self.inter_local(ex.inter)
+        E, r = ex.n_experts, self.rank
+        rows = [torch.arange(e * 2 * ex.inter + r * 2 * il, e * 2 * ex.inter + (r + 1) * 2 * il) for e in range(E)]
+        idx = torch.cat(rows).to(ex.w13.q.device)
+        q13 = ex.w13.q.index_select(0, idx).contiguous()
+        blocks = (idx.view(-1, 128)[:, 0] // 128)
+        sf13 = ex.w13.sf.index_select(0, blocks).contiguous()
+        w13 = MxWeight(q13, sf13, E * 2 * il, ex.w13.k, ex.w13.kind)
+        w2 = mx_cols(ex.w2, r * il, (r + 1) * il)
+        return ExpertBlock(w13, w2, E, il)
 
     def vocab_rows(self, vocab: int) -> tuple[int, int]:
         """(first row, rows) of this rank's head shard; the vocabulary is padded to
@@ -119,7 +156,8 @@ class TPGroup:
 
         W = self.world
         S = max(max_sample, 1)
-        sizes = [T * D * 4, cap_rows * D * 2, T * k * 4, S * 4, S * 4, N_PHASES * W * 4]
+        # expert rows: bf16 whole-expert rows ("ep" split) or f32 partial rows ("tp" split)
+        sizes = [T * D * 4, cap_rows * D * (4 if self.moe == "tp" else 2), T * k * 4, S * 4, S * 4, N_PHASES * W * 4]
         offs, cur = [], 0
         for sz in sizes:
             offs.append(cur)
@@ -134,7 +172,7 @@ class TPGroup:
         view = lambda i: buf[offs[i]:offs[i] + sizes[i]]
         b = dict(symm=buf, handle=hdl, k=k,
                  part=view(0).view(torch.float32).view(T, D),
-                 yperm=view(1).view(torch.bfloat16).view(cap_rows, D),
+                 yperm=view(1).view(torch.float32 if self.moe == "tp" else torch.bfloat16).view(cap_rows, D),
                  pos=view(2).view(torch.int32).view(T, k),
                  aval=view(3).view(torch.float32), aidx=view(4).view(torch.int32),
                  sig=view(5).view(torch.int32),
@@ -166,14 +204,19 @@ class TPGroup:
         return d
 
     def moe_desc(self, ids: torch.Tensor, e_local: int) -> torch.Tensor:
-        """hc_post descriptor: gather each pair's expert row from its owner (phase 1)."""
+        """hc_post descriptor (phase 1): gather each pair's expert row from its owner
+        ("ep" split), or sum every rank's f32 partial row of each pair ("tp" split)."""
         key = ("moe_desc", ids.data_ptr(), e_local)
         d = self._b.get(key)
         if d is None:
             b = self._b
-            d = torch.cat([torch.tensor([2], dtype=torch.int64), self._sync[PH_MOE],
-                           torch.tensor([0, b["peer_yperm"].data_ptr(), b["peer_pos"].data_ptr(), ids.data_ptr(),
-                                         e_local], dtype=torch.int64)])
+            if self.moe == "tp":
+                d = torch.cat([torch.tensor([3], dtype=torch.int64), self._sync[PH_MOE],
+                               torch.tensor([b["peer_yperm"].data_ptr(), 0, 0, 0, 0], dtype=torch.int64)])
+            else:
+                d = torch.cat([torch.tensor([2], dtype=torch.int64), self._sync[PH_MOE],
+                               torch.tensor([0, b["peer_yperm"].data_ptr(), b["peer_pos"].data_ptr(),
+                                             ids.data_ptr(), e_local], dtype=torch.int64)])
             b[key] = d
         return d
 

@@ -78,6 +78,8 @@ def main(argv=None):
     ap.add_argument("--seqs", type=int, default=3)
     ap.add_argument("--plen", type=int, default=40)
     ap.add_argument("--iters", type=int, default=30)
+    ap.add_argument("--moe", default="ep", choices=["ep", "tp"],
+                    help="experts owned whole by one rank (ep) or split by intermediate index over all ranks (tp)")
     a = ap.parse_args(argv)
 
     from ..engine.builder import build_model
@@ -94,7 +96,7 @@ def main(argv=None):
     cfg = small_cfg()
     w = make_random_weights(cfg, seed=11, include_mtp=False)
     ref = build_model(cfg, dev, max_tokens=256, n_slots=a.seqs + 1, max_seq_len=256, weights=w)
-    tp = TPGroup(rank, world, dist.group.WORLD, dev)
+    tp = TPGroup(rank, world, dist.group.WORLD, dev, moe=a.moe)
     m = build_model(cfg, dev, max_tokens=256, n_slots=a.seqs + 1, max_seq_len=256, weights=w, tp=tp)
     r0, rows = tp.vocab_rows(cfg.vocab_size)
     valid = max(0, min(rows, cfg.vocab_size - r0))
@@ -131,7 +133,7 @@ def main(argv=None):
     from ..engine.engine import Engine
     cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
     prompts = [[16 + (7 * i + 3 * j) % 900 for j in range(20 + 9 * i)] for i in range(2)]
-    tp2 = TPGroup(rank, world, dist.group.WORLD, dev)
+    tp2 = TPGroup(rank, world, dist.group.WORLD, dev, moe=a.moe)
     eng_tp = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=64, max_seq_len=256, weights=w, tp=tp2)
     if rank == 0:
         de = DistributedEngine(eng_tp, cpu_group, replicated=True)
@@ -147,7 +149,7 @@ def main(argv=None):
     serve_ok = torch.tensor([0 if rank != 0 or served == local else 1], device=dev)
     dist.all_reduce(serve_ok)
     flag += serve_ok
-    res = {"world": world, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
+    res = {"world": world, "moe_split": a.moe, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
            "served_matches_one_gpu": bool(serve_ok.item() == 0),
            "decode_ms_graph": round(ms_graph, 4), "decode_ms_eager": round(ms_eager, 4),
            "decode_ms_one_gpu_graph": round(ms_one, 4), "layers": cfg.n_layers}

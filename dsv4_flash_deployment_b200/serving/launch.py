@@ -57,7 +57,8 @@ def init_distributed(ec: EngineConfig):
     cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     if ec.parallel == "tp":
         from ..parallel.tp import TPGroup
-        return rank, world, TPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local)), cpu_group
+        tp = TPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), moe=ec.moe_split)
+        return rank, world, tp, cpu_group
     from ..parallel.ep import EPGroup
     ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), transport=ec.ep_transport)
     return rank, world, ep, cpu_group
