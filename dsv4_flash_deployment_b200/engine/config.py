@@ -37,7 +37,7 @@ class EngineConfig:
                                             # parallelism, throughput) or "tp" (tensor-parallel, latency)
     moe_split: str = "ep"                   # parallel="tp": experts owned whole ("ep") or split by
                                             # intermediate index over every GPU ("tp")
-    dspark: bool = False
+    dspark: bool = False                    # speculative decoding: SpecEngine only (the server refuses it)
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True
     host: str = "127.0.0.1"

@@ -73,6 +73,11 @@ def main(argv: list[str] | None = None) -> None:
     from .tokenizer import load_tokenizer
 
     ec = EngineConfig.from_args(argv)
+    if ec.dspark:
+        # speculative decoding runs through spec.dspark.SpecEngine (generate / draft /
+        # verify API, e.g. bench/v41_bench.py); the HTTP engine loop decodes greedily
+        raise SystemExit("--dspark: the OpenAI server decodes without speculation; use "
+                         "dsv4_flash_deployment_b200.spec.dspark.SpecEngine for DSpark generation")
     rank, world, par, cpu_group = init_distributed(ec)
     if ec.device == "cuda" and world == 1:
         torch.cuda.set_device(0)
