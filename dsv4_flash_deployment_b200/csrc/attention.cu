@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
       } else {
         const int jj = j - n_win;
         const int ci = p.comp_idx != nullptr ? p.comp_idx[(size_t)t * p.comp_k + jj] : jj;
-        r = p.comp + ((size_t)slot * p.max_c + ci) * kDh;
+        r = p.comp + kv_row(p.comp_pages, slot, ci, p.max_c) * kDh;
       }
       sRows[j] = r;
     }

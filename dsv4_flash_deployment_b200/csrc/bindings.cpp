@@ -48,6 +48,23 @@ int tma_elem_of(const Tensor& t, bool e2m1) {
 //   kind 0: bf16 x bf16; 1: e4m3 x e4m3 (MXFP8); 2: e2m1 (A) x e4m3 (B).
 //   A [a_rows, K] (packed e2m1: [a_rows, K/2]); B [b_rows, K].
 //   grouped: tiles int32 [n, 4] + n_tiles int32 [1] device tensors.
+// Optional int64 CPU tensor [block table address, ld, shift, logical max_c] of a
+// paged compressed cache -> KvPages; the logical per-slot capacity replaces the
+// pool tensor's size(1).  None = contiguous per-slot cache.
+static dsv4::KvPages kv_pages_of(const optional<Tensor>& d, int* max_c) {
+  dsv4::KvPages pg{};
+  if (!d) return pg;
+  TORCH_CHECK(!d->is_cuda() && d->scalar_type() == at::kLong && d->numel() >= 4, "pages: int64 CPU [4]");
+  const int64_t* v = d->data_ptr<int64_t>();
+  pg.table = reinterpret_cast<const int*>(v[0]);
+  pg.ld = (int)v[1];
+  pg.shift = (int)v[2];
+  *max_c = (int)v[3];
+  TORCH_CHECK(pg.table != nullptr && pg.ld > 0 && pg.shift >= 0 && pg.shift < 16 && *max_c > 0 &&
+              ((int64_t)pg.ld << pg.shift) >= *max_c, "bad page descriptor");
+  return pg;
+}
+
 // DSV4_GEMM_BM256=0 keeps every GEMM on 128-row weight tiles (A/B timing).
 static bool bm256_enabled() {
   static const bool on = [] {
@@ -313,7 +330,8 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
                const optional<Tensor>& comp, const Tensor& slot, const Tensor& pos, const Tensor& chunk_start,
                const Tensor& step_row0, const optional<Tensor>& comp_idx, const optional<Tensor>& comp_cnt,
                const Tensor& sink, double scale, const Tensor& out, const optional<Tensor>& workspace, int64_t T,
-               int64_t nsplit, const optional<Tensor>& win_end, int64_t win_len) {
+               int64_t nsplit, const optional<Tensor>& win_end, int64_t win_len,
+               const optional<Tensor>& comp_pages) {
   CHECK_CUDA(q);
   TORCH_CHECK(q.dim() == 3 && q.size(-1) == 512 && q.size(-2) <= 64 && q.stride(1) == 512 && q.stride(2) == 1,
               "q must be [T, H <= 64, 512]");
@@ -336,6 +354,7 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
   p.W = (int)ring.size(1);
   p.comp = ptr<const bf16>(comp);
   p.max_c = comp ? (int)comp->size(1) : 0;
+  if (comp) p.comp_pages = kv_pages_of(comp_pages, &p.max_c);
   p.slot = ptr<const int>(slot);
   p.pos = ptr<const int>(pos);
   p.chunk_start = ptr<const int>(chunk_start);
@@ -389,7 +408,7 @@ void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g
                    const Tensor& g_row0, int64_t r, int64_t co, const Tensor& proj, const optional<Tensor>& ape,
                    const Tensor& ring, const Tensor& norm_w, double eps, const Tensor& cos, const Tensor& sin,
                    const Tensor& comp_out, const optional<Tensor>& wk, const optional<Tensor>& k_norm_w,
-                   const optional<Tensor>& idx_out) {
+                   const optional<Tensor>& idx_out, const optional<Tensor>& pages) {
   dsv4::CompParams p{};
   p.n_groups = (int)n_groups;
   p.n_groups_dev = ptr<const int>(n_groups_dev);
@@ -413,6 +432,7 @@ void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g
   p.k_norm_w = ptr<const bf16>(k_norm_w);
   p.idx_out = ptr<bf16>(idx_out);
   p.idx_dim = idx_out ? (int)idx_out->size(2) : 0;
+  p.pages = kv_pages_of(pages, &p.max_c);
   CUDA_OK(dsv4::compress_pool(p, cur_stream()));
 }
 
@@ -478,7 +498,7 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
                   int64_t cand_mode, int64_t cand_block, int64_t cand_topk, int64_t T, const Tensor& err,
                   const optional<Tensor>& kcache_alt, const optional<Tensor>& pos,
                   const optional<Tensor>& chunk_start, const optional<Tensor>& last_pos, int64_t own_r,
-                  const Tensor& keys) {
+                  const Tensor& keys, const optional<Tensor>& pages, const optional<Tensor>& alt_pages) {
   dsv4::IdxParams p{};
   p.T = (int)T;
   p.n_heads = (int)q.size(1);
@@ -499,6 +519,8 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
   p.err = ptr<uint32_t>(err);
   p.kcache_alt = ptr<const bf16>(kcache_alt);
   p.alt_max_c = kcache_alt ? (int)kcache_alt->size(1) : 0;
+  p.pages = kv_pages_of(pages, &p.max_c);
+  if (kcache_alt) p.alt_pages = kv_pages_of(alt_pages, &p.alt_max_c);
   p.pos = ptr<const int>(pos);
   p.chunk_start = ptr<const int>(chunk_start);
   p.last_pos = ptr<const int>(last_pos);

@@ -19,9 +19,17 @@
 
 #include <utility>
 
+#include "kernels.h"
+
 #define DSV4_DEV __device__ __forceinline__
 
 namespace dsv4 {
+
+// Row of compressed entry ci of sequence slot `slot` in a (paged or contiguous) cache.
+DSV4_DEV size_t kv_row(const KvPages& pg, int slot, int ci, int max_c) {
+  if (pg.table == nullptr) return (size_t)slot * max_c + ci;
+  return ((size_t)pg.table[(size_t)slot * pg.ld + (ci >> pg.shift)] << pg.shift) + (ci & ((1 << pg.shift) - 1));
+}
 
 // ------------------------------------------------------------------ errors
 // Error word layout: bits [0,8) code, [8,16) kernel id, [16,32) detail.

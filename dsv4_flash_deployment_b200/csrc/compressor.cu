@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     amax = fmaxf(amax, 6.f * 0.001953125f);
     const float s = e4m3_to_f32(f32_to_e4m3(amax / 6.f));
-    p.comp_out[((size_t)slot * p.max_c + g) * dh + d] = __float2bfloat16(e2m1_qdq_c(z, s));
+    p.comp_out[kv_row(p.pages, slot, g, p.max_c) * dh + d] = __float2bfloat16(e2m1_qdq_c(z, s));
   }
   if (p.wk == nullptr) return;
   // ---- indexer key: k = bf16(latent @ wk^T) -> RMSNorm -> RoPE -> e2m1 (ue8m0 / 32)
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
   }
   const float amax = fmaxf(warp_max(fabsf(kn)), 6.f * 1.1754943508222875e-38f);
   const float s = exp_to_f32(pow2_ceil_exp(amax, 1.f / 6.f));
-  p.idx_out[((size_t)slot * p.max_c + g) * kd + d] = __float2bfloat16(e2m1_qdq_c(kn, s));
+  p.idx_out[kv_row(p.pages, slot, g, p.max_c) * kd + d] = __float2bfloat16(e2m1_qdq_c(kn, s));
 }
 
 cudaError_t compress_pool(const CompParams& p, cudaStream_t st) {

@@ -153,12 +153,14 @@ __global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* k
   const int slot = p.slot[t];
   const bool use_alt = p.kcache_alt != nullptr && ((p.pos[t] + 1) % p.own_r) != 0 &&
                        p.chunk_start[t] == p.last_pos[t];
-  const __nv_bfloat16* kbase = use_alt ? p.kcache_alt + (size_t)slot * p.alt_max_c * kIdxDh
-                                       : p.kcache + (size_t)slot * p.max_c * kIdxDh;
+  const __nv_bfloat16* kc = use_alt ? p.kcache_alt : p.kcache;
+  const KvPages kpg = use_alt ? p.alt_pages : p.pages;
+  const int kmax = use_alt ? p.alt_max_c : p.max_c;
   for (int c = tid; c < kIdxRows * (kIdxDh / 8); c += 128) {
     const int r = c / (kIdxDh / 8), ch = c % (kIdxDh / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r0 + r < clen) v = *reinterpret_cast<const uint4*>(kbase + (size_t)(r0 + r) * kIdxDh + ch * 8);
+    if (r0 + r < clen)
+      v = *reinterpret_cast<const uint4*>(kc + kv_row(kpg, slot, r0 + r, kmax) * kIdxDh + ch * 8);
     *reinterpret_cast<uint4*>(sK + r * kIdxPad + ch * 8) = v;
   }
   __syncthreads();

@@ -8,6 +8,15 @@
 
 namespace dsv4 {
 
+// Block table of a paged compressed cache: entry ci of sequence slot s lives in
+// pool row table[s * ld + (ci >> shift)] << shift | (ci & (2^shift - 1)).
+// table == nullptr: contiguous per-slot cache, row s * max_c + ci.
+struct KvPages {
+  const int* table;
+  int ld;
+  int shift;
+};
+
 // ------------------------------------------------------------ quant.cu
 cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t* q, int ldq, uint8_t* sf,
                          int k_tiles, cudaStream_t st);
@@ -76,8 +85,9 @@ struct AttnParams {
   const __nv_bfloat16* kv_step;     // this step's window rows [R, 512]
   const __nv_bfloat16* ring;        // [slots, W, 512]
   int W;
-  const __nv_bfloat16* comp;        // [slots, max_c, 512] or null
+  const __nv_bfloat16* comp;        // [slots, max_c, 512] or a paged pool, or null
   int max_c;
+  KvPages comp_pages;
   const int* slot;
   const int* pos;
   const int* chunk_start;           // first position of this step for the token's sequence
@@ -133,8 +143,9 @@ struct CompParams {
   float eps;
   const float* rope_cos;
   const float* rope_sin;
-  __nv_bfloat16* comp_out;          // [slots, max_c, dh]
+  __nv_bfloat16* comp_out;          // [slots, max_c, dh] or a paged pool (pages)
   int max_c;
+  KvPages pages;                    // rows of comp_out and idx_out
   const __nv_bfloat16* wk;          // indexer K projection [idx_dim, dh] (null = none)
   const __nv_bfloat16* k_norm_w;
   __nv_bfloat16* idx_out;           // [slots, max_c, idx_dim]
@@ -184,8 +195,9 @@ struct IdxParams {
   int T, n_heads, head_dim;
   const __nv_bfloat16* q;           // [T, n_heads, head_dim]
   const float* w;                   // [T, n_heads] (already bf16-rounded)
-  const __nv_bfloat16* kcache;      // [slots, max_c, head_dim]
+  const __nv_bfloat16* kcache;      // [slots, max_c, head_dim] or a paged pool (pages)
   int max_c;
+  KvPages pages;
   const int* slot;
   const int* clen;                  // [T] causal number of compressed entries
   int topk;
@@ -198,6 +210,7 @@ struct IdxParams {
   // tokens whose position does not close a group of ratio own_r read kcache_alt
   const __nv_bfloat16* kcache_alt;
   int alt_max_c;
+  KvPages alt_pages;
   const int* pos;
   const int* chunk_start;           // alt only applies to single-token (decode) chunks
   const int* last_pos;

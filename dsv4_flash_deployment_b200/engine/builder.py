@@ -21,7 +21,8 @@ def _pad_rows(w: torch.Tensor) -> torch.Tensor:
 
 def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
-                ep=None, tp=None, experts_from: DSV4Model | None = None) -> DSV4Model:
+                ep=None, tp=None, experts_from: DSV4Model | None = None, kv_block: int = 0,
+                kv_pool_tokens: int = 0) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -33,6 +34,9 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     wo_b columns, experts and head rows.  ``experts_from``: random init only; the
     layers reuse that model's expert blocks (a second layout of the same model on
     the same GPUs, e.g. tensor-parallel decode next to the expert-parallel batch).
+    ``kv_block``: entries per block of the paged compressed caches (0: one
+    contiguous ``max_seq_len`` cache per slot); ``kv_pool_tokens``: pool size in
+    tokens of context (0: ``n_slots * max_seq_len``).
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -76,7 +80,7 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
             tp.shard_layer(cfg, L)
         head = tp.shard_head(head, cfg.vocab_size)
     model = DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
-                      head_vocab=cfg.vocab_size, tp=tp)
+                      head_vocab=cfg.vocab_size, tp=tp, kv_block=kv_block, kv_pool_tokens=kv_pool_tokens)
     if cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
         model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed)

@@ -30,6 +30,8 @@ class EngineConfig:
     max_batched_tokens: int = 1024          # --max-num-batched-tokens
     chunk_size: int | None = None           # prefill chunk (default: the token budget)
     max_model_len: int = 16384
+    kv_block: int = 0                       # paged compressed caches: entries per block (0: per-slot caches)
+    kv_pool_tokens: int = 0                 # paged pool size in tokens of context (0: max_seqs * max_model_len)
     use_cuda_graphs: bool = True
     expert_storage_layers: int | None = None
     ep_transport: str = "nccl"              # "nccl" (baseline) or "p2p" (NVLink peer stores)

@@ -33,7 +33,8 @@ class Engine:
                  chunk_size: int | None = None, use_graphs: bool = True, eos_id: int | None = None):
         self.model = model
         self.cfg = model.cfg
-        self.sched = Scheduler(max_seqs, max_batched_tokens, max_seq_len, chunk_size)
+        self.sched = Scheduler(max_seqs, max_batched_tokens, max_seq_len, chunk_size,
+                               kv=getattr(model, "pager", None))
         self.use_graphs = use_graphs and model.dev.type == "cuda"
         self.graphs: dict = {}
         self.pinned: dict = {}
@@ -46,15 +47,18 @@ class Engine:
     def build(cls, cfg, device="cuda", max_seqs: int = 16, max_batched_tokens: int = 512, max_seq_len: int = 2048,
               weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None, ep=None,
               use_graphs: bool = True, chunk_size: int | None = None, extra_slots: int = 0, tp=None,
-              experts_from=None) -> "Engine":
+              experts_from=None, kv_block: int = 0, kv_pool_tokens: int = 0) -> "Engine":
         """``extra_slots`` cache slots beyond ``max_seqs`` are kept out of the scheduler
         (the multi-rank control plane runs its 1-token join steps on one).  ``tp``:
         tensor-parallel group (every rank runs the same steps).  ``experts_from``: a
-        model whose expert blocks this one shares (same expert ownership per rank)."""
+        model whose expert blocks this one shares (same expert ownership per rank).
+        ``kv_block`` / ``kv_pool_tokens``: paged compressed caches (admission then
+        also waits for free blocks)."""
         from .builder import build_model
         model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs + extra_slots,
                             max_seq_len=max_seq_len, weights=weights, seed=seed,
-                            expert_storage_layers=expert_storage_layers, ep=ep, tp=tp, experts_from=experts_from)
+                            expert_storage_layers=expert_storage_layers, ep=ep, tp=tp, experts_from=experts_from,
+                            kv_block=kv_block, kv_pool_tokens=kv_pool_tokens)
         return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs)
 
     # ------------------------------------------------------------------- API

@@ -7,6 +7,9 @@ step: every running sequence that has finished its prompt decodes one token;
 the remaining token budget goes to prompt chunks, oldest request first.  A
 request enters only when a cache slot is free (``max_seqs``) and its total
 length fits ``max_seq_len``.  Finished requests release their slot at once.
+With paged compressed caches (``kv``: models/kv_pages.py) admission also
+reserves every cache block the request can touch, oldest request first (a
+request that does not fit waits at the head of the queue); finishing releases them.
 """
 
 from __future__ import annotations
@@ -69,12 +72,14 @@ class SlotAllocator:
 
 
 class Scheduler:
-    def __init__(self, max_seqs: int, max_batched_tokens: int, max_seq_len: int, chunk_size: int | None = None):
+    def __init__(self, max_seqs: int, max_batched_tokens: int, max_seq_len: int, chunk_size: int | None = None,
+                 kv=None):
         self.max_seqs = max_seqs
         self.budget = max_batched_tokens
         self.max_seq_len = max_seq_len
         self.chunk = chunk_size or max_batched_tokens
         self.slots = SlotAllocator(max_seqs)
+        self.kv = kv                  # paged-cache reservations (fits / reserve / release) or None
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []
         self._ids = itertools.count()
@@ -84,6 +89,8 @@ class Scheduler:
             raise ValueError("empty prompt")
         if len(prompt) + max_new_tokens > self.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len {self.max_seq_len}")
+        if self.kv is not None and not self.kv.fits(len(prompt) + max_new_tokens):
+            raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds the paged cache pool")
         r = Request(next(self._ids), list(prompt), max_new_tokens, **kw)
         self.waiting.append(r)
         return r
@@ -114,8 +121,13 @@ class Scheduler:
                                           r.n_prefilled + n == len(r.prompt)))
                 budget -= n
         while budget > 0 and self.waiting and self.slots.n_free > 0:
-            r = self.waiting.popleft()
-            r.slot = self.slots.alloc()
+            r = self.waiting[0]
+            slot = self.slots.alloc()
+            if self.kv is not None and not self.kv.reserve(slot, len(r.prompt) + r.max_new_tokens):
+                self.slots.free.appendleft(slot)
+                break
+            self.waiting.popleft()
+            r.slot = slot
             self.running.append(r)
             n = min(self.chunk, budget, len(r.prompt))
             out.append(ScheduledChunk(r, 0, r.prompt[:n], n == len(r.prompt)))
@@ -150,6 +162,8 @@ class Scheduler:
         if r in self.running:
             self.running.remove(r)
         if r.slot >= 0:
+            if self.kv is not None:
+                self.kv.release(r.slot)
             self.slots.release(r.slot)
             r.slot = -1
 

@@ -106,7 +106,7 @@ class StepMeta:
 class DSV4Model:
     def __init__(self, cfg, layers: list[LayerW], embed: torch.Tensor, head: torch.Tensor, norm_w: torch.Tensor,
                  max_tokens: int, n_slots: int, max_seq_len: int, device, ep=None, max_sample: int | None = None,
-                 head_vocab: int | None = None, tp=None):
+                 head_vocab: int | None = None, tp=None, kv_block: int = 0, kv_pool_tokens: int = 0):
         self.cfg = cfg
         self.layers = layers
         self.dev = torch.device(device)
@@ -120,6 +120,10 @@ class DSV4Model:
         self.ep = ep
         self.tp = tp                          # tensor-parallel group (parallel/tp.py) or None
         self.max_sample = max_sample or max_tokens
+        self.pager = None                     # paged compressed caches (models/kv_pages.py) or None
+        if kv_block:
+            from .kv_pages import KvPager
+            self.pager = KvPager(cfg, self.dev, n_slots + 1, max_seq_len, kv_block, kv_pool_tokens)
         self.err = ErrorWord.get(self.dev)
         self.ext = _ext.load()
         self._alloc()
@@ -254,14 +258,19 @@ class DSV4Model:
             self.ring[l] = torch.zeros(S, cfg.sliding_window, cfg.head_dim, dtype=torch.bfloat16, device=dev)
         for l in cfg.kv_source_layer_ids:
             r, co = cfg.ratio(l), cfg.overlap(l)
-            max_c = max(1, self.max_seq_len // r)
-            self.comp[l] = torch.zeros(S, max_c, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            # contiguous: [slot, entry, dim]; paged: one pool [1, blocks * block, dim] per layer
+            shape = (S, max(1, self.max_seq_len // r)) if self.pager is None else (1, self.pager.rows(r))
+            self.comp[l] = torch.zeros(*shape, cfg.head_dim, dtype=torch.bfloat16, device=dev)
             if l in cfg.index_source_layer_ids:
-                self.idx_cache[l] = torch.zeros(S, max_c, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
+                self.idx_cache[l] = torch.zeros(*shape, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
             self.comp_ring[l] = torch.zeros(S, co * r, 2 * co * cfg.head_dim, dtype=torch.float32, device=dev)
         # order keys of the indexer scores, [T, widest index cache] (scoring CTAs -> select CTA)
-        kc = max([t.shape[1] for t in self.idx_cache.values()] or [1])
+        kc = max([max(1, self.max_seq_len // cfg.ratio(l)) for l in self.idx_cache] or [1])
         self.idx_keys = torch.empty(self.max_tokens, kc, dtype=torch.int32, device=dev)
+
+    def _pages(self, lid: int):
+        """Page descriptor of layer ``lid``'s compressed caches (None: contiguous)."""
+        return None if self.pager is None else self.pager.desc[self.cfg.ratio(lid)]
 
     def cache_bytes(self) -> int:
         tot = 0
@@ -288,6 +297,8 @@ class DSV4Model:
                 src = buf[: len(arr)]
             dst[: len(arr)].copy_(src, non_blocking=True)
 
+        if self.pager is not None:
+            self.pager.sync()
         put(self.m_ids, m.ids)
         put(self.m_pos, m.pos)
         put(self.m_slot, m.slot)
@@ -517,7 +528,7 @@ class DSV4Model:
         ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, ring, comp,
                       self.m_slot, self.m_pos, self.m_cstart, self.m_row0, comp_idx, comp_cnt, L.sink,
                       cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits,
-                      self.m_last if draft else None, win_len)
+                      self.m_last if draft else None, win_len, self._pages(src) if comp is not None else None)
         tctx.__exit__(None, None, None)
         if draft:
             pass
@@ -557,7 +568,8 @@ class DSV4Model:
             with self._t("comp_pool"):
                 ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
                                   self.comp_ring[lid], L.comp_norm, cfg.rms_norm_eps, cos, sin, self.comp[lid],
-                                  L.idx_wk, L.idx_knorm, self.idx_cache.get(lid) if L.idx_wk is not None else None)
+                                  L.idx_wk, L.idx_knorm, self.idx_cache.get(lid) if L.idx_wk is not None else None,
+                                  self._pages(lid))
         if self._defer:
             self._pending("proj", lid, proj, T)
         else:
@@ -590,7 +602,7 @@ class DSV4Model:
                          self.comp_idx, self.comp_cnt, self.cand if cand_mode else None, cand_mode,
                          cfg.candidate_block_size, cfg.candidate_topk_blocks, T, self.err,
                          self.idx_cache[alt] if alt is not None else None, self.m_pos, self.m_cstart, self.m_last, r,
-                         self.idx_keys)
+                         self.idx_keys, self._pages(src), self._pages(alt) if alt is not None else None)
         tk.__exit__(None, None, None)
 
     def _k_alt(self, lid: int) -> int | None:

@@ -1,5 +1,5 @@
-"""The native host library (plain C++, no CUDA): bulk file reads, Engram hashing
-and row gathers.  Built in-tree with g++ into ``_build/libdsv4_host.so`` and
+"""The native host library (plain C++, no CUDA): bulk file reads, Engram hashing,
+row gathers and the paged-cache block allocator.  Built in-tree with g++ into ``_build/libdsv4_host.so`` and
 bound with ctypes; :func:`lib` builds it on first use when the file is missing.
 """
 
@@ -49,6 +49,7 @@ def lib() -> ctypes.CDLL:
                                           ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
             L.dsv4_pread_many.restype = ctypes.c_int
             _declare_engram(L)
+            _declare_kv(L)
             _lib = L
     return _lib
 
@@ -61,6 +62,63 @@ def _declare_engram(L) -> None:
     L.dsv4_gather_rows.restype = ctypes.c_int
     L.dsv4_fill_random.argtypes = [vp, i64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     L.dsv4_fill_random.restype = ctypes.c_int
+
+
+def _declare_kv(L) -> None:
+    vp, c_int = ctypes.c_void_p, ctypes.c_int
+    L.dsv4_kv_create.argtypes = [c_int, c_int, c_int]
+    L.dsv4_kv_create.restype = vp
+    L.dsv4_kv_destroy.argtypes = [vp]
+    L.dsv4_kv_destroy.restype = None
+    L.dsv4_kv_free_blocks.argtypes = [vp]
+    L.dsv4_kv_free_blocks.restype = c_int
+    L.dsv4_kv_slot_blocks.argtypes = [vp, c_int]
+    L.dsv4_kv_slot_blocks.restype = c_int
+    L.dsv4_kv_reserve.argtypes = [vp, c_int, c_int]
+    L.dsv4_kv_reserve.restype = c_int
+    L.dsv4_kv_release.argtypes = [vp, c_int]
+    L.dsv4_kv_release.restype = None
+    L.dsv4_kv_row.argtypes = [vp, c_int, vp]
+    L.dsv4_kv_row.restype = None
+
+
+class KvBlockAllocator:
+    """Block pool + per-slot block table of one compression ratio (native,
+    ``csrc/host/kv_blocks.cpp``)."""
+
+    def __init__(self, n_blocks: int, n_slots: int, max_per_slot: int):
+        self._L = lib()
+        self._h = self._L.dsv4_kv_create(n_blocks, n_slots, max_per_slot)
+        if not self._h:
+            raise ValueError("invalid block allocator shape")
+        self.n_blocks, self.n_slots, self.max_per_slot = n_blocks, n_slots, max_per_slot
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._L.dsv4_kv_destroy(h)
+            self._h = None
+
+    @property
+    def free_blocks(self) -> int:
+        return self._L.dsv4_kv_free_blocks(self._h)
+
+    def slot_blocks(self, slot: int) -> int:
+        return self._L.dsv4_kv_slot_blocks(self._h, slot)
+
+    def reserve(self, slot: int, n_blocks: int) -> bool:
+        """Grows ``slot`` to ``n_blocks`` blocks; False (nothing changed) when they do not fit."""
+        return self._L.dsv4_kv_reserve(self._h, slot, n_blocks) == 0
+
+    def release(self, slot: int) -> None:
+        self._L.dsv4_kv_release(self._h, slot)
+
+    def row(self, slot: int):
+        """The slot's block ids (int32 numpy, -1 = unmapped)."""
+        import numpy as np
+        out = np.empty(self.max_per_slot, dtype=np.int32)
+        self._L.dsv4_kv_row(self._h, slot, out.ctypes.data)
+        return out
 
 
 def fill_random(t, seed: int, mode: int, lo: int = 118, threads: int = 32) -> None:

@@ -37,7 +37,7 @@ def _run(q, w, kc, slot, clen, topk, cand=None, cand_mode=0, cand_block=1, cand_
     cnt = torch.zeros(T, dtype=torch.int32, device=dev)
     keys = torch.empty(T, kc.shape[1], dtype=torch.int32, device=dev)
     ext.indexer_topk(q, w, kc, slot, clen, topk, idx, cnt, cand, cand_mode, cand_block, cand_topk, T,
-                     ErrorWord.get(dev), None, None, None, None, 1, keys)
+                     ErrorWord.get(dev), None, None, None, None, 1, keys, None, None)
     torch.cuda.synchronize()
     ErrorWord.check(dev)
     return idx.cpu(), cnt.cpu()

@@ -1,0 +1,92 @@
+"""Paged compressed caches, host side: the native block allocator, the per-ratio
+block tables and reservation-based admission in the scheduler (CPU only)."""
+
+import numpy as np
+import pytest
+
+from dsv4_flash_deployment_b200.config import v4_flash_config
+from dsv4_flash_deployment_b200.engine.scheduler import Scheduler
+from dsv4_flash_deployment_b200.models.kv_pages import KvPager
+from dsv4_flash_deployment_b200.ops.host import KvBlockAllocator
+
+
+def test_block_allocator_reserve_grow_release():
+    a = KvBlockAllocator(n_blocks=6, n_slots=3, max_per_slot=4)
+    assert a.free_blocks == 6
+    assert a.reserve(0, 3)
+    assert list(a.row(0)) == [0, 1, 2, -1]
+    assert a.reserve(0, 4)                     # grow keeps the mapped prefix
+    assert list(a.row(0)[:3]) == [0, 1, 2] and a.slot_blocks(0) == 4
+    assert not a.reserve(1, 3)                 # only 2 left: refused, nothing changed
+    assert a.free_blocks == 2 and a.slot_blocks(1) == 0
+    assert not a.reserve(2, 5)                 # beyond the table row
+    a.release(0)
+    assert a.free_blocks == 6 and list(a.row(0)) == [-1] * 4
+    assert a.reserve(1, 4)
+    assert sorted(a.row(1)) == [0, 1, 2, 3]    # released blocks are handed out again
+    with pytest.raises(ValueError):
+        KvBlockAllocator(0, 1, 1)
+
+
+def _pager(pool_tokens, max_seq=1024, block=16, slots=2):
+    cfg = v4_flash_config()                    # ratios 4 and 128
+    return cfg, KvPager(cfg, "cpu", slots + 1, max_seq, block, pool_tokens)
+
+
+def test_pager_geometry_and_tables():
+    cfg, pg = _pager(pool_tokens=1024)
+    assert pg.ratios == [4, 128]
+    assert pg.max_c == {4: 256, 128: 8}
+    assert pg.n_blocks == {4: 16, 128: 1}
+    assert pg.rows(4) == 17 * 16               # + the scratch block
+    # descriptor: table address, ld, shift, logical capacity
+    d4 = pg.desc[4].tolist()
+    assert d4[0] == pg.table[4].data_ptr() and d4[1:] == [16, 4, 256]
+    # unmapped entries point at the scratch block
+    assert (pg.host[4] == 16).all() and (pg.host[128] == 1).all()
+    assert pg.reserve(1, 700)                  # 176 entries of ratio 4 -> 11 blocks; 6 of ratio 128 -> 1
+    assert (pg.host[4][1, :11] == np.arange(11)).all() and (pg.host[4][1, 11:] == 16).all()
+    assert pg.host[128][1, 0] == 0
+    pg.sync()
+    assert (pg.table[4].numpy() == pg.host[4]).all()
+    assert not pg.reserve(0, 500)              # ratio 128 has no block left: all or nothing
+    assert pg.free_blocks() == {4: 5, 128: 0}
+    pg.release(1)
+    pg.sync()
+    assert pg.free_blocks() == {4: 16, 128: 1} and (pg.table[4].numpy() == 16).all()
+    with pytest.raises(ValueError):
+        KvPager(cfg, "cpu", 3, 1024, 12)       # block size must be a power of two
+
+
+def _finish_prompt_and_decode(s, steps):
+    out = []
+    for _ in range(steps):
+        chunks = s.schedule()
+        out.append([(c.req.req_id, len(c.tokens)) for c in chunks])
+        s.commit(chunks, [7] * sum(c.sample for c in chunks))
+    return out
+
+
+def test_scheduler_admission_waits_for_blocks():
+    _, pg = _pager(pool_tokens=1024)
+    s = Scheduler(max_seqs=2, max_batched_tokens=1024, max_seq_len=1024, kv=pg)
+    a = s.add(list(range(600)), 3, ignore_eos=True)
+    b = s.add(list(range(400)), 3, ignore_eos=True)
+    first = s.schedule()
+    # b has a free slot but not enough blocks: it waits at the head of the queue
+    assert [c.req for c in first] == [a] and b.slot < 0 and s.slots.n_free == 1
+    s.commit(first, [7])
+    while not a.finished:
+        s.commit(s.schedule(), [7])
+    assert pg.free_blocks() == {4: 16, 128: 1}
+    nxt = s.schedule()
+    assert [c.req for c in nxt] == [b] and b.slot >= 0
+    assert pg.alloc[4].slot_blocks(b.slot) == -(-(403 // 4 + 1) // 16)
+
+
+def test_scheduler_rejects_requests_larger_than_the_pool():
+    _, pg = _pager(pool_tokens=512)
+    s = Scheduler(max_seqs=2, max_batched_tokens=256, max_seq_len=1024, kv=pg)
+    with pytest.raises(ValueError, match="paged cache pool"):
+        s.add(list(range(900)), 10)
+    s.add(list(range(300)), 10)                # fits
