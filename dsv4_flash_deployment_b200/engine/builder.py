@@ -41,8 +41,6 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     dev = torch.device(device)
     if tp is not None and ep is not None:
         raise ValueError("tensor parallelism owns the experts itself; pass tp or ep, not both")
-    if tp is not None and (cfg.engram_layer_ids or cfg.n_mtp_layers):
-        raise NotImplementedError("tensor-parallel layout: V4 backbone without Engram / MTP stages")
     par = ep if ep is not None else tp
     e_begin, e_local = 0, cfg.n_routed_experts
     if par is not None:

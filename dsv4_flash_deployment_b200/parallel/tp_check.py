@@ -1,7 +1,8 @@
 """Tensor-parallel self-check and decode timing (run under torchrun, one rank per GPU).
 
-Every rank builds the same small V4-shaped model (same checkpoint tensors)
-twice: whole on its GPU (the reference) and tensor-parallel over all ranks.
+Every rank builds the same small V4-shaped model (or, with ``--family v41``, a
+V4.1-shaped one: ratio-2/1 compressors, reference index mode, MXFP4 experts and
+Engram layers, which every rank computes whole) twice: whole on its GPU (the reference) and tensor-parallel over all ranks.
 All ranks step the same sequences; the tensor-parallel next tokens must match
 the local model's and each rank's logits shard must match the same rows of the
 local model's logits.  Then a one-token decode step is timed on the device
@@ -27,6 +28,24 @@ def small_cfg(n_layers: int = 3):
     from .ep_check import small_cfg as cfg_of
 
     return cfg_of(n_layers)
+
+
+def small_v41_cfg():
+    """V4.1 structure at kernel dimensions (64 x 512 heads, 128-wide indexer heads):
+    ratio-2 and ratio-1 kv sources, a candidate-block source, reference index mode,
+    MXFP4 experts and two Engram layers with small tables."""
+    from ..config import ModelConfig
+
+    return ModelConfig(
+        name="tp-check-v41", family="v4.1", vocab_size=1024, padded_vocab_size=1024, dim=1024, n_layers=6,
+        n_mtp_layers=0, n_heads=64, head_dim=512, qk_rope_head_dim=64, q_lora_rank=256, o_lora_rank=128,
+        o_groups=8, sliding_window=16, compress_ratios=(0, 2, 2, 1, 1, 1), kv_source_layer_ids=(1, 3),
+        index_source_layer_ids=(1, 3, 4), candidate_source_layer_id=3, candidate_topk_blocks=4,
+        candidate_block_size=4, index_n_heads=8, index_head_dim=128, index_topk=8, n_routed_experts=32,
+        n_activated_experts=6, n_shared_experts=1, moe_inter_dim=512, expert_format="mxfp4",
+        engram_layer_ids=(1, 3), engram_max_ngram_size=4, engram_n_heads=8, engram_head_dim=64,
+        engram_vocab_size=2048, engram_num_embeddings=(51342, 54000), dspark_target_layer_ids=(),
+        index_k_mode="reference")
 
 
 def _meta(cfg, step: int, n_seq: int, plen: int):
@@ -80,6 +99,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=30)
     ap.add_argument("--moe", default="ep", choices=["ep", "tp"],
                     help="experts owned whole by one rank (ep) or split by intermediate index over all ranks (tp)")
+    ap.add_argument("--family", default="v4", choices=["v4", "v41"])
     a = ap.parse_args(argv)
 
     from ..engine.builder import build_model
@@ -93,7 +113,7 @@ def main(argv=None):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    cfg = small_cfg()
+    cfg = small_cfg() if a.family == "v4" else small_v41_cfg()
     w = make_random_weights(cfg, seed=11, include_mtp=False)
     ref = build_model(cfg, dev, max_tokens=256, n_slots=a.seqs + 1, max_seq_len=256, weights=w)
     tp = TPGroup(rank, world, dist.group.WORLD, dev, moe=a.moe)
@@ -149,7 +169,7 @@ def main(argv=None):
     serve_ok = torch.tensor([0 if rank != 0 or served == local else 1], device=dev)
     dist.all_reduce(serve_ok)
     flag += serve_ok
-    res = {"world": world, "moe_split": a.moe, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
+    res = {"world": world, "family": a.family, "moe_split": a.moe, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
            "served_matches_one_gpu": bool(serve_ok.item() == 0),
            "decode_ms_graph": round(ms_graph, 4), "decode_ms_eager": round(ms_eager, 4),
            "decode_ms_one_gpu_graph": round(ms_one, 4), "layers": cfg.n_layers}

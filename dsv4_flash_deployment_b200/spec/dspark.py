@@ -69,6 +69,8 @@ class DSparkDrafter:
         cfg = model.cfg
         if cfg.n_mtp_layers < 1 or not cfg.dspark_target_layer_ids:
             raise ValueError("config has no DSpark stages")
+        if getattr(model, "tp", None) is not None:
+            raise NotImplementedError("DSpark drafting runs on a whole (not tensor-parallel) backbone")
         self.m, self.cfg, dev = model, cfg, model.dev
         self.ext = model.ext
         self.blk = cfg.dspark_block_size
