@@ -10,7 +10,10 @@ Engram at layers 1 and 14 with its tables in page-locked host memory):
   device-timed (max over ranks);
 * C=1 TPOT: one sequence, 1-token steps through ``Engine.run_meta`` (pinned
   H2D + D2H + host sync every token), graph replay (reference megakernel
-  9.18 ms, ``MK/results/megakernel_v6e16_results.json:685``);
+  9.18 ms, ``MK/results/megakernel_v6e16_results.json:685``); on N > 1 GPUs
+  on the tensor-parallel layout (heads, ``wo_a`` groups, ``wo_b`` columns and
+  head rows split over the ranks, the batch model's expert blocks and Engram
+  runtime shared), with the batch layout's value beside it;
 * C=1 effective TPOT with DSpark 1+4 (single GPU): draft (3 MTP stages +
   Markov chain) + verify (5 tokens through the target) + ring commit + ingest
   per round, with the reference's forced-acceptance knob (random weights
@@ -68,6 +71,7 @@ def main(argv=None) -> None:
     ap.add_argument("--force-accept", type=int, default=4)
     ap.add_argument("--no-spec", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel C=1 measurement")
     a = ap.parse_args(argv)
 
     from ..config import v41_flash_config
@@ -97,7 +101,8 @@ def main(argv=None) -> None:
     # the DSpark stages' expert blocks (3 x 128 experts) come out of the reserve
     spec_gb = 0 if a.no_spec else cfg.n_mtp_layers * expert_block_bytes(
         dataclasses.replace(cfg, n_routed_experts=cfg.dspark_n_routed_experts), 1) / 2 ** 30
-    n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world, reserve_gb=12.0 + spec_gb)
+    tp_gb = 8.0 if world > 1 and not a.no_tp else 0.0      # the tensor-parallel C=1 model's dense shards
+    n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world, reserve_gb=12.0 + spec_gb + tp_gb)
     t_build = time.perf_counter()
     eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
                        expert_storage_layers=n_phys, ep=ep, use_graphs=not a.no_graphs, chunk_size=chunk)
@@ -142,6 +147,30 @@ def main(argv=None) -> None:
         dist.barrier()
     c1_dev, c1_wall = _timed(eng.stream, lambda i: eng.run_meta(c1m[i]), len(c1m))
     eng.check_errors()
+
+    # -------------------------------------------- C=1 tensor parallel (N > 1)
+    c1_tp = None
+    if world > 1 and not a.no_tp:
+        from ..parallel.tp import TPGroup
+        tpg = TPGroup(rank, world, group, dev, moe="ep")
+        eng_tp = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=16, max_seq_len=max_seq, tp=tpg,
+                              experts_from=model, engram_from=model, use_graphs=not a.no_graphs, chunk_size=16)
+        rng_tp = np.random.default_rng(4321)   # the same tokens on every rank
+        tpm = [StepMeta(cfg, [SeqChunk(0, c1_pos + i, [int(rng_tp.integers(0, cfg.vocab_size))], True)])
+               for i in range(3 + len(c1m))]
+        for i in range(3):
+            eng_tp.run_meta(tpm[i])
+        eng_tp.check_errors()
+        dist.barrier()
+        tp_dev, tp_wall = _timed(eng_tp.stream, lambda i: eng_tp.run_meta(tpm[3 + i]), len(c1m))
+        eng_tp.check_errors()
+        tp_t = torch.tensor([tp_dev, tp_wall], device=dev)
+        dist.all_reduce(tp_t, op=dist.ReduceOp.MAX)
+        c1_tp = tuple(float(x) for x in tp_t.tolist())
+        eng_tp.graphs.clear()
+        del eng_tp
+        tpg.release()
+        dist.barrier()
 
     # ------------------------------------------------ C=1 DSpark 1+4 (1 GPU)
     spec = None
@@ -190,8 +219,11 @@ def main(argv=None) -> None:
                        "engram": {"rows_per_table": a.engram_rows, "tables_gb_pinned_host": round(tables_gb, 1),
                                   "note": "reference tables 2 x ~101 GB exceed the 196 GB host RAM of the GPU box"},
                        "build_s": round(t_build, 1)},
-            "c1_tpot_ms": {"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,
-                           "baseline_ms": MK_TPOT},
+            "c1_tpot_ms": ({"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,
+                            "layout": "single GPU", "baseline_ms": MK_TPOT} if c1_tp is None else
+                           {"value": round(c1_tp[1], 3), "device_ms": round(c1_tp[0], 3), "context": c1_pos,
+                            "layout": f"tp{world} attention + ep{world} experts, Engram whole on every rank",
+                            "batch_layout_ms": round(c1_wall, 3), "baseline_ms": MK_TPOT}),
             "dspark": spec,
         }
         print(json.dumps(line), flush=True)

@@ -22,7 +22,7 @@ def _pad_rows(w: torch.Tensor) -> torch.Tensor:
 def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
                 ep=None, tp=None, experts_from: DSV4Model | None = None, kv_block: int = 0,
-                kv_pool_tokens: int = 0) -> DSV4Model:
+                kv_pool_tokens: int = 0, engram_from: DSV4Model | None = None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -36,7 +36,10 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     the same GPUs, e.g. tensor-parallel decode next to the expert-parallel batch).
     ``kv_block``: entries per block of the paged compressed caches (0: one
     contiguous ``max_seq_len`` cache per slot); ``kv_pool_tokens``: pool size in
-    tokens of context (0: ``n_slots * max_seq_len``).
+    tokens of context (0: ``n_slots * max_seq_len``).  ``engram_from``: a model
+    whose Engram runtime (host tables, token rings, staging buffers) this one
+    uses instead of building its own; it must have at least as many slots and
+    step tokens, and the two models must not step concurrently.
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -79,7 +82,12 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
         head = tp.shard_head(head, cfg.vocab_size)
     model = DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
                       head_vocab=cfg.vocab_size, tp=tp, kv_block=kv_block, kv_pool_tokens=kv_pool_tokens)
-    if cfg.engram_layer_ids:
+    if cfg.engram_layer_ids and engram_from is not None:
+        eg = engram_from.engram
+        if eg is None or eg.ring.shape[0] < n_slots or eg.rows.shape[0] < max_tokens:
+            raise ValueError("engram_from: runtime missing or smaller than this model's slots / step tokens")
+        model.engram = eg
+    elif cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
         model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed)
     return model
