@@ -230,6 +230,14 @@ class SpecEngine:
             raise ValueError("too many sequences for the drafter's buffers")
         self.slots = list(range(len(prompts)))
         self.outs = [[] for _ in prompts]
+        pg = getattr(m, "pager", None)
+        if pg is not None:
+            # paged compressed caches: each sequence holds blocks for the whole context
+            for s in range(pg.n_slots - 1):      # the speculative engine owns every slot of the model
+                pg.release(s)
+            for s in self.slots:
+                if not pg.reserve(s, m.max_seq_len):
+                    raise ValueError("paged cache pool too small for the speculative sequences")
         for j, p in enumerate(prompts):
             for c0 in range(0, len(p), m.max_tokens):
                 piece = p[c0:c0 + m.max_tokens]
