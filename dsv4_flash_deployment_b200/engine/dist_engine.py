@@ -149,6 +149,9 @@ class DistributedEngine:
         if len(prompt) + max_new_tokens > self.local.sched.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.local.sched.max_seq_len}")
+        kv = getattr(self.local.sched, "kv", None)
+        if kv is not None and not kv.fits(len(prompt) + max_new_tokens):
+            raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds the paged cache pool")
         r = -1 if self.replicated else min(range(self.world), key=lambda i: self.load[i])
         g = GlobalRequest(self.next_id, r, list(prompt), max_new_tokens)
         g._opts = (bool(ignore_eos), tuple(stop_ids))
