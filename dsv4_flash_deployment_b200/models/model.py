@@ -530,11 +530,10 @@ class DSV4Model:
                       cfg.head_dim ** -0.5, self.o, self.attn_ws if splits > 1 else None, T, splits,
                       self.m_last if draft else None, win_len, self._pages(src) if comp is not None else None)
         tctx.__exit__(None, None, None)
-        if draft:
-            pass
-        elif self._defer:
+        # draft blocks read the window but leave the ring alone (the verify step writes it)
+        if not draft and self._defer:
             self._pending("kv", lid, self.kv_step, T)
-        else:
+        elif not draft:
             with self._t("ring_update"):
                 ext.ring_update(ring, self.kv_step, T, self.m_slot, self.m_pos, self.m_last)
         groups = cfg.o_groups if self.tp is None else self.tp.groups(cfg.o_groups)
