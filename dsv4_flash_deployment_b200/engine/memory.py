@@ -20,7 +20,10 @@ def expert_block_bytes(cfg, ep_world: int = 1) -> int:
     return int(e_local * per * (1 + 1 / 32))
 
 
-def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int) -> int:
+def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int, kv_block: int = 0,
+                     kv_pool_tokens: int = 0) -> int:
+    """``kv_block`` > 0: the compressed caches are paged pools of ``kv_pool_tokens``
+    tokens of context (0: ``n_slots * max_seq``) plus one scratch block per ratio."""
     d = cfg.dim
     per_layer = ((cfg.q_lora_rank + cfg.head_dim) * d + cfg.q_dim * cfg.q_lora_rank + 2 * cfg.o_inter * cfg.o_group_in
                  + d * cfg.o_inter + 3 * d * cfg.n_shared_experts * cfg.moe_inter_dim
@@ -35,9 +38,14 @@ def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int) -> int:
     kv = cfg.n_layers * s * cfg.sliding_window * cfg.head_dim * 2
     for l in cfg.kv_source_layer_ids:
         r, co = cfg.ratio(l), cfg.overlap(l)
-        kv += s * (max_seq // r) * cfg.head_dim * 2 + s * co * r * 2 * co * cfg.head_dim * 4
+        if kv_block:
+            pool = kv_pool_tokens or n_slots * max_seq
+            rows = (-(-max(1, pool // r) // kv_block) + 1) * kv_block
+        else:
+            rows = s * (max_seq // r)
+        kv += rows * cfg.head_dim * 2 + s * co * r * 2 * co * cfg.head_dim * 4
         if l in cfg.index_source_layer_ids:
-            kv += s * (max_seq // r) * cfg.index_head_dim * 2
+            kv += rows * cfg.index_head_dim * 2
     t = max_tokens
     k = cfg.n_activated_experts
     cap = t * k * 2 + cfg.n_routed_experts * 128

@@ -90,3 +90,15 @@ def test_scheduler_rejects_requests_larger_than_the_pool():
     with pytest.raises(ValueError, match="paged cache pool"):
         s.add(list(range(900)), 10)
     s.add(list(range(300)), 10)                # fits
+
+
+def test_memory_estimate_counts_the_paged_pool():
+    from dsv4_flash_deployment_b200.engine.memory import non_expert_bytes
+
+    cfg = v4_flash_config()
+    full = non_expert_bytes(cfg, 512, 512, 16384)
+    paged_same = non_expert_bytes(cfg, 512, 512, 16384, kv_block=64)
+    paged_small = non_expert_bytes(cfg, 512, 512, 16384, kv_block=64, kv_pool_tokens=512 * 2048)
+    # same capacity: the pools only add the scratch blocks (and drop the padding slot)
+    assert abs(paged_same - full) < 0.01 * full
+    assert paged_small < full - 10 * 2 ** 30   # 2k instead of 16k tokens per sequence
