@@ -173,3 +173,39 @@ def test_client_smoke_and_determinism(served):
     s, d = _run(st, go)
     assert s["ok"], s
     assert d["ok"] and d["n"] == 6, d
+
+
+def test_eval_client_scores_and_resumes(served, tmp_path):
+    from dsv4_flash_deployment_b200.bench import evals
+
+    st, _ = served
+    mc = [{"question": f"q{i}", "choices": ["w", "x", "y", "z"], "answer": "C"} for i in range(4)]
+    math = [{"question": f"{i}+1", "answer": f"work #### {i + 1}"} for i in range(3)]
+    part = str(tmp_path / "mc.partial.jsonl")
+
+    async def go(c):
+        base = str(c.make_url("")).rstrip("/")
+        a = await evals.run_eval("mc", base, "toy", mc, 4, 0.0, 2, part, seed=1, template="{question} {options}")
+        b = await evals.run_eval("mc", base, "toy", mc, 4, 0.0, 2, part, seed=1, template="{question} {options}")
+        m = await evals.run_eval("math", base, "toy", math, 4, 0.0, 3, None, template="{question}=")
+        return a, b, m
+    a, b, m = _run(st, go)
+    assert a["n"] == 4 and a["errors"] == 0 and a["resumed"] == 0 and a["verdict"]["complete"]
+    assert b["n"] == 4 and b["resumed"] == 4           # every item came from the partial file
+    assert sum(1 for _ in open(part)) == 4
+    assert m["n"] == 3 and m["errors"] == 0
+
+
+def test_eval_parsing_and_shuffle():
+    from dsv4_flash_deployment_b200.bench import evals
+
+    item = {"question": "Q", "choices": ["right", "a", "b", "c"], "answer": 0}
+    p1, t1 = evals.mc_prompt(item, 5, 0)
+    p2, t2 = evals.mc_prompt(item, 5, 0)
+    assert (p1, t1) == (p2, t2)                        # seeded per (seed, item)
+    assert f"{t1}) right" in p1
+    assert evals.extract_letter("so...\nAnswer: (b)\n") == "B"
+    assert evals.extract_letter("Answer: A then Answer: **D**") == "D"
+    assert evals.extract_letter("no letter") is None
+    assert evals.math_target({"answer": "steps #### 1,234"}) == 1234.0
+    assert evals._number("the result is -3.5.") == -3.5
