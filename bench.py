@@ -167,6 +167,7 @@ def main() -> None:
     from dsv4_flash_deployment_b200.models.model import SeqChunk, StepMeta
     from dsv4_flash_deployment_b200.ops import _ext
     from dsv4_flash_deployment_b200.parallel import ep as ep_mod
+    from dsv4_flash_deployment_b200.utils.provenance import provenance
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -196,8 +197,10 @@ def main() -> None:
     max_seq = isl + osl
     ep = ep_mod.EPGroup(rank, world, group, dev, transport=args.ep_transport) if world > 1 else None
     n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world)
+    t_build = time.perf_counter()
     eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
                        expert_storage_layers=n_phys, ep=ep, use_graphs=not args.no_graphs, chunk_size=chunk_rank)
+    t_build = time.perf_counter() - t_build     # cold start: weights drawn on the device, buffers, peers
     model = eng.model
     rng = np.random.default_rng(1234 + rank)
 
@@ -419,6 +422,8 @@ def main() -> None:
                             "note": "one sequence, the same 1-token step on every rank through Engine.run_meta "
                                     "(pinned H2D + D2H + sync each token), graph replay, max over ranks"}),
             "clocks": clk.summary(),
+            "build_s": round(t_build, 1),
+            "hardware": provenance(dev),
         }
         print(json.dumps(line), flush=True)
     if group is not None:

@@ -79,6 +79,7 @@ def main(argv=None) -> None:
     from ..engine.memory import expert_block_bytes, plan_expert_storage
     from ..models.model import SeqChunk, StepMeta
     from ..parallel import ep as ep_mod
+    from ..utils.provenance import provenance
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -225,6 +226,7 @@ def main(argv=None) -> None:
                             "layout": f"tp{world} attention + ep{world} experts, Engram whole on every rank",
                             "batch_layout_ms": round(c1_wall, 3), "baseline_ms": MK_TPOT}),
             "dspark": spec,
+            "hardware": provenance(dev),
         }
         print(json.dumps(line), flush=True)
     eng.graphs.clear()
