@@ -697,6 +697,14 @@ void tp_argmax_merge(const Tensor& sync, const Tensor& peer_val, const Tensor& p
 
 }  // namespace
 
+int64_t debug_bounds_attach(const Tensor& err) {
+  TORCH_CHECK(err.is_cuda() && err.numel() >= 1 && err.element_size() == 4, "error word: int32 CUDA tensor");
+  c10::cuda::CUDAGuard g(err.device());
+  const int n = dsv4::dbg_bounds_attach(reinterpret_cast<uint32_t*>(err.data_ptr()));
+  TORCH_CHECK(n >= 0, "debug bounds attach failed: ", cudaGetErrorString((cudaError_t)(-n)));
+  return n;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "DeepSeek-V4 B200 kernels (sm_100a)";
   m.def("gemm", &gemm);
@@ -708,6 +716,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("hc_finish", &hc_finish);
   m.def("hc_num_slices", [](int64_t d) { return (int64_t)dsv4::hc_num_slices((int)d); });
   m.def("attention", &attention);
+  m.def("debug_bounds_attach", &debug_bounds_attach);
+#ifdef DSV4_DEBUG_BOUNDS
+  m.attr("debug_bounds") = true;
+#else
+  m.attr("debug_bounds") = false;
+#endif
   m.def("attn_smem", []() { return (int64_t)dsv4::attn_smem_bytes(); });
   m.def("qkv_post", &qkv_post);
   m.def("idx_q_prep", &idx_q_prep);

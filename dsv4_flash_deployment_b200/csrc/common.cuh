@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include <utility>
+#include <vector>
 
 #include "kernels.h"
 
@@ -25,11 +26,6 @@
 
 namespace dsv4 {
 
-// Row of compressed entry ci of sequence slot `slot` in a (paged or contiguous) cache.
-DSV4_DEV size_t kv_row(const KvPages& pg, int slot, int ci, int max_c) {
-  if (pg.table == nullptr) return (size_t)slot * max_c + ci;
-  return ((size_t)pg.table[(size_t)slot * pg.ld + (ci >> pg.shift)] << pg.shift) + (ci & ((1 << pg.shift) - 1));
-}
 
 // ------------------------------------------------------------------ errors
 // Error word layout: bits [0,8) code, [8,16) kernel id, [16,32) detail.
@@ -47,10 +43,60 @@ enum KernelId : uint32_t {
   KID_MOE = 3,
   KID_COMM = 4,
   KID_MEGA = 5,
+  KID_BOUNDS = 6,   // debug-bounds build: an index check failed (detail = site)
 };
 
 DSV4_DEV void report_error(uint32_t* err, uint32_t code, uint32_t kid, uint32_t detail) {
   if (err) atomicCAS(err, 0u, code | (kid << 8) | (detail << 16));
+}
+
+// ------------------------------------------------------------ debug bounds
+// Compiled with -DDSV4_DEBUG_BOUNDS (the separate debug extension, built when
+// DSV4_DEBUG_BOUNDS=1), cache gathers and writes check their indices: a bad
+// one is recorded as ERR_BAD_ARG / KID_BOUNDS in the device error word and the
+// access goes to row 0 of the same buffer instead, so the kernel completes and
+// the host raises on its next check.  Every translation unit has its own copy
+// of the error-word pointer; dbg_bounds_attach() (misc.cu) sets all of them
+// for the current device.  In the default build all of this compiles away.
+enum BoundsSite : uint32_t {
+  BS_KV_ENTRY = 1,      // compressed entry index outside [0, max_c) or a negative slot
+  BS_KV_UNMAPPED = 2,   // paged cache: the entry's block is not mapped (table entry < 0)
+};
+
+using DbgSetter = cudaError_t (*)(uint32_t*);
+std::vector<DbgSetter>& dbg_registry();   // misc.cu
+
+#ifdef DSV4_DEBUG_BOUNDS
+static __device__ uint32_t* dsv4_dbg_err;
+
+DSV4_DEV void dbg_bad(uint32_t site) { report_error(dsv4_dbg_err, ERR_BAD_ARG, KID_BOUNDS, site); }
+
+namespace {
+cudaError_t dbg_set_this_unit(uint32_t* p) { return cudaMemcpyToSymbol(dsv4_dbg_err, &p, sizeof(p)); }
+struct DbgRegistrar {
+  DbgRegistrar() { dbg_registry().push_back(&dbg_set_this_unit); }
+};
+DbgRegistrar dbg_registrar_instance;
+}  // namespace
+#endif
+
+// Row of compressed entry ci of sequence slot `slot` in a (paged or contiguous) cache.
+DSV4_DEV size_t kv_row(const KvPages& pg, int slot, int ci, int max_c) {
+#ifdef DSV4_DEBUG_BOUNDS
+  if (ci < 0 || ci >= max_c || slot < 0) {
+    dbg_bad(BS_KV_ENTRY);
+    return 0;
+  }
+#endif
+  if (pg.table == nullptr) return (size_t)slot * max_c + ci;
+  const int blk = pg.table[(size_t)slot * pg.ld + (ci >> pg.shift)];
+#ifdef DSV4_DEBUG_BOUNDS
+  if (blk < 0) {
+    dbg_bad(BS_KV_UNMAPPED);
+    return 0;
+  }
+#endif
+  return ((size_t)blk << pg.shift) + (ci & ((1 << pg.shift) - 1));
 }
 
 DSV4_DEV uint64_t globaltimer_ns() {

@@ -17,6 +17,12 @@ struct KvPages {
   int shift;
 };
 
+// ------------------------------------------------------------ misc.cu (debug bounds)
+// Points every translation unit's debug-bounds error pointer at `err` (current
+// device).  Returns the number of units set (0 in the default build, which has
+// no checks), or -cudaError on failure.
+int dbg_bounds_attach(uint32_t* err);
+
 // ------------------------------------------------------------ quant.cu
 cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t* q, int ldq, uint8_t* sf,
                          int k_tiles, cudaStream_t st);

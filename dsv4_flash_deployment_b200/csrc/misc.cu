@@ -8,6 +8,21 @@
 
 namespace dsv4 {
 
+std::vector<DbgSetter>& dbg_registry() {
+  static std::vector<DbgSetter> reg;
+  return reg;
+}
+
+int dbg_bounds_attach(uint32_t* err) {
+  int n = 0;
+  for (DbgSetter f : dbg_registry()) {
+    const cudaError_t e = f(err);
+    if (e != cudaSuccess) return -(int)e;
+    ++n;
+  }
+  return n;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("DSV4_PDL");

@@ -173,11 +173,14 @@ class DSV4Model:
         max_c = max([self.max_seq_len // cfg.ratio(l) for l in cfg.kv_source_layer_ids] or [1])
         self.cand = z(T, max(1, max_c // max(1, cfg.candidate_block_size)), dt=u8)
         # MoE
-        E = max(cfg.n_routed_experts, cfg.dspark_n_routed_experts if cfg.n_mtp_layers else 0)
-        k = max(cfg.n_activated_experts, cfg.dspark_n_activated_experts if cfg.n_mtp_layers else 0)
+        # the tensor-parallel layout runs the backbone only (no MTP stages, whose
+        # routing width differs)
+        mtp = cfg.n_mtp_layers if self.tp is None else 0
+        E = max(cfg.n_routed_experts, cfg.dspark_n_routed_experts if mtp else 0)
+        k = max(cfg.n_activated_experts, cfg.dspark_n_activated_experts if mtp else 0)
         self.router_logits = {}
         self.route = {}   # top-k -> (ids, wts, pos, rank)
-        for lid in range(cfg.n_total_layers):
+        for lid in range(cfg.n_layers + mtp):
             ee, kk = cfg.n_experts_for(lid), cfg.topk_for(lid)
             if ee not in self.router_logits:
                 self.router_logits[ee] = e(T, ee, dt=f32)
@@ -209,7 +212,7 @@ class DSV4Model:
         self.hperm_sf = z(self.cap // 128, I // 128, 512, dt=u8)
         self.yperm = e(self.cap, D)
         self.row_scale = z(self.cap, dt=f32)
-        si = cfg.n_shared_experts * I
+        si = cfg.n_shared_experts * cfg.moe_inter_dim     # the shared expert is never split
         self.hs = e(Tp, si, dt=u8)
         self.hs_sf = z(Tp // 128, si // 128, 512, dt=u8)
         self.shared_out = e(T, D)

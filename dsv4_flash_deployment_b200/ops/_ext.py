@@ -5,6 +5,12 @@
 ``dsv4_flash_deployment_b200/_build/dsv4_C.so``.  ``load()`` imports that file
 directly; it never compiles, so a GPU box that received a pre-built tree only
 loads it.  On a CUDA machine a missing extension is an error, not a fallback.
+
+``DSV4_DEBUG_BOUNDS=1`` selects the debug-bounds variant (``dsv4_C_dbg`` in
+``_build_dbg/``, compiled with ``-DDSV4_DEBUG_BOUNDS``): cache gathers and
+writes check their indices and record a bad one in the device error word
+instead of touching memory outside the buffer.  Build it with
+``build(debug_bounds=True)``.
 """
 
 from __future__ import annotations
@@ -97,23 +103,34 @@ def sources() -> list[str]:
     return sorted(glob.glob(str(CSRC / "*.cu")) + glob.glob(str(CSRC / "*.cpp")))
 
 
-def so_path() -> Path:
-    return BUILD / f"{NAME}.so"
+def debug_bounds() -> bool:
+    return os.environ.get("DSV4_DEBUG_BOUNDS", "0") == "1"
 
 
-def build(verbose: bool = False):
+def _variant(dbg: bool) -> tuple[str, Path]:
+    return (NAME + "_dbg", PKG / "_build_dbg") if dbg else (NAME, BUILD)
+
+
+def so_path(dbg: bool | None = None) -> Path:
+    name, d = _variant(debug_bounds() if dbg is None else dbg)
+    return d / f"{name}.so"
+
+
+def build(verbose: bool = False, debug_bounds: bool = False):
     """Compile the extension in-tree (works without a GPU)."""
     from torch.utils import cpp_extension
 
-    BUILD.mkdir(parents=True, exist_ok=True)
+    name, bdir = _variant(debug_bounds)
+    bdir.mkdir(parents=True, exist_ok=True)
     os.environ.setdefault("MAX_JOBS", str(max(1, (os.cpu_count() or 4))))
+    extra = ["-DDSV4_DEBUG_BOUNDS"] if debug_bounds else []
     mod = cpp_extension.load(
-        name=NAME,
+        name=name,
         sources=sources(),
-        extra_cflags=CXX_FLAGS,
-        extra_cuda_cflags=NVCC_FLAGS,
+        extra_cflags=CXX_FLAGS + extra,
+        extra_cuda_cflags=NVCC_FLAGS + extra,
         extra_include_paths=[str(CSRC)],
-        build_directory=str(BUILD),
+        build_directory=str(bdir),
         verbose=verbose,
         with_cuda=True,
     )
@@ -134,9 +151,10 @@ def load(required: bool | None = None):
         if required:
             raise RuntimeError(f"CUDA extension not built: {path} missing (run __graft_entry__.build())")
         return None
-    spec = importlib.util.spec_from_file_location(NAME, str(path))
+    name = path.stem
+    spec = importlib.util.spec_from_file_location(name, str(path))
     mod = importlib.util.module_from_spec(spec)
-    sys.modules[NAME] = mod
+    sys.modules[name] = mod
     spec.loader.exec_module(mod)
     _mod = _Counting(mod)
     return _mod

@@ -32,7 +32,12 @@ class ErrorWord:
     def get(cls, device) -> torch.Tensor:
         key = str(device)
         if key not in cls._words:
-            cls._words[key] = torch.zeros(1, dtype=torch.int32, device=device)
+            w = torch.zeros(1, dtype=torch.int32, device=device)
+            cls._words[key] = w
+            if w.is_cuda:
+                mod = _ext.load(required=False)
+                if mod is not None and getattr(mod, "debug_bounds", False):
+                    mod.debug_bounds_attach(w)     # index checks of the debug build report here
         return cls._words[key]
 
     @classmethod
