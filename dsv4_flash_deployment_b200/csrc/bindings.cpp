@@ -305,7 +305,7 @@ void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>&
     p.e_local = (int)v[12];
     p.err = reinterpret_cast<uint32_t*>(err->data_ptr<int>());
     TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr
-                : p.tp_mode == 3 ? (p.peer_y != nullptr && p.pos != nullptr && topk > 0)
+                : p.tp_mode == 3 ? (p.peer_y != nullptr && p.peer_pos != nullptr && topk > 0)
                                  : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
                 "tp mode tables missing");
     TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 3, "tp mode must be 1, 2 or 3");
@@ -717,6 +717,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("hc_num_slices", [](int64_t d) { return (int64_t)dsv4::hc_num_slices((int)d); });
   m.def("attention", &attention);
   m.def("debug_bounds_attach", &debug_bounds_attach);
+  m.def("debug_bounds_units", []() { return (int64_t)dsv4::dbg_bounds_units(); });
 #ifdef DSV4_DEBUG_BOUNDS
   m.attr("debug_bounds") = true;
 #else

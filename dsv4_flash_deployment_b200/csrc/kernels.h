@@ -22,6 +22,7 @@ struct KvPages {
 // device).  Returns the number of units set (0 in the default build, which has
 // no checks), or -cudaError on failure.
 int dbg_bounds_attach(uint32_t* err);
+int dbg_bounds_units();   // translation units with index checks (0 in the default build)
 
 // ------------------------------------------------------------ quant.cu
 cudaError_t act_quant_mx(const __nv_bfloat16* x, int ldx, int T, int K, uint8_t* q, int ldq, uint8_t* sf,
@@ -59,7 +60,8 @@ struct HcParams {
   // (token, slot) pair's expert row is read from the rank owning its expert
   // (peer_yperm / peer_pos; ids are identical on every rank); tp_mode 3 = experts
   // split by intermediate index: every rank's f32 partial row of each pair
-  // (peer_y tables, row pos[t, slot]) summed in rank order.  All wait first
+  // (peer_y tables, at row peer_pos[rank][t, slot] of that rank's own plan)
+  // summed in rank order.  All wait first
   // (bounded) until every rank has published the phase.
   int tp_mode;
   const float* const* peer_y;

@@ -141,14 +141,16 @@ __global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slice
       }
       if (p.tp_mode == 3) {
         // experts split over the ranks by intermediate index: every rank holds an
-        // f32 partial row for every routed pair (same row index on every rank);
+        // f32 partial row for every routed pair, at the row its own MoE plan gave
+        // the pair (the order inside an expert segment comes from atomics, so it
+        // differs between ranks: read each rank's row index from its pos table);
         // sum ranks in order, slots in order, so every rank gets the same bits
         const int k = min(p.topk, kMaxCombine);
-        int rw[kMaxCombine];
-#pragma unroll
-        for (int s = 0; s < kMaxCombine; ++s) rw[s] = s < k ? p.pos[(size_t)t * p.topk + s] : -1;
         for (int rk = 0; rk < p.wait.world; ++rk) {
           const float* base = p.peer_y[rk];
+          int rw[kMaxCombine];
+#pragma unroll
+          for (int s = 0; s < kMaxCombine; ++s) rw[s] = s < k ? p.peer_pos[rk][(size_t)t * p.topk + s] : -1;
           float4 a[kMaxCombine], b[kMaxCombine];
 #pragma unroll
           for (int s = 0; s < kMaxCombine; ++s)

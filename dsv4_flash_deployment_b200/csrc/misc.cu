@@ -23,6 +23,8 @@ int dbg_bounds_attach(uint32_t* err) {
   return n;
 }
 
+int dbg_bounds_units() { return (int)dbg_registry().size(); }
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("DSV4_PDL");

@@ -30,7 +30,10 @@ class ErrorWord:
 
     @classmethod
     def get(cls, device) -> torch.Tensor:
-        key = str(device)
+        d = torch.device(device)
+        if d.type == "cuda" and d.index is None:   # "cuda" and "cuda:<current>" share one word
+            d = torch.device("cuda", torch.cuda.current_device())
+        key = str(d)
         if key not in cls._words:
             w = torch.zeros(1, dtype=torch.int32, device=device)
             cls._words[key] = w

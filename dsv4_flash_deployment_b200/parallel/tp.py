@@ -211,8 +211,10 @@ class TPGroup:
         if d is None:
             b = self._b
             if self.moe == "tp":
+                # f32 partial rows of every rank, each at the row of that rank's own plan
                 d = torch.cat([torch.tensor([3], dtype=torch.int64), self._sync[PH_MOE],
-                               torch.tensor([b["peer_yperm"].data_ptr(), 0, 0, 0, 0], dtype=torch.int64)])
+                               torch.tensor([b["peer_yperm"].data_ptr(), 0, b["peer_pos"].data_ptr(), 0, 0],
+                                            dtype=torch.int64)])
             else:
                 d = torch.cat([torch.tensor([2], dtype=torch.int64), self._sync[PH_MOE],
                                torch.tensor([0, b["peer_yperm"].data_ptr(), b["peer_pos"].data_ptr(),
