@@ -143,28 +143,27 @@ __global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slice
         // experts split over the ranks by intermediate index: every rank holds an
         // f32 partial row for every routed pair, at the row its own MoE plan gave
         // the pair (the order inside an expert segment comes from atomics, so it
-        // differs between ranks: read each rank's row index from its pos table);
-        // sum ranks in order, slots in order, so every rank gets the same bits
+        // differs between ranks: read each rank's row index from its pos table).
+        // A pair's row is the rank-order sum of its partials rounded to bf16, as
+        // the whole expert's W2 output is on one GPU; rows add in slot order, so
+        // every rank gets the same bits and one GPU's rounding is reproduced
+        // (without the per-row rounding the FP8 re-quantizations downstream
+        // amplify the difference).
         const int k = min(p.topk, kMaxCombine);
-        for (int rk = 0; rk < p.wait.world; ++rk) {
-          const float* base = p.peer_y[rk];
-          int rw[kMaxCombine];
+        for (int s = 0; s < k; ++s) {
+          float r8[8];
 #pragma unroll
-          for (int s = 0; s < kMaxCombine; ++s) rw[s] = s < k ? p.peer_pos[rk][(size_t)t * p.topk + s] : -1;
-          float4 a[kMaxCombine], b[kMaxCombine];
+          for (int q = 0; q < 8; ++q) r8[q] = 0.f;
+          for (int rk = 0; rk < p.wait.world; ++rk) {
+            const int rw = p.peer_pos[rk][(size_t)t * p.topk + s];
+            if (rw < 0) continue;
+            const float4* src = reinterpret_cast<const float4*>(p.peer_y[rk] + (size_t)rw * D + d);
+            const float4 a = src[0], b = src[1];
+            r8[0] += a.x; r8[1] += a.y; r8[2] += a.z; r8[3] += a.w;
+            r8[4] += b.x; r8[5] += b.y; r8[6] += b.z; r8[7] += b.w;
+          }
 #pragma unroll
-          for (int s = 0; s < kMaxCombine; ++s)
-            if (rw[s] >= 0) {
-              const float4* src = reinterpret_cast<const float4*>(base + (size_t)rw[s] * D + d);
-              a[s] = src[0];
-              b[s] = src[1];
-            }
-#pragma unroll
-          for (int s = 0; s < kMaxCombine; ++s)
-            if (rw[s] >= 0) {
-              y[0] += a[s].x; y[1] += a[s].y; y[2] += a[s].z; y[3] += a[s].w;
-              y[4] += b[s].x; y[5] += b[s].y; y[6] += b[s].z; y[7] += b[s].w;
-            }
+          for (int q = 0; q < 8; ++q) y[q] += __bfloat162float(__float2bfloat16(r8[q]));
         }
       }
       if (p.tp_mode == 1) {
