@@ -15,9 +15,11 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+# The expert split's per-pair bf16 rounding fix was confirmed with the self-check at
+# world size 1 (cosine 0.9999999, every token equal); its 2-GPU run is still to come,
+# so a failure here is reported as xfail rather than stopping the suite.
 _SPLIT_OPEN = pytest.mark.xfail(strict=False, reason=(
-    "expert split on 2 GPUs matches the single-GPU logits only to cosine 0.984 (v4) / 0.989 (v4.1); the "
-    "sliced grouped GEMMs sum correctly on one GPU (test_expert_split_gpu.py), the cross-rank path is open"))
+    "expert split: confirmed at world size 1 after the per-pair rounding fix; not yet re-run on 2 GPUs"))
 
 
 @pytest.mark.parametrize("family,moe", [("v4", "ep"), pytest.param("v4", "tp", marks=_SPLIT_OPEN),
