@@ -14,7 +14,6 @@ import torch
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 # The expert split's per-pair bf16 rounding fix was confirmed with the self-check at
 # world size 1 (cosine 0.9999999, every token equal); its 2-GPU run is still to come,
 # so a failure here is reported as xfail rather than stopping the suite.
@@ -22,6 +21,7 @@ _SPLIT_OPEN = pytest.mark.xfail(strict=False, reason=(
     "expert split: confirmed at world size 1 after the per-pair rounding fix; not yet re-run on 2 GPUs"))
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("family,moe", [("v4", "ep"), pytest.param("v4", "tp", marks=_SPLIT_OPEN),
                                         pytest.param("v41", "tp", marks=_SPLIT_OPEN)])
 def test_tp_matches_single_gpu(family, moe):
