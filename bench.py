@@ -24,7 +24,7 @@ Multi-GPU: one rank per GPU; attention is data-parallel over the requests
 runs in the fused NVLink dispatch/combine kernels of ``parallel/ep.py``.
 
     python bench.py [--gpus N --steps K --warmup W]
-    python bench.py --impl reference     # the reference arm
+    python bench.py --impl reference     # the reference arm (prints why it is unavailable)
 """
 
 from __future__ import annotations
