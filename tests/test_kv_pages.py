@@ -102,3 +102,19 @@ def test_memory_estimate_counts_the_paged_pool():
     # same capacity: the pools only add the scratch blocks (and drop the padding slot)
     assert abs(paged_same - full) < 0.01 * full
     assert paged_small < full - 10 * 2 ** 30   # 2k instead of 16k tokens per sequence
+
+
+def test_cancel_releases_blocks_and_unblocks_the_queue():
+    _, pg = _pager(pool_tokens=1024)
+    s = Scheduler(max_seqs=2, max_batched_tokens=1024, max_seq_len=1024, kv=pg)
+    a = s.add(list(range(900)), 8, ignore_eos=True)
+    b = s.add(list(range(300)), 8, ignore_eos=True)
+    first = s.schedule()
+    assert [c.req for c in first] == [a] and b.slot < 0      # b waits for blocks
+    s.commit(first, [7])
+    s.cancel(a)
+    nxt = s.schedule()                                       # a's blocks return, b is admitted
+    assert a.finished and a.finish_reason == "cancelled"
+    assert [c.req for c in nxt] == [b]
+    assert pg.alloc[4].slot_blocks(b.slot) == -(-(308 // 4 + 1) // 16)
+    assert pg.free_blocks()[4] == 16 - pg.alloc[4].slot_blocks(b.slot)
