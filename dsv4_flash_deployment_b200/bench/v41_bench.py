@@ -67,6 +67,9 @@ def main(argv=None) -> None:
     ap.add_argument("--osl", type=int, default=1024)
     ap.add_argument("--chunk", type=int, default=256, help="prefill tokens per step (the reference's V4.1 chunk)")
     ap.add_argument("--engram-rows", type=int, default=96_000_000, help="rows per Engram table")
+    ap.add_argument("--engram-shm", default=None,
+                    help="keep the Engram tables in shared files with this prefix (e.g. /dev/shm/dsv4_engram): "
+                         "one copy per node instead of one per rank")
     ap.add_argument("--spec-rounds", type=int, default=12)
     ap.add_argument("--force-accept", type=int, default=4)
     ap.add_argument("--no-spec", action="store_true")
@@ -106,7 +109,8 @@ def main(argv=None) -> None:
     n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world, reserve_gb=12.0 + spec_gb + tp_gb)
     t_build = time.perf_counter()
     eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
-                       expert_storage_layers=n_phys, ep=ep, use_graphs=not a.no_graphs, chunk_size=chunk)
+                       expert_storage_layers=n_phys, ep=ep, use_graphs=not a.no_graphs, chunk_size=chunk,
+                       engram_shm=a.engram_shm)
     t_build = time.perf_counter() - t_build
     model = eng.model
     rng = np.random.default_rng(99 + rank)
@@ -218,6 +222,7 @@ def main(argv=None) -> None:
                        "expert_storage_layers": n_phys, "cuda_graphs": not a.no_graphs,
                        "l2": "inputs larger than L2 (experts 7.2 GB per layer)",
                        "engram": {"rows_per_table": a.engram_rows, "tables_gb_pinned_host": round(tables_gb, 1),
+                                  "shared_files": a.engram_shm,
                                   "note": "reference tables 2 x ~101 GB exceed the 196 GB host RAM of the GPU box"},
                        "build_s": round(t_build, 1)},
             "c1_tpot_ms": ({"value": round(c1_wall, 3), "device_ms": round(c1_dev, 3), "context": c1_pos,

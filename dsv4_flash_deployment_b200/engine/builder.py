@@ -22,7 +22,8 @@ def _pad_rows(w: torch.Tensor) -> torch.Tensor:
 def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, max_seq_len: int = 2048,
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
                 ep=None, tp=None, experts_from: DSV4Model | None = None, kv_block: int = 0,
-                kv_pool_tokens: int = 0, engram_from: DSV4Model | None = None) -> DSV4Model:
+                kv_pool_tokens: int = 0, engram_from: DSV4Model | None = None,
+                engram_shm: str | None = None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -39,7 +40,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     tokens of context (0: ``n_slots * max_seq_len``).  ``engram_from``: a model
     whose Engram runtime (host tables, token rings, staging buffers) this one
     uses instead of building its own; it must have at least as many slots and
-    step tokens, and the two models must not step concurrently.
+    step tokens, and the two models must not step concurrently.  ``engram_shm``:
+    random-init Engram tables in shared files with this prefix (one copy per node).
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -89,5 +91,6 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
         model.engram = eg
     elif cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
-        model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed)
+        model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed,
+                                     shm_prefix=engram_shm)
     return model

@@ -42,6 +42,7 @@ class EngineConfig:
     dspark: bool = False                    # speculative decoding: SpecEngine only (the server refuses it)
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True
+    engram_shm: str | None = None           # random-init Engram tables in shared files (e.g. /dev/shm/dsv4_engram)
     host: str = "127.0.0.1"
     port: int = 8000
     step_deadline_s: float = 600.0

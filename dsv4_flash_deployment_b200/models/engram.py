@@ -7,7 +7,9 @@ FP8 ``wkv`` projection to 4 keys + 1 value, and a per-stream sigmoid gate
 P/0005:1183-1370).  Here:
 
 * the tables stay in page-locked host memory (``cudaHostRegister`` of the
-  loaded arrays, or pinned allocations for random init) and the GPU reads the
+  loaded arrays, of pinned allocations for random init, or of shared files
+  under ``/dev/shm`` that every rank of the node maps, as the reference keeps
+  its tables in ``/dev/shm``: ``MK/megakernel/load.py:203-355``) and the GPU reads the
   rows it needs straight over the host link: 24 x (256 + 8) bytes per token
   and layer, with no host thread on the step's critical path;
 * hashing runs on the GPU from this step's tokens and a per-slot ring of the
@@ -28,6 +30,45 @@ import torch
 from ..ops.gemm import MxWeight
 from ..ops.layout import ceil_to, expand_block_scales
 from ..ref.engram import EngramHasher
+
+
+def shared_table(prefix: str, tag: str, rows: int, width: int, fill, signature: str) -> torch.Tensor:
+    """uint8 [rows, width] backed by the shared file ``<prefix>.<tag>`` (e.g. under
+    ``/dev/shm``), filled once for all processes.
+
+    The first process to take the file's lock creates and fills it and then writes
+    a ``.ready`` marker holding the shape and ``signature`` (the fill's seed and
+    mode); every later process (the other ranks of the node, or a restarted
+    server) maps the same pages without filling.  A marker for another shape or
+    signature makes the next process rebuild the file.  The files outlive the
+    processes; delete them to free the memory.
+    """
+    import fcntl
+    import json
+    import os
+
+    path = f"{prefix}.{tag}"
+    nbytes = rows * width
+    sig = json.dumps({"rows": rows, "width": width, "fill": signature})
+    with open(path + ".lock", "a") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            ready = path + ".ready"
+            ok = (os.path.exists(ready) and os.path.exists(path) and os.path.getsize(path) == nbytes
+                  and open(ready).read() == sig)
+            if not ok:
+                for f in (ready, path):
+                    if os.path.exists(f):
+                        os.remove(f)
+                t = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+                fill(t.view(rows, width))
+                with open(ready, "w") as f:
+                    f.write(sig)
+            else:
+                t = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
+    return t.view(rows, width)
 
 
 class HostTable:
@@ -81,7 +122,11 @@ class HostTable:
 
 
 class EngramRuntime:
-    def __init__(self, cfg, dev, n_slots: int, max_tokens: int, ext, weights: dict | None = None, seed: int = 0):
+    def __init__(self, cfg, dev, n_slots: int, max_tokens: int, ext, weights: dict | None = None, seed: int = 0,
+                 shm_prefix: str | None = None):
+        """``shm_prefix`` (random init only): keep the tables in shared files
+        ``<shm_prefix>.l<layer>.{q,sf}`` that every process of the node maps (one
+        copy per node instead of one per rank; see :func:`shared_table`)."""
         self.cfg, self.dev, self.ext = cfg, dev, ext
         h = EngramHasher(cfg)
         lay = h.layout
@@ -115,10 +160,17 @@ class EngramRuntime:
                 # multithreaded generator, then page-lock them in place (HostTable)
                 from ..ops import host
                 n_emb = lay.num_embeddings[i]
-                q = torch.empty(n_emb, self.hd, dtype=torch.uint8)
-                sf = torch.empty(n_emb, self.hd // 32, dtype=torch.uint8)
-                host.fill_random(q, seed * 1000 + 2 * i + 1, 0)
-                host.fill_random(sf, seed * 1000 + 2 * i + 2, 1, 118)
+                sq, ssf = seed * 1000 + 2 * i + 1, seed * 1000 + 2 * i + 2
+                if shm_prefix:
+                    q = shared_table(shm_prefix, f"l{lid}.q", n_emb, self.hd,
+                                     lambda t, s=sq: host.fill_random(t, s, 0), f"e4m3 seed {sq}")
+                    sf = shared_table(shm_prefix, f"l{lid}.sf", n_emb, self.hd // 32,
+                                      lambda t, s=ssf: host.fill_random(t, s, 1, 118), f"ue8m0 seed {ssf} lo 118")
+                else:
+                    q = torch.empty(n_emb, self.hd, dtype=torch.uint8)
+                    sf = torch.empty(n_emb, self.hd // 32, dtype=torch.uint8)
+                    host.fill_random(q, sq, 0)
+                    host.fill_random(sf, ssf, 1, 118)
                 wq = (torch.randn((hc + 1) * D, self.K, generator=g) * 0.5).to(torch.float8_e4m3fn)
                 ws = torch.randint(118, 123, ((hc + 1) * D // 32, self.K // 32), generator=g,
                                    dtype=torch.int32).to(torch.uint8)

@@ -30,7 +30,7 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
                         max_seq_len=ec.max_model_len, weights=_load_weights(ec, cfg), seed=ec.seed,
                         expert_storage_layers=ec.expert_storage_layers, ep=ep, use_graphs=ec.use_cuda_graphs,
                         chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp, kv_block=ec.kv_block,
-                        kv_pool_tokens=ec.kv_pool_tokens)
+                        kv_pool_tokens=ec.kv_pool_tokens, engram_shm=ec.engram_shm)
 
 
 def _load_weights(ec: EngineConfig, cfg):
