@@ -87,9 +87,9 @@ class _SchedView:
 
 def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int, replicated: bool = False) -> list[tuple]:
     """Applies a control message to this rank's engine and runs its part of the step."""
-    for gid, r, prompt, mt, ignore_eos, stop_ids in msg["adds"]:
+    for gid, r, prompt, mt, ignore_eos, stop_ids, temperature in msg["adds"]:
         if r == rank or r == -1:
-            req = engine.add_request(prompt, mt, ignore_eos=ignore_eos, stop_ids=stop_ids)
+            req = engine.add_request(prompt, mt, ignore_eos=ignore_eos, stop_ids=stop_ids, temperature=temperature)
             id_map[req.req_id] = gid
             id_map[("g", gid)] = req
     for gid in msg["cancels"]:
@@ -143,9 +143,11 @@ class DistributedEngine:
         self.eos_id = local_engine.eos_id
 
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
-                    stop_ids=()) -> GlobalRequest:
+                    stop_ids=(), temperature: float = 0.0) -> GlobalRequest:
         if not prompt:
             raise ValueError("empty prompt")
+        if temperature < 0:
+            raise ValueError("temperature must be >= 0")
         if len(prompt) + max_new_tokens > self.local.sched.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.local.sched.max_seq_len}")
@@ -154,7 +156,7 @@ class DistributedEngine:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds the paged cache pool")
         r = -1 if self.replicated else min(range(self.world), key=lambda i: self.load[i])
         g = GlobalRequest(self.next_id, r, list(prompt), max_new_tokens)
-        g._opts = (bool(ignore_eos), tuple(stop_ids))
+        g._opts = (bool(ignore_eos), tuple(stop_ids), float(temperature))
         self.next_id += 1
         self.load[r] += 1
         self.pending_adds.append(g)

@@ -65,15 +65,19 @@ class Engine:
 
     # ------------------------------------------------------------------- API
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
-                    stop_ids: Iterable[int] = ()) -> Request:
+                    stop_ids: Iterable[int] = (), temperature: float = 0.0) -> Request:
+        """``temperature`` 0 decodes greedily; > 0 samples softmax(logits / T)."""
+        if temperature < 0:
+            raise ValueError("temperature must be >= 0")
         return self.sched.add(prompt, max_new_tokens, ignore_eos=ignore_eos, eos_id=self.eos_id,
-                              stop_ids=tuple(stop_ids))
+                              stop_ids=tuple(stop_ids), temperature=float(temperature))
 
     def step(self) -> list[tuple[Request, int | None]]:
         chunks = self.sched.schedule()
         if not chunks:
             return []
-        meta = StepMeta(self.cfg, [SeqChunk(c.req.slot, c.start_pos, c.tokens, c.sample) for c in chunks])
+        meta = StepMeta(self.cfg, [SeqChunk(c.req.slot, c.start_pos, c.tokens, c.sample,
+                                            temperature=c.req.temperature) for c in chunks])
         ids = self.run_meta(meta)
         return self.sched.commit(chunks, ids)
 

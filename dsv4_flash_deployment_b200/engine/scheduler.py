@@ -28,6 +28,7 @@ class Request:
     ignore_eos: bool = False
     eos_id: int | None = None
     stop_ids: tuple[int, ...] = ()
+    temperature: float = 0.0          # 0 = greedy
     slot: int = -1
     n_prefilled: int = 0
     output: list[int] = field(default_factory=list)

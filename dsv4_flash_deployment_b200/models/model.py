@@ -48,6 +48,7 @@ class SeqChunk:
     tokens: list[int]
     sample: bool = True        # produce logits for the last token of the chunk
     sample_all: bool = False   # produce logits for every token (speculative verify, draft blocks)
+    temperature: float = 0.0   # > 0: sample the next token (Gumbel-max) instead of the argmax
 
 
 class StepMeta:
@@ -80,6 +81,11 @@ class StepMeta:
             self.sample_rows = np.concatenate(rows).astype(np.int32)
         else:
             self.sample_rows = (row0 + lens - 1)[samp].astype(np.int32)
+        # per sampled row: 0 = greedy, > 0 = temperature (one value per chunk)
+        temps = np.fromiter((c.temperature for c in chunks), np.float32, n)
+        per_chunk = np.where(sall, lens, samp.astype(np.int64))
+        self.temps = np.repeat(temps, per_chunk).astype(np.float32)
+        self.sampling = bool((self.temps > 0).any())
         self.max_pos = int(self.pos.max()) if T else 0
         # compressor groups closed in this step, per ratio (token order)
         self.groups = {}
@@ -97,7 +103,7 @@ class StepMeta:
     def key(self):
         """Graph key: shapes and control flow of the step."""
         return (self.T, len(self.sample_rows), self._lens.tobytes(),
-                tuple(self.index_bypass(r) for r in self.groups))
+                tuple(self.index_bypass(r) for r in self.groups), self.sampling)
 
 
 # --------------------------------------------------------------------------
@@ -220,6 +226,7 @@ class DSV4Model:
         self.u_sample = e(self.max_sample, D)
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
         self.next_ids = e(self.max_sample, dt=i32)
+        self.m_temp = z(self.max_sample, dt=f32)
         # multi-CTA argmax: partials [2 * max(S, 296)] + zeroed per-row counters at the end
         self.argmax_scratch = z(2 * max(self.max_sample, 296) + self.max_sample, dt=i32)
         if self.tp is not None:
@@ -309,6 +316,8 @@ class DSV4Model:
         put(self.m_row0, m.step_row0)
         put(self.m_last, m.last_pos)
         put(self.m_sample, m.sample_rows.astype(np.int64))
+        if m.sampling:
+            put(self.m_temp, m.temps)
         for r, g in m.groups.items():
             for dst, arr in zip(self.m_groups[r], g):
                 if len(arr):
@@ -442,6 +451,8 @@ class DSV4Model:
         with self._t("head"):
             torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
             self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
+            if m.sampling:
+                self._gumbel(S)
             if self.tp is None:
                 ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch, None, 0)
             else:
@@ -454,6 +465,22 @@ class DSV4Model:
                 ext.tp_argmax_merge(tp.sync(2), tp.buf("peer_aval"), tp.buf("peer_aidx"), S, self.next_ids[:S],
                                     self.err)
         return self.next_ids[:S]
+
+    def _gumbel(self, S: int) -> None:
+        """Temperature sampling by the Gumbel-max rule: the argmax of
+        logits + T * g (g ~ Gumbel(0, 1) per vocabulary entry) is a sample of
+        softmax(logits / T); rows with T = 0 keep their logits, so they stay
+        greedy.  The noise comes from the device generator (captured with the
+        step's CUDA graph); under the vocab-parallel head each rank draws the
+        noise of its own rows and the cross-rank merge keeps the best."""
+        if self._gnoise is None:   # first sampling step runs eagerly, before any capture of it
+            self._gnoise = torch.empty_like(self.logits)
+        g = self._gnoise[:S]
+        g.uniform_(1e-20, 1.0 - 1e-7)
+        g.log_().neg_().log_().neg_()
+        self.logits[:S].addcmul_(self.m_temp[:S, None], g)
+
+    _gnoise = None
 
     # ------------------------------------------------- deferred ring commits
     _defer = False

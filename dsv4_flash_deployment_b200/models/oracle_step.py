@@ -25,6 +25,7 @@ class OracleStepModel:
         self.ref = ref or RefModel(cfg, weights, max_seq_len=max_seq_len)
         self.states: list[RefState | None] = [None] * n_slots
         self.last_upload_bytes = 0
+        self._gen = torch.Generator().manual_seed(0)
 
     def upload(self, meta: StepMeta, pinned: dict | None = None) -> None:
         self.last_upload_bytes = 0
@@ -44,5 +45,9 @@ class OracleStepModel:
             for tok in c.tokens:
                 logits, _ = self.ref.step(torch.tensor([tok]), st)
             if c.sample:
-                out.append(int(logits[0].argmax()))
+                lg = logits[0].float()
+                if c.temperature > 0:   # Gumbel-max, as the device model samples
+                    u = torch.rand(lg.shape, generator=self._gen).clamp_(1e-20, 1.0 - 1e-7)
+                    lg = lg + c.temperature * (-torch.log(-torch.log(u)))
+                out.append(int(lg.argmax()))
         return torch.tensor(out, dtype=torch.int32)

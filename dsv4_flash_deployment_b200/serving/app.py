@@ -12,8 +12,10 @@ scripts/benchmark_sweep.py:70-125``):
   POST /v1/completions         prompt (text | ids | [text]), max_tokens, stream, ignore_eos, stop
   POST /v1/chat/completions    messages, max_tokens / max_completion_tokens, stream, stop
 
-Decoding is greedy (``temperature`` is accepted and reported; the engine
-samples argmax, as every reference benchmark does at temperature 0).
+Decoding: ``temperature`` 0 (the default when the field is absent, and what
+every reference benchmark sends) is greedy; ``temperature`` > 0 samples
+softmax(logits / T) on the device by the Gumbel-max rule.  ``top_p`` / ``top_k``
+other than their neutral values (1.0 / -1 or 0) are refused with 400.
 Streaming sends one SSE event per generated token and ends with
 ``data: [DONE]``; a client that disconnects cancels its request.
 
@@ -70,7 +72,16 @@ def _params(st: ServerState, body: dict, n_prompt: int) -> tuple[GenParams, list
     if isinstance(stop, str):
         stop = [stop]
     stop_ids = tuple(int(t) for t in (body.get("stop_token_ids") or []))
-    return GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids), [s for s in stop if s]
+    temp = body.get("temperature")
+    temp = 0.0 if temp is None else float(temp)
+    if temp < 0:
+        raise web.HTTPBadRequest(text=json.dumps({"error": "temperature must be >= 0"}),
+                                 content_type="application/json")
+    top_p, top_k = body.get("top_p"), body.get("top_k")
+    if (top_p is not None and float(top_p) < 1.0) or (top_k is not None and int(top_k) > 0):
+        raise web.HTTPBadRequest(text=json.dumps({"error": "top_p / top_k sampling is not supported"}),
+                                 content_type="application/json")
+    return GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids, temp), [s for s in stop if s]
 
 
 def _err(code: int, msg: str) -> web.Response:

@@ -30,6 +30,7 @@ class GenParams:
     max_tokens: int
     ignore_eos: bool = False
     stop_ids: tuple[int, ...] = ()
+    temperature: float = 0.0
 
 
 @dataclass
@@ -98,7 +99,8 @@ class EngineLoop:
                     s.put(("error", f"engine unhealthy: {self.error}"))
                     continue
                 try:
-                    req = eng.add_request(prompt, p.max_tokens, ignore_eos=p.ignore_eos, stop_ids=p.stop_ids)
+                    req = eng.add_request(prompt, p.max_tokens, ignore_eos=p.ignore_eos, stop_ids=p.stop_ids,
+                                          temperature=p.temperature)
                 except ValueError as e:
                     s.put(("error", str(e)))
                     continue

@@ -209,3 +209,29 @@ def test_eval_parsing_and_shuffle():
     assert evals.extract_letter("no letter") is None
     assert evals.math_target({"answer": "steps #### 1,234"}) == 1234.0
     assert evals._number("the result is -3.5.") == -3.5
+
+
+def test_temperature_sampling_and_refusals(served):
+    st, eng = served
+    ids = [0] + [30 + (5 * i) % 200 for i in range(30)]
+    want = _greedy(eng, ids, 8)
+
+    async def go(c):
+        g = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 8, "ignore_eos": True,
+                                                          "temperature": 0})).json()
+        hot = []
+        for _ in range(3):
+            r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 8, "ignore_eos": True,
+                                                      "temperature": 5.0, "top_p": 1.0})
+            hot.append(await r.json())
+        bad = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "top_p": 0.9})
+        neg = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "temperature": -1})
+        return g, hot, bad.status, neg.status
+    g, hot, bad, neg = _run(st, go)
+    tok = st.tok
+    assert g["choices"][0]["text"] == "".join(tok.decode_token(t) for t in want)
+    texts = [h["choices"][0]["text"] for h in hot]
+    assert all(h["usage"]["completion_tokens"] == 8 for h in hot)
+    # a near-flat random-init distribution at T=5: three samples of 8 tokens are not all the greedy text
+    assert any(t != g["choices"][0]["text"] for t in texts)
+    assert bad == 400 and neg == 400

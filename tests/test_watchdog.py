@@ -17,7 +17,7 @@ class FakeEngine:
         self.stats = {}
         self.mode, self.sleep_s = mode, sleep_s
 
-    def add_request(self, prompt, max_new_tokens, ignore_eos=False, stop_ids=()):
+    def add_request(self, prompt, max_new_tokens, ignore_eos=False, stop_ids=(), temperature=0.0):
         return self.sched.add(prompt, max_new_tokens, ignore_eos=ignore_eos, stop_ids=tuple(stop_ids))
 
     def step(self):
