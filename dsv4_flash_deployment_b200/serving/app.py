@@ -15,7 +15,8 @@ scripts/benchmark_sweep.py:70-125``):
 Decoding: ``temperature`` 0 (the default when the field is absent, and what
 every reference benchmark sends) is greedy; ``temperature`` > 0 samples
 softmax(logits / T) on the device by the Gumbel-max rule.  ``top_p`` / ``top_k``
-other than their neutral values (1.0 / -1 or 0) are refused with 400.
+other than their neutral values (1.0 / -1 or 0), ``n`` / ``best_of`` > 1 and
+``logprobs`` are refused with 400.
 Streaming sends one SSE event per generated token and ends with
 ``data: [DONE]``; a client that disconnects cancels its request.
 
@@ -76,6 +77,13 @@ def _params(st: ServerState, body: dict, n_prompt: int) -> tuple[GenParams, list
     temp = 0.0 if temp is None else float(temp)
     if temp < 0:
         raise web.HTTPBadRequest(text=json.dumps({"error": "temperature must be >= 0"}),
+                                 content_type="application/json")
+    for key in ("n", "best_of"):
+        if body.get(key) is not None and int(body[key]) != 1:
+            raise web.HTTPBadRequest(text=json.dumps({"error": f"{key} > 1 is not supported (one choice per request)"}),
+                                     content_type="application/json")
+    if body.get("logprobs") not in (None, False, 0) or body.get("top_logprobs"):
+        raise web.HTTPBadRequest(text=json.dumps({"error": "logprobs are not supported"}),
                                  content_type="application/json")
     top_p, top_k = body.get("top_p"), body.get("top_k")
     if (top_p is not None and float(top_p) < 1.0) or (top_k is not None and int(top_k) > 0):

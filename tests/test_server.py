@@ -226,6 +226,11 @@ def test_temperature_sampling_and_refusals(served):
             hot.append(await r.json())
         bad = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "top_p": 0.9})
         neg = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "temperature": -1})
+        for extra in ({"n": 2}, {"best_of": 3}, {"logprobs": 5}):
+            r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, **extra})
+            assert r.status == 400, extra
+        ok = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "n": 1, "logprobs": None})
+        assert ok.status == 200
         return g, hot, bad.status, neg.status
     g, hot, bad, neg = _run(st, go)
     tok = st.tok
