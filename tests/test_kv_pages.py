@@ -118,3 +118,19 @@ def test_cancel_releases_blocks_and_unblocks_the_queue():
     assert [c.req for c in nxt] == [b]
     assert pg.alloc[4].slot_blocks(b.slot) == -(-(308 // 4 + 1) // 16)
     assert pg.free_blocks()[4] == 16 - pg.alloc[4].slot_blocks(b.slot)
+
+
+def test_pager_for_ratio_one_and_two_caches():
+    from dsv4_flash_deployment_b200.config import v41_flash_config
+
+    cfg = v41_flash_config()
+    pg = KvPager(cfg, "cpu", 5, 4096, 64, pool_tokens=3 * 4096)
+    assert set(pg.ratios) <= {1, 2} and pg.ratios
+    for r in pg.ratios:
+        assert pg.max_c[r] == 4096 // r
+        assert pg.n_blocks[r] == -(-(3 * 4096 // r) // 64)
+        assert pg.desc[r][1].item() * 64 >= pg.max_c[r]          # ld blocks cover a whole sequence
+    assert pg.fits(4096) and pg.reserve(0, 4096) and pg.reserve(1, 4096) and pg.reserve(2, 4096)
+    assert not pg.reserve(3, 100)                                 # pool holds three full sequences
+    pg.release(1)
+    assert pg.reserve(3, 4096)
