@@ -1,10 +1,19 @@
-"""Per-op time breakdown of one model step, from CUDA events (no profiler).
+"""Per-op time breakdown of one model step (no profiler).
 
 Builds the same V4-Flash steady-state step as ``bench.py`` (or a smaller
-config), runs it eagerly with event pairs around every op group, and prints
-milliseconds per step per group plus the share of the step.
+config) and prints milliseconds per step per op group plus the share of the
+step.  Two ways to time it:
+
+* default: eager steps with CUDA-event pairs around every op group (host
+  launch gaps of eager mode are included);
+* ``--device-trace``: the step is captured in a CUDA graph with a device
+  timestamp mark after every op group (``utils/devtrace.py``) and replayed;
+  works under ``torchrun`` (every rank traces; the table shows the max over
+  ranks of each group and the untraced graph step time for comparison).
 
     python -m dsv4_flash_deployment_b200.bench.op_profile [--steps 3]
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m dsv4_flash_deployment_b200.bench.op_profile \
+        --device-trace --steps 5
 """
 
 from __future__ import annotations
@@ -32,6 +41,9 @@ def main() -> None:
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"])
     ap.add_argument("--decode-only", action="store_true", help="C decoding sequences per rank, no prefill chunk")
     ap.add_argument("--context", type=int, default=1024, help="decode positions start here (span of 1024)")
+    ap.add_argument("--device-trace", action="store_true",
+                    help="graph-replayed step with device timestamp marks (multi-rank capable)")
+    ap.add_argument("--json-out", default=None, help="also write the table as JSON here (rank 0)")
     a = ap.parse_args()
     import os
 
@@ -68,9 +80,14 @@ def main() -> None:
     def meta(i):
         ch = [SeqChunk(s, int(dec[s]) + i, [int(rng.integers(0, cfg.vocab_size))], True) for s in range(n_dec)]
         if chunk:
-            ch.append(SeqChunk(n_dec, (i % 2) * chunk, rng.integers(0, cfg.vocab_size, chunk).tolist(), i % 2 == 1))
+            # the trace replays one graph: every step has the same shape (the chunk samples)
+            samp = True if a.device_trace else i % 2 == 1
+            ch.append(SeqChunk(n_dec, (i % 2) * chunk, rng.integers(0, cfg.vocab_size, chunk).tolist(), samp))
         return StepMeta(cfg, ch)
 
+    if a.device_trace:
+        _device_trace(a, eng, cfg, meta, rank, world, T, n_phys)
+        return
     eng.run_meta(meta(0))
     m.op_timer = {}
     tot_s, tot_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -90,6 +107,101 @@ def main() -> None:
             print(f"{k:20s} {v:9.3f} ms  {100 * v / total:5.1f}%  ({len(m.op_timer[k]) // a.steps} launches/step)")
         print(json.dumps({"step_ms": round(total, 3), "sum_ops_ms": round(acc, 3), "T": T, "n_layers": cfg.n_layers,
                           "expert_storage_layers": n_phys, "world": world}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _device_trace(a, eng, cfg, meta, rank, world, T, n_phys) -> None:
+    import torch.distributed as dist
+
+    from ..utils.devtrace import DeviceTrace, summarize
+
+    m = eng.model
+    dev = m.dev
+    st = torch.cuda.Stream(dev)
+    tr = DeviceTrace(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(st):
+        # eager step with marks (fixes the mark names), then two captures: traced and plain
+        m.dev_trace = tr
+        mm = meta(0)
+        m.upload(mm)
+        tr.begin()
+        m.forward(mm)
+        st.synchronize()
+        eng.check_errors()
+        tr.freeze()
+        g_tr = torch.cuda.CUDAGraph()
+        mm = meta(1)
+        m.upload(mm)
+        with torch.cuda.graph(g_tr, stream=st):
+            tr.begin()
+            m.forward(mm)
+        m.dev_trace = None
+        g_plain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_plain, stream=st):
+            m.forward(mm)
+        m.dev_trace = tr
+        # warm-up replays of both graphs
+        for i in range(3):
+            mm = meta(2 + i)
+            m.upload(mm)
+            g_plain.replay()
+            g_tr.replay()
+        st.synchronize()
+        eng.check_errors()
+        # untraced step time (events around K replays)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        metas = [meta(10 + i) for i in range(a.steps)]
+        e0.record(st)
+        for mm in metas:
+            m.upload(mm)
+            g_plain.replay()
+        e1.record(st)
+        st.synchronize()
+        plain_ms = e0.elapsed_time(e1) / a.steps
+        runs, totals = [], []
+        barrier()
+        for i in range(a.steps):
+            mm = meta(100 + i)
+            m.upload(mm)
+            tr.cursor = 0
+            g_tr.replay()
+            st.synchronize()
+            tr.cursor = len(tr.names)
+            runs.append(tr.read())
+            totals.append(tr.total_ns() / 1e6)
+        eng.check_errors()
+    summ = summarize(runs)
+    names = sorted(summ)
+    vals = torch.tensor([summ[k]["ms"] for k in names] + [plain_ms, sum(totals) / len(totals)], dtype=torch.float64,
+                        device=dev)
+    vmax = vals.clone()
+    if world > 1:
+        dist.all_reduce(vmax, op=dist.ReduceOp.MAX)
+    vmax = vmax.tolist()
+    v0 = vals.tolist()
+    plain_max, traced_max = vmax[-2], vmax[-1]
+    if rank == 0:
+        rows = sorted(((k, vmax[i], v0[i], summ[k]["n"]) for i, k in enumerate(names)), key=lambda x: -x[1])
+        print(f"{'op group':20s} {'max-rank ms':>11s} {'rank0 ms':>9s} {'share':>6s}  launches-groups/step")
+        for k, vx, v, n in rows:
+            print(f"{k:20s} {vx:11.3f} {v:9.3f} {100 * vx / traced_max:5.1f}%  {n}")
+        res = {"step_ms_graph_plain_max_rank": round(plain_max, 3), "step_ms_traced_max_rank": round(traced_max, 3),
+               "T_per_rank": T, "n_layers": cfg.n_layers, "expert_storage_layers": n_phys, "world": world,
+               "ops": {k: {"max_rank_ms": round(vx, 4), "rank0_ms": round(v, 4), "groups_per_step": n}
+                       for k, vx, v, n in rows}}
+        print(json.dumps({k: v for k, v in res.items() if k != "ops"}))
+        if a.json_out:
+            with open(a.json_out, "w") as f:
+                json.dump(res, f, indent=1)
+    del g_tr, g_plain
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -97,7 +97,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
           const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
           double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
           const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
-          int64_t probe, const optional<Tensor>& publish) {
+          const optional<Tensor>& publish) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -170,7 +170,6 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.workspace = workspace ? workspace->data_ptr<float>() : nullptr;
   p.tile_counters = counters ? counters->data_ptr<int>() : nullptr;
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
-  p.probe = (int)probe;
   p.pub = peer_sync_of(publish);
   if (p.splits > 1 && !(workspace && counters)) {
     // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
@@ -686,6 +685,14 @@ void pdl_probe(const Tensor& stamps, int64_t ctas, int64_t ns) {
                           (unsigned long long)ns, cur_stream()));
 }
 
+// device timestamp ring: int64 [n]; ring[slot] = %globaltimer once the previous kernel has completed
+void ts_mark(const Tensor& ring, int64_t slot) {
+  TORCH_CHECK(ring.is_cuda() && ring.scalar_type() == at::kLong && slot >= 0 && slot < ring.numel(),
+              "ts_mark: int64 device ring, slot in range");
+  const c10::cuda::CUDAGuard guard(ring.device());
+  CUDA_OK(dsv4::ts_mark(reinterpret_cast<unsigned long long*>(ring.data_ptr()), (int)slot, cur_stream()));
+}
+
 // sync: int64 CPU [7] (PeerSync); peer_val / peer_idx: int64 device tables of each rank's pairs
 void tp_argmax_merge(const Tensor& sync, const Tensor& peer_val, const Tensor& peer_idx, int64_t T, const Tensor& out,
                      const Tensor& err) {
@@ -746,5 +753,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &argmax_rows);
   m.def("tp_argmax_merge", &tp_argmax_merge);
   m.def("pdl_probe", &pdl_probe);
+  m.def("ts_mark", &ts_mark);
   m.def("markov_step", &markov_step);
 }

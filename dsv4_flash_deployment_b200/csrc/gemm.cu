@@ -32,6 +32,8 @@
 // whose rows are [64 gate rows; 64 up rows]: h = silu(min(g, L)) * clip(u, L) *
 // row_weight, rounded to bf16 and re-quantized to MXFP8 (e4m3 + ue8m0 per 32)
 // for the W2 GEMM, so the intermediate never leaves the chip in high precision.
+#include <atomic>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "peer.cuh"
@@ -89,6 +91,21 @@ DSV4_DEV int k_of(const TileCoord& t, int i) {
 // scale-factor TMEM addresses on a 4-column boundary.
 DSV4_DEV int n_eff_for(int valid) { return valid <= 32 ? 32 : valid <= 64 ? 64 : valid <= 128 ? 128 : 256; }
 DSV4_DEV int bmap_index(int n_eff) { return n_eff == 32 ? 0 : n_eff == 64 ? 1 : n_eff == 128 ? 2 : 3; }
+
+// Accumulator columns [c0, c0 + kCols) of this warp's TMEM lane quadrant.  A
+// split whose k range is empty (more splits than k tiles allow) issued no MMA,
+// so its accumulator holds stale data: it contributes zeros instead.
+template <int kCols>
+DSV4_DEV void load_acc(uint32_t d_tmem, int q, int c0, uint32_t (&r)[32], bool kempty) {
+  if (kempty) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = 0u;
+    return;
+  }
+  if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
+  else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+  tmem_ld_wait();
+}
 
 template <bool GROUPED, int BN, int BM = 128>
 DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(192, 1)
             sfb_t = col + 4 * L::kSfaChunks;
           }
 #pragma unroll
-          for (int kk = 0; kk < ((p.probe & 1) ? 0 : 4); ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
             const uint64_t bd = sdesc_kmajor_sw128(b0 + kk * 32);
             const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
             // 256-row weight tiles: two M=128 MMAs (rows 0-127, 128-255) share the token tile
@@ -323,6 +340,7 @@ __global__ void __launch_bounds__(192, 1)
       TileCoord th = t;
       th.out_col0 += 128 * hh;
       const uint32_t d_tmem = tmem + acc * L::kAccCols + hh * L::kAccColsHalf;
+      const bool kempty = t.k_end <= t.k_begin;
       const bool split = p.splits > 1;
       constexpr int kCols = BN < 32 ? BN : 32;
       constexpr int kPS = BN + 4;   // padded row stride of a parked partial tile (floats)
@@ -333,9 +351,7 @@ __global__ void __launch_bounds__(192, 1)
         float* part = reinterpret_cast<float*>(smem);
         for (int c0 = 0; c0 < th.n_eff; c0 += kCols) {
           uint32_t r[32];
-          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
-          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
-          tmem_ld_wait();
+          load_acc<kCols>(d_tmem, q, c0, r, kempty);
           float4* dst = reinterpret_cast<float4*>(part + (size_t)row * kPS + c0);
 #pragma unroll
           for (int j = 0; j < kCols / 4; ++j)
@@ -372,7 +388,7 @@ __global__ void __launch_bounds__(192, 1)
               acc4.x += x.x, acc4.y += x.y, acc4.z += x.z, acc4.w += x.w;
             }
             const int m = th.out_col0 + r;
-            if ((p.probe & 2) || m >= p.m_valid) continue;
+            if (m >= p.m_valid) continue;
             const float vals[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -421,10 +437,8 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t e = pow2_ceil_exp(amax, 1.f / 448.f);
             const float qv = fminf(fmaxf(h / exp_to_f32(e), -448.f), 448.f);
             const int i_global = (th.out_col0 >> 1) + i_local;
-            if (!(p.probe & 2)) {
-              p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
-              if (lane == 0) p.hsf[sf_chunk_offset(brow, i_global >> 5, p.h_ktiles)] = (uint8_t)e;
-            }
+            p.hq[(size_t)brow * p.ldh + i_global] = f32_to_e4m3(qv);
+            if (lane == 0) p.hsf[sf_chunk_offset(brow, i_global >> 5, p.h_ktiles)] = (uint8_t)e;
           }
           c_begin = th.n_eff;
         }
@@ -432,9 +446,7 @@ __global__ void __launch_bounds__(192, 1)
         // Publish this split's partial tile, then let the last arrival reduce.
         for (int c0 = 0; c0 < th.n_eff; c0 += kCols) {
           uint32_t r[32];
-          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
-          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
-          tmem_ld_wait();
+          load_acc<kCols>(d_tmem, q, c0, r, kempty);
           // row-major partial tile: each thread stores whole 16-byte column groups of its row
           float4* dst = reinterpret_cast<float4*>(ws_tile + (size_t)th.split * 128 * BN + (size_t)row * BN + c0);
 #pragma unroll
@@ -506,9 +518,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         } else {
           uint32_t r[32];
-          if constexpr (kCols == 32) tmem_ld_32x32b_x32(d_tmem + ((uint32_t)(32 * q) << 16) + c0, r);
-          else tmem_ld_32x32b_x16(d_tmem + ((uint32_t)(32 * q) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
-          tmem_ld_wait();
+          load_acc<kCols>(d_tmem, q, c0, r, kempty);
 #pragma unroll
           for (int j = 0; j < kCols; ++j) v[j] = __uint_as_float(r[j]);
         }
@@ -568,7 +578,7 @@ __global__ void __launch_bounds__(192, 1)
           constexpr int kVecPerRow = 128 * kEl / 16;   // 16 (bf16) or 32 (fp32) vectors per token row
           const int tid = threadIdx.x - 64;
           const bool full_m = th.out_col0 + 128 <= p.m_valid && (p.ldo * kEl) % 16 == 0;
-          for (int e = tid; e < ((p.probe & 2) ? 0 : kCols * kVecPerRow); e += 128) {
+          for (int e = tid; e < kCols * kVecPerRow; e += 128) {
             const int j = e / kVecPerRow, vi = e % kVecPerRow;
             if (c0 + j >= th.b_valid) continue;
             const size_t orow = (size_t)(th.b_row0 + c0 + j) * p.ldo;
@@ -633,11 +643,17 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
                               cudaStream_t st) {
   using L = GemmSmem<BN, BM>;
   auto k = gemm_kernel<KIND, BN, EPI, GROUPED, BM>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  // the shared-memory attribute is a per-device setting of the function: set it
+  // once on every device this instantiation launches on
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit == 0 || !(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.fetch_or(bit, std::memory_order_release);
   }
   if (p.cluster_split && p.splits > 1) {
     // one CTA per (tile, split); the splits of a tile are one cluster
@@ -686,9 +702,17 @@ static cudaError_t dispatch_bn(int bn, int bm, const CUtensorMap& ta, const BMap
 // (clusters live inside one GPC, so this is below SMs / splits).  Cached.
 template <int KIND, int BN, int EPI, int BM = 128>
 static int cluster_cap(int splits) {
-  static int cache[9] = {0};
+  // per device: the answer depends on the GPU's SM and GPC layout
+  constexpr int kDevs = 64;
+  static std::atomic<int> cache[kDevs][9] = {};
   if (splits < 2 || splits > 8) return 0;
-  if (cache[splits]) return cache[splits];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  const int c = dev < kDevs ? cache[dev][splits].load(std::memory_order_relaxed) : 0;
+  if (c) return c;
   using L = GemmSmem<BN, BM>;
   auto k = gemm_kernel<KIND, BN, EPI, false, BM>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess) {
@@ -711,7 +735,7 @@ static int cluster_cap(int splits) {
     (void)cudaGetLastError();
     return 0;
   }
-  cache[splits] = n;
+  if (dev < kDevs) cache[dev][splits].store(n, std::memory_order_relaxed);
   return n;
 }
 

@@ -42,7 +42,6 @@ struct GemmParams {
   float* workspace;
   int* tile_counters;
   int cluster_split;
-  int probe;           // measurement only: bit 0 = no MMA (stages released as they land), bit 1 = no output stores
   // optional: after the last CTA has stored its tiles, publish the phase to every
   // peer (tensor-parallel partial sums read by the next kernel over NVLink)
   PeerSync pub;

@@ -289,6 +289,7 @@ cudaError_t argmax_rows(const float* logits, int T, int V, int ld, int* out, flo
                         float* out_val, int idx_base, cudaStream_t st);
 // stamps: [1 + 2 * ctas] u64 (see misc.cu)
 cudaError_t pdl_probe(unsigned long long* stamps, int ctas, unsigned long long ns, cudaStream_t st);
+cudaError_t ts_mark(unsigned long long* ring, int slot, cudaStream_t st);
 cudaError_t tp_argmax_merge(const PeerSync& s, const float* const* peer_val, const int* const* peer_idx, int T,
                             int* out, uint32_t* err, cudaStream_t st);
 cudaError_t markov_step(const float* logits, int ld, int blk, int i, const float* mlog, int mld, int V, int n,

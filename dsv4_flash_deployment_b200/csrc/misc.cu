@@ -65,6 +65,22 @@ cudaError_t pdl_probe(unsigned long long* stamps, int ctas, unsigned long long n
   return launch_pdl(pdl_probe_second, ctas, 32, 0, st, stamps);
 }
 
+// Device timestamp ring: one thread stores %globaltimer into ring[slot] after
+// the previous kernel on the stream has completed (griddepcontrol.wait waits for
+// the whole preceding grid and its memory operations).  Launched between op
+// groups of a captured step, the differences of consecutive slots are the
+// device time each group took inside a graph replay, on every rank at once.
+__global__ void ts_mark_kernel(unsigned long long* ring, int slot) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) ring[slot] = globaltimer_ns();
+}
+
+cudaError_t ts_mark(unsigned long long* ring, int slot, cudaStream_t st) {
+  launch_pdl(ts_mark_kernel, 1, 32, 0, st, ring, slot);
+  return cudaGetLastError();
+}
+
 // X[t, i, :] = table[ids[t], :] for every stream i (reference.py:909-911).
 __global__ void embed_streams_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids, int D,
                                      int hc, __nv_bfloat16* X) {

@@ -11,43 +11,22 @@
 // tile counters; this variant instead uses one scratch array that lives in the
 // library itself.
 //
-// Contract:
-//  * Scratch: a file-scope `static __device__` array of kScratchFloats floats
-//    for the split-K partial tiles plus kMaxTiles int32 tile counters
-//    (4 MiB + 16 KiB).  Every GPU that loads the library holds it until the
-//    process exits.
-//  * Set-up: the first call on a device looks up the array's device address
-//    with cudaGetSymbolAddress while that device is current.  That first call
-//    should happen before any stream capture starts.
-//  * Sharing: all calls on a device share the one array, which keeps the
-//    last call's contents.  Each call clears its tile counters before it
-//    launches.  Calls that overlap on the GPU (different streams, or different
-//    host threads on one device) race on the array and corrupt each other's
-//    results: serialize them.
-//  * Limits: problems whose split-K partials need more than kScratchFloats
-//    floats, or more than kMaxTiles output tiles, are rejected with return
-//    code DSV4_NOALLOC_TOO_LARGE and a message on stderr; nothing is launched.
-//  * No cudaMalloc, cudaFree or allocating library call is made.
-//
-// Arguments (all device pointers, row-major, the caller owns them):
-//   a      e4m3 weights [m, k] (m a multiple of 128)
-//   a_sf   ue8m0 scale chunks of a [m/128][k/128][512]
-//   b      e4m3 activations [b_rows, k] (b_rows >= n, a multiple of 128)
-//   b_sf   ue8m0 scale chunks of b [b_rows/128][k/128][512]
-//   out    bf16 [n, ldo]; out[t][j] = sum_k a[j][k] * b[t][k] for j < m
-//   err    one uint32 device word (0 on success; a kernel-side error code otherwise)
-// Returns 0 on success, DSV4_NOALLOC_TOO_LARGE, DSV4_NOALLOC_BAD_ARG, or a
-// cudaError_t value.
+// The public prototype, return codes, scratch limits and the full contract are
+// in dsv4_noalloc.h, which this file includes so the definition is checked
+// against it.
+#include <cuda.h>
+
 #include <cstdio>
 #include <mutex>
 
 #include "common.cuh"
+#include "dsv4_noalloc.h"
 #include "gemm.h"
 
 namespace {
 
-constexpr size_t kScratchFloats = size_t(1) << 20;  // 4 MiB of fp32 split-K partials
-constexpr int kMaxTiles = 4096;                      // tile counters (16 KiB)
+constexpr size_t kScratchFloats = DSV4_NOALLOC_SCRATCH_FLOATS;
+constexpr int kMaxTiles = DSV4_NOALLOC_MAX_TILES;
 constexpr int kMaxDevices = 64;
 
 struct ScratchArea {
@@ -57,26 +36,54 @@ struct ScratchArea {
 
 static __device__ __align__(256) ScratchArea g_scratch;
 
-ScratchArea* g_scratch_ptr[kMaxDevices] = {};
+// Looked-up address per device, valid for the context it was looked up in.
+struct ScratchSlot {
+  ScratchArea* ptr = nullptr;
+  CUcontext ctx = nullptr;
+};
+ScratchSlot g_slots[kMaxDevices];
 std::mutex g_setup_mutex;
 
-constexpr int DSV4_NOALLOC_TOO_LARGE = -1;
-constexpr int DSV4_NOALLOC_BAD_ARG = -2;
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 
-// Device address of this device's scratch array; looked up once per device.
+// cuCtxGetCurrent through the runtime (the library does not link libcuda).
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  CUcontext c = nullptr;
+  if (fn != nullptr && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
+
+// Device address of the scratch array in the current device's current context.
+// Looked up once, and again whenever the context differs from the one of the
+// last lookup (a reset device gets a new context).
 cudaError_t scratch_for_current_device(ScratchArea** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  // makes the runtime's context of this device current if no call has done so yet
+  // (cudaSetDevice initializes the primary context since CUDA 12)
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return e;
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchSlot& s = g_slots[dev];
+  if (s.ptr == nullptr || s.ctx != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_scratch);
     if (e != cudaSuccess) return e;
-    g_scratch_ptr[dev] = static_cast<ScratchArea*>(p);
+    s.ptr = static_cast<ScratchArea*>(p);
+    s.ctx = ctx;
   }
-  *out = g_scratch_ptr[dev];
+  *out = s.ptr;
   return cudaSuccess;
 }
 
@@ -86,7 +93,7 @@ extern "C" __attribute__((visibility("default"))) int dsv4_gemm_mx8_noalloc(
     const void* a, const void* a_sf, const void* b, const void* b_sf, void* out, int m, int n, int k, int b_rows,
     int ldo, int splits, void* err, cudaStream_t stream) {
   if (!a || !a_sf || !b || !b_sf || !out || !err || m <= 0 || n <= 0 || k <= 0 || m % 128 || k % 128 ||
-      b_rows < n || b_rows % 128 || splits < 1 || ldo < m) {
+      b_rows < n || b_rows % 128 || splits < 1 || splits > k / 128 || ldo < m) {
     std::fprintf(stderr, "dsv4_gemm_mx8_noalloc: invalid arguments (m=%d n=%d k=%d b_rows=%d ldo=%d splits=%d)\n", m,
                  n, k, b_rows, ldo, splits);
     return DSV4_NOALLOC_BAD_ARG;

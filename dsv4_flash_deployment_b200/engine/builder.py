@@ -23,7 +23,7 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
                 ep=None, tp=None, experts_from: DSV4Model | None = None, kv_block: int = 0,
                 kv_pool_tokens: int = 0, engram_from: DSV4Model | None = None,
-                engram_shm: str | None = None) -> DSV4Model:
+                engram_shm: str | None = None, engram_token_map=None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -42,6 +42,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     uses instead of building its own; it must have at least as many slots and
     step tokens, and the two models must not step concurrently.  ``engram_shm``:
     random-init Engram tables in shared files with this prefix (one copy per node).
+    ``engram_token_map``: the tokenizer's compressed token map for the Engram
+    hashes (``ref.engram.compressed_token_map``; None: ``id % C``).
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -92,5 +94,5 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     elif cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
         model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed,
-                                     shm_prefix=engram_shm)
+                                     shm_prefix=engram_shm, token_map=engram_token_map)
     return model

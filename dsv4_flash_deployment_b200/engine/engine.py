@@ -48,19 +48,20 @@ class Engine:
               weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None, ep=None,
               use_graphs: bool = True, chunk_size: int | None = None, extra_slots: int = 0, tp=None,
               experts_from=None, kv_block: int = 0, kv_pool_tokens: int = 0, engram_from=None,
-              engram_shm: str | None = None) -> "Engine":
+              engram_shm: str | None = None, engram_token_map=None) -> "Engine":
         """``extra_slots`` cache slots beyond ``max_seqs`` are kept out of the scheduler
         (the multi-rank control plane runs its 1-token join steps on one).  ``tp``:
         tensor-parallel group (every rank runs the same steps).  ``experts_from``: a
         model whose expert blocks this one shares (same expert ownership per rank).
         ``kv_block`` / ``kv_pool_tokens``: paged compressed caches (admission then
-        also waits for free blocks)."""
+        also waits for free blocks).  ``engram_token_map``: compressed token map of
+        the tokenizer for the Engram hashes (None: ``id % C``)."""
         from .builder import build_model
         model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs + extra_slots,
                             max_seq_len=max_seq_len, weights=weights, seed=seed,
                             expert_storage_layers=expert_storage_layers, ep=ep, tp=tp, experts_from=experts_from,
                             kv_block=kv_block, kv_pool_tokens=kv_pool_tokens, engram_from=engram_from,
-                            engram_shm=engram_shm)
+                            engram_shm=engram_shm, engram_token_map=engram_token_map)
         return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs)
 
     # ------------------------------------------------------------------- API

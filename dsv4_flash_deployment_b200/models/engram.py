@@ -123,12 +123,14 @@ class HostTable:
 
 class EngramRuntime:
     def __init__(self, cfg, dev, n_slots: int, max_tokens: int, ext, weights: dict | None = None, seed: int = 0,
-                 shm_prefix: str | None = None):
+                 shm_prefix: str | None = None, token_map=None):
         """``shm_prefix`` (random init only): keep the tables in shared files
         ``<shm_prefix>.l<layer>.{q,sf}`` that every process of the node maps (one
-        copy per node instead of one per rank; see :func:`shared_table`)."""
+        copy per node instead of one per rank; see :func:`shared_table`).
+        ``token_map``: token id -> compressed id (``ref.engram.compressed_token_map``
+        of the checkpoint's tokenizer); None: ``id % C``."""
         self.cfg, self.dev, self.ext = cfg, dev, ext
-        h = EngramHasher(cfg)
+        h = EngramHasher(cfg, token_map=token_map)
         lay = h.layout
         self.nl, self.N, self.H, self.hd = len(lay.layer_ids), lay.max_ngram, lay.n_heads, lay.head_dim
         self.cols = (self.N - 1) * self.H

@@ -329,11 +329,16 @@ class DSV4Model:
     op_timer: dict | None = None
     engram = None            # EngramRuntime for configs with Engram layers
 
+    dev_trace = None         # utils.devtrace.DeviceTrace: a timestamp mark after every op group
+
     @contextlib.contextmanager
     def _t(self, name: str):
-        """CUDA-event timing of one op group (eager runs only; off by default)."""
+        """CUDA-event timing of one op group (eager runs only; off by default), or a
+        device timestamp mark at its end (``dev_trace``; captured with the step)."""
         if self.op_timer is None:
             yield
+            if self.dev_trace is not None:
+                self.dev_trace.mark(name)
             return
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
@@ -709,13 +714,13 @@ class DSV4Model:
         c13.__enter__()
         ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                  self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, 0, None)
+                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
         split = self.tp is not None and self.tp.moe == "tp"   # f32 partial rows, summed over ranks
         ext.gemm(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm,
                  ex.w2.q.shape[0],
-                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1, 0,
+                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1,
                  self.tp.sync(1) if self.tp is not None else None)
         c2.__exit__(None, None, None)

@@ -117,16 +117,15 @@ def pick_bn(n_tokens: int) -> int:
 def gemm_mx(xq: torch.Tensor, xsf: torch.Tensor, n_tokens: int, w: MxWeight, out: torch.Tensor,
             epi: int = EPI_BF16, splits: int = 1, workspace=None, counters=None, row_scale=None,
             hq=None, hsf=None, swiglu_limit: float = 0.0, bn: int | None = None, max_grid: int = 0,
-            probe: int = 0, publish=None) -> torch.Tensor:
-    """out[t, :n] = dequant(x) @ dequant(w).T for t < n_tokens (CUDA).  ``probe`` is a
-    measurement switch (1: skip the MMAs, 2: skip the output stores); 0 in real use.
+            publish=None) -> torch.Tensor:
+    """out[t, :n] = dequant(x) @ dequant(w).T for t < n_tokens (CUDA).
     ``publish``: peer-sync descriptor (``parallel.tp``) published once every tile is stored."""
     bn = bn or pick_bn(n_tokens)
     ext = _ext.load()
     ext.gemm(w.kind, epi, w.q, w.sf, xq, xsf, out if epi != EPI_SWIGLU else None, w.q.shape[0], n_tokens, w.k,
              bn, splits, None, None, row_scale, hq, hsf, swiglu_limit, w.n,
              out.stride(0) if out is not None else 0, workspace, counters, ErrorWord.get(xq.device), max_grid, 1,
-             probe, publish)
+             publish)
     return out
 
 
@@ -143,7 +142,7 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, f32_out: bool
     bn = bn or pick_bn(t)
     _ext.load().gemm(KIND_BF16, EPI_F32 if f32_out else EPI_BF16, w, None, x, None, out, w.shape[0], t, k, bn,
                      splits, None, None, None, None, None, 0.0, m_valid or out.shape[1], out.stride(0), workspace,
-                     counters, ErrorWord.get(x.device), 0, groups, 0, publish)
+                     counters, ErrorWord.get(x.device), 0, groups, publish)
     return out
 
 

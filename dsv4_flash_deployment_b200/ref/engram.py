@@ -3,7 +3,10 @@
 States the hashing contract of the reference's ``engram_hash.py``
 (``models/DeepSeekV4.1-Flash-v6e16/tpu-v7x/deepseek_v41/engram_hash.py:29-333``):
 
-* a compressed token map (``id % C`` without a tokenizer),
+* a compressed token map: with a tokenizer, tokens whose decoded text
+  normalizes to the same key share one compressed id (ids assigned in token-id
+  order of first appearance, :func:`compressed_token_map`); without one,
+  ``id % C``,
 * per Engram layer, per n-gram order (2..max) and per head, a distinct prime
   modulus drawn in order layer -> order -> head, starting above
   ``engram_vocab_size - 1``; row offsets are the running sum of the primes,
@@ -16,11 +19,106 @@ This module is the oracle for the native hasher in ``csrc/engram``.
 
 from __future__ import annotations
 
+import re
+import unicodedata
 from dataclasses import dataclass
+from pathlib import Path
 
 import numpy as np
 
 DEFAULT_COMPRESSED_VOCAB = 99092
+
+_WS_RUN = re.compile(r"[ \t\r\n]+")
+# characters with the Unicode White_Space property (what the strip removes;
+# Python's own str.strip also removes U+001C..U+001F, which are not in it)
+_WHITE_SPACE = "\t\n\x0b\x0c\r \x85\xa0\u1680" + "".join(map(chr, range(0x2000, 0x200B))) + \
+    "\u2028\u2029\u202f\u205f\u3000"
+
+
+def _fold_py(text: str) -> str:
+    """The token-key normalization, restated with :mod:`unicodedata`.
+
+    Compatibility composition (NFKC), then canonical decomposition (NFD) with
+    the non-spacing marks dropped (accents), lowercase, every run of spaces,
+    tabs and newlines collapsed to one space, and outer whitespace stripped --
+    except that a text that is exactly one space stays one space.
+    """
+    s = unicodedata.normalize("NFD", unicodedata.normalize("NFKC", text))
+    # marks dropped (non-spacing and enclosing); lowercase one character at a
+    # time (no context-dependent final sigma)
+    s = "".join(ch.lower() for ch in s if unicodedata.category(ch) not in ("Mn", "Me"))
+    s = _WS_RUN.sub(" ", s)
+    return s if s == " " else s.strip(_WHITE_SPACE)
+
+
+def _fold_fn():
+    """The normalizer that produced the trained tables' keys: the HuggingFace
+    ``tokenizers`` normalizer sequence when that package is present (its Unicode
+    tables and whitespace rules are the ones the checkpoint was built with),
+    else the :mod:`unicodedata` restatement (which agrees with it except on
+    characters whose Unicode properties differ between the two libraries'
+    Unicode versions)."""
+    try:
+        from tokenizers import Regex, normalizers
+    except ImportError:
+        return _fold_py
+    keep = "\ue000"   # private-use placeholder: a lone space survives the strip
+    seq = normalizers.Sequence([
+        normalizers.NFKC(), normalizers.NFD(), normalizers.StripAccents(), normalizers.Lowercase(),
+        normalizers.Replace(Regex(r"[ \t\r\n]+"), " "), normalizers.Replace(Regex(r"^ $"), keep),
+        normalizers.Strip(), normalizers.Replace(keep, " "),
+    ])
+    return seq.normalize_str
+
+
+def _backend(tok):
+    """(decode(id) -> str, token string of id, vocabulary size) of a tokenizer."""
+    if isinstance(tok, (str, Path)):
+        from tokenizers import Tokenizer
+        p = Path(tok)
+        if p.is_dir():
+            p = p / "tokenizer.json"
+        tok = Tokenizer.from_file(str(p))
+        n = tok.get_vocab_size(with_added_tokens=True)
+    elif hasattr(tok, "backend_tokenizer"):            # transformers fast tokenizer
+        n = len(tok)
+        tok = tok.backend_tokenizer
+    else:
+        n = tok.get_vocab_size(with_added_tokens=True) if hasattr(tok, "get_vocab_size") else len(tok)
+    return (lambda i: tok.decode([i], skip_special_tokens=False)), tok.id_to_token, int(n)
+
+
+def compressed_token_map(tokenizer=None, vocab_size: int = 129280,
+                         compressed_vocab: int | None = None) -> tuple[np.ndarray, int]:
+    """Token id -> compressed id table and the compressed vocabulary size.
+
+    With a tokenizer (a ``tokenizer.json`` path or its directory, a
+    ``tokenizers.Tokenizer``, a transformers fast tokenizer, or any object with
+    ``decode``, ``id_to_token`` and a vocabulary size), each token's key is its
+    decoded text after the normalization of :func:`_fold_fn`; a token that
+    decodes to a partial UTF-8 sequence (U+FFFD in the text) keys on its raw
+    token string instead, and one whose key normalizes to nothing keeps its
+    text.  Keys get compressed ids in token-id order of first appearance.
+    Behaviour of ``engram_hash.py:74-140``
+    (``models/DeepSeekV4.1-Flash-v6e16/tpu-v7x/deepseek_v41/``).  Without a
+    tokenizer: ``id % C`` with C = ``compressed_vocab`` (default 99092 for the
+    129280-token vocabulary, else the vocabulary size).
+    """
+    if tokenizer is None:
+        c = int(compressed_vocab or (DEFAULT_COMPRESSED_VOCAB if vocab_size == 129280 else vocab_size))
+        return np.arange(vocab_size, dtype=np.int64) % c, c
+    decode, raw, n = _backend(tokenizer)
+    fold = _fold_fn()
+    ids: dict[str, int] = {}
+    table = np.empty(n, dtype=np.int64)
+    for t in range(n):
+        text = decode(t)
+        if "\ufffd" in text:
+            key = raw(t)
+        else:
+            key = fold(text) or text
+        table[t] = ids.setdefault(key, len(ids))
+    return table, len(ids)
 
 
 def _is_prime(n: int) -> bool:
@@ -112,8 +210,7 @@ class EngramHasher:
         if self.layout is None:
             raise ValueError("config has no Engram layers")
         if token_map is None:
-            c = compressed_vocab or (DEFAULT_COMPRESSED_VOCAB if cfg.vocab_size == 129280 else cfg.vocab_size)
-            token_map = np.arange(cfg.vocab_size, dtype=np.int64) % c
+            token_map, c = compressed_token_map(None, cfg.vocab_size, compressed_vocab)
         else:
             c = int(token_map.max()) + 1
         self.compressed_vocab = c

@@ -30,7 +30,29 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
                         max_seq_len=ec.max_model_len, weights=_load_weights(ec, cfg), seed=ec.seed,
                         expert_storage_layers=ec.expert_storage_layers, ep=ep, use_graphs=ec.use_cuda_graphs,
                         chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp, kv_block=ec.kv_block,
-                        kv_pool_tokens=ec.kv_pool_tokens, engram_shm=ec.engram_shm)
+                        kv_pool_tokens=ec.kv_pool_tokens, engram_shm=ec.engram_shm,
+                        engram_token_map=_engram_token_map(ec, cfg))
+
+
+def _engram_token_map(ec: EngineConfig, cfg):
+    """Engram hashes key on the tokenizer's normalized token texts when the served
+    tokenizer has a ``tokenizer.json`` (the checkpoint's tables were built that way)."""
+    if not cfg.engram_layer_ids or not ec.tokenizer:
+        return None
+    from pathlib import Path
+
+    p = Path(ec.tokenizer)
+    if p.is_dir():
+        p = p / "tokenizer.json"
+    if not p.exists():
+        return None
+    from ..ref.engram import compressed_token_map
+
+    table, _ = compressed_token_map(str(p))
+    if len(table) < cfg.vocab_size:   # ids the tokenizer never produces keep a map entry
+        import numpy as np
+        table = np.concatenate([table, np.arange(len(table), cfg.vocab_size, dtype=np.int64) % (table.max() + 1)])
+    return table[:cfg.vocab_size]
 
 
 def _load_weights(ec: EngineConfig, cfg):
