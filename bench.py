@@ -150,7 +150,7 @@ def main() -> None:
     ap.add_argument("--c1-moe", default="ep", choices=["ep", "tp"],
                     help="experts in the tensor-parallel C=1 model: owned whole (ep, shared with the batch model) "
                          "or split by intermediate index over all GPUs (tp)")
-    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl", "fused"],
                     help="expert exchange: NVLink peer stores (p2p) or the NCCL all-to-all baseline")
     args = ap.parse_args()
     if args.impl == "reference":

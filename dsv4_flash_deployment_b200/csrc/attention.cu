@@ -391,11 +391,10 @@ size_t attn_smem_bytes() { return kSmemTotal; }
 cudaError_t attention(const AttnParams& p, int nsplit, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
   if (p.n_heads < 1 || p.n_heads > kH) return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+  static std::atomic<uint64_t> smem_set{0};
+  {
+    const cudaError_t e = smem_attr_once(attn_kernel, (int)kSmemTotal, smem_set);
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   dim3 grid(p.T, nsplit);
   launch_pdl(attn_kernel, grid, 256, kSmemTotal, st, p);

@@ -97,7 +97,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
           const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
           double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
           const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
-          const optional<Tensor>& publish) {
+          const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -171,6 +171,16 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.tile_counters = counters ? counters->data_ptr<int>() : nullptr;
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
   p.pub = peer_sync_of(publish);
+  if (ret_meta || ret_peer) {
+    TORCH_CHECK(ret_meta && ret_peer && grouped && epi == dsv4::EPI_BF16, "return rows: grouped bf16 GEMMs with both tables");
+    TORCH_CHECK(ret_meta->is_cuda() && ret_meta->scalar_type() == at::kInt && ret_meta->numel() >= B.size(0),
+                "ret_meta: int32 device [B rows]");
+    TORCH_CHECK(ret_peer->is_cuda() && ret_peer->scalar_type() == at::kLong, "ret_peer: int64 device pointer table");
+    TORCH_CHECK(M % 128 == 0 && m_valid % 128 == 0 && (ldo * 2) % 16 == 0,
+                "return rows: whole 128-row tiles, 16-byte rows");
+    p.ret_meta = ret_meta->data_ptr<int>();
+    p.ret_peer = reinterpret_cast<__nv_bfloat16* const*>(ret_peer->data_ptr<int64_t>());
+  }
   if (p.splits > 1 && !(workspace && counters)) {
     // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
     // Halve the split count until every tile's cluster is resident at once.
@@ -305,9 +315,10 @@ void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>&
     p.err = reinterpret_cast<uint32_t*>(err->data_ptr<int>());
     TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr
                 : p.tp_mode == 3 ? (p.peer_y != nullptr && p.peer_pos != nullptr && topk > 0)
+                : p.tp_mode == 4 ? (p.yperm != nullptr && p.pos != nullptr && topk > 0)
                                  : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
                 "tp mode tables missing");
-    TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 3, "tp mode must be 1, 2 or 3");
+    TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 4, "tp mode must be 1 .. 4");
   }
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));
@@ -578,6 +589,73 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, 
                                 (int)my_rank, (int)world, ep_sync(sync, 1), cur_stream()));
 }
 
+// Fused expert-parallel dispatch.  tables: int64 CPU [5] = device addresses of
+// the [world] pointer tables (expert rows, their scale chunks, row weights, row
+// origins, per-expert counters) of every rank; pub: PeerSync of phase 0.
+void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
+                 double route_scale, const optional<Tensor>& ids, const optional<Tensor>& wts, const Tensor& xq,
+                 const Tensor& xsf, int64_t e_local, int64_t cap_e, const Tensor& tables, const Tensor& err,
+                 const Tensor& pub) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
+                  logits.stride(0) == logits.size(1), "logits: f32 [T, E] contiguous");
+  TORCH_CHECK(!tables.is_cuda() && tables.scalar_type() == at::kLong && tables.numel() == 5, "tables: int64 CPU [5]");
+  TORCH_CHECK(xq.size(0) >= T && xq.size(1) % 128 == 0, "xq: [>= T, D]");
+  TORCH_CHECK(ids.has_value() == wts.has_value(), "ids and wts together");
+  const int64_t* tb = tables.data_ptr<int64_t>();
+  dsv4::EpDispatchParams p{};
+  p.logits = logits.data_ptr<float>();
+  p.bias = ptr<const float>(bias);
+  p.T = (int)T;
+  p.E = (int)logits.size(1);
+  p.topk = (int)topk;
+  p.score_func = (int)score_func;
+  p.route_scale = (float)route_scale;
+  p.ids = ptr<int>(ids);
+  p.wts = ptr<float>(wts);
+  p.xq = ptr<const uint8_t>(xq);
+  p.xsf = ptr<const uint8_t>(xsf);
+  p.D = (int)xq.size(1);
+  p.e_local = (int)e_local;
+  p.cap_e = (int)cap_e;
+  p.peer_x = reinterpret_cast<uint8_t* const*>(tb[0]);
+  p.peer_xsf = reinterpret_cast<uint8_t* const*>(tb[1]);
+  p.peer_rscale = reinterpret_cast<float* const*>(tb[2]);
+  p.peer_meta = reinterpret_cast<int* const*>(tb[3]);
+  p.peer_cnt = reinterpret_cast<int* const*>(tb[4]);
+  p.err = ptr<uint32_t>(err);
+  p.pub = peer_sync_of(pub);
+  p.world = p.pub.world;
+  p.rank = p.pub.rank;
+  TORCH_CHECK(p.pub.done != nullptr && p.E == p.e_local * p.world, "dispatch: phase-0 sync and E = e_local * world");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  CUDA_OK(dsv4::ep_dispatch(p, cur_stream()));
+}
+
+// wait: PeerSync of phase 0; tiles: int32 [max, 4]; cnt: this rank's counters [e_local]
+void ep_plan(const Tensor& wait, const Tensor& cnt, int64_t cap_e, int64_t tile_rows, int64_t m13, int64_t m2,
+             const Tensor& tiles13, const Tensor& nt13, const Tensor& tiles2, const Tensor& nt2, const Tensor& err) {
+  CHECK_CUDA(cnt);
+  TORCH_CHECK(tiles13.dim() == 2 && tiles13.size(1) == 4 && tiles2.dim() == 2 && tiles2.size(1) == 4, "tiles [n, 4]");
+  dsv4::EpPlanParams p{};
+  p.wait = peer_sync_of(wait);
+  p.cnt = cnt.data_ptr<int>();
+  p.e_local = (int)cnt.numel();
+  p.cap_e = (int)cap_e;
+  p.tile_rows = (int)tile_rows;
+  p.m13 = (int)m13;
+  p.m2 = (int)m2;
+  p.tiles13 = reinterpret_cast<int4*>(tiles13.data_ptr<int>());
+  p.n_tiles13 = nt13.data_ptr<int>();
+  p.tiles2 = reinterpret_cast<int4*>(tiles2.data_ptr<int>());
+  p.n_tiles2 = nt2.data_ptr<int>();
+  p.max_tiles13 = (int)tiles13.size(0);
+  p.max_tiles2 = (int)tiles2.size(0);
+  p.err = ptr<uint32_t>(err);
+  const c10::cuda::CUDAGuard guard(cnt.device());
+  CUDA_OK(dsv4::ep_plan(p, cur_stream()));
+}
+
 // tables: int64 CPU tensor [nl, 3] = (device-mapped table address, scale table address, n_emb)
 void engram_prepare(const Tensor& ids, const Tensor& pos, const Tensor& slot, const Tensor& chunk_start,
                     const Tensor& step_row0, const Tensor& last_pos, int64_t T, const Tensor& token_map,
@@ -750,6 +828,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_unpack_meta", &ep_unpack_meta);
   m.def("ep_unpack_rows", &ep_unpack_rows);
   m.def("ep_combine_pack", &ep_combine_pack);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_plan", &ep_plan);
   m.def("argmax_rows", &argmax_rows);
   m.def("tp_argmax_merge", &tp_argmax_merge);
   m.def("pdl_probe", &pdl_probe);

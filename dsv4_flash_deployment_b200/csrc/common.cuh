@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 #include <vector>
 
@@ -388,6 +389,20 @@ __host__ __device__ inline size_t sf_chunk_offset(int row, int kblk, int k_tiles
   const int rt = row >> 7, m = row & 127;
   const int kt = kblk >> 2, j = kblk & 3;
   return ((size_t)rt * k_tiles + kt) * 512 + (size_t)((m & 31) * 16 + (m >> 5) * 4 + j);
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device, once per
+// device (the attribute is per device; `done` is the kernel's own bit mask).
+template <typename Kernel>
+inline cudaError_t smem_attr_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
 }
 
 }  // namespace dsv4

@@ -14,6 +14,7 @@
 // buffer).
 #include "common.cuh"
 #include "kernels.h"
+#include "moe_route.cuh"
 #include "peer.cuh"
 
 #include <algorithm>
@@ -210,6 +211,172 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const in
   if (n == 0 && sync.done == nullptr) return cudaSuccess;
   const unsigned grid = (unsigned)std::min<long long>(kEpGrid, std::max(1LL, (n * 32 + 255) / 256));
   launch_pdl(ep_combine_pack_kernel, grid, 256, 0, st, yperm, pos, cnt, D, cap, back, peer_back, my_rank, world, sync);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- fused path
+// Expert-parallel MoE in three kernels per layer instead of a pack / exchange /
+// unpack / plan / combine chain:
+//
+//   ep_dispatch  router top-k of each token (one warp per token), then each
+//                routed pair claims a row of its expert on the owning rank with
+//                a system-scope atomic on the owner's per-expert counter and
+//                stores the token's MXFP8 row, its scale words, the routing
+//                weight and the pair's origin straight into the owner's expert
+//                rows (symmetric memory, NVLink stores); the last CTA publishes
+//                phase 0.  Expert e of a rank owns rows [e * cap_e, (e+1) * cap_e)
+//                (cap_e >= every token of every rank), so no prefix sum over
+//                sources is needed and no row is ever copied twice.
+//   ep_plan      one CTA: bounded wait until every rank has published phase 0,
+//                the W13 / W2 tile lists from the per-expert counts, counters
+//                back to zero for the next layer.
+//   grouped W13 (SwiGLU epilogue, the routing weight folded in) and grouped W2
+//                whose epilogue stores each output row into the source rank's
+//                return buffer at the pair's index and publishes phase 1; the
+//                next mHC boundary kernel waits for phase 1 and sums the pairs.
+//
+// Counter reuse: a rank reaches the next layer's dispatch only after every
+// owner's W2 of this layer has published, and every owner's ep_plan (which
+// zeroed the counters) precedes its W2 in stream order.
+template <int kMaxPer>
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
+  pdl_entry();
+  const int warp = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int D = p.D;
+  const int kt = D / 128;
+  if (warp < p.T) {
+    const int t = warp;
+    int id;
+    float w;
+    route_token<kMaxPer>(p.logits + (size_t)t * p.E, p.E, p.bias, p.topk, p.score_func, p.route_scale, lane, id, w);
+    int owner = 0, row = -1;
+    if (lane < p.topk) {
+      if (p.ids) {
+        p.ids[(size_t)t * p.topk + lane] = id;
+        p.wts[(size_t)t * p.topk + lane] = w;
+      }
+      owner = id / p.e_local;
+      const int le = id - owner * p.e_local;
+      const int slot = atomicAdd_system(p.peer_cnt[owner] + le, 1);
+      if (slot < p.cap_e) {
+        row = le * p.cap_e + slot;
+      } else {
+        report_error(p.err, ERR_CAPACITY, KID_MOE, 3);
+      }
+    }
+    // the token's row (D bytes) and scale words (one 4-byte word per 128 columns)
+    // are loaded once and stored to each of the k owners
+    constexpr int kVec = 8;   // uint4 per lane for D <= 4096
+    uint4 v[kVec];
+    const int nvec = D / 16;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i)
+      if (lane + 32 * i < nvec) v[i] = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D)[lane + 32 * i];
+    uint32_t sfw = 0;
+    const int m_src = t & 127;
+    if (lane < kt)
+      sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + lane) * 512 + (m_src & 31) * 16 +
+                                                 (m_src >> 5) * 4);
+    for (int j = 0; j < p.topk; ++j) {
+      const int o = __shfl_sync(0xffffffffu, owner, j);
+      const int r = __shfl_sync(0xffffffffu, row, j);
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      if (r < 0) continue;
+      uint4* dst = reinterpret_cast<uint4*>(p.peer_x[o] + (size_t)r * D);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i)
+        if (lane + 32 * i < nvec) dst[lane + 32 * i] = v[i];
+      if (lane < kt) {
+        const int m = r & 127;
+        *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + lane) * 512 + (m & 31) * 16 +
+                                     (m >> 5) * 4) = sfw;
+      }
+      if (lane == 0) {
+        p.peer_rscale[o][r] = wj;
+        p.peer_meta[o][r] = (p.rank << 24) | (t * p.topk + j);
+      }
+    }
+  }
+  peer_publish_grid(p.pub);
+}
+
+cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st) {
+  if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D > 4096 || p.D / 128 > 32) return cudaErrorInvalidValue;
+  if ((long long)p.T * p.topk >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)std::max(1, (p.T * 32 + 255) / 256);   // every rank publishes, even with T = 0
+  const int per = (p.E + 31) / 32;
+#define DSV4_DISPATCH(P) launch_pdl(ep_dispatch_kernel<P>, grid, 256, 0, st, p)
+  if (per <= 2) DSV4_DISPATCH(2);
+  else if (per <= 4) DSV4_DISPATCH(4);
+  else if (per <= 8) DSV4_DISPATCH(8);
+  else if (per <= 12) DSV4_DISPATCH(12);
+  else DSV4_DISPATCH(16);
+#undef DSV4_DISPATCH
+  return cudaGetLastError();
+}
+
+// One CTA of 1024 threads (one expert per thread, e_local <= 1024).
+__global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
+  pdl_entry();
+  peer_wait(p.wait, p.err, KID_COMM);
+  __shared__ int s_wt[32];
+  __shared__ int s_ok;
+  const int e = threadIdx.x;
+  const int lane = e & 31, w = e >> 5;
+  int c = 0;
+  if (e < p.e_local) {
+    c = p.cnt[e];
+    if (c > p.cap_e) c = p.cap_e;   // dispatch reported the overflow; rows beyond cap_e were not written
+    p.cnt[e] = 0;                   // re-armed for the next layer (see the counter-reuse note above)
+  }
+  const int tl = (c + p.tile_rows - 1) / p.tile_rows;
+  int it = tl;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int b = __shfl_up_sync(0xffffffffu, it, o);
+    if (lane >= o) it += b;
+  }
+  if (lane == 31) s_wt[w] = it;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = (int)(blockDim.x >> 5);
+    int vt = lane < nw ? s_wt[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int b = __shfl_up_sync(0xffffffffu, vt, o);
+      if (lane >= o) vt += b;
+    }
+    s_wt[lane] = vt;
+  }
+  __syncthreads();
+  const int toff = (w > 0 ? s_wt[w - 1] : 0) + it - tl;
+  const int mt13 = p.m13 / 128, mt2 = p.m2 / 128;
+  if (e == 0) {
+    const int total = s_wt[31];
+    const bool ok = total * mt13 <= p.max_tiles13 && total * mt2 <= p.max_tiles2;
+    if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 4);
+    s_ok = ok;
+    *p.n_tiles13 = ok ? total * mt13 : 0;
+    *p.n_tiles2 = ok ? total * mt2 : 0;
+  }
+  __syncthreads();
+  if (!s_ok || e >= p.e_local) return;
+  int rt = toff;
+  for (int r0 = 0; r0 < c; r0 += p.tile_rows, ++rt) {
+    const int valid = min(p.tile_rows, c - r0);
+    const int b0 = e * p.cap_e + r0;
+    for (int mt = 0; mt < mt13; ++mt)
+      p.tiles13[(size_t)rt * mt13 + mt] = make_int4(e * p.m13 + mt * 128, b0, valid, mt * 128);
+    for (int mt = 0; mt < mt2; ++mt)
+      p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, b0, valid, mt * 128);
+  }
+}
+
+cudaError_t ep_plan(const EpPlanParams& p, cudaStream_t st) {
+  if (p.e_local < 1 || p.e_local > 1024 || p.cap_e % 256 || p.tile_rows % 128 || p.m13 % 128 || p.m2 % 128)
+    return cudaErrorInvalidValue;
+  launch_pdl(ep_plan_kernel, 1, 1024, 0, st, p);
   return cudaGetLastError();
 }
 

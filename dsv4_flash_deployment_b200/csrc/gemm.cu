@@ -583,7 +583,13 @@ __global__ void __launch_bounds__(192, 1)
             if (c0 + j >= th.b_valid) continue;
             const size_t orow = (size_t)(th.b_row0 + c0 + j) * p.ldo;
             const uint4 val = reinterpret_cast<const uint4*>(stage + (size_t)j * 128 * kEl)[vi];
-            if (full_m) {
+            if (GROUPED && p.ret_meta != nullptr) {
+              // expert-parallel return: straight into the source rank's buffer (NVLink)
+              const int mt = __ldg(p.ret_meta + th.b_row0 + c0 + j);
+              uint8_t* dst = reinterpret_cast<uint8_t*>(p.ret_peer[mt >> 24]) +
+                             ((size_t)(mt & 0xffffff) * p.ldo + th.out_col0) * kEl;
+              reinterpret_cast<uint4*>(dst)[vi] = val;
+            } else if (full_m) {
               reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (orow + th.out_col0) * kEl)[vi] = val;
             } else {
               const int m0 = th.out_col0 + vi * (16 / kEl);
@@ -646,14 +652,9 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
   // the shared-memory attribute is a per-device setting of the function: set it
   // once on every device this instantiation launches on
   static std::atomic<uint64_t> configured{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
-  if (bit == 0 || !(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  {
+    const cudaError_t e = smem_attr_once(k, L::kTotal, configured);
     if (e != cudaSuccess) return e;
-    configured.fetch_or(bit, std::memory_order_release);
   }
   if (p.cluster_split && p.splits > 1) {
     // one CTA per (tile, split); the splits of a tile are one cluster

@@ -1,6 +1,7 @@
 // Host-visible interface of the tcgen05 GEMM (gemm.cu).
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -45,6 +46,12 @@ struct GemmParams {
   // optional: after the last CTA has stored its tiles, publish the phase to every
   // peer (tensor-parallel partial sums read by the next kernel over NVLink)
   PeerSync pub;
+  // optional (grouped, bf16 output): output row b goes to row (ret_meta[b] &
+  // 0xffffff) of rank (ret_meta[b] >> 24)'s return buffer ret_peer[rank] (row
+  // stride ldo) instead of out -- the expert-parallel combine stores each expert
+  // row straight into the source rank's memory over NVLink
+  const int* ret_meta;
+  __nv_bfloat16* const* ret_peer;
   uint32_t* err;
 };
 

@@ -267,11 +267,11 @@ cudaError_t indexer_topk(const IdxParams& p, uint32_t* keys, int keys_ld, cudaSt
   const size_t smem = 256 * 4 + (size_t)(p.max_c + p.max_c / max(1, p.cand_block) + 1) * 4;
   // dynamic + the kernel's static shared memory must stay under the 227 KB opt-in limit
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  static size_t configured = 48 * 1024;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(idx_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 48 * 1024) {
+    // the limit is raised to the largest size this binding accepts, once per device
+    static std::atomic<uint64_t> smem_set{0};
+    const cudaError_t e = smem_attr_once(idx_select_kernel, 220 * 1024, smem_set);
     if (e != cudaSuccess) return e;
-    configured = smem;
   }
   launch_pdl(idx_select_kernel, p.T, 256, smem, st, p, keys, keys_ld);
   return cudaGetLastError();

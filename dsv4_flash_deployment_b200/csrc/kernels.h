@@ -61,7 +61,9 @@ struct HcParams {
   // (peer_yperm / peer_pos; ids are identical on every rank); tp_mode 3 = experts
   // split by intermediate index: every rank's f32 partial row of each pair
   // (peer_y tables, at row peer_pos[rank][t, slot] of that rank's own plan)
-  // summed in rank order.  All wait first
+  // summed in rank order; tp_mode 4 = expert parallelism with rows returned by
+  // the owners' W2 epilogues: the local yperm / pos combine once every rank has
+  // published the phase.  All wait first
   // (bounded) until every rank has published the phase.
   int tp_mode;
   const float* const* peer_y;
@@ -250,6 +252,41 @@ cudaError_t ep_unpack_rows(const uint8_t* recv, const int* cnt, int world, int c
 cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const int* cnt, int D, int cap,
                             __nv_bfloat16* back, __nv_bfloat16* const* peer_back, int my_rank, int world,
                             const EpSync& sync, cudaStream_t st);
+
+// Fused expert-parallel path (ep.cu): router top-k + direct stores into the
+// owners' expert rows, then a one-CTA plan that waits for every rank.
+struct EpDispatchParams {
+  const float* logits;        // [T, E] router logits (fp32)
+  const float* bias;          // [E] selection bias (optional)
+  int T, E, topk, score_func;
+  float route_scale;
+  int* ids;                   // optional local copy of the routing [T, topk]
+  float* wts;
+  const uint8_t* xq;          // [>= T, D] e4m3 token rows
+  const uint8_t* xsf;         // their scale chunks
+  int D, e_local, cap_e, world, rank;
+  uint8_t* const* peer_x;     // [world] expert rows [e_local * cap_e, D] of each rank
+  uint8_t* const* peer_xsf;   // [world] their scale chunks
+  float* const* peer_rscale;  // [world] routing weight per expert row
+  int* const* peer_meta;      // [world] (source rank << 24) | pair index per expert row
+  int* const* peer_cnt;       // [world] rows claimed per local expert (zero at rest)
+  uint32_t* err;
+  PeerSync pub;               // phase 0
+};
+cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st);
+
+struct EpPlanParams {
+  PeerSync wait;              // phase 0
+  int* cnt;                   // this rank's counters [e_local]
+  int e_local, cap_e, tile_rows, m13, m2;
+  int4* tiles13;
+  int* n_tiles13;
+  int4* tiles2;
+  int* n_tiles2;
+  int max_tiles13, max_tiles2;
+  uint32_t* err;
+};
+cudaError_t ep_plan(const EpPlanParams& p, cudaStream_t st);
 
 // ------------------------------------------------------------ engram.cu
 constexpr int kEngramMaxLayers = 4;

@@ -444,11 +444,10 @@ cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   const int ns = hc_num_slices(p.D);
   const size_t smem = (size_t)(kNMix + kTokTile) * kRowE * 2;
   static_assert((size_t)8 * kTokTile * kNMix * 4 <= (size_t)kNMix * kRowE * 2, "sRed must fit in sFn");
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(hc_post_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<uint64_t> smem_set{0};
+  {
+    const cudaError_t e = smem_attr_once(hc_post_kernel, (int)smem, smem_set);
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   dim3 g(ns, (p.T + kTokTile - 1) / kTokTile);
   launch_pdl(hc_post_kernel, g, 256, smem, st, p, ns);

@@ -10,15 +10,11 @@
 // moe_scatter: copies MXFP8 token rows and their scale bytes into permuted order.
 #include "common.cuh"
 #include "kernels.h"
+#include "moe_route.cuh"
 
 namespace dsv4 {
 
-// One warp per token: sqrt-softplus or sigmoid scores (+ bias for the choice),
-// top-k by repeated warp argmax (lowest expert id on ties), weights renormalized
-// over the chosen scores and scaled.  Register arrays are only indexed by
-// unrolled loop counters (no local memory); lane k keeps the k-th pick.
-// kMaxPer = experts per lane (ceil(E / 32)); one instantiation per width keeps the
-// unrolled code of a one-token launch small (instruction fetch dominates it).
+// One warp per token (route_token in moe_route.cuh); lane k < topk writes the k-th pick.
 template <int kMaxPer>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, int E,
                                                           const float* __restrict__ bias, int topk, int score_func,
@@ -27,63 +23,12 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
-  float sc[kMaxPer], key[kMaxPer];
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int e = lane + 32 * i;
-    sc[i] = 0.f;
-    key[i] = -INFINITY;
-    if (e < E) {
-      const float x = logits[(size_t)warp * E + e];
-      float sv;
-      if (score_func == 1) {
-        sv = 1.f / (1.f + expf(-x));
-      } else {
-        const float sp = x > 20.f ? x : log1pf(expf(x));
-        sv = sqrtf(sp);
-      }
-      sc[i] = sv;
-      key[i] = sv + (bias ? bias[e] : 0.f);
-    }
-  }
-  float my_s = 0.f, total = 0.f;
-  int my_id = 0;
-  uint32_t taken = 0;   // bit i: this lane's element i is already chosen
-  for (int k = 0; k < topk; ++k) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-      if (!((taken >> i) & 1u) && key[i] > bv) {
-        bv = key[i];
-        bi = lane + 32 * i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    float sv = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i)
-      if (i == (bi >> 5)) sv = sc[i];
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    sv = __shfl_sync(0xffffffffu, sv, bi & 31);
-    if (lane == k) {
-      my_s = sv;
-      my_id = bi;
-    }
-    total += sv;
-  }
+  int my_id;
+  float my_w;
+  route_token<kMaxPer>(logits + (size_t)warp * E, E, bias, topk, score_func, route_scale, lane, my_id, my_w);
   if (lane < topk) {
-    const float inv = topk > 1 ? 1.f / (total + 1e-20f) : 1.f;
     ids[(size_t)warp * topk + lane] = my_id;
-    wts[(size_t)warp * topk + lane] = my_s * inv * route_scale;
+    wts[(size_t)warp * topk + lane] = my_w;
   }
 }
 

@@ -88,11 +88,12 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
                       head_vocab=cfg.vocab_size, tp=tp, kv_block=kv_block, kv_pool_tokens=kv_pool_tokens)
     if cfg.engram_layer_ids and engram_from is not None:
         eg = engram_from.engram
-        if eg is None or eg.ring.shape[0] < n_slots or eg.rows.shape[0] < max_tokens:
+        if eg is None or eg.ring.shape[0] < n_slots + 1 or eg.rows.shape[0] < max_tokens:
             raise ValueError("engram_from: runtime missing or smaller than this model's slots / step tokens")
         model.engram = eg
     elif cfg.engram_layer_ids:
         from ..models.engram import EngramRuntime
-        model.engram = EngramRuntime(cfg, dev, n_slots, max_tokens, model.ext, weights=weights, seed=seed,
+        # + 1: the padding slot (bucketed steps and idle ranks park their tokens there)
+        model.engram = EngramRuntime(cfg, dev, n_slots + 1, max_tokens, model.ext, weights=weights, seed=seed,
                                      shm_prefix=engram_shm, token_map=engram_token_map)
     return model

@@ -34,12 +34,13 @@ class EngineConfig:
     kv_pool_tokens: int = 0                 # paged pool size in tokens of context (0: max_seqs * max_model_len)
     use_cuda_graphs: bool = True
     expert_storage_layers: int | None = None
-    ep_transport: str = "nccl"              # "nccl" (baseline) or "p2p" (NVLink peer stores)
+    ep_transport: str = "nccl"              # "nccl" (baseline), "p2p" (NVLink peer stores) or "fused"
+                                            # (dispatch into the owners' expert rows, rows returned by W2)
     parallel: str = "ep"                    # multi-GPU layout: "ep" (data-parallel attention + expert
                                             # parallelism, throughput) or "tp" (tensor-parallel, latency)
     moe_split: str = "ep"                   # parallel="tp": experts owned whole ("ep") or split by
                                             # intermediate index over every GPU ("tp")
-    dspark: bool = False                    # speculative decoding: SpecEngine only (the server refuses it)
+    dspark: bool = False                    # speculative decoding (DSpark 1+4, greedy; one GPU)
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True
     engram_shm: str | None = None           # random-init Engram tables in shared files (e.g. /dev/shm/dsv4_engram)

@@ -18,6 +18,7 @@ many sequences, and the vLLM scheduler loop for the vLLM-served recipes.
 from __future__ import annotations
 
 import time
+from collections import OrderedDict
 from typing import Iterable
 
 import numpy as np
@@ -29,18 +30,27 @@ from .scheduler import Request, Scheduler
 
 
 class Engine:
+    """``bucket``: graph-replayed steps are padded to bucketed token / sampled-row
+    counts (``StepMeta.padded``), so a serving run with changing batch
+    compositions replays a few dozen graphs instead of capturing one per
+    composition.  ``max_graphs`` bounds the graph cache (least recently used
+    graph released first)."""
+
     def __init__(self, model: DSV4Model, max_seqs: int, max_batched_tokens: int, max_seq_len: int,
-                 chunk_size: int | None = None, use_graphs: bool = True, eos_id: int | None = None):
+                 chunk_size: int | None = None, use_graphs: bool = True, eos_id: int | None = None,
+                 bucket: bool = True, max_graphs: int = 48):
         self.model = model
         self.cfg = model.cfg
         self.sched = Scheduler(max_seqs, max_batched_tokens, max_seq_len, chunk_size,
                                kv=getattr(model, "pager", None))
         self.use_graphs = use_graphs and model.dev.type == "cuda"
-        self.graphs: dict = {}
+        self.bucket = bucket
+        self.max_graphs = max(1, max_graphs)
+        self.graphs: OrderedDict = OrderedDict()
         self.pinned: dict = {}
         self.eos_id = self.cfg.eos_token_id if eos_id is None else eos_id
         self.stream = torch.cuda.Stream(model.dev) if model.dev.type == "cuda" else None
-        self.stats = {"steps": 0, "tokens": 0, "graph_captures": 0}
+        self.stats = {"steps": 0, "tokens": 0, "graph_captures": 0, "graph_evictions": 0, "padded_tokens": 0}
 
     # ----------------------------------------------------------------- build
     @classmethod
@@ -102,10 +112,16 @@ class Engine:
 
     def _run_device(self, meta: StepMeta) -> torch.Tensor:
         m = self.model
-        m.upload(meta, self.pinned)
         if self._trace_left is None:
             from ..utils.trace import trace_steps_from_env
             self._trace_left = trace_steps_from_env()
+        if self.use_graphs and self.bucket and self._trace_left <= 0:
+            # padded to bucketed shapes; the padding's sampled rows are dropped here
+            pm = meta.padded(m.max_tokens, m.max_sample, m.n_slots)
+            self.stats["padded_tokens"] += pm.T - meta.T
+            out = self._run_graph(pm)
+            return out[:pm.n_out]
+        m.upload(meta, self.pinned)
         if self._trace_left > 0:
             # numeric trace of the first steps (eager): per-layer stream statistics
             from ..utils.trace import format_stats, layer_stats, log
@@ -117,6 +133,12 @@ class Engine:
             return out
         if not self.use_graphs:
             return m.forward(meta)
+        return self._run_graph(meta, uploaded=True)
+
+    def _run_graph(self, meta: StepMeta, uploaded: bool = False) -> torch.Tensor:
+        m = self.model
+        if not uploaded:
+            m.upload(meta, self.pinned)
         key = meta.key()
         g = self.graphs.get(key)
         if g is None:
@@ -126,12 +148,16 @@ class Engine:
             out = m.forward(meta)
             torch.cuda.current_stream().synchronize()
             ErrorWord.check(m.dev)
+            while len(self.graphs) >= self.max_graphs:
+                self.graphs.popitem(last=False)       # least recently used
+                self.stats["graph_evictions"] += 1
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=torch.cuda.current_stream()):
                 gout = m.forward(meta)
             self.graphs[key] = (graph, gout)
             self.stats["graph_captures"] += 1
             return out
+        self.graphs.move_to_end(key)
         graph, out = g
         graph.replay()
         return out

@@ -100,10 +100,53 @@ class StepMeta:
         """True when every token's compressed length <= index_topk: top-k selects all."""
         return int(self.clen[r].max(initial=0)) <= self.cfg.index_topk
 
+    n_out = None   # sampled rows the caller wants (None: all); set by :meth:`padded`
+
+    @property
+    def chunk_bound(self) -> int:
+        """Bucketed chunk count: launch sizes that depend on the chunk count (the
+        compressor's group grid) are computed from this bound, not the exact count."""
+        return token_bucket(len(self.chunks), max(1, self.T))
+
+    def max_groups(self, r: int) -> int:
+        """Upper bound of the compressor groups ratio ``r`` can close in this step: a
+        chunk of l tokens closes at most l // r + 1 of them."""
+        return min(self.T, self.T // r + self.chunk_bound)
+
     def key(self):
-        """Graph key: shapes and control flow of the step."""
-        return (self.T, len(self.sample_rows), self._lens.tobytes(),
+        """Graph key: the launch shapes and control flow of the step (token count,
+        sampled rows, chunk-count bucket, indexer bypass per ratio, sampling) and
+        nothing else, so steps of different batch compositions share a graph."""
+        return (self.T, len(self.sample_rows), self.chunk_bound,
                 tuple(self.index_bypass(r) for r in self.groups), self.sampling)
+
+    def padded(self, max_tokens: int, max_sample: int, pad_slot: int) -> "StepMeta":
+        """This step padded to bucketed shapes (:func:`token_bucket`): a padding chunk
+        of ``T_b - T`` tokens at positions 0.. of the scratch slot ``pad_slot`` (its
+        caches absorb the writes), and extra sampled rows repeating row 0.  The
+        result's ``n_out`` is the number of real sampled rows."""
+        T_b = token_bucket(self.T, max_tokens)
+        S = len(self.sample_rows)
+        chunks = list(self.chunks)
+        if T_b > self.T:
+            chunks.append(SeqChunk(pad_slot, 0, [0] * (T_b - self.T), sample=False))
+        m = StepMeta(self.cfg, chunks)
+        S_b = token_bucket(S, max(S, min(max_sample, T_b)))
+        if S_b > S:
+            extra = S_b - S
+            m.sample_rows = np.concatenate([m.sample_rows, np.full(extra, m.sample_rows[0] if S else 0, np.int32)])
+            m.temps = np.concatenate([m.temps, np.zeros(extra, np.float32)])
+        m.n_out = S
+        return m
+
+
+def token_bucket(n: int, cap: int) -> int:
+    """Padded size of a token / row count: powers of two up to 64, then multiples
+    of 64, never above ``cap`` (a count already above ``cap`` stays as it is)."""
+    if n <= 0:
+        return 0
+    b = 1 << (n - 1).bit_length() if n <= 64 else ceil_to(n, 64)
+    return max(n, min(b, cap))
 
 
 # --------------------------------------------------------------------------
@@ -597,7 +640,7 @@ class DSV4Model:
         g = self.m_groups[r]
         cos, sin = self.rope["yarn"]
         # grid covers every token that could close a group; the kernel reads the real count
-        max_groups = min(T, int((m._lens // r + 1).sum()))
+        max_groups = m.max_groups(r)
         if max_groups:
             with self._t("comp_pool"):
                 ext.compress_pool(max_groups, self.m_ngroups[r], g[0], g[1], g[2], g[3], r, co, proj, L.comp_ape,
@@ -678,6 +721,11 @@ class DSV4Model:
         rctx.__enter__()
         self._gemm_bf16(self.u, L.gate_w, logits, T, f32_out=True)
         ids, wts, pos, rank = self.route[k]
+        if self.ep is not None and self.ep.transport == "fused":
+            # (also at world size 1: the same kernels with this GPU as the only peer)
+            rctx.__exit__(None, None, None)
+            # top-k, dispatch, plan, grouped GEMMs and the return of the rows (parallel/ep.py)
+            return self.ep.moe_fused(self, L, T, k, logits)
         ext.router_topk(logits, T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale, ids, wts)
         rctx.__exit__(None, None, None)
         if self.ep is not None and self.ep.world > 1:
@@ -714,7 +762,7 @@ class DSV4Model:
         c13.__enter__()
         ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                  self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None)
+                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None, None, None)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
@@ -722,5 +770,5 @@ class DSV4Model:
         ext.gemm(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm,
                  ex.w2.q.shape[0],
                  self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1,
-                 self.tp.sync(1) if self.tp is not None else None)
+                 self.tp.sync(1) if self.tp is not None else None, None, None)
         c2.__exit__(None, None, None)

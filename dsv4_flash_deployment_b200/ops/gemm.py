@@ -125,7 +125,7 @@ def gemm_mx(xq: torch.Tensor, xsf: torch.Tensor, n_tokens: int, w: MxWeight, out
     ext.gemm(w.kind, epi, w.q, w.sf, xq, xsf, out if epi != EPI_SWIGLU else None, w.q.shape[0], n_tokens, w.k,
              bn, splits, None, None, row_scale, hq, hsf, swiglu_limit, w.n,
              out.stride(0) if out is not None else 0, workspace, counters, ErrorWord.get(xq.device), max_grid, 1,
-             publish)
+             publish, None, None)
     return out
 
 
@@ -142,7 +142,7 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, f32_out: bool
     bn = bn or pick_bn(t)
     _ext.load().gemm(KIND_BF16, EPI_F32 if f32_out else EPI_BF16, w, None, x, None, out, w.shape[0], t, k, bn,
                      splits, None, None, None, None, None, 0.0, m_valid or out.shape[1], out.stride(0), workspace,
-                     counters, ErrorWord.get(x.device), 0, groups, publish)
+                     counters, ErrorWord.get(x.device), 0, groups, publish, None, None)
     return out
 
 

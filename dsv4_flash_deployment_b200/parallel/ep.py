@@ -14,9 +14,20 @@ Transports: ``nccl`` = ``all_to_all_single`` over fixed-capacity per-peer
 regions (the baseline; no host synchronization, graph-capturable); ``p2p`` =
 the pack/combine kernels store records straight into the peer's receive
 buffer through NVLink (symmetric memory) and a device barrier orders the two
-sides.  Capacity per peer is the worst case ``T * k`` pairs (every pair of a rank
-to one peer), so no routing can overflow; an overflow would be reported
-through the device error word, never dropped silently.
+sides; ``fused`` (the default of the benchmark) = three kernels per MoE layer
+and no copy on either side (:meth:`EPGroup.moe_fused`):
+
+  ep_dispatch  router top-k + each pair claims a row of its expert on the owner
+               (system-scope atomic) and stores the token's MXFP8 row there
+  ep_plan      waits for every rank's dispatch, builds the GEMM tile lists
+  grouped W13 / W2  the W2 epilogue stores each expert row into the source
+               rank's return buffer; the next mHC boundary kernel waits and
+               combines
+
+Capacity per peer (``nccl``/``p2p``) is the worst case ``T * k`` pairs (every
+pair of a rank to one peer), and per expert (``fused``) every token of every
+rank, so no routing can overflow; an overflow would be reported through the
+device error word, never dropped silently.
 """
 
 from __future__ import annotations
@@ -25,6 +36,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import _ext
+from ..ops.gemm import EPI_BF16, EPI_SWIGLU
 from ..ops.layout import ceil_to
 
 
@@ -112,6 +124,93 @@ class EPGroup:
         done, ep = b["done"].data_ptr(), b["epoch"].data_ptr()
         b["sync0"] = torch.tensor([b["peer_sig"].data_ptr(), b["peer_cnt"].data_ptr(), done, ep], dtype=torch.int64)
         b["sync1"] = torch.tensor([b["peer_sig"].data_ptr(), 0, done + 4, ep + 4], dtype=torch.int64)
+
+    # ------------------------------------------------------------ fused path
+    def _alloc_fused(self, T: int, k: int, D: int, I: int, e_local: int, tile_rows: int):
+        """One symmetric allocation per rank: [expert rows e4m3 | their scale chunks |
+        row weights f32 | row origins int32 | per-expert counters | return rows bf16
+        (T*k pairs) | signal words]; expert e owns rows [e*cap_e, (e+1)*cap_e) with
+        cap_e = every token of every rank (no routing can overflow it).  Local:
+        the SwiGLU intermediate in the same row layout and the tile lists."""
+        import torch.distributed._symmetric_memory as symm_mem
+
+        W = self.world
+        cap_e = ceil_to(max(1, T) * W, 256)
+        rows = e_local * cap_e
+        kt = D // 128
+        sizes = [rows * D, (rows // 128) * kt * 512, rows * 4, rows * 4, e_local * 4, max(1, T * k) * D * 2, 2 * W * 4]
+        offs, cur = [], 0
+        for sz in sizes:
+            offs.append(cur)
+            cur += ceil_to(sz, 256)
+        buf = symm_mem.empty(cur, dtype=torch.uint8, device=self.dev)
+        buf.zero_()
+        hdl = symm_mem.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        table = lambda i: torch.tensor([p + offs[i] for p in ptrs], dtype=torch.int64, device=self.dev)
+        view = lambda i: buf[offs[i]:offs[i] + sizes[i]]
+        e = lambda *s_, dt: torch.empty(*s_, dtype=dt, device=self.dev)
+        tiles_max = (T * W * k) // tile_rows + e_local + 1
+        b = dict(
+            cap_e=cap_e, rows=rows, k=k, tile_rows=tile_rows, symm=buf, symm_handle=hdl,
+            x=view(0).view(rows, D), xsf=view(1), rscale=view(2).view(torch.float32),
+            meta=view(3).view(torch.int32), cnt=view(4).view(torch.int32),
+            back=view(5).view(torch.bfloat16).view(max(1, T * k), D), sig=view(6).view(torch.int32),
+            tables=[table(i) for i in range(5)], peer_back=table(5), peer_sig=table(6),
+            done=torch.zeros(2, dtype=torch.int32, device=self.dev),
+            epoch=torch.zeros(2, dtype=torch.int32, device=self.dev),
+            h=e(rows, I, dt=torch.uint8), hsf=torch.zeros((rows // 128) * (I // 128) * 512, dtype=torch.uint8,
+                                                          device=self.dev),
+            tiles13=e(tiles_max * (2 * I // 128), 4, dt=torch.int32),
+            tiles2=e(tiles_max * (D // 128), 4, dt=torch.int32),
+            nt13=torch.zeros(1, dtype=torch.int32, device=self.dev),
+            nt2=torch.zeros(1, dtype=torch.int32, device=self.dev),
+            # the return buffer holds pair (t, slot) at row t * k + slot: the combine's positions
+            pos_id=torch.arange(max(1, T * k), dtype=torch.int32, device=self.dev).view(-1, k) if T * k else None,
+        )
+        b["tab_cpu"] = torch.tensor([t.data_ptr() for t in b["tables"]], dtype=torch.int64)
+        sync = lambda ph: torch.tensor([b["peer_sig"].data_ptr(), b["sig"].data_ptr(), b["done"].data_ptr() + 4 * ph,
+                                        b["epoch"].data_ptr() + 4 * ph, ph, W, self.rank], dtype=torch.int64)
+        b["sync0"], b["sync1"] = sync(0), sync(1)
+        # mHC boundary descriptor: wait for phase 1, then the local combine (tp_mode 4)
+        b["hc_desc"] = torch.cat([torch.tensor([4], dtype=torch.int64), b["sync1"],
+                                  torch.zeros(5, dtype=torch.int64)])
+        self._fb = b
+
+    def moe_fused(self, model, L, T: int, k: int, logits: torch.Tensor):
+        """Fused expert-parallel MoE block (router top-k included); returns
+        (rows, positions, topk, hc_post descriptor) for the next mHC boundary."""
+        cfg, ext = model.cfg, model.ext
+        D = cfg.dim
+        I = L.experts.inter
+        E = cfg.n_experts_for(L.layer_id)
+        _, e_local = self.expert_range(E)
+        if getattr(self, "_fb", None) is None:
+            self._alloc_fused(model.max_tokens, k, D, I, e_local, model.tile_rows)
+        b = self._fb
+        if b["k"] != k:
+            raise NotImplementedError("fused expert parallelism with several routing widths")
+        ids, wts, _, _ = model.route[k]
+        with model._t("ep_dispatch"):
+            ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
+                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tab_cpu"], model.err, b["sync0"])
+        with model._t("ep_plan"):
+            ext.ep_plan(b["sync0"], b["cnt"], b["cap_e"], b["tile_rows"], 2 * I, D, b["tiles13"], b["nt13"],
+                        b["tiles2"], b["nt2"], model.err)
+        ex = L.experts
+        with model._t("grouped_w13"):
+            ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, b["x"], b["xsf"], None, ex.w13.q.shape[0],
+                     b["rows"], D, b["tile_rows"], 1, b["tiles13"], b["nt13"], b["rscale"], b["h"], b["hsf"],
+                     cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None)
+        with model._t("grouped_w2"):
+            ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["rows"], I), b["hsf"], None, ex.w2.q.shape[0],
+                     b["rows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None, 0.0, D, D, None, None,
+                     model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"])
+        with model._t("shared_expert"):
+            model._shared_expert(L, T)
+        return b["back"], b["pos_id"], k, b["hc_desc"]
 
     def moe(self, model, L, T: int, k: int):
         """Runs the expert-parallel MoE block; returns (rows, positions, topk) for the combine."""

@@ -3,8 +3,10 @@
 Every rank builds the same small V4-shaped model (same checkpoint tensors)
 twice: once whole on its GPU (the reference) and once expert-parallel over
 all ranks.  Each rank steps its own sequences (data-parallel attention) and
-the EP logits must match the local model's.  Then the MoE exchange of both
-transports is timed on the device (max over ranks):
+the EP logits must match the local model's.  Then the step of every
+transport (NCCL all-to-all, NVLink peer stores, and the fused path whose
+dispatch stores straight into the owners' expert rows) is timed on the device
+(max over ranks):
 
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m dsv4_flash_deployment_b200.parallel.ep_check
 
@@ -55,6 +57,7 @@ def main(argv=None):
     ap.add_argument("--plen", type=int, default=40)
     ap.add_argument("--time-tokens", type=int, default=256)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--transports", default="nccl,p2p,fused")
     a = ap.parse_args(argv)
 
     from ..engine.builder import build_model
@@ -72,7 +75,7 @@ def main(argv=None):
     ref = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512, weights=w)
     ok = True
     results = {}
-    for transport in ("nccl", "p2p"):
+    for transport in a.transports.split(","):
         ep = EPGroup(rank, world, dist.group.WORLD, dev, transport=transport)
         m = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512, weights=w, ep=ep)
         worst, agree, total = 1.0, 0, 0

@@ -34,6 +34,20 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
                         engram_token_map=_engram_token_map(ec, cfg))
 
 
+def build_spec_engine(ec: EngineConfig, local):
+    """DSpark speculative decoding over the local engine's model: the MTP stages
+    from the checkpoint (or drawn at random), one drafter row per cache slot."""
+    from ..spec.dspark import SpecEngine
+    from ..spec.serving import SpecServingEngine
+
+    cfg = local.cfg
+    if cfg.n_mtp_layers < 1:
+        raise SystemExit(f"--dspark: model {cfg.name} has no MTP stages")
+    spec = SpecEngine(local.model, _load_weights(ec, cfg), max_seqs=ec.max_seqs,
+                      force_accept=ec.dspark_force_accept)
+    return SpecServingEngine(spec, ec.max_model_len, eos_id=local.eos_id)
+
+
 def _engram_token_map(ec: EngineConfig, cfg):
     """Engram hashes key on the tokenizer's normalized token texts when the served
     tokenizer has a ``tokenizer.json`` (the checkpoint's tables were built that way)."""
@@ -96,11 +110,10 @@ def main(argv: list[str] | None = None) -> None:
     from .tokenizer import load_tokenizer
 
     ec = EngineConfig.from_args(argv)
-    if ec.dspark:
-        # speculative decoding runs through spec.dspark.SpecEngine (generate / draft /
-        # verify API, e.g. bench/v41_bench.py); the HTTP engine loop decodes greedily
-        raise SystemExit("--dspark: the OpenAI server decodes without speculation; use "
-                         "dsv4_flash_deployment_b200.spec.dspark.SpecEngine for DSpark generation")
+    if ec.dspark and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--dspark serves on one GPU (the drafter runs on a whole backbone)")
+    if ec.dspark and ec.device != "cuda":
+        raise SystemExit("--dspark needs a CUDA device")
     rank, world, par, cpu_group = init_distributed(ec)
     if ec.device == "cuda" and world == 1:
         torch.cuda.set_device(0)
@@ -113,6 +126,8 @@ def main(argv: list[str] | None = None) -> None:
         dist.destroy_process_group()
         return
     eng = DistributedEngine(local, cpu_group, replicated=replicated) if world > 1 else local
+    if ec.dspark:
+        eng = build_spec_engine(ec, local)
     loop = EngineLoop(eng, step_deadline_s=ec.step_deadline_s).start()
     tok = load_tokenizer(ec.tokenizer, local.cfg)
     info = {"device": ec.device, "world_size": world, "engine_config": ec.to_dict()}

@@ -260,10 +260,54 @@ class SpecEngine:
         dr.toks[0, :na].copy_(torch.tensor([self.outs[j][-1] for j in act], dtype=torch.int32))
         return dr.draft(na).cpu().numpy()
 
-    def verify(self, act: list[int], blocks: list[list[int]], max_new_tokens: int | None = None) -> list[int]:
+    # ------------------------------------------------------- per-row serving
+    def open_rows(self) -> None:
+        """Per-row state for serving (rows admitted and released one by one)."""
+        self.slots = list(range(self.max_seqs))
+        self.outs = [[] for _ in range(self.max_seqs)]
+        self.pos = [0] * self.max_seqs
+
+    def add_sequence(self, j: int, prompt: list[int]) -> int:
+        """Prefills ``prompt`` (chunked) into row ``j`` (model slot ``j``) and fills the
+        MTP rings; returns the first generated token."""
+        m, cfg, dr = self.m, self.cfg, self.drafter
+        pg = getattr(m, "pager", None)
+        if pg is not None and not pg.reserve(self.slots[j], m.max_seq_len):
+            raise ValueError("paged cache pool has no room for another speculative sequence")
+        first = None
+        for c0 in range(0, len(prompt), m.max_tokens):
+            piece = prompt[c0:c0 + m.max_tokens]
+            last = c0 + len(piece) == len(prompt)
+            meta = StepMeta(cfg, [SeqChunk(self.slots[j], c0, piece, last)])
+            ids = self._run(meta, taps=dr.taps)
+            dr.ingest(None, meta.T)
+            if last:
+                first = int(ids[0])
+        self.outs[j] = [first]
+        self.pos[j] = len(prompt)
+        return first
+
+    def release_row(self, j: int) -> None:
+        pg = getattr(self.m, "pager", None)
+        if pg is not None:
+            pg.release(self.slots[j])
+        self.outs[j] = []
+
+    def round(self, act: list[int], limits: list[int]) -> list[list[int]]:
+        """One draft + verify round for rows ``act`` (``limits``: output length cap
+        per row); returns the tokens each row emitted."""
+        before = [len(self.outs[j]) for j in act]
+        toks = self.draft(act)
+        blocks = [[self.outs[j][-1]] + [int(toks[i + 1, a]) for i in range(self.blk - 1)]
+                  for a, j in enumerate(act)]
+        self.verify(act, blocks, limits)
+        return [self.outs[j][b:] for j, b in zip(act, before)]
+
+    def verify(self, act: list[int], blocks: list[list[int]], max_new_tokens=None) -> list[int]:
         """Verifies blocks [root, d1..d_{B-1}] per sequence; commits, ingests, emits.
 
-        Returns the accepted draft count per sequence."""
+        ``max_new_tokens``: output length cap, one for all rows or a list per row
+        of ``act``.  Returns the accepted draft count per sequence."""
         m, cfg, dr = self.m, self.cfg, self.drafter
         na = len(act)
         vmeta = StepMeta(cfg, [SeqChunk(self.slots[j], self.pos[j], blocks[a], True, True) for a, j in enumerate(act)])
@@ -288,7 +332,8 @@ class SpecEngine:
         for a, j in enumerate(act):
             k = n_acc[a]
             emitted = blocks[a][1:k + 1] + [int(preds[a, k])]
-            room = len(emitted) if max_new_tokens is None else max_new_tokens - len(self.outs[j])
+            cap = max_new_tokens[a] if isinstance(max_new_tokens, (list, tuple)) else max_new_tokens
+            room = len(emitted) if cap is None else cap - len(self.outs[j])
             self.outs[j].extend(emitted[:room])
             self.pos[j] += k + 1
             self.stats.rounds += 1

@@ -1,6 +1,7 @@
-"""Expert parallelism on 2+ GPUs: both transports (NCCL all-to-all baseline,
-NVLink peer stores with bounded signal waits) must reproduce the single-GPU
-model's logits.  Runs the self-check under torchrun; skipped with < 2 GPUs."""
+"""Expert parallelism on 2+ GPUs: every transport (NCCL all-to-all baseline,
+NVLink peer stores with bounded signal waits, and the fused dispatch that
+stores straight into the owners' expert rows and returns rows from the W2
+epilogue) must reproduce the single-GPU model's logits.  Runs the self-check under torchrun; skipped with < 2 GPUs."""
 
 import os
 import subprocess
@@ -23,4 +24,6 @@ def test_ep_transports_match_single_gpu():
            "-m", "dsv4_flash_deployment_b200.parallel.ep_check", "--steps", "3", "--iters", "5"]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(os.path.dirname(__file__)))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert '"transport": "p2p"' in r.stdout and '"ok": true' in r.stdout
+    assert '"transport": "p2p"' in r.stdout and '"transport": "fused"' in r.stdout
+    assert '"ok": false' not in r.stdout and r.stdout.count('"ok": true') == 3
+

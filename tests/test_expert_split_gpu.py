@@ -29,10 +29,10 @@ def _ffn(ext, err, ex: ExpertBlock, xq, xsf, rw, starts, counts, rows, D):
     y = torch.zeros(rows, D, dtype=torch.float32, device="cuda")
     ext.gemm(ex.w13.kind, G.EPI_SWIGLU, ex.w13.q, ex.w13.sf, xq, xsf, None, ex.w13.q.shape[0], rows, D, 128, 1, t13,
              torch.tensor([len(t13)], dtype=torch.int32, device="cuda"), rw, hq, hsf, 10.0, 2 * I, 0, None,
-             None, err, 0, 1, None)
+             None, err, 0, 1, None, None, None)
     ext.gemm(ex.w2.kind, G.EPI_F32, ex.w2.q, ex.w2.sf, hq, hsf, y, ex.w2.q.shape[0], rows, I, 128, 1, t2,
              torch.tensor([len(t2)], dtype=torch.int32, device="cuda"), None, None, None, 0.0, D, D, None, None,
-             err, 0, 1, None)
+             err, 0, 1, None, None, None)
     return y
 
 

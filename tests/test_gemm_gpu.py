@@ -149,7 +149,7 @@ def test_grouped_mx8():
     nt = torch.tensor([len(tiles)], dtype=torch.int32, device="cuda")
     out = torch.zeros(rows, n, dtype=torch.bfloat16, device="cuda")
     G._ext.load().gemm(G.KIND_MX8, G.EPI_BF16, mw.q, mw.sf, xq, xsf, out, mw.q.shape[0], rows, k, 256, 1, tl, nt,
-                       None, None, None, 0.0, n, n, None, None, G.ErrorWord.get("cuda"), 0, 1, None)
+                       None, None, None, 0.0, n, n, None, None, G.ErrorWord.get("cuda"), 0, 1, None, None, None)
     torch.cuda.synchronize()
     G.ErrorWord.check("cuda")
     for ei, (st, c) in enumerate(zip(starts, counts)):
@@ -227,10 +227,10 @@ def test_grouped_expert_ffn_matches_oracle(fmt):
     err = G.ErrorWord.get("cuda")
     ext.gemm(w13.kind, G.EPI_SWIGLU, w13.q, w13.sf, xq, xsf, None, w13.q.shape[0], rows, D, 128, 1, t13,
              torch.tensor([len(t13)], dtype=torch.int32, device="cuda"), rw.cuda(), hq, hsf, 10.0, 2 * I, 0, None,
-             None, err, 0, 1, None)
+             None, err, 0, 1, None, None, None)
     ext.gemm(w2.kind, G.EPI_BF16, w2.q, w2.sf, hq, hsf, y, w2.q.shape[0], rows, I, 128, 1, t2,
              torch.tensor([len(t2)], dtype=torch.int32, device="cuda"), None, None, None, 0.0, D, D, None, None,
-             err, 0, 1, None)
+             err, 0, 1, None, None, None)
     torch.cuda.synchronize()
     G.ErrorWord.check("cuda")
     for e, (st, c) in enumerate(zip(starts, counts)):
