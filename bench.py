@@ -21,7 +21,9 @@ Two numbers:
 
 Multi-GPU: one rank per GPU; attention is data-parallel over the requests
 (512/N per rank) and experts are split over ranks (EP=N).  The expert exchange
-runs in the fused NVLink dispatch/combine kernels of ``parallel/ep.py``.
+runs in the fused path of ``parallel/ep.py``: the dispatch kernel stores each
+routed token row straight into its owner's expert rows over NVLink, and the
+grouped W2 GEMM's epilogue stores each expert row back into the source rank.
 
     python bench.py [--gpus N --steps K --warmup W]
     python bench.py --impl reference     # the reference arm (prints why it is unavailable)
@@ -150,8 +152,9 @@ def main() -> None:
     ap.add_argument("--c1-moe", default="ep", choices=["ep", "tp"],
                     help="experts in the tensor-parallel C=1 model: owned whole (ep, shared with the batch model) "
                          "or split by intermediate index over all GPUs (tp)")
-    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl", "fused"],
-                    help="expert exchange: NVLink peer stores (p2p) or the NCCL all-to-all baseline")
+    ap.add_argument("--ep-transport", default="fused", choices=["p2p", "nccl", "fused"],
+                    help="expert exchange: fused (dispatch into the owners' expert rows, rows returned by the W2 "
+                         "epilogue), p2p (peer-store pack/unpack kernels) or the NCCL all-to-all baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
@@ -310,7 +313,8 @@ def main() -> None:
             eng.add_request(rng.integers(0, cfg.vocab_size, isl).tolist(), osl, ignore_eos=True)
 
     top_up()
-    for _ in range(2):
+    # warm-up steps: the compositions of the steady state (bucketed shapes) get their graphs
+    for _ in range(4):
         eng.step()
         top_up()
     if group is not None:

@@ -238,62 +238,68 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const in
 // Counter reuse: a rank reaches the next layer's dispatch only after every
 // owner's W2 of this layer has published, and every owner's ep_plan (which
 // zeroed the counters) precedes its W2 in stream order.
+// One CTA (8 warps) per token: warp 0 routes the token and claims the k rows on
+// their owners; then warp j stores pair j (and j + 8) -- k NVLink row stores in
+// parallel per token, and every SM busy at decode-sized token counts.
 template <int kMaxPer>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
   pdl_entry();
-  const int warp = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  __shared__ int s_owner[16], s_row[16];
+  __shared__ float s_w[16];
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = p.D;
   const int kt = D / 128;
-  if (warp < p.T) {
-    const int t = warp;
-    int id;
-    float w;
-    route_token<kMaxPer>(p.logits + (size_t)t * p.E, p.E, p.bias, p.topk, p.score_func, p.route_scale, lane, id, w);
-    int owner = 0, row = -1;
-    if (lane < p.topk) {
-      if (p.ids) {
-        p.ids[(size_t)t * p.topk + lane] = id;
-        p.wts[(size_t)t * p.topk + lane] = w;
-      }
-      owner = id / p.e_local;
-      const int le = id - owner * p.e_local;
-      const int slot = atomicAdd_system(p.peer_cnt[owner] + le, 1);
-      if (slot < p.cap_e) {
-        row = le * p.cap_e + slot;
-      } else {
-        report_error(p.err, ERR_CAPACITY, KID_MOE, 3);
+  if (t < p.T) {
+    if (warp == 0) {
+      int id;
+      float w;
+      route_token<kMaxPer>(p.logits + (size_t)t * p.E, p.E, p.bias, p.topk, p.score_func, p.route_scale, lane, id,
+                           w);
+      if (lane < p.topk) {
+        if (p.ids) {
+          p.ids[(size_t)t * p.topk + lane] = id;
+          p.wts[(size_t)t * p.topk + lane] = w;
+        }
+        const int owner = id / p.e_local;
+        const int le = id - owner * p.e_local;
+        const int slot = atomicAdd_system(p.peer_cnt[owner] + le, 1);
+        int row = -1;
+        if (slot < p.cap_e) {
+          row = le * p.cap_e + slot;
+        } else {
+          report_error(p.err, ERR_CAPACITY, KID_MOE, 3);
+        }
+        s_owner[lane] = owner;
+        s_row[lane] = row;
+        s_w[lane] = w;
       }
     }
+    __syncthreads();
     // the token's row (D bytes) and scale words (one 4-byte word per 128 columns)
-    // are loaded once and stored to each of the k owners
     constexpr int kVec = 8;   // uint4 per lane for D <= 4096
-    uint4 v[kVec];
     const int nvec = D / 16;
-#pragma unroll
-    for (int i = 0; i < kVec; ++i)
-      if (lane + 32 * i < nvec) v[i] = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D)[lane + 32 * i];
-    uint32_t sfw = 0;
     const int m_src = t & 127;
-    if (lane < kt)
-      sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + lane) * 512 + (m_src & 31) * 16 +
-                                                 (m_src >> 5) * 4);
-    for (int j = 0; j < p.topk; ++j) {
-      const int o = __shfl_sync(0xffffffffu, owner, j);
-      const int r = __shfl_sync(0xffffffffu, row, j);
-      const float wj = __shfl_sync(0xffffffffu, w, j);
+    for (int j = warp; j < p.topk; j += 8) {
+      const int o = s_owner[j], r = s_row[j];
       if (r < 0) continue;
+      uint4 v[kVec];
+#pragma unroll
+      for (int i = 0; i < kVec; ++i)
+        if (lane + 32 * i < nvec) v[i] = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D)[lane + 32 * i];
       uint4* dst = reinterpret_cast<uint4*>(p.peer_x[o] + (size_t)r * D);
 #pragma unroll
       for (int i = 0; i < kVec; ++i)
         if (lane + 32 * i < nvec) dst[lane + 32 * i] = v[i];
       if (lane < kt) {
+        const uint32_t sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + lane) * 512 +
+                                                                (m_src & 31) * 16 + (m_src >> 5) * 4);
         const int m = r & 127;
         *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + lane) * 512 + (m & 31) * 16 +
                                      (m >> 5) * 4) = sfw;
       }
       if (lane == 0) {
-        p.peer_rscale[o][r] = wj;
+        p.peer_rscale[o][r] = s_w[j];
         p.peer_meta[o][r] = (p.rank << 24) | (t * p.topk + j);
       }
     }
@@ -304,7 +310,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
 cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st) {
   if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D > 4096 || p.D / 128 > 32) return cudaErrorInvalidValue;
   if ((long long)p.T * p.topk >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
-  const unsigned grid = (unsigned)std::max(1, (p.T * 32 + 255) / 256);   // every rank publishes, even with T = 0
+  const unsigned grid = (unsigned)std::max(1, p.T);   // every rank publishes, even with T = 0
   const int per = (p.E + 31) / 32;
 #define DSV4_DISPATCH(P) launch_pdl(ep_dispatch_kernel<P>, grid, 256, 0, st, p)
   if (per <= 2) DSV4_DISPATCH(2);

@@ -25,6 +25,7 @@ tap buffers and a few small work arrays are added.
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -199,7 +200,10 @@ class SpecEngine:
 
     ``force_accept``: accept exactly this many drafts per round regardless of
     agreement (the reference's knob for random-weight runs, engine.py:332);
-    outputs then differ from greedy, the acceptance path is exercised.
+    outputs then differ from greedy, the acceptance path is exercised.  A
+    fractional value f accepts floor(f) or ceil(f) drafts per round in a fixed
+    pattern whose mean is f (e.g. 2.15 reproduces the reference's measured
+    3.15 tokens per round, ``MK/results/megakernel_v6e16_results.json:777``).
     """
 
     def __init__(self, model, weights: dict | None, max_seqs: int = 16, force_accept: int | None = None):
@@ -208,6 +212,7 @@ class SpecEngine:
         self.drafter = DSparkDrafter(model, weights, max_seqs)
         self.blk = self.cfg.dspark_block_size
         self.force_accept = force_accept
+        self._forced_rounds = 0
         self.stats = SpecStats(histogram=[0] * self.blk)
         self.max_seqs = max_seqs
         self.pinned: dict = {}
@@ -315,7 +320,10 @@ class SpecEngine:
         n_acc = []
         for a in range(na):
             if self.force_accept is not None:
-                k = min(int(self.force_accept), self.blk - 1)
+                f = float(self.force_accept)
+                r = self._forced_rounds
+                self._forced_rounds += 1
+                k = min(int(math.floor((r + 1) * f + 1e-9) - math.floor(r * f + 1e-9)), self.blk - 1)
             else:
                 k = 0
                 while k < self.blk - 1 and preds[a, k] == blocks[a][k + 1]:
