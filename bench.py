@@ -147,6 +147,8 @@ def main() -> None:
     ap.add_argument("--chunk", type=int, default=None, help="prefill tokens per step (all ranks)")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-v41", action="store_true",
+                    help="skip the V4.1 measurements (C=190 step, C=1 TPOT, DSpark effective TPOT) in the same line")
     ap.add_argument("--c1-layout", default="auto", choices=["auto", "tp", "dp"],
                     help="C=1 TPOT on N>1 GPUs: tensor-parallel decode model (auto/tp) or the batch layout (dp)")
     ap.add_argument("--c1-moe", default="ep", choices=["ep", "tp"],
@@ -379,6 +381,37 @@ def main() -> None:
         tpg.release()
         dist.barrier()
 
+    # ------------------------------------------------------------ V4.1 family
+    # the V4.1 model (40 layers + 3 DSpark stages, 384 MXFP4 experts, Engram)
+    # measured in the same job after the V4-Flash model is released; its
+    # numbers ride in the same line under "v41"
+    v41 = None
+    run_v41 = not args.no_v41 and args.workload == "1k1k"
+    if run_v41:
+        import gc
+
+        eng.graphs.clear()
+        if ep is not None:
+            ep.release()
+        del eng, model
+        gc.collect()
+        torch.cuda.empty_cache()
+        from dsv4_flash_deployment_b200.bench import v41_bench
+        # Engram tables at 2 x 4M rows (2 GB page-locked per rank): hashing and the
+        # per-token row reads do not depend on the table size
+        va = v41_bench.parser().parse_args(["--steps", str(max(3, min(args.steps, 6))), "--warmup", "2",
+                                            "--spec-rounds", "8", "--engram-rows", "4000000",
+                                            "--ep-transport", args.ep_transport])
+        try:
+            r = v41_bench.measure(va, dev, rank, world, group)
+            if rank == 0:
+                v41 = {"metric": "V4.1-Flash output tok/s @1k/1k C=190; C=1 TPOT; DSpark 1+4 effective TPOT",
+                       "value": r["value"], "unit": "tok/s", "ms_per_step": r["ms_per_step"],
+                       "vs_baseline": r["vs_baseline"], "baseline": 1471.6, "steps": va.steps,
+                       "config": r["config"], "c1_tpot_ms": r["c1_tpot_ms"], "dspark": r["dspark"]}
+        except Exception as e:  # noqa: BLE001  (the V4-Flash line above is still reported)
+            v41 = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+
     if rank == 0:
         line = {
             "metric": METRIC if args.workload == "1k1k" else
@@ -428,10 +461,12 @@ def main() -> None:
             "clocks": clk.summary(),
             "build_s": round(t_build, 1),
             "hardware": provenance(dev),
+            "v41": v41,
         }
         print(json.dumps(line), flush=True)
     if group is not None:
-        eng.graphs.clear()
+        if not run_v41:
+            eng.graphs.clear()     # graphs holding NCCL work go before the process group
         dist.barrier()
         dist.destroy_process_group()
 

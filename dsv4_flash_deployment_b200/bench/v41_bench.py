@@ -58,7 +58,7 @@ def _timed(stream, fn, n: int) -> tuple[float, float]:
     return e0.elapsed_time(e1) / n, (time.perf_counter() - w0) / n * 1e3
 
 
-def main(argv=None) -> None:
+def parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser()
     ap.add_argument("--concurrency", type=int, default=190)
     ap.add_argument("--steps", type=int, default=6)
@@ -77,15 +77,12 @@ def main(argv=None) -> None:
     ap.add_argument("--no-spec", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel C=1 measurement")
-    a = ap.parse_args(argv)
+    ap.add_argument("--ep-transport", default="fused", choices=["p2p", "nccl", "fused"])
+    return ap
 
-    from ..config import v41_flash_config
-    from ..engine.engine import Engine
-    from ..engine.memory import expert_block_bytes, plan_expert_storage
-    from ..models.model import SeqChunk, StepMeta
-    from ..parallel import ep as ep_mod
-    from ..utils.provenance import provenance
 
+def main(argv=None) -> None:
+    a = parser().parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -96,6 +93,25 @@ def main(argv=None) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
+    line = measure(a, dev, rank, world, group)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure(a, dev, rank: int, world: int, group) -> dict:
+    """Runs every V4.1 measurement on this rank (the process group, if any, is
+    already up); returns the result line (complete on rank 0)."""
+
+    from ..config import v41_flash_config
+    from ..engine.engine import Engine
+    from ..engine.memory import expert_block_bytes, plan_expert_storage
+    from ..models.model import SeqChunk, StepMeta
+    from ..parallel import ep as ep_mod
+    from ..utils.provenance import provenance
+
     cfg = v41_flash_config(engram_num_embeddings=(a.engram_rows, a.engram_rows))
     C = a.concurrency
     c_rank = max(2, C // world)
@@ -103,7 +119,7 @@ def main(argv=None) -> None:
     chunk = max(1, a.chunk // world)
     max_tokens = n_dec + chunk
     max_seq = a.isl + a.osl
-    ep = ep_mod.EPGroup(rank, world, group, dev, transport="p2p") if world > 1 else None
+    ep = ep_mod.EPGroup(rank, world, group, dev, transport=a.ep_transport) if world > 1 else None
     # the DSpark stages' expert blocks (3 x 128 experts) come out of the reserve
     spec_gb = 0 if a.no_spec else cfg.n_mtp_layers * expert_block_bytes(
         dataclasses.replace(cfg, n_routed_experts=cfg.dspark_n_routed_experts), 1) / 2 ** 30
@@ -215,6 +231,7 @@ def main(argv=None) -> None:
                              "(5 tokens, deferred rings) + ring commit + main-hidden ingest; prompt of isl tokens; "
                              "the first entry forces the reference's measured mean acceptance"})
 
+    line = {}
     if rank == 0:
         eg = model.engram
         tables_gb = sum(t.q.numel() + t.sf.numel() for t in eg.tables) / 2 ** 30 if eg is not None else 0
@@ -244,11 +261,10 @@ def main(argv=None) -> None:
             "dspark": spec,
             "hardware": provenance(dev),
         }
-        print(json.dumps(line), flush=True)
     eng.graphs.clear()
-    if group is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    if ep is not None:
+        ep.release()
+    return line
 
 
 if __name__ == "__main__":

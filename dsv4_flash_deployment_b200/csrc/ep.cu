@@ -276,26 +276,22 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
       }
     }
     __syncthreads();
-    // the token's row (D bytes) and scale words (one 4-byte word per 128 columns)
-    constexpr int kVec = 8;   // uint4 per lane for D <= 4096
+    // the token's row (D bytes, 16-byte vectors) and its scale words (one 4-byte
+    // word per 128 columns in the chunk layout); the k warps' reads of the same
+    // row hit in L1/L2
     const int nvec = D / 16;
     const int m_src = t & 127;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D);
     for (int j = warp; j < p.topk; j += 8) {
       const int o = s_owner[j], r = s_row[j];
       if (r < 0) continue;
-      uint4 v[kVec];
-#pragma unroll
-      for (int i = 0; i < kVec; ++i)
-        if (lane + 32 * i < nvec) v[i] = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D)[lane + 32 * i];
       uint4* dst = reinterpret_cast<uint4*>(p.peer_x[o] + (size_t)r * D);
-#pragma unroll
-      for (int i = 0; i < kVec; ++i)
-        if (lane + 32 * i < nvec) dst[lane + 32 * i] = v[i];
-      if (lane < kt) {
-        const uint32_t sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + lane) * 512 +
+      for (int i = lane; i < nvec; i += 32) dst[i] = src[i];
+      const int m = r & 127;
+      for (int b = lane; b < kt; b += 32) {
+        const uint32_t sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + b) * 512 +
                                                                 (m_src & 31) * 16 + (m_src >> 5) * 4);
-        const int m = r & 127;
-        *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + lane) * 512 + (m & 31) * 16 +
+        *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + b) * 512 + (m & 31) * 16 +
                                      (m >> 5) * 4) = sfw;
       }
       if (lane == 0) {
@@ -308,7 +304,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
 }
 
 cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st) {
-  if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D > 4096 || p.D / 128 > 32) return cudaErrorInvalidValue;
+  if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D < 128) return cudaErrorInvalidValue;
   if ((long long)p.T * p.topk >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)std::max(1, p.T);   // every rank publishes, even with T = 0
   const int per = (p.E + 31) / 32;

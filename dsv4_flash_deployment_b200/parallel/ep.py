@@ -212,6 +212,12 @@ class EPGroup:
             model._shared_expert(L, T)
         return b["back"], b["pos_id"], k, b["hc_desc"]
 
+    def release(self) -> None:
+        """Drops the exchange buffers (symmetric memory) once the device is idle."""
+        torch.cuda.synchronize(self.dev)
+        self._bufs = None
+        self._fb = None
+
     def moe(self, model, L, T: int, k: int):
         """Runs the expert-parallel MoE block; returns (rows, positions, topk) for the combine."""
         cfg, ext = model.cfg, model.ext

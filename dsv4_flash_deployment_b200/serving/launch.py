@@ -26,9 +26,19 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
         w = _load_weights(ec, cfg) or make_random_weights(cfg, seed=ec.seed, include_mtp=False)
         model = OracleStepModel(cfg, w, n_slots=ec.max_seqs + extra_slots, max_seq_len=ec.max_model_len)
         return Engine(model, ec.max_seqs, ec.max_batched_tokens, ec.max_model_len, ec.chunk_size, use_graphs=False)
+    weights = _load_weights(ec, cfg)
+    storage = ec.expert_storage_layers
+    if storage is None and weights is None:
+        # random init: as many distinct expert blocks as fit next to the caches and
+        # step buffers (layers share blocks round-robin beyond that)
+        from ..engine.memory import plan_expert_storage
+
+        world = ep.world if ep is not None else (tp.world if tp is not None and tp.moe == "ep" else 1)
+        storage = plan_expert_storage(cfg, torch.device(ec.device, torch.cuda.current_device()),
+                                      ec.max_batched_tokens, ec.max_seqs + extra_slots + 1, ec.max_model_len, world)
     return Engine.build(cfg, device=ec.device, max_seqs=ec.max_seqs, max_batched_tokens=ec.max_batched_tokens,
-                        max_seq_len=ec.max_model_len, weights=_load_weights(ec, cfg), seed=ec.seed,
-                        expert_storage_layers=ec.expert_storage_layers, ep=ep, use_graphs=ec.use_cuda_graphs,
+                        max_seq_len=ec.max_model_len, weights=weights, seed=ec.seed,
+                        expert_storage_layers=storage, ep=ep, use_graphs=ec.use_cuda_graphs,
                         chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp, kv_block=ec.kv_block,
                         kv_pool_tokens=ec.kv_pool_tokens, engram_shm=ec.engram_shm,
                         engram_token_map=_engram_token_map(ec, cfg))

@@ -39,6 +39,10 @@ def render_prometheus(st) -> str:
     metric("cache_slots_used_ratio", "gauge", "Fraction of KV cache slots in use.",
            f"{1.0 - sched.slots.n_free / max(sched.max_seqs, 1):.4f}")
     metric("graph_captures_total", "counter", "CUDA graphs captured.", eng.stats.get("graph_captures", 0))
+    metric("graph_evictions_total", "counter", "CUDA graphs released by the bounded graph cache.",
+           eng.stats.get("graph_evictions", 0))
+    metric("padded_tokens_total", "counter", "Padding tokens added to reach bucketed step shapes.",
+           eng.stats.get("padded_tokens", 0))
     spec = eng.stats.get("spec")
     if spec:
         metric("spec_accepted_tokens_total", "counter", "Draft tokens accepted.", spec.get("accepted", 0))

@@ -35,6 +35,26 @@ class _Queue:
     def idle(self) -> bool:
         return not self.o.waiting and not self.o.active
 
+    @property
+    def running(self) -> list:
+        return list(self.o.active.values())
+
+    @property
+    def waiting(self):
+        return self.o.waiting
+
+    @property
+    def max_seqs(self) -> int:
+        return self.o.spec.max_seqs
+
+    @property
+    def slots(self):
+        return self
+
+    @property
+    def n_free(self) -> int:
+        return len(self.o.free_rows)
+
     def cancel(self, req: Request) -> None:
         req.cancelled = True
         if req in self.o.waiting:
@@ -113,4 +133,5 @@ class SpecServingEngine:
             sp.release_row(j)
             self.free_rows.append(j)
         self.stats["steps"] += 1
+        self.stats["spec"] = sp.stats.as_dict()
         return events

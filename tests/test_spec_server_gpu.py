@@ -69,6 +69,15 @@ def test_spec_server_is_lossless_and_batches(spec_served):
     assert eng.stats["rounds"] - rounds0 <= 2 * n_new
 
 
+def test_spec_server_metrics(spec_served):
+    st, _, _ = spec_served
+
+    async def go(c):
+        return await (await c.get("/metrics")).text()
+    text = _run(st, go)
+    assert "dsv4_spec_draft_tokens_total" in text and "dsv4_healthy 1" in text
+
+
 def test_spec_server_refuses_sampling(spec_served):
     st, _, _ = spec_served
 
