@@ -594,8 +594,8 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, 
 // origins, per-expert counters) of every rank; pub: PeerSync of phase 0.
 void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
                  double route_scale, const optional<Tensor>& ids, const optional<Tensor>& wts, const Tensor& xq,
-                 const Tensor& xsf, int64_t e_local, int64_t cap_e, const Tensor& tables, const Tensor& err,
-                 const Tensor& pub) {
+                 const Tensor& xsf, int64_t e_local, int64_t cap_e, int64_t tile_rows, const Tensor& tables,
+                 const Tensor& err, const Tensor& pub) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) == logits.size(1), "logits: f32 [T, E] contiguous");
@@ -618,6 +618,7 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
   p.D = (int)xq.size(1);
   p.e_local = (int)e_local;
   p.cap_e = (int)cap_e;
+  p.tile_rows = (int)tile_rows;
   p.peer_x = reinterpret_cast<uint8_t* const*>(tb[0]);
   p.peer_xsf = reinterpret_cast<uint8_t* const*>(tb[1]);
   p.peer_rscale = reinterpret_cast<float* const*>(tb[2]);

@@ -391,6 +391,23 @@ __host__ __device__ inline size_t sf_chunk_offset(int row, int kblk, int k_tiles
   return ((size_t)rt * k_tiles + kt) * 512 + (size_t)((m & 31) * 16 + (m >> 5) * 4 + j);
 }
 
+// Row layout of an expert's segment in the permuted activation buffer.  Tiles of
+// tile_rows >= 128 rows are packed (a segment is its row count rounded up to
+// 128); tiles of 32 or 64 rows each start on a 128-row boundary (a 128-row slot
+// per tile), because the GEMM uses every tile's 128-row scale chunk unshifted.
+__host__ __device__ inline int seg_rows(int count, int tile_rows) {
+  return tile_rows < 128 ? (count + tile_rows - 1) / tile_rows * 128 : (count + 127) & ~127;
+}
+__host__ __device__ inline int seg_row(int i, int tile_rows) {   // i-th pair of the expert
+  return tile_rows < 128 ? (i / tile_rows) * 128 + i % tile_rows : i;
+}
+__host__ __device__ inline int seg_tile_row(int r0, int tile_rows) {   // first row of the tile holding pair r0
+  return tile_rows < 128 ? (r0 / tile_rows) * 128 : r0;
+}
+__host__ __device__ inline int seg_pairs(int rows, int tile_rows) {   // pairs a segment of `rows` rows holds
+  return tile_rows < 128 ? rows / 128 * tile_rows : rows;
+}
+
 // Raises a kernel's dynamic shared-memory limit on the current device, once per
 // device (the attribute is per device; `done` is the kernel's own bit mask).
 template <typename Kernel>

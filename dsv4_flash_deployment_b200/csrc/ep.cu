@@ -265,8 +265,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
         const int le = id - owner * p.e_local;
         const int slot = atomicAdd_system(p.peer_cnt[owner] + le, 1);
         int row = -1;
-        if (slot < p.cap_e) {
-          row = le * p.cap_e + slot;
+        if (slot < seg_pairs(p.cap_e, p.tile_rows)) {
+          row = le * p.cap_e + seg_row(slot, p.tile_rows);
         } else {
           report_error(p.err, ERR_CAPACITY, KID_MOE, 3);
         }
@@ -329,7 +329,8 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
   int c = 0;
   if (e < p.e_local) {
     c = p.cnt[e];
-    if (c > p.cap_e) c = p.cap_e;   // dispatch reported the overflow; rows beyond cap_e were not written
+    // dispatch reported an overflow; pairs past the segment were not written
+    c = min(c, seg_pairs(p.cap_e, p.tile_rows));
     p.cnt[e] = 0;                   // re-armed for the next layer (see the counter-reuse note above)
   }
   const int tl = (c + p.tile_rows - 1) / p.tile_rows;
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
   int rt = toff;
   for (int r0 = 0; r0 < c; r0 += p.tile_rows, ++rt) {
     const int valid = min(p.tile_rows, c - r0);
-    const int b0 = e * p.cap_e + r0;
+    const int b0 = e * p.cap_e + seg_tile_row(r0, p.tile_rows);
     for (int mt = 0; mt < mt13; ++mt)
       p.tiles13[(size_t)rt * mt13 + mt] = make_int4(e * p.m13 + mt * 128, b0, valid, mt * 128);
     for (int mt = 0; mt < mt2; ++mt)
@@ -376,7 +377,8 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
 }
 
 cudaError_t ep_plan(const EpPlanParams& p, cudaStream_t st) {
-  if (p.e_local < 1 || p.e_local > 1024 || p.cap_e % 256 || p.tile_rows % 128 || p.m13 % 128 || p.m2 % 128)
+  if (p.e_local < 1 || p.e_local > 1024 || p.cap_e % 256 || p.m13 % 128 || p.m2 % 128 ||
+      (p.tile_rows != 32 && p.tile_rows != 64 && p.tile_rows != 128 && p.tile_rows != 256))
     return cudaErrorInvalidValue;
   launch_pdl(ep_plan_kernel, 1, 1024, 0, st, p);
   return cudaGetLastError();

@@ -179,7 +179,7 @@ struct MoePlanParams {
   int* counts;                      // [E_local] scratch (zeroed by the plan)
   int* seg_start;                   // [E_local]
   int* rank;                        // [T, topk] scratch
-  int tile_rows;                    // 128 or 256
+  int tile_rows;                    // token rows per GEMM tile: 32, 64 (one 128-row slot each), 128 or 256
   int m13, m2;                      // W13 / W2 output rows per expert
   int4* tiles13;
   int* n_tiles13;
@@ -265,6 +265,7 @@ struct EpDispatchParams {
   const uint8_t* xq;          // [>= T, D] e4m3 token rows
   const uint8_t* xsf;         // their scale chunks
   int D, e_local, cap_e, world, rank;
+  int tile_rows;              // GEMM tile rows (the row layout of an expert segment, seg_row)
   uint8_t* const* peer_x;     // [world] expert rows [e_local * cap_e, D] of each rank
   uint8_t* const* peer_xsf;   // [world] their scale chunks
   float* const* peer_rscale;  // [world] routing weight per expert row

@@ -4,6 +4,7 @@
 //   experts = top-k of (score + bias) (ties -> lower expert id); weights =
 //   score / sum(score) * route_scale (reference.py:355-382).  One warp per token.
 // moe_plan: per-expert counts -> 128-row-aligned segments of the permuted
+//   activation buffer (tiles under 128 rows get a 128-row slot each, seg_rows)
 //   activation buffer -> GEMM tile lists for W13 and W2 (device-built, so the
 //   whole MoE block replays inside a CUDA graph) -> permuted row of every
 //   (token, slot) and its routing weight.
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
     const int e = threadIdx.x;
     const int lane = e & 31, w = e >> 5;
     const int c = e < p.E_local ? cnt[e] : 0;
-    const int rows = (c + 127) & ~127;
+    const int rows = seg_rows(c, p.tile_rows);
     const int tl = (c + p.tile_rows - 1) / p.tile_rows;
     int ir = rows, it = tl;   // inclusive within the warp
 #pragma unroll
@@ -137,10 +138,11 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
     int rt = toff[e];
     for (int r0 = 0; r0 < c; r0 += p.tile_rows, ++rt) {
       const int valid = min(p.tile_rows, c - r0);
+      const int b0 = start[e] + seg_tile_row(r0, p.tile_rows);
       for (int mt = 0; mt < mt13; ++mt)
-        p.tiles13[(size_t)rt * mt13 + mt] = make_int4(e * p.m13 + mt * 128, start[e] + r0, valid, mt * 128);
+        p.tiles13[(size_t)rt * mt13 + mt] = make_int4(e * p.m13 + mt * 128, b0, valid, mt * 128);
       for (int mt = 0; mt < mt2; ++mt)
-        p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, start[e] + r0, valid, mt * 128);
+        p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, b0, valid, mt * 128);
     }
   }
   for (int sg = 0; sg < n_seg; ++sg) {
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
       const int i = sg * seg_len + j;
       const int e = p.ids[i] - p.e_begin;
       if (ok && e >= 0 && e < p.E_local) {
-        const int row = start[e] + p.rank[i];
+        const int row = start[e] + seg_row(p.rank[i], p.tile_rows);
         p.pos[i] = row;
         p.row_scale[row] = p.wts[i];
       } else {
@@ -161,6 +163,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
 
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
   if (p.E_local < 1 || p.E_local > 1024) return cudaErrorInvalidValue;
+  if (p.tile_rows != 32 && p.tile_rows != 64 && p.tile_rows != 128 && p.tile_rows != 256) return cudaErrorInvalidValue;
   if (p.seg_cnt && (p.seg_cap < 1 || (p.T * p.topk) % p.seg_cap)) return cudaErrorInvalidValue;
   const int smem = (3 * p.E_local + 2) * 4;
   launch_pdl(moe_plan_kernel, 1, 1024, smem, st, p);

@@ -25,6 +25,7 @@ from __future__ import annotations
 import contextlib
 import itertools
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -243,11 +244,20 @@ class DSV4Model:
         elif self.tp is not None:
             e_local = self.tp.experts_per_rank(E)
         recv_rows = T * k if self.ep is None else self.ep.recv_rows(T, k)
-        self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
         # 128-row expert tiles keep two accumulators in TMEM (epilogue overlaps the
         # next tile); 256-row tiles halve weight re-reads when experts get many rows
-        # (decided on the expected rows per rank, T*k, not on the worst-case capacity)
-        self.tile_rows = 128 if T * k <= 192 * e_local else 256
+        # (decided on the expected rows per rank, T*k, not on the worst-case capacity);
+        # DSV4_EXPERT_TILE_ROWS=32/64/128/256 overrides (32/64-row tiles take a
+        # 128-row slot each and a deeper shared-memory pipeline)
+        self.tile_rows = int(os.environ.get("DSV4_EXPERT_TILE_ROWS", "0")) or (
+            128 if T * k <= 192 * e_local else 256)
+        if self.tile_rows not in (32, 64, 128, 256):
+            raise ValueError(f"expert tile rows {self.tile_rows}: 32, 64, 128 or 256")
+        # worst-case permuted rows: every expert's segment rounded up (seg_rows in common.cuh)
+        if self.tile_rows >= 128:
+            self.cap = ceil_to(recv_rows + e_local * 127 + 128, 128)
+        else:
+            self.cap = ceil_to(-(-recv_rows // self.tile_rows) * 128 + e_local * 128 + 128, 128)
         tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
         # expert intermediate width on this rank (a tensor-parallel expert split keeps 1/N)
         I = self.tp.inter_local(cfg.moe_inter_dim) if self.tp is not None else cfg.moe_inter_dim

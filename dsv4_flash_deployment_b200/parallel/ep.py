@@ -135,7 +135,10 @@ class EPGroup:
         import torch.distributed._symmetric_memory as symm_mem
 
         W = self.world
-        cap_e = ceil_to(max(1, T) * W, 256)
+        # rows per expert: every pair of every rank, in the GEMM tiles' row layout
+        # (tiles under 128 rows each take a 128-row slot)
+        pairs = max(1, T) * W
+        cap_e = ceil_to(pairs if tile_rows >= 128 else -(-pairs // tile_rows) * 128, 256)
         rows = e_local * cap_e
         kt = D // 128
         sizes = [rows * D, (rows // 128) * kt * 512, rows * 4, rows * 4, e_local * 4, max(1, T * k) * D * 2, 2 * W * 4]
@@ -152,7 +155,7 @@ class EPGroup:
         table = lambda i: torch.tensor([p + offs[i] for p in ptrs], dtype=torch.int64, device=self.dev)
         view = lambda i: buf[offs[i]:offs[i] + sizes[i]]
         e = lambda *s_, dt: torch.empty(*s_, dtype=dt, device=self.dev)
-        tiles_max = (T * W * k) // tile_rows + e_local + 1
+        tiles_max = (T * W * k) // tile_rows + e_local + 1   # sum over experts of ceil(rows / tile_rows)
         b = dict(
             cap_e=cap_e, rows=rows, k=k, tile_rows=tile_rows, symm=buf, symm_handle=hdl,
             x=view(0).view(rows, D), xsf=view(1), rscale=view(2).view(torch.float32),
@@ -195,7 +198,8 @@ class EPGroup:
         ids, wts, _, _ = model.route[k]
         with model._t("ep_dispatch"):
             ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
-                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tab_cpu"], model.err, b["sync0"])
+                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], b["tab_cpu"],
+                            model.err, b["sync0"])
         with model._t("ep_plan"):
             ext.ep_plan(b["sync0"], b["cnt"], b["cap_e"], b["tile_rows"], 2 * I, D, b["tiles13"], b["nt13"],
                         b["tiles2"], b["nt2"], model.err)

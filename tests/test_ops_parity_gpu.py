@@ -128,3 +128,130 @@ def test_qkv_post_matches_oracle(T):
     assert _cos(kv, kv_ref) > 0.99999
     assert float((kv.cpu().float() != kv_ref.float()).float().mean()) < 0.01
     assert math.isfinite(float(kv.float().abs().max()))
+
+
+@pytest.mark.parametrize("T", [1, 19])
+def test_engram_gate_matches_oracle(T):
+    """Engram gate: per stream s, dot = <h_s * w_s, key_s> * rsqrt(ms(h_s)) * rsqrt(ms(key_s))
+    / sqrt(D), g = sigmoid(signed sqrt(dot)), h_s += g * value (ref/model.py ``_engram``)."""
+    ext = _ext.load(required=True)
+    D, eps = 1024, 1e-6
+    g = torch.Generator().manual_seed(7 + T)
+    X = torch.randn(T, HC, D, generator=g).to(torch.bfloat16)
+    kv = torch.randn(T, (HC + 1) * D, generator=g).to(torch.bfloat16)
+    wgt = 1.0 + 0.1 * torch.randn(HC, D, generator=g)
+    Xd = X.cuda().clone()
+    ext.engram_gate(Xd, kv.cuda(), wgt.cuda().contiguous(), T, eps)
+    torch.cuda.synchronize()
+
+    hf = X.float()
+    key = kv[:, :HC * D].float().reshape(T, HC, D)
+    val = kv[:, HC * D:].float()
+    rstd = torch.rsqrt(hf.square().mean(-1) + eps) * torch.rsqrt(key.square().mean(-1) + eps)
+    dot = (hf * wgt * key).sum(-1) * rstd * D ** -0.5
+    gate = torch.sigmoid(torch.copysign(torch.sqrt(dot.abs().clamp_min(1e-6)), dot))
+    ref = (hf + gate[..., None] * val[:, None, :]).to(torch.bfloat16)
+    _ulp_close(Xd.cpu(), ref, max_mismatch=0.02)
+
+
+@pytest.mark.parametrize("r,co", [(4, 2), (16, 1)])
+def test_compress_pool_matches_oracle(r, co):
+    """Compressor of one prefill chunk at positions 0..T-1: softmax-gated pooling of the
+    group's r projections (2r with the overlap: the previous group's first half),
+    RMSNorm, RoPE at the group start, e2m1 / e4m3-per-16 round trip; the indexer key
+    from the same latent (bf16 GEMV, RMSNorm, RoPE, e2m1 / ue8m0-per-32).  Reference:
+    ``ref/model.py`` ``_compressor`` and ``_indexer``."""
+    from dsv4_flash_deployment_b200.config import v4_flash_config
+
+    ext = _ext.load(required=True)
+    cfg = v4_flash_config(n_layers=2)
+    dh, kd, eps = 512, 128, cfg.rms_norm_eps
+    T = 4 * r + 3
+    g_ = torch.Generator().manual_seed(31 * r + co)
+    proj = torch.randn(T, 2 * co * dh, generator=g_)
+    ape = torch.randn(r, co * dh, generator=g_) * 0.5
+    norm_w = (1.0 + 0.1 * torch.randn(dh, generator=g_)).to(torch.bfloat16)
+    wk = (torch.randn(kd, dh, generator=g_) * dh ** -0.5).to(torch.bfloat16)
+    k_norm = (1.0 + 0.1 * torch.randn(kd, generator=g_)).to(torch.bfloat16)
+    cos, sin = N.layer_rope_tables(cfg, 4096)["yarn"]
+    closes = [p for p in range(T) if (p + 1) % r == 0]
+    G = len(closes)
+
+    dev = "cuda"
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+    max_c = 64
+    comp = torch.zeros(2, max_c, dh, dtype=torch.bfloat16, device=dev)
+    idx = torch.zeros(2, max_c, kd, dtype=torch.bfloat16, device=dev)
+    ring = torch.zeros(2, co * r, 2 * co * dh, dtype=torch.float32, device=dev)
+    ext.compress_pool(G, i32([G]), i32([0] * G), i32([p // r for p in closes]), i32([0] * G), i32([0] * G), r, co,
+                      proj.to(dev), ape.to(dev), ring, norm_w.to(dev), eps, cos.to(dev).contiguous(),
+                      sin.to(dev).contiguous(), comp, wk.to(dev), k_norm.to(dev), idx, None)
+    torch.cuda.synchronize()
+
+    d = dh
+    sc_all = proj[:, co * dh:] + ape[torch.arange(T) % r]
+    kv_all = proj[:, :co * dh]
+    for gi, p in enumerate(closes):
+        g = p // r
+        kvs, scs = [], []
+        if co == 2:
+            for t in range((g - 1) * r, g * r):
+                if t >= 0:
+                    kvs.append(kv_all[t, :d])
+                    scs.append(sc_all[t, :d])
+        for t in range(g * r, (g + 1) * r):
+            kvs.append(kv_all[t, (co - 1) * d:])
+            scs.append(sc_all[t, (co - 1) * d:])
+        kv_s, sc_s = torch.stack(kvs), torch.stack(scs)
+        pooled = (kv_s * torch.softmax(sc_s, 0)).sum(0)
+        latent = N.rms_norm(pooled.to(torch.bfloat16), norm_w, eps)
+        c, s = cos[g * r], sin[g * r]
+        want = N.fp4_act_quant_roundtrip(N.apply_rope(latent, c, s), 16, "e4m3")
+        got = comp[0, g].cpu()
+        assert _cos(got, want) > 0.9995, (g, _cos(got, want))
+        assert float((got.float() != want.float()).float().mean()) < 0.05
+        k = N.rms_norm(N.bf16_linear(latent[None], wk), k_norm, eps)
+        k_want = N.fp4_act_quant_roundtrip(N.apply_rope(k, c, s), 32, "e8m0")[0]
+        k_got = idx[0, g].cpu()
+        assert _cos(k_got, k_want) > 0.999, (g, _cos(k_got, k_want))
+
+
+@pytest.mark.parametrize("tile_rows", [32, 64, 256])
+def test_expert_tile_rows_layouts_match(tile_rows, monkeypatch):
+    """The MoE plan's row layouts (32/64-row tiles in 128-row slots, packed 128 / 256-row
+    tiles) give the same logits as the default layout: every expert row is computed
+    the same way whatever tile it lands in."""
+    from test_model_gpu import small_v4
+
+    from dsv4_flash_deployment_b200.engine.builder import build_model
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
+    from dsv4_flash_deployment_b200.models.model import SeqChunk, StepMeta
+    from dsv4_flash_deployment_b200.ops.gemm import ErrorWord
+
+    cfg = small_v4()
+    w = make_random_weights(cfg, seed=3, include_mtp=False)
+
+    def run():
+        m = build_model(cfg, "cuda", max_tokens=96, n_slots=4, max_seq_len=128, weights=w)
+        out = []
+        g = torch.Generator().manual_seed(1)
+        for step in range(3):
+            if step == 0:
+                meta = StepMeta(cfg, [SeqChunk(i, 0, torch.randint(16, 1000, (20 + 7 * i,), generator=g).tolist(),
+                                               True) for i in range(3)])
+            else:
+                meta = StepMeta(cfg, [SeqChunk(i, 19 + 7 * i + step, [int(40 + 11 * i + step)], True)
+                                      for i in range(3)])
+            m.upload(meta)
+            m.forward(meta)
+            out.append(m.logits[:3].clone())
+        torch.cuda.synchronize()
+        ErrorWord.check("cuda")
+        return torch.stack(out)
+
+    monkeypatch.delenv("DSV4_EXPERT_TILE_ROWS", raising=False)
+    base = run()
+    monkeypatch.setenv("DSV4_EXPERT_TILE_ROWS", str(tile_rows))
+    other = run()
+    assert _cos(base, other) > 0.99999
+    assert torch.equal(base.argmax(-1), other.argmax(-1))
