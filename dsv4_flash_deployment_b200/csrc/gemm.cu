@@ -52,7 +52,8 @@ struct GemmSmem {
   static constexpr int kStage = kA + kB + kSf;
   static constexpr int kXbuf = 4 * 32 * 32 * 4;        // SwiGLU exchange (4 warps x 32 cols x 32 lanes)
   static constexpr int kBarriers = 256;
-  static constexpr int kTotal = 1024 + kStages * kStage + kXbuf + kBarriers;
+  static constexpr int kRetPtrs = 32 * 8;              // return-row destinations of one 32-token chunk
+  static constexpr int kTotal = 1024 + kStages * kStage + kXbuf + kBarriers + kRetPtrs;
   static_assert(kTotal <= 227 * 1024, "GEMM shared memory exceeds the per-CTA limit");
   static_assert(8 * (2 * kStages + 2 * 2 + 1) + 16 <= kBarriers, "barrier region too small");
   // TMEM: NUM_ACC accumulator buffers (double-buffered when they fit, so the
@@ -151,6 +152,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sSF = sB + S * L::kB;
   float* xbuf = reinterpret_cast<float*>(sSF + S * L::kSf);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + L::kXbuf);
+  uint8_t** ret_rows = reinterpret_cast<uint8_t**>(reinterpret_cast<uint8_t*>(bars) + L::kBarriers);
   constexpr int NA = L::kNumAcc;
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
@@ -565,6 +567,12 @@ __global__ void __launch_bounds__(192, 1)
           // whole 256-byte (bf16) / 512-byte (fp32) token rows with 16-byte writes.
           constexpr int kEl = EPI == EPI_F32 ? 4 : 2;
           uint8_t* stage = reinterpret_cast<uint8_t*>(xbuf);   // 32 x 128 x 4 B = 16 KB
+          if (GROUPED && p.ret_meta != nullptr && row < kCols && c0 + row < th.b_valid) {
+            // destination row of each token of the chunk, resolved once (its load
+            // overlaps the staging below instead of sitting in front of every store)
+            const int mt = __ldg(p.ret_meta + th.b_row0 + c0 + row);
+            ret_rows[row] = reinterpret_cast<uint8_t*>(p.ret_peer[mt >> 24]) + (size_t)(mt & 0xffffff) * p.ldo * kEl;
+          }
 #pragma unroll
           for (int j = 0; j < kCols; ++j) {
             float x = v[j];
@@ -585,10 +593,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint4 val = reinterpret_cast<const uint4*>(stage + (size_t)j * 128 * kEl)[vi];
             if (GROUPED && p.ret_meta != nullptr) {
               // expert-parallel return: straight into the source rank's buffer (NVLink)
-              const int mt = __ldg(p.ret_meta + th.b_row0 + c0 + j);
-              uint8_t* dst = reinterpret_cast<uint8_t*>(p.ret_peer[mt >> 24]) +
-                             ((size_t)(mt & 0xffffff) * p.ldo + th.out_col0) * kEl;
-              reinterpret_cast<uint4*>(dst)[vi] = val;
+              reinterpret_cast<uint4*>(ret_rows[j] + (size_t)th.out_col0 * kEl)[vi] = val;
             } else if (full_m) {
               reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (orow + th.out_col0) * kEl)[vi] = val;
             } else {
