@@ -24,30 +24,46 @@ DSV4_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
 
 // Called by every thread of every CTA after the CTA's last global store of the
 // phase; the last CTA to arrive advances the epoch and release-stores it into
-// slot [phase * world + rank] of every rank's signal array.
+// slot [phase * world + rank] of every rank's signal array.  The world stores
+// are issued by as many threads at once (one NVLink round trip instead of one
+// per peer): thread 0's system fence, taken after it observed every other CTA's
+// arrival, is ordered before them by the barrier.
 DSV4_DEV void peer_publish_grid(const PeerSync& s) {
   if (s.done == nullptr) return;
+  __shared__ uint32_t s_pub_epoch;
+  __shared__ int s_pub_last;
   __syncthreads();
-  if (threadIdx.x != 0) return;
-  __threadfence_system();
-  const int n_cta = (int)(gridDim.x * gridDim.y * gridDim.z);
-  if (atomicAdd(s.done, 1) != n_cta - 1) return;
-  *s.done = 0;
-  const uint32_t ep = *s.epoch + 1u;
-  *s.epoch = ep;
-  __threadfence_system();
-  for (int r = 0; r < s.world; ++r) st_release_sys(s.peer_sig[r] + s.phase * s.world + s.rank, ep);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int n_cta = (int)(gridDim.x * gridDim.y * gridDim.z);
+    const bool last = atomicAdd(s.done, 1) == n_cta - 1;
+    if (last) {
+      *s.done = 0;
+      const uint32_t ep = *s.epoch + 1u;
+      *s.epoch = ep;
+      __threadfence_system();
+      s_pub_epoch = ep;
+    }
+    s_pub_last = last;
+  }
+  __syncthreads();
+  if (s_pub_last && (int)threadIdx.x < s.world)
+    st_release_sys(s.peer_sig[threadIdx.x] + s.phase * s.world + s.rank, s_pub_epoch);
 }
 
-// Single-CTA form (thread 0 publishes; the caller's stores of the phase precede it).
+// Single-CTA form (the caller's stores of the phase precede it).
 DSV4_DEV void peer_publish_cta(const PeerSync& s) {
+  __shared__ uint32_t s_pub_epoch;
   __syncthreads();
-  if (threadIdx.x != 0) return;
-  __threadfence_system();
-  const uint32_t ep = *s.epoch + 1u;
-  *s.epoch = ep;
-  __threadfence_system();
-  for (int r = 0; r < s.world; ++r) st_release_sys(s.peer_sig[r] + s.phase * s.world + s.rank, ep);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t ep = *s.epoch + 1u;
+    *s.epoch = ep;
+    __threadfence_system();
+    s_pub_epoch = ep;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < s.world) st_release_sys(s.peer_sig[threadIdx.x] + s.phase * s.world + s.rank, s_pub_epoch);
 }
 
 // Thread 0 waits until every rank has published this rank's current epoch of

@@ -41,7 +41,15 @@ from ..ops.layout import ceil_to
 
 
 class EPGroup:
-    def __init__(self, rank: int, world: int, group=None, device=None, transport: str = "nccl"):
+    def __init__(self, rank: int, world: int, group=None, device=None, transport: str = "nccl",
+                 shared_first: bool | None = None):
+        """``shared_first`` (fused transport): run the shared expert between the
+        dispatch and the plan's wait instead of after the W2 GEMM (default from
+        ``DSV4_EP_SHARED_FIRST``, off)."""
+        import os
+
+        self.shared_first = (os.environ.get("DSV4_EP_SHARED_FIRST", "0") == "1") if shared_first is None \
+            else shared_first
         self.rank = rank
         self.world = world
         self.group = group
@@ -200,6 +208,10 @@ class EPGroup:
             ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
                             ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], b["tab_cpu"],
                             model.err, b["sync0"])
+        if self.shared_first:
+            # the shared expert runs while the peers' dispatched rows are in flight
+            with model._t("shared_expert"):
+                model._shared_expert(L, T)
         with model._t("ep_plan"):
             ext.ep_plan(b["sync0"], b["cnt"], b["cap_e"], b["tile_rows"], 2 * I, D, b["tiles13"], b["nt13"],
                         b["tiles2"], b["nt2"], model.err)
@@ -212,8 +224,10 @@ class EPGroup:
             ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["rows"], I), b["hsf"], None, ex.w2.q.shape[0],
                      b["rows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None, 0.0, D, D, None, None,
                      model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"])
-        with model._t("shared_expert"):
-            model._shared_expert(L, T)
+        if not self.shared_first:
+            # the shared expert runs while the expert rows travel back
+            with model._t("shared_expert"):
+                model._shared_expert(L, T)
         return b["back"], b["pos_id"], k, b["hc_desc"]
 
     def release(self) -> None:
