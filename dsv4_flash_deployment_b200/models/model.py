@@ -293,7 +293,11 @@ class DSV4Model:
         # split-K scratch (reused sequentially on the stream)
         self.ws = e(8 * 1024 * 1024, dt=f32)
         self.counters = z(65536, dt=i32)
-        self.attn_ws = e(max(1, min(T, 8)) * 16 * 64 * 514, dt=f32)
+        # split-row attention at decode sizes: T <= 8 tokens x up to 32 splits
+        self.attn_splits = int(os.environ.get("DSV4_ATTN_SPLITS", "8"))
+        if not 1 <= self.attn_splits <= 32:
+            raise ValueError("DSV4_ATTN_SPLITS must be 1..32")
+        self.attn_ws = e(max(1, min(T, 8)) * max(16, self.attn_splits) * 64 * 514, dt=f32)
         # step metadata (device)
         self.m_ids, self.m_pos, self.m_slot = e(T, dt=i32), e(T, dt=i32), e(T, dt=i32)
         self.m_cstart, self.m_row0, self.m_last = e(T, dt=i32), e(T, dt=i32), e(T, dt=i32)
@@ -610,7 +614,7 @@ class DSV4Model:
             comp = self.comp[src]
         splits = 1
         if T <= 8:
-            splits = 8
+            splits = self.attn_splits
         tctx = self._t("attention")
         tctx.__enter__()
         ext.attention(self.q, cos, sin, None, cfg.q_head_norm, cfg.rms_norm_eps, self.kv_step, ring, comp,
