@@ -44,6 +44,8 @@ def main() -> None:
     ap.add_argument("--device-trace", action="store_true",
                     help="graph-replayed step with device timestamp marks (multi-rank capable)")
     ap.add_argument("--json-out", default=None, help="also write the table as JSON here (rank 0)")
+    ap.add_argument("--ep-loopback", action="store_true",
+                    help="run the fused expert-parallel kernels at world size 1 (under torchrun --nproc-per-node 1)")
     a = ap.parse_args()
     import os
 
@@ -56,9 +58,11 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     ep = None
-    if world > 1:
+    if world > 1 or a.ep_loopback:
+        # --ep-loopback: the fused expert-parallel path at world size 1 (this GPU is its only peer)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), transport=a.ep_transport)
+        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local),
+                     transport="fused" if a.ep_loopback else a.ep_transport)
     kw = {"n_layers": a.layers} if a.layers else {}
     if a.experts:
         kw["n_routed_experts"] = a.experts
@@ -107,7 +111,7 @@ def main() -> None:
             print(f"{k:20s} {v:9.3f} ms  {100 * v / total:5.1f}%  ({len(m.op_timer[k]) // a.steps} launches/step)")
         print(json.dumps({"step_ms": round(total, 3), "sum_ops_ms": round(acc, 3), "T": T, "n_layers": cfg.n_layers,
                           "expert_storage_layers": n_phys, "world": world}))
-    if world > 1:
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
 
@@ -123,7 +127,7 @@ def _device_trace(a, eng, cfg, meta, rank, world, T, n_phys) -> None:
     tr = DeviceTrace(dev)
 
     def barrier():
-        if world > 1:
+        if dist.is_initialized():
             dist.barrier()
 
     with torch.cuda.stream(st):
@@ -183,7 +187,7 @@ def _device_trace(a, eng, cfg, meta, rank, world, T, n_phys) -> None:
     vals = torch.tensor([summ[k]["ms"] for k in names] + [plain_ms, sum(totals) / len(totals)], dtype=torch.float64,
                         device=dev)
     vmax = vals.clone()
-    if world > 1:
+    if dist.is_initialized():
         dist.all_reduce(vmax, op=dist.ReduceOp.MAX)
     vmax = vmax.tolist()
     v0 = vals.tolist()
@@ -202,7 +206,7 @@ def _device_trace(a, eng, cfg, meta, rank, world, T, n_phys) -> None:
             with open(a.json_out, "w") as f:
                 json.dump(res, f, indent=1)
     del g_tr, g_plain
-    if world > 1:
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
 
