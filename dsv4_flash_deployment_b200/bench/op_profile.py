@@ -46,6 +46,9 @@ def main() -> None:
     ap.add_argument("--json-out", default=None, help="also write the table as JSON here (rank 0)")
     ap.add_argument("--ep-loopback", action="store_true",
                     help="run the fused expert-parallel kernels at world size 1 (under torchrun --nproc-per-node 1)")
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1: the tensor-parallel decode layout (every rank runs the same tokens; use with "
+                         "--decode-only --concurrency 1 for the C=1 step)")
     a = ap.parse_args()
     import os
 
@@ -57,12 +60,20 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    ep = None
+    ep = tp = None
     if world > 1 or a.ep_loopback:
-        # --ep-loopback: the fused expert-parallel path at world size 1 (this GPU is its only peer)
+        # --ep-loopback: the fused expert-parallel path at world size 1 (this GPU is its only peer);
+        # runs without torchrun too (one process, a one-rank group at 127.0.0.1)
+        for k_, v_ in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29599"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+            os.environ.setdefault(k_, v_)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-        ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local),
-                     transport="fused" if a.ep_loopback else a.ep_transport)
+        if a.tp:
+            from ..parallel.tp import TPGroup
+            tp = TPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local), moe="ep")
+        else:
+            ep = EPGroup(rank, world, dist.group.WORLD, torch.device("cuda", local),
+                         transport="fused" if a.ep_loopback else a.ep_transport)
+    per_rank = 1 if tp is not None else world     # the tensor-parallel layout replicates the tokens
     kw = {"n_layers": a.layers} if a.layers else {}
     if a.experts:
         kw["n_routed_experts"] = a.experts
@@ -70,15 +81,15 @@ def main() -> None:
         kw["n_activated_experts"] = a.topk
     cfg = v4_flash_config(**kw)
     dev = torch.device("cuda", local)
-    n_dec = a.concurrency // world - (0 if a.decode_only else 1)
-    chunk = 0 if a.decode_only else a.chunk // world
+    n_dec = a.concurrency // per_rank - (0 if a.decode_only else 1)
+    chunk = 0 if a.decode_only else a.chunk // per_rank
     T = n_dec + chunk
     max_seq = a.context + 1024 + 16
     n_phys = plan_expert_storage(cfg, dev, T, n_dec + 2, max_seq, world)
     eng = Engine.build(cfg, dev, max_seqs=n_dec + 2, max_batched_tokens=T, max_seq_len=max_seq,
-                       expert_storage_layers=n_phys, use_graphs=False, ep=ep)
+                       expert_storage_layers=n_phys, use_graphs=False, ep=ep, tp=tp)
     m = eng.model
-    rng = np.random.default_rng(0)
+    rng = np.random.default_rng(0)     # the same seed on every rank: identical steps under --tp
     dec = a.context + (np.arange(n_dec) * (1024 // max(1, n_dec)) + 1) % 1024
 
     def meta(i):

@@ -246,11 +246,15 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const in
 // dimension, and every pair is sent to all tp of them (copy c = pair j, partner
 // q with c = j * tp + q); partner q's W2 writes its partial row to return row
 // (t * topk + j) * tp + q of the source.
+constexpr int kDispatchMaxD = 8192;   // hidden sizes the dispatch stages in shared memory
+
 template <int kMaxPer>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
   pdl_entry();
   __shared__ int s_owner[32], s_row[32], s_ret[32];
   __shared__ float s_w[32];
+  __shared__ uint4 s_xrow[kDispatchMaxD / 16];
+  __shared__ uint32_t s_sfw[kDispatchMaxD / 128];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = p.D;
@@ -288,25 +292,27 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
         s_ret[lane] = (t * p.topk + j) * tp + q;
       }
     }
-    __syncthreads();
-    // the token's row (D bytes, 16-byte vectors) and its scale words (one 4-byte
-    // word per 128 columns in the chunk layout); the warps' reads of the same
-    // row hit in L1/L2
+    // the token's row (D bytes) and its scale words (one 4-byte word per 128
+    // columns in the chunk layout) are staged in shared memory once, with every
+    // load in flight together, while warp 0 routes; then each warp streams its
+    // copies out of shared memory
     const int nvec = D / 16;
     const int m_src = t & 127;
     const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D);
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) s_xrow[i] = src[i];
+    for (int b = threadIdx.x; b < kt; b += blockDim.x)
+      s_sfw[b] = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + b) * 512 + (m_src & 31) * 16 +
+                                                    (m_src >> 5) * 4);
+    __syncthreads();
     for (int c = warp; c < copies; c += 8) {
       const int o = s_owner[c], r = s_row[c];
       if (r < 0) continue;
       uint4* dst = reinterpret_cast<uint4*>(p.peer_x[o] + (size_t)r * D);
-      for (int i = lane; i < nvec; i += 32) dst[i] = src[i];
+      for (int i = lane; i < nvec; i += 32) dst[i] = s_xrow[i];
       const int m = r & 127;
-      for (int b = lane; b < kt; b += 32) {
-        const uint32_t sfw = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + b) * 512 +
-                                                                (m_src & 31) * 16 + (m_src >> 5) * 4);
+      for (int b = lane; b < kt; b += 32)
         *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + b) * 512 + (m & 31) * 16 +
-                                     (m >> 5) * 4) = sfw;
-      }
+                                     (m >> 5) * 4) = s_sfw[b];
       if (lane == 0) {
         p.peer_rscale[o][r] = s_w[c];
         p.peer_meta[o][r] = (p.rank << 24) | s_ret[c];
@@ -317,7 +323,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
 }
 
 cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st) {
-  if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D < 128) return cudaErrorInvalidValue;
+  if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D < 128 || p.D > kDispatchMaxD)
+    return cudaErrorInvalidValue;
   if (p.tp < 1 || p.topk * p.tp > 32 || p.world % p.tp) return cudaErrorInvalidValue;
   if ((long long)p.T * p.topk * p.tp >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)std::max(1, p.T);   // every rank publishes, even with T = 0
