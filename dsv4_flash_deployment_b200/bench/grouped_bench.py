@@ -22,16 +22,17 @@ from ..ops.gemm import EPI_BF16, EPI_SWIGLU, KIND_MX8
 D, I = 4096, 2048
 
 
-def run(E: int, bns: list[int], iters: int = 20, seed: int = 0) -> dict:
+def run(E: int, bns: list[int], iters: int = 20, seed: int = 0, copies: int = 1) -> dict:
     ext = _ext.load(required=True)
     dev = "cuda"
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     u8 = torch.uint8
-    w13 = torch.randint(0, 120, (E * 2 * I, D), device=dev, dtype=u8, generator=g)
-    s13 = torch.full((E * 2 * I // 128, D // 128, 512), 120, device=dev, dtype=u8)
-    w2 = torch.randint(0, 120, (E * D, I), device=dev, dtype=u8, generator=g)
-    s2 = torch.full((E * D // 128, I // 128, 512), 120, device=dev, dtype=u8)
+    W13 = [torch.randint(0, 120, (E * 2 * I, D), device=dev, dtype=u8, generator=g) for _ in range(copies)]
+    S13 = [torch.full((E * 2 * I // 128, D // 128, 512), 120, device=dev, dtype=u8) for _ in range(copies)]
+    W2 = [torch.randint(0, 120, (E * D, I), device=dev, dtype=u8, generator=g) for _ in range(copies)]
+    S2 = [torch.full((E * D // 128, I // 128, 512), 120, device=dev, dtype=u8) for _ in range(copies)]
+    w13, w2 = W13[0], W2[0]
     rows = torch.randint(9, 64, (E,), generator=torch.Generator().manual_seed(seed)).tolist()
     R = E * 128
     x = torch.randint(0, 120, (R, D), device=dev, dtype=u8, generator=g)
@@ -45,24 +46,26 @@ def run(E: int, bns: list[int], iters: int = 20, seed: int = 0) -> dict:
     t2 = i32([[e * D + mt * 128, e * 128, rows[e], mt * 128] for e in range(E) for mt in range(D // 128)])
     n13, n2 = i32([len(t13)]), i32([len(t2)])
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    out = {"experts": E, "rows_mean": round(sum(rows) / E, 2)}
+    out = {"experts": E, "rows_mean": round(sum(rows) / E, 2), "weight_copies": copies}
     for bn in bns:
-        def f13():
-            ext.gemm(KIND_MX8, EPI_SWIGLU, w13, s13, x, xsf, None, w13.shape[0], R, D, bn, 1, t13, n13, rs, h, hsf,
-                     10.0, 2 * I, 0, None, None, err, 0, 1, None, None, None)
+        def f13(i):
+            c = i % copies
+            ext.gemm(KIND_MX8, EPI_SWIGLU, W13[c], S13[c], x, xsf, None, w13.shape[0], R, D, bn, 1, t13, n13, rs, h,
+                     hsf, 10.0, 2 * I, 0, None, None, err, 0, 1, None, None, None)
 
-        def f2():
-            ext.gemm(KIND_MX8, EPI_BF16, w2, s2, h, hsf, y, w2.shape[0], R, I, bn, 1, t2, n2, None, None, None, 0.0,
-                     D, D, None, None, err, 0, 1, None, None, None)
+        def f2(i):
+            c = i % copies
+            ext.gemm(KIND_MX8, EPI_BF16, W2[c], S2[c], h, hsf, y, w2.shape[0], R, I, bn, 1, t2, n2, None, None, None,
+                     0.0, D, D, None, None, err, 0, 1, None, None, None)
 
-        for fn, name, nbytes in ((f13, "w13", w13.numel() + s13.numel()), (f2, "w2", w2.numel() + s2.numel())):
-            for _ in range(3):
-                fn()
+        for fn, name, nbytes in ((f13, "w13", w13.numel() + S13[0].numel()), (f2, "w2", w2.numel() + S2[0].numel())):
+            for i in range(3):
+                fn(i)
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            for _ in range(iters):
-                fn()
+            for i in range(iters):
+                fn(i)
             b.record()
             torch.cuda.synchronize()
             us = a.elapsed_time(b) / iters * 1e3
@@ -78,9 +81,10 @@ def main(argv=None) -> None:
     ap.add_argument("--experts", type=int, nargs="*", default=[32, 128, 256])
     ap.add_argument("--bn", type=int, nargs="*", default=[32, 64, 128])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--copies", type=int, default=1, help="separately allocated weight copies to cycle over")
     a = ap.parse_args(argv)
     for E in a.experts:
-        print(json.dumps(run(E, a.bn, a.iters)), flush=True)
+        print(json.dumps(run(E, a.bn, a.iters, copies=a.copies)), flush=True)
 
 
 if __name__ == "__main__":
