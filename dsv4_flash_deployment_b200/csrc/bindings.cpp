@@ -181,6 +181,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
                 "return rows: whole 128-row tiles, 16-byte rows");
     p.ret_meta = ret_meta->data_ptr<int>();
     p.ret_peer = reinterpret_cast<__nv_bfloat16* const*>(ret_peer->data_ptr<int64_t>());
+    p.ret_world = (int)ret_peer->numel();
   }
   if (p.splits > 1 && !(workspace && counters)) {
     // split-K through a thread-block cluster per tile (dense GEMMs, <= 8 splits).
@@ -603,7 +604,7 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, 
 void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
                  double route_scale, const optional<Tensor>& ids, const optional<Tensor>& wts, const Tensor& xq,
                  const Tensor& xsf, int64_t e_local, int64_t cap_e, int64_t tile_rows, int64_t tp_size,
-                 const Tensor& tables, const Tensor& err, const Tensor& pub) {
+                 int64_t ret_rows, const Tensor& tables, const Tensor& err, const Tensor& pub) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) == logits.size(1), "logits: f32 [T, E] contiguous");
@@ -628,6 +629,8 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
   p.cap_e = (int)cap_e;
   p.tile_rows = (int)tile_rows;
   p.tp = (int)tp_size;
+  p.rows = (int)(e_local * cap_e);
+  p.ret_rows = (int)ret_rows;
   p.peer_x = reinterpret_cast<uint8_t* const*>(tb[0]);
   p.peer_xsf = reinterpret_cast<uint8_t* const*>(tb[1]);
   p.peer_rscale = reinterpret_cast<float* const*>(tb[2]);

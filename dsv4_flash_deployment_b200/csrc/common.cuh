@@ -62,6 +62,10 @@ DSV4_DEV void report_error(uint32_t* err, uint32_t code, uint32_t kid, uint32_t 
 enum BoundsSite : uint32_t {
   BS_KV_ENTRY = 1,      // compressed entry index outside [0, max_c) or a negative slot
   BS_KV_UNMAPPED = 2,   // paged cache: the entry's block is not mapped (table entry < 0)
+  BS_EP_OWNER = 3,      // expert-parallel dispatch: owner rank or expert row out of range
+  BS_EP_RET = 4,        // expert-parallel dispatch: return row index out of range
+  BS_GEMM_TILE = 5,     // grouped GEMM tile outside the A or B operand rows
+  BS_GEMM_RET = 6,      // grouped GEMM return row: source rank out of range
 };
 
 using DbgSetter = cudaError_t (*)(uint32_t*);

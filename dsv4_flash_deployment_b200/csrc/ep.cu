@@ -286,6 +286,16 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
         } else {
           report_error(p.err, ERR_CAPACITY, KID_MOE, 3);
         }
+#ifdef DSV4_DEBUG_BOUNDS
+        if (owner < 0 || owner >= p.world || (row >= 0 && row >= p.rows)) {
+          dbg_bad(BS_EP_OWNER);
+          row = -1;
+        }
+        if ((t * p.topk + j) * tp + q >= p.ret_rows) {
+          dbg_bad(BS_EP_RET);
+          row = -1;
+        }
+#endif
         s_owner[lane] = owner;
         s_row[lane] = row;
         s_w[lane] = wj;

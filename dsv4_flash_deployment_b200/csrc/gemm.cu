@@ -121,6 +121,12 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
     t.b_valid = r.z;
     t.out_col0 = r.w;
     t.n_eff = min(BN, n_eff_for(r.z));
+#ifdef DSV4_DEBUG_BOUNDS
+    if (r.x < 0 || r.x + BM > p.M || r.y < 0 || r.y + t.n_eff > p.N || r.z < 0) {
+      dbg_bad(BS_GEMM_TILE);
+      return false;   // the rest of this CTA's work list is dropped
+    }
+#endif
   } else {
     const int m_tiles = p.M / BM;
     const int mt = tile % m_tiles, nt = tile / m_tiles;
@@ -570,7 +576,13 @@ __global__ void __launch_bounds__(192, 1)
           if (GROUPED && p.ret_meta != nullptr && row < kCols && c0 + row < th.b_valid) {
             // destination row of each token of the chunk, resolved once (its load
             // overlaps the staging below instead of sitting in front of every store)
-            const int mt = __ldg(p.ret_meta + th.b_row0 + c0 + row);
+            int mt = __ldg(p.ret_meta + th.b_row0 + c0 + row);
+#ifdef DSV4_DEBUG_BOUNDS
+            if ((mt >> 24) < 0 || (mt >> 24) >= p.ret_world) {
+              dbg_bad(BS_GEMM_RET);
+              mt = 0;
+            }
+#endif
             ret_rows[row] = reinterpret_cast<uint8_t*>(p.ret_peer[mt >> 24]) + (size_t)(mt & 0xffffff) * p.ldo * kEl;
           }
 #pragma unroll

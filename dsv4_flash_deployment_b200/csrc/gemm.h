@@ -52,6 +52,7 @@ struct GemmParams {
   // row straight into the source rank's memory over NVLink
   const int* ret_meta;
   __nv_bfloat16* const* ret_peer;
+  int ret_world;       // entries of ret_peer (checked in the debug-bounds build)
   uint32_t* err;
 };
 

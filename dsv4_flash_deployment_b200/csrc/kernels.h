@@ -271,6 +271,8 @@ struct EpDispatchParams {
   int D, e_local, cap_e, world, rank;
   int tile_rows;              // GEMM tile rows (the row layout of an expert segment, seg_row)
   int tp;                     // tensor-parallel partners per expert group (hybrid EP x TP; 1 = plain EP)
+  int rows;                   // expert rows of every rank (e_local * cap_e), for the debug-bounds build
+  int ret_rows;               // return rows of every rank (max tokens * topk * tp), for the debug-bounds build
   uint8_t* const* peer_x;     // [world] expert rows [e_local * cap_e, D] of each rank
   uint8_t* const* peer_xsf;   // [world] their scale chunks
   float* const* peer_rscale;  // [world] routing weight per expert row

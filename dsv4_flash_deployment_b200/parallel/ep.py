@@ -247,7 +247,7 @@ class EPGroup:
         with model._t("ep_dispatch"):
             ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
                             ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], self.tp,
-                            b["tab_cpu"], model.err, b["sync0"])
+                            b["back"].shape[0], b["tab_cpu"], model.err, b["sync0"])
         if self.shared_first:
             # the shared expert runs while the peers' dispatched rows are in flight
             with model._t("shared_expert"):

@@ -163,21 +163,33 @@ def main(argv=None):
         worker_loop(eng_tp, cpu_group, replicated=True)
         served = None
     eng_tp.graphs.clear()
+    # the control plane must deliver exactly what the same tensor-parallel engines
+    # produce when every rank steps them directly (the numerics against one GPU are
+    # the teacher-forced logits check above; free-running greedy tokens are reported:
+    # one near-tie flipped by the tensor-parallel summation order changes the rest)
+    tp3 = TPGroup(rank, world, dist.group.WORLD, dev, moe=a.moe)
+    eng_tp3 = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=64, max_seq_len=256, weights=w, tp=tp3)
+    direct = eng_tp3.generate(prompts, 6, ignore_eos=True)
+    eng_tp3.graphs.clear()
     eng_one = Engine.build(cfg, dev, max_seqs=2, max_batched_tokens=64, max_seq_len=256, weights=w)
     local = eng_one.generate(prompts, 6, ignore_eos=True)
     eng_one.graphs.clear()
-    serve_ok = torch.tensor([0 if rank != 0 or served == local else 1], device=dev)
+    n_tok = sum(len(x) for x in local)
+    same_one = sum(int(x == y) for p_, q_ in zip(direct, local) for x, y in zip(p_, q_))
+    serve_ok = torch.tensor([0 if rank != 0 or served == direct else 1], device=dev)
     dist.all_reduce(serve_ok)
     flag += serve_ok
     res = {"world": world, "family": a.family, "moe_split": a.moe, "min_logit_cos": worst, "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
-           "served_matches_one_gpu": bool(serve_ok.item() == 0),
+           "served_matches_direct": bool(serve_ok.item() == 0),
+           "direct_vs_one_gpu_tokens": f"{same_one}/{n_tok}" if rank == 0 else None,
            "decode_ms_graph": round(ms_graph, 4), "decode_ms_eager": round(ms_eager, 4),
            "decode_ms_one_gpu_graph": round(ms_one, 4), "layers": cfg.n_layers}
     if rank == 0:
         print(json.dumps(res), flush=True)
-    del m, eng_tp
+    del m, eng_tp, eng_tp3
     tp.release()
     tp2.release()
+    tp3.release()
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
