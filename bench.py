@@ -154,8 +154,6 @@ def main() -> None:
     ap.add_argument("--c1-moe", default="ep", choices=["ep", "tp"],
                     help="experts in the tensor-parallel C=1 model: owned whole (ep, shared with the batch model) "
                          "or split by intermediate index over all GPUs (tp)")
-    ap.add_argument("--ep-tp", type=int, default=1,
-                    help="hybrid EP x TP for the experts: partners per expert group (fused transport)")
     ap.add_argument("--ep-transport", default="fused", choices=["p2p", "nccl", "fused"],
                     help="expert exchange: fused (dispatch into the owners' expert rows, rows returned by the W2 "
                          "epilogue), p2p (peer-store pack/unpack kernels) or the NCCL all-to-all baseline")
@@ -202,8 +200,7 @@ def main() -> None:
         chunk_rank = (args.chunk // world) if args.chunk else max(1, -(-n_dec * isl // osl))
     max_tokens = n_dec + chunk_rank
     max_seq = isl + osl
-    ep = (ep_mod.EPGroup(rank, world, group, dev, transport=args.ep_transport, tp_size=args.ep_tp)
-          if world > 1 else None)
+    ep = ep_mod.EPGroup(rank, world, group, dev, transport=args.ep_transport) if world > 1 else None
     n_phys = plan_expert_storage(cfg, dev, max_tokens, c_rank + 1, max_seq, world)
     t_build = time.perf_counter()
     eng = Engine.build(cfg, dev, max_seqs=c_rank + 1, max_batched_tokens=max_tokens, max_seq_len=max_seq,
@@ -404,7 +401,7 @@ def main() -> None:
         # per-token row reads do not depend on the table size
         va = v41_bench.parser().parse_args(["--steps", str(max(3, min(args.steps, 6))), "--warmup", "2",
                                             "--spec-rounds", "8", "--engram-rows", "4000000",
-                                            "--ep-transport", args.ep_transport, "--ep-tp", str(args.ep_tp)])
+                                            "--ep-transport", args.ep_transport])
         try:
             r = v41_bench.measure(va, dev, rank, world, group)
             if rank == 0:
@@ -436,9 +433,7 @@ def main() -> None:
                 "seq_len": max_seq,
                 "workload": f"{args.workload} C={C} steady-state step: {n_dec * world} decode + "
                             f"{chunk_rank * world} prefill tokens",
-                "parallelism": (f"dp-attention{world} x ep{world}" if args.ep_tp == 1 else
-                                f"dp-attention{world} x ep{world // args.ep_tp} x tp{args.ep_tp} (experts)")
-                               if world > 1 else "single GPU",
+                "parallelism": f"dp-attention{world} x ep{world}" if world > 1 else "single GPU",
                 "weights": "fp8 e4m3 block-scaled dense (checkpoint-native), mxfp8 experts, bf16 activations",
                 "expert_storage_layers": n_phys,
                 "l2": "inputs larger than L2 (expert weights 6.6 GB/layer/all ranks, caches)",

@@ -78,7 +78,6 @@ def parser() -> argparse.ArgumentParser:
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel C=1 measurement")
     ap.add_argument("--ep-transport", default="fused", choices=["p2p", "nccl", "fused"])
-    ap.add_argument("--ep-tp", type=int, default=1, help="hybrid EP x TP partners per expert group (fused)")
     return ap
 
 
@@ -120,8 +119,7 @@ def measure(a, dev, rank: int, world: int, group) -> dict:
     chunk = max(1, a.chunk // world)
     max_tokens = n_dec + chunk
     max_seq = a.isl + a.osl
-    ep = (ep_mod.EPGroup(rank, world, group, dev, transport=a.ep_transport, tp_size=a.ep_tp)
-          if world > 1 else None)
+    ep = ep_mod.EPGroup(rank, world, group, dev, transport=a.ep_transport) if world > 1 else None
     # the DSpark stages' expert blocks (3 x 128 experts) come out of the reserve
     spec_gb = 0 if a.no_spec else cfg.n_mtp_layers * expert_block_bytes(
         dataclasses.replace(cfg, n_routed_experts=cfg.dspark_n_routed_experts), 1) / 2 ** 30
@@ -248,9 +246,7 @@ def measure(a, dev, rank: int, world: int, group) -> dict:
                        "global_batch": C, "seq_len": max_seq,
                        "workload": f"1k1k C={C} steady-state step: {n_dec * world} decode + {chunk * world} "
                                    "prefill tokens",
-                       "parallelism": (f"dp-attention{world} x ep{world}" if a.ep_tp == 1 else
-                                       f"dp-attention{world} x ep{world // a.ep_tp} x tp{a.ep_tp} (experts)")
-                                      if world > 1 else "single GPU",
+                       "parallelism": f"dp-attention{world} x ep{world}" if world > 1 else "single GPU",
                        "expert_storage_layers": n_phys, "cuda_graphs": not a.no_graphs,
                        "l2": "inputs larger than L2 (experts 7.2 GB per layer)",
                        "engram": {"rows_per_table": a.engram_rows, "tables_gb_pinned_host": round(tables_gb, 1),

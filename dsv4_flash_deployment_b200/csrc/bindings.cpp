@@ -172,12 +172,11 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int>());
   p.pub = peer_sync_of(publish);
   if (ret_meta || ret_peer) {
-    TORCH_CHECK(ret_meta && ret_peer && grouped && (epi == dsv4::EPI_BF16 || epi == dsv4::EPI_F32),
-                "return rows: grouped bf16 / f32 GEMMs with both tables");
+    TORCH_CHECK(ret_meta && ret_peer && grouped && epi == dsv4::EPI_BF16, "return rows: grouped bf16 GEMMs with both tables");
     TORCH_CHECK(ret_meta->is_cuda() && ret_meta->scalar_type() == at::kInt && ret_meta->numel() >= B.size(0),
                 "ret_meta: int32 device [B rows]");
     TORCH_CHECK(ret_peer->is_cuda() && ret_peer->scalar_type() == at::kLong, "ret_peer: int64 device pointer table");
-    TORCH_CHECK(M % 128 == 0 && m_valid % 128 == 0 && (ldo * (epi == dsv4::EPI_F32 ? 4 : 2)) % 16 == 0,
+    TORCH_CHECK(M % 128 == 0 && m_valid % 128 == 0 && (ldo * 2) % 16 == 0,
                 "return rows: whole 128-row tiles, 16-byte rows");
     p.ret_meta = ret_meta->data_ptr<int>();
     p.ret_peer = reinterpret_cast<__nv_bfloat16* const*>(ret_peer->data_ptr<int64_t>());
@@ -315,19 +314,12 @@ void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>&
     p.ids = reinterpret_cast<const int*>(v[11]);
     p.e_local = (int)v[12];
     p.err = reinterpret_cast<uint32_t*>(err->data_ptr<int>());
-    if (p.tp_mode == 5) {
-      // [..., ret_f32 address, tp_parts] after the 13 common fields
-      TORCH_CHECK(tp->numel() >= 15, "tp mode 5: int64 CPU [15]");
-      p.ret_f32 = reinterpret_cast<const float*>(v[13]);
-      p.tp_parts = (int)v[14];
-    }
     TORCH_CHECK(p.tp_mode == 1 ? p.peer_y != nullptr
                 : p.tp_mode == 3 ? (p.peer_y != nullptr && p.peer_pos != nullptr && topk > 0)
                 : p.tp_mode == 4 ? (p.yperm != nullptr && p.pos != nullptr && topk > 0)
-                : p.tp_mode == 5 ? (p.ret_f32 != nullptr && p.tp_parts >= 1 && topk > 0)
                                  : (p.peer_yperm && p.peer_pos && p.ids && p.e_local > 0 && topk > 0),
                 "tp mode tables missing");
-    TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 5, "tp mode must be 1 .. 5");
+    TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 4, "tp mode must be 1 .. 4");
   }
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));
@@ -603,8 +595,8 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, 
 // origins, per-expert counters) of every rank; pub: PeerSync of phase 0.
 void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
                  double route_scale, const optional<Tensor>& ids, const optional<Tensor>& wts, const Tensor& xq,
-                 const Tensor& xsf, int64_t e_local, int64_t cap_e, int64_t tile_rows, int64_t tp_size,
-                 int64_t ret_rows, const Tensor& tables, const Tensor& err, const Tensor& pub) {
+                 const Tensor& xsf, int64_t e_local, int64_t cap_e, int64_t tile_rows, int64_t ret_rows,
+                 const Tensor& tables, const Tensor& err, const Tensor& pub) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) == logits.size(1), "logits: f32 [T, E] contiguous");
@@ -628,7 +620,6 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
   p.e_local = (int)e_local;
   p.cap_e = (int)cap_e;
   p.tile_rows = (int)tile_rows;
-  p.tp = (int)tp_size;
   p.rows = (int)(e_local * cap_e);
   p.ret_rows = (int)ret_rows;
   p.peer_x = reinterpret_cast<uint8_t* const*>(tb[0]);
@@ -640,8 +631,7 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
   p.pub = peer_sync_of(pub);
   p.world = p.pub.world;
   p.rank = p.pub.rank;
-  TORCH_CHECK(p.pub.done != nullptr && p.tp >= 1 && p.world % p.tp == 0 && p.E == p.e_local * (p.world / p.tp),
-              "dispatch: phase-0 sync and E = e_local * (world / tp)");
+  TORCH_CHECK(p.pub.done != nullptr && p.E == p.e_local * p.world, "dispatch: phase-0 sync and E = e_local * world");
   const c10::cuda::CUDAGuard guard(logits.device());
   CUDA_OK(dsv4::ep_dispatch(p, cur_stream()));
 }

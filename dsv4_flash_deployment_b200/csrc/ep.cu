@@ -239,46 +239,34 @@ cudaError_t ep_combine_pack(const __nv_bfloat16* yperm, const int* pos, const in
 // owner's W2 of this layer has published, and every owner's ep_plan (which
 // zeroed the counters) precedes its W2 in stream order.
 // One CTA (8 warps) per token: warp 0 routes the token and claims the k rows on
-// their owners; then warp j stores copy j (and j + 8, ...) -- the NVLink row
-// stores of a token run in parallel, and every SM is busy at decode-sized token
-// counts.  Hybrid EP x TP (tp > 1): expert group g = id / e_local lives on ranks
-// g * tp .. g * tp + tp - 1, each holding 1/tp of every expert's intermediate
-// dimension, and every pair is sent to all tp of them (copy c = pair j, partner
-// q with c = j * tp + q); partner q's W2 writes its partial row to return row
-// (t * topk + j) * tp + q of the source.
+// their owners; then warp j stores pair j (and j + 8) -- the NVLink row stores
+// of a token run in parallel, and every SM is busy at decode-sized token counts.
 constexpr int kDispatchMaxD = 8192;   // hidden sizes the dispatch stages in shared memory
 
 template <int kMaxPer>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
   pdl_entry();
-  __shared__ int s_owner[32], s_row[32], s_ret[32];
-  __shared__ float s_w[32];
+  __shared__ int s_owner[16], s_row[16];
+  __shared__ float s_w[16];
   __shared__ uint4 s_xrow[kDispatchMaxD / 16];
   __shared__ uint32_t s_sfw[kDispatchMaxD / 128];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = p.D;
   const int kt = D / 128;
-  const int tp = p.tp;
-  const int copies = p.topk * tp;
   if (t < p.T) {
     if (warp == 0) {
       int id;
       float w;
       route_token<kMaxPer>(p.logits + (size_t)t * p.E, p.E, p.bias, p.topk, p.score_func, p.route_scale, lane, id,
                            w);
-      if (lane < p.topk && p.ids) {
-        p.ids[(size_t)t * p.topk + lane] = id;
-        p.wts[(size_t)t * p.topk + lane] = w;
-      }
-      // copy c of the token: pair j = c / tp (its pick sits in lane j), partner q = c % tp
-      const int j = lane / tp, q = lane - (lane / tp) * tp;
-      const int idj = __shfl_sync(0xffffffffu, id, j < p.topk ? j : 0);
-      const float wj = __shfl_sync(0xffffffffu, w, j < p.topk ? j : 0);
-      if (lane < copies) {
-        const int grp = idj / p.e_local;
-        const int le = idj - grp * p.e_local;
-        const int owner = grp * tp + q;
+      if (lane < p.topk) {
+        if (p.ids) {
+          p.ids[(size_t)t * p.topk + lane] = id;
+          p.wts[(size_t)t * p.topk + lane] = w;
+        }
+        const int owner = id / p.e_local;
+        const int le = id - owner * p.e_local;
         const int slot = atomicAdd_system(p.peer_cnt[owner] + le, 1);
         int row = -1;
         if (slot < seg_pairs(p.cap_e, p.tile_rows)) {
@@ -291,21 +279,20 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
           dbg_bad(BS_EP_OWNER);
           row = -1;
         }
-        if ((t * p.topk + j) * tp + q >= p.ret_rows) {
+        if (t * p.topk + lane >= p.ret_rows) {
           dbg_bad(BS_EP_RET);
           row = -1;
         }
 #endif
         s_owner[lane] = owner;
         s_row[lane] = row;
-        s_w[lane] = wj;
-        s_ret[lane] = (t * p.topk + j) * tp + q;
+        s_w[lane] = w;
       }
     }
     // the token's row (D bytes) and its scale words (one 4-byte word per 128
     // columns in the chunk layout) are staged in shared memory once, with every
     // load in flight together, while warp 0 routes; then each warp streams its
-    // copies out of shared memory
+    // pairs out of shared memory
     const int nvec = D / 16;
     const int m_src = t & 127;
     const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)t * D);
@@ -314,8 +301,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
       s_sfw[b] = *reinterpret_cast<const uint32_t*>(p.xsf + ((size_t)(t >> 7) * kt + b) * 512 + (m_src & 31) * 16 +
                                                     (m_src >> 5) * 4);
     __syncthreads();
-    for (int c = warp; c < copies; c += 8) {
-      const int o = s_owner[c], r = s_row[c];
+    for (int j = warp; j < p.topk; j += 8) {
+      const int o = s_owner[j], r = s_row[j];
       if (r < 0) continue;
       uint4* dst = reinterpret_cast<uint4*>(p.peer_x[o] + (size_t)r * D);
       for (int i = lane; i < nvec; i += 32) dst[i] = s_xrow[i];
@@ -324,8 +311,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
         *reinterpret_cast<uint32_t*>(p.peer_xsf[o] + ((size_t)(r >> 7) * kt + b) * 512 + (m & 31) * 16 +
                                      (m >> 5) * 4) = s_sfw[b];
       if (lane == 0) {
-        p.peer_rscale[o][r] = s_w[c];
-        p.peer_meta[o][r] = (p.rank << 24) | s_ret[c];
+        p.peer_rscale[o][r] = s_w[j];
+        p.peer_meta[o][r] = (p.rank << 24) | (t * p.topk + j);
       }
     }
   }
@@ -335,8 +322,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
 cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st) {
   if (p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 128 || p.D < 128 || p.D > kDispatchMaxD)
     return cudaErrorInvalidValue;
-  if (p.tp < 1 || p.topk * p.tp > 32 || p.world % p.tp) return cudaErrorInvalidValue;
-  if ((long long)p.T * p.topk * p.tp >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
+  if ((long long)p.T * p.topk >= (1 << 24) || p.world > 127 || p.e_local < 1) return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)std::max(1, p.T);   // every rank publishes, even with T = 0
   const int per = (p.E + 31) / 32;
 #define DSV4_DISPATCH(P) launch_pdl(ep_dispatch_kernel<P>, grid, 256, 0, st, p)

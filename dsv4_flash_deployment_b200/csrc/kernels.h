@@ -63,9 +63,7 @@ struct HcParams {
   // (peer_y tables, at row peer_pos[rank][t, slot] of that rank's own plan)
   // summed in rank order; tp_mode 4 = expert parallelism with rows returned by
   // the owners' W2 epilogues: the local yperm / pos combine once every rank has
-  // published the phase; tp_mode 5 = hybrid EP x TP: each pair's tp_parts f32
-  // partial rows (ret_f32 row (t * topk + slot) * tp_parts + q) summed in q order,
-  // rounded to bf16, then summed over the slots.  All wait first
+  // published the phase.  All wait first
   // (bounded) until every rank has published the phase.
   int tp_mode;
   const float* const* peer_y;
@@ -73,8 +71,6 @@ struct HcParams {
   const int* const* peer_pos;
   const int* ids;
   int e_local;
-  const float* ret_f32;             // tp_mode 5: the local return rows [T * topk * tp_parts, D]
-  int tp_parts;
   PeerSync wait;
   uint32_t* err;
 };
@@ -270,9 +266,8 @@ struct EpDispatchParams {
   const uint8_t* xsf;         // their scale chunks
   int D, e_local, cap_e, world, rank;
   int tile_rows;              // GEMM tile rows (the row layout of an expert segment, seg_row)
-  int tp;                     // tensor-parallel partners per expert group (hybrid EP x TP; 1 = plain EP)
   int rows;                   // expert rows of every rank (e_local * cap_e), for the debug-bounds build
-  int ret_rows;               // return rows of every rank (max tokens * topk * tp), for the debug-bounds build
+  int ret_rows;               // return rows of every rank (max tokens * topk), for the debug-bounds build
   uint8_t* const* peer_x;     // [world] expert rows [e_local * cap_e, D] of each rank
   uint8_t* const* peer_xsf;   // [world] their scale chunks
   float* const* peer_rscale;  // [world] routing weight per expert row

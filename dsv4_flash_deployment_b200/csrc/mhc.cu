@@ -139,26 +139,6 @@ __global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slice
           }
         }
       }
-      if (p.tp_mode == 5) {
-        // hybrid EP x TP: the tp_parts partners of each pair's expert group each
-        // returned an f32 partial row; their q-order sum is rounded to bf16 per
-        // pair (one GPU's W2 rounding), then the pairs add in slot order
-        const int k = min(p.topk, kMaxCombine);
-        for (int s = 0; s < k; ++s) {
-          float r8[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) r8[q] = 0.f;
-          const float* base = p.ret_f32 + ((size_t)t * p.topk + s) * p.tp_parts * D + d;
-          for (int q = 0; q < p.tp_parts; ++q) {
-            const float4* src = reinterpret_cast<const float4*>(base + (size_t)q * D);
-            const float4 a = src[0], b = src[1];
-            r8[0] += a.x; r8[1] += a.y; r8[2] += a.z; r8[3] += a.w;
-            r8[4] += b.x; r8[5] += b.y; r8[6] += b.z; r8[7] += b.w;
-          }
-#pragma unroll
-          for (int q = 0; q < 8; ++q) y[q] += __bfloat162float(__float2bfloat16(r8[q]));
-        }
-      }
       if (p.tp_mode == 3) {
         // experts split over the ranks by intermediate index: every rank holds an
         // f32 partial row for every routed pair, at the row its own MoE plan gave

@@ -59,8 +59,6 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
             L = load_layer(cfg, weights, lid, dev, expert_range=rng)
             if tp is not None and tp.moe == "tp":
                 L.experts = tp.shard_experts(L.experts)   # this rank's intermediate slice
-            elif ep is not None and getattr(ep, "tp", 1) > 1:
-                L.experts = ep.shard_experts(L.experts)   # hybrid EP x TP: the group partner's slice
             layers.append(L)
         embed = weights["embed.weight"].to(dev)
         head = _pad_rows(weights["head.weight"]).to(dev)
@@ -74,11 +72,7 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
                 raise ValueError("shared expert blocks belong to a different expert split")
         else:
             n_phys = expert_storage_layers or cfg.n_layers
-            inter = None
-            if tp is not None:
-                inter = tp.inter_local(cfg.moe_inter_dim)
-            elif ep is not None and getattr(ep, "tp", 1) > 1:
-                inter = ep.inter_local(cfg.moe_inter_dim)
+            inter = tp.inter_local(cfg.moe_inter_dim) if tp is not None else None
             stores = [random_experts(cfg, e_local, dev, g, inter=inter) for _ in range(min(n_phys, cfg.n_layers))]
         for lid in range(cfg.n_layers):
             layers.append(random_layer(cfg, lid, dev, g, stores[lid % len(stores)]))

@@ -260,11 +260,7 @@ class DSV4Model:
             self.cap = ceil_to(-(-recv_rows // self.tile_rows) * 128 + e_local * 128 + 128, 128)
         tiles_rows_max = recv_rows // self.tile_rows + e_local + 1
         # expert intermediate width on this rank (a tensor-parallel expert split keeps 1/N)
-        I = cfg.moe_inter_dim
-        if self.tp is not None:
-            I = self.tp.inter_local(I)
-        elif self.ep is not None and getattr(self.ep, "tp", 1) > 1:
-            I = self.ep.inter_local(I)      # hybrid EP x TP
+        I = self.tp.inter_local(cfg.moe_inter_dim) if self.tp is not None else cfg.moe_inter_dim
         self.inter_local = I
         self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)
         self.tiles2 = e(tiles_rows_max * (D // 128), 4, dt=i32)

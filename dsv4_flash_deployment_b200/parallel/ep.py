@@ -36,64 +36,33 @@ import torch
 import torch.distributed as dist
 
 from ..ops import _ext
-from ..ops.gemm import EPI_BF16, EPI_F32, EPI_SWIGLU
+from ..ops.gemm import EPI_BF16, EPI_SWIGLU
 from ..ops.layout import ceil_to
 
 
 class EPGroup:
     def __init__(self, rank: int, world: int, group=None, device=None, transport: str = "nccl",
-                 shared_first: bool | None = None, tp_size: int = 1):
+                 shared_first: bool | None = None):
         """``shared_first`` (fused transport): run the shared expert between the
         dispatch and the plan's wait instead of after the W2 GEMM (default from
-        ``DSV4_EP_SHARED_FIRST``, off).
-
-        ``tp_size`` > 1 (fused transport): hybrid EP x TP.  Ranks form world /
-        tp_size expert groups of tp_size consecutive ranks; a group owns
-        E * tp_size / world experts and each of its ranks holds 1/tp_size of every
-        such expert's intermediate dimension (W13 rows in 128-row blocks, W2 input
-        columns).  Every routed pair is dispatched to all partners of its group;
-        each returns an f32 partial row and the source sums them in partner order
-        (reference layout: EP8 x TP2 pairs, ``FK/patches/tpu-inference/0026``)."""
+        ``DSV4_EP_SHARED_FIRST``, off)."""
         import os
 
         self.shared_first = (os.environ.get("DSV4_EP_SHARED_FIRST", "0") == "1") if shared_first is None \
             else shared_first
-        if tp_size < 1 or world % tp_size:
-            raise ValueError(f"tp_size {tp_size} does not divide world {world}")
-        if tp_size > 1 and transport != "fused":
-            raise ValueError("hybrid EP x TP runs on the fused transport")
         self.rank = rank
         self.world = world
-        self.tp = tp_size
-        self.ep_size = world // tp_size
-        self.group_id, self.tp_rank = rank // tp_size, rank % tp_size
         self.group = group
         self.dev = torch.device(device) if device is not None else torch.device("cuda", rank)
         self.transport = transport
         self._bufs = None
 
     def expert_range(self, n_experts: int) -> tuple[int, int]:
-        per = n_experts // self.ep_size
-        return self.group_id * per, per
+        per = n_experts // self.world
+        return self.rank * per, per
 
     def experts_per_rank(self, n_experts: int) -> int:
-        return n_experts // self.ep_size
-
-    def inter_local(self, inter: int) -> int:
-        """Expert intermediate width on this rank (1/tp_size of it in the hybrid layout)."""
-        if self.tp == 1:
-            return inter
-        if inter % (128 * self.tp):
-            raise ValueError(f"expert intermediate {inter} does not split into 128-wide slices over {self.tp}")
-        return inter // self.tp
-
-    def shard_experts(self, ex):
-        """This rank's intermediate slice of its group's expert block (checkpoint path);
-        the same slicing as the tensor-parallel expert split, over the group's partners."""
-        if self.tp == 1:
-            return ex
-        from .tp import TPGroup
-        return TPGroup(self.tp_rank, self.tp, device=self.dev, moe="tp").shard_experts(ex)
+        return n_experts // self.world
 
     def cap_per_peer(self, T: int, k: int) -> int:
         # worst case: every routed pair of this rank goes to one peer (a token's k
@@ -180,9 +149,7 @@ class EPGroup:
         cap_e = ceil_to(pairs if tile_rows >= 128 else -(-pairs // tile_rows) * 128, 256)
         rows = e_local * cap_e
         kt = D // 128
-        # return rows: bf16 [T*k, D], or with partners f32 partials [T*k*tp, D]
-        ret_bytes = max(1, T * k) * D * 2 if self.tp == 1 else max(1, T * k) * self.tp * D * 4
-        sizes = [rows * D, (rows // 128) * kt * 512, rows * 4, rows * 4, e_local * 4, ret_bytes, 2 * W * 4]
+        sizes = [rows * D, (rows // 128) * kt * 512, rows * 4, rows * 4, e_local * 4, max(1, T * k) * D * 2, 2 * W * 4]
         offs, cur = [], 0
         for sz in sizes:
             offs.append(cur)
@@ -201,9 +168,7 @@ class EPGroup:
             cap_e=cap_e, rows=rows, k=k, tile_rows=tile_rows, symm=buf, symm_handle=hdl,
             x=view(0).view(rows, D), xsf=view(1), rscale=view(2).view(torch.float32),
             meta=view(3).view(torch.int32), cnt=view(4).view(torch.int32),
-            back=(view(5).view(torch.bfloat16).view(max(1, T * k), D) if self.tp == 1
-                  else view(5).view(torch.float32).view(max(1, T * k) * self.tp, D)),
-            sig=view(6).view(torch.int32),
+            back=view(5).view(torch.bfloat16).view(max(1, T * k), D), sig=view(6).view(torch.int32),
             tables=[table(i) for i in range(5)], peer_back=table(5), peer_sig=table(6),
             done=torch.zeros(2, dtype=torch.int32, device=self.dev),
             epoch=torch.zeros(2, dtype=torch.int32, device=self.dev),
@@ -220,14 +185,9 @@ class EPGroup:
         sync = lambda ph: torch.tensor([b["peer_sig"].data_ptr(), b["sig"].data_ptr(), b["done"].data_ptr() + 4 * ph,
                                         b["epoch"].data_ptr() + 4 * ph, ph, W, self.rank], dtype=torch.int64)
         b["sync0"], b["sync1"] = sync(0), sync(1)
-        # mHC boundary descriptor: wait for phase 1, then the local combine (tp_mode 4:
-        # bf16 rows; tp_mode 5: the partners' f32 partial rows summed per pair)
-        if self.tp == 1:
-            b["hc_desc"] = torch.cat([torch.tensor([4], dtype=torch.int64), b["sync1"],
-                                      torch.zeros(5, dtype=torch.int64)])
-        else:
-            b["hc_desc"] = torch.cat([torch.tensor([5], dtype=torch.int64), b["sync1"], torch.zeros(5, dtype=torch.int64),
-                                      torch.tensor([b["back"].data_ptr(), self.tp], dtype=torch.int64)])
+        # mHC boundary descriptor: wait for phase 1, then the local combine (tp_mode 4)
+        b["hc_desc"] = torch.cat([torch.tensor([4], dtype=torch.int64), b["sync1"],
+                                  torch.zeros(5, dtype=torch.int64)])
         self._fb = b
 
     def moe_fused(self, model, L, T: int, k: int, logits: torch.Tensor):
@@ -246,8 +206,8 @@ class EPGroup:
         ids, wts, _, _ = model.route[k]
         with model._t("ep_dispatch"):
             ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
-                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], self.tp,
-                            b["back"].shape[0], b["tab_cpu"], model.err, b["sync0"])
+                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], b["back"].shape[0],
+                            b["tab_cpu"], model.err, b["sync0"])
         if self.shared_first:
             # the shared expert runs while the peers' dispatched rows are in flight
             with model._t("shared_expert"):
@@ -261,8 +221,8 @@ class EPGroup:
                      b["rows"], D, b["tile_rows"], 1, b["tiles13"], b["nt13"], b["rscale"], b["h"], b["hsf"],
                      cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None)
         with model._t("grouped_w2"):
-            ext.gemm(ex.w2.kind, EPI_BF16 if self.tp == 1 else EPI_F32, ex.w2.q, ex.w2.sf, b["h"].view(b["rows"], I),
-                     b["hsf"], None, ex.w2.q.shape[0],
+            ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["rows"], I), b["hsf"], None,
+                     ex.w2.q.shape[0],
                      b["rows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None, 0.0, D, D, None, None,
                      model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"])
         if not self.shared_first:

@@ -58,8 +58,6 @@ def main(argv=None):
     ap.add_argument("--time-tokens", type=int, default=256)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--transports", default="nccl,p2p,fused")
-    ap.add_argument("--ep-tp", type=int, default=1,
-                    help="hybrid EP x TP: partners per expert group (fused transport only)")
     a = ap.parse_args(argv)
 
     from ..engine.builder import build_model
@@ -78,8 +76,7 @@ def main(argv=None):
     ok = True
     results = {}
     for transport in a.transports.split(","):
-        ep = EPGroup(rank, world, dist.group.WORLD, dev, transport=transport,
-                     tp_size=a.ep_tp if transport == "fused" else 1)
+        ep = EPGroup(rank, world, dist.group.WORLD, dev, transport=transport)
         m = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512, weights=w, ep=ep)
         worst, agree, total = 1.0, 0, 0
         for s in range(a.steps):
@@ -118,7 +115,7 @@ def main(argv=None):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         flag = torch.tensor([0 if good else 1], device=dev)
         dist.all_reduce(flag)
-        results[transport] = {"transport": transport, "world": world, "ep_tp": ep.tp, "min_logit_cos": worst,
+        results[transport] = {"transport": transport, "world": world, "min_logit_cos": worst,
                               "token_agree": f"{agree}/{total}", "ok": bool(flag.item() == 0),
                               "step_ms_T%d" % T: round(ms.item(), 4), "layers": cfg.n_layers}
         ok = ok and flag.item() == 0

@@ -65,7 +65,7 @@ class TPGroup:
     experts and gathers a pair's row from its owner.  "tp": every rank holds the
     1/N slice of every expert's intermediate dimension (W13 rows, W2 input
     columns), runs every routed pair on its slice, and the mHC boundary sums the
-    N f32 partial rows of each pair (the hybrid EP x TP layout with TP = N);
+    N f32 partial rows of each pair (an EP x TP layout with TP = N);
     balanced weight streaming for decode batches where few experts are active."""
 
     def __init__(self, rank: int, world: int, group=None, device=None, moe: str = "ep"):
