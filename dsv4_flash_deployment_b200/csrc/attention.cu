@@ -12,9 +12,15 @@
 // Window rows of positions at or after the token's chunk start come from this
 // step's kv buffer (prefill chunks), earlier ones from the per-sequence ring.
 //
-// One CTA (8 warps) per (token, split).  Rows are gathered with cp.async into
-// double-buffered shared memory; QK^T and PV use mma.sync m16n8k16 bf16 with
-// fp32 accumulators (PV accumulators stay in registers, 64 dims per warp).
+// The caches hold quantized row records (common.cuh): window rows (the ring and
+// this step's rows) as KV8 (e4m3 + ue8m0 per 32, 528 bytes), compressed rows as
+// KV4 (packed e2m1 + e4m3 per 16, 288 bytes).  Both decode exactly to the bf16
+// values of the reference's round trips.
+//
+// One CTA (8 warps) per (token, split).  A block's raw records are gathered with
+// cp.async into double-buffered shared memory, then decoded into one bf16 tile;
+// QK^T and PV use mma.sync m16n8k16 bf16 with fp32 accumulators (PV accumulators
+// stay in registers, 64 dims per warp).
 // With splits > 1 the partial (acc, max, sum) go to a workspace and
 // attn_combine merges them (C = 1 decode spreads a token over many SMs).
 #include "common.cuh"
@@ -31,12 +37,51 @@ constexpr int kPadE = 8;                 // row padding (bf16 elements) to sprea
 constexpr int kRowE = kDh + kPadE;       // 520
 constexpr int kPPad = kBlk + 8;          // P row stride (bf16)
 
+constexpr int kRec8 = kv8_bytes(kDh);   // 528
+constexpr int kRec4 = kv4_bytes(kDh);   // 288
+constexpr int kRecChunks = kRec8 / 16;  // 16-byte pieces of the widest record
+
 constexpr size_t kSmemQ = (size_t)kH * kRowE * 2;
-constexpr size_t kSmemKV = (size_t)kBlk * kRowE * 2;
+constexpr size_t kSmemKV = (size_t)kBlk * kRowE * 2;     // one decoded block
+constexpr size_t kSmemRaw = (size_t)kBlk * kRec8;        // one block of raw records (x2)
 constexpr size_t kSmemP = (size_t)kH * kPPad * 2;
 constexpr size_t kSmemRows = (size_t)kAttnMaxRows * 8;
 constexpr size_t kSmemStats = (size_t)kH * 4 * 7;  // max, sum, corr, 2x partial max, 2x partial sum
-constexpr size_t kSmemTotal = kSmemQ + 2 * kSmemKV + kSmemP + kSmemRows + kSmemStats;
+constexpr size_t kSmemTotal = kSmemQ + kSmemKV + 2 * kSmemRaw + kSmemP + kSmemRows + kSmemStats;
+static_assert(kRec8 % 16 == 0 && kRec4 % 16 == 0, "records must be whole 16-byte pieces");
+static_assert(kSmemTotal <= 227 * 1024, "attention shared memory exceeds the per-CTA limit");
+
+// Eight columns [8c, 8c + 8) of a KV8 record -> bf16.
+DSV4_DEV uint4 decode8_kv8(const uint8_t* rec, int c) {
+  const uint2 codes = *reinterpret_cast<const uint2*>(rec + 8 * c);
+  const uint32_t e = rec[kDh + (c >> 2)];
+  const float sc = e ? __uint_as_float(e << 23) : 0.f;
+  uint4 o;
+  uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
+  const uint32_t w[2] = {codes.x, codes.y};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b = w[i >> 1] >> (16 * (i & 1));
+    const float lo = e4m3_to_f32((uint8_t)(b & 0xFF)) * sc;
+    const float hi = e4m3_to_f32((uint8_t)((b >> 8) & 0xFF)) * sc;
+    o32[i] = pack_bf16(lo, hi);
+  }
+  return o;
+}
+
+// Eight columns [8c, 8c + 8) of a KV4 record -> bf16.
+DSV4_DEV uint4 decode8_kv4(const uint8_t* rec, int c) {
+  const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * c);
+  const float sc = e4m3_to_f32(rec[kDh / 2 + (c >> 1)]);
+  uint4 o;
+  uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b = (codes >> (8 * i)) & 0xFF;
+    o32[i] = pack_bf16(e2m1_value(b & 0xF) * sc, e2m1_value(b >> 4) * sc);
+  }
+  return o;
+}
 }  // namespace
 
 __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
@@ -44,9 +89,10 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* sKV = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ);
-  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ + 2 * kSmemKV);
-  const __nv_bfloat16** sRows = reinterpret_cast<const __nv_bfloat16**>(smem + kSmemQ + 2 * kSmemKV + kSmemP);
-  float* sMax = reinterpret_cast<float*>(smem + kSmemQ + 2 * kSmemKV + kSmemP + kSmemRows);
+  uint8_t* sRaw = smem + kSmemQ + kSmemKV;
+  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + kSmemQ + kSmemKV + 2 * kSmemRaw);
+  const uint8_t** sRows = reinterpret_cast<const uint8_t**>(smem + kSmemQ + kSmemKV + 2 * kSmemRaw + kSmemP);
+  float* sMax = reinterpret_cast<float*>(smem + kSmemQ + kSmemKV + 2 * kSmemRaw + kSmemP + kSmemRows);
   float* sSum = sMax + kH;
   float* sCorr = sSum + kH;
   float* sPMax = sCorr + kH;   // [kH][2]
@@ -60,24 +106,24 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   const int slot = p.slot[t];
   const int rope_pos = p.rope_pos ? p.rope_pos[t] : pos;
 
-  // ---------------- row list: window, then compressed entries (valid ones first)
+  // ---------------- row list: window (KV8), then compressed entries (KV4, valid ones first)
   const int we = p.win_end ? p.win_end[t] : pos;
   const int n_win = min(we + 1, p.win_len > 0 ? p.win_len : p.W);
   const int n_comp = p.comp != nullptr ? min(p.comp_cnt[t], kAttnMaxRows - n_win) : 0;
   {
     const int cs = p.chunk_start[t];
     for (int j = tid; j < n_win + n_comp; j += blockDim.x) {
-      const __nv_bfloat16* r;
+      const uint8_t* r;
       if (j < n_win) {
         const int pp = we - n_win + 1 + j;
         if (pp >= cs)
-          r = p.kv_step + (size_t)(p.step_row0[t] + (pp - cs)) * kDh;
+          r = p.kv_step + (size_t)(p.step_row0[t] + (pp - cs)) * kRec8;
         else
-          r = p.ring + ((size_t)slot * p.W + (pp % p.W)) * kDh;
+          r = p.ring + ((size_t)slot * p.W + (pp % p.W)) * kRec8;
       } else {
         const int jj = j - n_win;
         const int ci = p.comp_idx != nullptr ? p.comp_idx[(size_t)t * p.comp_k + jj] : jj;
-        r = p.comp + kv_row(p.comp_pages, slot, ci, p.max_c) * kDh;
+        r = p.comp + kv_row(p.comp_pages, slot, ci, p.max_c) * kRec4;
       }
       sRows[j] = r;
     }
@@ -137,16 +183,30 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   const int b_begin = split * bps;
   const int b_end = min(n_blocks, b_begin + bps);
 
+  // raw records of block b -> sRaw[buf] (rows past the end are zero-filled, which
+  // decodes to zeros; the unused tail of a KV4 row is not copied)
   auto load_block = [&](int b, int buf) {
-    __nv_bfloat16* dst = sKV + (size_t)buf * kBlk * kRowE;
-    for (int c = tid; c < kBlk * (kDh / 8); c += 256) {
-      const int r = c / (kDh / 8), ch = c % (kDh / 8);
+    uint8_t* dst = sRaw + (size_t)buf * kSmemRaw;
+    for (int c = tid; c < kBlk * kRecChunks; c += 256) {
+      const int r = c / kRecChunks, ch = c % kRecChunks;
       const int gr = b * kBlk + r;
       const bool ok = gr < n_rows;
-      const __nv_bfloat16* src = ok ? sRows[gr] + ch * 8 : p.q;  // any valid address when masked
-      cp_async16(dst + (size_t)r * kRowE + ch * 8, src, ok);
+      if (ok && gr >= n_win && ch * 16 >= kRec4) continue;
+      const uint8_t* src = ok ? sRows[gr] + ch * 16 : reinterpret_cast<const uint8_t*>(p.q);
+      cp_async16(dst + (size_t)r * kRec8 + ch * 16, src, ok);
     }
     cp_async_commit();
+  };
+  // sRaw[buf] -> the bf16 tile: thread -> 8-column chunk (tid % 64) of rows tid / 64 + 4i
+  auto decode_block = [&](int b, int buf) {
+    const uint8_t* raw = sRaw + (size_t)buf * kSmemRaw;
+    const int c = tid & 63;
+    for (int r = tid >> 6; r < kBlk; r += 4) {
+      const int gr = b * kBlk + r;
+      const uint8_t* rec = raw + (size_t)r * kRec8;
+      const uint4 v = (gr >= n_win && gr < n_rows) ? decode8_kv4(rec, c) : decode8_kv8(rec, c);
+      *reinterpret_cast<uint4*>(sKV + (size_t)r * kRowE + 8 * c) = v;
+    }
   };
 
   float acc[4][8][4];
@@ -168,7 +228,9 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
       cp_async_wait0();
     }
     __syncthreads();
-    const __nv_bfloat16* kv = sKV + (size_t)buf * kBlk * kRowE;
+    decode_block(b, buf);
+    __syncthreads();
+    const __nv_bfloat16* kv = sKV;
     // ---- S = Q K^T : warp -> heads (warp%4)*16, rows (warp/4)*32
     {
       const int h0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;

@@ -360,10 +360,18 @@ void attention(const Tensor& q, const Tensor& cos, const Tensor& sin, const opti
   p.rope_pos = ptr<const int>(rope_pos);
   p.q_head_norm = q_head_norm;
   p.norm_eps = (float)norm_eps;
-  p.kv_step = ptr<const bf16>(kv_step);
-  p.ring = ptr<const bf16>(ring);
+  // window rows are KV8 records, compressed rows KV4 records (csrc/common.cuh)
+  TORCH_CHECK(kv_step.scalar_type() == at::kByte && kv_step.dim() == 2 && kv_step.size(1) == dsv4::kv8_bytes(512),
+              "kv_step must be [R, 528] uint8 KV8 records");
+  TORCH_CHECK(ring.scalar_type() == at::kByte && ring.dim() == 3 && ring.size(2) == dsv4::kv8_bytes(512),
+              "ring must be [slots, W, 528] uint8 KV8 records");
+  if (comp)
+    TORCH_CHECK(comp->scalar_type() == at::kByte && comp->dim() == 3 && comp->size(2) == dsv4::kv4_bytes(512),
+                "comp must be [slots, max_c, 288] uint8 KV4 records");
+  p.kv_step = ptr<const uint8_t>(kv_step);
+  p.ring = ptr<const uint8_t>(ring);
   p.W = (int)ring.size(1);
-  p.comp = ptr<const bf16>(comp);
+  p.comp = ptr<const uint8_t>(comp);
   p.max_c = comp ? (int)comp->size(1) : 0;
   if (comp) p.comp_pages = kv_pages_of(comp_pages, &p.max_c);
   p.slot = ptr<const int>(slot);
@@ -403,7 +411,9 @@ void qkv_post(const Tensor& in, int64_t q_dim, int64_t kv_dim, const Tensor& q_n
   p.rope_cos = ptr<const float>(cos);
   p.rope_sin = ptr<const float>(sin);
   p.pos = ptr<const int>(pos);
-  p.kv_out = ptr<bf16>(kv_out);
+  TORCH_CHECK(kv_out.scalar_type() == at::kByte && kv_out.size(-1) == dsv4::kv8_bytes((int)kv_dim),
+              "kv_out must hold kv8_bytes(kv_dim) uint8 per row (KV8 records)");
+  p.kv_out = ptr<uint8_t>(kv_out);
   const c10::cuda::CUDAGuard guard(in.device());
   CUDA_OK(dsv4::qkv_post(p, cur_stream()));
 }
@@ -429,7 +439,10 @@ void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g
   p.g_row0 = ptr<const int>(g_row0);
   p.r = (int)r;
   p.co = (int)co;
-  p.dh = (int)comp_out.size(2);
+  // comp_out holds KV4 records: 288 bytes per 512-dim row
+  TORCH_CHECK(comp_out.scalar_type() == at::kByte && comp_out.size(2) == dsv4::kv4_bytes(512),
+              "comp_out must be [slots, max_c, 288] uint8 KV4 records");
+  p.dh = 512;
   p.proj = ptr<const float>(proj);
   p.ape = ptr<const float>(ape);
   p.ring = ptr<const float>(ring);
@@ -437,7 +450,7 @@ void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g
   p.eps = (float)eps;
   p.rope_cos = ptr<const float>(cos);
   p.rope_sin = ptr<const float>(sin);
-  p.comp_out = ptr<bf16>(comp_out);
+  p.comp_out = ptr<uint8_t>(comp_out);
   p.max_c = (int)comp_out.size(1);
   p.wk = ptr<const bf16>(wk);
   p.k_norm_w = ptr<const bf16>(k_norm_w);
@@ -451,9 +464,13 @@ void ring_update(const Tensor& ring, const Tensor& src, int64_t T, const Tensor&
                  const Tensor& last_pos) {
   const int depth = (int)ring.size(1);
   const int width = (int)ring.size(2);
+  TORCH_CHECK(src.scalar_type() == ring.scalar_type() && src.size(-1) == width, "ring / source row mismatch");
   if (ring.scalar_type() == at::kFloat)
     CUDA_OK(dsv4::ring_update_f32(ptr<float>(ring), depth, width, ptr<const float>(src), (int)T, ptr<const int>(slot),
                                   ptr<const int>(pos), ptr<const int>(last_pos), cur_stream()));
+  else if (ring.scalar_type() == at::kByte)
+    CUDA_OK(dsv4::ring_update_rec(ptr<uint8_t>(ring), depth, width, ptr<const uint8_t>(src), (int)T,
+                                  ptr<const int>(slot), ptr<const int>(pos), ptr<const int>(last_pos), cur_stream()));
   else
     CUDA_OK(dsv4::ring_update_bf16(ptr<bf16>(ring), depth, width, ptr<const bf16>(src), (int)T, ptr<const int>(slot),
                                    ptr<const int>(pos), ptr<const int>(last_pos), cur_stream()));

@@ -1,7 +1,7 @@
 // KV compressor: softmax-gated pooling of r (or 2r, overlapped) token
 // projections into one compressed latent row, then RMSNorm, RoPE at the group
-// start, e2m1/e4m3-per-16 round trip and a store into the sequence's
-// compressed cache; optionally the indexer key of the same entry (latent @ wk
+// start, e2m1 codes with e4m3 scales per 16 stored as a KV4 record (common.cuh)
+// into the sequence's compressed cache; optionally the indexer key of the same entry (latent @ wk
 // -> RMSNorm -> RoPE -> e2m1/ue8m0-per-32 round trip).  Reference:
 // _compressor_step (reference.py:547-603), _indexer_step k path (:621-640),
 // latent store (:792-807).
@@ -122,14 +122,19 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
     z = (d & 1) ? (e * s + o * c) : (e * c - o * s);
     z = __bfloat162float(__float2bfloat16(z));
   }
-  // e2m1 round trip, e4m3 scale per 16 (16 consecutive dims = half a warp)
+  // e2m1 with an e4m3 scale per 16 (16 consecutive dims = half a warp), stored as
+  // a KV4 record: packed codes (even dim in the low nibble), then the scale bytes
   {
     float amax = fabsf(z);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     amax = fmaxf(amax, 6.f * 0.001953125f);
-    const float s = e4m3_to_f32(f32_to_e4m3(amax / 6.f));
-    p.comp_out[kv_row(p.pages, slot, g, p.max_c) * dh + d] = __float2bfloat16(e2m1_qdq_c(z, s));
+    const uint8_t sb = f32_to_e4m3(amax / 6.f);
+    const uint32_t code = e2m1_code(z, e4m3_to_f32(sb));
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
+    uint8_t* rec = p.comp_out + kv_row(p.pages, slot, g, p.max_c) * kv4_bytes(dh);
+    if ((d & 1) == 0) rec[d >> 1] = (uint8_t)(code | (hi << 4));
+    if ((d & 15) == 0) rec[dh / 2 + (d >> 4)] = sb;
   }
   if (p.wk == nullptr) return;
   // ---- indexer key: k = bf16(latent @ wk^T) -> RMSNorm -> RoPE -> e2m1 (ue8m0 / 32)
@@ -212,6 +217,27 @@ cudaError_t ring_update_bf16(__nv_bfloat16* ring, int depth, int width, const __
                              const int* slot, const int* pos, const int* last_pos, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   launch_pdl(ring_update_kernel<__nv_bfloat16>, T, 256, 0, st, ring, depth, width, src, T, slot, pos, last_pos);
+  return cudaGetLastError();
+}
+
+// Byte rows (KV8 records): 16-byte vectors, width a multiple of 16.
+__global__ void ring_update_rec_kernel(uint8_t* ring, int depth, int width, const uint8_t* src, int T_,
+                                       const int* slot, const int* pos, const int* last_pos) {
+  pdl_entry();
+  const int t = blockIdx.x;
+  if (t >= T_) return;
+  const int ps = pos[t];
+  if (ps > last_pos[t] || ps <= last_pos[t] - depth) return;
+  uint4* dst = reinterpret_cast<uint4*>(ring + ((size_t)slot[t] * depth + (ps % depth)) * width);
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)t * width);
+  for (int i = threadIdx.x; i < width / 16; i += blockDim.x) dst[i] = s[i];
+}
+
+cudaError_t ring_update_rec(uint8_t* ring, int depth, int width, const uint8_t* src, int T, const int* slot,
+                            const int* pos, const int* last_pos, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (width % 16) return cudaErrorInvalidValue;
+  launch_pdl(ring_update_rec_kernel, T, 64, 0, st, ring, depth, width, src, T, slot, pos, last_pos);
   return cudaGetLastError();
 }
 

@@ -8,6 +8,15 @@
 
 namespace dsv4 {
 
+// Cache row records.  The attention caches hold each row in the quantized form
+// of the round trip it went through.  KV8 (window rows): d e4m3 codes, then
+// d/32 ue8m0 scale bytes.  KV4 (compressed rows): d/2 bytes of e2m1 codes
+// (column 2i in the low nibble of byte i, 2i+1 in the high nibble), then d/16
+// e4m3 scale bytes.  Both decode exactly to the bf16 values of the round trip
+// (at most 6 significant bits).
+__host__ __device__ constexpr int kv8_bytes(int d) { return d + d / 32; }
+__host__ __device__ constexpr int kv4_bytes(int d) { return d / 2 + d / 16; }
+
 // Block table of a paged compressed cache: entry ci of sequence slot s lives in
 // pool row table[s * ld + (ci >> shift)] << shift | (ci & (2^shift - 1)).
 // table == nullptr: contiguous per-slot cache, row s * max_c + ci.
@@ -92,10 +101,10 @@ struct AttnParams {
   const int* rope_pos;              // optional rope position (default pos)
   int q_head_norm;
   float norm_eps;
-  const __nv_bfloat16* kv_step;     // this step's window rows [R, 512]
-  const __nv_bfloat16* ring;        // [slots, W, 512]
+  const uint8_t* kv_step;           // this step's window rows [R, 528] (KV8 records)
+  const uint8_t* ring;              // [slots, W, 528] KV8 records
   int W;
-  const __nv_bfloat16* comp;        // [slots, max_c, 512] or a paged pool, or null
+  const uint8_t* comp;              // [slots, max_c, 288] KV4 records or a paged pool, or null
   int max_c;
   KvPages comp_pages;
   const int* slot;
@@ -128,7 +137,7 @@ struct QkvParams {
   const float* rope_cos;
   const float* rope_sin;
   const int* pos;
-  __nv_bfloat16* kv_out;            // [T, kv_dim]
+  uint8_t* kv_out;                  // [T, kv8_bytes(kv_dim)] KV8 records
 };
 cudaError_t qkv_post(const QkvParams& p, cudaStream_t st);
 
@@ -153,7 +162,7 @@ struct CompParams {
   float eps;
   const float* rope_cos;
   const float* rope_sin;
-  __nv_bfloat16* comp_out;          // [slots, max_c, dh] or a paged pool (pages)
+  uint8_t* comp_out;                // [slots, max_c, kv4_bytes(dh)] KV4 records or a paged pool (pages)
   int max_c;
   KvPages pages;                    // rows of comp_out and idx_out
   const __nv_bfloat16* wk;          // indexer K projection [idx_dim, dh] (null = none)
@@ -168,6 +177,8 @@ cudaError_t ring_update_f32(float* ring, int depth, int width, const float* src,
                             const int* pos, const int* last_pos, cudaStream_t st);
 cudaError_t ring_update_bf16(__nv_bfloat16* ring, int depth, int width, const __nv_bfloat16* src, int T,
                              const int* slot, const int* pos, const int* last_pos, cudaStream_t st);
+cudaError_t ring_update_rec(uint8_t* ring, int depth, int width, const uint8_t* src, int T, const int* slot,
+                            const int* pos, const int* last_pos, cudaStream_t st);
 
 // ------------------------------------------------------------ moe.cu
 cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,

@@ -3,7 +3,8 @@
 // qkv_post: the fused wq_a|wkv GEMM output row is split into
 //   qr = bf16(rmsnorm(q part) * q_norm)   -> MXFP8 for the wq_b / indexer GEMMs
 //   kv = bf16(rmsnorm(kv part) * kv_norm) -> RoPE at pos (fp32, rounded to bf16)
-//        -> FP8 e4m3 / ue8m0-per-32 round trip (the window KV contract)
+//        -> FP8 e4m3 / ue8m0 per 32, stored as a KV8 record (common.cuh): the
+//        window KV contract, kept in its quantized form
 // (reference.py:704-731).
 #include "common.cuh"
 #include "kernels.h"
@@ -122,16 +123,16 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_post_kernel(QkvParams p) {
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      const float sc = exp_to_f32(pow2_ceil_exp(fmaxf(amax, 1e-4f), 1.f / 448.f));
-      uint4 o;
-      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+      const uint32_t e = pow2_ceil_exp(fmaxf(amax, 1e-4f), 1.f / 448.f);
+      const float sc = exp_to_f32(e);
+      // KV8 record: the e4m3 codes, then the ue8m0 exponent of each 32 columns
+      uint8_t* rec = p.kv_out + (size_t)t * kv8_bytes(p.kv_dim);
+      uint32_t qb[2] = {0, 0};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(y[2 * i] / sc, -448.f), 448.f))) * sc;
-        const float b = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(y[2 * i + 1] / sc, -448.f), 448.f))) * sc;
-        o2[i] = __floats2bfloat162_rn(a, b);
-      }
-      *reinterpret_cast<uint4*>(p.kv_out + (size_t)t * p.kv_dim + 8 * c) = o;
+      for (int i = 0; i < 8; ++i)
+        qb[i >> 2] |= (uint32_t)f32_to_e4m3(fminf(fmaxf(y[i] / sc, -448.f), 448.f)) << (8 * (i & 3));
+      *reinterpret_cast<uint2*>(rec + 8 * c) = make_uint2(qb[0], qb[1]);
+      if ((lane & 3) == 0) rec[p.kv_dim + (c >> 2)] = (uint8_t)e;
     }
   }
 }

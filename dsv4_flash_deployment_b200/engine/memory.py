@@ -11,6 +11,8 @@ from __future__ import annotations
 
 import torch
 
+from ..models.kv_format import kv4_bytes, kv8_bytes
+
 
 def expert_block_bytes(cfg, ep_world: int = 1) -> int:
     e_local = cfg.n_routed_experts // ep_world
@@ -35,7 +37,8 @@ def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int, kv_block:
         dense += cfg.index_n_heads * cfg.index_head_dim * cfg.q_lora_rank + 2 * 128 * d
     emb = 2 * 2 * cfg.vocab_size * d
     s = n_slots + 1
-    kv = cfg.n_layers * s * cfg.sliding_window * cfg.head_dim * 2
+    # window rows are KV8 records, compressed rows KV4 records (models/kv_format.py)
+    kv = cfg.n_layers * s * cfg.sliding_window * kv8_bytes(cfg.head_dim)
     for l in cfg.kv_source_layer_ids:
         r, co = cfg.ratio(l), cfg.overlap(l)
         if kv_block:
@@ -43,7 +46,7 @@ def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int, kv_block:
             rows = (-(-max(1, pool // r) // kv_block) + 1) * kv_block
         else:
             rows = s * (max_seq // r)
-        kv += rows * cfg.head_dim * 2 + s * co * r * 2 * co * cfg.head_dim * 4
+        kv += rows * kv4_bytes(cfg.head_dim) + s * co * r * 2 * co * cfg.head_dim * 4
         if l in cfg.index_source_layer_ids:
             kv += rows * cfg.index_head_dim * 2
     t = max_tokens

@@ -32,6 +32,7 @@ import numpy as np
 import torch
 
 from ..ops import _ext
+from .kv_format import kv4_bytes, kv8_bytes
 from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
                         pick_bn)
 from ..ops.layout import ceil_to
@@ -201,7 +202,7 @@ class DSV4Model:
         self.qkv = e(T, qa + cfg.head_dim)
         self.qr_q = e(Tp, qa, dt=u8)
         self.qr_sf = z(Tp // 128, qa // 128, 512, dt=u8)
-        self.kv_step = e(T, cfg.head_dim)
+        self.kv_step = z(T, kv8_bytes(cfg.head_dim), dt=u8)   # KV8 records (models/kv_format.py)
         tpw = self.tp.world if self.tp is not None else 1
         self.n_heads_local = cfg.n_heads // tpw
         o_inter = cfg.o_inter // tpw
@@ -322,12 +323,12 @@ class DSV4Model:
         self.idx_cache = {}
         self.comp_ring = {}
         for l in range(cfg.n_layers):
-            self.ring[l] = torch.zeros(S, cfg.sliding_window, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            self.ring[l] = torch.zeros(S, cfg.sliding_window, kv8_bytes(cfg.head_dim), dtype=torch.uint8, device=dev)
         for l in cfg.kv_source_layer_ids:
             r, co = cfg.ratio(l), cfg.overlap(l)
             # contiguous: [slot, entry, dim]; paged: one pool [1, blocks * block, dim] per layer
             shape = (S, max(1, self.max_seq_len // r)) if self.pager is None else (1, self.pager.rows(r))
-            self.comp[l] = torch.zeros(*shape, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            self.comp[l] = torch.zeros(*shape, kv4_bytes(cfg.head_dim), dtype=torch.uint8, device=dev)
             if l in cfg.index_source_layer_ids:
                 self.idx_cache[l] = torch.zeros(*shape, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
             self.comp_ring[l] = torch.zeros(S, co * r, 2 * co * cfg.head_dim, dtype=torch.float32, device=dev)

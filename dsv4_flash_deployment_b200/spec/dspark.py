@@ -17,7 +17,7 @@ reference.py:1116-1248, ``verify_block`` :1250-1329, the v7x drafter
           position-indexed caches are rewritten before anything reads them
   ingest  main_hidden (mean of the 4 streams entering each tap layer) of the
           accepted rows -> main_proj -> RMSNorm -> per stage wkv -> kv norm ->
-          RoPE -> FP8 round trip -> the stage's ring
+          RoPE -> FP8 (KV8 record) -> the stage's ring
 
 Every step reuses the target model's device buffers; only the MTP rings, the
 tap buffers and a few small work arrays are added.
@@ -31,6 +31,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from ..models.kv_format import kv8_bytes
 from ..models.model import SeqChunk, StepMeta
 from ..models.weights import load_layer
 from ..ops.gemm import MxWeight, gemm_mx, quantize
@@ -92,7 +93,8 @@ class DSparkDrafter:
         self.R = self.memb.shape[1]
         S = model.n_slots + 1
         W = cfg.sliding_window
-        self.rings = [torch.zeros(S, W, cfg.head_dim, dtype=torch.bfloat16, device=dev) for _ in range(self.K)]
+        # KV8 records, like the target model's window rings (models/kv_format.py)
+        self.rings = [torch.zeros(S, W, kv8_bytes(cfg.head_dim), dtype=torch.uint8, device=dev) for _ in range(self.K)]
         T = model.max_tokens
         D = cfg.dim
         nt = len(cfg.dspark_target_layer_ids)
@@ -100,7 +102,7 @@ class DSparkDrafter:
         self.mh = torch.zeros(T, nt * D, dtype=torch.bfloat16, device=dev)
         self.mx = torch.zeros(T, D, dtype=torch.bfloat16, device=dev)
         self.kvraw = torch.zeros(T, cfg.head_dim, dtype=torch.bfloat16, device=dev)
-        self.kvq = torch.zeros(T, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+        self.kvq = torch.zeros(T, kv8_bytes(cfg.head_dim), dtype=torch.uint8, device=dev)
         n = max_seqs
         self.toks = torch.zeros(self.blk + 1, n, dtype=torch.int32, device=dev)
         self.emb = torch.zeros(n, self.R, dtype=torch.bfloat16, device=dev)

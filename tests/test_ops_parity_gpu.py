@@ -3,7 +3,8 @@
 
 * the mHC boundary pair (``hc_post`` + ``hc_finish``): stream update, the 24
   mixes after Sinkhorn, the RMS-normed collapse and its MXFP8 quantization;
-* ``qkv_post``: q RMSNorm + MXFP8, kv RMSNorm + RoPE + FP8 round trip.
+* ``qkv_post``: q RMSNorm + MXFP8, kv RMSNorm + RoPE + FP8 (a KV8 record, decoded here);
+* sparse attention over KV8 / KV4 record caches (window + selected compressed rows).
 
 Rounding points follow the oracle; where the kernel's fp32 summation order
 differs from torch's, one bf16 ulp is allowed on a small fraction of elements.
@@ -14,6 +15,7 @@ import math
 import pytest
 import torch
 
+from dsv4_flash_deployment_b200.models.kv_format import kv4_bytes, kv4_decode, kv8_bytes, kv8_decode
 from dsv4_flash_deployment_b200.models.weights import hc_fn_hilo
 from dsv4_flash_deployment_b200.ops import _ext
 from dsv4_flash_deployment_b200.ops.layout import ceil_to, chunks_to_sf
@@ -112,10 +114,11 @@ def test_qkv_post_matches_oracle(T):
     Tp = ceil_to(T, 128)
     qr_q = torch.empty(Tp, qd, dtype=torch.uint8, device=dev)
     qr_sf = torch.zeros(Tp // 128, qd // 128, 512, dtype=torch.uint8, device=dev)
-    kv = torch.empty(T, kvd, dtype=torch.bfloat16, device=dev)
+    kv_rec = torch.empty(T, kv8_bytes(kvd), dtype=torch.uint8, device=dev)
     ext.qkv_post(x.to(dev), qd, kvd, wq.to(dev), wk.to(dev), eps, qr_q, qr_sf, cos.to(dev).contiguous(),
-                 sin.to(dev).contiguous(), pos.to(dev), kv, T)
+                 sin.to(dev).contiguous(), pos.to(dev), kv_rec, T)
     torch.cuda.synchronize()
+    kv = kv8_decode(kv_rec.cpu(), kvd).to(torch.bfloat16)   # exact: the record holds the round trip
 
     qr = N.rms_norm(x[:, :qd], wq, eps)
     q_ref, s_ref = N.act_quant(qr)
@@ -180,7 +183,7 @@ def test_compress_pool_matches_oracle(r, co):
     dev = "cuda"
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
     max_c = 64
-    comp = torch.zeros(2, max_c, dh, dtype=torch.bfloat16, device=dev)
+    comp = torch.zeros(2, max_c, kv4_bytes(dh), dtype=torch.uint8, device=dev)
     idx = torch.zeros(2, max_c, kd, dtype=torch.bfloat16, device=dev)
     ring = torch.zeros(2, co * r, 2 * co * dh, dtype=torch.float32, device=dev)
     ext.compress_pool(G, i32([G]), i32([0] * G), i32([p // r for p in closes]), i32([0] * G), i32([0] * G), r, co,
@@ -207,13 +210,69 @@ def test_compress_pool_matches_oracle(r, co):
         latent = N.rms_norm(pooled.to(torch.bfloat16), norm_w, eps)
         c, s = cos[g * r], sin[g * r]
         want = N.fp4_act_quant_roundtrip(N.apply_rope(latent, c, s), 16, "e4m3")
-        got = comp[0, g].cpu()
+        got = kv4_decode(comp[0, g].cpu(), dh)
         assert _cos(got, want) > 0.9995, (g, _cos(got, want))
         assert float((got.float() != want.float()).float().mean()) < 0.05
         k = N.rms_norm(N.bf16_linear(latent[None], wk), k_norm, eps)
         k_want = N.fp4_act_quant_roundtrip(N.apply_rope(k, c, s), 32, "e8m0")[0]
         k_got = idx[0, g].cpu()
         assert _cos(k_got, k_want) > 0.999, (g, _cos(k_got, k_want))
+
+
+@pytest.mark.parametrize("nsplit", [1, 4])
+def test_attention_over_record_caches_matches_oracle(nsplit):
+    """Sparse attention of decode tokens over the quantized caches: window rows as
+    KV8 records (ring + this step's row), selected compressed rows as KV4 records.
+    Oracle: RoPE on q, ``N.sparse_attn`` over the decoded rows in the kernel's row
+    order (window ascending, then the selected entries), inverse RoPE on the output
+    (``reference.py:172-235``, ``ref/model.py`` ``_attention``)."""
+    from dsv4_flash_deployment_b200.config import v4_flash_config
+    from dsv4_flash_deployment_b200.models.kv_format import kv4_encode, kv8_encode
+
+    ext = _ext.load(required=True)
+    cfg = v4_flash_config(n_layers=2)
+    H, dh, W, max_c, k_sel = 64, 512, 128, 300, 200
+    g = torch.Generator().manual_seed(17 + nsplit)
+    pos = [70, 900, 1500]                      # window partly filled / full
+    T = len(pos)
+    q = (torch.randn(T, H, dh, generator=g)).to(torch.bfloat16)
+    ring_vals = torch.randn(T, W, dh, generator=g) * 0.7
+    step_vals = torch.randn(T, dh, generator=g) * 0.7
+    comp_vals = torch.randn(T, max_c, dh, generator=g) * 0.7
+    sink = torch.randn(H, generator=g)
+    cos, sin = N.layer_rope_tables(cfg, 4096)["yarn"]
+    sel = torch.stack([torch.randperm(max_c, generator=g)[:k_sel] for _ in range(T)]).to(torch.int32)
+    cnt = torch.tensor([k_sel, 150, k_sel], dtype=torch.int32)
+
+    dev = "cuda"
+    ring = kv8_encode(ring_vals)                     # [T slots, W, 528]
+    step = kv8_encode(step_vals)                     # [T, 528]
+    comp = kv4_encode(comp_vals)                     # [T slots, max_c, 288]
+    i32 = lambda v: torch.as_tensor(v, dtype=torch.int32).to(dev)
+    out = torch.empty(T, H, dh, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(T * nsplit * 64 * 514, dtype=torch.float32, device=dev)
+    ext.attention(q.to(dev), cos.to(dev).contiguous(), sin.to(dev).contiguous(), None, False, cfg.rms_norm_eps,
+                  step.to(dev), ring.to(dev), comp.to(dev), i32(range(T)), i32(pos), i32(pos), i32(range(T)),
+                  sel.to(dev), cnt.to(dev), sink.to(dev), dh ** -0.5, out, ws if nsplit > 1 else None, T, nsplit,
+                  None, 0, None)
+    torch.cuda.synchronize()
+
+    ring_dec = kv8_decode(ring, dh)
+    comp_dec = kv4_decode(comp, dh)
+    step_dec = kv8_decode(step, dh)
+    for t, p in enumerate(pos):
+        rows = []
+        for pp in range(max(0, p - W + 1), p + 1):    # window, ascending; this step's row last
+            rows.append(step_dec[t] if pp == p else ring_dec[t, pp % W])
+        rows += [comp_dec[t, int(ci)] for ci in sel[t, :int(cnt[t])]]
+        kv_all = torch.stack(rows)
+        qr = N.apply_rope(q[t], cos[p], sin[p])
+        idx = torch.arange(kv_all.shape[0])[None, None]
+        o = N.sparse_attn(qr[None, None], kv_all[None], sink, idx, dh ** -0.5)[0, 0]
+        want = N.apply_rope(o.to(torch.bfloat16), cos[p], sin[p], inverse=True)
+        got = out[t].cpu()
+        assert _cos(got, want) > 0.9995, (t, _cos(got, want))
+        assert float((got.float() - want.float()).abs().max()) < 0.05 * float(want.float().abs().max())
 
 
 @pytest.mark.parametrize("tile_rows", [32, 64, 256])
