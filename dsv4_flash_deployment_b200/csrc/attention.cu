@@ -12,7 +12,7 @@
 // Window rows of positions at or after the token's chunk start come from this
 // step's kv buffer (prefill chunks), earlier ones from the per-sequence ring.
 //
-// The caches hold quantized row records (common.cuh): window rows (the ring and
+// The caches hold quantized row records (kernels.h): window rows (the ring and
 // this step's rows) as KV8 (e4m3 + ue8m0 per 32, 528 bytes), compressed rows as
 // KV4 (packed e2m1 + e4m3 per 16, 288 bytes).  Both decode exactly to the bf16
 // values of the reference's round trips.
@@ -23,6 +23,8 @@
 // stay in registers, 64 dims per warp).
 // With splits > 1 the partial (acc, max, sum) go to a workspace and
 // attn_combine merges them (C = 1 decode spreads a token over many SMs).
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "mma_sync.cuh"
@@ -51,7 +53,8 @@ constexpr size_t kSmemTotal = kSmemQ + kSmemKV + 2 * kSmemRaw + kSmemP + kSmemRo
 static_assert(kRec8 % 16 == 0 && kRec4 % 16 == 0, "records must be whole 16-byte pieces");
 static_assert(kSmemTotal <= 227 * 1024, "attention shared memory exceeds the per-CTA limit");
 
-// Eight columns [8c, 8c + 8) of a KV8 record -> bf16.
+// Eight columns [8c, 8c + 8) of a KV8 record -> bf16: two e4m3 codes per
+// hardware conversion to f16 (exact), then the power-of-two scale in fp32.
 DSV4_DEV uint4 decode8_kv8(const uint8_t* rec, int c) {
   const uint2 codes = *reinterpret_cast<const uint2*>(rec + 8 * c);
   const uint32_t e = rec[kDh + (c >> 2)];
@@ -61,24 +64,27 @@ DSV4_DEV uint4 decode8_kv8(const uint8_t* rec, int c) {
   const uint32_t w[2] = {codes.x, codes.y};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t b = w[i >> 1] >> (16 * (i & 1));
-    const float lo = e4m3_to_f32((uint8_t)(b & 0xFF)) * sc;
-    const float hi = e4m3_to_f32((uint8_t)((b >> 8) & 0xFF)) * sc;
-    o32[i] = pack_bf16(lo, hi);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i >> 1] >> (16 * (i & 1))), __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    o32[i] = pack_bf16(f.x * sc, f.y * sc);
   }
   return o;
 }
 
-// Eight columns [8c, 8c + 8) of a KV4 record -> bf16.
+// Eight columns [8c, 8c + 8) of a KV4 record -> bf16: two e2m1 codes per
+// hardware conversion to f16, times the e4m3 scale in f16 (e2m1 x e4m3 lies in
+// [2^-10, 2688] with at most 6 significant bits: exact in f16 and in bf16).
 DSV4_DEV uint4 decode8_kv4(const uint8_t* rec, int c) {
   const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * c);
-  const float sc = e4m3_to_f32(rec[kDh / 2 + (c >> 1)]);
+  const __half_raw sr = __nv_cvt_fp8_to_halfraw(rec[kDh / 2 + (c >> 1)], __NV_E4M3);
+  const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(&sr));
   uint4 o;
   uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t b = (codes >> (8 * i)) & 0xFF;
-    o32[i] = pack_bf16(e2m1_value(b & 0xF) * sc, e2m1_value(b >> 4) * sc);
+    const __half2_raw hr = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((codes >> (8 * i)) & 0xFF), __NV_E2M1);
+    const float2 f = __half22float2(__hmul2(*reinterpret_cast<const __half2*>(&hr), s2));
+    o32[i] = pack_bf16(f.x, f.y);
   }
   return o;
 }
@@ -201,6 +207,7 @@ __global__ void __launch_bounds__(256, 1) attn_kernel(AttnParams p) {
   auto decode_block = [&](int b, int buf) {
     const uint8_t* raw = sRaw + (size_t)buf * kSmemRaw;
     const int c = tid & 63;
+#pragma unroll 4
     for (int r = tid >> 6; r < kBlk; r += 4) {
       const int gr = b * kBlk + r;
       const uint8_t* rec = raw + (size_t)r * kRec8;

@@ -454,8 +454,11 @@ void compress_pool(int64_t n_groups, const Tensor& n_groups_dev, const Tensor& g
   p.max_c = (int)comp_out.size(1);
   p.wk = ptr<const bf16>(wk);
   p.k_norm_w = ptr<const bf16>(k_norm_w);
-  p.idx_out = ptr<bf16>(idx_out);
-  p.idx_dim = idx_out ? (int)idx_out->size(2) : 0;
+  if (idx_out)
+    TORCH_CHECK(idx_out->scalar_type() == at::kByte && idx_out->size(2) == dsv4::ik4_bytes(128),
+                "idx_out must be [slots, max_c, 68] uint8 IK4 records (128-dim keys)");
+  p.idx_out = ptr<uint8_t>(idx_out);
+  p.idx_dim = idx_out ? 128 : 0;
   p.pages = kv_pages_of(pages, &p.max_c);
   CUDA_OK(dsv4::compress_pool(p, cur_stream()));
 }
@@ -533,7 +536,14 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
   p.head_dim = (int)q.size(2);
   p.q = ptr<const bf16>(q);
   p.w = ptr<const float>(w);
-  p.kcache = ptr<const bf16>(kcache);
+  // key caches hold IK4 records (kernels.h): 68 bytes per 128-dim key
+  TORCH_CHECK(q.size(2) == 128, "indexer head dim must be 128");
+  TORCH_CHECK(kcache.scalar_type() == at::kByte && kcache.dim() == 3 && kcache.size(2) == dsv4::ik4_bytes(128),
+              "kcache must be [slots, max_c, 68] uint8 IK4 records");
+  if (kcache_alt)
+    TORCH_CHECK(kcache_alt->scalar_type() == at::kByte && kcache_alt->size(2) == dsv4::ik4_bytes(128),
+                "kcache_alt must hold IK4 records");
+  p.kcache = ptr<const uint8_t>(kcache);
   p.max_c = (int)kcache.size(1);
   p.slot = ptr<const int>(slot);
   p.clen = ptr<const int>(clen);
@@ -545,7 +555,7 @@ void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const 
   p.cand_block = (int)std::max<int64_t>(1, cand_block);
   p.cand_topk = (int)cand_topk;
   p.err = ptr<uint32_t>(err);
-  p.kcache_alt = ptr<const bf16>(kcache_alt);
+  p.kcache_alt = ptr<const uint8_t>(kcache_alt);
   p.alt_max_c = kcache_alt ? (int)kcache_alt->size(1) : 0;
   p.pages = kv_pages_of(pages, &p.max_c);
   if (kcache_alt) p.alt_pages = kv_pages_of(alt_pages, &p.alt_max_c);

@@ -375,18 +375,13 @@ DSV4_DEV float e4m3_to_f32(uint8_t b) {
 }
 
 // ------------------------------------------------------ cache row records
-// (layouts: kv8_bytes / kv4_bytes in kernels.h)
+// (layouts: kv8_bytes / kv4_bytes / ik4_bytes in kernels.h)
 // E2M1 code of x at scale s (bit 3 = sign): exact midpoint compares, ties to even.
 DSV4_DEV uint32_t e2m1_code(float x, float s) {
   const float ax = fabsf(x);
   const uint32_t mag = (ax > 0.25f * s) + (ax >= 0.75f * s) + (ax > 1.25f * s) + (ax >= 1.75f * s) +
                        (ax > 2.5f * s) + (ax >= 3.5f * s) + (ax > 5.0f * s);
   return mag | (signbit(x) ? 8u : 0u);
-}
-DSV4_DEV float e2m1_value(uint32_t code) {
-  const uint32_t c = code & 7u;
-  const float mag = c <= 4 ? 0.5f * (float)c : (c == 5 ? 3.f : (c == 6 ? 4.f : 6.f));
-  return (code & 8u) ? -mag : mag;
 }
 
 DSV4_DEV float warp_max(float v) {

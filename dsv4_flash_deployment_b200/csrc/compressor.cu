@@ -1,8 +1,9 @@
 // KV compressor: softmax-gated pooling of r (or 2r, overlapped) token
 // projections into one compressed latent row, then RMSNorm, RoPE at the group
-// start, e2m1 codes with e4m3 scales per 16 stored as a KV4 record (common.cuh)
-// into the sequence's compressed cache; optionally the indexer key of the same entry (latent @ wk
-// -> RMSNorm -> RoPE -> e2m1/ue8m0-per-32 round trip).  Reference:
+// start, e2m1 codes with e4m3 scales per 16 stored as a KV4 record (kernels.h)
+// into the sequence's compressed cache; optionally the indexer key of the same
+// entry (latent @ wk -> RMSNorm -> RoPE -> e2m1 with ue8m0 scales per 32, an
+// IK4 record).  Reference:
 // _compressor_step (reference.py:547-603), _indexer_step k path (:621-640),
 // latent store (:792-807).
 //
@@ -13,14 +14,6 @@
 #include "kernels.h"
 
 namespace dsv4 {
-
-DSV4_DEV float e2m1_qdq_c(float x, float s) {
-  const float ax = fabsf(x);
-  const int c = (ax > 0.25f * s) + (ax >= 0.75f * s) + (ax > 1.25f * s) + (ax >= 1.75f * s) + (ax > 2.5f * s) +
-                (ax >= 3.5f * s) + (ax > 5.0f * s);
-  const float mag = c <= 4 ? 0.5f * c : (c == 5 ? 3.f : (c == 6 ? 4.f : 6.f));
-  return (signbit(x) ? -mag : mag) * s;
-}
 
 template <int NT>
 DSV4_DEV float block_sum(float v, float* red) {
@@ -179,9 +172,14 @@ __global__ void __launch_bounds__(512) compress_pool_kernel(CompParams p) {
       kn = __bfloat162float(__float2bfloat16(kn));
     }
   }
+  // IK4 record: packed e2m1 codes, then the ue8m0 exponent of each 32 dims (one warp)
   const float amax = fmaxf(warp_max(fabsf(kn)), 6.f * 1.1754943508222875e-38f);
-  const float s = exp_to_f32(pow2_ceil_exp(amax, 1.f / 6.f));
-  p.idx_out[kv_row(p.pages, slot, g, p.max_c) * kd + d] = __float2bfloat16(e2m1_qdq_c(kn, s));
+  const uint32_t e = pow2_ceil_exp(amax, 1.f / 6.f);
+  const uint32_t code = e2m1_code(kn, exp_to_f32(e));
+  const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
+  uint8_t* rec = p.idx_out + kv_row(p.pages, slot, g, p.max_c) * ik4_bytes(kd);
+  if ((d & 1) == 0) rec[d >> 1] = (uint8_t)(code | (hi << 4));
+  if ((d & 31) == 0) rec[kd / 2 + (d >> 5)] = (uint8_t)e;
 }
 
 cudaError_t compress_pool(const CompParams& p, cudaStream_t st) {

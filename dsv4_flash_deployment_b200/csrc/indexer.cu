@@ -19,6 +19,8 @@
 //               select and ordered compaction on the keys in shared memory
 // Spreading the scoring over the compressed rows keeps long contexts (9K
 // tokens = 2304 entries at ratio 4) from serializing on one CTA per token.
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "mma_sync.cuh"
@@ -127,6 +129,7 @@ DSV4_DEV int ordered_select(const uint32_t* keys, int n, uint32_t kth, int n_eq_
 constexpr int kIdxRows = 64;            // compressed rows per scoring CTA
 constexpr int kIdxDh = 128;             // indexer head dim (both model families)
 constexpr int kIdxPad = kIdxDh + 8;     // smem row stride (bf16) against bank conflicts
+constexpr int kIk4 = ik4_bytes(kIdxDh);  // 68-byte key records (4-byte aligned)
 constexpr int kIdxMaxHeads = 64;
 
 DSV4_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
@@ -153,14 +156,28 @@ __global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* k
   const int slot = p.slot[t];
   const bool use_alt = p.kcache_alt != nullptr && ((p.pos[t] + 1) % p.own_r) != 0 &&
                        p.chunk_start[t] == p.last_pos[t];
-  const __nv_bfloat16* kc = use_alt ? p.kcache_alt : p.kcache;
+  const uint8_t* kc = use_alt ? p.kcache_alt : p.kcache;
   const KvPages kpg = use_alt ? p.alt_pages : p.pages;
   const int kmax = use_alt ? p.alt_max_c : p.max_c;
+  // keys are IK4 records: 8 columns = one 4-byte word of e2m1 codes; the scale is
+  // the ue8m0 byte of their 32-column block.  Decoded exactly to bf16.
   for (int c = tid; c < kIdxRows * (kIdxDh / 8); c += 128) {
     const int r = c / (kIdxDh / 8), ch = c % (kIdxDh / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r0 + r < clen)
-      v = *reinterpret_cast<const uint4*>(kc + kv_row(kpg, slot, r0 + r, kmax) * kIdxDh + ch * 8);
+    if (r0 + r < clen) {
+      const uint8_t* rec = kc + kv_row(kpg, slot, r0 + r, kmax) * kIk4;
+      const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * ch);
+      const uint32_t e = rec[kIdxDh / 2 + (ch >> 2)];
+      const float sc = e ? __uint_as_float(e << 23) : 0.f;
+      uint32_t* v32 = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {   // two e2m1 codes per hardware conversion (exact in f16)
+        const __half2_raw hr =
+            __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((codes >> (8 * i)) & 0xFF), __NV_E2M1);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        v32[i] = pack_bf16(f.x * sc, f.y * sc);
+      }
+    }
     *reinterpret_cast<uint4*>(sK + r * kIdxPad + ch * 8) = v;
   }
   __syncthreads();

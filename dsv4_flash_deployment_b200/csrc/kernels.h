@@ -12,10 +12,12 @@ namespace dsv4 {
 // of the round trip it went through.  KV8 (window rows): d e4m3 codes, then
 // d/32 ue8m0 scale bytes.  KV4 (compressed rows): d/2 bytes of e2m1 codes
 // (column 2i in the low nibble of byte i, 2i+1 in the high nibble), then d/16
-// e4m3 scale bytes.  Both decode exactly to the bf16 values of the round trip
+// e4m3 scale bytes.  IK4 (indexer keys): the same packed e2m1 codes, then d/32
+// ue8m0 scale bytes.  All decode exactly to the bf16 values of the round trip
 // (at most 6 significant bits).
 __host__ __device__ constexpr int kv8_bytes(int d) { return d + d / 32; }
 __host__ __device__ constexpr int kv4_bytes(int d) { return d / 2 + d / 16; }
+__host__ __device__ constexpr int ik4_bytes(int d) { return d / 2 + d / 32; }
 
 // Block table of a paged compressed cache: entry ci of sequence slot s lives in
 // pool row table[s * ld + (ci >> shift)] << shift | (ci & (2^shift - 1)).
@@ -167,7 +169,7 @@ struct CompParams {
   KvPages pages;                    // rows of comp_out and idx_out
   const __nv_bfloat16* wk;          // indexer K projection [idx_dim, dh] (null = none)
   const __nv_bfloat16* k_norm_w;
-  __nv_bfloat16* idx_out;           // [slots, max_c, idx_dim]
+  uint8_t* idx_out;                 // [slots, max_c, ik4_bytes(idx_dim)] IK4 records
   int idx_dim;
 };
 cudaError_t compress_pool(const CompParams& p, cudaStream_t st);
@@ -216,7 +218,7 @@ struct IdxParams {
   int T, n_heads, head_dim;
   const __nv_bfloat16* q;           // [T, n_heads, head_dim]
   const float* w;                   // [T, n_heads] (already bf16-rounded)
-  const __nv_bfloat16* kcache;      // [slots, max_c, head_dim] or a paged pool (pages)
+  const uint8_t* kcache;            // [slots, max_c, ik4_bytes(head_dim)] IK4 records or a paged pool
   int max_c;
   KvPages pages;
   const int* slot;
@@ -229,7 +231,7 @@ struct IdxParams {
   int cand_block, cand_topk;
   uint32_t* err;
   // tokens whose position does not close a group of ratio own_r read kcache_alt
-  const __nv_bfloat16* kcache_alt;
+  const uint8_t* kcache_alt;
   int alt_max_c;
   KvPages alt_pages;
   const int* pos;

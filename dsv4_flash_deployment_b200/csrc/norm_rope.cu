@@ -3,7 +3,7 @@
 // qkv_post: the fused wq_a|wkv GEMM output row is split into
 //   qr = bf16(rmsnorm(q part) * q_norm)   -> MXFP8 for the wq_b / indexer GEMMs
 //   kv = bf16(rmsnorm(kv part) * kv_norm) -> RoPE at pos (fp32, rounded to bf16)
-//        -> FP8 e4m3 / ue8m0 per 32, stored as a KV8 record (common.cuh): the
+//        -> FP8 e4m3 / ue8m0 per 32, stored as a KV8 record (kernels.h): the
 //        window KV contract, kept in its quantized form
 // (reference.py:704-731).
 #include "common.cuh"

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import torch
 
-from ..models.kv_format import kv4_bytes, kv8_bytes
+from ..models.kv_format import ik4_bytes, kv4_bytes, kv8_bytes
 
 
 def expert_block_bytes(cfg, ep_world: int = 1) -> int:
@@ -37,7 +37,7 @@ def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int, kv_block:
         dense += cfg.index_n_heads * cfg.index_head_dim * cfg.q_lora_rank + 2 * 128 * d
     emb = 2 * 2 * cfg.vocab_size * d
     s = n_slots + 1
-    # window rows are KV8 records, compressed rows KV4 records (models/kv_format.py)
+    # window rows are KV8 records, compressed rows KV4, indexer keys IK4 (models/kv_format.py)
     kv = cfg.n_layers * s * cfg.sliding_window * kv8_bytes(cfg.head_dim)
     for l in cfg.kv_source_layer_ids:
         r, co = cfg.ratio(l), cfg.overlap(l)
@@ -48,7 +48,7 @@ def non_expert_bytes(cfg, max_tokens: int, n_slots: int, max_seq: int, kv_block:
             rows = s * (max_seq // r)
         kv += rows * kv4_bytes(cfg.head_dim) + s * co * r * 2 * co * cfg.head_dim * 4
         if l in cfg.index_source_layer_ids:
-            kv += rows * cfg.index_head_dim * 2
+            kv += rows * ik4_bytes(cfg.index_head_dim)
     t = max_tokens
     k = cfg.n_activated_experts
     cap = t * k * 2 + cfg.n_routed_experts * 128

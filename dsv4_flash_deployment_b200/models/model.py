@@ -32,7 +32,7 @@ import numpy as np
 import torch
 
 from ..ops import _ext
-from .kv_format import kv4_bytes, kv8_bytes
+from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
 from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
                         pick_bn)
 from ..ops.layout import ceil_to
@@ -330,7 +330,7 @@ class DSV4Model:
             shape = (S, max(1, self.max_seq_len // r)) if self.pager is None else (1, self.pager.rows(r))
             self.comp[l] = torch.zeros(*shape, kv4_bytes(cfg.head_dim), dtype=torch.uint8, device=dev)
             if l in cfg.index_source_layer_ids:
-                self.idx_cache[l] = torch.zeros(*shape, cfg.index_head_dim, dtype=torch.bfloat16, device=dev)
+                self.idx_cache[l] = torch.zeros(*shape, ik4_bytes(cfg.index_head_dim), dtype=torch.uint8, device=dev)
             self.comp_ring[l] = torch.zeros(S, co * r, 2 * co * cfg.head_dim, dtype=torch.float32, device=dev)
         # order keys of the indexer scores, [T, widest index cache] (scoring CTAs -> select CTA)
         kc = max([max(1, self.max_seq_len // cfg.ratio(l)) for l in self.idx_cache] or [1])

@@ -11,6 +11,7 @@ reference scores up to that tolerance, in ascending index order.
 import pytest
 import torch
 
+from dsv4_flash_deployment_b200.models.kv_format import ik4_decode, ik4_encode
 from dsv4_flash_deployment_b200.ops import _ext
 from dsv4_flash_deployment_b200.ops.gemm import ErrorWord
 
@@ -19,10 +20,16 @@ pytestmark = pytest.mark.gpu
 HD = 128
 
 
+def _keys(S, max_c):
+    """Key cache as IK4 records on the device, and its exact decoded values (CPU)."""
+    rec = ik4_encode(torch.randn(S, max_c, HD))
+    return rec.cuda(), ik4_decode(rec, HD).bfloat16()
+
+
 def _ref_scores(q, w, kc, slot, clen):
     out = []
     for t in range(q.shape[0]):
-        k = kc[slot[t], :clen[t]].float()
+        k = kc[slot[t], :clen[t]].float()          # decoded key values
         raw = (q[t].float() @ k.T).bfloat16().float()                     # [H, clen]
         terms = (raw.clamp_min(0) * w[t, :, None]).bfloat16().float()
         out.append(terms.sum(0).bfloat16().float())
@@ -74,13 +81,13 @@ def test_indexer_topk_matches_reference(H, lens):
     max_c = 2304
     S = 3
     T = len(lens)
-    kc = torch.randn(S, max_c, HD).bfloat16().to(dev)
+    kc, kvals = _keys(S, max_c)
     q = torch.randn(T, H, HD).bfloat16().to(dev)
     w = (torch.randn(T, H) * 0.3).bfloat16().float().to(dev)
     slot = torch.tensor([i % S for i in range(T)], dtype=torch.int32, device=dev)
     clen = torch.tensor(lens, dtype=torch.int32, device=dev)
     idx, cnt = _run(q, w, kc, slot, clen, topk)
-    ref = _ref_scores(q.cpu(), w.cpu(), kc.cpu(), slot.cpu(), lens)
+    ref = _ref_scores(q.cpu(), w.cpu(), kvals, slot.cpu(), lens)
     _check_topk(idx, cnt, ref, topk)
 
 
@@ -91,7 +98,7 @@ def test_indexer_candidate_blocks():
     topk, blk, ctop, max_c, H = 16, 16, 4, 512, 16
     lens = [500, 70, 33]
     T, S = len(lens), 2
-    kc = torch.randn(S, max_c, HD).bfloat16().to(dev)
+    kc, kvals = _keys(S, max_c)
     q1 = torch.randn(T, H, HD).bfloat16().to(dev)
     q2 = torch.randn(T, H, HD).bfloat16().to(dev)
     w = (torch.rand(T, H) + 0.1).bfloat16().float().to(dev)
@@ -100,7 +107,7 @@ def test_indexer_candidate_blocks():
     cand = torch.zeros(T, max_c // blk, dtype=torch.uint8, device=dev)
     _run(q1, w, kc, slot, clen, topk, cand, 1, blk, ctop)
     cand_cpu = cand.cpu().bool()
-    ref1 = _ref_scores(q1.cpu(), w.cpu(), kc.cpu(), slot.cpu(), lens)
+    ref1 = _ref_scores(q1.cpu(), w.cpu(), kvals, slot.cpu(), lens)
     allowed = []
     for t, sc in enumerate(ref1):
         n = sc.numel()
@@ -116,7 +123,7 @@ def test_indexer_candidate_blocks():
             assert float(lo) >= float(hi) - abs(float(hi)) * 2 ** -7 - 1e-6
         allowed.append(got.repeat_interleave(blk))
     idx, cnt = _run(q2, w, kc, slot, clen, topk, cand, 2, blk, ctop)
-    ref2 = _ref_scores(q2.cpu(), w.cpu(), kc.cpu(), slot.cpu(), lens)
+    ref2 = _ref_scores(q2.cpu(), w.cpu(), kvals, slot.cpu(), lens)
     for t in range(T):
         sel = idx[t, :int(cnt[t])].long()
         assert allowed[t][sel].all(), "level-2 picks stay inside candidate blocks"

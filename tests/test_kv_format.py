@@ -63,3 +63,14 @@ def test_kv4_nibble_order_is_the_checkpoint_packing():
 def test_record_caches_are_smaller():
     d = 512
     assert kv8_bytes(d) / (2 * d) < 0.52 and kv4_bytes(d) / (2 * d) < 0.29
+
+
+def test_ik4_record_is_the_indexer_key_round_trip():
+    from dsv4_flash_deployment_b200.models.kv_format import ik4_bytes, ik4_decode, ik4_encode
+
+    x = _rows(d=128, seed=3)
+    rec = ik4_encode(x)
+    assert ik4_bytes(128) == 68 and rec.shape == (64, 68)
+    dec = ik4_decode(rec, 128)
+    assert torch.equal(dec.to(torch.bfloat16), N.fp4_act_quant_roundtrip(x, 32, "e8m0"))
+    assert torch.equal(dec, dec.to(torch.bfloat16).float())

@@ -15,7 +15,8 @@ import math
 import pytest
 import torch
 
-from dsv4_flash_deployment_b200.models.kv_format import kv4_bytes, kv4_decode, kv8_bytes, kv8_decode
+from dsv4_flash_deployment_b200.models.kv_format import (ik4_bytes, ik4_decode, kv4_bytes, kv4_decode, kv8_bytes,
+                                                         kv8_decode)
 from dsv4_flash_deployment_b200.models.weights import hc_fn_hilo
 from dsv4_flash_deployment_b200.ops import _ext
 from dsv4_flash_deployment_b200.ops.layout import ceil_to, chunks_to_sf
@@ -184,7 +185,7 @@ def test_compress_pool_matches_oracle(r, co):
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
     max_c = 64
     comp = torch.zeros(2, max_c, kv4_bytes(dh), dtype=torch.uint8, device=dev)
-    idx = torch.zeros(2, max_c, kd, dtype=torch.bfloat16, device=dev)
+    idx = torch.zeros(2, max_c, ik4_bytes(kd), dtype=torch.uint8, device=dev)
     ring = torch.zeros(2, co * r, 2 * co * dh, dtype=torch.float32, device=dev)
     ext.compress_pool(G, i32([G]), i32([0] * G), i32([p // r for p in closes]), i32([0] * G), i32([0] * G), r, co,
                       proj.to(dev), ape.to(dev), ring, norm_w.to(dev), eps, cos.to(dev).contiguous(),
@@ -215,7 +216,7 @@ def test_compress_pool_matches_oracle(r, co):
         assert float((got.float() != want.float()).float().mean()) < 0.05
         k = N.rms_norm(N.bf16_linear(latent[None], wk), k_norm, eps)
         k_want = N.fp4_act_quant_roundtrip(N.apply_rope(k, c, s), 32, "e8m0")[0]
-        k_got = idx[0, g].cpu()
+        k_got = ik4_decode(idx[0, g].cpu(), kd)
         assert _cos(k_got, k_want) > 0.999, (g, _cos(k_got, k_want))
 
 
