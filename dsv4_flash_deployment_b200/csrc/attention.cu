@@ -23,6 +23,8 @@
 // stay in registers, 64 dims per warp).
 // With splits > 1 the partial (acc, max, sum) go to a workspace and
 // attn_combine merges them (C = 1 decode spreads a token over many SMs).
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "mma_sync.cuh"
@@ -51,40 +53,38 @@ constexpr size_t kSmemTotal = kSmemQ + kSmemKV + 2 * kSmemRaw + kSmemP + kSmemRo
 static_assert(kRec8 % 16 == 0 && kRec4 % 16 == 0, "records must be whole 16-byte pieces");
 static_assert(kSmemTotal <= 227 * 1024, "attention shared memory exceeds the per-CTA limit");
 
-// Eight columns [8c, 8c + 8) of a KV8 record -> bf16, exactly: code bits in an
-// fp32 (common.cuh), times 2^120, times the power-of-two scale; all full-rate
-// integer / FMUL work (the conversion unit would bound this loop).
+// Eight columns [8c, 8c + 8) of a KV8 record -> bf16: two e4m3 codes per
+// hardware conversion to f16 (exact), then the power-of-two scale in fp32.
 DSV4_DEV uint4 decode8_kv8(const uint8_t* rec, int c) {
   const uint2 codes = *reinterpret_cast<const uint2*>(rec + 8 * c);
   const uint32_t e = rec[kDh + (c >> 2)];
   const float sc = e ? __uint_as_float(e << 23) : 0.f;
-  const float k120 = pow2_f32(120);
   uint4 o;
   uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
   const uint32_t w[2] = {codes.x, codes.y};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t b = w[i >> 1] >> (16 * (i & 1));
-    const float lo = e4m3_field_f32(b) * k120 * sc;
-    const float hi = e4m3_field_f32(b >> 8) * k120 * sc;
-    o32[i] = pack_bf16_exact(lo, hi);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i >> 1] >> (16 * (i & 1))), __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    o32[i] = pack_bf16(f.x * sc, f.y * sc);
   }
   return o;
 }
 
-// Eight columns [8c, 8c + 8) of a KV4 record -> bf16, exactly: e2m1 code bits in
-// an fp32 times 2^126 (the code's value), times the e4m3 scale (decoded the same
-// way); e2m1 x e4m3 has at most 6 significant bits.
+// Eight columns [8c, 8c + 8) of a KV4 record -> bf16: two e2m1 codes per
+// hardware conversion to f16, times the e4m3 scale in f16 (e2m1 x e4m3 lies in
+// [2^-10, 2688] with at most 6 significant bits: exact in f16 and in bf16).
 DSV4_DEV uint4 decode8_kv4(const uint8_t* rec, int c) {
   const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * c);
-  const float sc = e4m3_field_f32(rec[kDh / 2 + (c >> 1)]) * pow2_f32(120);
-  const float k126 = pow2_f32(126);
+  const __half_raw sr = __nv_cvt_fp8_to_halfraw(rec[kDh / 2 + (c >> 1)], __NV_E4M3);
+  const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(&sr));
   uint4 o;
   uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t b = codes >> (8 * i);
-    o32[i] = pack_bf16_exact(e2m1_field_f32(b) * k126 * sc, e2m1_field_f32(b >> 4) * k126 * sc);
+    const __half2_raw hr = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((codes >> (8 * i)) & 0xFF), __NV_E2M1);
+    const float2 f = __half22float2(__hmul2(*reinterpret_cast<const __half2*>(&hr), s2));
+    o32[i] = pack_bf16(f.x, f.y);
   }
   return o;
 }

@@ -384,24 +384,6 @@ DSV4_DEV uint32_t e2m1_code(float x, float s) {
   return mag | (signbit(x) ? 8u : 0u);
 }
 
-// Exact decode of small float codes without the conversion unit.  Placing a
-// code's exponent and mantissa bits into the matching fields of an fp32 gives
-// value / 2^120 for e4m3 (exponent bias 7) and value / 2^126 for e2m1 (bias 1);
-// a zero exponent lands on an fp32 subnormal with the same scale, so one map
-// covers normal and subnormal codes.  One full-rate FMUL by 2^120 / 2^126
-// restores the value exactly.
-DSV4_DEV float e4m3_field_f32(uint32_t b) {   // code in bits [0, 8)
-  return __uint_as_float(((b & 0x7Fu) << 20) | ((b & 0x80u) << 24));
-}
-DSV4_DEV float e2m1_field_f32(uint32_t c) {   // code in bits [0, 4)
-  return __uint_as_float(((c & 7u) << 22) | ((c & 8u) << 28));
-}
-DSV4_DEV float pow2_f32(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }   // 2^e, e in [-126, 127]
-// Two fp32 values that are exact in bf16 -> packed bf16x2 (truncation is exact).
-DSV4_DEV uint32_t pack_bf16_exact(float lo, float hi) {
-  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
-}
-
 DSV4_DEV float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -19,6 +19,8 @@
 //               select and ordered compaction on the keys in shared memory
 // Spreading the scoring over the compressed rows keeps long contexts (9K
 // tokens = 2304 entries at ratio 4) from serializing on one CTA per token.
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "mma_sync.cuh"
@@ -168,11 +170,12 @@ __global__ void __launch_bounds__(128) idx_score_kernel(IdxParams p, uint32_t* k
       const uint32_t e = rec[kIdxDh / 2 + (ch >> 2)];
       const float sc = e ? __uint_as_float(e << 23) : 0.f;
       uint32_t* v32 = reinterpret_cast<uint32_t*>(&v);
-      const float k126 = pow2_f32(126);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {   // exact integer / FMUL decode (common.cuh)
-        const uint32_t b = codes >> (8 * i);
-        v32[i] = pack_bf16_exact(e2m1_field_f32(b) * k126 * sc, e2m1_field_f32(b >> 4) * k126 * sc);
+      for (int i = 0; i < 4; ++i) {   // two e2m1 codes per hardware conversion (exact in f16)
+        const __half2_raw hr =
+            __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((codes >> (8 * i)) & 0xFF), __NV_E2M1);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        v32[i] = pack_bf16(f.x * sc, f.y * sc);
       }
     }
     *reinterpret_cast<uint4*>(sK + r * kIdxPad + ch * 8) = v;
