@@ -81,7 +81,7 @@ def main(argv=None):
         for T in Ts:
             def layer():
                 yp, ps, kk, _ = m._moe(L, T)
-                m._hc(T, Y=m.shared_out, yperm=yp, pos=ps, topk=kk, prev=m.mixF)
+                m._hc(T, Y=m.shared_y, yperm=yp, pos=ps, topk=kk, prev=m.mixF)
 
             for _ in range(3):
                 layer()

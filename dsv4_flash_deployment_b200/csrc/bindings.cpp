@@ -91,13 +91,17 @@ static dsv4::PeerSync peer_sync_of(const optional<Tensor>& t) {
   return s;
 }
 
-void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_sf, const Tensor& B,
-          const optional<Tensor>& B_sf, const optional<Tensor>& out, int64_t M, int64_t N, int64_t K, int64_t bn,
-          int64_t splits, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
-          const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
-          double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
-          const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
-          const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer) {
+// A2 / A2_sf (grouped GEMMs, optional): a second weight matrix of the same K and
+// kind; tile records whose a_row0 carries kTileA2 read it (the shared expert in
+// the routed experts' tile list).
+void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_sf, const Tensor& B,
+             const optional<Tensor>& B_sf, const optional<Tensor>& out, int64_t M, int64_t N, int64_t K, int64_t bn,
+             int64_t splits, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
+             const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
+             double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
+             const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
+             const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer,
+             const optional<Tensor>& A2, const optional<Tensor>& A2_sf) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -119,10 +123,18 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
                   (bn == 64 || bn == 128) && !caller_ws && splits <= 1 && k_tiles_mx >= 64 && tiles256 >= 96 &&
                   bm256_enabled())
                      ? 256 : 128;
-  CUtensorMap ta;
+  dsv4::AMaps ta{};
   dsv4::BMaps tb;
-  TORCH_CHECK(dsv4::make_tma_2d(&ta, A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
+  TORCH_CHECK(dsv4::make_tma_2d(&ta.m[0], A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
               "TMA(A) encode failed");
+  if (A2) {
+    TORCH_CHECK(grouped && bm == 128 && A2->is_cuda() && A2->is_contiguous() && A2->dim() == 2 && A2->size(0) % 128 == 0,
+                "A2: grouped GEMMs only, [rows (multiple of 128), K] contiguous");
+    TORCH_CHECK(A2->scalar_type() == A.scalar_type() && A2->size(1) == A.size(1), "A2 must match A's type and K");
+    TORCH_CHECK(kind == dsv4::KIND_BF16 || A2_sf.has_value(), "block-scaled A2 needs A2_sf");
+    TORCH_CHECK(dsv4::make_tma_2d(&ta.m[1], A2->data_ptr(), tma_elem_of(*A2, e2m1), A2->size(0), K, (uint32_t)bm),
+                "TMA(A2) encode failed");
+  }
   if (grouped) {
     const uint32_t boxes[4] = {32, 64, 128, 256};
     for (int i = 0; i < 4; ++i)
@@ -147,6 +159,8 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   p.splits = (int)std::max<int64_t>(1, splits);
   p.sfa = u8ptr(A_sf);
   p.sfa_ktiles = (int)(K / 128);
+  p.sfa2 = A2 ? (A2_sf ? u8ptr(A2_sf) : reinterpret_cast<const uint8_t*>(A2->data_ptr())) : nullptr;
+  p.M2 = A2 ? (int)A2->size(0) : 0;
   p.sfb = u8ptr(B_sf);
   p.sfb_ktiles = (int)(b_cols / 128);
   if (groups > 1) {
@@ -210,6 +224,18 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
   }
   int grid = p.cluster_split ? units : std::min(units, max_grid > 0 ? (int)max_grid : num_sms());
   CUDA_OK(dsv4::gemm_launch((int)kind, (int)epi, grouped, (int)bn, bm, ta, tb, p, grid, cur_stream()));
+}
+
+void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_sf, const Tensor& B,
+          const optional<Tensor>& B_sf, const optional<Tensor>& out, int64_t M, int64_t N, int64_t K, int64_t bn,
+          int64_t splits, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
+          const optional<Tensor>& row_scale, const optional<Tensor>& hq, const optional<Tensor>& hsf,
+          double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
+          const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
+          const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer) {
+  gemm_a2(kind, epi, A, A_sf, B, B_sf, out, M, N, K, bn, splits, tiles, n_tiles, row_scale, hq, hsf, swiglu_limit,
+          m_valid, ldo, workspace, counters, err, max_grid, groups, publish, ret_meta, ret_peer, c10::nullopt,
+          c10::nullopt);
 }
 
 void act_quant_mx(const Tensor& x, Tensor& q, Tensor& sf) {
@@ -489,7 +515,8 @@ void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const T
               const Tensor& counts, const Tensor& seg_start, const Tensor& rank, int64_t tile_rows, int64_t m13,
               int64_t m2, const Tensor& tiles13, const Tensor& n_tiles13, const Tensor& tiles2,
               const Tensor& n_tiles2, int64_t cap_rows, const Tensor& pos, const Tensor& row_scale,
-              const Tensor& err, const optional<Tensor>& seg_cnt, int64_t seg_cap) {
+              const Tensor& err, const optional<Tensor>& seg_cnt, int64_t seg_cap, int64_t shared_rows,
+              int64_t shared_row0) {
   dsv4::MoePlanParams p{};
   p.T = (int)T;
   p.topk = (int)topk;
@@ -515,13 +542,19 @@ void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const T
   p.err = ptr<uint32_t>(err);
   p.seg_cnt = ptr<const int>(seg_cnt);
   p.seg_cap = (int)seg_cap;
+  p.shared_rows = (int)shared_rows;
+  p.shared_row0 = (int)shared_row0;
+  if (shared_rows > 0)
+    TORCH_CHECK(shared_row0 + shared_rows <= row_scale.numel(), "shared segment outside row_scale");
   CUDA_OK(dsv4::moe_plan(p, cur_stream()));
 }
 
 void moe_scatter(const Tensor& xq, const Tensor& xsf, int64_t T, int64_t topk, const Tensor& pos, const Tensor& pq,
-                 const Tensor& psf) {
+                 const Tensor& psf, int64_t shared_row0) {
+  if (shared_row0 >= 0) TORCH_CHECK(shared_row0 + T <= pq.size(0), "shared segment outside the permuted buffer");
   CUDA_OK(dsv4::moe_scatter(ptr<const uint8_t>(xq), ptr<const uint8_t>(xsf), (int)T, (int)xq.size(1), (int)topk,
-                            ptr<const int>(pos), ptr<uint8_t>(pq), ptr<uint8_t>(psf), cur_stream()));
+                            ptr<const int>(pos), ptr<uint8_t>(pq), ptr<uint8_t>(psf), (int)shared_row0,
+                            cur_stream()));
 }
 
 void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const Tensor& slot, const Tensor& clen,
@@ -623,7 +656,7 @@ void ep_combine_pack(const Tensor& yperm, const Tensor& pos, const Tensor& cnt, 
 void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, int64_t topk, int64_t score_func,
                  double route_scale, const optional<Tensor>& ids, const optional<Tensor>& wts, const Tensor& xq,
                  const Tensor& xsf, int64_t e_local, int64_t cap_e, int64_t tile_rows, int64_t ret_rows,
-                 const Tensor& tables, const Tensor& err, const Tensor& pub) {
+                 const Tensor& tables, const Tensor& err, const Tensor& pub, int64_t shared_row0) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) == logits.size(1), "logits: f32 [T, E] contiguous");
@@ -658,6 +691,8 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
   p.pub = peer_sync_of(pub);
   p.world = p.pub.world;
   p.rank = p.pub.rank;
+  p.shared_row0 = (int)shared_row0;
+  TORCH_CHECK(shared_row0 < 0 || shared_row0 >= p.rows, "dispatch: the shared segment follows the expert rows");
   TORCH_CHECK(p.pub.done != nullptr && p.E == p.e_local * p.world, "dispatch: phase-0 sync and E = e_local * world");
   const c10::cuda::CUDAGuard guard(logits.device());
   CUDA_OK(dsv4::ep_dispatch(p, cur_stream()));
@@ -665,7 +700,8 @@ void ep_dispatch(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
 
 // wait: PeerSync of phase 0; tiles: int32 [max, 4]; cnt: this rank's counters [e_local]
 void ep_plan(const Tensor& wait, const Tensor& cnt, int64_t cap_e, int64_t tile_rows, int64_t m13, int64_t m2,
-             const Tensor& tiles13, const Tensor& nt13, const Tensor& tiles2, const Tensor& nt2, const Tensor& err) {
+             const Tensor& tiles13, const Tensor& nt13, const Tensor& tiles2, const Tensor& nt2, const Tensor& err,
+             int64_t shared_rows, int64_t shared_row0) {
   CHECK_CUDA(cnt);
   TORCH_CHECK(tiles13.dim() == 2 && tiles13.size(1) == 4 && tiles2.dim() == 2 && tiles2.size(1) == 4, "tiles [n, 4]");
   dsv4::EpPlanParams p{};
@@ -683,6 +719,8 @@ void ep_plan(const Tensor& wait, const Tensor& cnt, int64_t cap_e, int64_t tile_
   p.max_tiles13 = (int)tiles13.size(0);
   p.max_tiles2 = (int)tiles2.size(0);
   p.err = ptr<uint32_t>(err);
+  p.shared_rows = (int)shared_rows;
+  p.shared_row0 = (int)shared_row0;
   const c10::cuda::CUDAGuard guard(cnt.device());
   CUDA_OK(dsv4::ep_plan(p, cur_stream()));
 }
@@ -824,6 +862,7 @@ int64_t debug_bounds_attach(const Tensor& err) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "DeepSeek-V4 B200 kernels (sm_100a)";
   m.def("gemm", &gemm);
+  m.def("gemm_a2", &gemm_a2);
   m.def("gemm_smem", &gemm_smem);
   m.def("act_quant_mx", &act_quant_mx);
   m.def("act_roundtrip", &act_roundtrip);

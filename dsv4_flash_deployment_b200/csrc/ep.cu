@@ -315,6 +315,17 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDispatchParams p) {
         p.peer_meta[o][r] = (p.rank << 24) | (t * p.topk + j);
       }
     }
+    if (p.shared_row0 >= 0 && warp == p.topk % 8) {
+      // the shared expert's input: this token's row in this rank's own segment (its
+      // row weight 1 and return destination are constant, set at allocation)
+      const int r = p.shared_row0 + t;
+      uint4* dst = reinterpret_cast<uint4*>(p.peer_x[p.rank] + (size_t)r * D);
+      for (int i = lane; i < nvec; i += 32) dst[i] = s_xrow[i];
+      const int m = r & 127;
+      for (int b = lane; b < kt; b += 32)
+        *reinterpret_cast<uint32_t*>(p.peer_xsf[p.rank] + ((size_t)(r >> 7) * kt + b) * 512 + (m & 31) * 16 +
+                                     (m >> 5) * 4) = s_sfw[b];
+    }
   }
   peer_publish_grid(p.pub);
 }
@@ -372,8 +383,9 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
   __syncthreads();
   const int toff = (w > 0 ? s_wt[w - 1] : 0) + it - tl;
   const int mt13 = p.m13 / 128, mt2 = p.m2 / 128;
+  const int st = (p.shared_rows + p.tile_rows - 1) / p.tile_rows;   // shared expert row tiles
   if (e == 0) {
-    const int total = s_wt[31];
+    const int total = s_wt[31] + st;
     const bool ok = total * mt13 <= p.max_tiles13 && total * mt2 <= p.max_tiles2;
     if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 4);
     s_ok = ok;
@@ -381,7 +393,22 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
     *p.n_tiles2 = ok ? total * mt2 : 0;
   }
   __syncthreads();
-  if (!s_ok || e >= p.e_local) return;
+  if (!s_ok) return;
+  if (st > 0) {
+    // the shared expert: row tiles after the routed ones, weights from the GEMMs' second operand
+    const int t0 = s_wt[31];
+    for (int i = threadIdx.x; i < st * mt13; i += blockDim.x) {
+      const int j = i / mt13, mt = i % mt13;
+      p.tiles13[(size_t)(t0 + j) * mt13 + mt] = make_int4(kTileA2 | (mt * 128), p.shared_row0 + j * p.tile_rows,
+                                                          min(p.tile_rows, p.shared_rows - j * p.tile_rows), mt * 128);
+    }
+    for (int i = threadIdx.x; i < st * mt2; i += blockDim.x) {
+      const int j = i / mt2, mt = i % mt2;
+      p.tiles2[(size_t)(t0 + j) * mt2 + mt] = make_int4(kTileA2 | (mt * 128), p.shared_row0 + j * p.tile_rows,
+                                                        min(p.tile_rows, p.shared_rows - j * p.tile_rows), mt * 128);
+    }
+  }
+  if (e >= p.e_local) return;
   int rt = toff;
   for (int r0 = 0; r0 < c; r0 += p.tile_rows, ++rt) {
     const int valid = min(p.tile_rows, c - r0);
@@ -396,6 +423,9 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
 cudaError_t ep_plan(const EpPlanParams& p, cudaStream_t st) {
   if (p.e_local < 1 || p.e_local > 1024 || p.cap_e % 256 || p.m13 % 128 || p.m2 % 128 ||
       (p.tile_rows != 32 && p.tile_rows != 64 && p.tile_rows != 128 && p.tile_rows != 256))
+    return cudaErrorInvalidValue;
+  if (p.shared_rows < 0 || (p.shared_rows > 0 && (p.tile_rows < 128 || p.shared_row0 < p.e_local * p.cap_e ||
+                                                  p.shared_row0 % 256)))
     return cudaErrorInvalidValue;
   launch_pdl(ep_plan_kernel, 1, 1024, 0, st, p);
   return cudaGetLastError();

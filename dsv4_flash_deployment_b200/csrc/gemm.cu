@@ -74,6 +74,7 @@ DSV4_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)
 
 struct TileCoord {
   int a_row0, b_row0, b_valid, out_col0, k_begin, k_end, split, tile, n_eff;
+  bool a2;     // grouped: the tile reads the second weight operand
   int k_rot;   // the k loop starts at k_begin + k_rot and wraps (0: plain order; a
                // rotated start per tile was measured and gave no gain)
 };
@@ -116,13 +117,15 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
   const int split = w % p.splits;
   if (GROUPED) {
     const int4 r = p.tiles[tile];
-    t.a_row0 = r.x;
+    t.a2 = (r.x & kTileA2) != 0;
+    t.a_row0 = r.x & ~kTileA2;
     t.b_row0 = r.y;
     t.b_valid = r.z;
     t.out_col0 = r.w;
     t.n_eff = min(BN, n_eff_for(r.z));
 #ifdef DSV4_DEBUG_BOUNDS
-    if (r.x < 0 || r.x + BM > p.M || r.y < 0 || r.y + t.n_eff > p.N || r.z < 0) {
+    if (r.x < 0 || t.a_row0 + BM > (t.a2 ? p.M2 : p.M) || (t.a2 && p.sfa2 == nullptr) || r.y < 0 ||
+        r.y + t.n_eff > p.N || r.z < 0) {
       dbg_bad(BS_GEMM_TILE);
       return false;   // the rest of this CTA's work list is dropped
     }
@@ -131,6 +134,7 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
     const int m_tiles = p.M / BM;
     const int mt = tile % m_tiles, nt = tile / m_tiles;
     t.a_row0 = mt * BM;
+    t.a2 = false;
     t.b_row0 = nt * BN;
     t.b_valid = min(BN, p.N - t.b_row0);
     t.out_col0 = mt * BM;
@@ -147,7 +151,7 @@ DSV4_DEV bool get_work(const GemmParams& p, int w, TileCoord& t) {
 
 template <int KIND, int BN, int EPI, bool GROUPED, int BM = 128>
 __global__ void __launch_bounds__(192, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ BMaps tma_b, GemmParams p) {
+    gemm_kernel(const __grid_constant__ AMaps tma_a, const __grid_constant__ BMaps tma_b, GemmParams p) {
   using L = GemmSmem<BN, BM>;
   constexpr bool MX = KIND != KIND_BF16;
   constexpr int S = L::kStages;
@@ -189,7 +193,8 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_a.m[0]);
+    if (GROUPED && p.sfa2 != nullptr) tma_prefetch_desc(&tma_a.m[1]);
     tma_prefetch_desc(&tma_b.m[0]);
   }
   if (warp == 1) {
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int i = 0; i < pre; ++i) {
             const int kt = k_of(t, i);
             mbar_arrive_expect_tx(&full[i], tx);
-            tma_load_2d(sA + i * L::kA, &tma_a, &full[i], kt * kBkElems, t.a_row0);
+            tma_load_2d(sA + i * L::kA, &tma_a.m[0], &full[i], kt * kBkElems, t.a_row0);
             if constexpr (MX)
               for (int h = 0; h < L::kSfaChunks; ++h)
                 bulk_load(sSF + i * L::kSf + 512 * h, p.sfa + ((size_t)((t.a_row0 >> 7) + h) * p.sfa_ktiles + kt) * 512,
@@ -241,6 +246,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
+      const CUtensorMap* amap = t.a2 ? &tma_a.m[1] : &tma_a.m[0];
+      const uint8_t* sfa = t.a2 ? p.sfa2 : p.sfa;
       for (int i = 0; i < t.k_end - t.k_begin; ++i) {
         const int kt = k_of(t, i);
         const bool prefetched = first && i < pre;   // fresh stage: its A half is already in flight
@@ -248,14 +255,14 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) {
           if (!prefetched) {
             mbar_arrive_expect_tx(&full[stage], tx);
-            tma_load_2d(sA + stage * L::kA, &tma_a, &full[stage], kt * kBkElems, t.a_row0);
+            tma_load_2d(sA + stage * L::kA, amap, &full[stage], kt * kBkElems, t.a_row0);
           }
           tma_load_2d(sB + stage * L::kB, bmap, &full[stage], b_kofs + kt * kBkElems, t.b_row0);
           if constexpr (MX) {
             uint8_t* sf = sSF + stage * L::kSf;
             if (!prefetched)
               for (int h = 0; h < L::kSfaChunks; ++h)
-                bulk_load(sf + 512 * h, p.sfa + ((size_t)((t.a_row0 >> 7) + h) * p.sfa_ktiles + kt) * 512, 512,
+                bulk_load(sf + 512 * h, sfa + ((size_t)((t.a_row0 >> 7) + h) * p.sfa_ktiles + kt) * 512, 512,
                           &full[stage]);
             for (int c = 0; c < sfb_chunks; ++c)
               bulk_load(sf + 512 * (L::kSfaChunks + c),
@@ -662,7 +669,7 @@ done:
 
 // ------------------------------------------------------------------- host
 template <int KIND, int BN, int EPI, bool GROUPED, int BM = 128>
-static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
+static cudaError_t launch_one(const AMaps& ta, const BMaps& tb, const GemmParams& p, int grid,
                               cudaStream_t st) {
   using L = GemmSmem<BN, BM>;
   auto k = gemm_kernel<KIND, BN, EPI, GROUPED, BM>;
@@ -695,7 +702,7 @@ static cudaError_t launch_one(const CUtensorMap& ta, const BMaps& tb, const Gemm
 }
 
 template <int KIND, int EPI, bool GROUPED>
-static cudaError_t dispatch_bn(int bn, int bm, const CUtensorMap& ta, const BMaps& tb, const GemmParams& p, int grid,
+static cudaError_t dispatch_bn(int bn, int bm, const AMaps& ta, const BMaps& tb, const GemmParams& p, int grid,
                                cudaStream_t st) {
   if constexpr (KIND != KIND_BF16 && !GROUPED && EPI != EPI_SWIGLU) {
     if (bm == 256) {
@@ -807,7 +814,7 @@ int gemm_smem_bytes(int bn) {
   }
 }
 
-cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const CUtensorMap& ta, const BMaps& tb,
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const AMaps& ta, const BMaps& tb,
                         const GemmParams& p, int grid, cudaStream_t st) {
   if (kind == KIND_BF16) {
     if (grouped) return cudaErrorInvalidValue;

@@ -22,7 +22,8 @@ struct GemmParams {
   int sfa_ktiles;
   const uint8_t* sfb;  // B scale chunks [rows/128][sfb_ktiles][512]
   int sfb_ktiles;
-  const int4* tiles;   // grouped: {a_row0, b_row0, b_valid, out_col0}
+  const int4* tiles;   // grouped: {a_row0, b_row0, b_valid, out_col0}; a_row0 with
+                       // kTileA2 set reads the second weight operand (AMaps::m[1], sfa2)
   const int* n_tiles_ptr;
   // batched dense mode: A rows group_rows apart read B columns group_k apart
   int group_rows;
@@ -50,6 +51,10 @@ struct GemmParams {
   // 0xffffff) of rank (ret_meta[b] >> 24)'s return buffer ret_peer[rank] (row
   // stride ldo) instead of out -- the expert-parallel combine stores each expert
   // row straight into the source rank's memory over NVLink
+  // grouped: second weight operand (the shared expert riding in the routed experts'
+  // tile list): scale chunks [M2/128][sfa_ktiles][512]
+  const uint8_t* sfa2;
+  int M2;
   const int* ret_meta;
   __nv_bfloat16* const* ret_peer;
   int ret_world;       // entries of ret_peer (checked in the debug-bounds build)
@@ -61,12 +66,17 @@ struct GemmParams {
 struct BMaps {
   CUtensorMap m[4];
 };
+// Weight tensor maps: m[0] the GEMM's weights; m[1] (grouped GEMMs, optional)
+// a second weight matrix of the same K for tiles flagged with kTileA2.
+struct AMaps {
+  CUtensorMap m[2];
+};
 
 int gemm_smem_bytes(int bn);
 // bm: weight rows per tile, 128, or 256 (two 128-row MMAs sharing the token tile;
 // dense MXFP8/MXFP4 GEMMs with bf16/fp32 outputs and 64/128-token tiles only)
 int gemm_max_clusters(int kind, int epi, int bn, int splits, int bm);   // resident clusters of `splits` CTAs
-cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const CUtensorMap& ta, const BMaps& tb,
+cudaError_t gemm_launch(int kind, int epi, bool grouped, int bn, int bm, const AMaps& ta, const BMaps& tb,
                         const GemmParams& p, int grid, cudaStream_t st);
 
 // 2-D tensor map over a row-major [rows, cols] matrix of 1-byte (e4m3), 2-byte

@@ -19,6 +19,11 @@ __host__ __device__ constexpr int kv8_bytes(int d) { return d + d / 32; }
 __host__ __device__ constexpr int kv4_bytes(int d) { return d / 2 + d / 16; }
 __host__ __device__ constexpr int ik4_bytes(int d) { return d / 2 + d / 32; }
 
+// Grouped-GEMM tile records {a_row0, b_row0, valid, out_col0}: a_row0 with this
+// bit set reads the GEMM's second weight operand (the shared expert riding in
+// the routed experts' tile list).
+constexpr int kTileA2 = 1 << 30;
+
 // Block table of a paged compressed cache: entry ci of sequence slot s lives in
 // pool row table[s * ld + (ci >> shift)] << shift | (ci & (2^shift - 1)).
 // table == nullptr: contiguous per-slot cache, row s * max_c + ci.
@@ -207,11 +212,16 @@ struct MoePlanParams {
   // first seg_cnt[s] are valid (expert-parallel receive buffers); others are skipped
   const int* seg_cnt;
   int seg_cap;
+  // optional: shared_rows > 0 appends the shared expert's tiles (flagged
+  // kTileA2) for rows [shared_row0, shared_row0 + shared_rows) of the permuted
+  // buffers (token t at row shared_row0 + t, row_scale 1); tile_rows >= 128
+  int shared_rows, shared_row0;
 };
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st);
-// Copies quantized token rows (e4m3 + scale chunks) into permuted-row order.
+// Copies quantized token rows (e4m3 + scale chunks) into permuted-row order;
+// shared_row0 >= 0 also copies token t to row shared_row0 + t.
 cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
-                        uint8_t* psf, cudaStream_t st);
+                        uint8_t* psf, int shared_row0, cudaStream_t st);
 
 // ----------------------------------------------------------- indexer.cu
 struct IdxParams {
@@ -288,6 +298,8 @@ struct EpDispatchParams {
   int* const* peer_cnt;       // [world] rows claimed per local expert (zero at rest)
   uint32_t* err;
   PeerSync pub;               // phase 0
+  int shared_row0;            // >= 0: each token row is also stored at this rank's expert row
+                              // shared_row0 + t (the shared expert's input segment)
 };
 cudaError_t ep_dispatch(const EpDispatchParams& p, cudaStream_t st);
 
@@ -301,6 +313,9 @@ struct EpPlanParams {
   int* n_tiles2;
   int max_tiles13, max_tiles2;
   uint32_t* err;
+  // shared_rows > 0: the shared expert's tiles (kTileA2) for this rank's rows
+  // [shared_row0, shared_row0 + shared_rows) follow the routed tiles
+  int shared_rows, shared_row0;
 };
 cudaError_t ep_plan(const EpPlanParams& p, cudaStream_t st);
 

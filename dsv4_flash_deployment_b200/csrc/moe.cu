@@ -121,11 +121,13 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
       const int acc = base_r + ir, tacc = base_t + it;
       start[p.E_local] = acc;
       toff[p.E_local] = tacc;
-      const bool ok = acc <= p.cap_rows && tacc * mt13 <= p.max_tiles13 && tacc * mt2 <= p.max_tiles2;
+      const int st = (p.shared_rows + p.tile_rows - 1) / p.tile_rows;   // shared expert row tiles
+      const bool ok = acc <= p.cap_rows && (tacc + st) * mt13 <= p.max_tiles13 && (tacc + st) * mt2 <= p.max_tiles2 &&
+                      (p.shared_rows == 0 || acc <= p.shared_row0);
       if (!ok) report_error(p.err, ERR_CAPACITY, KID_MOE, 1);
       s_ok = ok;
-      *p.n_tiles13 = ok ? tacc * mt13 : 0;  // run nothing rather than overrun the buffers
-      *p.n_tiles2 = ok ? tacc * mt2 : 0;
+      *p.n_tiles13 = ok ? (tacc + st) * mt13 : 0;  // run nothing rather than overrun the buffers
+      *p.n_tiles2 = ok ? (tacc + st) * mt2 : 0;
     }
   }
   __syncthreads();
@@ -144,6 +146,21 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
       for (int mt = 0; mt < mt2; ++mt)
         p.tiles2[(size_t)rt * mt2 + mt] = make_int4(e * p.m2 + mt * 128, b0, valid, mt * 128);
     }
+  }
+  if (ok && p.shared_rows > 0) {
+    // the shared expert: row tiles after the routed ones, weights from the second operand
+    const int st = (p.shared_rows + p.tile_rows - 1) / p.tile_rows, t0 = toff[p.E_local];
+    for (int i = threadIdx.x; i < st * mt13; i += blockDim.x) {
+      const int j = i / mt13, mt = i % mt13;
+      p.tiles13[(size_t)(t0 + j) * mt13 + mt] = make_int4(kTileA2 | (mt * 128), p.shared_row0 + j * p.tile_rows,
+                                                          min(p.tile_rows, p.shared_rows - j * p.tile_rows), mt * 128);
+    }
+    for (int i = threadIdx.x; i < st * mt2; i += blockDim.x) {
+      const int j = i / mt2, mt = i % mt2;
+      p.tiles2[(size_t)(t0 + j) * mt2 + mt] = make_int4(kTileA2 | (mt * 128), p.shared_row0 + j * p.tile_rows,
+                                                        min(p.tile_rows, p.shared_rows - j * p.tile_rows), mt * 128);
+    }
+    for (int t = threadIdx.x; t < p.shared_rows; t += blockDim.x) p.row_scale[p.shared_row0 + t] = 1.f;
   }
   for (int sg = 0; sg < n_seg; ++sg) {
     const int c = p.seg_cnt ? min(p.seg_cnt[sg], p.seg_cap) : n;
@@ -165,33 +182,41 @@ cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
   if (p.E_local < 1 || p.E_local > 1024) return cudaErrorInvalidValue;
   if (p.tile_rows != 32 && p.tile_rows != 64 && p.tile_rows != 128 && p.tile_rows != 256) return cudaErrorInvalidValue;
   if (p.seg_cnt && (p.seg_cap < 1 || (p.T * p.topk) % p.seg_cap)) return cudaErrorInvalidValue;
+  if (p.shared_rows < 0 || (p.shared_rows > 0 && (p.tile_rows < 128 || p.shared_row0 % 256)))
+    return cudaErrorInvalidValue;
   const int smem = (3 * p.E_local + 2) * 4;
   launch_pdl(moe_plan_kernel, 1, 1024, smem, st, p);
   return cudaGetLastError();
 }
 
-// One warp per (token, slot): 16-byte copies of the e4m3 row, then scale bytes.
+// One warp per (token, slot): 16-byte copies of the e4m3 row, then scale bytes;
+// with a shared segment, the warps of slot 0 also copy the token to its row there.
 __global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int T, int D,
-                                   int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf) {
+                                   int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf, int shared_row0) {
   pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= T * topk) return;
-  const int row = pos[w];
-  if (row < 0) return;
   const int t = w / topk;
   const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)t * D);
-  uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
-  for (int i = lane; i < D / 16; i += 32) dst[i] = src[i];
   const int kt = D / 128;
-  for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = xsf[sf_chunk_offset(t, b, kt)];
+  const int rows[2] = {pos[w], (shared_row0 >= 0 && w % topk == 0) ? shared_row0 + t : -1};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int row = rows[c];
+    if (row < 0) continue;
+    uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
+    for (int i = lane; i < D / 16; i += 32) dst[i] = src[i];
+    for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = xsf[sf_chunk_offset(t, b, kt)];
+  }
 }
 
 cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
-                        uint8_t* psf, cudaStream_t st) {
+                        uint8_t* psf, int shared_row0, cudaStream_t st) {
   const long long warps = (long long)T * topk;
   if (warps == 0) return cudaSuccess;
-  launch_pdl(moe_scatter_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, xq, xsf, T, D, topk, pos, pq, psf);
+  launch_pdl(moe_scatter_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, xq, xsf, T, D, topk, pos, pq, psf,
+             shared_row0);
   return cudaGetLastError();
 }
 

@@ -111,9 +111,9 @@ extern "C" __attribute__((visibility("default"))) int dsv4_gemm_mx8_noalloc(
   ScratchArea* scratch = nullptr;
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return (int)e;
-  CUtensorMap ta;
+  dsv4::AMaps ta{};
   dsv4::BMaps tb;
-  if (!dsv4::make_tma_2d(&ta, a, dsv4::TMA_U8, (uint64_t)m, (uint64_t)k, 128) ||
+  if (!dsv4::make_tma_2d(&ta.m[0], a, dsv4::TMA_U8, (uint64_t)m, (uint64_t)k, 128) ||
       !dsv4::make_tma_2d(&tb.m[0], b, dsv4::TMA_U8, (uint64_t)b_rows, (uint64_t)k, (uint32_t)bn)) {
     std::fprintf(stderr, "dsv4_gemm_mx8_noalloc: tensor map encoding failed (alignment of a or b?)\n");
     return DSV4_NOALLOC_BAD_ARG;

@@ -263,19 +263,33 @@ class DSV4Model:
         # expert intermediate width on this rank (a tensor-parallel expert split keeps 1/N)
         I = self.tp.inter_local(cfg.moe_inter_dim) if self.tp is not None else cfg.moe_inter_dim
         self.inter_local = I
+        si = cfg.n_shared_experts * cfg.moe_inter_dim     # the shared expert is never split
+        # the shared expert rides in the routed experts' grouped GEMMs (its tiles read a
+        # second weight operand) when it has their format and intermediate width: its
+        # input rows follow the routed rows of the permuted buffers (shared_row0), its
+        # output rows are read there by the next mHC boundary.  Not with tensor
+        # parallelism, the p2p / NCCL exchanges or token tiles under 128 rows.
+        ep_ok = self.ep is None or self.ep.transport == "fused"
+        self.merge_shared = (os.environ.get("DSV4_MERGE_SHARED", "1") != "0" and cfg.expert_format == "mxfp8"
+                             and si == I and self.tile_rows >= 128 and self.tp is None and ep_ok)
+        self.shared_row0 = ceil_to(self.cap, 256)
+        rows_all = self.shared_row0 + ceil_to(T, 256) if self.merge_shared else self.cap
+        self.perm_rows = rows_all
+        if self.merge_shared:
+            tiles_rows_max += -(-T // self.tile_rows)
         self.tiles13 = e(tiles_rows_max * (2 * I // 128), 4, dt=i32)
         self.tiles2 = e(tiles_rows_max * (D // 128), 4, dt=i32)
         self.nt13, self.nt2 = z(1, dt=i32), z(1, dt=i32)
-        self.xperm = e(self.cap, D, dt=u8)
-        self.xperm_sf = z(self.cap // 128, D // 128, 512, dt=u8)
-        self.hperm = e(self.cap, I, dt=u8)
-        self.hperm_sf = z(self.cap // 128, I // 128, 512, dt=u8)
-        self.yperm = e(self.cap, D)
-        self.row_scale = z(self.cap, dt=f32)
-        si = cfg.n_shared_experts * cfg.moe_inter_dim     # the shared expert is never split
+        self.xperm = e(rows_all, D, dt=u8)
+        self.xperm_sf = z(rows_all // 128, D // 128, 512, dt=u8)
+        self.hperm = e(rows_all, I, dt=u8)
+        self.hperm_sf = z(rows_all // 128, I // 128, 512, dt=u8)
+        self.yperm = e(rows_all, D)
+        self.row_scale = z(rows_all, dt=f32)
         self.hs = e(Tp, si, dt=u8)
         self.hs_sf = z(Tp // 128, si // 128, 512, dt=u8)
         self.shared_out = e(T, D)
+        self.shared_y = self.shared_out   # the shared expert's rows for the next mHC boundary
         # head
         self.u_sample = e(self.max_sample, D)
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
@@ -482,7 +496,7 @@ class DSV4Model:
                 # only then this block's mixes and collapse (reference.py:925-931)
                 if moe_state is not None:
                     yp, ps, kk, td = moe_state
-                    self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, tp=td)
+                    self._hc(T, Y=self.shared_y, yperm=yp, pos=ps, topk=kk, prev=self.mixF, tp=td)
                 with self._t("engram"):
                     eng.apply(self, lid, T)
                 self._hc(T, prev=None, mixes=L.hc_attn, cw=cw if moe_state is None else self.mixF,
@@ -492,7 +506,7 @@ class DSV4Model:
                          uq=self.uq, usf=self.usf, tap=tap)
             else:
                 yp, ps, kk, td = moe_state
-                self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
+                self._hc(T, Y=self.shared_y, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=L.hc_attn,
                          cw=self.mixF, norm=L.attn_norm, mix_out=self.mixA, u=self.u, uq=self.uq, usf=self.usf,
                          tap=tap, tp=td)
             if trace is not None:
@@ -506,7 +520,7 @@ class DSV4Model:
             moe_state = self._moe(L, T)
         # final collapse + norm on all tokens, then head on the sampled rows
         yp, ps, kk, td = moe_state
-        self._hc(T, Y=self.shared_out, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=None, cw=self.mixF,
+        self._hc(T, Y=self.shared_y, yperm=yp, pos=ps, topk=kk, prev=self.mixF, mixes=None, cw=self.mixF,
                  norm=self.norm_w, u=self.u, tp=td)
         S = len(m.sample_rows)
         if S == 0:
@@ -748,14 +762,20 @@ class DSV4Model:
         e_begin, e_local = (0, E) if self.tp is None else self.tp.expert_range(E)
         pctx = self._t("moe_plan_scatter")
         pctx.__enter__()
+        merged = self.merge_shared and L.shared_w13 is not None
+        s_rows, s_row0 = (T, self.shared_row0) if merged else (0, 0)
         ext.moe_plan(T, k, e_local, e_begin, ids, wts, self.counts, self.seg, rank, self.tile_rows, 2 * I, D,
                      self.tiles13, self.nt13, self.tiles2, self.nt2, self.cap, pos, self.row_scale, self.err,
-                     None, 0)
-        ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf)
+                     None, 0, s_rows, s_row0)
+        ext.moe_scatter(self.uq, self.usf, T, k, pos, self.xperm, self.xperm_sf, s_row0 if merged else -1)
         pctx.__exit__(None, None, None)
-        self._grouped(L, k)
-        with self._t("shared_expert"):
-            self._shared_expert(L, T)
+        self._grouped(L, k, shared=merged)
+        if merged:
+            self.shared_y = self.yperm[self.shared_row0:self.shared_row0 + T]
+        else:
+            with self._t("shared_expert"):
+                self._shared_expert(L, T)
+            self.shared_y = self.shared_out
         if self.tp is not None:
             # the next mHC boundary reads every pair's row from the rank owning its expert
             # (expert ownership) or sums every rank's partial row of each pair (expert split)
@@ -768,22 +788,26 @@ class DSV4Model:
                    swiglu_limit=cfg.swiglu_limit)
         self._gemm(self.hs, self.hs_sf, T, L.shared_w2, self.shared_out)
 
-    def _grouped(self, L: LayerW, k: int):
+    def _grouped(self, L: LayerW, k: int, shared: bool = False):
+        """Grouped expert GEMMs over the permuted rows; ``shared``: the tile lists also
+        hold the shared expert's tiles (second weight operand)."""
         cfg, ext = self.cfg, self.ext
         I, D = L.experts.inter, cfg.dim
         ex = L.experts
         bn = self.tile_rows
+        rows = self.perm_rows
+        a13 = (L.shared_w13.q, L.shared_w13.sf) if shared else (None, None)
+        a2 = (L.shared_w2.q, L.shared_w2.sf) if shared else (None, None)
         c13 = self._t("grouped_w13")
         c13.__enter__()
-        ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
-                 self.cap, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                 cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None, None, None)
+        ext.gemm_a2(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
+                    rows, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
+                    cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None, None, None, *a13)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
         split = self.tp is not None and self.tp.moe == "tp"   # f32 partial rows, summed over ranks
-        ext.gemm(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf, self.yperm,
-                 ex.w2.q.shape[0],
-                 self.cap, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D, None, None, self.err, 0, 1,
-                 self.tp.sync(1) if self.tp is not None else None, None, None)
+        ext.gemm_a2(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf,
+                    self.yperm, ex.w2.q.shape[0], rows, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D,
+                    None, None, self.err, 0, 1, self.tp.sync(1) if self.tp is not None else None, None, None, *a2)
         c2.__exit__(None, None, None)

@@ -134,12 +134,17 @@ class EPGroup:
         b["sync1"] = torch.tensor([b["peer_sig"].data_ptr(), 0, done + 4, ep + 4], dtype=torch.int64)
 
     # ------------------------------------------------------------ fused path
-    def _alloc_fused(self, T: int, k: int, D: int, I: int, e_local: int, tile_rows: int):
+    def _alloc_fused(self, T: int, k: int, D: int, I: int, e_local: int, tile_rows: int, shared: bool = False):
         """One symmetric allocation per rank: [expert rows e4m3 | their scale chunks |
         row weights f32 | row origins int32 | per-expert counters | return rows bf16
         (T*k pairs) | signal words]; expert e owns rows [e*cap_e, (e+1)*cap_e) with
         cap_e = every token of every rank (no routing can overflow it).  Local:
-        the SwiGLU intermediate in the same row layout and the tile lists."""
+        the SwiGLU intermediate in the same row layout and the tile lists.
+
+        ``shared``: the shared expert rides in the grouped GEMMs.  Its input segment
+        (this rank's T tokens) follows the expert rows at ``shared_row0`` (row weight
+        1, return destination row T*k + t of this rank's own return buffer, both
+        constant) and its output rows follow the T*k pair rows of the return buffer."""
         import torch.distributed._symmetric_memory as symm_mem
 
         W = self.world
@@ -148,8 +153,12 @@ class EPGroup:
         pairs = max(1, T) * W
         cap_e = ceil_to(pairs if tile_rows >= 128 else -(-pairs // tile_rows) * 128, 256)
         rows = e_local * cap_e
+        srows = ceil_to(max(1, T), 256) if shared else 0
+        xrows = rows + srows
+        ret0 = max(1, T * k)                       # first shared output row of the return buffer
         kt = D // 128
-        sizes = [rows * D, (rows // 128) * kt * 512, rows * 4, rows * 4, e_local * 4, max(1, T * k) * D * 2, 2 * W * 4]
+        sizes = [xrows * D, (xrows // 128) * kt * 512, xrows * 4, xrows * 4, e_local * 4, (ret0 + srows) * D * 2,
+                 2 * W * 4]
         offs, cur = [], 0
         for sz in sizes:
             offs.append(cur)
@@ -164,16 +173,18 @@ class EPGroup:
         view = lambda i: buf[offs[i]:offs[i] + sizes[i]]
         e = lambda *s_, dt: torch.empty(*s_, dtype=dt, device=self.dev)
         tiles_max = (T * W * k) // tile_rows + e_local + 1   # sum over experts of ceil(rows / tile_rows)
+        tiles_max += srows // tile_rows
         b = dict(
-            cap_e=cap_e, rows=rows, k=k, tile_rows=tile_rows, symm=buf, symm_handle=hdl,
-            x=view(0).view(rows, D), xsf=view(1), rscale=view(2).view(torch.float32),
+            cap_e=cap_e, rows=rows, xrows=xrows, k=k, tile_rows=tile_rows, symm=buf, symm_handle=hdl,
+            shared=shared, shared_row0=rows if shared else -1, ret0=ret0,
+            x=view(0).view(xrows, D), xsf=view(1), rscale=view(2).view(torch.float32),
             meta=view(3).view(torch.int32), cnt=view(4).view(torch.int32),
-            back=view(5).view(torch.bfloat16).view(max(1, T * k), D), sig=view(6).view(torch.int32),
+            back=view(5).view(torch.bfloat16).view(ret0 + srows, D), sig=view(6).view(torch.int32),
             tables=[table(i) for i in range(5)], peer_back=table(5), peer_sig=table(6),
             done=torch.zeros(2, dtype=torch.int32, device=self.dev),
             epoch=torch.zeros(2, dtype=torch.int32, device=self.dev),
-            h=e(rows, I, dt=torch.uint8), hsf=torch.zeros((rows // 128) * (I // 128) * 512, dtype=torch.uint8,
-                                                          device=self.dev),
+            h=e(xrows, I, dt=torch.uint8), hsf=torch.zeros((xrows // 128) * (I // 128) * 512, dtype=torch.uint8,
+                                                           device=self.dev),
             tiles13=e(tiles_max * (2 * I // 128), 4, dt=torch.int32),
             tiles2=e(tiles_max * (D // 128), 4, dt=torch.int32),
             nt13=torch.zeros(1, dtype=torch.int32, device=self.dev),
@@ -181,6 +192,12 @@ class EPGroup:
             # the return buffer holds pair (t, slot) at row t * k + slot: the combine's positions
             pos_id=torch.arange(max(1, T * k), dtype=torch.int32, device=self.dev).view(-1, k) if T * k else None,
         )
+        if shared:
+            # constant per shared row: weight 1, returned to this rank's row ret0 + t
+            b["rscale"][rows:xrows].fill_(1.0)
+            b["meta"][rows:xrows].copy_((self.rank << 24) + ret0 + torch.arange(srows, dtype=torch.int32,
+                                                                               device=self.dev))
+            torch.cuda.synchronize(self.dev)
         b["tab_cpu"] = torch.tensor([t.data_ptr() for t in b["tables"]], dtype=torch.int64)
         sync = lambda ph: torch.tensor([b["peer_sig"].data_ptr(), b["sig"].data_ptr(), b["done"].data_ptr() + 4 * ph,
                                         b["epoch"].data_ptr() + 4 * ph, ph, W, self.rank], dtype=torch.int64)
@@ -199,36 +216,43 @@ class EPGroup:
         E = cfg.n_experts_for(L.layer_id)
         _, e_local = self.expert_range(E)
         if getattr(self, "_fb", None) is None:
-            self._alloc_fused(model.max_tokens, k, D, I, e_local, model.tile_rows)
+            self._alloc_fused(model.max_tokens, k, D, I, e_local, model.tile_rows, shared=model.merge_shared)
         b = self._fb
         if b["k"] != k:
             raise NotImplementedError("fused expert parallelism with several routing widths")
+        merged = b["shared"] and L.shared_w13 is not None
         ids, wts, _, _ = model.route[k]
         with model._t("ep_dispatch"):
             ext.ep_dispatch(logits[:T], T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale,
-                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], b["back"].shape[0],
-                            b["tab_cpu"], model.err, b["sync0"])
-        if self.shared_first:
+                            ids, wts, model.uq, model.usf, e_local, b["cap_e"], b["tile_rows"], b["ret0"],
+                            b["tab_cpu"], model.err, b["sync0"], b["shared_row0"] if merged else -1)
+        if self.shared_first and not merged:
             # the shared expert runs while the peers' dispatched rows are in flight
             with model._t("shared_expert"):
                 model._shared_expert(L, T)
         with model._t("ep_plan"):
             ext.ep_plan(b["sync0"], b["cnt"], b["cap_e"], b["tile_rows"], 2 * I, D, b["tiles13"], b["nt13"],
-                        b["tiles2"], b["nt2"], model.err)
+                        b["tiles2"], b["nt2"], model.err, T if merged else 0, b["shared_row0"] if merged else 0)
         ex = L.experts
+        a13 = (L.shared_w13.q, L.shared_w13.sf) if merged else (None, None)
+        a2 = (L.shared_w2.q, L.shared_w2.sf) if merged else (None, None)
         with model._t("grouped_w13"):
-            ext.gemm(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, b["x"], b["xsf"], None, ex.w13.q.shape[0],
-                     b["rows"], D, b["tile_rows"], 1, b["tiles13"], b["nt13"], b["rscale"], b["h"], b["hsf"],
-                     cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None)
+            ext.gemm_a2(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, b["x"], b["xsf"], None, ex.w13.q.shape[0],
+                        b["xrows"], D, b["tile_rows"], 1, b["tiles13"], b["nt13"], b["rscale"], b["h"], b["hsf"],
+                        cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None, *a13)
         with model._t("grouped_w2"):
-            ext.gemm(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["rows"], I), b["hsf"], None,
-                     ex.w2.q.shape[0],
-                     b["rows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None, 0.0, D, D, None, None,
-                     model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"])
-        if not self.shared_first:
-            # the shared expert runs while the expert rows travel back
-            with model._t("shared_expert"):
-                model._shared_expert(L, T)
+            ext.gemm_a2(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["xrows"], I), b["hsf"], None,
+                        ex.w2.q.shape[0], b["xrows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None,
+                        0.0, D, D, None, None, model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"], *a2)
+        if merged:
+            # the shared expert's rows came back with the routed ones (rows ret0 + t)
+            model.shared_y = b["back"][b["ret0"]:b["ret0"] + T]
+        else:
+            if not self.shared_first:
+                # the shared expert runs while the expert rows travel back
+                with model._t("shared_expert"):
+                    model._shared_expert(L, T)
+            model.shared_y = model.shared_out
         return b["back"], b["pos_id"], k, b["hc_desc"]
 
     def release(self) -> None:
@@ -266,7 +290,7 @@ class EPGroup:
             # only the valid prefix of each peer's segment (rcnt) is visited
             ext.moe_plan(n, 1, e_local, 0, b["ids"], b["wts"], model.counts, model.seg, b["rank"], model.tile_rows,
                          2 * I, D, model.tiles13, model.nt13, model.tiles2, model.nt2, model.cap, b["pos"],
-                         model.row_scale, model.err, b["rcnt"], cap)
+                         model.row_scale, model.err, b["rcnt"], cap, 0, 0)
             ext.ep_unpack_rows(b["recv"], b["rcnt"], self.world, cap, rec, D, b["pos"], model.xperm, model.xperm_sf)
         model._grouped(L, 1)
         with model._t("ep_combine"):

@@ -179,14 +179,14 @@ class DSparkDrafter:
                       usf=m.usf)
             else:
                 yp, ps, kk, _ = moe_state
-                m._hc(T, Y=m.shared_out, yperm=yp, pos=ps, topk=kk, prev=m.mixF, mixes=L.hc_attn, cw=m.mixF,
+                m._hc(T, Y=m.shared_y, yperm=yp, pos=ps, topk=kk, prev=m.mixF, mixes=L.hc_attn, cw=m.mixF,
                       norm=L.attn_norm, mix_out=m.mixA, u=m.u, uq=m.uq, usf=m.usf)
             m._attention(L, meta, ring=self.rings[k], win_len=win)
             m._hc(T, Y=m.attn_out, prev=m.mixA, mixes=L.hc_ffn, cw=m.mixA, norm=L.ffn_norm, mix_out=m.mixF, u=m.u,
                   uq=m.uq, usf=m.usf)
             moe_state = m._moe(L, T)
         yp, ps, kk, _ = moe_state
-        m._hc(T, Y=m.shared_out, yperm=yp, pos=ps, topk=kk, prev=m.mixF, mixes=None, cw=m.mixF,
+        m._hc(T, Y=m.shared_y, yperm=yp, pos=ps, topk=kk, prev=m.mixF, mixes=None, cw=m.mixF,
               norm=self.final_norm, u=m.u)
         m._gemm_bf16(m.u[:T], m.head, m.logits[:T], T, f32_out=True)
         V = m.vocab

@@ -145,3 +145,28 @@ def test_small_v41_engram_prefill_and_decode():
     worst, mean, agree = _run(cfg, seqs, prefill_lens=[20, 9])
     assert mean >= 0.995 and worst >= 0.97, (mean, worst)
     assert agree >= 0.8, agree
+
+
+def test_shared_expert_in_grouped_gemms_matches_separate(monkeypatch):
+    """The shared expert riding in the routed experts' grouped GEMMs (second weight
+    operand, rows after the routed ones) against the separate dense shared-expert
+    GEMMs: same logits up to fp32 summation order (split-K vs one pass)."""
+    torch.manual_seed(4)
+    cfg = small_v4()
+    w = make_random_weights(cfg, seed=3)
+    seq = torch.randint(0, cfg.vocab_size, (40,)).tolist()
+    out = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("DSV4_MERGE_SHARED", flag)
+        model = build_model(cfg, "cuda", max_tokens=64, n_slots=2, max_seq_len=64, weights=w)
+        assert model.merge_shared == (flag == "1")
+        rows = []
+        for meta in (StepMeta(cfg, [SeqChunk(0, 0, seq[:33], True)]), StepMeta(cfg, [SeqChunk(0, 33, seq[33:34], True)])):
+            model.upload(meta)
+            model.forward(meta)
+            torch.cuda.synchronize()
+            ErrorWord.check("cuda")
+            rows.append(model.logits[0, : cfg.vocab_size].float().cpu())
+        out[flag] = torch.stack(rows)
+    c = _cos(out["1"], out["0"])
+    assert float(c.min()) > 0.9999, c
