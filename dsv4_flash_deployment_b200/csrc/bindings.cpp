@@ -127,12 +127,16 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
   dsv4::BMaps tb;
   TORCH_CHECK(dsv4::make_tma_2d(&ta.m[0], A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
               "TMA(A) encode failed");
+  // MXFP4 weights (A packed [rows, K/2]) may take an MXFP8 second operand ([rows, K])
+  const bool a2_e4m3 = A2 && e2m1 && A2->size(1) == K;
   if (A2) {
     TORCH_CHECK(grouped && bm == 128 && A2->is_cuda() && A2->is_contiguous() && A2->dim() == 2 && A2->size(0) % 128 == 0,
                 "A2: grouped GEMMs only, [rows (multiple of 128), K] contiguous");
-    TORCH_CHECK(A2->scalar_type() == A.scalar_type() && A2->size(1) == A.size(1), "A2 must match A's type and K");
+    TORCH_CHECK(A2->scalar_type() == A.scalar_type() && (A2->size(1) == A.size(1) || a2_e4m3),
+                "A2 must match A's type and K (or be MXFP8 beside MXFP4 weights)");
     TORCH_CHECK(kind == dsv4::KIND_BF16 || A2_sf.has_value(), "block-scaled A2 needs A2_sf");
-    TORCH_CHECK(dsv4::make_tma_2d(&ta.m[1], A2->data_ptr(), tma_elem_of(*A2, e2m1), A2->size(0), K, (uint32_t)bm),
+    TORCH_CHECK(dsv4::make_tma_2d(&ta.m[1], A2->data_ptr(), tma_elem_of(*A2, e2m1 && !a2_e4m3), A2->size(0), K,
+                                  (uint32_t)bm),
                 "TMA(A2) encode failed");
   }
   if (grouped) {
@@ -161,6 +165,7 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
   p.sfa_ktiles = (int)(K / 128);
   p.sfa2 = A2 ? (A2_sf ? u8ptr(A2_sf) : reinterpret_cast<const uint8_t*>(A2->data_ptr())) : nullptr;
   p.M2 = A2 ? (int)A2->size(0) : 0;
+  p.a2_e4m3 = a2_e4m3 ? 1 : 0;
   p.sfb = u8ptr(B_sf);
   p.sfb_ktiles = (int)(b_cols / 128);
   if (groups > 1) {

@@ -243,7 +243,8 @@ __global__ void __launch_bounds__(192, 1)
     bool first = true;
     for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x, first = false) {
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-      const uint32_t tx = kATx + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
+      const uint32_t txa = (KIND == KIND_MX4A && t.a2 && p.a2_e4m3) ? (uint32_t)L::kA : kATx;
+      const uint32_t tx = txa + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
       const CUtensorMap* bmap = GROUPED ? &tma_b.m[bmap_index(t.n_eff)] : &tma_b.m[0];
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
       const CUtensorMap* amap = t.a2 ? &tma_a.m[1] : &tma_a.m[0];
@@ -285,7 +286,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t acc_phase = 0;
     TileCoord t;
     for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x) {
-      const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, KIND == KIND_MX4A ? 5 : 0, 0) : idesc_bf16(128, t.n_eff);
+      const uint32_t afmt = (KIND == KIND_MX4A && !(t.a2 && p.a2_e4m3)) ? 5 : 0;   // e2m1 or e4m3 weights
+      const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, afmt, 0) : idesc_bf16(128, t.n_eff);
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
       const uint32_t d_tmem = tmem + acc * L::kAccCols;
       if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;

@@ -55,6 +55,9 @@ struct GemmParams {
   // tile list): scale chunks [M2/128][sfa_ktiles][512]
   const uint8_t* sfa2;
   int M2;
+  int a2_e4m3;         // KIND_MX4A: the second operand is e4m3 (MXFP8), not e2m1 -- both sit
+                       // one byte per element in shared memory; only the TMA byte count and
+                       // the A format of the instruction descriptor differ
   const int* ret_meta;
   __nv_bfloat16* const* ret_peer;
   int ret_world;       // entries of ret_peer (checked in the debug-bounds build)

@@ -264,14 +264,15 @@ class DSV4Model:
         I = self.tp.inter_local(cfg.moe_inter_dim) if self.tp is not None else cfg.moe_inter_dim
         self.inter_local = I
         si = cfg.n_shared_experts * cfg.moe_inter_dim     # the shared expert is never split
-        # the shared expert rides in the routed experts' grouped GEMMs (its tiles read a
-        # second weight operand) when it has their format and intermediate width: its
-        # input rows follow the routed rows of the permuted buffers (shared_row0), its
-        # output rows are read there by the next mHC boundary.  Not with tensor
-        # parallelism, the p2p / NCCL exchanges or token tiles under 128 rows.
+        # the shared expert (MXFP8) rides in the routed experts' grouped GEMMs (its tiles
+        # read a second weight operand, beside MXFP8 or MXFP4 experts) when it has their
+        # intermediate width: its input rows follow the routed rows of the permuted
+        # buffers (shared_row0), its output rows are read there by the next mHC
+        # boundary.  Not with tensor parallelism, the p2p / NCCL exchanges or token
+        # tiles under 128 rows.
         ep_ok = self.ep is None or self.ep.transport == "fused"
-        self.merge_shared = (os.environ.get("DSV4_MERGE_SHARED", "1") != "0" and cfg.expert_format == "mxfp8"
-                             and si == I and self.tile_rows >= 128 and self.tp is None and ep_ok)
+        self.merge_shared = (os.environ.get("DSV4_MERGE_SHARED", "1") != "0" and si == I and self.tile_rows >= 128
+                             and self.tp is None and ep_ok)
         self.shared_row0 = ceil_to(self.cap, 256)
         rows_all = self.shared_row0 + ceil_to(T, 256) if self.merge_shared else self.cap
         self.perm_rows = rows_all

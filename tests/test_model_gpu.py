@@ -147,12 +147,14 @@ def test_small_v41_engram_prefill_and_decode():
     assert agree >= 0.8, agree
 
 
-def test_shared_expert_in_grouped_gemms_matches_separate(monkeypatch):
+@pytest.mark.parametrize("family", ["v4", "v41"])
+def test_shared_expert_in_grouped_gemms_matches_separate(monkeypatch, family):
     """The shared expert riding in the routed experts' grouped GEMMs (second weight
-    operand, rows after the routed ones) against the separate dense shared-expert
-    GEMMs: same logits up to fp32 summation order (split-K vs one pass)."""
+    operand, rows after the routed ones; V4.1: MXFP8 shared tiles beside MXFP4
+    experts) against the separate dense shared-expert GEMMs: same logits up to
+    fp32 summation order (split-K vs one pass)."""
     torch.manual_seed(4)
-    cfg = small_v4()
+    cfg = small_v4() if family == "v4" else small_v41()
     w = make_random_weights(cfg, seed=3)
     seq = torch.randint(0, cfg.vocab_size, (40,)).tolist()
     out = {}
