@@ -4,9 +4,14 @@ The reference's MoE microbench configuration: hidden 4096, 256 routed SwiGLU
 experts (intermediate 2048), top-8 sigmoid gating with router logits ~N(0, 1),
 one shared expert, bf16 activations quantized on the fly to MXFP8 (e4m3 +
 ue8m0 per 32), MXFP8 expert weights; tokens per rank T in {1, 16, 128, 512,
-4096}.  One MoE layer of this engine is timed per T, for both expert
-transports:
+4096}.  One MoE layer of this engine is timed per T, for each expert
+transport:
 
+* ``fused`` (the default transport) router top-k fused with the dispatch that
+  stores each routed row straight into its owner's expert rows over NVLink,
+  the plan, grouped W13 / W2 GEMMs (the shared expert's tiles in the same
+  launches) whose W2 epilogue stores each expert row into the source's return
+  buffer, and the weighted top-k reduction in the next mHC boundary kernel;
 * ``p2p``  router GEMM + top-k, the packing kernel storing (token, expert)
   records straight into each owner's receive buffer over NVLink, plan + unpack,
   grouped W13 (SwiGLU + requant epilogue) / W2 GEMMs, the combine kernel storing
@@ -50,7 +55,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,128,512,4096")
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--transports", default="p2p,nccl")
+    ap.add_argument("--transports", default="fused,p2p,nccl")
     a = ap.parse_args(argv)
 
     from ..engine.builder import build_model
