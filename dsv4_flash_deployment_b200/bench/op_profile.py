@@ -38,7 +38,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=None, help="override n_layers (smaller smoke runs)")
     ap.add_argument("--experts", type=int, default=None, help="override routed experts (small profiling cases)")
     ap.add_argument("--topk", type=int, default=None)
-    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl", "fused"])
+    ap.add_argument("--ep-transport", default="fused", choices=["p2p", "nccl", "fused"])
     ap.add_argument("--decode-only", action="store_true", help="C decoding sequences per rank, no prefill chunk")
     ap.add_argument("--context", type=int, default=1024, help="decode positions start here (span of 1024)")
     ap.add_argument("--device-trace", action="store_true",
