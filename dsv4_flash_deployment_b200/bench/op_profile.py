@@ -33,6 +33,9 @@ from ..models.model import SeqChunk, StepMeta
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--family", default="v4", choices=["v4", "v41"],
+                    help="v4: the V4-Flash-shaped model; v41: the V4.1-Flash architecture (Engram, MXFP4 experts)")
+    ap.add_argument("--engram-rows", type=int, default=4_000_000, help="v41: rows per Engram table")
     ap.add_argument("--concurrency", type=int, default=512)
     ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--layers", type=int, default=None, help="override n_layers (smaller smoke runs)")
@@ -79,7 +82,11 @@ def main() -> None:
         kw["n_routed_experts"] = a.experts
     if a.topk:
         kw["n_activated_experts"] = a.topk
-    cfg = v4_flash_config(**kw)
+    if a.family == "v41":
+        from ..config import v41_flash_config
+        cfg = v41_flash_config(engram_num_embeddings=(a.engram_rows, a.engram_rows), n_mtp_layers=0, **kw)
+    else:
+        cfg = v4_flash_config(**kw)
     dev = torch.device("cuda", local)
     n_dec = a.concurrency // per_rank - (0 if a.decode_only else 1)
     chunk = 0 if a.decode_only else a.chunk // per_rank
