@@ -516,6 +516,32 @@ void router_topk(const Tensor& logits, int64_t T, const optional<Tensor>& bias, 
                             (int)score_func, (float)route_scale, ptr<int>(ids), ptr<float>(wts), cur_stream()));
 }
 
+void router_small(const Tensor& u, const Tensor& w, int64_t T, const Tensor& logits, const optional<Tensor>& bias,
+                  int64_t topk, int64_t score_func, double route_scale, const Tensor& ids, const Tensor& wts,
+                  const Tensor& counter) {
+  TORCH_CHECK(u.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && u.is_contiguous() &&
+                  w.is_contiguous() && u.size(1) == w.size(1), "router_small: bf16 u [T, D] and gate [E, D]");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.size(1) == w.size(0) && logits.stride(0) == w.size(0),
+              "router_small: f32 logits [T, E]");
+  TORCH_CHECK(counter.scalar_type() == at::kInt && counter.is_cuda(), "router_small: int32 counter");
+  dsv4::RouterSmallParams p{};
+  p.u = ptr<const bf16>(u);
+  p.w = ptr<const bf16>(w);
+  p.T = (int)T;
+  p.D = (int)u.size(1);
+  p.E = (int)w.size(0);
+  p.logits = logits.data_ptr<float>();
+  p.bias = ptr<const float>(bias);
+  p.topk = (int)topk;
+  p.score_func = (int)score_func;
+  p.route_scale = (float)route_scale;
+  p.ids = ptr<int>(ids);
+  p.wts = ptr<float>(wts);
+  p.counter = counter.data_ptr<int>();
+  const c10::cuda::CUDAGuard guard(u.device());
+  CUDA_OK(dsv4::router_small(p, cur_stream()));
+}
+
 void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const Tensor& ids, const Tensor& wts,
               const Tensor& counts, const Tensor& seg_start, const Tensor& rank, int64_t tile_rows, int64_t m13,
               int64_t m2, const Tensor& tiles13, const Tensor& n_tiles13, const Tensor& tiles2,
@@ -889,6 +915,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compress_pool", &compress_pool);
   m.def("ring_update", &ring_update);
   m.def("router_topk", &router_topk);
+  m.def("router_small", &router_small);
   m.def("moe_plan", &moe_plan);
   m.def("moe_scatter", &moe_scatter);
   m.def("indexer_topk", &indexer_topk);

@@ -188,6 +188,22 @@ cudaError_t ring_update_rec(uint8_t* ring, int depth, int width, const uint8_t* 
                             const int* pos, const int* last_pos, cudaStream_t st);
 
 // ------------------------------------------------------------ moe.cu
+// Router GEMV + top-k in one launch for T <= kRouterSmallMaxT tokens; counter: one
+// zeroed device int (the kernel leaves it zero).
+constexpr int kRouterSmallMaxT = 4;
+struct RouterSmallParams {
+  const __nv_bfloat16* u;           // [T, D] normalized activations
+  const __nv_bfloat16* w;           // [E, D] gate weights
+  int T, D, E;
+  float* logits;                    // [T, E] out
+  const float* bias;
+  int topk, score_func;
+  float route_scale;
+  int* ids;
+  float* wts;
+  int* counter;
+};
+cudaError_t router_small(const RouterSmallParams& p, cudaStream_t st);
 cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,
                         float route_scale, int* ids, float* wts, cudaStream_t st);
 struct MoePlanParams {

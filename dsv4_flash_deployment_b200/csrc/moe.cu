@@ -3,6 +3,7 @@
 // router_topk: scores = sqrt(softplus(logit)) (V4 family) or sigmoid(logit);
 //   experts = top-k of (score + bias) (ties -> lower expert id); weights =
 //   score / sum(score) * route_scale (reference.py:355-382).  One warp per token.
+// router_small: the gate GEMV and the top-k in one launch for decode-sized T.
 // moe_plan: per-expert counts -> 128-row-aligned segments of the permuted
 //   activation buffer (tiles under 128 rows get a 128-row slot each, seg_rows)
 //   activation buffer -> GEMM tile lists for W13 and W2 (device-built, so the
@@ -31,6 +32,80 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     ids[(size_t)warp * topk + lane] = my_id;
     wts[(size_t)warp * topk + lane] = my_w;
   }
+}
+
+// Small-T router (decode steps): logits = u . gate_w^T on CUDA cores (fp32
+// accumulation of the bf16 products), one warp per expert for every token, 8
+// experts per CTA; the last CTA to finish (device counter; nothing waits) copies
+// each token's logits to shared memory with L2 loads and runs its top-k
+// (route_token), then re-arms the counter.  Replaces a split-K tensor-core GEMM
+// plus a separate top-k launch where the gate matrix is a few MB.
+template <int kMaxPer>
+__global__ void __launch_bounds__(256) router_small_kernel(RouterSmallParams p) {
+  pdl_entry();
+  __shared__ float s_log[kRouterSmallMaxT][512];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  if (e < p.E) {
+    float acc[kRouterSmallMaxT];
+#pragma unroll
+    for (int t = 0; t < kRouterSmallMaxT; ++t) acc[t] = 0.f;
+    const __nv_bfloat16* wr = p.w + (size_t)e * p.D;
+    for (int d = lane * 8; d < p.D; d += 256) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(wr + d);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+#pragma unroll
+      for (int t = 0; t < kRouterSmallMaxT; ++t) {
+        if (t >= p.T) break;
+        const uint4 uv = *reinterpret_cast<const uint4*>(p.u + (size_t)t * p.D + d);
+        const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = __bfloat1622float2(w2[i]), b = __bfloat1622float2(u2[i]);
+          acc[t] += a.x * b.x + a.y * b.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterSmallMaxT; ++t) {
+      if (t >= p.T) break;
+      const float v = warp_sum(acc[t]);
+      if (lane == 0) p.logits[(size_t)t * p.E + e] = v;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < p.T * p.E; i += blockDim.x) s_log[i / p.E][i % p.E] = __ldcg(p.logits + i);
+  __syncthreads();
+  if (warp < p.T) {
+    int my_id;
+    float my_w;
+    route_token<kMaxPer>(s_log[warp], p.E, p.bias, p.topk, p.score_func, p.route_scale, lane, my_id, my_w);
+    if (lane < p.topk) {
+      p.ids[(size_t)warp * p.topk + lane] = my_id;
+      p.wts[(size_t)warp * p.topk + lane] = my_w;
+    }
+  }
+  if (threadIdx.x == 0) *p.counter = 0;
+}
+
+cudaError_t router_small(const RouterSmallParams& p, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  if (p.T > kRouterSmallMaxT || p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 256 || p.counter == nullptr)
+    return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)((p.E + 7) / 8);
+  const int per = (p.E + 31) / 32;
+  if (per <= 2) launch_pdl(router_small_kernel<2>, grid, 256, 0, st, p);
+  else if (per <= 4) launch_pdl(router_small_kernel<4>, grid, 256, 0, st, p);
+  else if (per <= 8) launch_pdl(router_small_kernel<8>, grid, 256, 0, st, p);
+  else if (per <= 12) launch_pdl(router_small_kernel<12>, grid, 256, 0, st, p);
+  else launch_pdl(router_small_kernel<16>, grid, 256, 0, st, p);
+  return cudaGetLastError();
 }
 
 cudaError_t router_topk(const float* logits, int T, int E, const float* bias, int topk, int score_func,

@@ -32,12 +32,14 @@ import numpy as np
 import torch
 
 from ..ops import _ext
-from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
 from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
                         pick_bn)
 from ..ops.layout import ceil_to
 from ..ref import numerics as N
+from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
 from .weights import LayerW
+
+ROUTER_SMALL_T = 4   # steps of at most this many tokens route with csrc/moe.cu router_small
 
 
 # --------------------------------------------------------------------------
@@ -291,6 +293,7 @@ class DSV4Model:
         self.hs_sf = z(Tp // 128, si // 128, 512, dt=u8)
         self.shared_out = e(T, D)
         self.shared_y = self.shared_out   # the shared expert's rows for the next mHC boundary
+        self.router_counter = z(1, dt=i32)   # router_small's last-CTA counter (left at zero)
         # head
         self.u_sample = e(self.max_sample, D)
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
@@ -749,14 +752,22 @@ class DSV4Model:
         logits = self.router_logits[E]
         rctx = self._t("router")
         rctx.__enter__()
-        self._gemm_bf16(self.u, L.gate_w, logits, T, f32_out=True)
         ids, wts, pos, rank = self.route[k]
-        if self.ep is not None and self.ep.transport == "fused":
+        sfn = 1 if cfg.score_func == "sigmoid" else 0
+        fused = self.ep is not None and self.ep.transport == "fused"
+        if T <= ROUTER_SMALL_T and not fused:
+            # decode-sized steps: gate GEMV and top-k in one launch
+            ext.router_small(self.u, L.gate_w, T, logits, L.gate_b, k, sfn, cfg.route_scale, ids, wts,
+                             self.router_counter)
+        else:
+            self._gemm_bf16(self.u, L.gate_w, logits, T, f32_out=True)
+        if fused:
             # (also at world size 1: the same kernels with this GPU as the only peer)
             rctx.__exit__(None, None, None)
             # top-k, dispatch, plan, grouped GEMMs and the return of the rows (parallel/ep.py)
             return self.ep.moe_fused(self, L, T, k, logits)
-        ext.router_topk(logits, T, L.gate_b, k, 1 if cfg.score_func == "sigmoid" else 0, cfg.route_scale, ids, wts)
+        if T > ROUTER_SMALL_T:
+            ext.router_topk(logits, T, L.gate_b, k, sfn, cfg.route_scale, ids, wts)
         rctx.__exit__(None, None, None)
         if self.ep is not None and self.ep.world > 1:
             return self.ep.moe(self, L, T, k) + (None,)

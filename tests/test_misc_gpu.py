@@ -1,4 +1,5 @@
-"""Small device kernels vs plain PyTorch references: row argmax (single- and multi-CTA rows)."""
+"""Small device kernels vs plain PyTorch references: row argmax (single- and multi-CTA
+rows); the decode-step router (gate GEMV + top-k in one launch)."""
 
 import pytest
 import torch
@@ -29,6 +30,34 @@ def test_argmax_rows_matches_torch(T, V):
         torch.cuda.synchronize()
         assert torch.equal(out, want)
     assert int(scratch[-256:].abs().sum()) == 0
+
+
+@pytest.mark.parametrize("T", [1, 4])
+@pytest.mark.parametrize("E,D,k,score_func", [(256, 4096, 8, 0), (384, 5120, 6, 1)])
+def test_router_small_matches_reference(T, E, D, k, score_func):
+    """Logits = u . gate^T (fp32 accumulation of bf16 products), then the same top-k
+    as router_topk on those logits: picks and weights equal the reference routing of
+    the kernel's own logits, and the logits match an fp32 matmul to rounding."""
+    ext = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(T + E)
+    u = torch.randn(T, D, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, D, device="cuda", generator=g) * D ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(E, device="cuda", generator=g) * 0.1
+    logits = torch.zeros(T, E, device="cuda")
+    ids = torch.zeros(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(T, k, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(3):   # the counter must come back to zero
+        ext.router_small(u, w, T, logits, bias, k, score_func, 1.5, ids, wts, counter)
+    torch.cuda.synchronize()
+    assert int(counter) == 0
+    want = u.float() @ w.float().t()
+    assert float((logits - want).abs().max()) < 1e-3 * float(want.abs().max())
+    ids2 = torch.zeros_like(ids)
+    wts2 = torch.zeros_like(wts)
+    ext.router_topk(logits, T, bias, k, score_func, 1.5, ids2, wts2)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids2) and torch.equal(wts, wts2)
 
 
 def _probe(ext, graph: bool):
