@@ -521,15 +521,16 @@ void router_small(const Tensor& u, const Tensor& w, int64_t T, const Tensor& log
                   const Tensor& counter) {
   TORCH_CHECK(u.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && u.is_contiguous() &&
                   w.is_contiguous() && u.size(1) == w.size(1), "router_small: bf16 u [T, D] and gate [E, D]");
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.size(1) == w.size(0) && logits.stride(0) == w.size(0),
-              "router_small: f32 logits [T, E]");
+  // the gate matrix may carry padding rows past E (128-row GEMM tiles): E is the logits width
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(0) == logits.size(1) &&
+                  logits.stride(1) == 1 && w.size(0) >= logits.size(1), "router_small: f32 logits [T, E], E <= gate rows");
   TORCH_CHECK(counter.scalar_type() == at::kInt && counter.is_cuda(), "router_small: int32 counter");
   dsv4::RouterSmallParams p{};
   p.u = ptr<const bf16>(u);
   p.w = ptr<const bf16>(w);
   p.T = (int)T;
   p.D = (int)u.size(1);
-  p.E = (int)w.size(0);
+  p.E = (int)logits.size(1);
   p.logits = logits.data_ptr<float>();
   p.bias = ptr<const float>(bias);
   p.topk = (int)topk;
