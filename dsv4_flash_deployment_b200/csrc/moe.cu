@@ -35,31 +35,47 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 }
 
 // Small-T router (decode steps): logits = u . gate_w^T on CUDA cores (fp32
-// accumulation of the bf16 products), one warp per expert for every token, 8
+// accumulation of the bf16 products), two warps per expert for every token, 4
 // experts per CTA; the last CTA to finish (device counter; nothing waits) copies
 // each token's logits to shared memory with L2 loads and runs its top-k
 // (route_token), then re-arms the counter.  Replaces a split-K tensor-core GEMM
 // plus a separate top-k launch where the gate matrix is a few MB.
+constexpr int kRouterSmallChunks = 12;   // 16-byte pieces per lane: two warps per row, D <= 6144
+
 template <int kMaxPer>
 __global__ void __launch_bounds__(256) router_small_kernel(RouterSmallParams p) {
   pdl_entry();
   __shared__ float s_log[kRouterSmallMaxT][512];
+  __shared__ float s_half[8][kRouterSmallMaxT];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
+  const int e = blockIdx.x * 4 + (warp >> 1), half = warp & 1;   // two warps per gate row
+  float acc[kRouterSmallMaxT];
+#pragma unroll
+  for (int t = 0; t < kRouterSmallMaxT; ++t) acc[t] = 0.f;
   if (e < p.E) {
-    float acc[kRouterSmallMaxT];
-#pragma unroll
-    for (int t = 0; t < kRouterSmallMaxT; ++t) acc[t] = 0.f;
     const __nv_bfloat16* wr = p.w + (size_t)e * p.D;
-    for (int d = lane * 8; d < p.D; d += 256) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(wr + d);
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    // every 16-byte piece of this lane's share of the gate row is requested before
+    // any is used (one DRAM round trip, not one per piece)
+    uint4 wv[kRouterSmallChunks];
 #pragma unroll
-      for (int t = 0; t < kRouterSmallMaxT; ++t) {
-        if (t >= p.T) break;
-        const uint4 uv = *reinterpret_cast<const uint4*>(p.u + (size_t)t * p.D + d);
-        const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+    for (int c = 0; c < kRouterSmallChunks; ++c) {
+      const int d = lane * 8 + (2 * c + half) * 256;
+      wv[c] = d < p.D ? *reinterpret_cast<const uint4*>(wr + d) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterSmallMaxT; ++t) {
+      if (t >= p.T) break;
+      uint4 uv[kRouterSmallChunks];
+#pragma unroll
+      for (int c = 0; c < kRouterSmallChunks; ++c) {
+        const int d = lane * 8 + (2 * c + half) * 256;
+        uv[c] = d < p.D ? *reinterpret_cast<const uint4*>(p.u + (size_t)t * p.D + d) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int c = 0; c < kRouterSmallChunks; ++c) {
+        const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[c]);
+        const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv[c]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 a = __bfloat1622float2(w2[i]), b = __bfloat1622float2(u2[i]);
@@ -67,13 +83,15 @@ __global__ void __launch_bounds__(256) router_small_kernel(RouterSmallParams p) 
         }
       }
     }
-#pragma unroll
-    for (int t = 0; t < kRouterSmallMaxT; ++t) {
-      if (t >= p.T) break;
-      const float v = warp_sum(acc[t]);
-      if (lane == 0) p.logits[(size_t)t * p.E + e] = v;
-    }
   }
+#pragma unroll
+  for (int t = 0; t < kRouterSmallMaxT; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0) s_half[warp][t] = v;
+  }
+  __syncthreads();
+  if (half == 0 && lane < p.T && e < p.E)
+    p.logits[(size_t)lane * p.E + e] = s_half[warp][lane] + s_half[warp + 1][lane];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1) == (int)gridDim.x - 1;
@@ -96,9 +114,10 @@ __global__ void __launch_bounds__(256) router_small_kernel(RouterSmallParams p) 
 
 cudaError_t router_small(const RouterSmallParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  if (p.T > kRouterSmallMaxT || p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 256 || p.counter == nullptr)
+  if (p.T > kRouterSmallMaxT || p.E > 512 || p.topk > 16 || p.topk > p.E || p.D % 256 ||
+      p.D > 512 * kRouterSmallChunks || p.counter == nullptr)
     return cudaErrorInvalidValue;
-  const unsigned grid = (unsigned)((p.E + 7) / 8);
+  const unsigned grid = (unsigned)((p.E + 3) / 4);
   const int per = (p.E + 31) / 32;
   if (per <= 2) launch_pdl(router_small_kernel<2>, grid, 256, 0, st, p);
   else if (per <= 4) launch_pdl(router_small_kernel<4>, grid, 256, 0, st, p);

@@ -313,7 +313,7 @@ class DSV4Model:
         self.ws = e(8 * 1024 * 1024, dt=f32)
         self.counters = z(65536, dt=i32)
         # split-row attention at decode sizes: T <= 8 tokens x up to 32 splits
-        self.attn_splits = int(os.environ.get("DSV4_ATTN_SPLITS", "8"))
+        self.attn_splits = int(os.environ.get("DSV4_ATTN_SPLITS", "16"))
         if not 1 <= self.attn_splits <= 32:
             raise ValueError("DSV4_ATTN_SPLITS must be 1..32")
         self.attn_ws = e(max(1, min(T, 8)) * max(16, self.attn_splits) * 64 * 514, dt=f32)
