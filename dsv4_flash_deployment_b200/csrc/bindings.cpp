@@ -325,9 +325,15 @@ dsv4::HcParams hc_params(const Tensor& X, const optional<Tensor>& Y, const optio
   return p;
 }
 
-// tp: int64 CPU [mode, peer_sig, sig, done, epoch, phase, world, rank, peer_y, peer_yperm, peer_pos, ids, e_local]
-static void set_hc_tp(dsv4::HcParams& p, const optional<Tensor>& tp, const optional<Tensor>& err, int64_t topk) {
+void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
+             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn_hilo,
+             const optional<Tensor>& cw, int64_t cw_stride, const Tensor& c, const Tensor& partials,
+             const optional<Tensor>& tap, int64_t T, const optional<Tensor>& tp, const optional<Tensor>& err) {
+  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, fn_hilo, c10::nullopt, c10::nullopt, cw, cw_stride,
+                     c10::nullopt, c10::nullopt, c, partials, c10::nullopt, c10::nullopt, c10::nullopt, tap, T, 0, 0,
+                     0);
   if (tp) {
+    // int64 CPU [mode, peer_sig, sig, done, epoch, phase, world, rank, peer_y, peer_yperm, peer_pos, ids, e_local]
     TORCH_CHECK(!tp->is_cuda() && tp->scalar_type() == at::kLong && tp->numel() >= 13, "tp: int64 CPU [13]");
     TORCH_CHECK(err.has_value(), "tp mode needs the error word");
     const int64_t* v = tp->data_ptr<int64_t>();
@@ -346,35 +352,6 @@ static void set_hc_tp(dsv4::HcParams& p, const optional<Tensor>& tp, const optio
                 "tp mode tables missing");
     TORCH_CHECK(p.tp_mode >= 1 && p.tp_mode <= 4, "tp mode must be 1 .. 4");
   }
-}
-
-void hc_post(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm, const optional<Tensor>& pos,
-             int64_t topk, const optional<Tensor>& prev_mix, const optional<Tensor>& fn_hilo,
-             const optional<Tensor>& cw, int64_t cw_stride, const Tensor& c, const Tensor& partials,
-             const optional<Tensor>& tap, int64_t T, const optional<Tensor>& tp, const optional<Tensor>& err) {
-  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, fn_hilo, c10::nullopt, c10::nullopt, cw, cw_stride,
-                     c10::nullopt, c10::nullopt, c, partials, c10::nullopt, c10::nullopt, c10::nullopt, tap, T, 0, 0,
-                     0);
-  set_hc_tp(p, tp, err, topk);
-  const c10::cuda::CUDAGuard guard(X.device());
-  CUDA_OK(dsv4::hc_post(p, cur_stream()));
-}
-
-// hc_post + hc_finish in one launch for decode-sized steps (T <= kHcFuseMaxT): the
-// union of both argument lists plus an int32 device counter (zero, left at zero).
-void hc_post_finish(const Tensor& X, const optional<Tensor>& Y, const optional<Tensor>& yperm,
-                    const optional<Tensor>& pos, int64_t topk, const optional<Tensor>& prev_mix,
-                    const optional<Tensor>& fn_hilo, const optional<Tensor>& scale, const optional<Tensor>& base,
-                    const optional<Tensor>& cw, const optional<Tensor>& norm_w, const optional<Tensor>& mix_out,
-                    const Tensor& c, const Tensor& partials, const optional<Tensor>& u, const optional<Tensor>& uq,
-                    const optional<Tensor>& usf, const optional<Tensor>& tap, int64_t T, int64_t iters, double hc_eps,
-                    double norm_eps, const optional<Tensor>& tp, const optional<Tensor>& err, const Tensor& counter) {
-  TORCH_CHECK(T <= dsv4::kHcFuseMaxT, "hc_post_finish: decode-sized steps only");
-  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt, "hc_post_finish: int32 device counter");
-  auto p = hc_params(X, Y, yperm, pos, topk, prev_mix, fn_hilo, scale, base, cw, 24, norm_w, mix_out, c, partials, u,
-                     uq, usf, tap, T, iters, hc_eps, norm_eps);
-  set_hc_tp(p, tp, err, topk);
-  p.fin_counter = counter.data_ptr<int>();
   const c10::cuda::CUDAGuard guard(X.device());
   CUDA_OK(dsv4::hc_post(p, cur_stream()));
 }
@@ -924,7 +901,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp4_roundtrip", &fp4_roundtrip);
   m.def("hc_post", &hc_post);
   m.def("hc_finish", &hc_finish);
-  m.def("hc_post_finish", &hc_post_finish);
   m.def("hc_num_slices", [](int64_t d) { return (int64_t)dsv4::hc_num_slices((int)d); });
   m.def("attention", &attention);
   m.def("debug_bounds_attach", &debug_bounds_attach);

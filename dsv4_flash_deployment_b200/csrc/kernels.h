@@ -82,7 +82,6 @@ struct HcParams {
   // published the phase.  All wait first
   // (bounded) until every rank has published the phase.
   int tp_mode;
-  int* fin_counter;                 // hc_post: the last CTA also finishes (T <= kHcFuseMaxT; left at zero)
   const float* const* peer_y;
   const __nv_bfloat16* const* peer_yperm;
   const int* const* peer_pos;
@@ -92,7 +91,6 @@ struct HcParams {
   uint32_t* err;
 };
 int hc_num_slices(int D);
-constexpr int kHcFuseMaxT = 8;
 cudaError_t hc_post(const HcParams& p, cudaStream_t st);
 cudaError_t hc_finish(const HcParams& p, cudaStream_t st);
 

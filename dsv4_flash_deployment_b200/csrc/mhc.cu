@@ -13,8 +13,7 @@
 //            from the previous boundary
 //   u      = bf16( rmsnorm(c) * norm_w ), then MXFP8-quantized for the next GEMM.
 //
-// Two launches per boundary (one for decode-sized steps: hc_post's last CTA runs
-// the finish, see hc_post_kernel):
+// Two launches per boundary:
 //   hc_post    one pass over X per (16-token, 128-column) tile: X', the collapse c,
 //              sums of squares, and the tile's share of the 24-mix projection on
 //              tensor cores (mma.sync, bf16 operands, fp32 accumulate): hc_fn is
@@ -54,7 +53,9 @@ DSV4_DEV void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 // 256 threads.  Thread -> (token tid/16, 8 columns (tid%16)*8 of the slice).
 constexpr int kMaxCombine = 8;   // routed experts per token summed by the MoE combine
 
-DSV4_DEV void hc_post_body(const HcParams& p, int n_slices, uint8_t* smem) {
+__global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slices) {
+  pdl_entry();
+  extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sFn = reinterpret_cast<__nv_bfloat16*>(smem);                 // [48][kRowE]
   __nv_bfloat16* sX = sFn + kNMix * kRowE;                                      // [16][kRowE]
   // [8 warps][16][48] cross-warp sums of the mixes; aliases sFn, which is dead
@@ -311,22 +312,17 @@ DSV4_DEV void hc_post_body(const HcParams& p, int n_slices, uint8_t* smem) {
   }
 }
 
-// Per-token finish of a boundary, run by 4 warps (warp = 0..3 within the group):
-// partials per slice (48 projections = hi | lo rows of hc_fn, sumsq(X'),
-// sumsq(c)) reduced in slice order (8 slices' loads in flight), warp 0 forms the
-// mixes and runs Sinkhorn, the four warps share the RMSNorm + MXFP8 pass over D.
-// s_part: 256 floats of shared memory for the group.  bar_id 0 = the whole CTA
-// is the group (__syncthreads); otherwise a named barrier of 128 threads.  The
-// partials and the collapse row are read through L2 (__ldcg): inside hc_post
-// they were written by other CTAs of the same launch.
+// One CTA (4 warps) per token.  Partials per slice: 48 projections (hi | lo
+// rows of hc_fn), sumsq(X'), sumsq(c); every warp reduces them in slice order
+// (8 slices' loads in flight), warp 0 forms the mixes and runs Sinkhorn, and the
+// four warps share the RMSNorm + MXFP8 pass over the D columns.
 constexpr int kFinMaxIt = 5;   // norm pass: 1024 columns per iteration, D <= 5120
 
-DSV4_DEV void group_sync(int bar_id) {
-  if (bar_id == 0) __syncthreads();
-  else asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-}
-
-DSV4_DEV void finish_token(const HcParams& p, int n_slices, int t, int warp, int lane, float* s_part, int bar_id) {
+__global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
+  pdl_entry();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  if (t >= p.T) return;
   const int D = p.D;
   const bool do_norm = p.cw != nullptr && p.u != nullptr;
   // the collapse row and the norm weights do not depend on the partials: load them first
@@ -336,7 +332,7 @@ DSV4_DEV void finish_token(const HcParams& p, int n_slices, int t, int warp, int
     for (int i = 0; i < kFinMaxIt; ++i) {
       const int d0 = warp * 256 + i * 1024 + lane * 8;
       if (d0 < D) {
-        craw[i] = __ldcg(reinterpret_cast<const uint4*>(p.c + (size_t)t * D + d0));
+        craw[i] = *reinterpret_cast<const uint4*>(p.c + (size_t)t * D + d0);
         wraw[i] = *reinterpret_cast<const uint4*>(p.norm_w + d0);
       }
     }
@@ -348,14 +344,15 @@ DSV4_DEV void finish_token(const HcParams& p, int n_slices, int t, int warp, int
   float r0 = 0.f, r1 = 0.f;
 #pragma unroll 4
   for (int s = warp; s < n_slices; s += 4) {
-    r0 += __ldcg(part + s * kNPart + lane);
-    if (hi_lane) r1 += __ldcg(part + s * kNPart + 32 + lane);
+    r0 += part[s * kNPart + lane];
+    if (hi_lane) r1 += part[s * kNPart + 32 + lane];
   }
-  s_part[warp * 64 + lane] = r0;
-  s_part[warp * 64 + 32 + lane] = r1;
-  group_sync(bar_id);
-  r0 = ((s_part[lane] + s_part[64 + lane]) + s_part[128 + lane]) + s_part[192 + lane];
-  r1 = ((s_part[32 + lane] + s_part[96 + lane]) + s_part[160 + lane]) + s_part[224 + lane];
+  __shared__ float s_part[4][64];
+  s_part[warp][lane] = r0;
+  s_part[warp][32 + lane] = r1;
+  __syncthreads();
+  r0 = ((s_part[0][lane] + s_part[1][lane]) + s_part[2][lane]) + s_part[3][lane];
+  r1 = ((s_part[0][32 + lane] + s_part[1][32 + lane]) + s_part[2][32 + lane]) + s_part[3][32 + lane];
   const float ssx = __shfl_sync(0xffffffffu, r1, kNMix - 32);
   const float ssc = __shfl_sync(0xffffffffu, r1, kNMix + 1 - 32);
   if (p.fn_hilo != nullptr && warp == 0) {
@@ -438,46 +435,10 @@ DSV4_DEV void finish_token(const HcParams& p, int n_slices, int t, int warp, int
   }
 }
 
-// One CTA (4 warps) per token.
-__global__ void __launch_bounds__(128) hc_finish_kernel(HcParams p, int n_slices) {
-  pdl_entry();
-  __shared__ float s_part[256];
-  const int t = blockIdx.x;
-  if (t >= p.T) return;
-  finish_token(p, n_slices, t, threadIdx.x >> 5, threadIdx.x & 31, s_part, 0);
-}
-
-// hc_post; with fin_counter (a single token tile, T <= kHcFuseMaxT) the last CTA
-// to finish also runs hc_finish for every token: CTAs count themselves in on a
-// device counter after their partials and collapse columns are stored (nothing
-// waits), the last one reads them through L2, two groups of 4 warps take
-// alternate tokens, and the counter is re-armed.
-__global__ void __launch_bounds__(256, 3) hc_post_kernel(HcParams p, int n_slices) {
-  pdl_entry();
-  extern __shared__ __align__(16) uint8_t smem[];
-  hc_post_body(p, n_slices, smem);
-  if (p.fin_counter == nullptr) return;
-  __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(p.fin_counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = warp >> 2;
-  float* s_part = reinterpret_cast<float*>(smem) + g * 256;   // the fn tile is dead by now
-  for (int t = g; t < p.T; t += 2) {
-    finish_token(p, n_slices, t, warp & 3, lane, s_part, 1 + g);
-    group_sync(1 + g);   // s_part is reused by the group's next token
-  }
-  if (threadIdx.x == 0) *p.fin_counter = 0;
-}
-
 int hc_num_slices(int D) { return (D + kSlice - 1) / kSlice; }
 
 cudaError_t hc_post(const HcParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
-  if (p.fin_counter != nullptr && (p.T > kHcFuseMaxT || p.D % 256 || p.D > 1024 * kFinMaxIt)) return cudaErrorInvalidValue;
   if ((p.yperm != nullptr || p.tp_mode >= 2) && p.topk > kMaxCombine) return cudaErrorInvalidValue;
   if (p.D % kSlice) return cudaErrorInvalidValue;
   const int ns = hc_num_slices(p.D);

@@ -40,7 +40,6 @@ from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
 from .weights import LayerW
 
 ROUTER_SMALL_T = 4   # steps of at most this many tokens route with csrc/moe.cu router_small
-HC_FUSE_T = 8        # ... and run each mHC boundary as one launch (csrc/mhc.cu hc_post_kernel)
 
 
 # --------------------------------------------------------------------------
@@ -295,7 +294,6 @@ class DSV4Model:
         self.shared_out = e(T, D)
         self.shared_y = self.shared_out   # the shared expert's rows for the next mHC boundary
         self.router_counter = z(1, dt=i32)   # router_small's last-CTA counter (left at zero)
-        self.hc_counter = z(1, dt=i32)       # hc_post_finish's last-CTA counter (left at zero)
         # head
         self.u_sample = e(self.max_sample, D)
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
@@ -454,18 +452,10 @@ class DSV4Model:
         fnhl = scale = base = None
         if mixes is not None:
             fnhl, scale, base = mixes
-        finish = mixes is not None or (cw is not None and u is not None)
-        if finish and T <= HC_FUSE_T:
-            # decode-sized steps: hc_post's last CTA runs the finish (one launch)
-            with self._t("hc_post"):
-                ext.hc_post_finish(self.X, Y, yperm, pos, topk, prev, fnhl, scale, base, cw, norm, mix_out,
-                                   self.hc_c, self.hc_part, u, uq, usf, tap, T, self.sinkhorn_iters, cfg.hc_eps,
-                                   cfg.rms_norm_eps, tp, self.err, self.hc_counter)
-            return
         with self._t("hc_post"):
             ext.hc_post(self.X, Y, yperm, pos, topk, prev, fnhl, cw, 24, self.hc_c, self.hc_part, tap, T, tp,
                         self.err)
-        if finish:
+        if mixes is not None or (cw is not None and u is not None):
             with self._t("hc_finish"):
                 ext.hc_finish(self.X, fnhl, scale, base, cw, norm, mix_out, self.hc_c, self.hc_part, u, uq, usf, T,
                               self.sinkhorn_iters, cfg.hc_eps, cfg.rms_norm_eps)

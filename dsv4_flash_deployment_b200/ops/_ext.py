@@ -39,7 +39,7 @@ _mod = None
 
 # kernels launched per binding call (used to report how many of this
 # library's kernels a step issues)
-_KERNELS_PER_CALL = {"hc_post": 1, "hc_finish": 1, "hc_post_finish": 1, "attention": 1, "gemm": 1, "gemm_a2": 1, "act_quant_mx": 1, "qkv_post": 1, "idx_q_prep": 1,
+_KERNELS_PER_CALL = {"hc_post": 1, "hc_finish": 1, "attention": 1, "gemm": 1, "gemm_a2": 1, "act_quant_mx": 1, "qkv_post": 1, "idx_q_prep": 1,
                      "compress_pool": 1, "ring_update": 1, "router_topk": 1, "router_small": 1, "moe_plan": 1, "moe_scatter": 1,
                      "indexer_topk": 2, "embed_streams": 1, "argmax_rows": 1, "act_roundtrip": 1,
                      "fp4_roundtrip": 1, "ep_pack": 1, "ep_unpack_meta": 1, "ep_unpack_rows": 1,
