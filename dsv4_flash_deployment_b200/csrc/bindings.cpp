@@ -66,15 +66,6 @@ static dsv4::KvPages kv_pages_of(const optional<Tensor>& d, int* max_c) {
 }
 
 // DSV4_GEMM_BM256=0 keeps every GEMM on 128-row weight tiles (A/B timing).
-// DSV4_GEMM_PAIRS=0: grouped GEMMs take their tiles one at a time (A/B timing)
-static bool gemm_pairs_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("DSV4_GEMM_PAIRS");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 static bool bm256_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("DSV4_GEMM_BM256");
@@ -175,7 +166,6 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
   p.sfa2 = A2 ? (A2_sf ? u8ptr(A2_sf) : reinterpret_cast<const uint8_t*>(A2->data_ptr())) : nullptr;
   p.M2 = A2 ? (int)A2->size(0) : 0;
   p.a2_e4m3 = a2_e4m3 ? 1 : 0;
-  p.pairs = grouped && gemm_pairs_enabled() ? 1 : 0;
   p.sfb = u8ptr(B_sf);
   p.sfb_ktiles = (int)(b_cols / 128);
   if (groups > 1) {

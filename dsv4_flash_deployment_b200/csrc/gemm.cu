@@ -164,11 +164,6 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + L::kXbuf);
   uint8_t** ret_rows = reinterpret_cast<uint8_t**>(reinterpret_cast<uint8_t*>(bars) + L::kBarriers);
   constexpr int NA = L::kNumAcc;
-  // grouped GEMMs with two accumulators take their tiles in pairs: the k-steps of
-  // tiles w and w + grid alternate through the stage ring, one accumulator each,
-  // so two independent MMA chains are in flight (the epilogue still drains the
-  // tiles in list order)
-  const int P = (GROUPED && NA == 2 && p.pairs) ? 2 : 1;
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* acc_full = bars + 2 * S;
@@ -246,15 +241,7 @@ __global__ void __launch_bounds__(192, 1)
       pdl_wait();
     }
     bool first = true;
-    for (int w = blockIdx.x;; w += P * gridDim.x, first = false) {
-      TileCoord tg[2];
-      if (!get_work<GROUPED, BN, BM>(p, w, tg[0])) break;
-      const int ng = (P == 2 && get_work<GROUPED, BN, BM>(p, w + gridDim.x, tg[1])) ? 2 : 1;
-      const int nk = max(tg[0].k_end - tg[0].k_begin, ng == 2 ? tg[1].k_end - tg[1].k_begin : 0);
-      for (int i = 0; i < nk; ++i)
-      for (int u = 0; u < ng; ++u) {
-      const TileCoord& t = tg[u];
-      if (i >= t.k_end - t.k_begin) continue;
+    for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x, first = false) {
       const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
       const uint32_t txa = (KIND == KIND_MX4A && t.a2 && p.a2_e4m3) ? (uint32_t)L::kA : kATx;
       const uint32_t tx = txa + t.n_eff * 128 + (MX ? 512 * (L::kSfaChunks + sfb_chunks) : 0);
@@ -262,9 +249,9 @@ __global__ void __launch_bounds__(192, 1)
       const int b_kofs = p.group_k * (t.a_row0 / p.group_rows);
       const CUtensorMap* amap = t.a2 ? &tma_a.m[1] : &tma_a.m[0];
       const uint8_t* sfa = t.a2 ? p.sfa2 : p.sfa;
-      {
+      for (int i = 0; i < t.k_end - t.k_begin; ++i) {
         const int kt = k_of(t, i);
-        const bool prefetched = first && u == 0 && i < pre;   // fresh stage: its A half is already in flight
+        const bool prefetched = first && i < pre;   // fresh stage: its A half is already in flight
         if (!prefetched && !mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, KID_GEMM, 1)) goto done;
         if (lane == 0) {
           if (!prefetched) {
@@ -290,7 +277,6 @@ __global__ void __launch_bounds__(192, 1)
           phase ^= 1;
         }
       }
-      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -298,23 +284,15 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int w = blockIdx.x;; w += P * gridDim.x) {
-      TileCoord tg[2];
-      if (!get_work<GROUPED, BN, BM>(p, w, tg[0])) break;
-      const int ng = (P == 2 && get_work<GROUPED, BN, BM>(p, w + gridDim.x, tg[1])) ? 2 : 1;
-      const int nk = max(tg[0].k_end - tg[0].k_begin, ng == 2 ? tg[1].k_end - tg[1].k_begin : 0);
-      // a pair starts at accumulator 0 (only the list's last tile can be alone)
-      for (int u = 0; u < ng; ++u)
-        if (!mbar_wait(&acc_empty[acc + u], acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
+    TileCoord t;
+    for (int w = blockIdx.x; get_work<GROUPED, BN, BM>(p, w, t); w += gridDim.x) {
+      const uint32_t afmt = (KIND == KIND_MX4A && !(t.a2 && p.a2_e4m3)) ? 5 : 0;   // e2m1 or e4m3 weights
+      const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, afmt, 0) : idesc_bf16(128, t.n_eff);
+      const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
+      const uint32_t d_tmem = tmem + acc * L::kAccCols;
+      if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, KID_GEMM, 2)) goto done;
       tc_fence_after();
-      for (int i = 0; i < nk; ++i)
-      for (int u = 0; u < ng; ++u) {
-        const TileCoord& t = tg[u];
-        if (i >= t.k_end - t.k_begin) continue;
-        const uint32_t afmt = (KIND == KIND_MX4A && !(t.a2 && p.a2_e4m3)) ? 5 : 0;   // e2m1 or e4m3 weights
-        const uint32_t idesc = MX ? idesc_mx(128, t.n_eff, afmt, 0) : idesc_bf16(128, t.n_eff);
-        const int sfb_chunks = t.n_eff > 128 ? 2 : 1;
-        const uint32_t d_tmem = tmem + (acc + u) * L::kAccCols;
+      for (int i = 0; i < t.k_end - t.k_begin; ++i) {
         if (!mbar_wait(&full[stage], phase, abort_flag, p.err, KID_GEMM, 3)) goto done;
         tc_fence_after();
         if (lane == 0) {
@@ -354,14 +332,12 @@ __global__ void __launch_bounds__(192, 1)
           phase ^= 1;
         }
       }
-      if (lane == 0)
-        for (int u = 0; u < ng; ++u) umma_commit(&acc_full[acc + u]);
+      if (lane == 0) umma_commit(&acc_full[acc]);
       __syncwarp();
-      for (int u = 0; u < ng; ++u)
-        if (++acc == NA) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
+      if (++acc == NA) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
     }
   } else {
     // ----------------------------------------------------------- epilogue
