@@ -6,7 +6,7 @@ per expert, weights larger than L2 at E >= 32), one tile per (expert, 128 output
 rows), and times the same tile lists at each requested BN with CUDA events.
 BN 32 covers only the first 32 rows of a tile, so its bytes are a lower bound.
 
-    python -m dsv4_flash_deployment_b200.bench.grouped_bench --experts 32 128 256 --bn 32 64 128 [--tiled]
+    python -m dsv4_flash_deployment_b200.bench.grouped_bench --experts 32 128 256 --bn 32 64 128
 """
 
 from __future__ import annotations
@@ -18,12 +18,11 @@ import torch
 
 from ..ops import _ext
 from ..ops.gemm import EPI_BF16, EPI_SWIGLU, KIND_MX8
-from ..ops.layout import tile_major
 
 D, I = 4096, 2048
 
 
-def run(E: int, bns: list[int], iters: int = 20, seed: int = 0, copies: int = 1, tiled: bool = False) -> dict:
+def run(E: int, bns: list[int], iters: int = 20, seed: int = 0, copies: int = 1) -> dict:
     ext = _ext.load(required=True)
     dev = "cuda"
     g = torch.Generator(device=dev)
@@ -34,9 +33,6 @@ def run(E: int, bns: list[int], iters: int = 20, seed: int = 0, copies: int = 1,
     W2 = [torch.randint(0, 120, (E * D, I), device=dev, dtype=u8, generator=g) for _ in range(copies)]
     S2 = [torch.full((E * D // 128, I // 128, 512), 120, device=dev, dtype=u8) for _ in range(copies)]
     w13, w2 = W13[0], W2[0]
-    # tiled: the same bytes stored tile-major (one contiguous block per 128 rows x k-tile)
-    A13 = [tile_major(w, D) for w in W13] if tiled else W13
-    A2 = [tile_major(w, I) for w in W2] if tiled else W2
     rows = torch.randint(9, 64, (E,), generator=torch.Generator().manual_seed(seed)).tolist()
     R = E * 128
     x = torch.randint(0, 120, (R, D), device=dev, dtype=u8, generator=g)
@@ -50,17 +46,17 @@ def run(E: int, bns: list[int], iters: int = 20, seed: int = 0, copies: int = 1,
     t2 = i32([[e * D + mt * 128, e * 128, rows[e], mt * 128] for e in range(E) for mt in range(D // 128)])
     n13, n2 = i32([len(t13)]), i32([len(t2)])
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    out = {"experts": E, "rows_mean": round(sum(rows) / E, 2), "weight_copies": copies, "tile_major": tiled}
+    out = {"experts": E, "rows_mean": round(sum(rows) / E, 2), "weight_copies": copies}
     for bn in bns:
         def f13(i):
             c = i % copies
-            ext.gemm_a2(KIND_MX8, EPI_SWIGLU, A13[c], S13[c], x, xsf, None, w13.shape[0], R, D, bn, 1, t13, n13, rs,
-                        h, hsf, 10.0, 2 * I, 0, None, None, err, 0, 1, None, None, None, None, None, tiled)
+            ext.gemm(KIND_MX8, EPI_SWIGLU, W13[c], S13[c], x, xsf, None, w13.shape[0], R, D, bn, 1, t13, n13, rs, h,
+                     hsf, 10.0, 2 * I, 0, None, None, err, 0, 1, None, None, None)
 
         def f2(i):
             c = i % copies
-            ext.gemm_a2(KIND_MX8, EPI_BF16, A2[c], S2[c], h, hsf, y, w2.shape[0], R, I, bn, 1, t2, n2, None, None,
-                        None, 0.0, D, D, None, None, err, 0, 1, None, None, None, None, None, tiled)
+            ext.gemm(KIND_MX8, EPI_BF16, W2[c], S2[c], h, hsf, y, w2.shape[0], R, I, bn, 1, t2, n2, None, None, None,
+                     0.0, D, D, None, None, err, 0, 1, None, None, None)
 
         for fn, name, nbytes in ((f13, "w13", w13.numel() + S13[0].numel()), (f2, "w2", w2.numel() + S2[0].numel())):
             for i in range(3):
@@ -86,10 +82,9 @@ def main(argv=None) -> None:
     ap.add_argument("--bn", type=int, nargs="*", default=[32, 64, 128])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=1, help="separately allocated weight copies to cycle over")
-    ap.add_argument("--tiled", action="store_true", help="weights stored tile-major (ops/layout.py tile_major)")
     a = ap.parse_args(argv)
     for E in a.experts:
-        print(json.dumps(run(E, a.bn, a.iters, copies=a.copies, tiled=a.tiled)), flush=True)
+        print(json.dumps(run(E, a.bn, a.iters, copies=a.copies)), flush=True)
 
 
 if __name__ == "__main__":

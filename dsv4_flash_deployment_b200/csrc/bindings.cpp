@@ -101,7 +101,7 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
              double swiglu_limit, int64_t m_valid, int64_t ldo, const optional<Tensor>& workspace,
              const optional<Tensor>& counters, const Tensor& err, int64_t max_grid, int64_t groups,
              const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer,
-             const optional<Tensor>& A2, const optional<Tensor>& A2_sf, bool a_tiled) {
+             const optional<Tensor>& A2, const optional<Tensor>& A2_sf) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CONTIG(A);
@@ -125,17 +125,8 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
                      ? 256 : 128;
   dsv4::AMaps ta{};
   dsv4::BMaps tb;
-  if (a_tiled) {
-    // tile-major weights: [M / 128 * K / 128 * 128, one 128-element k-tile] (ops/layout.py tile_major)
-    TORCH_CHECK(grouped && bm == 128 && kind != dsv4::KIND_BF16 && A.dim() == 2 && A.size(1) == (e2m1 ? 64 : 128) &&
-                    A.size(0) == M * (K / 128),
-                "tile-major A: grouped block-scaled GEMMs, [M * K/128, one 128-element k-tile]");
-    TORCH_CHECK(dsv4::make_tma_2d(&ta.m[0], A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), 128, (uint32_t)bm),
-                "TMA(A) encode failed");
-  } else {
-    TORCH_CHECK(dsv4::make_tma_2d(&ta.m[0], A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
-                "TMA(A) encode failed");
-  }
+  TORCH_CHECK(dsv4::make_tma_2d(&ta.m[0], A.data_ptr(), tma_elem_of(A, e2m1), A.size(0), K, (uint32_t)bm),
+              "TMA(A) encode failed");
   // MXFP4 weights (A packed [rows, K/2]) may take an MXFP8 second operand ([rows, K])
   const bool a2_e4m3 = A2 && e2m1 && A2->size(1) == K;
   if (A2) {
@@ -175,7 +166,6 @@ void gemm_a2(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>&
   p.sfa2 = A2 ? (A2_sf ? u8ptr(A2_sf) : reinterpret_cast<const uint8_t*>(A2->data_ptr())) : nullptr;
   p.M2 = A2 ? (int)A2->size(0) : 0;
   p.a2_e4m3 = a2_e4m3 ? 1 : 0;
-  p.a_tiled = a_tiled ? 1 : 0;
   p.sfb = u8ptr(B_sf);
   p.sfb_ktiles = (int)(b_cols / 128);
   if (groups > 1) {
@@ -250,7 +240,7 @@ void gemm(int64_t kind, int64_t epi, const Tensor& A, const optional<Tensor>& A_
           const optional<Tensor>& publish, const optional<Tensor>& ret_meta, const optional<Tensor>& ret_peer) {
   gemm_a2(kind, epi, A, A_sf, B, B_sf, out, M, N, K, bn, splits, tiles, n_tiles, row_scale, hq, hsf, swiglu_limit,
           m_valid, ldo, workspace, counters, err, max_grid, groups, publish, ret_meta, ret_peer, c10::nullopt,
-          c10::nullopt, false);
+          c10::nullopt);
 }
 
 void act_quant_mx(const Tensor& x, Tensor& q, Tensor& sf) {

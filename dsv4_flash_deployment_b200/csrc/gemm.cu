@@ -256,10 +256,7 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) {
           if (!prefetched) {
             mbar_arrive_expect_tx(&full[stage], tx);
-            if (GROUPED && p.a_tiled && !t.a2)
-              tma_load_2d(sA + stage * L::kA, amap, &full[stage], 0, ((t.a_row0 >> 7) * p.k_tiles + kt) * 128);
-            else
-              tma_load_2d(sA + stage * L::kA, amap, &full[stage], kt * kBkElems, t.a_row0);
+            tma_load_2d(sA + stage * L::kA, amap, &full[stage], kt * kBkElems, t.a_row0);
           }
           tma_load_2d(sB + stage * L::kB, bmap, &full[stage], b_kofs + kt * kBkElems, t.b_row0);
           if constexpr (MX) {

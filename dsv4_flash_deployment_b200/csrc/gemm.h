@@ -55,8 +55,6 @@ struct GemmParams {
   // tile list): scale chunks [M2/128][sfa_ktiles][512]
   const uint8_t* sfa2;
   int M2;
-  int a_tiled;         // grouped: the first weight operand is stored tile-major (each 128-row x
-                       // one-k-tile block contiguous): row (a_row0 / 128 * k_tiles + kt) * 128
   int a2_e4m3;         // KIND_MX4A: the second operand is e4m3 (MXFP8), not e2m1 -- both sit
                        // one byte per element in shared memory; only the TMA byte count and
                        // the A format of the instruction descriptor differ

@@ -814,13 +814,12 @@ class DSV4Model:
         c13.__enter__()
         ext.gemm_a2(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, self.xperm, self.xperm_sf, None, ex.w13.q.shape[0],
                     rows, D, bn, 1, self.tiles13, self.nt13, self.row_scale, self.hperm, self.hperm_sf,
-                    cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None, None, None, *a13, False)
+                    cfg.swiglu_limit, 2 * I, 0, None, None, self.err, 0, 1, None, None, None, *a13)
         c13.__exit__(None, None, None)
         c2 = self._t("grouped_w2")
         c2.__enter__()
         split = self.tp is not None and self.tp.moe == "tp"   # f32 partial rows, summed over ranks
         ext.gemm_a2(ex.w2.kind, EPI_F32 if split else EPI_BF16, ex.w2.q, ex.w2.sf, self.hperm, self.hperm_sf,
                     self.yperm, ex.w2.q.shape[0], rows, I, bn, 1, self.tiles2, self.nt2, None, None, None, 0.0, D, D,
-                    None, None, self.err, 0, 1, self.tp.sync(1) if self.tp is not None else None, None, None, *a2,
-                    False)
+                    None, None, self.err, 0, 1, self.tp.sync(1) if self.tp is not None else None, None, None, *a2)
         c2.__exit__(None, None, None)

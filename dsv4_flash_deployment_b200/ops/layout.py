@@ -49,16 +49,3 @@ def interleave_w13(w1: torch.Tensor, w3: torch.Tensor, block: int = 64) -> torch
     a = w1.reshape(i // block, block, *w1.shape[1:])
     b = w3.reshape(i // block, block, *w3.shape[1:])
     return torch.cat([a, b], 1).reshape(2 * i, *w1.shape[1:])
-
-
-def tile_major(q: torch.Tensor, k_elems: int) -> torch.Tensor:
-    """Row-major block-scaled weight bytes [R, Kb] -> tile-major [R / 128 * KT * 128, Kb / KT]
-    (KT = k_elems / 128): every 128-row x one-k-tile block is stored contiguously, row
-    block after row block, k-tile after k-tile, so each stage of the grouped GEMM reads
-    one contiguous block (the ``a_tiled`` operand of ``gemm_a2``).  Scales are unchanged."""
-    R, Kb = q.shape
-    KT = k_elems // 128
-    if R % 128 or k_elems % 128 or Kb % KT:
-        raise ValueError(f"tile_major: [{R}, {Kb}] with K = {k_elems}")
-    tb = Kb // KT
-    return q.view(R // 128, 128, KT, tb).permute(0, 2, 1, 3).contiguous().view(R // 128 * KT * 128, tb)

@@ -239,11 +239,11 @@ class EPGroup:
         with model._t("grouped_w13"):
             ext.gemm_a2(ex.w13.kind, EPI_SWIGLU, ex.w13.q, ex.w13.sf, b["x"], b["xsf"], None, ex.w13.q.shape[0],
                         b["xrows"], D, b["tile_rows"], 1, b["tiles13"], b["nt13"], b["rscale"], b["h"], b["hsf"],
-                        cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None, *a13, False)
+                        cfg.swiglu_limit, 2 * I, 0, None, None, model.err, 0, 1, None, None, None, *a13)
         with model._t("grouped_w2"):
             ext.gemm_a2(ex.w2.kind, EPI_BF16, ex.w2.q, ex.w2.sf, b["h"].view(b["xrows"], I), b["hsf"], None,
                         ex.w2.q.shape[0], b["xrows"], I, b["tile_rows"], 1, b["tiles2"], b["nt2"], None, None, None,
-                        0.0, D, D, None, None, model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"], *a2, False)
+                        0.0, D, D, None, None, model.err, 0, 1, b["sync1"], b["meta"], b["peer_back"], *a2)
         if merged:
             # the shared expert's rows came back with the routed ones (rows ret0 + t)
             model.shared_y = b["back"][b["ret0"]:b["ret0"] + T]

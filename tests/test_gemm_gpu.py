@@ -239,18 +239,6 @@ def test_grouped_expert_ffn_matches_oracle(fmt):
         (w1, s1), (w3, s3), (w2_, s2) = experts[e]
         ref = N.expert_ffn(x[st:st + c], w1, s1, w3, s3, w2_, s2, 10.0, rw[st:st + c, None])
         _close(y[st:st + c], ref, 0.05)
-    # the same weights stored tile-major give the same bits
-    from dsv4_flash_deployment_b200.ops.layout import tile_major
-    hq2, hsf2, y2 = torch.zeros_like(hq), torch.zeros_like(hsf), torch.zeros_like(y)
-    ext.gemm_a2(w13.kind, G.EPI_SWIGLU, tile_major(w13.q, D), w13.sf, xq, xsf, None, w13.q.shape[0], rows, D, 128, 1,
-                t13, torch.tensor([len(t13)], dtype=torch.int32, device="cuda"), rw.cuda(), hq2, hsf2, 10.0, 2 * I, 0,
-                None, None, err, 0, 1, None, None, None, None, None, True)
-    ext.gemm_a2(w2.kind, G.EPI_BF16, tile_major(w2.q, I), w2.sf, hq2, hsf2, y2, w2.q.shape[0], rows, I, 128, 1, t2,
-                torch.tensor([len(t2)], dtype=torch.int32, device="cuda"), None, None, None, 0.0, D, D, None, None,
-                err, 0, 1, None, None, None, None, None, True)
-    torch.cuda.synchronize()
-    G.ErrorWord.check("cuda")
-    assert torch.equal(hq2, hq) and torch.equal(hsf2, hsf) and torch.equal(y2, y)
 
 
 @pytest.mark.parametrize("n_tok", [1, 20, 64, 127, 200])
