@@ -576,6 +576,7 @@ void moe_plan(int64_t T, int64_t topk, int64_t e_local, int64_t e_begin, const T
   p.seg_cap = (int)seg_cap;
   p.shared_rows = (int)shared_rows;
   p.shared_row0 = (int)shared_row0;
+  p.rs_rows = (int)row_scale.numel();
   if (shared_rows > 0)
     TORCH_CHECK(shared_row0 + shared_rows <= row_scale.numel(), "shared segment outside row_scale");
   CUDA_OK(dsv4::moe_plan(p, cur_stream()));
@@ -586,7 +587,7 @@ void moe_scatter(const Tensor& xq, const Tensor& xsf, int64_t T, int64_t topk, c
   if (shared_row0 >= 0) TORCH_CHECK(shared_row0 + T <= pq.size(0), "shared segment outside the permuted buffer");
   CUDA_OK(dsv4::moe_scatter(ptr<const uint8_t>(xq), ptr<const uint8_t>(xsf), (int)T, (int)xq.size(1), (int)topk,
                             ptr<const int>(pos), ptr<uint8_t>(pq), ptr<uint8_t>(psf), (int)shared_row0,
-                            cur_stream()));
+                            (int)pq.size(0), cur_stream()));
 }
 
 void indexer_topk(const Tensor& q, const Tensor& w, const Tensor& kcache, const Tensor& slot, const Tensor& clen,

@@ -66,6 +66,7 @@ enum BoundsSite : uint32_t {
   BS_EP_RET = 4,        // expert-parallel dispatch: return row index out of range
   BS_GEMM_TILE = 5,     // grouped GEMM tile outside the A or B operand rows
   BS_GEMM_RET = 6,      // grouped GEMM return row: source rank out of range
+  BS_MOE_ROW = 7,       // MoE plan / scatter: a permuted row outside the permuted buffers
 };
 
 using DbgSetter = cudaError_t (*)(uint32_t*);

@@ -232,12 +232,13 @@ struct MoePlanParams {
   // kTileA2) for rows [shared_row0, shared_row0 + shared_rows) of the permuted
   // buffers (token t at row shared_row0 + t, row_scale 1); tile_rows >= 128
   int shared_rows, shared_row0;
+  int rs_rows;                      // rows of row_scale (the debug-bounds build checks every write)
 };
 cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st);
 // Copies quantized token rows (e4m3 + scale chunks) into permuted-row order;
 // shared_row0 >= 0 also copies token t to row shared_row0 + t.
 cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
-                        uint8_t* psf, int shared_row0, cudaStream_t st);
+                        uint8_t* psf, int shared_row0, int pq_rows, cudaStream_t st);
 
 // ----------------------------------------------------------- indexer.cu
 struct IdxParams {

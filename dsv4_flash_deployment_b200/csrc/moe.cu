@@ -254,7 +254,15 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
       p.tiles2[(size_t)(t0 + j) * mt2 + mt] = make_int4(kTileA2 | (mt * 128), p.shared_row0 + j * p.tile_rows,
                                                         min(p.tile_rows, p.shared_rows - j * p.tile_rows), mt * 128);
     }
-    for (int t = threadIdx.x; t < p.shared_rows; t += blockDim.x) p.row_scale[p.shared_row0 + t] = 1.f;
+    for (int t = threadIdx.x; t < p.shared_rows; t += blockDim.x) {
+#ifdef DSV4_DEBUG_BOUNDS
+      if (p.shared_row0 + t >= p.rs_rows) {
+        dbg_bad(BS_MOE_ROW);
+        break;
+      }
+#endif
+      p.row_scale[p.shared_row0 + t] = 1.f;
+    }
   }
   for (int sg = 0; sg < n_seg; ++sg) {
     const int c = p.seg_cnt ? min(p.seg_cnt[sg], p.seg_cap) : n;
@@ -264,6 +272,13 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(MoePlanParams p) {
       if (ok && e >= 0 && e < p.E_local) {
         const int row = start[e] + seg_row(p.rank[i], p.tile_rows);
         p.pos[i] = row;
+#ifdef DSV4_DEBUG_BOUNDS
+        if (row < 0 || row >= p.rs_rows) {
+          dbg_bad(BS_MOE_ROW);
+          p.pos[i] = -1;
+          continue;
+        }
+#endif
         p.row_scale[row] = p.wts[i];
       } else {
         p.pos[i] = -1;
@@ -286,7 +301,8 @@ cudaError_t moe_plan(const MoePlanParams& p, cudaStream_t st) {
 // One warp per (token, slot): 16-byte copies of the e4m3 row, then scale bytes;
 // with a shared segment, the warps of slot 0 also copy the token to its row there.
 __global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int T, int D,
-                                   int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf, int shared_row0) {
+                                   int topk, const int* __restrict__ pos, uint8_t* pq, uint8_t* psf, int shared_row0,
+                                   int pq_rows) {
   pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -299,6 +315,12 @@ __global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t
   for (int c = 0; c < 2; ++c) {
     const int row = rows[c];
     if (row < 0) continue;
+#ifdef DSV4_DEBUG_BOUNDS
+    if (row >= pq_rows) {
+      dbg_bad(BS_MOE_ROW);
+      continue;
+    }
+#endif
     uint4* dst = reinterpret_cast<uint4*>(pq + (size_t)row * D);
     for (int i = lane; i < D / 16; i += 32) dst[i] = src[i];
     for (int b = lane; b < D / 32; b += 32) psf[sf_chunk_offset(row, b, kt)] = xsf[sf_chunk_offset(t, b, kt)];
@@ -306,11 +328,11 @@ __global__ void moe_scatter_kernel(const uint8_t* __restrict__ xq, const uint8_t
 }
 
 cudaError_t moe_scatter(const uint8_t* xq, const uint8_t* xsf, int T, int D, int topk, const int* pos, uint8_t* pq,
-                        uint8_t* psf, int shared_row0, cudaStream_t st) {
+                        uint8_t* psf, int shared_row0, int pq_rows, cudaStream_t st) {
   const long long warps = (long long)T * topk;
   if (warps == 0) return cudaSuccess;
   launch_pdl(moe_scatter_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, xq, xsf, T, D, topk, pos, pq, psf,
-             shared_row0);
+             shared_row0, pq_rows);
   return cudaGetLastError();
 }
 
