@@ -92,10 +92,14 @@ class HostTable:
     def _device_addr(self, t: torch.Tensor, ext) -> int:
         st = t.untyped_storage()
         base = st.data_ptr()
-        if t.is_pinned():
-            return int(ext.host_device_ptr(base)) + (t.data_ptr() - base)
+        # our own registrations first: a registered range also reports is_pinned(),
+        # and a table that took it as pinned memory would hold no user count, so
+        # the release of another table over the same storage (a second model
+        # built from the same weights) would unregister it under this one
         reg = HostTable._registered.get(base)
         if reg is None:
+            if t.is_pinned():
+                return int(ext.host_device_ptr(base)) + (t.data_ptr() - base)
             reg = (int(ext.host_register(base, st.nbytes())), 0)
         HostTable._registered[base] = (reg[0], reg[1] + 1)
         self.storages.append(base)

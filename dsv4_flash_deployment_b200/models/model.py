@@ -275,8 +275,7 @@ class DSV4Model:
         ep_ok = self.ep is None or self.ep.transport == "fused"
         # Off by default: with the V4.1 tensor-parallel check's configuration (dim 1024,
         # 32 experts top-6, 120-token prefill, then 3-token decode) the merged model
-        # drifts from the separate one (logit cosine 0.988) and one traced run of it
-        # raised an illegal address; the cause is not found.  DSV4_MERGE_SHARED=1 turns it on.
+        # drifts from the separate one (logit cosine 0.988).  DSV4_MERGE_SHARED=1 turns it on.
         self.merge_shared = (os.environ.get("DSV4_MERGE_SHARED", "0") == "1" and si == I and self.tile_rows >= 128
                              and self.tp is None and ep_ok)
         self.shared_row0 = ceil_to(self.cap, 256)

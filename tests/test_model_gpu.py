@@ -150,7 +150,7 @@ def test_small_v41_engram_prefill_and_decode():
 
 
 @pytest.mark.skipif(os.environ.get("DSV4_MERGE_SHARED") != "1",
-                    reason="the merged shared expert is off by default (an unexplained fault); opt in with "
+                    reason="the merged shared expert is off by default (logit drift against the separate GEMMs); opt in with "
                            "DSV4_MERGE_SHARED=1")
 @pytest.mark.parametrize("family", ["v4", "v41"])
 def test_shared_expert_in_grouped_gemms_matches_separate(monkeypatch, family):
