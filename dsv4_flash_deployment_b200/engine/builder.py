@@ -23,7 +23,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
                 weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None,
                 ep=None, tp=None, experts_from: DSV4Model | None = None, kv_block: int = 0,
                 kv_pool_tokens: int = 0, engram_from: DSV4Model | None = None,
-                engram_shm: str | None = None, engram_token_map=None) -> DSV4Model:
+                engram_shm: str | None = None, engram_token_map=None,
+                merge_shared: bool | None = None) -> DSV4Model:
     """Builds the backbone.
 
     ``weights``: checkpoint dict (names of the reference checkpoint); None draws
@@ -44,6 +45,9 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
     random-init Engram tables in shared files with this prefix (one copy per node).
     ``engram_token_map``: the tokenizer's compressed token map for the Engram
     hashes (``ref.engram.compressed_token_map``; None: ``id % C``).
+    ``merge_shared``: the shared expert's tiles ride in the routed experts' grouped
+    GEMMs where the layout allows it (None: ``DSV4_MERGE_SHARED``, default on;
+    False: two separate dense GEMMs).
     """
     dev = torch.device(device)
     if tp is not None and ep is not None:
@@ -85,7 +89,8 @@ def build_model(cfg, device="cuda", max_tokens: int = 512, n_slots: int = 16, ma
             tp.shard_layer(cfg, L)
         head = tp.shard_head(head, cfg.vocab_size)
     model = DSV4Model(cfg, layers, embed, head, norm, max_tokens, n_slots, max_seq_len, dev, ep=ep,
-                      head_vocab=cfg.vocab_size, tp=tp, kv_block=kv_block, kv_pool_tokens=kv_pool_tokens)
+                      head_vocab=cfg.vocab_size, tp=tp, kv_block=kv_block, kv_pool_tokens=kv_pool_tokens,
+                      merge_shared=merge_shared)
     if cfg.engram_layer_ids and engram_from is not None:
         eg = engram_from.engram
         if eg is None or eg.ring.shape[0] < n_slots + 1 or eg.rows.shape[0] < max_tokens:

@@ -72,12 +72,18 @@ def main(argv=None):
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     cfg = small_cfg()
     w = make_random_weights(cfg, seed=11, include_mtp=False)
-    ref = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512, weights=w)
+    refs = {}   # one-GPU reference per shared-expert form (merged into the grouped GEMMs or not)
     ok = True
     results = {}
     for transport in a.transports.split(","):
         ep = EPGroup(rank, world, dist.group.WORLD, dev, transport=transport)
         m = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512, weights=w, ep=ep)
+        # compare against the same rounding: the fused transport carries the shared
+        # expert in its grouped GEMMs, the NCCL / p2p exchanges run it separately
+        if m.merge_shared not in refs:
+            refs[m.merge_shared] = build_model(cfg, dev, max_tokens=512, n_slots=a.seqs, max_seq_len=512,
+                                               weights=w, merge_shared=m.merge_shared)
+        ref = refs[m.merge_shared]
         worst, agree, total = 1.0, 0, 0
         for s in range(a.steps):
             meta = _meta(cfg, rank, s, a.seqs, a.plen)

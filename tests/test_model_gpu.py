@@ -11,7 +11,6 @@ position may dip where bf16-rounded indexer scores nearly tie and one pick
 flips (>= 0.97).
 """
 
-import os
 
 import pytest
 import torch
@@ -149,31 +148,52 @@ def test_small_v41_engram_prefill_and_decode():
     assert agree >= 0.8, agree
 
 
-@pytest.mark.skipif(os.environ.get("DSV4_MERGE_SHARED") != "1",
-                    reason="the merged shared expert is off by default (logit drift against the separate GEMMs); opt in with "
-                           "DSV4_MERGE_SHARED=1")
+def _steps(model, cfg, seqs, plen):
+    """Prefill ``plen`` tokens of every sequence, then one token per step; the
+    sampled logits keyed by (sequence, position)."""
+    got, pos = {}, [0] * len(seqs)
+    while any(p < len(s) for p, s in zip(pos, seqs)):
+        chunks = [(i, SeqChunk(i, pos[i], s[pos[i]:pos[i] + (plen if pos[i] == 0 else 1)], True))
+                  for i, s in enumerate(seqs) if pos[i] < len(s)]
+        meta = StepMeta(cfg, [c for _, c in chunks])
+        model.upload(meta)
+        model.forward(meta)
+        torch.cuda.synchronize()
+        ErrorWord.check("cuda")
+        lg = model.logits[: len(chunks), : cfg.vocab_size].float().cpu()
+        for row, (i, c) in enumerate(chunks):
+            pos[i] = c.start_pos + len(c.tokens)
+            got[(i, pos[i] - 1)] = lg[row]
+    return got
+
+
 @pytest.mark.parametrize("family", ["v4", "v41"])
-def test_shared_expert_in_grouped_gemms_matches_separate(monkeypatch, family):
+def test_shared_expert_in_grouped_gemms_matches_separate(family):
     """The shared expert riding in the routed experts' grouped GEMMs (second weight
     operand, rows after the routed ones; V4.1: MXFP8 shared tiles beside MXFP4
-    experts) against the separate dense shared-expert GEMMs: same logits up to
-    fp32 summation order (split-K vs one pass)."""
+    experts) against the separate dense shared-expert GEMMs, both against the fp32
+    oracle: the two forms round differently (one K pass vs split-K before the
+    MXFP8 hidden), which V4 absorbs (same logits) and the V4.1 random model
+    amplifies through near-tied indexer picks, so there the bar is the oracle:
+    the merged form agrees with it as well as the separate one does."""
     torch.manual_seed(4)
     cfg = small_v4() if family == "v4" else small_v41()
     w = make_random_weights(cfg, seed=3)
-    seq = torch.randint(0, cfg.vocab_size, (40,)).tolist()
-    out = {}
-    for flag in ("1", "0"):
-        monkeypatch.setenv("DSV4_MERGE_SHARED", flag)
-        model = build_model(cfg, "cuda", max_tokens=64, n_slots=2, max_seq_len=64, weights=w)
-        assert model.merge_shared == (flag == "1")
-        rows = []
-        for meta in (StepMeta(cfg, [SeqChunk(0, 0, seq[:33], True)]), StepMeta(cfg, [SeqChunk(0, 33, seq[33:34], True)])):
-            model.upload(meta)
-            model.forward(meta)
-            torch.cuda.synchronize()
-            ErrorWord.check("cuda")
-            rows.append(model.logits[0, : cfg.vocab_size].float().cpu())
-        out[flag] = torch.stack(rows)
-    c = _cos(out["1"], out["0"])
-    assert float(c.min()) > 0.9999, c
+    seqs = [torch.randint(16, cfg.vocab_size, (44,)).tolist() for _ in range(3)]
+    ref = _oracle_logits(cfg, w, seqs, 128)
+    out, stats = {}, {}
+    for merged in (True, False):
+        model = build_model(cfg, "cuda", max_tokens=128, n_slots=4, max_seq_len=128, weights=w, merge_shared=merged)
+        assert model.merge_shared == merged
+        out[merged] = _steps(model, cfg, seqs, 36)
+        cs = torch.stack([_cos(lg, ref[i][p]) for (i, p), lg in out[merged].items()])
+        top1 = sum(int(lg.argmax() == ref[i][p].argmax()) for (i, p), lg in out[merged].items()) / len(cs)
+        stats[merged] = (float(cs.min()), float(cs.mean()), top1)
+        del model
+    (w_m, m_m, t_m), (w_s, m_s, t_s) = stats[True], stats[False]
+    assert m_m >= m_s - 0.002 and w_m >= 0.97 and t_m >= t_s - 0.05, stats
+    between = torch.stack([_cos(out[True][k], out[False][k]) for k in out[True]])
+    if family == "v4":
+        assert float(between.min()) > 0.9999, between
+    else:
+        assert float(between.mean()) > 0.995, between
