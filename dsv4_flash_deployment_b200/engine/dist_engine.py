@@ -8,7 +8,7 @@ model step, so all ranks step in lockstep.  Per step:
   all      apply the adds/cancels to the local scheduler; if any rank has
            work, run a real step (or a 1-token dummy step on a reserved slot
            when this rank has none, to join the step's collectives)
-  all      gather     [(request id, token, finished, reason)] -> rank 0
+  all      gather     [(request id, token, finished, reason, logprob)] -> rank 0
 
 Rank 0 assigns new requests to the rank with the fewest live requests.  In the
 replicated mode (tensor-parallel layout) every request goes to every rank: the
@@ -48,6 +48,7 @@ class GlobalRequest:
     t_arrival: float = field(default_factory=time.perf_counter)
     t_first_token: float | None = None
     t_done: float | None = None
+    logprobs: list = field(default_factory=list)   # per token when the request asked for them
 
 
 class _SchedView:
@@ -87,9 +88,10 @@ class _SchedView:
 
 def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int, replicated: bool = False) -> list[tuple]:
     """Applies a control message to this rank's engine and runs its part of the step."""
-    for gid, r, prompt, mt, ignore_eos, stop_ids, temperature in msg["adds"]:
+    for gid, r, prompt, mt, ignore_eos, stop_ids, temperature, extra in msg["adds"]:
         if r == rank or r == -1:
-            req = engine.add_request(prompt, mt, ignore_eos=ignore_eos, stop_ids=stop_ids, temperature=temperature)
+            req = engine.add_request(prompt, mt, ignore_eos=ignore_eos, stop_ids=stop_ids, temperature=temperature,
+                                     **extra)
             id_map[req.req_id] = gid
             id_map[("g", gid)] = req
     for gid in msg["cancels"]:
@@ -107,13 +109,14 @@ def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int, repli
     out = []
     for req, tok in events:
         gid = id_map.get(req.req_id)
-        out.append((gid, tok, req.finished, req.finish_reason))
+        lp = req.logprobs[len(req.output) - 1] if tok is not None and req.logprobs else None
+        out.append((gid, tok, req.finished, req.finish_reason, lp))
     # requests finished without an event this step (cancelled before scheduling)
     for key in [k for k in id_map if isinstance(k, tuple)]:
         req = id_map[key]
         if req.finished:
             if not any(e[0] == key[1] for e in out):
-                out.append((key[1], None, True, req.finish_reason))
+                out.append((key[1], None, True, req.finish_reason, None))
             del id_map[key]
             id_map.pop(req.req_id, None)
     if replicated and rank != 0:
@@ -143,11 +146,12 @@ class DistributedEngine:
         self.eos_id = local_engine.eos_id
 
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
-                    stop_ids=(), temperature: float = 0.0) -> GlobalRequest:
+                    stop_ids=(), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                    logprobs: int | None = None) -> GlobalRequest:
         if not prompt:
             raise ValueError("empty prompt")
-        if temperature < 0:
-            raise ValueError("temperature must be >= 0")
+        # checked here, on rank 0, so that no rank is sent a request its engine refuses
+        sp = self.local.sampling_params(temperature, top_k, top_p, logprobs)
         if len(prompt) + max_new_tokens > self.local.sched.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.local.sched.max_seq_len}")
@@ -156,7 +160,9 @@ class DistributedEngine:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds the paged cache pool")
         r = -1 if self.replicated else min(range(self.world), key=lambda i: self.load[i])
         g = GlobalRequest(self.next_id, r, list(prompt), max_new_tokens)
-        g._opts = (bool(ignore_eos), tuple(stop_ids), float(temperature))
+        extra = {} if not (sp.top_k or sp.top_p < 1.0 or sp.wants_logprobs) else \
+            {"top_k": sp.top_k, "top_p": sp.top_p, "logprobs": sp.logprobs}
+        g._opts = (bool(ignore_eos), tuple(stop_ids), sp.temperature, extra)
         self.next_id += 1
         self.load[r] += 1
         self.pending_adds.append(g)
@@ -177,12 +183,14 @@ class DistributedEngine:
         now = time.perf_counter()
         events = []
         for evs in gathered:
-            for gid, tok, fin, reason in evs or []:
+            for gid, tok, fin, reason, lp in evs or []:
                 g = self.live.get(gid)
                 if g is None:
                     continue
                 if tok is not None:
                     g.output.append(int(tok))
+                    if lp is not None:
+                        g.logprobs.append(lp)
                     if g.t_first_token is None:
                         g.t_first_token = now
                 if fin:

@@ -25,6 +25,7 @@ import numpy as np
 import torch
 
 from ..models.model import DSV4Model, SeqChunk, StepMeta
+from ..models.sampling import SamplingParams, logprob_entries
 from ..ops.gemm import ErrorWord
 from .scheduler import Request, Scheduler
 
@@ -76,21 +77,47 @@ class Engine:
 
     # ------------------------------------------------------------------- API
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
-                    stop_ids: Iterable[int] = (), temperature: float = 0.0) -> Request:
-        """``temperature`` 0 decodes greedily; > 0 samples softmax(logits / T)."""
-        if temperature < 0:
-            raise ValueError("temperature must be >= 0")
+                    stop_ids: Iterable[int] = (), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                    logprobs: int | None = None) -> Request:
+        """``temperature`` 0 decodes greedily; > 0 samples softmax(logits / T),
+        restricted to the ``top_k`` most likely tokens (0: all) and to the top-p
+        nucleus (``top_p`` 1.0: all).  ``logprobs`` n >= 0: every generated token
+        also carries its log-probability and the n most likely alternatives
+        (``Request.logprobs``), from the raw logits."""
+        sp = self.sampling_params(temperature, top_k, top_p, logprobs)
         return self.sched.add(prompt, max_new_tokens, ignore_eos=ignore_eos, eos_id=self.eos_id,
-                              stop_ids=tuple(stop_ids), temperature=float(temperature))
+                              stop_ids=tuple(stop_ids), temperature=sp.temperature, top_k=sp.top_k, top_p=sp.top_p,
+                              want_logprobs=sp.logprobs)
+
+    def sampling_params(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                        logprobs: int | None = None) -> SamplingParams:
+        """Checked decoding rule of a request (ValueError when this engine cannot
+        apply it: top-k / top-p / log-probabilities need the whole vocabulary's
+        logits on one GPU, so the vocab-parallel head refuses them)."""
+        sp = SamplingParams(float(temperature), int(top_k or 0), float(1.0 if top_p is None else top_p),
+                            None if logprobs is None else int(logprobs))
+        if (sp.filters or sp.wants_logprobs) and getattr(self.model, "tp", None) is not None:
+            raise ValueError("top_k / top_p / logprobs are not supported with the tensor-parallel (vocab-parallel) head")
+        return sp
 
     def step(self) -> list[tuple[Request, int | None]]:
         chunks = self.sched.schedule()
         if not chunks:
             return []
         meta = StepMeta(self.cfg, [SeqChunk(c.req.slot, c.start_pos, c.tokens, c.sample,
-                                            temperature=c.req.temperature) for c in chunks])
+                                            temperature=c.req.temperature, top_k=c.req.top_k, top_p=c.req.top_p,
+                                            logprobs=c.req.want_logprobs) for c in chunks])
         ids = self.run_meta(meta)
+        if meta.want_lp:
+            it = iter(self.last_logprobs)
+            for c in chunks:
+                if c.sample:
+                    e = next(it)
+                    if e is not None:
+                        c.req.logprobs.append(e)
         return self.sched.commit(chunks, ids)
+
+    last_logprobs: list = []   # per sampled row of the last step that asked for log-probabilities
 
     _trace_left: int | None = None
 
@@ -105,6 +132,11 @@ class Engine:
         else:
             out = self._run_device(meta)
             host = out
+        if meta.want_lp:
+            n = len(host)
+            m = self.model
+            self.last_logprobs = logprob_entries(m.lp_chosen[:n].tolist(), m.lp_vals[:n].tolist(),
+                                                 m.lp_ids[:n].tolist(), meta.lp_want[:n])
         self.stats["steps"] += 1
         self.stats["tokens"] += meta.T
         self.stats["last_T"] = meta.T

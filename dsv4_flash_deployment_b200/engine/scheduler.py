@@ -29,6 +29,9 @@ class Request:
     eos_id: int | None = None
     stop_ids: tuple[int, ...] = ()
     temperature: float = 0.0          # 0 = greedy
+    top_k: int = 0                    # 0 = off
+    top_p: float = 1.0                # 1.0 = off
+    want_logprobs: int | None = None  # alternatives per generated token (None: no log-probabilities)
     slot: int = -1
     n_prefilled: int = 0
     output: list[int] = field(default_factory=list)
@@ -38,6 +41,8 @@ class Request:
     t_first_token: float | None = None
     t_done: float | None = None
     cancelled: bool = False
+    # per generated token when ``want_logprobs`` is set: {"logprob": lp, "top": [(id, lp), ...]}
+    logprobs: list = field(default_factory=list)
 
     @property
     def prompt_done(self) -> bool:

@@ -37,6 +37,7 @@ from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxW
 from ..ops.layout import ceil_to
 from ..ref import numerics as N
 from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
+from .sampling import LOGPROB_TOP_N, chosen_logprob, gumbel_, logprob_top, top_k_top_p_mask_
 from .weights import LayerW
 
 ROUTER_SMALL_T = 4   # steps of at most this many tokens route with csrc/moe.cu router_small
@@ -53,6 +54,9 @@ class SeqChunk:
     sample: bool = True        # produce logits for the last token of the chunk
     sample_all: bool = False   # produce logits for every token (speculative verify, draft blocks)
     temperature: float = 0.0   # > 0: sample the next token (Gumbel-max) instead of the argmax
+    top_k: int = 0             # > 0: sample among the k most likely tokens only (temperature > 0)
+    top_p: float = 1.0         # < 1: sample within the top-p nucleus only (temperature > 0)
+    logprobs: int | None = None  # n >= 0: also return the sampled token's log-probability and n alternatives
 
 
 class StepMeta:
@@ -90,6 +94,15 @@ class StepMeta:
         per_chunk = np.where(sall, lens, samp.astype(np.int64))
         self.temps = np.repeat(temps, per_chunk).astype(np.float32)
         self.sampling = bool((self.temps > 0).any())
+        # top-k / top-p per sampled row (0 / 1.0: off); they only act on rows with T > 0
+        topk = np.fromiter((c.top_k for c in chunks), np.int32, n)
+        topp = np.fromiter((c.top_p for c in chunks), np.float32, n)
+        self.topk = np.repeat(topk, per_chunk).astype(np.int32)
+        self.topp = np.repeat(topp, per_chunk).astype(np.float32)
+        self.filtering = bool(((self.temps > 0) & ((self.topk > 0) | (self.topp < 1.0))).any())
+        # alternatives wanted per sampled row (None: no log-probabilities)
+        self.lp_want = [c.logprobs for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
+        self.want_lp = any(w is not None for w in self.lp_want)
         self.max_pos = int(self.pos.max()) if T else 0
         # compressor groups closed in this step, per ratio (token order)
         self.groups = {}
@@ -122,7 +135,7 @@ class StepMeta:
         sampled rows, chunk-count bucket, indexer bypass per ratio, sampling) and
         nothing else, so steps of different batch compositions share a graph."""
         return (self.T, len(self.sample_rows), self.chunk_bound,
-                tuple(self.index_bypass(r) for r in self.groups), self.sampling)
+                tuple(self.index_bypass(r) for r in self.groups), self.sampling, self.filtering, self.want_lp)
 
     def padded(self, max_tokens: int, max_sample: int, pad_slot: int) -> "StepMeta":
         """This step padded to bucketed shapes (:func:`token_bucket`): a padding chunk
@@ -140,6 +153,9 @@ class StepMeta:
             extra = S_b - S
             m.sample_rows = np.concatenate([m.sample_rows, np.full(extra, m.sample_rows[0] if S else 0, np.int32)])
             m.temps = np.concatenate([m.temps, np.zeros(extra, np.float32)])
+            m.topk = np.concatenate([m.topk, np.zeros(extra, np.int32)])
+            m.topp = np.concatenate([m.topp, np.ones(extra, np.float32)])
+            m.lp_want = m.lp_want + [None] * extra
         m.n_out = S
         return m
 
@@ -308,6 +324,12 @@ class DSV4Model:
         self.logits = e(self.max_sample, self.head.shape[0], dt=f32)
         self.next_ids = e(self.max_sample, dt=i32)
         self.m_temp = z(self.max_sample, dt=f32)
+        self.m_topk = z(self.max_sample, dt=i32)
+        self.m_topp = torch.ones(self.max_sample, dtype=f32, device=dev)
+        # log-probabilities of the sampled rows (written only by steps that ask for them)
+        self.lp_chosen = z(self.max_sample, dt=f32)
+        self.lp_vals = z(self.max_sample, LOGPROB_TOP_N, dt=f32)
+        self.lp_ids = z(self.max_sample, LOGPROB_TOP_N, dt=i32)
         # multi-CTA argmax: partials [2 * max(S, 296)] + zeroed per-row counters at the end
         self.argmax_scratch = z(2 * max(self.max_sample, 296) + self.max_sample, dt=i32)
         if self.tp is not None:
@@ -403,6 +425,9 @@ class DSV4Model:
         put(self.m_sample, m.sample_rows.astype(np.int64))
         if m.sampling:
             put(self.m_temp, m.temps)
+        if m.filtering:
+            put(self.m_topk, m.topk)
+            put(self.m_topp, m.topp)
         for r, g in m.groups.items():
             for dst, arr in zip(self.m_groups[r], g):
                 if len(arr):
@@ -541,10 +566,22 @@ class DSV4Model:
         with self._t("head"):
             torch.index_select(self.u[:T], 0, self.m_sample[:S], out=self.u_sample[:S])
             self._gemm_bf16(self.u_sample[:S], self.head, self.logits[:S], S, f32_out=True)
+            if (m.filtering or m.want_lp) and self.tp is not None:
+                raise NotImplementedError("top-k / top-p / log-probabilities with the vocab-parallel head")
+            if m.want_lp:
+                raw = self._raw_logits(S)
+                n_top = min(LOGPROB_TOP_N, self.vocab)
+                lse, vals, ids = logprob_top(raw, n_top)
+                self.lp_vals[:S, :n_top].copy_(vals)
+                self.lp_ids[:S, :n_top].copy_(ids)
+            if m.filtering:
+                top_k_top_p_mask_(self.logits[:S, :self.vocab], self.m_temp[:S], self.m_topk[:S], self.m_topp[:S])
             if m.sampling:
                 self._gumbel(S)
             if self.tp is None:
                 ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch, None, 0)
+                if m.want_lp:
+                    self.lp_chosen[:S].copy_(chosen_logprob(raw, self.next_ids[:S], lse))
             else:
                 # vocab-parallel head: best (value, index) of this shard, then the merge over ranks
                 tp = self.tp
@@ -565,12 +602,22 @@ class DSV4Model:
         noise of its own rows and the cross-rank merge keeps the best."""
         if self._gnoise is None:   # first sampling step runs eagerly, before any capture of it
             self._gnoise = torch.empty_like(self.logits)
-        g = self._gnoise[:S]
-        g.uniform_(1e-20, 1.0 - 1e-7)
-        g.log_().neg_().log_().neg_()
-        self.logits[:S].addcmul_(self.m_temp[:S, None], g)
+        gumbel_(self.logits[:S], self.m_temp[:S], self._gnoise[:S])
 
     _gnoise = None
+
+    def _raw_logits(self, S: int) -> torch.Tensor:
+        """Copy of the sampled rows' raw logits (the real vocabulary columns), kept for
+        the log-probabilities while filtering and noise change ``logits`` in place.
+        Allocated by the first step that asks for log-probabilities (an eager step:
+        a step shape's first run precedes its capture)."""
+        if self._lp_raw is None:
+            self._lp_raw = torch.empty(self.max_sample, self.vocab, dtype=torch.float32, device=self.dev)
+        raw = self._lp_raw[:S]
+        raw.copy_(self.logits[:S, :self.vocab])
+        return raw
+
+    _lp_raw = None
 
     # ------------------------------------------------- deferred ring commits
     _defer = False

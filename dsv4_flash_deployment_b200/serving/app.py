@@ -14,9 +14,14 @@ scripts/benchmark_sweep.py:70-125``):
 
 Decoding: ``temperature`` 0 (the default when the field is absent, and what
 every reference benchmark sends) is greedy; ``temperature`` > 0 samples
-softmax(logits / T) on the device by the Gumbel-max rule.  ``top_p`` / ``top_k``
-other than their neutral values (1.0 / -1 or 0), ``n`` / ``best_of`` > 1 and
-``logprobs`` are refused with 400.
+softmax(logits / T) on the device by the Gumbel-max rule, restricted by
+``top_k`` (> 0) and ``top_p`` (< 1) when given.  ``logprobs`` (completions: the
+number of alternatives, 0-20; chat: ``logprobs: true`` with ``top_logprobs``
+0-20) returns each generated token's log-probability under the raw logits and
+its most likely alternatives, in the OpenAI response layouts.  ``n`` /
+``best_of`` > 1 are refused with 400, and so is any request the engine cannot
+serve (top-k / top-p / logprobs on the tensor-parallel head, logprobs or
+temperature under speculative decoding).
 Streaming sends one SSE event per generated token and ends with
 ``data: [DONE]``; a client that disconnects cancels its request.
 
@@ -32,6 +37,7 @@ import uuid
 
 from aiohttp import web
 
+from ..models.sampling import SamplingParams
 from .engine_loop import EngineLoop, GenParams
 
 
@@ -60,7 +66,7 @@ def _prompt_ids(st: ServerState, body: dict, chat: bool) -> list[int]:
     return st.tok.encode(str(p), add_bos=True)
 
 
-def _params(st: ServerState, body: dict, n_prompt: int) -> tuple[GenParams, list[str]]:
+def _params(st: ServerState, body: dict, n_prompt: int, chat: bool = False) -> tuple[GenParams, list[str]]:
     mt = body.get("max_completion_tokens") or body.get("max_tokens") or body.get("max_new_tokens") or 256
     mt = int(mt)
     if mt < 1:
@@ -82,14 +88,53 @@ def _params(st: ServerState, body: dict, n_prompt: int) -> tuple[GenParams, list
         if body.get(key) is not None and int(body[key]) != 1:
             raise web.HTTPBadRequest(text=json.dumps({"error": f"{key} > 1 is not supported (one choice per request)"}),
                                      content_type="application/json")
-    if body.get("logprobs") not in (None, False, 0) or body.get("top_logprobs"):
-        raise web.HTTPBadRequest(text=json.dumps({"error": "logprobs are not supported"}),
-                                 content_type="application/json")
-    top_p, top_k = body.get("top_p"), body.get("top_k")
-    if (top_p is not None and float(top_p) < 1.0) or (top_k is not None and int(top_k) > 0):
-        raise web.HTTPBadRequest(text=json.dumps({"error": "top_p / top_k sampling is not supported"}),
-                                 content_type="application/json")
-    return GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids, temp), [s for s in stop if s]
+    try:
+        top_p = 1.0 if body.get("top_p") is None else float(body["top_p"])
+        top_k = 0 if body.get("top_k") is None else int(body["top_k"])
+        lp = _logprobs_field(body, chat)
+        sp = SamplingParams(temp, max(top_k, 0), top_p, lp)     # top_k -1 (vLLM's "off") counts as 0
+    except (TypeError, ValueError) as e:
+        raise web.HTTPBadRequest(text=json.dumps({"error": str(e)}), content_type="application/json") from None
+    return (GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids, temp, sp.top_k, sp.top_p, sp.logprobs),
+            [s for s in stop if s])
+
+
+def _logprobs_field(body: dict, chat: bool) -> int | None:
+    """Alternatives per token the request asks for (None: no log-probabilities).
+    Chat: ``logprobs`` is a switch and ``top_logprobs`` the count; completions:
+    ``logprobs`` is the count."""
+    if chat:
+        if not body.get("logprobs"):
+            if body.get("top_logprobs"):
+                raise ValueError("top_logprobs needs logprobs: true")
+            return None
+        return int(body.get("top_logprobs") or 0)
+    v = body.get("logprobs")
+    if v is None or v is False:
+        return None
+    return int(v)
+
+
+def _lp_entry(st: "ServerState", piece: str, lp: dict, chat: bool):
+    """One token's log-probability record in the chat layout (the completions
+    layout is assembled from the same values by :func:`_completion_logprobs`)."""
+    alts = [(st.tok.decode_token(t), v) for t, v in lp["top"]]
+    if chat:
+        return {"token": piece, "logprob": lp["logprob"], "bytes": list(piece.encode("utf-8")),
+                "top_logprobs": [{"token": a, "logprob": v, "bytes": list(a.encode("utf-8"))} for a, v in alts]}
+    return piece, lp["logprob"], alts
+
+
+def _completion_logprobs(entries: list, offset0: int) -> dict:
+    tokens, lps, tops, offs = [], [], [], []
+    off = offset0
+    for piece, v, alts in entries:
+        tokens.append(piece)
+        lps.append(v)
+        tops.append({a: w for a, w in alts})
+        offs.append(off)
+        off += len(piece)
+    return {"tokens": tokens, "token_logprobs": lps, "top_logprobs": tops, "text_offset": offs}
 
 
 def _err(code: int, msg: str) -> web.Response:
@@ -103,7 +148,7 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
         return _err(400, f"invalid JSON: {e}")
     try:
         ids = _prompt_ids(st, body, chat)
-        params, stops = _params(st, body, len(ids))
+        params, stops = _params(st, body, len(ids), chat)
     except web.HTTPBadRequest as e:
         return web.Response(status=400, text=e.text, content_type="application/json")
     if not st.loop.healthy:
@@ -115,16 +160,22 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
     out_ids: list[int] = []
     text = ""
     finish = None
+    want_lp = params.logprobs is not None
+    lp_entries: list = []        # per emitted token (chat records, or (piece, lp, alts) for completions)
 
-    def chunk_obj(piece: str | None, fin: str | None) -> dict:
+    def chunk_obj(piece: str | None, fin: str | None, lpe=None) -> dict:
         if chat:
             delta = {} if piece is None else {"content": piece}
             if piece is not None and not out_ids[:-1]:
                 delta["role"] = "assistant"
+            ch = {"index": 0, "delta": delta, "finish_reason": fin}
+            if want_lp:
+                ch["logprobs"] = {"content": [lpe]} if lpe is not None else None
             return {"id": rid, "object": "chat.completion.chunk", "created": created, "model": st.model_name,
-                    "choices": [{"index": 0, "delta": delta, "finish_reason": fin}]}
+                    "choices": [ch]}
+        lpo = _completion_logprobs([lpe], len(text) - len(piece or "")) if lpe is not None else None
         return {"id": rid, "object": "text_completion", "created": created, "model": st.model_name,
-                "choices": [{"index": 0, "text": piece or "", "finish_reason": fin, "logprobs": None}]}
+                "choices": [{"index": 0, "text": piece or "", "finish_reason": fin, "logprobs": lpo}]}
 
     resp = None
     if stream:
@@ -142,7 +193,7 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
             if kind == "done":
                 finish = "stop" if val == "stop" else ("length" if val == "length" else val)
                 break
-            tok = int(val)
+            tok, lp = int(val[0]), val[1]
             out_ids.append(tok)
             if tok == st.tok.eos_token_id and not params.ignore_eos:
                 continue
@@ -154,8 +205,11 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
                     piece = cand[:hit][len(text):]
                     text = cand[:hit]
                     st.loop.cancel(ts)
+                    lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None and piece) else None
+                    if lpe is not None:
+                        lp_entries.append(lpe)
                     if resp is not None and piece:
-                        await resp.write(f"data: {json.dumps(chunk_obj(piece, None))}\n\n".encode())
+                        await resp.write(f"data: {json.dumps(chunk_obj(piece, None, lpe))}\n\n".encode())
                     finish = "stop"
                     # drain until the engine confirms the cancel
                     while True:
@@ -163,9 +217,12 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
                         if k2 in ("done", "error"):
                             break
                     break
+            lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None) else None
+            if lpe is not None:
+                lp_entries.append(lpe)
             text += piece
             if resp is not None:
-                await resp.write(f"data: {json.dumps(chunk_obj(piece, None))}\n\n".encode())
+                await resp.write(f"data: {json.dumps(chunk_obj(piece, None, lpe))}\n\n".encode())
     except (asyncio.CancelledError, ConnectionResetError):
         st.loop.cancel(ts)
         raise
@@ -179,9 +236,12 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
         return resp
     if chat:
         choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish}
+        if want_lp:
+            choice["logprobs"] = {"content": lp_entries}
         obj = "chat.completion"
     else:
-        choice = {"index": 0, "text": text, "finish_reason": finish, "logprobs": None}
+        choice = {"index": 0, "text": text, "finish_reason": finish,
+                  "logprobs": _completion_logprobs(lp_entries, 0) if want_lp else None}
         obj = "text_completion"
     req = ts.req
     metrics = {"ttft_s": (req.t_first_token - req.t_arrival) if req and req.t_first_token else None,

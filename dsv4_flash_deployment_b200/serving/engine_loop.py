@@ -31,6 +31,9 @@ class GenParams:
     ignore_eos: bool = False
     stop_ids: tuple[int, ...] = ()
     temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    logprobs: int | None = None     # alternatives per token (None: no log-probabilities)
 
 
 @dataclass
@@ -99,9 +102,14 @@ class EngineLoop:
                     s.put(("error", f"engine unhealthy: {self.error}"))
                     continue
                 try:
+                    # the filtering / log-probability options only when asked for, so an
+                    # engine front that does not take them still serves the rest
+                    kw = {}
+                    if p.top_k or p.top_p < 1.0 or p.logprobs is not None:
+                        kw = {"top_k": p.top_k, "top_p": p.top_p, "logprobs": p.logprobs}
                     req = eng.add_request(prompt, p.max_tokens, ignore_eos=p.ignore_eos, stop_ids=p.stop_ids,
-                                          temperature=p.temperature)
-                except ValueError as e:
+                                          temperature=p.temperature, **kw)
+                except (ValueError, TypeError) as e:
                     s.put(("error", str(e)))
                     continue
                 s.req = req
@@ -162,7 +170,9 @@ class EngineLoop:
                     self.stats["generated_tokens"] += 1
                     if len(req.output) == 1:
                         self.ttft_window.append(time.perf_counter() - s.t_submit)
-                    s.put(("token", tok))
+                    lps = getattr(req, "logprobs", None)
+                    lp = lps[len(req.output) - 1] if lps and len(lps) >= len(req.output) else None
+                    s.put(("token", (tok, lp)))
             # finished (length / stop / cancelled) requests
             for rid in [rid for rid, s in self._live.items() if s.req.finished]:
                 s = self._live.pop(rid)

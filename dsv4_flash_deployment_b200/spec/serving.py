@@ -77,9 +77,12 @@ class SpecServingEngine:
         spec.open_rows()
 
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
-                    stop_ids=(), temperature: float = 0.0) -> Request:
+                    stop_ids=(), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                    logprobs: int | None = None) -> Request:
         if temperature > 0:
             raise ValueError("speculative decoding (DSpark) decodes greedily; temperature > 0 is not supported")
+        if logprobs is not None:
+            raise ValueError("speculative decoding (DSpark) does not return logprobs")
         if not prompt:
             raise ValueError("empty prompt")
         if len(prompt) + max_new_tokens + self.spec.blk > self.max_seq_len:

@@ -224,9 +224,9 @@ def test_temperature_sampling_and_refusals(served):
             r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 8, "ignore_eos": True,
                                                       "temperature": 5.0, "top_p": 1.0})
             hot.append(await r.json())
-        bad = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "top_p": 0.9})
+        bad = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "top_p": 1.5})
         neg = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "temperature": -1})
-        for extra in ({"n": 2}, {"best_of": 3}, {"logprobs": 5}):
+        for extra in ({"n": 2}, {"best_of": 3}, {"logprobs": 21}, {"top_p": 0}, {"top_k": "x"}):
             r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, **extra})
             assert r.status == 400, extra
         ok = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "n": 1, "logprobs": None})
@@ -240,3 +240,51 @@ def test_temperature_sampling_and_refusals(served):
     # a near-flat random-init distribution at T=5: three samples of 8 tokens are not all the greedy text
     assert any(t != g["choices"][0]["text"] for t in texts)
     assert bad == 400 and neg == 400
+
+
+def test_logprobs_and_nucleus_sampling(served):
+    """Completions and chat return per-token log-probabilities in the OpenAI
+    layouts; the greedy token's log-probability is its top alternative's and
+    equals log_softmax of the oracle logits; top-k 1 at any temperature decodes
+    greedily, and top-p / top-k samples stay within their sets."""
+    st, eng = served
+    ids = [0] + [40 + (3 * i) % 150 for i in range(25)]
+    want = _greedy(eng, ids, 5)
+
+    async def go(c):
+        comp = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 5, "ignore_eos": True,
+                                                             "logprobs": 3})).json()
+        chat = await (await c.post("/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "hi"}], "max_tokens": 4, "ignore_eos": True,
+            "logprobs": True, "top_logprobs": 2})).json()
+        k1 = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 5, "ignore_eos": True,
+                                                           "temperature": 3.0, "top_k": 1})).json()
+        streamed = []
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 3, "ignore_eos": True,
+                                                  "logprobs": 1, "stream": True})
+        async for raw in r.content:
+            line = raw.decode().strip()
+            if line.startswith("data: {"):
+                streamed.append(json.loads(line[6:]))
+        return comp, chat, k1, streamed
+    comp, chat, k1, streamed = _run(st, go)
+    tok = st.tok
+    lp = comp["choices"][0]["logprobs"]
+    assert lp["tokens"] == [tok.decode_token(t) for t in want]
+    assert len(lp["token_logprobs"]) == 5 and all(len(d) <= 3 for d in lp["top_logprobs"])
+    assert lp["text_offset"][0] == 0
+    for piece, v, tops in zip(lp["tokens"], lp["token_logprobs"], lp["top_logprobs"]):
+        assert v <= 0 and abs(max(tops.values()) - v) < 1e-5 and tops.get(piece) is not None
+    # the first token's value against the oracle's own logits
+    ref = RefModel(eng.cfg, eng.model.ref.w, max_seq_len=256)
+    st0 = ref.new_state(1)
+    for t in ids:
+        logits, _ = ref.step(torch.tensor([t]), st0)
+    lsm = torch.log_softmax(logits[0].float()[: eng.cfg.vocab_size], -1)
+    assert abs(lsm[want[0]].item() - lp["token_logprobs"][0]) < 1e-4
+    c = chat["choices"][0]["logprobs"]["content"]
+    assert len(c) == 4 and all(len(e["top_logprobs"]) == 2 and e["logprob"] <= 0 for e in c)
+    assert all(e["bytes"] == list(e["token"].encode()) for e in c)
+    assert k1["choices"][0]["text"] == "".join(tok.decode_token(t) for t in want)
+    pieces = [ch["choices"][0]["logprobs"] for ch in streamed if ch["choices"][0]["text"]]
+    assert len(pieces) == 3 and all(len(p["tokens"]) == 1 for p in pieces)
