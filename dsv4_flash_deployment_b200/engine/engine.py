@@ -35,15 +35,17 @@ class Engine:
     counts (``StepMeta.padded``), so a serving run with changing batch
     compositions replays a few dozen graphs instead of capturing one per
     composition.  ``max_graphs`` bounds the graph cache (least recently used
-    graph released first)."""
+    graph released first).  ``preempt``: with paged caches, admit on the
+    prompt's blocks and preempt (recompute) the newest request when the pool
+    runs short, instead of reserving every block up front (engine/scheduler.py)."""
 
     def __init__(self, model: DSV4Model, max_seqs: int, max_batched_tokens: int, max_seq_len: int,
                  chunk_size: int | None = None, use_graphs: bool = True, eos_id: int | None = None,
-                 bucket: bool = True, max_graphs: int = 48):
+                 bucket: bool = True, max_graphs: int = 48, preempt: bool = False):
         self.model = model
         self.cfg = model.cfg
         self.sched = Scheduler(max_seqs, max_batched_tokens, max_seq_len, chunk_size,
-                               kv=getattr(model, "pager", None))
+                               kv=getattr(model, "pager", None), preempt=preempt)
         self.use_graphs = use_graphs and model.dev.type == "cuda"
         self.bucket = bucket
         self.max_graphs = max(1, max_graphs)
@@ -59,13 +61,14 @@ class Engine:
               weights: dict | None = None, seed: int = 0, expert_storage_layers: int | None = None, ep=None,
               use_graphs: bool = True, chunk_size: int | None = None, extra_slots: int = 0, tp=None,
               experts_from=None, kv_block: int = 0, kv_pool_tokens: int = 0, engram_from=None,
-              engram_shm: str | None = None, engram_token_map=None) -> "Engine":
+              engram_shm: str | None = None, engram_token_map=None, kv_preempt: bool = False) -> "Engine":
         """``extra_slots`` cache slots beyond ``max_seqs`` are kept out of the scheduler
         (the multi-rank control plane runs its 1-token join steps on one).  ``tp``:
         tensor-parallel group (every rank runs the same steps).  ``experts_from``: a
         model whose expert blocks this one shares (same expert ownership per rank).
         ``kv_block`` / ``kv_pool_tokens``: paged compressed caches (admission then
-        also waits for free blocks).  ``engram_token_map``: compressed token map of
+        also waits for free blocks; ``kv_preempt``: optimistic admission with
+        recompute preemption instead).  ``engram_token_map``: compressed token map of
         the tokenizer for the Engram hashes (None: ``id % C``)."""
         from .builder import build_model
         model = build_model(cfg, device, max_tokens=max_batched_tokens, n_slots=max_seqs + extra_slots,
@@ -73,7 +76,7 @@ class Engine:
                             expert_storage_layers=expert_storage_layers, ep=ep, tp=tp, experts_from=experts_from,
                             kv_block=kv_block, kv_pool_tokens=kv_pool_tokens, engram_from=engram_from,
                             engram_shm=engram_shm, engram_token_map=engram_token_map)
-        return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs)
+        return cls(model, max_seqs, max_batched_tokens, max_seq_len, chunk_size, use_graphs, preempt=kv_preempt)
 
     # ------------------------------------------------------------------- API
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,

@@ -10,6 +10,16 @@ length fits ``max_seq_len``.  Finished requests release their slot at once.
 With paged compressed caches (``kv``: models/kv_pages.py) admission also
 reserves every cache block the request can touch, oldest request first (a
 request that does not fit waits at the head of the queue); finishing releases them.
+
+``preempt=True`` (with paged caches) admits optimistically instead, as vLLM's
+scheduler does: a request reserves the blocks of its prompt, and a decoding
+sequence grows its reservation as it crosses block boundaries.  When the pool
+cannot grow one, the most recently admitted running request is preempted: its
+slot and blocks are released and it goes back to the head of the queue with
+its prompt and the tokens generated so far as the context to recompute
+(vLLM's recompute preemption); no request is admitted in a step that
+preempted.  The oldest request always progresses, since a lone request fits
+the pool (checked when it is added).
 """
 
 from __future__ import annotations
@@ -43,15 +53,27 @@ class Request:
     cancelled: bool = False
     # per generated token when ``want_logprobs`` is set: {"logprob": lp, "top": [(id, lp), ...]}
     logprobs: list = field(default_factory=list)
+    # recompute after a preemption: the context to prefill (prompt + the tokens
+    # generated before it) and how many of ``output`` it holds
+    ctx: list[int] | None = None
+    folded: int = 0
+    kv_len: int = 0               # tokens of context the slot's cache reservation covers
+    preemptions: int = 0
+
+    @property
+    def prefill(self) -> list[int]:
+        """Tokens to prefill: the prompt, or after a preemption the whole context so far."""
+        return self.prompt if self.ctx is None else self.ctx
 
     @property
     def prompt_done(self) -> bool:
-        return self.n_prefilled >= len(self.prompt)
+        return self.n_prefilled >= len(self.prefill)
 
     @property
     def position(self) -> int:
         """Next position to be written."""
-        return self.n_prefilled + len(self.output) - (1 if self.output else 0)
+        new = len(self.output) - self.folded
+        return self.n_prefilled + new - (1 if new > 0 else 0)
 
 
 @dataclass
@@ -79,13 +101,15 @@ class SlotAllocator:
 
 class Scheduler:
     def __init__(self, max_seqs: int, max_batched_tokens: int, max_seq_len: int, chunk_size: int | None = None,
-                 kv=None):
+                 kv=None, preempt: bool = False):
         self.max_seqs = max_seqs
         self.budget = max_batched_tokens
         self.max_seq_len = max_seq_len
         self.chunk = chunk_size or max_batched_tokens
         self.slots = SlotAllocator(max_seqs)
         self.kv = kv                  # paged-cache reservations (fits / reserve / release) or None
+        self.preempt = bool(preempt) and kv is not None
+        self.n_preempted = 0
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []
         self._ids = itertools.count()
@@ -111,6 +135,7 @@ class Scheduler:
         for r in [r for r in self.waiting if r.cancelled]:
             self._finish(r, "cancelled")
         self.waiting = deque(r for r in self.waiting if not r.cancelled)
+        preempted = self._grow_or_preempt() if self.preempt else 0
         out: list[ScheduledChunk] = []
         budget = self.budget
         for r in self.running:
@@ -122,23 +147,62 @@ class Scheduler:
             if budget <= 0:
                 break
             if not r.prompt_done:
-                n = min(self.chunk, budget, len(r.prompt) - r.n_prefilled)
-                out.append(ScheduledChunk(r, r.n_prefilled, r.prompt[r.n_prefilled:r.n_prefilled + n],
-                                          r.n_prefilled + n == len(r.prompt)))
+                pf = r.prefill
+                n = min(self.chunk, budget, len(pf) - r.n_prefilled)
+                out.append(ScheduledChunk(r, r.n_prefilled, pf[r.n_prefilled:r.n_prefilled + n],
+                                          r.n_prefilled + n == len(pf)))
                 budget -= n
-        while budget > 0 and self.waiting and self.slots.n_free > 0:
+        while budget > 0 and self.waiting and self.slots.n_free > 0 and not preempted:
             r = self.waiting[0]
+            pf = r.prefill
+            # reserve mode: every block the request can touch; preempt mode: its context
+            need = len(pf) + 1 if self.preempt else len(r.prompt) + r.max_new_tokens
             slot = self.slots.alloc()
-            if self.kv is not None and not self.kv.reserve(slot, len(r.prompt) + r.max_new_tokens):
+            if self.kv is not None and not self.kv.reserve(slot, need):
                 self.slots.free.appendleft(slot)
                 break
             self.waiting.popleft()
             r.slot = slot
+            r.kv_len = need
             self.running.append(r)
-            n = min(self.chunk, budget, len(r.prompt))
-            out.append(ScheduledChunk(r, 0, r.prompt[:n], n == len(r.prompt)))
+            n = min(self.chunk, budget, len(pf))
+            out.append(ScheduledChunk(r, 0, pf[:n], n == len(pf)))
             budget -= n
         return out
+
+    def _grow_or_preempt(self) -> int:
+        """Grows each decoding sequence's reservation to cover the position it writes
+        this step, oldest first; preempts the newest running requests while the pool
+        is short.  Returns the number preempted."""
+        n = 0
+        for r in list(self.running):
+            if r not in self.running or not r.prompt_done:
+                continue
+            need = r.position + 1
+            if need <= r.kv_len:
+                continue
+            while not self.kv.reserve(r.slot, need):
+                victim = self.running[-1]
+                self._preempt(victim)
+                n += 1
+                if victim is r:
+                    break
+            else:
+                r.kv_len = need
+        return n
+
+    def _preempt(self, r: Request) -> None:
+        self.running.remove(r)
+        self.kv.release(r.slot)
+        self.slots.release(r.slot)
+        r.slot = -1
+        r.ctx = r.prompt + r.output
+        r.folded = len(r.output)
+        r.n_prefilled = 0
+        r.kv_len = 0
+        r.preemptions += 1
+        self.n_preempted += 1
+        self.waiting.appendleft(r)
 
     def commit(self, chunks: list[ScheduledChunk], next_ids: list[int]) -> list[tuple[Request, int | None]]:
         """Applies a step's results; returns (request, new token or None) per chunk."""

@@ -40,7 +40,7 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
                         max_seq_len=ec.max_model_len, weights=weights, seed=ec.seed,
                         expert_storage_layers=storage, ep=ep, use_graphs=ec.use_cuda_graphs,
                         chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp, kv_block=ec.kv_block,
-                        kv_pool_tokens=ec.kv_pool_tokens, engram_shm=ec.engram_shm,
+                        kv_pool_tokens=ec.kv_pool_tokens, kv_preempt=ec.kv_preempt, engram_shm=ec.engram_shm,
                         engram_token_map=_engram_token_map(ec, cfg))
 
 

@@ -38,6 +38,8 @@ def render_prometheus(st) -> str:
     metric("waiting_requests", "gauge", "Requests queued for a slot.", len(sched.waiting))
     metric("cache_slots_used_ratio", "gauge", "Fraction of KV cache slots in use.",
            f"{1.0 - sched.slots.n_free / max(sched.max_seqs, 1):.4f}")
+    metric("preemptions_total", "counter", "Requests preempted for recompute (paged caches, kv_preempt).",
+           getattr(sched, "n_preempted", 0))
     metric("graph_captures_total", "counter", "CUDA graphs captured.", eng.stats.get("graph_captures", 0))
     metric("graph_evictions_total", "counter", "CUDA graphs released by the bounded graph cache.",
            eng.stats.get("graph_evictions", 0))

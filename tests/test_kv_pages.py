@@ -134,3 +134,101 @@ def test_pager_for_ratio_one_and_two_caches():
     assert not pg.reserve(3, 100)                                 # pool holds three full sequences
     pg.release(1)
     assert pg.reserve(3, 4096)
+
+
+class _Seq:
+    """Deterministic stand-in for a model: the next token is a function of the
+    whole context (so a recompute after a preemption must rebuild it exactly)."""
+
+    @staticmethod
+    def next_token(ctx):
+        return (sum((i + 1) * t for i, t in enumerate(ctx)) * 31 + len(ctx)) % 1000
+
+
+def _drive(sched, reqs, max_steps=2000):
+    """Runs the scheduler with _Seq as the model: every sampled chunk's token is
+    _Seq.next_token of its request's full context (prefill + generated)."""
+    steps = 0
+    while not all(r.finished for r in reqs):
+        chunks = sched.schedule()
+        toks = []
+        for c in chunks:
+            if c.sample:
+                r = c.req
+                ctx = r.prefill[:c.start_pos + len(c.tokens)] if not r.prompt_done else \
+                    r.prefill + r.output[r.folded:]
+                toks.append(_Seq.next_token(ctx))
+        sched.commit(chunks, toks)
+        steps += 1
+        assert steps < max_steps
+    return steps
+
+
+def _want(prompt, n):
+    ctx, out = list(prompt), []
+    for _ in range(n):
+        t = _Seq.next_token(ctx)
+        out.append(t)
+        ctx.append(t)
+    return out
+
+
+def test_preemption_recomputes_and_keeps_every_token():
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+
+    cfg = toy_v4_config()                                # ratio 4 only
+    pg = KvPager(cfg, "cpu", 4 + 1, 1024, 16, 640)      # ratio 4: 160 entries = 10 blocks of 16
+    sched = Scheduler(max_seqs=4, max_batched_tokens=96, max_seq_len=1024, chunk_size=64, kv=pg, preempt=True)
+    prompts = [[(7 * i + j) % 1000 for j in range(n)] for i, n in enumerate((100, 90, 120, 70))]
+    reqs = [sched.add(p, 200, ignore_eos=True) for p in prompts]
+    _drive(sched, reqs)
+    assert sched.n_preempted > 0 and any(r.preemptions for r in reqs)
+    for p, r in zip(prompts, reqs):
+        assert r.output == _want(p, 200), r.req_id
+    assert pg.free_blocks() == {4: 10}
+    # reservation mode on the same pool: no preemption, same tokens, fewer requests at once
+    pg2 = KvPager(cfg, "cpu", 4 + 1, 1024, 16, 640)
+    s2 = Scheduler(max_seqs=4, max_batched_tokens=96, max_seq_len=1024, chunk_size=64, kv=pg2)
+    reqs2 = [s2.add(p, 200, ignore_eos=True) for p in prompts]
+    _drive(s2, reqs2)
+    assert s2.n_preempted == 0 and [r.output for r in reqs2] == [r.output for r in reqs]
+
+
+def test_preempted_request_positions_continue_after_recompute():
+    from dsv4_flash_deployment_b200.engine.scheduler import Request
+
+    r = Request(0, [1, 2, 3], 10)
+    r.n_prefilled = 3
+    r.output = [9, 8]
+    assert r.position == 4                       # token 8 goes to position 4
+    r.ctx, r.folded, r.n_prefilled = r.prompt + r.output, 2, 0
+    assert not r.prompt_done and r.prefill == [1, 2, 3, 9, 8]
+    r.n_prefilled = 5
+    r.output.append(7)                           # sampled at the end of the recompute
+    assert r.prompt_done and r.position == 5
+
+
+def test_engine_with_preemption_matches_greedy_on_the_oracle():
+    import torch
+
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.engine.engine import Engine
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
+    from dsv4_flash_deployment_b200.models.oracle_step import OracleStepModel
+    from dsv4_flash_deployment_b200.ref.model import RefModel
+
+    cfg = toy_v4_config()
+    w = make_random_weights(cfg, seed=3, include_mtp=False)
+    model = OracleStepModel(cfg, w, n_slots=3, max_seq_len=128)
+    model.pager = KvPager(cfg, "cpu", 3 + 1, 128, 4, 96)   # 24 entries of ratio 4: 6 blocks of 4
+    eng = Engine(model, 3, 48, 128, 16, use_graphs=False, preempt=True)
+    prompts = [[(5 * i + 3 * j) % 900 + 20 for j in range(n)] for i, n in enumerate((22, 15, 30))]
+    reqs = [eng.add_request(p, 26, ignore_eos=True, logprobs=1) for p in prompts]
+    while not all(r.finished for r in reqs):
+        eng.step()
+    assert eng.sched.n_preempted > 0
+    ref = RefModel(cfg, w, max_seq_len=128)
+    for p, r in zip(prompts, reqs):
+        out, _ = ref.generate(torch.tensor([p]), 26)
+        assert r.output == out[0].tolist()
+        assert len(r.logprobs) == 26 and all(e["top"][0][0] == t for e, t in zip(r.logprobs, r.output))
