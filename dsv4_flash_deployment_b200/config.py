@@ -336,11 +336,46 @@ def toy_v4_config(**overrides: Any) -> ModelConfig:
     return ModelConfig(**d)
 
 
+def v4_check_config(**overrides: Any) -> ModelConfig:
+    """Four-layer V4-shaped model at the kernels' dimensions (64 heads x 512 latent,
+    64 RoPE dims, 128-wide indexer heads) with overlapped ratio-4 and ratio-16
+    compressors and MXFP8 experts: small enough for the CPU oracle, large enough
+    that every device kernel path runs.  The verification runner's default."""
+    d = dict(name="v4-check", family="v4", vocab_size=1024, padded_vocab_size=1024, dim=512, n_layers=4,
+             n_mtp_layers=0, n_heads=64, head_dim=512, qk_rope_head_dim=64, q_lora_rank=256, o_lora_rank=128,
+             o_groups=8, sliding_window=16, compress_ratios=(0, 4, 16, 4), compress_overlap=(1, 2, 1, 2),
+             compressor_ape=True, q_head_norm=True, kv_source_layer_ids=(1, 2, 3), index_source_layer_ids=(1, 3),
+             candidate_source_layer_id=-1, index_n_heads=8, index_head_dim=128, index_topk=8,
+             n_routed_experts=16, n_activated_experts=4, n_shared_experts=1, moe_inter_dim=256, route_scale=1.5,
+             score_func="sqrtsoftplus", expert_format="mxfp8", engram_layer_ids=(), engram_num_embeddings=(),
+             dspark_target_layer_ids=(), index_k_mode="intended")
+    d.update(overrides)
+    return ModelConfig(**d)
+
+
+def v41_check_config(**overrides: Any) -> ModelConfig:
+    """V4.1-structured model at the kernels' dimensions with two DSpark MTP stages
+    (ratio-2 / ratio-1 compressors, 1+4 draft blocks, Markov head): the
+    verification runner's speculative-decoding model."""
+    d = dict(name="v4.1-check", family="v4.1", vocab_size=1024, padded_vocab_size=1024, dim=512, n_layers=4,
+             n_mtp_layers=2, n_heads=64, head_dim=512, qk_rope_head_dim=64, q_lora_rank=256, o_lora_rank=128,
+             o_groups=8, sliding_window=16, compress_ratios=(0, 2, 1, 1), kv_source_layer_ids=(1, 2),
+             index_source_layer_ids=(1, 2), candidate_source_layer_id=-1, index_n_heads=8, index_head_dim=128,
+             index_topk=8, n_routed_experts=16, n_activated_experts=4, n_shared_experts=1, moe_inter_dim=256,
+             expert_format="mxfp8", engram_layer_ids=(), engram_num_embeddings=(), index_k_mode="intended",
+             dspark_n_routed_experts=8, dspark_n_activated_experts=2, dspark_block_size=5,
+             dspark_noise_token_id=1023, dspark_target_layer_ids=(1, 2, 3), markov_rank=128)
+    d.update(overrides)
+    return ModelConfig(**d)
+
+
 CONFIGS = {
     "v4.1-flash": v41_flash_config,
     "v4.1-tiny": v41_tiny_config,
     "v4-flash": v4_flash_config,
     "toy-v4": toy_v4_config,
+    "v4-check": v4_check_config,
+    "v4.1-check": v41_check_config,
 }
 
 
