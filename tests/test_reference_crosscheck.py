@@ -1,0 +1,102 @@
+"""Cross-checks against the reference's own code where it runs on a CPU without
+its TPU stack: its configuration tables and its Engram hasher and token map
+(pure numpy / sympy / tokenizers; the model oracle itself needs JAX, which this
+image does not have).
+
+Set ``DSV4_REFERENCE_ROOT`` to a checkout of the reference (the directory that
+holds ``models/``); without it every test here is skipped.  Checked:
+
+* the V4.1-Flash hyperparameters and the reference's ``tiny_config`` against
+  ``config.py`` field by field;
+* Engram row ids of random token sequences (full V4.1 layout and the tiny one)
+  against the reference's ``compute_engram_hash_ids``, bit for bit;
+* the tokenizer-normalized compressed token map against the reference's
+  ``build_compressed_token_map`` on a tokenizer fixture.
+"""
+
+import dataclasses
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = os.environ.get("DSV4_REFERENCE_ROOT")
+PKG = Path(ROOT) / "models" / "DeepSeekV4.1-Flash-v6e16" / "tpu-v7x" if ROOT else None
+
+pytestmark = pytest.mark.skipif(PKG is None or not (PKG / "deepseek_v41" / "config.py").exists(),
+                                reason="DSV4_REFERENCE_ROOT does not point at the reference checkout")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    pytest.importorskip("sympy")
+    sys.path.insert(0, str(PKG))
+    try:
+        from deepseek_v41 import config as rc
+        from deepseek_v41 import engram_hash as rh
+    finally:
+        sys.path.remove(str(PKG))
+    return rc, rh
+
+
+def _same(ours, theirs, skip=()):
+    diffs = {}
+    for f in dataclasses.fields(theirs):
+        if f.name in skip or not hasattr(ours, f.name):
+            continue
+        a, b = getattr(ours, f.name), getattr(theirs, f.name)
+        if isinstance(b, (list, tuple)):
+            a, b = tuple(a), tuple(b)
+        if a != b:
+            diffs[f.name] = (a, b)
+    return diffs
+
+
+def test_v41_config_tables_match(ref):
+    from dsv4_flash_deployment_b200.config import v41_flash_config, v41_tiny_config
+
+    rc, _ = ref
+    assert _same(v41_flash_config(), rc.DSV41Config()) == {}
+    assert _same(v41_tiny_config(), rc.tiny_config()) == {}
+    # every reference field has a counterpart here
+    missing = [f.name for f in dataclasses.fields(rc.DSV41Config) if not hasattr(v41_flash_config(), f.name)]
+    assert missing == []
+
+
+@pytest.mark.parametrize("which", ["tiny", "full"])
+def test_engram_row_ids_match_bit_for_bit(ref, which):
+    from dsv4_flash_deployment_b200.config import v41_flash_config, v41_tiny_config
+    from dsv4_flash_deployment_b200.ref.engram import EngramHasher
+
+    rc, rh = ref
+    ours_cfg, theirs_cfg = ((v41_tiny_config(), rc.tiny_config()) if which == "tiny"
+                            else (v41_flash_config(), rc.DSV41Config()))
+    rng = np.random.default_rng(7)
+    ids = rng.integers(0, ours_cfg.vocab_size, size=(3, 41), dtype=np.int64)
+    ids[1, 5:9] = ours_cfg.engram_pad_id           # pad tokens inside a sequence
+    want = rh.compute_engram_hash_ids(ids, theirs_cfg)          # [B, L, layers, cols]
+    h = EngramHasher(ours_cfg)
+    for b in range(ids.shape[0]):
+        got = h.hash(h.compress(ids[b]), np.arange(ids.shape[1]))
+        assert np.array_equal(got, want[b]), which
+
+
+def test_compressed_token_map_matches(ref, tmp_path):
+    tokenizers = pytest.importorskip("tokenizers")
+    from dsv4_flash_deployment_b200.ref.engram import compressed_token_map
+
+    _, rh = ref
+    vocab = ["<unk>", "Hello", "hello", "HÉLLO", " ", "\t\t", "ﬁne", "fine", "Straße", "x\ny", "x y", "café",
+             "cafe", "  Word　", "Ⅻ", "İ", " ", "á"]
+    tok = tokenizers.Tokenizer(tokenizers.models.WordLevel({t: i for i, t in enumerate(vocab)}, unk_token="<unk>"))
+    p = tmp_path / "tokenizer.json"
+    tok.save(str(p))
+    want, wc = rh.build_compressed_token_map(str(p))
+    got, gc = compressed_token_map(str(p))
+    assert gc == wc and got.tolist() == want.tolist()
+    # no tokenizer: id % C on both sides
+    w2, c2 = rh.build_compressed_token_map(None, vocab_size=129280)
+    g2, d2 = compressed_token_map(None, 129280)
+    assert d2 == c2 and np.array_equal(g2, w2)
