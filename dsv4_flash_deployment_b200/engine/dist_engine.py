@@ -147,11 +147,11 @@ class DistributedEngine:
 
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
                     stop_ids=(), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
-                    logprobs: int | None = None) -> GlobalRequest:
+                    logprobs: int | None = None, seed: int | None = None) -> GlobalRequest:
         if not prompt:
             raise ValueError("empty prompt")
         # checked here, on rank 0, so that no rank is sent a request its engine refuses
-        sp = self.local.sampling_params(temperature, top_k, top_p, logprobs)
+        sp = self.local.sampling_params(temperature, top_k, top_p, logprobs, seed)
         if len(prompt) + max_new_tokens > self.local.sched.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.local.sched.max_seq_len}")
@@ -160,8 +160,8 @@ class DistributedEngine:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds the paged cache pool")
         r = -1 if self.replicated else min(range(self.world), key=lambda i: self.load[i])
         g = GlobalRequest(self.next_id, r, list(prompt), max_new_tokens)
-        extra = {} if not (sp.top_k or sp.top_p < 1.0 or sp.wants_logprobs) else \
-            {"top_k": sp.top_k, "top_p": sp.top_p, "logprobs": sp.logprobs}
+        extra = {} if not (sp.top_k or sp.top_p < 1.0 or sp.wants_logprobs or sp.seed is not None) else \
+            {"top_k": sp.top_k, "top_p": sp.top_p, "logprobs": sp.logprobs, "seed": sp.seed}
         g._opts = (bool(ignore_eos), tuple(stop_ids), sp.temperature, extra)
         self.next_id += 1
         self.load[r] += 1

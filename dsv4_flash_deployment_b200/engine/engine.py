@@ -81,24 +81,26 @@ class Engine:
     # ------------------------------------------------------------------- API
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
                     stop_ids: Iterable[int] = (), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
-                    logprobs: int | None = None) -> Request:
+                    logprobs: int | None = None, seed: int | None = None) -> Request:
         """``temperature`` 0 decodes greedily; > 0 samples softmax(logits / T),
         restricted to the ``top_k`` most likely tokens (0: all) and to the top-p
         nucleus (``top_p`` 1.0: all).  ``logprobs`` n >= 0: every generated token
         also carries its log-probability and the n most likely alternatives
-        (``Request.logprobs``), from the raw logits."""
-        sp = self.sampling_params(temperature, top_k, top_p, logprobs)
+        (``Request.logprobs``), from the raw logits.  ``seed``: the request's samples
+        depend on (seed, position) only, so a seeded request repeats its output
+        whatever it is batched with."""
+        sp = self.sampling_params(temperature, top_k, top_p, logprobs, seed)
         return self.sched.add(prompt, max_new_tokens, ignore_eos=ignore_eos, eos_id=self.eos_id,
                               stop_ids=tuple(stop_ids), temperature=sp.temperature, top_k=sp.top_k, top_p=sp.top_p,
-                              want_logprobs=sp.logprobs)
+                              want_logprobs=sp.logprobs, seed=sp.seed)
 
     def sampling_params(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
-                        logprobs: int | None = None) -> SamplingParams:
+                        logprobs: int | None = None, seed: int | None = None) -> SamplingParams:
         """Checked decoding rule of a request (ValueError when this engine cannot
         apply it: top-k / top-p / log-probabilities need the whole vocabulary's
         logits on one GPU, so the vocab-parallel head refuses them)."""
         sp = SamplingParams(float(temperature), int(top_k or 0), float(1.0 if top_p is None else top_p),
-                            None if logprobs is None else int(logprobs))
+                            None if logprobs is None else int(logprobs), None if seed is None else int(seed))
         if (sp.filters or sp.wants_logprobs) and getattr(self.model, "tp", None) is not None:
             raise ValueError("top_k / top_p / logprobs are not supported with the tensor-parallel (vocab-parallel) head")
         return sp
@@ -109,7 +111,7 @@ class Engine:
             return []
         meta = StepMeta(self.cfg, [SeqChunk(c.req.slot, c.start_pos, c.tokens, c.sample,
                                             temperature=c.req.temperature, top_k=c.req.top_k, top_p=c.req.top_p,
-                                            logprobs=c.req.want_logprobs) for c in chunks])
+                                            logprobs=c.req.want_logprobs, seed=c.req.seed) for c in chunks])
         ids = self.run_meta(meta)
         if meta.want_lp:
             it = iter(self.last_logprobs)

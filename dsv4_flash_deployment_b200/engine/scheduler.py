@@ -42,6 +42,7 @@ class Request:
     top_k: int = 0                    # 0 = off
     top_p: float = 1.0                # 1.0 = off
     want_logprobs: int | None = None  # alternatives per generated token (None: no log-probabilities)
+    seed: int | None = None           # samples depend on (seed, position) only
     slot: int = -1
     n_prefilled: int = 0
     output: list[int] = field(default_factory=list)

@@ -37,7 +37,7 @@ from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxW
 from ..ops.layout import ceil_to
 from ..ref import numerics as N
 from .kv_format import ik4_bytes, kv4_bytes, kv8_bytes
-from .sampling import LOGPROB_TOP_N, chosen_logprob, gumbel_, logprob_top, top_k_top_p_mask_
+from .sampling import LOGPROB_TOP_N, chosen_logprob, gumbel_, logprob_top, seed_key, top_k_top_p_mask_
 from .weights import LayerW
 
 ROUTER_SMALL_T = 4   # steps of at most this many tokens route with csrc/moe.cu router_small
@@ -57,6 +57,7 @@ class SeqChunk:
     top_k: int = 0             # > 0: sample among the k most likely tokens only (temperature > 0)
     top_p: float = 1.0         # < 1: sample within the top-p nucleus only (temperature > 0)
     logprobs: int | None = None  # n >= 0: also return the sampled token's log-probability and n alternatives
+    seed: int | None = None    # samples depend on (seed, position) only (temperature > 0)
 
 
 class StepMeta:
@@ -100,6 +101,13 @@ class StepMeta:
         self.topk = np.repeat(topk, per_chunk).astype(np.int32)
         self.topp = np.repeat(topp, per_chunk).astype(np.float32)
         self.filtering = bool(((self.temps > 0) & ((self.topk > 0) | (self.topp < 1.0))).any())
+        # seeded rows: the noise key of (seed, position of the sampled token)
+        seeds = [c.seed for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
+        spos = self.pos[self.sample_rows] if len(self.sample_rows) else np.zeros(0, np.int32)
+        self.has_seed = np.array([sd is not None for sd in seeds], dtype=bool)
+        self.seedkey = np.array([seed_key(sd, int(p)) if sd is not None else 0 for sd, p in zip(seeds, spos)],
+                                dtype=np.int64)
+        self.seeded = bool((self.has_seed & (self.temps > 0)).any())
         # alternatives wanted per sampled row (None: no log-probabilities)
         self.lp_want = [c.logprobs for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
         self.want_lp = any(w is not None for w in self.lp_want)
@@ -135,7 +143,8 @@ class StepMeta:
         sampled rows, chunk-count bucket, indexer bypass per ratio, sampling) and
         nothing else, so steps of different batch compositions share a graph."""
         return (self.T, len(self.sample_rows), self.chunk_bound,
-                tuple(self.index_bypass(r) for r in self.groups), self.sampling, self.filtering, self.want_lp)
+                tuple(self.index_bypass(r) for r in self.groups), self.sampling, self.filtering, self.want_lp,
+                self.seeded)
 
     def padded(self, max_tokens: int, max_sample: int, pad_slot: int) -> "StepMeta":
         """This step padded to bucketed shapes (:func:`token_bucket`): a padding chunk
@@ -156,6 +165,8 @@ class StepMeta:
             m.topk = np.concatenate([m.topk, np.zeros(extra, np.int32)])
             m.topp = np.concatenate([m.topp, np.ones(extra, np.float32)])
             m.lp_want = m.lp_want + [None] * extra
+            m.has_seed = np.concatenate([m.has_seed, np.zeros(extra, bool)])
+            m.seedkey = np.concatenate([m.seedkey, np.zeros(extra, np.int64)])
         m.n_out = S
         return m
 
@@ -326,6 +337,8 @@ class DSV4Model:
         self.m_temp = z(self.max_sample, dt=f32)
         self.m_topk = z(self.max_sample, dt=i32)
         self.m_topp = torch.ones(self.max_sample, dtype=f32, device=dev)
+        self.m_seedkey = z(self.max_sample, dt=torch.int64)
+        self.m_hasseed = torch.zeros(self.max_sample, dtype=torch.bool, device=dev)
         # log-probabilities of the sampled rows (written only by steps that ask for them)
         self.lp_chosen = z(self.max_sample, dt=f32)
         self.lp_vals = z(self.max_sample, LOGPROB_TOP_N, dt=f32)
@@ -428,6 +441,9 @@ class DSV4Model:
         if m.filtering:
             put(self.m_topk, m.topk)
             put(self.m_topp, m.topp)
+        if m.seeded:
+            put(self.m_seedkey, m.seedkey)
+            put(self.m_hasseed, m.has_seed)
         for r, g in m.groups.items():
             for dst, arr in zip(self.m_groups[r], g):
                 if len(arr):
@@ -577,7 +593,7 @@ class DSV4Model:
             if m.filtering:
                 top_k_top_p_mask_(self.logits[:S, :self.vocab], self.m_temp[:S], self.m_topk[:S], self.m_topp[:S])
             if m.sampling:
-                self._gumbel(S)
+                self._gumbel(S, seeded=m.seeded)
             if self.tp is None:
                 ext.argmax_rows(self.logits[:S], S, self.vocab, self.next_ids[:S], self.argmax_scratch, None, 0)
                 if m.want_lp:
@@ -593,7 +609,7 @@ class DSV4Model:
                                     self.err)
         return self.next_ids[:S]
 
-    def _gumbel(self, S: int) -> None:
+    def _gumbel(self, S: int, seeded: bool = False) -> None:
         """Temperature sampling by the Gumbel-max rule: the argmax of
         logits + T * g (g ~ Gumbel(0, 1) per vocabulary entry) is a sample of
         softmax(logits / T); rows with T = 0 keep their logits, so they stay
@@ -602,7 +618,13 @@ class DSV4Model:
         noise of its own rows and the cross-rank merge keeps the best."""
         if self._gnoise is None:   # first sampling step runs eagerly, before any capture of it
             self._gnoise = torch.empty_like(self.logits)
-        gumbel_(self.logits[:S], self.m_temp[:S], self._gnoise[:S])
+        sd = None
+        v0 = 0
+        if seeded:    # rows with a request seed: noise from (seed, position, vocabulary index) only
+            sd = (self.m_seedkey[:S], self.m_hasseed[:S])
+            if self.tp is not None:
+                v0 = self.tp.vocab_rows(self.vocab)[0]
+        gumbel_(self.logits[:S], self.m_temp[:S], self._gnoise[:S], sd, v0)
 
     _gnoise = None
 

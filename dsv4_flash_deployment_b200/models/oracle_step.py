@@ -17,7 +17,7 @@ import torch
 
 from ..ref.model import RefModel, RefState
 from .model import StepMeta
-from .sampling import LOGPROB_TOP_N, chosen_logprob, logprob_top, top_k_top_p_mask_
+from .sampling import LOGPROB_TOP_N, chosen_logprob, logprob_top, seed_key, seeded_gumbel, top_k_top_p_mask_
 
 
 class OracleStepModel:
@@ -56,8 +56,13 @@ class OracleStepModel:
                     top_k_top_p_mask_(lg, temp, torch.tensor([c.top_k], dtype=torch.int32),
                                       torch.tensor([c.top_p]))
                 if c.temperature > 0:   # Gumbel-max, as the device model samples
-                    u = torch.rand(lg.shape, generator=self._gen).clamp_(1e-20, 1.0 - 1e-7)
-                    lg = lg + c.temperature * (-torch.log(-torch.log(u)))
+                    if c.seed is not None:
+                        key = torch.tensor([seed_key(c.seed, c.start_pos + len(c.tokens) - 1)])
+                        g = seeded_gumbel(key, lg.shape[1])
+                    else:
+                        u = torch.rand(lg.shape, generator=self._gen).clamp_(1e-20, 1.0 - 1e-7)
+                        g = -torch.log(-torch.log(u))
+                    lg = lg + c.temperature * g
                 tok = int(lg.argmax())
                 out.append(tok)
                 n_top = min(LOGPROB_TOP_N, raw.shape[1])

@@ -30,12 +30,14 @@ class SamplingParams:
     """Per-request decoding rule.  ``temperature`` 0 is greedy (top-k / top-p then
     change nothing); ``top_k`` 0 and ``top_p`` 1.0 are off; ``logprobs`` None asks
     for none, n >= 0 for the sampled token's log-probability plus the n most
-    likely alternatives."""
+    likely alternatives; ``seed`` makes the request's samples a function of
+    (seed, position) only (:func:`seeded_gumbel`), whatever it is batched with."""
 
     temperature: float = 0.0
     top_k: int = 0
     top_p: float = 1.0
     logprobs: int | None = None
+    seed: int | None = None
 
     def __post_init__(self):
         if self.temperature < 0:
@@ -57,13 +59,68 @@ class SamplingParams:
         return self.logprobs is not None
 
 
-def gumbel_(logits: torch.Tensor, temps: torch.Tensor, noise: torch.Tensor) -> None:
+def gumbel_(logits: torch.Tensor, temps: torch.Tensor, noise: torch.Tensor,
+            seeded: tuple[torch.Tensor, torch.Tensor] | None = None, v0: int = 0) -> None:
     """In place: ``logits += temps * g`` with g ~ Gumbel(0, 1) drawn into ``noise``
     (same shape).  The argmax of the result is a sample of softmax(logits / T);
-    rows at T = 0 are unchanged (greedy)."""
+    rows at T = 0 are unchanged (greedy).  ``seeded`` = (row keys int64 [S], row
+    has a seed bool [S]): those rows take :func:`seeded_gumbel` noise for
+    vocabulary columns ``v0 ..`` instead of the device generator's."""
     noise.uniform_(1e-20, 1.0 - 1e-7)
     noise.log_().neg_().log_().neg_()
+    if seeded is not None:
+        keys, has = seeded
+        noise.copy_(torch.where(has[:, None], seeded_gumbel(keys, noise.shape[1], v0), noise))
     logits.addcmul_(temps[:, None], noise)
+
+
+# SplitMix64 (G. Steele, D. Lea, C. Flood, "Fast splittable pseudorandom number
+# generators", OOPSLA 2014): the golden-ratio increment and the two multipliers
+# of its output mix, as signed 64-bit values (torch has no unsigned int64).
+def _s64(x: int) -> int:
+    x &= (1 << 64) - 1
+    return x - (1 << 64) if x >> 63 else x
+
+
+_SM_GAMMA = _s64(0x9E3779B97F4A7C15)
+_SM_M1 = _s64(0xBF58476D1CE4E5B9)
+_SM_M2 = _s64(0x94D049BB133111EB)
+
+
+def _srl(x: torch.Tensor, k: int) -> torch.Tensor:
+    """Logical right shift of int64 values (torch's >> is arithmetic)."""
+    return (x >> k) & ((1 << (64 - k)) - 1)
+
+
+def _mix(z: torch.Tensor) -> torch.Tensor:
+    z = (z ^ _srl(z, 30)) * _SM_M1
+    z = (z ^ _srl(z, 27)) * _SM_M2
+    return z ^ _srl(z, 31)
+
+
+def splitmix64(x: int) -> int:
+    """The SplitMix64 output for state ``x`` (host integers, exact mod 2^64)."""
+    m = (1 << 64) - 1
+    z = (x + 0x9E3779B97F4A7C15) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    return z ^ (z >> 31)
+
+
+def seed_key(seed: int, position: int) -> int:
+    """Per (request seed, token position) key of the seeded noise, as a signed int64."""
+    return _s64(splitmix64(splitmix64(seed & ((1 << 64) - 1)) ^ (position & ((1 << 64) - 1))))
+
+
+def seeded_gumbel(keys: torch.Tensor, n: int, v0: int = 0) -> torch.Tensor:
+    """Gumbel(0, 1) noise [S, n] for vocabulary columns v0 .. v0 + n - 1: entry
+    (s, v) is a function of keys[s] and v only (SplitMix64 of key + v * gamma, top
+    24 bits as a uniform in (0, 1)), the same on every device and under any
+    vocabulary split."""
+    v = torch.arange(v0, v0 + n, device=keys.device, dtype=torch.int64)
+    z = _mix(keys[:, None] + v[None, :] * _SM_GAMMA)
+    u = (_srl(z, 40).to(torch.float32) + 0.5) * (1.0 / (1 << 24))
+    return -torch.log(-torch.log(u))
 
 
 def top_k_top_p_mask_(logits: torch.Tensor, temps: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor) -> None:

@@ -15,7 +15,8 @@ scripts/benchmark_sweep.py:70-125``):
 Decoding: ``temperature`` 0 (the default when the field is absent, and what
 every reference benchmark sends) is greedy; ``temperature`` > 0 samples
 softmax(logits / T) on the device by the Gumbel-max rule, restricted by
-``top_k`` (> 0) and ``top_p`` (< 1) when given.  ``logprobs`` (completions: the
+``top_k`` (> 0) and ``top_p`` (< 1) when given; ``seed`` makes the samples a
+function of (seed, position) only, so a seeded request repeats its output.  ``logprobs`` (completions: the
 number of alternatives, 0-20; chat: ``logprobs: true`` with ``top_logprobs``
 0-20) returns each generated token's log-probability under the raw logits and
 its most likely alternatives, in the OpenAI response layouts.  ``n`` /
@@ -92,10 +93,12 @@ def _params(st: ServerState, body: dict, n_prompt: int, chat: bool = False) -> t
         top_p = 1.0 if body.get("top_p") is None else float(body["top_p"])
         top_k = 0 if body.get("top_k") is None else int(body["top_k"])
         lp = _logprobs_field(body, chat)
-        sp = SamplingParams(temp, max(top_k, 0), top_p, lp)     # top_k -1 (vLLM's "off") counts as 0
+        seed = None if body.get("seed") is None else int(body["seed"])
+        sp = SamplingParams(temp, max(top_k, 0), top_p, lp, seed)     # top_k -1 (vLLM's "off") counts as 0
     except (TypeError, ValueError) as e:
         raise web.HTTPBadRequest(text=json.dumps({"error": str(e)}), content_type="application/json") from None
-    return (GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids, temp, sp.top_k, sp.top_p, sp.logprobs),
+    return (GenParams(mt, bool(body.get("ignore_eos", False)), stop_ids, temp, sp.top_k, sp.top_p, sp.logprobs,
+                      sp.seed),
             [s for s in stop if s])
 
 

@@ -34,6 +34,7 @@ class GenParams:
     top_k: int = 0
     top_p: float = 1.0
     logprobs: int | None = None     # alternatives per token (None: no log-probabilities)
+    seed: int | None = None
 
 
 @dataclass
@@ -105,8 +106,8 @@ class EngineLoop:
                     # the filtering / log-probability options only when asked for, so an
                     # engine front that does not take them still serves the rest
                     kw = {}
-                    if p.top_k or p.top_p < 1.0 or p.logprobs is not None:
-                        kw = {"top_k": p.top_k, "top_p": p.top_p, "logprobs": p.logprobs}
+                    if p.top_k or p.top_p < 1.0 or p.logprobs is not None or p.seed is not None:
+                        kw = {"top_k": p.top_k, "top_p": p.top_p, "logprobs": p.logprobs, "seed": p.seed}
                     req = eng.add_request(prompt, p.max_tokens, ignore_eos=p.ignore_eos, stop_ids=p.stop_ids,
                                           temperature=p.temperature, **kw)
                 except (ValueError, TypeError) as e:

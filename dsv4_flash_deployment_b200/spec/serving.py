@@ -78,7 +78,7 @@ class SpecServingEngine:
 
     def add_request(self, prompt: list[int], max_new_tokens: int, ignore_eos: bool = False,
                     stop_ids=(), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
-                    logprobs: int | None = None) -> Request:
+                    logprobs: int | None = None, seed: int | None = None) -> Request:
         if temperature > 0:
             raise ValueError("speculative decoding (DSpark) decodes greedily; temperature > 0 is not supported")
         if logprobs is not None:

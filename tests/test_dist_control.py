@@ -135,3 +135,40 @@ def test_dead_rank_is_detected_not_hung():
     assert r0[0] == "ok", r0
     assert r0[1]["detected"] and r0[1]["after_s"] < 60, r0
     assert ei.value.results[1][0] == "missing"
+
+
+def _rank_generate_sampling_options(rank, world):
+    import torch.distributed as dist
+
+    from dsv4_flash_deployment_b200.engine.dist_engine import DistributedEngine, worker_loop
+
+    eng = _engine()
+    if rank != 0:
+        worker_loop(eng, dist.group.WORLD)
+        return {}
+    de = DistributedEngine(eng, dist.group.WORLD)
+    greedy_lp = [de.add_request(p, N_NEW, ignore_eos=True, logprobs=2) for p in PROMPTS]
+    seeded = [de.add_request(PROMPTS[0], N_NEW, ignore_eos=True, temperature=3.0, seed=5, top_k=50)
+              for _ in range(2)]
+    while not all(r.finished for r in greedy_lp + seeded):
+        de.step()
+    de.shutdown()
+    return {"outs": [r.output for r in greedy_lp], "lps": [r.logprobs for r in greedy_lp],
+            "seeded": [r.output for r in seeded], "seeded_ranks": [r.rank for r in seeded]}
+
+
+def test_sampling_options_cross_the_control_plane():
+    """Log-probabilities come back from the rank that served the request, and a
+    seeded request gives the same samples on either rank."""
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
+    from dsv4_flash_deployment_b200.ref.model import RefModel
+
+    res = spawn(_rank_generate_sampling_options, 2, timeout_s=300)[0]
+    cfg = toy_v4_config()
+    ref = RefModel(cfg, make_random_weights(cfg, seed=0, include_mtp=False), max_seq_len=96)
+    for p, got, lps in zip(PROMPTS, res["outs"], res["lps"]):
+        want, _ = ref.generate(torch.tensor([p]), N_NEW)
+        assert got == want[0].tolist()
+        assert len(lps) == N_NEW and all(e["top"][0][0] == t and len(e["top"]) == 2 for e, t in zip(lps, got))
+    assert res["seeded"][0] == res["seeded"][1] and sorted(res["seeded_ranks"]) == [0, 1]

@@ -2,6 +2,7 @@
 CPU tensors: rows at temperature 0 keep their logits exactly (greedy), and the
 argmax of logits + T * Gumbel noise follows softmax(logits / T)."""
 
+import math
 import types
 
 import torch
@@ -139,3 +140,71 @@ def test_sampling_params_validation():
     for bad in (dict(temperature=-1), dict(top_k=-2), dict(top_p=0.0), dict(top_p=1.2), dict(logprobs=21)):
         with pytest.raises(ValueError):
             SamplingParams(**bad)
+
+
+def test_seeded_noise_is_splitmix64_and_split_invariant():
+    from dsv4_flash_deployment_b200.models import sampling as S
+
+    keys = torch.tensor([S.seed_key(123, 5), S.seed_key(-7, 0), S.seed_key(2 ** 40 + 3, 99)])
+    g = S.seeded_gumbel(keys, 12)
+    m = (1 << 64) - 1
+    for i, k in enumerate(keys.tolist()):
+        for v in range(12):
+            # entry (s, v) is SplitMix64 at state key + (v - 1) * gamma, top 24 bits as a uniform
+            z = S.splitmix64(((k & m) + (v - 1) * 0x9E3779B97F4A7C15) & m)
+            u = ((z >> 40) + 0.5) / 2 ** 24
+            assert abs(-math.log(-math.log(u)) - g[i, v].item()) < 1e-5
+    # a vocabulary shard starting at v0 draws the same columns
+    assert torch.equal(S.seeded_gumbel(keys, 5, 7), g[:, 7:12])
+    # Gumbel-max over seeded noise still samples softmax(logits / T)
+    base = torch.tensor([1.0, 0.5, 0.0, -0.5, 2.0, 0.2])
+    n, T = 30000, 0.8
+    ks = torch.tensor([S.seed_key(s, 11) for s in range(n)])
+    picks = (base / T + S.seeded_gumbel(ks, 6)).argmax(1)
+    freq = torch.bincount(picks, minlength=6).float() / n
+    assert (freq - torch.softmax(base / T, 0)).abs().max().item() < 0.012
+
+
+def test_seeded_rows_in_the_head_rule():
+    from dsv4_flash_deployment_b200.models import sampling as S
+
+    lg = torch.zeros(3, 40)
+    keys = torch.tensor([S.seed_key(5, 3), 0, S.seed_key(5, 3)])
+    has = torch.tensor([True, False, True])
+    a, b = lg.clone(), lg.clone()
+    gumbel_(a, torch.ones(3), torch.empty_like(a), (keys, has))
+    gumbel_(b, torch.ones(3), torch.empty_like(b), (keys, has))
+    assert torch.equal(a[0], b[0]) and torch.equal(a[0], a[2])      # same (seed, position): same noise
+    assert not torch.equal(a[1], b[1])                               # unseeded row: the generator's
+
+
+def test_step_meta_seed_keys_follow_positions():
+    from dsv4_flash_deployment_b200.models.sampling import seed_key
+
+    cfg = toy_v4_config()
+    m = StepMeta(cfg, [SeqChunk(0, 4, [5, 6, 7], True, temperature=1.0, seed=9), SeqChunk(1, 2, [1], True)])
+    assert m.seeded and m.has_seed.tolist() == [True, False]
+    assert m.seedkey[0] == seed_key(9, 6)
+    greedy_seeded = StepMeta(cfg, [SeqChunk(0, 4, [5], True, seed=9)])
+    assert not greedy_seeded.seeded
+    p = m.padded(64, 8, 7)
+    assert len(p.seedkey) == len(p.has_seed) == len(p.sample_rows)
+
+
+def test_seeded_request_repeats_whatever_its_batch():
+    from dsv4_flash_deployment_b200.engine.config import EngineConfig
+    from dsv4_flash_deployment_b200.serving.launch import build_local_engine
+
+    eng = build_local_engine(EngineConfig(device="cpu", model="toy-v4", max_seqs=3, max_batched_tokens=48,
+                                          chunk_size=16, max_model_len=96))
+    p = [3 + (7 * i) % 200 for i in range(20)]
+    alone = eng.add_request(p, 8, ignore_eos=True, temperature=3.0, seed=42)
+    while not alone.finished:
+        eng.step()
+    others = [eng.add_request([9, 8, 7, 6] * k, 10, ignore_eos=True, temperature=3.0) for k in (2, 3)]
+    again = eng.add_request(p, 8, ignore_eos=True, temperature=3.0, seed=42)
+    other_seed = eng.add_request(p, 8, ignore_eos=True, temperature=3.0, seed=43)
+    while not all(r.finished for r in others + [again, other_seed]):
+        eng.step()
+    assert again.output == alone.output
+    assert other_seed.output != alone.output
