@@ -32,6 +32,44 @@ from ..ops.layout import ceil_to, expand_block_scales
 from ..ref.engram import EngramHasher
 
 
+PAGE_LOCKABLE_FS = ("tmpfs", "hugetlbfs")
+
+
+def mount_fs_type(path: str) -> str | None:
+    """File system type of the mount that holds ``path`` (from ``/proc/mounts``),
+    or None where that is unknown."""
+    import os
+
+    p = os.path.realpath(path)
+    best, typ = "", None
+    try:
+        with open("/proc/mounts") as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) < 3:
+                    continue
+                mnt = parts[1].replace("\\040", " ")
+                inside = p == mnt or p.startswith(mnt.rstrip("/") + "/")
+                if inside and len(mnt) >= len(best):
+                    best, typ = mnt, parts[2]
+    except OSError:
+        return None
+    return typ
+
+
+def check_page_lockable(prefix: str) -> None:
+    """Shared table files must sit on tmpfs (``/dev/shm``) or hugetlbfs: Linux
+    refuses long-term pinning of writable shared mappings of regular files, so
+    ``cudaHostRegister`` of such a mapping fails ("invalid argument")."""
+    import os
+
+    d = os.path.dirname(os.path.abspath(prefix)) or "."
+    typ = mount_fs_type(d)
+    if typ is not None and typ not in PAGE_LOCKABLE_FS:
+        raise ValueError(f"Engram shared tables at {prefix!r} are on a {typ} file system; the GPU reads them "
+                         f"from page-locked memory, which needs tmpfs or hugetlbfs (e.g. /dev/shm/<name>)")
+
+
 def shared_table(prefix: str, tag: str, rows: int, width: int, fill, signature: str) -> torch.Tensor:
     """uint8 [rows, width] backed by the shared file ``<prefix>.<tag>`` (e.g. under
     ``/dev/shm``), filled once for all processes.
@@ -134,6 +172,8 @@ class EngramRuntime:
         ``token_map``: token id -> compressed id (``ref.engram.compressed_token_map``
         of the checkpoint's tokenizer); None: ``id % C``."""
         self.cfg, self.dev, self.ext = cfg, dev, ext
+        if shm_prefix and weights is None:
+            check_page_lockable(shm_prefix)
         h = EngramHasher(cfg, token_map=token_map)
         lay = h.layout
         self.nl, self.N, self.H, self.hd = len(lay.layer_ids), lay.max_ngram, lay.n_heads, lay.head_dim

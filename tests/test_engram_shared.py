@@ -58,3 +58,19 @@ def test_concurrent_processes_fill_once(tmp_path):
     assert all(p.returncode == 0 for p in procs)
     assert sum(int(o[0]) for o in outs) == 1              # exactly one process filled
     assert len({o[1] for o in outs}) == 1                 # all saw the same bytes
+
+
+def test_shared_tables_must_be_page_lockable(monkeypatch):
+    """The GPU page-locks the shared mapping: tmpfs / hugetlbfs prefixes pass, a
+    regular file system is refused up front with the reason."""
+    import pytest
+
+    from dsv4_flash_deployment_b200.models import engram as E
+
+    monkeypatch.setattr(E, "mount_fs_type", lambda p: "ext4")
+    with pytest.raises(ValueError, match="tmpfs"):
+        E.check_page_lockable("/somewhere/engram")
+    monkeypatch.setattr(E, "mount_fs_type", lambda p: "tmpfs")
+    E.check_page_lockable("/dev/shm/engram")
+    monkeypatch.setattr(E, "mount_fs_type", lambda p: None)      # unknown: not refused
+    E.check_page_lockable("/x/engram")
