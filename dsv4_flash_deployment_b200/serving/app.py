@@ -9,19 +9,21 @@ scripts/benchmark_sweep.py:70-125``):
   GET  /metrics                Prometheus text: requests, tokens, step time, batch, TTFT, slots
   POST /tokenize               {"prompt"} or {"messages"} -> {"count", "tokens", "max_model_len"}
   POST /detokenize             {"tokens"} -> {"prompt"}
-  POST /v1/completions         prompt (text | ids | [text]), max_tokens, stream, ignore_eos, stop
-  POST /v1/chat/completions    messages, max_tokens / max_completion_tokens, stream, stop
+  POST /v1/completions         prompt (text | ids | a list of either), n, max_tokens, stream, ignore_eos, stop
+  POST /v1/chat/completions    messages, n, max_tokens / max_completion_tokens, stream, stop
 
 Decoding: ``temperature`` 0 (the default when the field is absent, and what
 every reference benchmark sends) is greedy; ``temperature`` > 0 samples
 softmax(logits / T) on the device by the Gumbel-max rule, restricted by
 ``top_k`` (> 0) and ``top_p`` (< 1) when given; ``seed`` makes the samples a
-function of (seed, position) only, so a seeded request repeats its output.  ``logprobs`` (completions: the
-number of alternatives, 0-20; chat: ``logprobs: true`` with ``top_logprobs``
-0-20) returns each generated token's log-probability under the raw logits and
-its most likely alternatives, in the OpenAI response layouts.  ``n`` /
-``best_of`` > 1 are refused with 400, and so is any request the engine cannot
-serve (top-k / top-p / logprobs on the tensor-parallel head, logprobs or
+function of (seed, position) only, so a seeded request repeats its output.
+``logprobs`` (completions: the number of alternatives, 0-20; chat:
+``logprobs: true`` with ``top_logprobs`` 0-20) returns each generated token's
+log-probability under the raw logits and its most likely alternatives, in the
+OpenAI response layouts.  ``n`` choices per prompt (and a list of prompts)
+run as separate engine requests that share the engine's steps; ``best_of``
+is accepted only equal to ``n``.  A request the engine cannot serve is refused
+with 400 (top-k / top-p / logprobs on the tensor-parallel head, logprobs or
 temperature under speculative decoding).
 Streaming sends one SSE event per generated token and ends with
 ``data: [DONE]``; a client that disconnects cancels its request.
@@ -32,6 +34,7 @@ Run: ``python -m dsv4_flash_deployment_b200.serving --config v4-flash --port 800
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 import json
 import time
 import uuid
@@ -52,19 +55,44 @@ class ServerState:
         self.t_start = time.time()
 
 
-def _prompt_ids(st: ServerState, body: dict, chat: bool) -> list[int]:
+MAX_CHOICES = 64   # prompts x n per request
+
+
+def _prompt_ids(st: ServerState, body: dict, chat: bool) -> list[list[int]]:
+    """Token ids of every prompt: chat messages (one), or a completions ``prompt``
+    that is a string, a list of token ids, or a list of either (a batch)."""
     if chat:
         text = st.tok.apply_chat_template(body.get("messages") or [])
-        return st.tok.encode(text, add_bos=True)
+        return [st.tok.encode(text, add_bos=True)]
     p = body.get("prompt", "")
-    if isinstance(p, list):
-        if p and all(isinstance(t, int) for t in p):
-            return [int(t) for t in p]
-        if len(p) != 1:
-            raise web.HTTPBadRequest(text=json.dumps({"error": "batched prompts: send one prompt per request"}),
-                                     content_type="application/json")
-        p = p[0]
-    return st.tok.encode(str(p), add_bos=True)
+    if isinstance(p, list) and p and all(isinstance(t, int) for t in p):
+        return [[int(t) for t in p]]
+    items = p if isinstance(p, list) else [p]
+    if not items or len(items) > MAX_CHOICES:
+        raise web.HTTPBadRequest(text=json.dumps({"error": f"between 1 and {MAX_CHOICES} prompts per request"}),
+                                 content_type="application/json")
+    out = []
+    for it in items:
+        if isinstance(it, list) and all(isinstance(t, int) for t in it):
+            out.append([int(t) for t in it])
+        else:
+            out.append(st.tok.encode(str(it), add_bos=True))
+    if any(not ids for ids in out):
+        raise web.HTTPBadRequest(text=json.dumps({"error": "empty prompt"}), content_type="application/json")
+    return out
+
+
+def _n_choices(body: dict) -> int:
+    """``n`` choices per prompt; ``best_of`` is accepted only as n (no ranking)."""
+    try:
+        n = 1 if body.get("n") is None else int(body["n"])
+        best_of = body.get("best_of")
+        if not 1 <= n <= MAX_CHOICES or (best_of is not None and int(best_of) != n):
+            raise ValueError
+    except (TypeError, ValueError):
+        raise web.HTTPBadRequest(text=json.dumps({"error": f"n must be 1..{MAX_CHOICES}; best_of, if given, "
+                                                           "must equal n"}), content_type="application/json") from None
+    return n
 
 
 def _params(st: ServerState, body: dict, n_prompt: int, chat: bool = False) -> tuple[GenParams, list[str]]:
@@ -85,10 +113,6 @@ def _params(st: ServerState, body: dict, n_prompt: int, chat: bool = False) -> t
     if temp < 0:
         raise web.HTTPBadRequest(text=json.dumps({"error": "temperature must be >= 0"}),
                                  content_type="application/json")
-    for key in ("n", "best_of"):
-        if body.get(key) is not None and int(body[key]) != 1:
-            raise web.HTTPBadRequest(text=json.dumps({"error": f"{key} > 1 is not supported (one choice per request)"}),
-                                     content_type="application/json")
     try:
         top_p = 1.0 if body.get("top_p") is None else float(body["top_p"])
         top_k = 0 if body.get("top_k") is None else int(body["top_k"])
@@ -144,14 +168,74 @@ def _err(code: int, msg: str) -> web.Response:
     return web.json_response({"error": {"message": msg, "code": code}}, status=code)
 
 
+class _Choice:
+    """One generated sequence of a request: its token stream, the text after the
+    EOS and stop-string rules, the token count and the log-probability records."""
+
+    def __init__(self, index: int, n_prompt: int, ts, params: GenParams, stops: list[str]):
+        self.index, self.n_prompt, self.ts, self.params, self.stops = index, n_prompt, ts, params, stops
+        self.text = ""
+        self.out_ids: list[int] = []
+        self.finish: str | None = None
+        self.error: str | None = None
+        self.lp_entries: list = []   # chat records, or (piece, lp, alts) for completions
+
+
+async def _consume(st: ServerState, ch: _Choice, chat: bool, emit=None) -> None:
+    """Reads the choice's stream to its end; ``emit(ch, piece, lp_record)`` is awaited
+    for every piece of text (streaming responses)."""
+    want_lp = ch.params.logprobs is not None
+    ts = ch.ts
+    while True:
+        kind, val = await ts.q.get()
+        if kind == "error":
+            ch.error, ch.finish = val, "error"
+            return
+        if kind == "done":
+            ch.finish = "stop" if val == "stop" else ("length" if val == "length" else val)
+            return
+        tok, lp = int(val[0]), val[1]
+        ch.out_ids.append(tok)
+        if tok == st.tok.eos_token_id and not ch.params.ignore_eos:
+            continue
+        piece = st.tok.decode_token(tok)
+        if ch.stops:
+            cand = ch.text + piece
+            hit = min((cand.find(s) for s in ch.stops if s in cand), default=-1)
+            if hit >= 0:
+                piece = cand[:hit][len(ch.text):]
+                ch.text = cand[:hit]
+                st.loop.cancel(ts)
+                lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None and piece) else None
+                if lpe is not None:
+                    ch.lp_entries.append(lpe)
+                if emit is not None and piece:
+                    await emit(ch, piece, lpe)
+                ch.finish = "stop"
+                while True:          # drain until the engine confirms the cancel
+                    k2, _ = await ts.q.get()
+                    if k2 in ("done", "error"):
+                        return
+        lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None) else None
+        if lpe is not None:
+            ch.lp_entries.append(lpe)
+        ch.text += piece
+        if emit is not None:
+            await emit(ch, piece, lpe)
+
+
 async def _generate(st: ServerState, request: web.Request, chat: bool):
+    """One request: every prompt (completions take a list) times ``n`` choices, each
+    its own engine request (a seeded request's choice j uses seed + j); choice
+    index = prompt index * n + j."""
     try:
         body = await request.json()
     except Exception as e:  # noqa: BLE001
         return _err(400, f"invalid JSON: {e}")
     try:
-        ids = _prompt_ids(st, body, chat)
-        params, stops = _params(st, body, len(ids), chat)
+        prompts = _prompt_ids(st, body, chat)
+        params, stops = _params(st, body, max(len(p) for p in prompts), chat)
+        n = _n_choices(body)
     except web.HTTPBadRequest as e:
         return web.Response(status=400, text=e.text, content_type="application/json")
     if not st.loop.healthy:
@@ -159,98 +243,77 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
     stream = bool(body.get("stream", False))
     rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:16]
     created = int(time.time())
-    ts = st.loop.submit(ids, params)
-    out_ids: list[int] = []
-    text = ""
-    finish = None
     want_lp = params.logprobs is not None
-    lp_entries: list = []        # per emitted token (chat records, or (piece, lp, alts) for completions)
+    choices = []
+    for pi, ids in enumerate(prompts):
+        for j in range(n):
+            pj = params if params.seed is None or j == 0 else dataclasses.replace(params, seed=params.seed + j)
+            choices.append(_Choice(pi * n + j, len(ids), st.loop.submit(ids, pj), pj, stops))
 
-    def chunk_obj(piece: str | None, fin: str | None, lpe=None) -> dict:
+    def chunk_obj(ch: _Choice, piece: str | None, fin: str | None, lpe=None) -> dict:
         if chat:
             delta = {} if piece is None else {"content": piece}
-            if piece is not None and not out_ids[:-1]:
+            if piece is not None and not ch.out_ids[:-1]:
                 delta["role"] = "assistant"
-            ch = {"index": 0, "delta": delta, "finish_reason": fin}
+            c = {"index": ch.index, "delta": delta, "finish_reason": fin}
             if want_lp:
-                ch["logprobs"] = {"content": [lpe]} if lpe is not None else None
+                c["logprobs"] = {"content": [lpe]} if lpe is not None else None
             return {"id": rid, "object": "chat.completion.chunk", "created": created, "model": st.model_name,
-                    "choices": [ch]}
-        lpo = _completion_logprobs([lpe], len(text) - len(piece or "")) if lpe is not None else None
+                    "choices": [c]}
+        lpo = _completion_logprobs([lpe], len(ch.text) - len(piece or "")) if lpe is not None else None
         return {"id": rid, "object": "text_completion", "created": created, "model": st.model_name,
-                "choices": [{"index": 0, "text": piece or "", "finish_reason": fin, "logprobs": lpo}]}
+                "choices": [{"index": ch.index, "text": piece or "", "finish_reason": fin, "logprobs": lpo}]}
 
     resp = None
+    emit = None
     if stream:
         resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
         await resp.prepare(request)
+
+        async def emit(ch, piece, lpe):
+            await resp.write(f"data: {json.dumps(chunk_obj(ch, piece, None, lpe))}\n\n".encode())
     try:
-        while True:
-            kind, val = await ts.q.get()
-            if kind == "error":
-                if resp is None:
-                    return _err(500 if ts.req is not None else 400, val)
-                await resp.write(f"data: {json.dumps({'error': {'message': val}})}\n\n".encode())
-                finish = "error"
-                break
-            if kind == "done":
-                finish = "stop" if val == "stop" else ("length" if val == "length" else val)
-                break
-            tok, lp = int(val[0]), val[1]
-            out_ids.append(tok)
-            if tok == st.tok.eos_token_id and not params.ignore_eos:
-                continue
-            piece = st.tok.decode_token(tok)
-            if stops:
-                cand = text + piece
-                hit = min((cand.find(s) for s in stops if s in cand), default=-1)
-                if hit >= 0:
-                    piece = cand[:hit][len(text):]
-                    text = cand[:hit]
-                    st.loop.cancel(ts)
-                    lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None and piece) else None
-                    if lpe is not None:
-                        lp_entries.append(lpe)
-                    if resp is not None and piece:
-                        await resp.write(f"data: {json.dumps(chunk_obj(piece, None, lpe))}\n\n".encode())
-                    finish = "stop"
-                    # drain until the engine confirms the cancel
-                    while True:
-                        k2, _ = await ts.q.get()
-                        if k2 in ("done", "error"):
-                            break
-                    break
-            lpe = _lp_entry(st, piece, lp, chat) if (want_lp and lp is not None) else None
-            if lpe is not None:
-                lp_entries.append(lpe)
-            text += piece
-            if resp is not None:
-                await resp.write(f"data: {json.dumps(chunk_obj(piece, None, lpe))}\n\n".encode())
+        await asyncio.gather(*(_consume(st, ch, chat, emit) for ch in choices))
     except (asyncio.CancelledError, ConnectionResetError):
-        st.loop.cancel(ts)
+        for ch in choices:
+            st.loop.cancel(ch.ts)
         raise
-    usage = {"prompt_tokens": len(ids), "completion_tokens": len(out_ids), "total_tokens": len(ids) + len(out_ids)}
+    failed = [ch for ch in choices if ch.error is not None]
+    if failed and resp is None:
+        for ch in choices:
+            st.loop.cancel(ch.ts)
+        refused = any(ch.ts.req is None for ch in failed)    # the engine refused it before it started
+        return _err(400 if refused else 500, failed[0].error)
+    n_out = sum(len(ch.out_ids) for ch in choices)
+    n_in = sum(len(p) for p in prompts)
+    usage = {"prompt_tokens": n_in, "completion_tokens": n_out, "total_tokens": n_in + n_out}
     if resp is not None:
-        last = chunk_obj(None, finish)
-        last["usage"] = usage
-        await resp.write(f"data: {json.dumps(last)}\n\n".encode())
+        for ch in choices:
+            if ch.error is not None:
+                await resp.write(f"data: {json.dumps({'error': {'message': ch.error}})}\n\n".encode())
+            last = chunk_obj(ch, None, ch.finish)
+            if ch is choices[-1]:
+                last["usage"] = usage
+            await resp.write(f"data: {json.dumps(last)}\n\n".encode())
         await resp.write(b"data: [DONE]\n\n")
         await resp.write_eof()
         return resp
-    if chat:
-        choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish}
-        if want_lp:
-            choice["logprobs"] = {"content": lp_entries}
-        obj = "chat.completion"
-    else:
-        choice = {"index": 0, "text": text, "finish_reason": finish,
-                  "logprobs": _completion_logprobs(lp_entries, 0) if want_lp else None}
-        obj = "text_completion"
-    req = ts.req
+    out = []
+    for ch in choices:
+        if chat:
+            c = {"index": ch.index, "message": {"role": "assistant", "content": ch.text}, "finish_reason": ch.finish}
+            if want_lp:
+                c["logprobs"] = {"content": ch.lp_entries}
+        else:
+            c = {"index": ch.index, "text": ch.text, "finish_reason": ch.finish,
+                 "logprobs": _completion_logprobs(ch.lp_entries, 0) if want_lp else None}
+        out.append(c)
+    req = choices[0].ts.req
     metrics = {"ttft_s": (req.t_first_token - req.t_arrival) if req and req.t_first_token else None,
                "e2e_s": (req.t_done - req.t_arrival) if req and req.t_done else None}
-    return web.json_response({"id": rid, "object": obj, "created": created, "model": st.model_name,
-                              "choices": [choice], "usage": usage, "x_metrics": metrics})
+    return web.json_response({"id": rid, "object": "chat.completion" if chat else "text_completion",
+                              "created": created, "model": st.model_name, "choices": out, "usage": usage,
+                              "x_metrics": metrics})
 
 
 def build_app(st: ServerState) -> web.Application:

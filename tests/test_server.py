@@ -226,7 +226,7 @@ def test_temperature_sampling_and_refusals(served):
             hot.append(await r.json())
         bad = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "top_p": 1.5})
         neg = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "temperature": -1})
-        for extra in ({"n": 2}, {"best_of": 3}, {"logprobs": 21}, {"top_p": 0}, {"top_k": "x"}):
+        for extra in ({"n": 0}, {"best_of": 3}, {"logprobs": 21}, {"top_p": 0}, {"top_k": "x"}, {"n": 65}):
             r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, **extra})
             assert r.status == 400, extra
         ok = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "n": 1, "logprobs": None})
@@ -288,3 +288,42 @@ def test_logprobs_and_nucleus_sampling(served):
     assert k1["choices"][0]["text"] == "".join(tok.decode_token(t) for t in want)
     pieces = [ch["choices"][0]["logprobs"] for ch in streamed if ch["choices"][0]["text"]]
     assert len(pieces) == 3 and all(len(p["tokens"]) == 1 for p in pieces)
+
+
+def test_n_choices_and_batched_prompts(served):
+    """A list of prompts times n choices: greedy choices equal the oracle per
+    prompt with index = prompt * n + j; seeded sampled choices repeat on a second
+    request; a streamed request tags every chunk with its choice index."""
+    st, eng = served
+    p1 = [0] + [50 + (3 * i) % 120 for i in range(14)]
+    p2 = [0] + [60 + (7 * i) % 110 for i in range(9)]
+    w1, w2 = _greedy(eng, p1, 4), _greedy(eng, p2, 4)
+
+    async def go(c):
+        batch = await (await c.post("/v1/completions", json={"prompt": [p1, p2], "n": 2, "max_tokens": 4,
+                                                              "ignore_eos": True})).json()
+        body = {"messages": [{"role": "user", "content": "pick"}], "n": 3, "max_tokens": 5, "ignore_eos": True,
+                "temperature": 3.0, "seed": 11}
+        s1 = await (await c.post("/v1/chat/completions", json=body)).json()
+        s2 = await (await c.post("/v1/chat/completions", json=body)).json()
+        r = await c.post("/v1/completions", json={"prompt": p1, "n": 2, "max_tokens": 4, "ignore_eos": True,
+                                                  "stream": True})
+        parts = {}
+        async for raw in r.content:
+            line = raw.decode().strip()
+            if line.startswith("data: {"):
+                ch = json.loads(line[6:])["choices"][0]
+                parts.setdefault(ch["index"], []).append(ch["text"])
+        return batch, s1, s2, parts
+    batch, s1, s2, parts = _run(st, go)
+    tok = st.tok
+    t1, t2 = ("".join(tok.decode_token(t) for t in w) for w in (w1, w2))
+    ch = sorted(batch["choices"], key=lambda c: c["index"])
+    assert [c["index"] for c in ch] == [0, 1, 2, 3]
+    assert [c["text"] for c in ch] == [t1, t1, t2, t2]
+    assert batch["usage"]["completion_tokens"] == 16 and batch["usage"]["prompt_tokens"] == len(p1) + len(p2)
+    a = {c["index"]: c["message"]["content"] for c in s1["choices"]}
+    b = {c["index"]: c["message"]["content"] for c in s2["choices"]}
+    assert a == b and sorted(a) == [0, 1, 2]
+    assert len(set(a.values())) > 1        # choices draw with seeds 11, 12, 13
+    assert {i: "".join(v) for i, v in parts.items()} == {0: t1, 1: t1}
