@@ -38,6 +38,14 @@ def render_prometheus(st) -> str:
     metric("waiting_requests", "gauge", "Requests queued for a slot.", len(sched.waiting))
     metric("cache_slots_used_ratio", "gauge", "Fraction of KV cache slots in use.",
            f"{1.0 - sched.slots.n_free / max(sched.max_seqs, 1):.4f}")
+    kv = getattr(sched, "kv", None)
+    if kv is not None and hasattr(kv, "free_blocks"):
+        free = kv.free_blocks()
+        lines.append("# HELP dsv4_kv_blocks_used_ratio Fraction of the paged compressed-cache blocks in use, per "
+                     "compression ratio.")
+        lines.append("# TYPE dsv4_kv_blocks_used_ratio gauge")
+        for r in sorted(free):
+            lines.append(f'dsv4_kv_blocks_used_ratio{{ratio="{r}"}} {1.0 - free[r] / max(kv.n_blocks[r], 1):.4f}')
     metric("preemptions_total", "counter", "Requests preempted for recompute (paged caches, kv_preempt).",
            getattr(sched, "n_preempted", 0))
     metric("graph_captures_total", "counter", "CUDA graphs captured.", eng.stats.get("graph_captures", 0))

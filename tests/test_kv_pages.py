@@ -232,3 +232,22 @@ def test_engine_with_preemption_matches_greedy_on_the_oracle():
         out, _ = ref.generate(torch.tensor([p]), 26)
         assert r.output == out[0].tolist()
         assert len(r.logprobs) == 26 and all(e["top"][0][0] == t for e, t in zip(r.logprobs, r.output))
+
+
+def test_metrics_report_paged_block_use():
+    import types
+
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.serving.metrics import render_prometheus
+
+    pg = KvPager(toy_v4_config(), "cpu", 3, 1024, 16, 640)
+    sched = Scheduler(max_seqs=2, max_batched_tokens=64, max_seq_len=1024, kv=pg)
+    sched.add(list(range(300)), 10)
+    sched.schedule()                                   # admits: 78 entries of ratio 4 -> 5 of 10 blocks
+    loop = types.SimpleNamespace(stats={"requests": 1, "finished": 0, "failed": 0, "prompt_tokens": 300,
+                                        "generated_tokens": 0, "steps": 0, "step_time_s": 0.0,
+                                        "last_batch_tokens": 0},
+                                 step_ms_window=[], ttft_window=[], healthy=True,
+                                 engine=types.SimpleNamespace(sched=sched, stats={}))
+    text = render_prometheus(types.SimpleNamespace(loop=loop))
+    assert 'dsv4_kv_blocks_used_ratio{ratio="4"} 0.5000' in text
