@@ -46,6 +46,8 @@ class EngineConfig:
     dspark_force_accept: int | None = None
     engram_host_tables: bool = True
     engram_shm: str | None = None           # random-init Engram tables in shared files (e.g. /dev/shm/dsv4_engram)
+    control_plane: str = "shm"              # multi-rank control messages: "shm" (one node, shared memory)
+                                            # or "gloo" (the CPU process group)
     host: str = "127.0.0.1"
     port: int = 8000
     step_deadline_s: float = 600.0

@@ -10,6 +10,10 @@ model step, so all ranks step in lockstep.  Per step:
            when this rank has none, to join the step's collectives)
   all      gather     [(request id, token, finished, reason, logprob)] -> rank 0
 
+The messages travel on a control channel (engine/control.py): by default a
+shared-memory file for the ranks of one node (tens of microseconds per round
+trip), or the CPU process group (gloo; milliseconds, across nodes).
+
 Rank 0 assigns new requests to the rank with the fewest live requests.  In the
 replicated mode (tensor-parallel layout) every request goes to every rank: the
 local schedulers see the same adds and cancels in the same order, so they
@@ -30,9 +34,8 @@ from __future__ import annotations
 import time
 from dataclasses import dataclass, field
 
-import torch.distributed as dist
-
 from ..models.model import SeqChunk, StepMeta
+from .control import GlooControl
 
 
 @dataclass
@@ -127,13 +130,15 @@ def _local_step(engine, msg: dict, rank: int, id_map: dict, pad_slot: int, repli
 class DistributedEngine:
     """Rank-0 front with the :class:`.engine.Engine` API over all ranks."""
 
-    def __init__(self, local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False):
+    def __init__(self, local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False,
+                 control=None):
         self.local = local_engine
         self.replicated = replicated
         self.cfg = local_engine.cfg
         self.group = cpu_group
-        self.rank = dist.get_rank(cpu_group)
-        self.world = dist.get_world_size(cpu_group)
+        self.ctl = control if control is not None else GlooControl(cpu_group)
+        self.rank = self.ctl.rank
+        self.world = self.ctl.world
         self.pad_slot = local_engine.sched.max_seqs if pad_slot is None else pad_slot
         self.live: dict[int, GlobalRequest] = {}
         self.pending_adds: list[GlobalRequest] = []
@@ -175,11 +180,9 @@ class DistributedEngine:
         self.pending_adds = []
         msg = {"adds": adds, "cancels": self.pending_cancels, "any_work": bool(self.live), "stop": False}
         self.pending_cancels = []
-        box = [msg]
-        dist.broadcast_object_list(box, src=0, group=self.group)
+        self.ctl.broadcast(msg)
         mine = _local_step(self.local, msg, 0, self.id_map, self.pad_slot, self.replicated)
-        gathered = [None] * self.world
-        dist.gather_object(mine, gathered, dst=0, group=self.group)
+        gathered = self.ctl.gather(mine)
         now = time.perf_counter()
         events = []
         for evs in gathered:
@@ -209,8 +212,8 @@ class DistributedEngine:
         self.step()
 
     def shutdown(self) -> None:
-        box = [{"adds": [], "cancels": [], "any_work": False, "stop": True}]
-        dist.broadcast_object_list(box, src=0, group=self.group)
+        self.ctl.broadcast({"adds": [], "cancels": [], "any_work": False, "stop": True})
+        self.ctl.close()
 
     def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False) -> list[list[int]]:
         reqs = [self.add_request(p, max_new_tokens, ignore_eos) for p in prompts]
@@ -219,18 +222,19 @@ class DistributedEngine:
         return [r.output for r in reqs]
 
 
-def worker_loop(local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False) -> int:
+def worker_loop(local_engine, cpu_group=None, pad_slot: int | None = None, replicated: bool = False,
+                control=None) -> int:
     """Ranks > 0: follow rank 0's control messages until it sends stop. Returns steps run."""
-    rank = dist.get_rank(cpu_group)
+    ctl = control if control is not None else GlooControl(cpu_group)
+    rank = ctl.rank
     pad = local_engine.sched.max_seqs if pad_slot is None else pad_slot
     id_map: dict = {}
     n = 0
     while True:
-        box = [None]
-        dist.broadcast_object_list(box, src=0, group=cpu_group)
-        msg = box[0]
+        msg = ctl.broadcast()
         if msg["stop"]:
+            ctl.close()
             return n
         mine = _local_step(local_engine, msg, rank, id_map, pad, replicated)
-        dist.gather_object(mine, None, dst=0, group=cpu_group)
+        ctl.gather(mine)
         n += 1

@@ -130,12 +130,16 @@ def main(argv: list[str] | None = None) -> None:
     replicated = world > 1 and ec.parallel == "tp"
     local = build_local_engine(ec, None if replicated else par, extra_slots=1 if world > 1 else 0,
                                tp=par if replicated else None)
+    ctl = None
+    if world > 1:
+        from ..engine.control import make_control
+        ctl = make_control(ec.control_plane, cpu_group)
     if rank != 0:
-        worker_loop(local, cpu_group, replicated=replicated)
+        worker_loop(local, cpu_group, replicated=replicated, control=ctl)
         local.graphs.clear()
         dist.destroy_process_group()
         return
-    eng = DistributedEngine(local, cpu_group, replicated=replicated) if world > 1 else local
+    eng = DistributedEngine(local, cpu_group, replicated=replicated, control=ctl) if world > 1 else local
     if ec.dspark:
         eng = build_spec_engine(ec, local)
     loop = EngineLoop(eng, step_deadline_s=ec.step_deadline_s).start()
