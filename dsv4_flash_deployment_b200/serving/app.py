@@ -270,8 +270,20 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
         resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
         await resp.prepare(request)
 
+        # the per-token event without log-probabilities, past the first chunk of a
+        # chat choice (which carries the role), is the same text around the piece:
+        # built from a fixed head and tail instead of encoding a dict per token
+        head = json.dumps({"id": rid, "object": "chat.completion.chunk" if chat else "text_completion",
+                           "created": created, "model": st.model_name})[:-1]
+        tail = ('}, "finish_reason": null}]}\n\n' if chat else ', "finish_reason": null, "logprobs": null}]}\n\n')
+
         async def emit(ch, piece, lpe):
-            await resp.write(f"data: {json.dumps(chunk_obj(ch, piece, None, lpe))}\n\n".encode())
+            if lpe is None and not want_lp and not (chat and not ch.out_ids[:-1]):
+                key = '"delta": {"content": ' if chat else '"text": '
+                line = f'data: {head}, "choices": [{{"index": {ch.index}, {key}{json.dumps(piece)}{tail}'
+            else:
+                line = f"data: {json.dumps(chunk_obj(ch, piece, None, lpe))}\n\n"
+            await resp.write(line.encode())
     try:
         await asyncio.gather(*(_consume(st, ch, chat, emit) for ch in choices))
     except (asyncio.CancelledError, ConnectionResetError):

@@ -48,6 +48,29 @@ class TokenStream:
         self.loop.call_soon_threadsafe(self.q.put_nowait, item)
 
 
+def _deliver(items) -> None:
+    for q, item in items:
+        q.put_nowait(item)
+
+
+class _Outbox:
+    """A step's stream items, handed to each event loop in one call: one wake-up of
+    the HTTP thread per step instead of one per generated token (each
+    ``call_soon_threadsafe`` writes to the loop's wake-up pipe and takes the lock
+    of its ready queue)."""
+
+    def __init__(self):
+        self.by_loop: dict = {}
+
+    def put(self, s: TokenStream, item) -> None:
+        self.by_loop.setdefault(s.loop, []).append((s.q, item))
+
+    def flush(self) -> None:
+        for loop, items in self.by_loop.items():
+            loop.call_soon_threadsafe(_deliver, items)
+        self.by_loop = {}
+
+
 class EngineLoop:
     def __init__(self, engine, step_deadline_s: float = 600.0, idle_wait_s: float = 0.002):
         self.engine = engine
@@ -163,6 +186,7 @@ class EngineLoop:
             if dt > self.step_deadline_s:
                 self.healthy = False
                 self.error = f"step took {dt:.1f} s (deadline {self.step_deadline_s} s)"
+            out = _Outbox()
             for req, tok in events:
                 s = self._live.get(req.req_id)
                 if s is None:
@@ -173,11 +197,12 @@ class EngineLoop:
                         self.ttft_window.append(time.perf_counter() - s.t_submit)
                     lps = getattr(req, "logprobs", None)
                     lp = lps[len(req.output) - 1] if lps and len(lps) >= len(req.output) else None
-                    s.put(("token", (tok, lp)))
+                    out.put(s, ("token", (tok, lp)))
             # finished (length / stop / cancelled) requests
             for rid in [rid for rid, s in self._live.items() if s.req.finished]:
                 s = self._live.pop(rid)
                 self.stats["finished"] += 1
-                s.put(("done", s.req.finish_reason))
+                out.put(s, ("done", s.req.finish_reason))
+            out.flush()
             if not self.healthy:
                 self._fail_all(self.error)

@@ -327,3 +327,24 @@ def test_n_choices_and_batched_prompts(served):
     assert a == b and sorted(a) == [0, 1, 2]
     assert len(set(a.values())) > 1        # choices draw with seeds 11, 12, 13
     assert {i: "".join(v) for i, v in parts.items()} == {0: t1, 1: t1}
+
+
+def test_streamed_chat_chunks_parse_and_match_the_full_answer(served):
+    st, _ = served
+    body = {"messages": [{"role": "user", "content": "stream me"}], "max_tokens": 6, "ignore_eos": True}
+
+    async def go(c):
+        full = await (await c.post("/v1/chat/completions", json=body)).json()
+        r = await c.post("/v1/chat/completions", json={**body, "stream": True})
+        chunks = []
+        async for raw in r.content:
+            line = raw.decode().strip()
+            if line.startswith("data: {"):
+                chunks.append(json.loads(line[6:]))
+        return full, chunks
+    full, chunks = _run(st, go)
+    deltas = [c["choices"][0]["delta"] for c in chunks]
+    assert deltas[0].get("role") == "assistant"
+    assert all(c["object"] == "chat.completion.chunk" and c["id"] == chunks[0]["id"] for c in chunks)
+    assert "".join(d.get("content", "") for d in deltas) == full["choices"][0]["message"]["content"]
+    assert chunks[-1]["choices"][0]["finish_reason"] == "length" and "usage" in chunks[-1]
