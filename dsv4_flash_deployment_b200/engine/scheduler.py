@@ -139,20 +139,23 @@ class Scheduler:
         preempted = self._grow_or_preempt() if self.preempt else 0
         out: list[ScheduledChunk] = []
         budget = self.budget
+        prefilling = []
         for r in self.running:
-            if r.prompt_done and budget > 0:
-                out.append(ScheduledChunk(r, r.position, [r.output[-1]], True))
-                budget -= 1
+            if r.prompt_done:
+                if budget > 0:
+                    out.append(ScheduledChunk(r, r.position, [r.output[-1]], True))
+                    budget -= 1
+            else:
+                prefilling.append(r)
         # continue partially prefilled requests first, then admit new ones
-        for r in self.running:
+        for r in prefilling:
             if budget <= 0:
                 break
-            if not r.prompt_done:
-                pf = r.prefill
-                n = min(self.chunk, budget, len(pf) - r.n_prefilled)
-                out.append(ScheduledChunk(r, r.n_prefilled, pf[r.n_prefilled:r.n_prefilled + n],
-                                          r.n_prefilled + n == len(pf)))
-                budget -= n
+            pf = r.prefill
+            n = min(self.chunk, budget, len(pf) - r.n_prefilled)
+            out.append(ScheduledChunk(r, r.n_prefilled, pf[r.n_prefilled:r.n_prefilled + n],
+                                      r.n_prefilled + n == len(pf)))
+            budget -= n
         while budget > 0 and self.waiting and self.slots.n_free > 0 and not preempted:
             r = self.waiting[0]
             pf = r.prefill

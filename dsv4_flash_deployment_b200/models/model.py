@@ -63,27 +63,40 @@ class SeqChunk:
 class StepMeta:
     """Host description of one mixed step, and its pinned/device mirrors."""
 
-    def __init__(self, cfg, chunks: list[SeqChunk], ring_pad_slot: int | None = None):
+    # per-chunk numeric fields, one column each (built in one pass over the chunks)
+    _FIELDS = ("len", "start", "slot", "sample", "sample_all", "temperature", "top_k", "top_p")
+
+    @staticmethod
+    def _columns(chunks: list[SeqChunk]) -> np.ndarray:
+        if not chunks:
+            return np.zeros((0, len(StepMeta._FIELDS)))
+        return np.array([(len(c.tokens), c.start_pos, c.slot, c.sample, c.sample_all, c.temperature, c.top_k, c.top_p)
+                         for c in chunks], dtype=np.float64)
+
+    def __init__(self, cfg, chunks: list[SeqChunk], ring_pad_slot: int | None = None, _cols=None, _ids=None):
         self.cfg = cfg
         self.chunks = chunks
         n = len(chunks)
-        lens = np.fromiter((len(c.tokens) for c in chunks), np.int64, n)
-        starts = np.fromiter((c.start_pos for c in chunks), np.int64, n)
-        slots = np.fromiter((c.slot for c in chunks), np.int64, n)
-        samp = np.fromiter((c.sample for c in chunks), bool, n)
+        cols = self._columns(chunks) if _cols is None else _cols
+        self._cols = cols
+        lens = cols[:, 0].astype(np.int64)
+        starts = cols[:, 1].astype(np.int64)
+        slots = cols[:, 2].astype(np.int64)
+        samp = cols[:, 3] != 0
         row0 = np.zeros(n, np.int64)
         if n:
             row0[1:] = np.cumsum(lens)[:-1]
         T = int(lens.sum())
         self.T = T
-        self.ids = np.fromiter(itertools.chain.from_iterable(c.tokens for c in chunks), np.int32, T)
+        self.ids = (np.fromiter(itertools.chain.from_iterable(c.tokens for c in chunks), np.int32, T)
+                    if _ids is None else _ids)
         offs = np.arange(T, dtype=np.int64) - np.repeat(row0, lens)
         self.pos = (np.repeat(starts, lens) + offs).astype(np.int32)
         self.slot = np.repeat(slots, lens).astype(np.int32)
         self.chunk_start = np.repeat(starts, lens).astype(np.int32)
         self.step_row0 = np.repeat(row0, lens).astype(np.int32)
         self.last_pos = np.repeat(starts + lens - 1, lens).astype(np.int32)
-        sall = np.fromiter((c.sample_all for c in chunks), bool, n)
+        sall = cols[:, 4] != 0
         if sall.any():
             rows = [np.arange(row0[i], row0[i] + lens[i]) if sall[i] else
                     (np.array([row0[i] + lens[i] - 1]) if samp[i] else np.zeros(0, np.int64)) for i in range(n)]
@@ -91,25 +104,31 @@ class StepMeta:
         else:
             self.sample_rows = (row0 + lens - 1)[samp].astype(np.int32)
         # per sampled row: 0 = greedy, > 0 = temperature (one value per chunk)
-        temps = np.fromiter((c.temperature for c in chunks), np.float32, n)
+        temps = cols[:, 5].astype(np.float32)
         per_chunk = np.where(sall, lens, samp.astype(np.int64))
         self.temps = np.repeat(temps, per_chunk).astype(np.float32)
         self.sampling = bool((self.temps > 0).any())
         # top-k / top-p per sampled row (0 / 1.0: off); they only act on rows with T > 0
-        topk = np.fromiter((c.top_k for c in chunks), np.int32, n)
-        topp = np.fromiter((c.top_p for c in chunks), np.float32, n)
+        topk = cols[:, 6].astype(np.int32)
+        topp = cols[:, 7].astype(np.float32)
         self.topk = np.repeat(topk, per_chunk).astype(np.int32)
         self.topp = np.repeat(topp, per_chunk).astype(np.float32)
         self.filtering = bool(((self.temps > 0) & ((self.topk > 0) | (self.topp < 1.0))).any())
-        # seeded rows: the noise key of (seed, position of the sampled token)
-        seeds = [c.seed for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
-        spos = self.pos[self.sample_rows] if len(self.sample_rows) else np.zeros(0, np.int32)
-        self.has_seed = np.array([sd is not None for sd in seeds], dtype=bool)
-        self.seedkey = np.array([seed_key(sd, int(p)) if sd is not None else 0 for sd, p in zip(seeds, spos)],
-                                dtype=np.int64)
+        S = len(self.sample_rows)
+        if any(c.seed is not None or c.logprobs is not None for c in chunks):
+            # seeded rows: the noise key of (seed, position of the sampled token)
+            seeds = [c.seed for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
+            spos = self.pos[self.sample_rows] if S else np.zeros(0, np.int32)
+            self.has_seed = np.array([sd is not None for sd in seeds], dtype=bool)
+            self.seedkey = np.array([seed_key(sd, int(p)) if sd is not None else 0 for sd, p in zip(seeds, spos)],
+                                    dtype=np.int64)
+            # alternatives wanted per sampled row (None: no log-probabilities)
+            self.lp_want = [c.logprobs for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
+        else:
+            self.has_seed = np.zeros(S, bool)
+            self.seedkey = np.zeros(S, np.int64)
+            self.lp_want = [None] * S
         self.seeded = bool((self.has_seed & (self.temps > 0)).any())
-        # alternatives wanted per sampled row (None: no log-probabilities)
-        self.lp_want = [c.logprobs for c, k in zip(chunks, per_chunk) for _ in range(int(k))]
         self.want_lp = any(w is not None for w in self.lp_want)
         self.max_pos = int(self.pos.max()) if T else 0
         # compressor groups closed in this step, per ratio (token order)
@@ -154,9 +173,13 @@ class StepMeta:
         T_b = token_bucket(self.T, max_tokens)
         S = len(self.sample_rows)
         chunks = list(self.chunks)
+        cols, ids = self._cols, self.ids
         if T_b > self.T:
-            chunks.append(SeqChunk(pad_slot, 0, [0] * (T_b - self.T), sample=False))
-        m = StepMeta(self.cfg, chunks)
+            pad = SeqChunk(pad_slot, 0, [0] * (T_b - self.T), sample=False)
+            chunks.append(pad)
+            cols = np.concatenate([cols, self._columns([pad])])
+            ids = np.concatenate([ids, np.zeros(T_b - self.T, np.int32)])
+        m = StepMeta(self.cfg, chunks, _cols=cols, _ids=ids)
         S_b = token_bucket(S, max(S, min(max_sample, T_b)))
         if S_b > S:
             extra = S_b - S

@@ -61,3 +61,37 @@ def test_padded_step_keeps_real_rows_first():
     # never above the buffers
     big = StepMeta(cfg, [SeqChunk(0, 0, list(range(1, 500)))]).padded(max_tokens=500, max_sample=4, pad_slot=9)
     assert big.T == 500 and len(big.sample_rows) == 1
+
+
+def test_padded_meta_extends_every_array_of_the_step():
+    """The padded step keeps every real token's and sampled row's values and
+    appends the padding chunk (positions 0.. of the pad slot, not sampled)."""
+    import numpy as np
+
+    from dsv4_flash_deployment_b200.config import toy_v4_config
+    from dsv4_flash_deployment_b200.models.model import SeqChunk, StepMeta
+
+    cfg = toy_v4_config()
+    rng = np.random.default_rng(3)
+    for trial in range(20):
+        chunks = []
+        for i in range(int(rng.integers(1, 9))):
+            n = int(rng.integers(1, 12))
+            chunks.append(SeqChunk(i, int(rng.integers(0, 40)), rng.integers(0, 1000, n).tolist(), bool(rng.random() < .8),
+                                   sample_all=bool(rng.random() < .2), temperature=float(rng.choice([0.0, 0.7])),
+                                   top_k=int(rng.choice([0, 5])), seed=None if rng.random() < .5 else int(trial)))
+        m = StepMeta(cfg, chunks)
+        p = m.padded(64, 64, 9)
+        T, S = m.T, len(m.sample_rows)
+        for name in ("ids", "pos", "slot", "chunk_start", "step_row0", "last_pos"):
+            assert np.array_equal(getattr(p, name)[:T], getattr(m, name)), name
+        assert p.T >= T and (p.ids[T:] == 0).all() and (p.slot[T:] == 9).all()
+        assert np.array_equal(p.pos[T:], np.arange(p.T - T))
+        for name in ("sample_rows", "temps", "topk", "topp", "seedkey", "has_seed"):
+            assert np.array_equal(getattr(p, name)[:S], getattr(m, name)), name
+        assert p.n_out == S and p.lp_want[:S] == m.lp_want
+        assert (p.sampling, p.filtering, p.seeded) == (m.sampling, m.filtering, m.seeded)
+        # the same step built directly from its chunks
+        q = StepMeta(cfg, p.chunks)
+        for name in ("ids", "pos", "slot", "last_pos"):
+            assert np.array_equal(getattr(q, name), getattr(p, name)), name
