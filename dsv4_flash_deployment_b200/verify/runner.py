@@ -21,6 +21,9 @@ Stages:
                       pass: mean cosine >= 0.995, worst >= 0.97, top-1 >= 0.8
   parity_neg_control  the same with the mHC Sinkhorn iterations set to 0, which must
                       break parity; pass: mean cosine < 0.99
+  golden              teacher-forced greedy tokens against a golden file (--golden; made by
+                      verify/golden.py from the oracle, or made here when none is given);
+                      pass: tie-aware top-1 >= --min-tie-aware (0.8)
   perf_b{1,2,4,8}     decode TPOT with B sequences at --ctx tokens of context through
                       the serving engine (CUDA-graph replay, H2D + D2H each step)
   dspark_verify       DSpark 1+4 speculative decoding against greedy decoding
@@ -51,8 +54,8 @@ import time
 import traceback
 from pathlib import Path
 
-ALL_STAGES = ("cold_startup", "parity_ref", "parity_neg_control", "perf_b1", "perf_b2", "perf_b4", "perf_b8",
-              "dspark_verify", "tp_parity", "ep_parity", "gsm8k", "gpqa_diamond")
+ALL_STAGES = ("cold_startup", "parity_ref", "parity_neg_control", "golden", "perf_b1", "perf_b2", "perf_b4",
+              "perf_b8", "dspark_verify", "tp_parity", "ep_parity", "gsm8k", "gpqa_diamond")
 
 
 # ------------------------------------------------------------------ result files
@@ -206,6 +209,24 @@ class Runner:
         r["reference_rule_top1_below_0.5"] = r["top1"] < 0.5
         return r
 
+    def stage_golden(self, st: str) -> dict:
+        from .golden import compare, make_golden
+
+        if self.a.golden:
+            with open(self.a.golden) as f:
+                gold = json.load(f)
+            if gold["model"] != self.cfg.name:
+                return skipped(f"golden file is for {gold['model']}, the runner's model is {self.cfg.name}")
+            src = self.a.golden
+        else:
+            prompts = self.sequences(4, 20, self.a.seed + 13)
+            gold = make_golden(self.cfg, self.weights(), prompts, 16, self.a.max_len)
+            src = "made by the oracle in this run"
+        r = compare(gold, self.cfg, self.weights(), self.device)
+        r.update(golden=src, rule=f"tie_aware_top1 >= {self.a.min_tie_aware}",
+                 passed=r["tie_aware_top1"] >= self.a.min_tie_aware)
+        return r
+
     def _perf(self, B: int) -> dict:
         import torch
 
@@ -340,6 +361,8 @@ def parser() -> argparse.ArgumentParser:
     ap.add_argument("--n-seqs", type=int, default=3)
     ap.add_argument("--seq-len", type=int, default=52)
     ap.add_argument("--max-startup-s", type=float, default=900.0)
+    ap.add_argument("--golden", default=None, help="golden token file (verify/golden.py make)")
+    ap.add_argument("--min-tie-aware", type=float, default=0.8)
     ap.add_argument("--ctx", type=int, default=256, help="context of the perf stages")
     ap.add_argument("--perf-steps", type=int, default=20)
     ap.add_argument("--perf-warmup", type=int, default=3)

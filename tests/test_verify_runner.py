@@ -56,3 +56,27 @@ def test_unknown_stage_is_refused(tmp_path):
 
     with pytest.raises(SystemExit):
         vr.main(["--out", str(tmp_path), "--stages", "parity_ref,bogus", *ARGS])
+
+
+def test_golden_files_round_trip_and_catch_a_changed_token(tmp_path):
+    from dsv4_flash_deployment_b200.verify import golden as G
+
+    path = tmp_path / "g.json"
+    assert G.main(["make", "--model", "toy-v4", "--prompts", "2", "--steps", "5", "--prompt-len", "9",
+                   "--out", str(path)]) == 0
+    gold = json.loads(path.read_text())
+    assert gold["model"] == "toy-v4" and len(gold["sequences"]) == 2
+    s0 = gold["sequences"][0]
+    assert len(s0["tokens"]) == 5 and all(lp <= 0 for lp in s0["logprobs"]) and all(g >= 0 for g in s0["top2_gap"])
+    assert G.main(["check", str(path), "--device", "cpu"]) == 0
+    # a golden token that is not the model's argmax (and not a near tie) is caught
+    s0["tokens"][2] = (s0["tokens"][2] + 1) % 1000
+    s0["top2_gap"][2] = 1.0
+    path.write_text(json.dumps(gold))
+    assert G.main(["check", str(path), "--device", "cpu", "--min-tie-aware", "1.0"]) == 1
+    # the runner's golden stage reads a file for its own model
+    out = tmp_path / "v"
+    assert vr.main(["--out", str(out), "--stages", "golden", "--golden", str(path), *ARGS, "--min-tie-aware", "0.5"]) == 0
+    rec = _rec(out, "golden")
+    assert rec["passed"] and rec["strict_top1"] < 1.0 and rec["positions"] == 10
+    assert G.bf16_ulp(1.0) == 2 ** -7 and G.bf16_ulp(-3.0) == 2 ** -6
