@@ -90,3 +90,34 @@ def test_engine_loads_checkpoint(tmp_path):
     ec2 = EngineConfig(device="cpu", model="toy-v4", max_seqs=2, max_batched_tokens=32, max_model_len=64)
     b = build_local_engine(ec2).generate([[0, 5, 9, 33, 70]], 3, ignore_eos=True)
     assert a == b
+
+
+def test_checkpoint_command_line_tools(tmp_path, capsys):
+    """synth -> inspect -> verify -> preshard through the CLI; a checkpoint of
+    another model is reported tensor by tensor and a corrupted file fails verify."""
+    import json
+
+    from dsv4_flash_deployment_b200.io.__main__ import main
+
+    ck, sh = tmp_path / "ck", tmp_path / "sh"
+
+    def run(*args):
+        rc = main(list(args))
+        return rc, json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+
+    rc, out = run("synth", "--model", "toy-v4", "--out", str(ck), "--shard-gib", "0.001")
+    assert rc == 0 and out["tensors"] == 175 and out["files"] > 1
+    rc, out = run("inspect", "--model", "toy-v4", "--ckpt", str(ck))
+    assert rc == 0 and out["ok"] and out["missing"] == out["mismatched"] == out["unexpected"] == 0
+    rc, out = run("inspect", "--model", "v4-check", "--ckpt", str(ck))
+    assert rc == 1 and out["missing"] > 0 and out["first_missing"]
+    rc, out = run("verify", "--ckpt", str(ck))
+    assert rc == 0 and out["files"] == len(list(ck.glob("*.safetensors")))
+    rc, out = run("preshard", "--model", "toy-v4", "--ckpt", str(ck), "--out", str(sh), "--world", "2")
+    assert rc == 0 and len(out["files"]) == 2
+    f = sorted(ck.glob("*.safetensors"))[0]
+    raw = bytearray(f.read_bytes())
+    raw[-1] ^= 0xFF
+    f.write_bytes(bytes(raw))
+    rc, out = run("verify", "--ckpt", str(ck))
+    assert rc == 1 and "sha256 mismatch" in out["error"]
