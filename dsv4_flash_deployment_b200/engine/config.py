@@ -32,6 +32,8 @@ class EngineConfig:
     max_model_len: int = 16384
     kv_block: int = 0                       # paged compressed caches: entries per block (0: per-slot caches)
     kv_pool_tokens: int = 0                 # paged pool size in tokens of context (0: max_seqs * max_model_len)
+    gpu_memory_utilization: float | None = None  # paged caches without kv_pool_tokens: size the pool to
+                                            # fill this fraction of the GPU's memory (vLLM's flag)
     kv_preempt: bool = False                # paged caches: admit on the prompt's blocks, preempt (recompute)
                                             # the newest request when the pool runs short
     use_cuda_graphs: bool = True

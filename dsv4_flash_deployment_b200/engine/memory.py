@@ -63,3 +63,30 @@ def plan_expert_storage(cfg, device, max_tokens: int, n_slots: int, max_seq: int
     avail = free - non_expert_bytes(cfg, max_tokens, n_slots, max_seq) - int(reserve_gb * 2 ** 30)
     n = int(avail // expert_block_bytes(cfg, ep_world))
     return max(1, min(cfg.n_layers, n))
+
+
+def kv_pool_tokens_for(cfg, total_bytes: int, utilization: float, max_tokens: int, n_slots: int, max_seq: int,
+                       kv_block: int, ep_world: int = 1, expert_layers: int | None = None) -> int:
+    """Tokens of context the paged compressed-cache pools can hold when the instance
+    may use ``utilization`` of ``total_bytes`` of HBM (vLLM's
+    ``--gpu-memory-utilization``, which the reference serves with at 0.85): the
+    budget minus the expert blocks of ``expert_layers`` layers (all layers by
+    default, as with a checkpoint) and everything else that is not pool, divided
+    by the pool's bytes per token of context.  Rounded down to whole blocks of
+    the largest ratio; at least one request of ``max_seq`` tokens must fit."""
+    if not 0.0 < utilization <= 1.0:
+        raise ValueError("gpu memory utilization must be in (0, 1]")
+    layers = cfg.n_layers if expert_layers is None else expert_layers
+    experts = layers * expert_block_bytes(cfg, ep_world)
+    p0, p1 = max_seq, max_seq + (1 << 20)
+    b0 = non_expert_bytes(cfg, max_tokens, n_slots, max_seq, kv_block, p0)
+    b1 = non_expert_bytes(cfg, max_tokens, n_slots, max_seq, kv_block, p1)
+    per_token = (b1 - b0) / (p1 - p0)
+    spare = utilization * total_bytes - experts - b0
+    pool = p0 + int(spare // per_token) if per_token > 0 else p0
+    step = max(cfg.ratio(l) for l in cfg.kv_source_layer_ids) * kv_block
+    pool = pool // step * step
+    if pool < max_seq:
+        raise ValueError(f"{utilization:.2f} of {total_bytes / 2 ** 30:.1f} GiB holds the weights and buffers but "
+                         f"not one {max_seq}-token request's caches")
+    return pool

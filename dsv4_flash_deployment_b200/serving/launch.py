@@ -36,11 +36,22 @@ def build_local_engine(ec: EngineConfig, ep=None, extra_slots: int = 0, tp=None)
         world = ep.world if ep is not None else (tp.world if tp is not None and tp.moe == "ep" else 1)
         storage = plan_expert_storage(cfg, torch.device(ec.device, torch.cuda.current_device()),
                                       ec.max_batched_tokens, ec.max_seqs + extra_slots + 1, ec.max_model_len, world)
+    pool = ec.kv_pool_tokens
+    if ec.kv_block and not pool and ec.gpu_memory_utilization:
+        # the paged pools take what the utilization leaves after the weights and buffers
+        from ..engine.memory import kv_pool_tokens_for
+
+        dev = torch.device(ec.device, torch.cuda.current_device())
+        world = ep.world if ep is not None else (tp.world if tp is not None and tp.moe == "ep" else 1)
+        pool = kv_pool_tokens_for(cfg, torch.cuda.get_device_properties(dev).total_memory,
+                                  ec.gpu_memory_utilization, ec.max_batched_tokens, ec.max_seqs + extra_slots + 1,
+                                  ec.max_model_len, ec.kv_block, world,
+                                  expert_layers=None if weights is not None else storage)
     return Engine.build(cfg, device=ec.device, max_seqs=ec.max_seqs, max_batched_tokens=ec.max_batched_tokens,
                         max_seq_len=ec.max_model_len, weights=weights, seed=ec.seed,
                         expert_storage_layers=storage, ep=ep, use_graphs=ec.use_cuda_graphs,
                         chunk_size=ec.chunk_size, extra_slots=extra_slots, tp=tp, kv_block=ec.kv_block,
-                        kv_pool_tokens=ec.kv_pool_tokens, kv_preempt=ec.kv_preempt, engram_shm=ec.engram_shm,
+                        kv_pool_tokens=pool, kv_preempt=ec.kv_preempt, engram_shm=ec.engram_shm,
                         engram_token_map=_engram_token_map(ec, cfg))
 
 

@@ -251,3 +251,28 @@ def test_metrics_report_paged_block_use():
                                  engine=types.SimpleNamespace(sched=sched, stats={}))
     text = render_prometheus(types.SimpleNamespace(loop=loop))
     assert 'dsv4_kv_blocks_used_ratio{ratio="4"} 0.5000' in text
+
+
+def test_pool_size_from_memory_utilization():
+    """The pool fills what the utilization leaves after weights and buffers: its
+    bytes plus everything else come to the budget (within one block of the largest
+    ratio), more memory gives a larger pool, and a budget without room for one
+    request is refused."""
+    from dsv4_flash_deployment_b200.engine.memory import (expert_block_bytes, kv_pool_tokens_for,
+                                                           non_expert_bytes)
+
+    cfg = v4_flash_config()
+    GiB = 2 ** 30
+    args = dict(max_tokens=1024, n_slots=513, max_seq=2048, kv_block=64, ep_world=8)
+    pool = kv_pool_tokens_for(cfg, 178 * GiB, 0.85, **args)
+    used = non_expert_bytes(cfg, 1024, 513, 2048, 64, pool) + cfg.n_layers * expert_block_bytes(cfg, 8)
+    step = 128 * 64
+    per_tok = (non_expert_bytes(cfg, 1024, 513, 2048, 64, pool + step) - non_expert_bytes(cfg, 1024, 513, 2048, 64,
+                                                                                          pool)) / step
+    assert used <= 0.85 * 178 * GiB < used + (step + 1) * per_tok
+    assert pool % step == 0 and pool > 513 * 2048       # more context than the per-slot caches would hold
+    assert kv_pool_tokens_for(cfg, 178 * GiB, 0.95, **args) > pool
+    with pytest.raises(ValueError, match="not one"):
+        kv_pool_tokens_for(cfg, 20 * GiB, 0.85, **args)
+    with pytest.raises(ValueError):
+        kv_pool_tokens_for(cfg, 178 * GiB, 1.5, **args)
