@@ -51,12 +51,17 @@ class EngineConfig:
     control_plane: str = "shm"              # multi-rank control messages: "shm" (one node, shared memory)
                                             # or "gloo" (the CPU process group)
     host: str = "127.0.0.1"
+    api_key: str | None = None              # bearer key the API requires (or DSV4_API_KEY); None: open
     port: int = 8000
     step_deadline_s: float = 600.0
     overrides: dict = field(default_factory=dict)   # ModelConfig field overrides
 
     def to_dict(self) -> dict:
-        return dataclasses.asdict(self)
+        """The fields as a dict (echoed into results and ``/health``), the API key redacted."""
+        d = dataclasses.asdict(self)
+        if d.get("api_key"):
+            d["api_key"] = "(set)"
+        return d
 
     def model_config(self):
         from ..config import ModelConfig, get_config

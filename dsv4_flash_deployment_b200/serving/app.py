@@ -46,7 +46,13 @@ from .engine_loop import EngineLoop, GenParams
 
 
 class ServerState:
-    def __init__(self, loop: EngineLoop, tokenizer, model_name: str, max_model_len: int, info: dict | None = None):
+    """``api_key``: when set, every ``/v1/*``, ``/tokenize`` and ``/detokenize``
+    request must carry ``Authorization: Bearer <api_key>`` (vLLM's ``--api-key``);
+    ``/health`` and ``/metrics`` stay open for probes and scrapers."""
+
+    def __init__(self, loop: EngineLoop, tokenizer, model_name: str, max_model_len: int, info: dict | None = None,
+                 api_key: str | None = None):
+        self.api_key = api_key
         self.loop = loop
         self.tok = tokenizer
         self.model_name = model_name
@@ -328,8 +334,21 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
                               "x_metrics": metrics})
 
 
+OPEN_PATHS = ("/health", "/metrics")
+
+
 def build_app(st: ServerState) -> web.Application:
-    app = web.Application(client_max_size=64 * 1024 * 1024)
+    @web.middleware
+    async def auth(request, handler):
+        if st.api_key and request.path not in OPEN_PATHS:
+            import hmac
+
+            got = request.headers.get("Authorization", "")
+            if not hmac.compare_digest(got.encode(), f"Bearer {st.api_key}".encode()):
+                return _err(401, "missing or wrong API key")
+        return await handler(request)
+
+    app = web.Application(client_max_size=64 * 1024 * 1024, middlewares=[auth])
 
     async def health(_):
         lp = st.loop

@@ -158,7 +158,8 @@ def main(argv: list[str] | None = None) -> None:
     info = {"device": ec.device, "world_size": world, "engine_config": ec.to_dict()}
     if ec.device == "cuda":
         info["device_name"] = torch.cuda.get_device_name()
-    st = ServerState(loop, tok, ec.served_model_name, ec.max_model_len, info)
+    st = ServerState(loop, tok, ec.served_model_name, ec.max_model_len, info,
+                     api_key=ec.api_key or os.environ.get("DSV4_API_KEY") or None)
     try:
         web.run_app(build_app(st), host=ec.host, port=ec.port, print=None)
     finally:

@@ -348,3 +348,21 @@ def test_streamed_chat_chunks_parse_and_match_the_full_answer(served):
     assert all(c["object"] == "chat.completion.chunk" and c["id"] == chunks[0]["id"] for c in chunks)
     assert "".join(d.get("content", "") for d in deltas) == full["choices"][0]["message"]["content"]
     assert chunks[-1]["choices"][0]["finish_reason"] == "length" and "usage" in chunks[-1]
+
+
+def test_api_key_guards_the_api_but_not_health(served):
+    st, _ = served
+
+    async def go(c):
+        st.api_key = "s3cret"
+        try:
+            no = await c.post("/v1/completions", json={"prompt": [0, 5], "max_tokens": 1})
+            bad = await c.get("/v1/models", headers={"Authorization": "Bearer nope"})
+            ok = await c.get("/v1/models", headers={"Authorization": "Bearer s3cret"})
+            health = await c.get("/health")
+            return no.status, bad.status, ok.status, health.status
+        finally:
+            st.api_key = None
+    assert _run(st, go) == (401, 401, 200, 200)
+    from dsv4_flash_deployment_b200.engine.config import EngineConfig
+    assert EngineConfig(api_key="k").to_dict()["api_key"] == "(set)"
