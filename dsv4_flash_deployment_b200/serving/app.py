@@ -26,7 +26,10 @@ is accepted only equal to ``n``.  A request the engine cannot serve is refused
 with 400 (top-k / top-p / logprobs on the tensor-parallel head, logprobs or
 temperature under speculative decoding).
 Streaming sends one SSE event per generated token and ends with
-``data: [DONE]``; a client that disconnects cancels its request.
+``data: [DONE]``; usage rides on the last finish chunk, or with
+``stream_options: {"include_usage": true}`` in one more chunk with no choices.
+``echo`` (completions) puts the prompt's text before the completion.  A
+client that disconnects cancels its request.
 
 Run: ``python -m dsv4_flash_deployment_b200.serving --config v4-flash --port 8000``.
 """
@@ -306,13 +309,20 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
     n_in = sum(len(p) for p in prompts)
     usage = {"prompt_tokens": n_in, "completion_tokens": n_out, "total_tokens": n_in + n_out}
     if resp is not None:
+        # stream_options.include_usage: usage in one more chunk with no choices (the
+        # OpenAI layout); otherwise on the last finish chunk
+        usage_chunk = bool((body.get("stream_options") or {}).get("include_usage"))
         for ch in choices:
             if ch.error is not None:
                 await resp.write(f"data: {json.dumps({'error': {'message': ch.error}})}\n\n".encode())
             last = chunk_obj(ch, None, ch.finish)
-            if ch is choices[-1]:
+            if ch is choices[-1] and not usage_chunk:
                 last["usage"] = usage
             await resp.write(f"data: {json.dumps(last)}\n\n".encode())
+        if usage_chunk:
+            u = {"id": rid, "object": "chat.completion.chunk" if chat else "text_completion", "created": created,
+                 "model": st.model_name, "choices": [], "usage": usage}
+            await resp.write(f"data: {json.dumps(u)}\n\n".encode())
         await resp.write(b"data: [DONE]\n\n")
         await resp.write_eof()
         return resp
@@ -323,8 +333,10 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
             if want_lp:
                 c["logprobs"] = {"content": ch.lp_entries}
         else:
-            c = {"index": ch.index, "text": ch.text, "finish_reason": ch.finish,
-                 "logprobs": _completion_logprobs(ch.lp_entries, 0) if want_lp else None}
+            # echo: the prompt's text before the completion (its tokens carry no log-probabilities)
+            pre = st.tok.decode(prompts[ch.index // n]) if body.get("echo") else ""
+            c = {"index": ch.index, "text": pre + ch.text, "finish_reason": ch.finish,
+                 "logprobs": _completion_logprobs(ch.lp_entries, len(pre)) if want_lp else None}
         out.append(c)
     req = choices[0].ts.req
     metrics = {"ttft_s": (req.t_first_token - req.t_arrival) if req and req.t_first_token else None,

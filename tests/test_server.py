@@ -366,3 +366,26 @@ def test_api_key_guards_the_api_but_not_health(served):
     assert _run(st, go) == (401, 401, 200, 200)
     from dsv4_flash_deployment_b200.engine.config import EngineConfig
     assert EngineConfig(api_key="k").to_dict()["api_key"] == "(set)"
+
+
+def test_stream_usage_chunk_and_echo(served):
+    st, eng = served
+    ids = [0] + [33 + (5 * i) % 100 for i in range(8)]
+
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 3, "ignore_eos": True, "stream": True,
+                                                  "stream_options": {"include_usage": True}})
+        chunks = []
+        async for raw in r.content:
+            line = raw.decode().strip()
+            if line.startswith("data: {"):
+                chunks.append(json.loads(line[6:]))
+        e = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 3, "ignore_eos": True,
+                                                          "echo": True})).json()
+        plain = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 3,
+                                                              "ignore_eos": True})).json()
+        return chunks, e, plain
+    chunks, e, plain = _run(st, go)
+    assert chunks[-1]["choices"] == [] and chunks[-1]["usage"]["completion_tokens"] == 3
+    assert all("usage" not in ch for ch in chunks[:-1])
+    assert e["choices"][0]["text"] == st.tok.decode(ids) + plain["choices"][0]["text"]
