@@ -17,11 +17,9 @@ many sequences, and the vLLM scheduler loop for the vLLM-served recipes.
 
 from __future__ import annotations
 
-import time
 from collections import OrderedDict
 from typing import Iterable
 
-import numpy as np
 import torch
 
 from ..models.model import DSV4Model, SeqChunk, StepMeta

@@ -24,7 +24,6 @@ from __future__ import annotations
 
 import contextlib
 import itertools
-import math
 import os
 from dataclasses import dataclass
 
@@ -32,7 +31,7 @@ import numpy as np
 import torch
 
 from ..ops import _ext
-from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, KIND_BF16, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
+from ..ops.gemm import (EPI_BF16, EPI_F32, EPI_SWIGLU, ErrorWord, MxWeight, gemm_bf16, gemm_mx,
                         pick_bn)
 from ..ops.layout import ceil_to
 from ..ref import numerics as N

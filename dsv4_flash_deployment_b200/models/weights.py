@@ -26,7 +26,7 @@ from dataclasses import dataclass, field
 import torch
 
 from ..ops.gemm import MxWeight, prepare_w13
-from ..ops.layout import ceil_to, expand_block_scales, interleave_w13, sf_to_chunks
+from ..ops.layout import ceil_to, expand_block_scales
 from ..ref import numerics as N
 
 

@@ -35,7 +35,6 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from ..ops import _ext
 from ..ops.gemm import EPI_BF16, EPI_SWIGLU
 from ..ops.layout import ceil_to
 

@@ -34,7 +34,7 @@ import torch
 from ..models.kv_format import kv8_bytes
 from ..models.model import SeqChunk, StepMeta
 from ..models.weights import load_layer
-from ..ops.gemm import MxWeight, gemm_mx, quantize
+from ..ops.gemm import MxWeight, quantize
 from ..ops.layout import ceil_to
 
 

@@ -208,10 +208,9 @@ def check_storage(path: str | None) -> dict:
         return {"skipped": "no --storage-path"}
     import torch
 
-    from ..io.safetensors import read_tensors  # noqa: F401  (the reader module's native path)
-    from ..ops.host import lib
-
     import ctypes
+
+    from ..ops.host import lib
 
     size = os.path.getsize(path)
     buf = torch.empty(size, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
