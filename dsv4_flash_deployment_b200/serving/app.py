@@ -184,6 +184,7 @@ class _Choice:
     def __init__(self, index: int, n_prompt: int, ts, params: GenParams, stops: list[str]):
         self.index, self.n_prompt, self.ts, self.params, self.stops = index, n_prompt, ts, params, stops
         self.text = ""
+        self.detok = None             # the tokenizer's streaming decoder (set by _consume)
         self.out_ids: list[int] = []
         self.finish: str | None = None
         self.error: str | None = None
@@ -195,6 +196,8 @@ async def _consume(st: ServerState, ch: _Choice, chat: bool, emit=None) -> None:
     for every piece of text (streaming responses)."""
     want_lp = ch.params.logprobs is not None
     ts = ch.ts
+    mk = getattr(st.tok, "stream_decoder", None)
+    ch.detok = mk() if mk is not None else None
     while True:
         kind, val = await ts.q.get()
         if kind == "error":
@@ -202,12 +205,19 @@ async def _consume(st: ServerState, ch: _Choice, chat: bool, emit=None) -> None:
             return
         if kind == "done":
             ch.finish = "stop" if val == "stop" else ("length" if val == "length" else val)
+            tail = ch.detok.flush() if ch.detok is not None else ""
+            if tail:
+                ch.text += tail
+                if emit is not None:
+                    await emit(ch, tail, None)
             return
         tok, lp = int(val[0]), val[1]
         ch.out_ids.append(tok)
         if tok == st.tok.eos_token_id and not ch.params.ignore_eos:
             continue
-        piece = st.tok.decode_token(tok)
+        piece = ch.detok.push(tok) if ch.detok is not None else st.tok.decode_token(tok)
+        if not piece and lp is None:
+            continue                  # the token's text is still incomplete: nothing to send yet
         if ch.stops:
             cand = ch.text + piece
             hit = min((cand.find(s) for s in ch.stops if s in cand), default=-1)

@@ -47,6 +47,57 @@ class ByteTokenizer:
     def apply_chat_template(self, messages: list[dict]) -> str:
         return render_chat(messages)
 
+    def stream_decoder(self) -> "PieceDecoder":
+        """One text piece per token (the benchmark clients count tokens by chunks)."""
+        return PieceDecoder(self)
+
+
+class PieceDecoder:
+    """Streaming text of a token sequence, one token's own text per token."""
+
+    def __init__(self, tok):
+        self.tok = tok
+
+    def push(self, tid: int) -> str:
+        return self.tok.decode_token(tid)
+
+    def flush(self) -> str:
+        return ""
+
+
+class IncrementalDecoder:
+    """Streaming text of a token sequence for tokenizers whose tokens are not whole
+    characters (byte-level BPE): each token's delta is the new text of the decoded
+    window ``ids[prefix:]`` beyond the text of ``ids[prefix:read]``, and a delta
+    that would end in U+FFFD (a character whose bytes are still arriving) is held
+    back until a later token completes it.  Decoding a short window keeps the
+    tokenizer's context-dependent rules (leading spaces, merges) right at its
+    edge.  This is the incremental detokenization that text-generation servers
+    use (Hugging Face ``TextStreamer``, vLLM's ``detokenize_incrementally``)."""
+
+    def __init__(self, decode):
+        self.decode = decode          # list[int] -> str
+        self.ids: list[int] = []
+        self.prefix = 0
+        self.read = 0
+
+    def push(self, tid: int) -> str:
+        self.ids.append(tid)
+        before = self.decode(self.ids[self.prefix:self.read])
+        now = self.decode(self.ids[self.prefix:])
+        if len(now) > len(before) and not now.endswith("\ufffd"):
+            self.prefix, self.read = self.read, len(self.ids)
+            return now[len(before):]
+        return ""
+
+    def flush(self) -> str:
+        """Text still held back at the end of the sequence (an incomplete character
+        comes out as U+FFFD)."""
+        before = self.decode(self.ids[self.prefix:self.read])
+        now = self.decode(self.ids[self.prefix:])
+        self.prefix = self.read = len(self.ids)
+        return now[len(before):]
+
 
 def render_chat(messages: list[dict]) -> str:
     """DeepSeek-style chat rendering used when the tokenizer has no template."""
@@ -83,6 +134,9 @@ class HFTokenizer:
 
     def decode(self, ids: list[int]) -> str:
         return self.tok.decode(ids, skip_special_tokens=True)
+
+    def stream_decoder(self) -> IncrementalDecoder:
+        return IncrementalDecoder(self.decode)
 
     def apply_chat_template(self, messages: list[dict]) -> str:
         if getattr(self.tok, "chat_template", None):

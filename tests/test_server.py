@@ -389,3 +389,56 @@ def test_stream_usage_chunk_and_echo(served):
     assert chunks[-1]["choices"] == [] and chunks[-1]["usage"]["completion_tokens"] == 3
     assert all("usage" not in ch for ch in chunks[:-1])
     assert e["choices"][0]["text"] == st.tok.decode(ids) + plain["choices"][0]["text"]
+
+
+def test_incremental_decoder_holds_back_split_characters():
+    from dsv4_flash_deployment_b200.serving.tokenizer import ByteTokenizer, IncrementalDecoder
+
+    tok = ByteTokenizer(1024)
+    text = "añ€😀 ok"
+    ids = tok.encode(text, add_bos=False)
+    dec = IncrementalDecoder(tok.decode)
+    pieces = [dec.push(t) for t in ids]
+    assert "".join(pieces) + dec.flush() == text
+    assert all("�" not in p for p in pieces)
+    assert pieces.count("") == len(ids) - len(text)      # one empty piece per continuation byte
+    # a character cut off at the end comes out of flush as U+FFFD
+    dec = IncrementalDecoder(tok.decode)
+    got = [dec.push(t) for t in tok.encode("x€", add_bos=False)[:-1]]
+    assert "".join(got) == "x" and dec.flush() == "�"
+
+
+def test_server_streams_whole_characters_with_an_incremental_tokenizer(served):
+    """A tokenizer whose tokens are bytes (as byte-level BPE ones are): the streamed
+    pieces never split a character and add up to the text of all generated ids."""
+    from dsv4_flash_deployment_b200.serving.tokenizer import ByteTokenizer, IncrementalDecoder
+
+    st, eng = served
+
+    class ByteLevel(ByteTokenizer):
+        def stream_decoder(self):
+            return IncrementalDecoder(self.decode)
+
+    old = st.tok
+    st.tok = ByteLevel(old.vocab_size, old.bos_token_id, old.eos_token_id)
+    ids = [0] + [40 + (9 * i) % 150 for i in range(10)]
+
+    async def go(c):
+        r = await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 12, "ignore_eos": True,
+                                                  "stream": True})
+        pieces = []
+        async for raw in r.content:
+            line = raw.decode().strip()
+            if line.startswith("data: {"):
+                ch = json.loads(line[6:])["choices"]
+                if ch and ch[0]["text"]:
+                    pieces.append(ch[0]["text"])
+        full = await (await c.post("/v1/completions", json={"prompt": ids, "max_tokens": 12,
+                                                             "ignore_eos": True})).json()
+        return pieces, full
+    try:
+        pieces, full = _run(st, go)
+    finally:
+        st.tok = old
+    want = st.tok.decode(_greedy(eng, ids, 12))
+    assert "".join(pieces) == full["choices"][0]["text"] == want
