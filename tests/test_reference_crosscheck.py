@@ -3,8 +3,10 @@ its TPU stack: its configuration tables and its Engram hasher and token map
 (pure numpy / sympy / tokenizers; the model oracle itself needs JAX, which this
 image does not have).
 
-Set ``DSV4_REFERENCE_ROOT`` to a checkout of the reference (the directory that
-holds ``models/``); without it every test here is skipped.  Checked:
+The reference is looked up at ``DSV4_REFERENCE_ROOT`` (a checkout: the directory
+that holds ``models/``), else at the repository's ``baseline/_ref`` (the
+git-ignored place the reference is installed into); without either, every test
+here is skipped.  Checked:
 
 * the V4.1-Flash hyperparameters and the reference's ``tiny_config`` against
   ``config.py`` field by field;
@@ -22,11 +24,11 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-ROOT = os.environ.get("DSV4_REFERENCE_ROOT")
+ROOT = os.environ.get("DSV4_REFERENCE_ROOT") or str(Path(__file__).resolve().parent.parent / "baseline" / "_ref")
 PKG = Path(ROOT) / "models" / "DeepSeekV4.1-Flash-v6e16" / "tpu-v7x" if ROOT else None
 
 pytestmark = pytest.mark.skipif(PKG is None or not (PKG / "deepseek_v41" / "config.py").exists(),
-                                reason="DSV4_REFERENCE_ROOT does not point at the reference checkout")
+                                reason="no reference checkout (DSV4_REFERENCE_ROOT or baseline/_ref)")
 
 
 @pytest.fixture(scope="module")
