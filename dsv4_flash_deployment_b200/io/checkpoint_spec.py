@@ -92,6 +92,11 @@ def _layer_specs(cfg, prefix: str, layer_id: int, backbone: bool) -> dict[str, t
         s[f"{ep}.w3.scale"] = (E8, (inter, d // 32))
         s[f"{ep}.w2.scale"] = (E8, (d, inter // 32))
     s[f"{prefix}.ffn.gate.bias"] = (F32, (n_exp,))
+    if cfg.family == "v4.1":
+        # the V4.1 checkpoint's second routing bias, for image-sentinel tokens; text
+        # tokens route with ``gate.bias``, so this text-only engine loads it and never
+        # reads it (the reference's tensor list holds it: checkpoint.py:145)
+        s[f"{prefix}.ffn.gate.bias_vl"] = (F32, (n_exp,))
     s[f"{prefix}.ffn.gate.weight"] = (BF16, (n_exp, d))
     si = cfg.n_shared_experts * inter
     fp8("ffn.shared_experts.w1", si, d)

@@ -13,7 +13,13 @@ here is skipped.  Checked:
 * Engram row ids of random token sequences (full V4.1 layout and the tiny one)
   against the reference's ``compute_engram_hash_ids``, bit for bit;
 * the tokenizer-normalized compressed token map against the reference's
-  ``build_compressed_token_map`` on a tokenizer fixture.
+  ``build_compressed_token_map`` on a tokenizer fixture;
+* the checkpoint contract: every tensor name, dtype and shape against the
+  reference's ``expected_checkpoint_specs`` (full V4.1 and tiny, MTP stages
+  included), a checkpoint written by the reference's
+  ``write_synthetic_checkpoint`` loaded by this library's validated reader bit
+  for bit, and one written by this library read by the reference's
+  ``SafetensorsCheckpoint`` bit for bit.
 """
 
 import dataclasses
@@ -41,6 +47,18 @@ def ref():
     finally:
         sys.path.remove(str(PKG))
     return rc, rh
+
+
+@pytest.fixture(scope="module")
+def ref_ckpt():
+    pytest.importorskip("ml_dtypes")
+    sys.path.insert(0, str(PKG))
+    try:
+        from deepseek_v41 import checkpoint as rk
+        from deepseek_v41 import config as rc
+    finally:
+        sys.path.remove(str(PKG))
+    return rc, rk
 
 
 def _same(ours, theirs, skip=()):
@@ -102,3 +120,47 @@ def test_compressed_token_map_matches(ref, tmp_path):
     w2, c2 = rh.build_compressed_token_map(None, vocab_size=129280)
     g2, d2 = compressed_token_map(None, 129280)
     assert d2 == c2 and np.array_equal(g2, w2)
+
+
+@pytest.mark.parametrize("which", ["tiny", "full"])
+def test_checkpoint_specs_match(ref_ckpt, which):
+    from dsv4_flash_deployment_b200.config import v41_flash_config, v41_tiny_config
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import checkpoint_specs
+
+    rc, rk = ref_ckpt
+    ours_cfg, theirs_cfg = ((v41_tiny_config(), rc.tiny_config()) if which == "tiny"
+                            else (v41_flash_config(), rc.DSV41Config()))
+    want = {k: (t, tuple(s)) for k, (t, s) in rk.expected_checkpoint_specs(theirs_cfg, include_mtp=True).items()}
+    got = {k: (t, tuple(s)) for k, (t, s) in checkpoint_specs(ours_cfg, include_mtp=True).items()}
+    assert sorted(set(want) - set(got)) == [] and sorted(set(got) - set(want)) == []
+    diff = {k: (got[k], want[k]) for k in want if got[k] != want[k]}
+    assert diff == {}
+
+
+def _bytes(x):
+    import numpy as np
+    import torch
+
+    if isinstance(x, torch.Tensor):
+        return x.contiguous().view(torch.uint8).numpy().tobytes()
+    return np.ascontiguousarray(x).view(np.uint8).tobytes()
+
+
+def test_reference_checkpoint_loads_here_and_ours_loads_there(ref_ckpt, tmp_path):
+    from dsv4_flash_deployment_b200.config import v41_tiny_config
+    from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
+    from dsv4_flash_deployment_b200.io.safetensors import load_checkpoint, save_checkpoint
+
+    rc, rk = ref_ckpt
+    theirs = rk.write_synthetic_checkpoint(rc.tiny_config(), tmp_path / "theirs", seed=5, num_shards=3)
+    got = load_checkpoint(tmp_path / "theirs", v41_tiny_config(), include_mtp=True)
+    assert set(got) == set(theirs)
+    bad = [k for k in theirs if _bytes(got[k]) != _bytes(theirs[k])]
+    assert bad == []
+
+    ours = make_random_weights(v41_tiny_config(), seed=6, include_mtp=True)
+    save_checkpoint(tmp_path / "ours", ours, v41_tiny_config(), shard_bytes=1 << 20)
+    reader = rk.SafetensorsCheckpoint(tmp_path / "ours")
+    assert sorted(reader.keys()) == sorted(ours)
+    bad = [k for k in ours if _bytes(reader.read_tensor(k)) != _bytes(ours[k])]
+    assert bad == []
