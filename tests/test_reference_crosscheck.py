@@ -151,9 +151,14 @@ def test_reference_checkpoint_loads_here_and_ours_loads_there(ref_ckpt, tmp_path
     from dsv4_flash_deployment_b200.io.checkpoint_spec import make_random_weights
     from dsv4_flash_deployment_b200.io.safetensors import load_checkpoint, save_checkpoint
 
+    from dsv4_flash_deployment_b200.config import ModelConfig
+
     rc, rk = ref_ckpt
     theirs = rk.write_synthetic_checkpoint(rc.tiny_config(), tmp_path / "theirs", seed=5, num_shards=3)
-    got = load_checkpoint(tmp_path / "theirs", v41_tiny_config(), include_mtp=True)
+    # the checkpoint's config.json, read by this library's loader, is the same model
+    cfg_here = ModelConfig.from_json(tmp_path / "theirs" / "config.json")
+    assert _same(cfg_here, rc.tiny_config()) == {}
+    got = load_checkpoint(tmp_path / "theirs", cfg_here, include_mtp=True)
     assert set(got) == set(theirs)
     bad = [k for k in theirs if _bytes(got[k]) != _bytes(theirs[k])]
     assert bad == []
