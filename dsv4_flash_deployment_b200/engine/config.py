@@ -54,6 +54,7 @@ class EngineConfig:
     api_key: str | None = None              # bearer key the API requires (or DSV4_API_KEY); None: open
     port: int = 8000
     step_deadline_s: float = 600.0
+    drain_timeout_s: float = 30.0           # on SIGTERM: refuse new requests, let live ones finish this long
     overrides: dict = field(default_factory=dict)   # ModelConfig field overrides
 
     def to_dict(self) -> dict:

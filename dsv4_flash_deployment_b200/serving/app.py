@@ -259,6 +259,8 @@ async def _generate(st: ServerState, request: web.Request, chat: bool):
         return web.Response(status=400, text=e.text, content_type="application/json")
     if not st.loop.healthy:
         return _err(503, f"engine unhealthy: {st.loop.error}")
+    if st.loop.draining:
+        return _err(503, "the server is shutting down")
     stream = bool(body.get("stream", False))
     rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:16]
     created = int(time.time())
@@ -374,11 +376,12 @@ def build_app(st: ServerState) -> web.Application:
 
     async def health(_):
         lp = st.loop
-        body = {"status": "ok" if lp.healthy else "unhealthy", "error": lp.error, "model": st.model_name,
+        status = "unhealthy" if not lp.healthy else ("draining" if lp.draining else "ok")
+        body = {"status": status, "error": lp.error, "model": st.model_name,
                 "uptime_s": time.time() - st.t_start, "live_requests": lp.n_live,
                 "total_requests": lp.stats["requests"], "total_generated_tokens": lp.stats["generated_tokens"],
                 **st.info}
-        return web.json_response(body, status=200 if lp.healthy else 503)
+        return web.json_response(body, status=200 if status == "ok" else 503)
 
     async def models(_):
         return web.json_response({"object": "list", "data": [

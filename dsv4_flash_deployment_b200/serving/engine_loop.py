@@ -78,6 +78,7 @@ class EngineLoop:
         self.step_deadline_s = step_deadline_s
         self.idle_wait_s = idle_wait_s
         self.healthy = True
+        self.draining = False         # set by drain(): new requests are refused, live ones finish
         self.error: str | None = None
         self._stop = threading.Event()
         self._wake = threading.Event()
@@ -97,6 +98,17 @@ class EngineLoop:
         self._stop.set()
         self._wake.set()
         self.thread.join(timeout=30)
+
+    def drain(self, timeout_s: float = 30.0) -> bool:
+        """Graceful shutdown: refuse new requests and wait (up to ``timeout_s``) for
+        the live ones to finish.  Returns True when none is left."""
+        self.draining = True
+        deadline = time.perf_counter() + timeout_s
+        while time.perf_counter() < deadline:
+            if not self._live and self.inbox.empty():
+                return True
+            time.sleep(0.01)
+        return not self._live
 
     def submit(self, prompt: list[int], params: GenParams) -> TokenStream:
         s = TokenStream(asyncio.get_running_loop())
@@ -124,6 +136,9 @@ class EngineLoop:
                 _, prompt, p, s = msg
                 if not self.healthy:
                     s.put(("error", f"engine unhealthy: {self.error}"))
+                    continue
+                if self.draining:
+                    s.put(("error", "the server is shutting down"))
                     continue
                 try:
                     # the filtering / log-probability options only when asked for, so an

@@ -161,7 +161,15 @@ def main(argv: list[str] | None = None) -> None:
     st = ServerState(loop, tok, ec.served_model_name, ec.max_model_len, info,
                      api_key=ec.api_key or os.environ.get("DSV4_API_KEY") or None)
     try:
-        web.run_app(build_app(st), host=ec.host, port=ec.port, print=None)
+        app = build_app(st)
+
+        async def drain(_app):
+            # SIGTERM / SIGINT: /health answers 503 "draining", new requests are refused,
+            # live ones run to completion for up to drain_timeout_s
+            import asyncio
+            await asyncio.to_thread(loop.drain, ec.drain_timeout_s)
+        app.on_shutdown.append(drain)
+        web.run_app(app, host=ec.host, port=ec.port, print=None, shutdown_timeout=ec.drain_timeout_s + 5)
     finally:
         loop.stop()
         if world > 1:

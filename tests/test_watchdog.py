@@ -62,3 +62,30 @@ def test_step_past_deadline_fails_requests():
     assert [k for k, _ in items] == ["error", "error", "error"]
     assert "deadline" in items[0][1]
     assert not loop.healthy
+
+
+def test_drain_refuses_new_requests_and_lets_live_ones_finish():
+    async def go(loop):
+        live = loop.submit(list(range(10, 20)), GenParams(max_tokens=20, ignore_eos=True))
+        while live.req is None:
+            await asyncio.sleep(0.005)
+        drained = asyncio.get_running_loop().run_in_executor(None, loop.drain, 30.0)
+        while not loop.draining:
+            await asyncio.sleep(0.001)
+        late = loop.submit([1, 2, 3], GenParams(max_tokens=2))
+        late_item = await asyncio.wait_for(late.q.get(), timeout=30)
+        n = 0
+        while True:
+            kind, _ = await asyncio.wait_for(live.q.get(), timeout=30)
+            if kind == "done":
+                break
+            n += kind == "token"
+        return late_item, n, await drained
+
+    loop = EngineLoop(FakeEngine("slow", sleep_s=0.01)).start()
+    try:
+        late_item, n, ok = asyncio.run(go(loop))
+    finally:
+        loop.stop()
+    assert late_item[0] == "error" and "shutting down" in late_item[1]
+    assert n == 20 and ok and loop.healthy
