@@ -71,9 +71,11 @@ async def calibrate_words(s, base, model, n_prompts: int, isl: int) -> tuple[int
 
 async def one_request(s, base, model, prompt, max_tokens: int) -> dict:
     t0 = time.perf_counter()
-    ttft, ntok = None, 0
+    ttft, ntok, usage_tok = None, 0, None
+    # the usage chunk counts tokens even where a tokenizer holds a piece back (a
+    # character split over tokens), as the reference's client does (recipes/benchmark.py:50,104)
     body = {"model": model, "prompt": prompt, "max_tokens": max_tokens, "temperature": 0.0, "stream": True,
-            "ignore_eos": True}
+            "ignore_eos": True, "stream_options": {"include_usage": True}}
     async with s.post(f"{base}/v1/completions", json=body) as r:
         if r.status != 200:
             raise RuntimeError(f"HTTP {r.status}: {(await r.text())[:300]}")
@@ -87,11 +89,13 @@ async def one_request(s, base, model, prompt, max_tokens: int) -> dict:
             ev = json.loads(data)
             if "error" in ev:
                 raise RuntimeError(f"stream error: {ev['error']}")
-            if ev["choices"][0].get("text"):
+            if ev.get("usage"):
+                usage_tok = ev["usage"].get("completion_tokens", usage_tok)
+            if ev["choices"] and ev["choices"][0].get("text"):
                 if ttft is None:
                     ttft = time.perf_counter() - t0
                 ntok += 1
-    return {"ttft_s": ttft, "total_s": time.perf_counter() - t0, "ntok": ntok}
+    return {"ttft_s": ttft, "total_s": time.perf_counter() - t0, "ntok": usage_tok if usage_tok is not None else ntok}
 
 
 async def run_point(base, model, prompts, concurrency: int, max_tokens: int, timeout_s: float):
