@@ -58,4 +58,5 @@ def render_prometheus(st) -> str:
         metric("spec_accepted_tokens_total", "counter", "Draft tokens accepted.", spec.get("accepted", 0))
         metric("spec_draft_tokens_total", "counter", "Draft tokens proposed.", spec.get("drafted", 0))
     metric("healthy", "gauge", "1 when the engine loop is healthy.", 1 if lp.healthy else 0)
+    metric("draining", "gauge", "1 while a shutdown drains the live requests.", 1 if getattr(lp, "draining", False) else 0)
     return "\n".join(lines) + "\n"
