@@ -59,6 +59,11 @@ ALL_STAGES = ("cold_startup", "parity_ref", "parity_neg_control", "golden", "per
 
 
 # ------------------------------------------------------------------ result files
+# named stage sets for --stages
+PRESETS = {"all": ALL_STAGES, "quick": ("cold_startup", "parity_ref", "parity_neg_control", "golden"),
+           "perf": ("perf_b1", "perf_b2", "perf_b4", "perf_b8")}
+
+
 def stage_path(out: Path, stage: str) -> Path:
     return Path(out) / f"{stage}.json"
 
@@ -85,6 +90,25 @@ def write_stage_result(out: Path, stage: str, rec: dict) -> None:
     tmp = p.with_suffix(".json.tmp")
     tmp.write_text(json.dumps(rec, indent=1, sort_keys=True) + "\n")
     os.replace(tmp, p)
+
+
+def render_summary(out: Path, model: str, device: str) -> str:
+    """A markdown table of every stage record in ``out``: state, rule and the key
+    measurements (the numbers a reader checks first)."""
+    keys = ("build_s", "cos_mean", "cos_min", "top1", "strict_top1", "tie_aware_top1", "tpot_ms_median",
+            "decode_tok_s", "identical_fraction", "pass@1", "rc", "reason", "error")
+    rows = [f"# Verification stages: {model} on {device}", "", "| stage | state | rule | measurements |",
+            "|---|---|---|---|"]
+    for st in ALL_STAGES:
+        r = read_stage(out, st)
+        if r is None:
+            rows.append(f"| {st} | not run | | |")
+            continue
+        state = "skipped" if r.get("skipped") else ("passed" if r.get("passed") else "failed")
+        meas = ", ".join(f"{k} {r[k]:.4g}" if isinstance(r[k], float) else f"{k} {r[k]}"
+                         for k in keys if k in r and r[k] is not None)
+        rows.append(f"| {st} | {state} | {r.get('rule', '')} | {meas[:300]} |")
+    return "\n".join(rows) + "\n"
 
 
 def skipped(reason: str) -> dict:
@@ -125,7 +149,8 @@ class Runner:
     def run(self) -> dict:
         from ..utils.provenance import provenance
 
-        stages = list(ALL_STAGES) if self.a.stages == "all" else [s.strip() for s in self.a.stages.split(",")]
+        stages = (list(PRESETS[self.a.stages]) if self.a.stages in PRESETS
+                  else [s.strip() for s in self.a.stages.split(",")])
         unknown = [s for s in stages if s not in ALL_STAGES]
         if unknown:
             raise SystemExit(f"unknown stages {unknown}; known: {list(ALL_STAGES)}")
@@ -154,6 +179,7 @@ class Runner:
                     "passed" if r.get("passed") else "failed") for s, r in all_stages.items()}
         write_stage_result(self.out, "summary", {"this_run": summary, "stages": full, "model": self.cfg.name,
                                                  "device": self.device})
+        (self.out / "summary.md").write_text(render_summary(self.out, self.cfg.name, self.device))
         return summary
 
     def _release(self) -> None:
@@ -351,7 +377,7 @@ class Runner:
 def parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description="resumable model-level verification stages")
     ap.add_argument("--out", required=True, help="directory of the <stage>.json records")
-    ap.add_argument("--stages", default="all", help="comma-separated stage names, or 'all'")
+    ap.add_argument("--stages", default="all", help="comma-separated stage names, or a preset: all, quick, perf")
     ap.add_argument("--model", default="v4-check", help="named model config")
     ap.add_argument("--device", default=None, choices=["cuda", "cpu"], help="default: cuda when available")
     ap.add_argument("--checkpoint", default=None, help="safetensors directory (default: random weights)")

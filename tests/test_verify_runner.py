@@ -31,6 +31,8 @@ def test_stages_records_and_resume(tmp_path, monkeypatch):
     assert d["skipped"] and not d["passed"] and "MTP" in d["reason"]
     summ = _rec(out, "summary")
     assert summ["stages"]["parity_ref"] == "passed" and summ["stages"]["gsm8k"] == "not run"
+    md = (out / "summary.md").read_text()
+    assert "| parity_ref | passed |" in md and "| gsm8k | not run |" in md and "cos_mean" in md
 
     # resume: passed stages are kept as they are; a failing stage is recorded, the run goes on
     t_before = _rec(out, "parity_ref")["time"]
