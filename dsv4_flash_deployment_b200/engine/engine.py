@@ -197,8 +197,11 @@ class Engine:
         graph.replay()
         return out
 
-    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False) -> list[list[int]]:
-        reqs = [self.add_request(p, max_new_tokens, ignore_eos) for p in prompts]
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False,
+                 **sampling) -> list[list[int]]:
+        """Runs the prompts to completion; ``sampling``: :meth:`add_request`'s decoding
+        options (temperature, top_k, top_p, seed, logprobs)."""
+        reqs = [self.add_request(p, max_new_tokens, ignore_eos, **sampling) for p in prompts]
         while not all(r.finished for r in reqs):
             self.step()
         return [r.output for r in reqs]
