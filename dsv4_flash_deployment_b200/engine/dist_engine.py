@@ -215,8 +215,9 @@ class DistributedEngine:
         self.ctl.broadcast({"adds": [], "cancels": [], "any_work": False, "stop": True})
         self.ctl.close()
 
-    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False) -> list[list[int]]:
-        reqs = [self.add_request(p, max_new_tokens, ignore_eos) for p in prompts]
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = False,
+                 **sampling) -> list[list[int]]:
+        reqs = [self.add_request(p, max_new_tokens, ignore_eos, **sampling) for p in prompts]
         while not all(r.finished for r in reqs):
             self.step()
         return [r.output for r in reqs]
