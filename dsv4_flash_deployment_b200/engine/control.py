@@ -100,6 +100,34 @@ class ShmControl:
             raise ControlError(f"cannot open the control file {path} (rank {rank} of {world})")
         self._lens = (ctypes.c_int64 * world)()
 
+    @staticmethod
+    def remove_stale(directory: str = "/dev/shm") -> list[str]:
+        """Removes control files left by a rank 0 that died without closing them
+        (named ``dsv4_ctl_<pid>_<tag>``; a file is stale when that process is gone)."""
+        import glob
+
+        gone = []
+        for path in glob.glob(os.path.join(directory, "dsv4_ctl_*_*")):
+            try:
+                pid = int(os.path.basename(path).split("_")[2])
+            except (IndexError, ValueError):
+                continue
+            if pid == os.getpid():
+                continue
+            try:
+                os.kill(pid, 0)
+                continue                    # its creator is alive
+            except ProcessLookupError:
+                pass
+            except PermissionError:
+                continue                    # another user's live process
+            try:
+                os.remove(path)
+                gone.append(path)
+            except OSError:
+                pass
+        return gone
+
     @classmethod
     def create(cls, group=None, directory: str = "/dev/shm", timeout_s: float = 600.0, **kw) -> "ShmControl":
         """Rank 0 creates the file and broadcasts its path over ``group``; every rank
@@ -108,6 +136,7 @@ class ShmControl:
         box = [os.path.join(directory, f"dsv4_ctl_{os.getpid()}_{uuid.uuid4().hex[:8]}") if rank == 0 else None]
         ch = None
         if rank == 0:
+            cls.remove_stale(directory)
             ch = cls(box[0], 0, world, timeout_s=timeout_s, **kw)
         dist.broadcast_object_list(box, src=0, group=group)
         if rank != 0:

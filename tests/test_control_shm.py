@@ -152,3 +152,20 @@ def test_serving_front_over_shared_memory_matches_oracle():
         want, _ = ref.generate(torch.tensor([p]), 4)
         assert got == want[0].tolist()
     assert sorted(set(res[0]["ranks"])) == [0, 1] and res[1]["steps"] > 0
+
+
+def test_stale_control_files_are_removed(tmp_path):
+    import subprocess
+    import sys
+
+    from dsv4_flash_deployment_b200.engine.control import ShmControl
+
+    p = subprocess.run([sys.executable, "-c", "import os; print(os.getpid())"], capture_output=True, text=True)
+    dead = int(p.stdout)
+    stale = tmp_path / f"dsv4_ctl_{dead}_abcd1234"
+    live = tmp_path / f"dsv4_ctl_{os.getpid()}_beef0000"
+    other = tmp_path / "dsv4_ctl_notapid_x"
+    for f in (stale, live, other):
+        f.write_bytes(b"x")
+    assert ShmControl.remove_stale(str(tmp_path)) == [str(stale)]
+    assert live.exists() and other.exists() and not stale.exists()
